@@ -1,0 +1,335 @@
+"""Benchmark: boosting rounds/s of the reference's binary-logloss path on B200.
+
+Workload (BASELINE.json metric "boosting rounds/sec at 1M x 100 depth 6"):
+config 4's data -- 1,000,000 x 100 float32, 30 % NaN, 60 N(0,1) / 30 Exp(1) /
+10 integer-level columns, 99/1 sparse-logistic label (seeded synthetic
+stand-in) -- binned with the reference's rules (255 bins + NaN bin), trained
+with max_depth 6, 63 leaves, lr 0.08, subsample 0.75, colsample 0.7,
+min_child_weight 3, lambda 1, class_weight balanced_sqrt (power 0.35).
+
+A step is one boosting round: the reference's row/feature sampler, the tree
+(gradients, histograms, splits, partitions), the F update and the train
+logloss.  `value` times K rounds on the binned matrix already resident in
+HBM (device CUDA events on the engine stream, L2 flushed between rounds);
+`e2e` times the public estimator API (`fit_binned`) from host arrays,
+including the upload of the binned matrix and every round's mask/tree
+copies.  Rows are sharded over N GPUs (one process per GPU, NCCL allreduce
+of the exact histogram words), so the total work is fixed: strong scaling.
+
+--impl reference times the reference's algorithm on the host cores instead:
+the CPU oracle (a C restatement of the reference's Numba path, OpenMP over
+features like its prange), the same config and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "bsscl-gbm_b200"), os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "boosting rounds/sec at 1M x 100 depth 6"
+CFG = dict(n=1_000_000, max_depth=6, max_leaves=63, lr=0.08, subsample=0.75, colsample=0.7,
+           mcw=3.0, lam=1.0, msl=5, class_weight="balanced_sqrt", seed=0)
+
+
+def workload(n):
+    """config 4 data, binned exactly as the reference bins it."""
+    from bsscl_gbm_b200 import binning, datasets
+    X, y = datasets.config4(n=n)
+    edges, counts, nanb = binning.build_bin_edges(X, 255)
+    Xb = binning.bin_features(X, edges, counts, nanb)
+    return Xb, y, counts
+
+
+class Clocks:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for k, nm in enumerate(names):
+                if f[5 + k].lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peak_hbm():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def cpu_rounds(Xb, y, counts, rounds, warmup=1, budget_s=None):
+    """The reference's loop on the CPU oracle (REF mode): rounds/s."""
+    import oracle as O
+    c = CFG
+    kw = dict(learning_rate=c["lr"], max_leaves=c["max_leaves"], max_depth=c["max_depth"],
+              min_samples_leaf=c["msl"], min_child_weight=c["mcw"], reg_lambda=c["lam"],
+              gamma=0.0, subsample=c["subsample"], colsample=c["colsample"],
+              class_weight=c["class_weight"], random_state=c["seed"], mode=O.MODE_REF)
+    O.fit_binary(Xb, y, counts, n_estimators=warmup, **kw)
+    t0 = time.perf_counter()
+    done = 0
+    while True:
+        O.fit_binary(Xb, y, counts, n_estimators=1, **kw)
+        done += 1
+        el = time.perf_counter() - t0
+        if done >= rounds or (budget_s is not None and el > budget_s):
+            break
+    # each call also pays one base-score/gradient pass; that is part of a round anyway
+    return done / el, done, O.num_threads()
+
+
+def run_reference(args):
+    """--impl reference: the reference's algorithm (CPU oracle) on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle as O
+    Xb, y, counts = workload(CFG["n"])
+    c = CFG
+    kw = dict(learning_rate=c["lr"], max_leaves=c["max_leaves"], max_depth=c["max_depth"],
+              min_samples_leaf=c["msl"], min_child_weight=c["mcw"], reg_lambda=c["lam"],
+              gamma=0.0, subsample=c["subsample"], colsample=c["colsample"],
+              class_weight=c["class_weight"], random_state=c["seed"], mode=O.MODE_REF)
+    O.fit_binary(Xb, y, counts, n_estimators=max(1, args.warmup), **kw)
+    t0 = time.perf_counter()
+    O.fit_binary(Xb, y, counts, n_estimators=args.steps, **kw)
+    el = time.perf_counter() - t0
+    v = args.steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "rounds/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * el / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic (config 4 stand-in, seed 3)",
+        "config": {"workload": "config4 1M x 100 f32 30% NaN, depth 6, 63 leaves", "n_rows": CFG["n"],
+                   "n_features": 100, "max_depth": 6, "max_leaves": 63, "subsample": 0.75,
+                   "colsample": 0.7},
+        "cpu_baseline": {"value": v, "unit": "rounds/s", "cores": O.num_threads(), "kind": "port",
+                         "sample": f"{args.steps} rounds of the full workload"},
+        "e2e": {"value": v, "unit": "rounds/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_engine(args):
+    import torch
+    from bsscl_gbm_b200 import Engine, GbmParams, HybridHistGBMNumbaV1_0_1, Sampler, binning
+    import oracle as O
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    c = CFG
+    n = c["n"]
+    Xb, y, counts = workload(n)
+    p = Xb.shape[1]
+    lo, hi = (n * rank) // world, (n * (rank + 1)) // world
+    w2 = O.class_weights(y, c["class_weight"])
+    base = O.base_score(y, w2)
+    Xd = binning.device_bins(Xb, counts)
+
+    eng = Engine(local)
+    if world > 1:
+        uid = [Engine.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        eng.init_comm(uid[0], world, rank, timeout_ms=120000)
+    eng.upload_bins(Xd[lo:hi], counts)
+    eng.upload_labels(y[lo:hi].astype(np.uint8), w2, base, n_global=n)
+    prm = GbmParams(c["lam"], 0.0, c["mcw"], c["lr"], c["msl"], c["max_depth"], c["max_leaves"], 0,
+                    None)
+    cap = 2 * c["max_leaves"] + 2
+    n_sub, n_feat = int(n * c["subsample"]), int(p * c["colsample"])
+    sampler = Sampler(c["seed"], n, p, n_sub, n_feat, True, True, look_ahead=3)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
+
+    def step():
+        _, mask, feat = sampler.next()
+        return eng.round(mask[lo:hi], feat, prm, cap)
+
+    for _ in range(args.warmup):
+        step()
+    eng.set_profiling(True)
+    eng.reset_stats()
+    clocks = Clocks(local)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    round_ms = []
+    losses = []
+    for _ in range(args.steps):
+        flush.zero_()                       # L2 flush between timed rounds (256 MB > 126 MB L2)
+        torch.cuda.synchronize()
+        eng.event(0)
+        _, loss, _ = step()
+        eng.event(1)
+        round_ms.append(eng.elapsed_ms(0, 1))
+        losses.append(loss)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if dist is not None:
+        dist.barrier()
+    st = eng.stats()
+    eng.set_profiling(False)
+    total_ms = float(sum(round_ms))
+    if dist is not None:
+        t = torch.tensor([total_ms], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = args.steps / (total_ms / 1000.0)
+
+    # ---- e2e: the public estimator API from host arrays ----------------------
+    m = HybridHistGBMNumbaV1_0_1(n_estimators=args.steps, max_depth=c["max_depth"],
+                                 learning_rate=c["lr"], min_child_weight=c["mcw"],
+                                 subsample=c["subsample"], colsample_bytree=c["colsample"],
+                                 reg_lambda=c["lam"], class_weight=c["class_weight"],
+                                 random_state=c["seed"], verbose=False)
+    m.max_leaves = c["max_leaves"]
+    m._engine, m._engine_dev = eng, local
+    if dist is not None:
+        dist.barrier()
+    eng.event(2)
+    t0 = time.perf_counter()
+    m.fit_binned(Xb, y, counts)
+    eng.event(3)
+    e2e_ms = eng.elapsed_ms(2, 3)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = args.steps / (e2e_ms / 1000.0)
+    rows = hi - lo
+    h2d = (rows * p + rows + args.steps * (rows + 4 * n_feat)) / args.steps
+    d2h = cap * 40 + 8
+
+    # ---- predict rows/s (device-resident rows and ensemble) ----------------------
+    from bsscl_gbm_b200 import datasets
+    ens = datasets.config5_ensemble(n_trees=1000, depth=8, p=p, seed=5)
+    eng.predict_set_model(ens, 1000, p)
+    eng.predict_upload(Xd[lo:hi])
+    eng.predict_run(c["lr"], base)
+    eng.sync()
+    eng.event(4)
+    reps = 3
+    for _ in range(reps):
+        eng.predict_run(c["lr"], base)
+    eng.event(5)
+    pred_ms = eng.elapsed_ms(4, 5) / reps
+    if dist is not None:
+        t = torch.tensor([pred_ms], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pred_ms = float(t.item())
+    pred_rows_s = n / (pred_ms / 1000.0)
+
+    peak, peak_kind = measured_peak_hbm()
+    achieved = (st["hist_alg_bytes"] / (st["hist_ms"] / 1000.0)) / 1e9 if st["hist_ms"] > 0 else 0.0
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v_cpu, done, cores = cpu_rounds(Xb, y, counts, rounds=50, warmup=1, budget_s=20.0)
+        cpu = {"value": v_cpu, "unit": "rounds/s", "cores": cores, "kind": "port",
+               "sample": f"{done} rounds of the full workload on the CPU oracle (REF mode)"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "rounds/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (config 4 stand-in, seed 3)",
+            "config": {"workload": "config4 1M x 100 f32 30% NaN, depth 6, 63 leaves",
+                       "n_rows": n, "n_features": p, "max_depth": c["max_depth"],
+                       "max_leaves": c["max_leaves"], "subsample": c["subsample"],
+                       "colsample": c["colsample"], "parallelism": f"rows sharded x{world}",
+                       "l2": "flushed between timed rounds (256 MB write)"},
+            "roofline": {"bound": "hbm", "kernel": "k_hist", "achieved": achieved, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": achieved / peak if peak else None, "traffic": None,
+                         "hist_launches": st["hist_launches"], "hist_ms": st["hist_ms"],
+                         "alg_bytes": st["hist_alg_bytes"]},
+            "e2e": {"value": e2e, "unit": "rounds/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": st["kernel_launches"],
+            "predict": {"rows_per_s": pred_rows_s, "node_visits_per_s": pred_rows_s * 1000 * 8,
+                        "ensemble": "1000 full depth-8 random trees (config 5 ensemble, p=100)"},
+            "train_loss_last": losses[-1] if losses else None,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    sampler.close()
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_engine(args)
+
+
+if __name__ == "__main__":
+    main()

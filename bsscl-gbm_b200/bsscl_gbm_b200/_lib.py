@@ -1,0 +1,327 @@
+"""ctypes binding of libgbm_b200.so (the C ABI declared in include/gbm_b200.h).
+
+The library is the only compute path of this package: importing works
+without a GPU, but every engine call fails loudly (RuntimeError) when the
+shared object is missing or no CUDA device is present.  There is no CPU
+fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libgbm_b200.so")
+CSRC = os.path.join(os.path.dirname(HERE), "csrc")
+
+GBM_OK = 0
+ERRORS = {1: "invalid argument", 2: "allocation failed", 3: "CUDA error", 4: "bad state",
+          5: "communicator error", 6: "timeout", 7: "unsupported"}
+
+# Every symbol include/gbm_b200.h declares.
+EXPORTS = (
+    "gbm_ctx_create", "gbm_ctx_destroy", "gbm_last_error", "gbm_ctx_init_comm",
+    "gbm_nccl_unique_id", "gbm_upload_bins", "gbm_upload_labels", "gbm_round", "gbm_build_tree",
+    "gbm_scale_bits", "gbm_get_F", "gbm_get_grad", "gbm_predict", "gbm_predict_set_model",
+    "gbm_predict_upload", "gbm_predict_run", "gbm_predict_fetch", "gbm_sync",
+    "gbm_sampler_create", "gbm_sampler_next", "gbm_sampler_destroy",
+    "gbm_set_profiling", "gbm_get_stats", "gbm_reset_stats", "gbm_event_record",
+    "gbm_event_elapsed",
+)
+
+
+class GbmParams(C.Structure):
+    _fields_ = [("reg_lambda", C.c_double), ("gamma", C.c_double),
+                ("min_child_weight", C.c_double), ("learning_rate", C.c_double),
+                ("min_samples_leaf", C.c_int32), ("max_depth", C.c_int32),
+                ("max_leaves", C.c_int32), ("grow_policy", C.c_int32),
+                ("monotone", C.c_void_p)]
+
+
+class GbmTreeOut(C.Structure):
+    _fields_ = [("capacity", C.c_int32), ("tf", C.c_void_p), ("tt", C.c_void_p),
+                ("tv", C.c_void_p), ("tl", C.c_void_p), ("tr", C.c_void_p),
+                ("sg", C.c_void_p), ("n_nodes", C.c_int32), ("leaf_of_row", C.c_void_p)]
+
+
+class GbmPacked(C.Structure):
+    _fields_ = [("features", C.c_void_p), ("thresholds", C.c_void_p), ("values", C.c_void_p),
+                ("left", C.c_void_p), ("right", C.c_void_p), ("offsets", C.c_void_p),
+                ("n_trees", C.c_int32)]
+
+
+class GbmStats(C.Structure):
+    _fields_ = [("kernel_launches", C.c_int64), ("hist_launches", C.c_int64),
+                ("hist_rows", C.c_int64), ("waves", C.c_int64), ("hist_ms", C.c_double),
+                ("hist_alg_bytes", C.c_double)]
+
+
+_lib = None
+
+
+def build(force=False):
+    """Compile libgbm_b200.so for sm_100a with nvcc (see csrc/Makefile)."""
+    import subprocess
+    if force and os.path.exists(LIB_PATH):
+        os.remove(LIB_PATH)
+    subprocess.run(["make", "-s", "-C", CSRC], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"libgbm_b200.so not found at {LIB_PATH}; build it with "
+            "`make -C bsscl-gbm_b200/csrc` (nvcc, sm_100a). There is no CPU fallback.")
+    L = C.CDLL(LIB_PATH)
+    P, i32, i64, f64 = C.c_void_p, C.c_int32, C.c_int64, C.c_double
+    L.gbm_ctx_create.argtypes = [i32, C.POINTER(C.c_void_p)]
+    L.gbm_ctx_destroy.argtypes = [P]
+    L.gbm_ctx_destroy.restype = None
+    L.gbm_last_error.argtypes = [P]
+    L.gbm_last_error.restype = C.c_char_p
+    L.gbm_ctx_init_comm.argtypes = [P, P, i32, i32, i32]
+    L.gbm_nccl_unique_id.argtypes = [P]
+    L.gbm_upload_bins.argtypes = [P, P, i64, i32, P]
+    L.gbm_upload_labels.argtypes = [P, P, P, f64, i64]
+    L.gbm_round.argtypes = [P, P, P, i32, C.POINTER(GbmParams), C.POINTER(GbmTreeOut),
+                            C.POINTER(C.c_double)]
+    L.gbm_build_tree.argtypes = [P, P, P, P, P, i32, C.POINTER(GbmParams), C.POINTER(GbmTreeOut)]
+    L.gbm_scale_bits.argtypes = [P]
+    L.gbm_scale_bits.restype = i32
+    L.gbm_get_F.argtypes = [P, P]
+    L.gbm_get_grad.argtypes = [P, P, P]
+    L.gbm_predict.argtypes = [P, P, i64, i32, C.POINTER(GbmPacked), f64, f64, P, P]
+    L.gbm_predict_set_model.argtypes = [P, C.POINTER(GbmPacked), i32]
+    L.gbm_predict_upload.argtypes = [P, P, i64, i32]
+    L.gbm_predict_run.argtypes = [P, f64, f64]
+    L.gbm_predict_fetch.argtypes = [P, P, P]
+    L.gbm_sync.argtypes = [P]
+    L.gbm_sampler_create.argtypes = [C.c_uint32, i64, i32, i64, i32, i32, i32, i32,
+                                     C.POINTER(C.c_void_p)]
+    L.gbm_sampler_next.argtypes = [P, P, P, P]
+    L.gbm_sampler_destroy.argtypes = [P]
+    L.gbm_sampler_destroy.restype = None
+    L.gbm_set_profiling.argtypes = [P, i32]
+    L.gbm_get_stats.argtypes = [P, C.POINTER(GbmStats)]
+    L.gbm_reset_stats.argtypes = [P]
+    L.gbm_event_record.argtypes = [P, i32]
+    L.gbm_event_elapsed.argtypes = [P, i32, i32, C.POINTER(C.c_float)]
+    _lib = L
+    return L
+
+
+def ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+class Engine:
+    """One device context (one GPU, one CUDA stream)."""
+
+    def __init__(self, device=0):
+        self._L = lib()
+        self._h = C.c_void_p()
+        rc = self._L.gbm_ctx_create(int(device), C.byref(self._h))
+        if rc != GBM_OK:
+            msg = self.last_error()
+            self.close()
+            raise RuntimeError(f"gbm_ctx_create(device={device}) failed: {msg}")
+
+    # -- plumbing --
+    def last_error(self):
+        if not self._h:
+            return "no context"
+        return self._L.gbm_last_error(self._h).decode(errors="replace")
+
+    def check(self, rc, what):
+        if rc != GBM_OK:
+            raise RuntimeError(f"{what} failed ({ERRORS.get(rc, rc)}): {self.last_error()}")
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.gbm_ctx_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- multi-GPU --
+    @staticmethod
+    def nccl_unique_id():
+        buf = (C.c_uint8 * 128)()
+        rc = lib().gbm_nccl_unique_id(C.cast(buf, C.c_void_p))
+        if rc != GBM_OK:
+            raise RuntimeError("ncclGetUniqueId failed (is libnccl.so.2 available?)")
+        return bytes(buf)
+
+    def init_comm(self, uid: bytes, nranks: int, rank: int, timeout_ms: int = 60000):
+        buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+        self.check(self._L.gbm_ctx_init_comm(self._h, C.cast(buf, C.c_void_p), nranks, rank,
+                                             timeout_ms), "gbm_ctx_init_comm")
+
+    # -- training --
+    def upload_bins(self, xbin_u8, counts):
+        xb = np.ascontiguousarray(xbin_u8, dtype=np.uint8)
+        cnt = np.ascontiguousarray(counts, dtype=np.int32)
+        n, p = xb.shape
+        self.n, self.p = n, p
+        self.check(self._L.gbm_upload_bins(self._h, ptr(xb), n, p, ptr(cnt)), "gbm_upload_bins")
+
+    def upload_labels(self, y01, w2, base_score, n_global=0):
+        y = np.ascontiguousarray(y01, dtype=np.uint8)
+        w = np.ascontiguousarray(w2, dtype=np.float64)
+        self.check(self._L.gbm_upload_labels(self._h, ptr(y), ptr(w), float(base_score),
+                                             int(n_global)), "gbm_upload_labels")
+
+    def round(self, inbag_mask, feat_idx, params: GbmParams, capacity, want_leaf=False):
+        mask = np.ascontiguousarray(inbag_mask, dtype=np.uint8)
+        fidx = np.ascontiguousarray(feat_idx, dtype=np.int32)
+        tf = np.empty(capacity, np.int32); tt = np.empty(capacity, np.int64)
+        tv = np.empty(capacity, np.float64); tl = np.empty(capacity, np.int32)
+        tr = np.empty(capacity, np.int32); sg = np.empty(capacity, np.float64)
+        leaf = np.empty(self.n, np.int32) if want_leaf else None
+        out = GbmTreeOut(capacity, ptr(tf), ptr(tt), ptr(tv), ptr(tl), ptr(tr), ptr(sg), 0,
+                         ptr(leaf))
+        loss = C.c_double(0.0)
+        self.check(self._L.gbm_round(self._h, ptr(mask), ptr(fidx), len(fidx), C.byref(params),
+                                     C.byref(out), C.byref(loss)), "gbm_round")
+        return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value), leaf
+
+    def build_tree(self, grad, hess, inbag_mask, feat_idx, params: GbmParams, capacity):
+        """One tree from given gradients (the reference's _build_one_tree seam)."""
+        g = np.ascontiguousarray(grad, dtype=np.float64)
+        h = np.ascontiguousarray(hess, dtype=np.float64)
+        mask = np.ascontiguousarray(inbag_mask, dtype=np.uint8)
+        fidx = np.ascontiguousarray(feat_idx, dtype=np.int32)
+        tf = np.empty(capacity, np.int32); tt = np.empty(capacity, np.int64)
+        tv = np.empty(capacity, np.float64); tl = np.empty(capacity, np.int32)
+        tr = np.empty(capacity, np.int32); sg = np.empty(capacity, np.float64)
+        out = GbmTreeOut(capacity, ptr(tf), ptr(tt), ptr(tv), ptr(tl), ptr(tr), ptr(sg), 0, None)
+        self.check(self._L.gbm_build_tree(self._h, ptr(g), ptr(h), ptr(mask), ptr(fidx), len(fidx),
+                                          C.byref(params), C.byref(out)), "gbm_build_tree")
+        return (tf, tt, tv, tl, tr, int(out.n_nodes), sg)
+
+    def scale_bits(self):
+        return int(self._L.gbm_scale_bits(self._h))
+
+    def get_F(self):
+        F = np.empty(self.n, np.float64)
+        self.check(self._L.gbm_get_F(self._h, ptr(F)), "gbm_get_F")
+        return F
+
+    def get_grad(self):
+        g = np.empty(self.n, np.float64); h = np.empty(self.n, np.float64)
+        self.check(self._L.gbm_get_grad(self._h, ptr(g), ptr(h)), "gbm_get_grad")
+        return g, h
+
+    # -- predict --
+    @staticmethod
+    def packed_struct(packed, n_trees):
+        keep = {
+            "features": np.ascontiguousarray(packed["features"], dtype=np.int16),
+            "thresholds": np.ascontiguousarray(packed["thresholds"], dtype=np.int64),
+            "values": np.ascontiguousarray(packed["values"], dtype=np.float64),
+            "left": np.ascontiguousarray(packed["left"], dtype=np.int32),
+            "right": np.ascontiguousarray(packed["right"], dtype=np.int32),
+            "offsets": np.ascontiguousarray(packed["offsets"], dtype=np.int32),
+        }
+        s = GbmPacked(ptr(keep["features"]), ptr(keep["thresholds"]), ptr(keep["values"]),
+                      ptr(keep["left"]), ptr(keep["right"]), ptr(keep["offsets"]), int(n_trees))
+        return s, keep
+
+    def predict(self, xbin_u8, packed, n_trees, lr, base, want_F=True, want_proba=True):
+        xb = np.ascontiguousarray(xbin_u8, dtype=np.uint8)
+        n, p = xb.shape
+        s, keep = self.packed_struct(packed, n_trees)
+        F = np.empty(n, np.float64) if want_F else None
+        P = np.empty(n, np.float64) if want_proba else None
+        self.check(self._L.gbm_predict(self._h, ptr(xb), n, p, C.byref(s), float(lr), float(base),
+                                       ptr(F), ptr(P)), "gbm_predict")
+        return F, P
+
+    def predict_set_model(self, packed, n_trees, n_features):
+        s, keep = self.packed_struct(packed, n_trees)
+        self.check(self._L.gbm_predict_set_model(self._h, C.byref(s), int(n_features)),
+                   "gbm_predict_set_model")
+
+    def predict_upload(self, xbin_u8):
+        xb = np.ascontiguousarray(xbin_u8, dtype=np.uint8)
+        self._pn = xb.shape[0]
+        self.check(self._L.gbm_predict_upload(self._h, ptr(xb), xb.shape[0], xb.shape[1]),
+                   "gbm_predict_upload")
+
+    def predict_run(self, lr, base):
+        self.check(self._L.gbm_predict_run(self._h, float(lr), float(base)), "gbm_predict_run")
+
+    def predict_fetch(self, want_F=True, want_proba=True):
+        F = np.empty(self._pn, np.float64) if want_F else None
+        P = np.empty(self._pn, np.float64) if want_proba else None
+        self.check(self._L.gbm_predict_fetch(self._h, ptr(F), ptr(P)), "gbm_predict_fetch")
+        return F, P
+
+    def sync(self):
+        self.check(self._L.gbm_sync(self._h), "gbm_sync")
+
+    # -- instrumentation --
+    def set_profiling(self, on=True):
+        self.check(self._L.gbm_set_profiling(self._h, int(bool(on))), "gbm_set_profiling")
+
+    def stats(self):
+        st = GbmStats()
+        self.check(self._L.gbm_get_stats(self._h, C.byref(st)), "gbm_get_stats")
+        return {k: getattr(st, k) for k, _ in GbmStats._fields_}
+
+    def reset_stats(self):
+        self.check(self._L.gbm_reset_stats(self._h), "gbm_reset_stats")
+
+    def event(self, slot):
+        self.check(self._L.gbm_event_record(self._h, int(slot)), "gbm_event_record")
+
+    def elapsed_ms(self, a, b):
+        ms = C.c_float(0.0)
+        self.check(self._L.gbm_event_elapsed(self._h, int(a), int(b), C.byref(ms)),
+                   "gbm_event_elapsed")
+        return float(ms.value)
+
+
+class Sampler:
+    """The reference's RandomState row/feature subsample stream (native, bit-exact)."""
+
+    def __init__(self, seed, n, p, n_sub, n_feat, subsample_on, colsample_on, look_ahead=2):
+        self._L = lib()
+        self._h = C.c_void_p()
+        self.n, self.p, self.n_sub, self.n_feat = int(n), int(p), int(n_sub), int(n_feat)
+        rc = self._L.gbm_sampler_create(C.c_uint32(int(seed) & 0xFFFFFFFF), self.n, self.p,
+                                        self.n_sub, self.n_feat, int(bool(subsample_on)),
+                                        int(bool(colsample_on)), int(look_ahead),
+                                        C.byref(self._h))
+        if rc != GBM_OK:
+            raise ValueError(f"gbm_sampler_create failed ({ERRORS.get(rc, rc)})")
+
+    def next(self, want_sample=False, want_mask=True):
+        s = np.empty(self.n_sub, np.int64) if want_sample else None
+        m = np.empty(self.n, np.uint8) if want_mask else None
+        f = np.empty(self.n_feat, np.int32)
+        rc = self._L.gbm_sampler_next(self._h, ptr(s), ptr(m), ptr(f))
+        if rc != GBM_OK:
+            raise RuntimeError("gbm_sampler_next failed")
+        return s, m, f
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.gbm_sampler_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

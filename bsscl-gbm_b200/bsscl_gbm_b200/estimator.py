@@ -1,0 +1,594 @@
+"""``HybridHistGBMNumbaV1_0_1`` -- the reference's estimator API on the B200 engine.
+
+Mirrors the public surface of src/bsscl_gbm/estimator_v1_0_1.py (E):
+constructor and 'auto' resolution (E:1820-1923, E:1925-2029), ``fit``
+(E:3070-3271), ``predict_proba`` (E:3274-3336), ``predict`` (E:3345-3368),
+``get_params`` / ``set_params`` (E:3773-3796), the fitted attributes
+(``trees``, ``_packed_*``, ``_tree_offsets``, ``base_score_``, ``bin_edges``,
+``feature_bin_counts``, ``_nan_bin_id``, ``train_loss_history_``,
+``val_loss_history_``, ``feature_importances_``, ``times``,
+``n_trees_fitted_``) and its ValueErrors.
+
+Every boosting round runs on the GPU through libgbm_b200.so (``gbm_round``);
+predict_proba runs ``gbm_predict``.  There is no CPU path: ``device`` must
+name a CUDA device ('b200', 'cuda', 'cuda:N'), and a missing device or
+library raises.  Binary log-loss only; the reference's other objectives,
+GOSS, DART and categorical features raise NotImplementedError.
+
+Row sharding: when ``torch.distributed`` is initialised with more than one
+rank, every rank passes the same full ``X``/``y`` and trains on its
+contiguous block of rows; histograms are summed exactly over ranks, so
+every rank grows the same trees as one GPU would.
+"""
+
+from __future__ import annotations
+
+import os
+import time
+
+import numpy as np
+
+from . import binning
+from ._lib import Engine, GbmParams, Sampler
+
+
+def _device_index(device):
+    if device in ("b200", "cuda", "gpu", "auto"):
+        return None
+    if isinstance(device, str) and device.startswith("cuda:"):
+        return int(device.split(":", 1)[1])
+    if isinstance(device, int):
+        return device
+    raise ValueError(f"device={device!r}: this engine runs on CUDA devices only "
+                     "('b200', 'cuda', 'cuda:N'); it has no CPU path")
+
+
+def _dist():
+    try:
+        import torch.distributed as dist
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+            return dist
+    except Exception:
+        pass
+    return None
+
+
+class HybridHistGBMNumbaV1_0_1:
+    """Histogram GBM (binary log-loss) trained and evaluated on NVIDIA B200."""
+
+    def __init__(self, n_estimators='auto', max_depth='auto', learning_rate='auto',
+                 n_bins='auto', reg_lambda=1.0, min_samples_leaf=5,
+                 min_child_weight='auto', gamma='auto',
+                 subsample='auto', colsample_bytree='auto',
+                 class_weight='balanced_sqrt',
+                 grow_policy='leaf', max_leaves=31, binning_strategy='auto',
+                 monotone_constraints=None, categorical_features=None,
+                 early_stopping_rounds=None, verbose=True, random_state=None,
+                 objective='auto', focal_gamma=2.0, loss='mse', device='b200',
+                 sampling_method='uniform', top_rate=0.2, other_rate=0.1,
+                 scale_pos_weight=None, custom_objective=None, boosting_type='gbdt',
+                 dart_rate=0.1, interaction_constraints=None):
+        self.binning_strategy_init = binning_strategy
+        self.n_estimators_init = n_estimators
+        self.max_depth_init = max_depth
+        self.learning_rate_init = learning_rate
+        self.n_bins_init = n_bins
+        self.reg_lambda = reg_lambda
+        self.min_samples_leaf = min_samples_leaf
+        self.min_child_weight_init = min_child_weight
+        self.gamma_init = gamma
+        self.subsample_init = subsample
+        self.colsample_init = colsample_bytree
+        self.device = device
+        _device_index(device)
+        self.sampling_method = sampling_method
+        self.top_rate = top_rate
+        self.other_rate = other_rate
+        self.scale_pos_weight = scale_pos_weight
+        self.class_weight = class_weight
+        self.grow_policy = grow_policy
+        self.custom_objective = custom_objective
+        self.boosting_type = boosting_type
+        self.dart_rate = dart_rate
+        self.interaction_constraints = interaction_constraints
+        self.max_leaves = max_leaves
+        self.monotone_constraints = monotone_constraints
+        self.categorical_features = categorical_features
+        self.early_stopping_rounds = early_stopping_rounds
+        self.verbose = verbose
+        self.random_state = random_state
+        self.n_estimators = 100 if n_estimators == 'auto' else n_estimators
+        self.max_depth = 5 if max_depth == 'auto' else max_depth
+        self.learning_rate = 0.1 if learning_rate == 'auto' else learning_rate
+        self.n_bins = 256 if n_bins == 'auto' else n_bins
+        self.min_child_weight = 1.0 if min_child_weight == 'auto' else min_child_weight
+        self.gamma = 0.0 if gamma == 'auto' else gamma
+        self.subsample = 0.8 if subsample == 'auto' else subsample
+        self.colsample_bytree = 0.8 if colsample_bytree == 'auto' else colsample_bytree
+        self.objective = objective
+        self.focal_gamma = focal_gamma
+        self.loss = loss
+        self.init_score_ = 0.0
+        self.trees = []
+        self.bin_edges = None
+        self.feature_bin_counts = None
+        self._max_bins = 0
+        self.n_features_in_ = None
+        self.n_classes_ = 2
+        self.classes_ = None
+        self._is_multiclass = False
+        self.mc_trees = None
+        self.feature_importances_ = None
+        self.feature_split_counts_ = None
+        self.train_loss_history_ = []
+        self.val_loss_history_ = []
+        self.n_trees_fitted_ = 0
+        self.best_iteration_ = 0
+        self.times = {'binning': 0.0, 'training': 0.0, 'inference': 0.0}
+        self._packed_features = None
+        self._packed_thresholds = None
+        self._packed_values = None
+        self._packed_left = None
+        self._packed_right = None
+        self._tree_offsets = None
+        self._mc_packed = None
+        self._nan_bin_id = None
+        self._engine = None
+        self._engine_dev = None
+        self.scale_bits_ = None
+
+    # ------------------------------------------------------------------
+    # sklearn-style parameter access (E:3773-3796)
+    # ------------------------------------------------------------------
+    _PARAM_NAMES = ('n_estimators', 'max_depth', 'learning_rate', 'n_bins', 'reg_lambda',
+                    'min_samples_leaf', 'min_child_weight', 'gamma', 'subsample',
+                    'colsample_bytree', 'class_weight', 'grow_policy', 'max_leaves',
+                    'binning_strategy', 'monotone_constraints', 'categorical_features',
+                    'early_stopping_rounds', 'verbose', 'random_state', 'objective',
+                    'focal_gamma', 'loss', 'device', 'sampling_method', 'top_rate',
+                    'other_rate', 'scale_pos_weight', 'custom_objective', 'boosting_type',
+                    'dart_rate', 'interaction_constraints')
+    _INIT_ALIAS = {'n_estimators': 'n_estimators_init', 'max_depth': 'max_depth_init',
+                   'learning_rate': 'learning_rate_init', 'n_bins': 'n_bins_init',
+                   'min_child_weight': 'min_child_weight_init', 'gamma': 'gamma_init',
+                   'subsample': 'subsample_init', 'colsample_bytree': 'colsample_init',
+                   'binning_strategy': 'binning_strategy_init'}
+
+    def get_params(self, deep=True):
+        out = {}
+        for k in self._PARAM_NAMES:
+            out[k] = getattr(self, self._INIT_ALIAS.get(k, k), None)
+        return out
+
+    def set_params(self, **params):
+        for k, v in params.items():
+            if k not in self._PARAM_NAMES:
+                raise ValueError(f"Invalid parameter {k!r}")
+            if k in self._INIT_ALIAS:
+                setattr(self, self._INIT_ALIAS[k], v)
+                if v != 'auto':
+                    setattr(self, k, v)
+            else:
+                setattr(self, k, v)
+                if k == 'device':
+                    _device_index(v)
+        return self
+
+    def __getstate__(self):
+        st = self.__dict__.copy()
+        st['_engine'] = None
+        st['_engine_dev'] = None
+        return st
+
+    # ------------------------------------------------------------------
+    # adaptive hyper-parameters (E:1925-2029)
+    # ------------------------------------------------------------------
+    def _compute_adaptive_hyperparameters(self, X, y):
+        n, p = X.shape
+        K = self.n_classes_
+        if self.binning_strategy_init == 'auto':
+            self.binning_strategy = 'hybrid' if (n > 20000 or p > 40) else 'standard'
+        else:
+            self.binning_strategy = self.binning_strategy_init
+        if self.max_depth_init == 'auto':
+            if K > 10:
+                self.max_depth = min(8, max(4, int(np.log2(max(n // 8, 8)))))
+            else:
+                self.max_depth = min(6, max(3, int(np.log2(max(n // 10, 8)))))
+        if self.learning_rate_init == 'auto':
+            data_std = np.std(X)
+            if n > 20000:
+                self.learning_rate = 0.08
+            elif data_std > 2.0:
+                self.learning_rate = 0.10
+            elif data_std > 1.5:
+                self.learning_rate = 0.12
+            elif data_std > 1.0:
+                self.learning_rate = 0.15
+            elif data_std > 0.5:
+                self.learning_rate = 0.18
+            else:
+                self.learning_rate = 0.20
+            if K > 10:
+                self.learning_rate *= 0.75
+            elif K > 6:
+                self.learning_rate *= 0.85
+        if self.n_bins_init == 'auto':
+            self.n_bins = min(256, p * 8 + 32)
+        if self.n_estimators_init == 'auto':
+            if K <= 2:
+                self.n_estimators = 150
+            elif K <= 6:
+                self.n_estimators = max(150, min(300, n // 10))
+            elif K <= 15:
+                self.n_estimators = max(200, min(400, n // 8))
+            else:
+                self.n_estimators = max(250, min(500, n // 6))
+        if self.gamma_init == 'auto':
+            self.gamma = 0.0
+        if self.min_child_weight_init == 'auto':
+            self.min_child_weight = 3.0 if n > 20000 else (2.0 if n > 5000 else 1.0)
+        if self.subsample_init == 'auto':
+            self.subsample = 0.5 if n > 1000000 else (0.75 if n > 20000 else 0.8)
+        if n > 1000000:
+            self.reg_lambda = max(self.reg_lambda, 5.0)
+        if self.colsample_init == 'auto':
+            self.colsample_bytree = 0.7 if p > 40 else 0.8
+        if n > 10000:
+            self.max_leaves = 63
+        elif n < 2000:
+            self.max_leaves = 15
+        else:
+            self.max_leaves = 31
+        if self.verbose:
+            print("  Adaptive Hyperparameters:")
+            print(f"     n_estimators:  {self.n_estimators}")
+            print(f"     max_depth:     {self.max_depth} (from {n} samples)")
+            print(f"     learning_rate: {self.learning_rate:.4f}")
+            print(f"     n_bins:        {self.n_bins} (from {p} features)")
+            print(f"     gamma:         {self.gamma:.2f}")
+            print(f"     min_child_w:   {self.min_child_weight:.1f}")
+            print(f"     subsample:     {self.subsample}")
+            print(f"     colsample:     {self.colsample_bytree}")
+
+    # ------------------------------------------------------------------
+    # class weights and base score (E:2570-2603, E:2829-2835)
+    # ------------------------------------------------------------------
+    def _class_weight_pair(self, y01):
+        if self.scale_pos_weight is not None and self.objective == 'binary':
+            return np.array([1.0, float(self.scale_pos_weight)])
+        if self.class_weight not in ('balanced', 'balanced_sqrt'):
+            return np.array([1.0, 1.0])
+        n = len(y01)
+        w = np.ones(2)
+        for k in range(2):
+            nk = int(np.sum(y01 == k))
+            wk = n / (2 * max(nk, 1))
+            if self.class_weight == 'balanced_sqrt':
+                wk = wk ** 0.35
+            w[k] = wk
+        return w
+
+    # ------------------------------------------------------------------
+    # device plumbing
+    # ------------------------------------------------------------------
+    def _get_engine(self):
+        idx = _device_index(self.device)
+        if idx is None:
+            idx = int(os.environ.get("LOCAL_RANK", 0)) if _dist() is not None else 0
+        if self._engine is None or self._engine_dev != idx:
+            self._engine = Engine(idx)
+            self._engine_dev = idx
+        return self._engine
+
+    def _params_struct(self):
+        policy = 0 if self.grow_policy == 'leaf' else 1
+        self._mono_keep = None
+        mono_ptr = None
+        if self._mono_arr is not None:
+            self._mono_keep = np.ascontiguousarray(self._mono_arr, dtype=np.int32)
+            mono_ptr = self._mono_keep.ctypes.data
+        return GbmParams(float(self.reg_lambda), float(self.gamma), float(self.min_child_weight),
+                         float(self.learning_rate), int(self.min_samples_leaf), int(self.max_depth),
+                         int(self.max_leaves), policy, mono_ptr)
+
+    def _tree_capacity(self):
+        if self.grow_policy == 'leaf':
+            return 2 * int(self.max_leaves) + 2
+        return (1 << (int(self.max_depth) + 1)) - 1
+
+    # ------------------------------------------------------------------
+    # fit
+    # ------------------------------------------------------------------
+    def _check_supported(self):
+        if self.objective not in ('auto', 'binary'):
+            raise NotImplementedError(f"objective={self.objective!r}: the B200 engine trains "
+                                      "binary log-loss only")
+        if self.sampling_method != 'uniform':
+            raise NotImplementedError("sampling_method='goss' is not on the B200 engine")
+        if self.boosting_type != 'gbdt':
+            raise NotImplementedError("boosting_type='dart' is not on the B200 engine")
+        if self.custom_objective is not None:
+            raise NotImplementedError("custom_objective is not on the B200 engine")
+        if self.categorical_features is not None:
+            raise NotImplementedError("categorical_features is not on the B200 engine")
+
+    def fit(self, X, y, group=None, X_val=None, y_val=None, group_val=None, eval_set=None):
+        try:
+            import scipy.sparse
+            if scipy.sparse.issparse(X):
+                X = X.toarray()
+            if X_val is not None and scipy.sparse.issparse(X_val):
+                X_val = X_val.toarray()
+        except ImportError:
+            pass
+        if self.max_depth != 'auto' and self.max_depth <= 0:
+            raise ValueError(f"max_depth must be > 0, got {self.max_depth}")
+        if self.learning_rate <= 0:
+            raise ValueError(f"learning_rate must be > 0, got {self.learning_rate}")
+        if self.n_estimators <= 0:
+            raise ValueError(f"n_estimators must be > 0, got {self.n_estimators}")
+        self._check_supported()
+        if eval_set is not None and len(eval_set) > 0:
+            X_val, y_val = eval_set[0]
+        X = np.asarray(X)
+        y = np.asarray(y)
+        if X.ndim != 2:
+            raise ValueError(f"X must be 2-D, got shape {X.shape}")
+        if len(y) != X.shape[0]:
+            raise ValueError(f"X has {X.shape[0]} rows but y has {len(y)}")
+        if X.shape[0] == 0:
+            raise ValueError("X is empty")
+        self.classes_ = np.unique(y)
+        self.n_classes_ = len(self.classes_)
+        if self.n_classes_ > 2:
+            raise NotImplementedError("multi-class softmax is not on the B200 engine")
+        self._is_multiclass = False
+        label_map = {c: i for i, c in enumerate(self.classes_)}
+        y = np.array([label_map[v] for v in y], dtype=np.int64)
+        if y_val is not None:
+            y_val = np.array([label_map[v] for v in y_val], dtype=np.int64)
+        self.trees = []
+        self.mc_trees = None
+        self.train_loss_history_ = []
+        self.val_loss_history_ = []
+        self.n_features_in_ = X.shape[1]
+        if self.monotone_constraints is not None:
+            mc = self.monotone_constraints
+            if isinstance(mc, dict):
+                arr = np.zeros(X.shape[1], dtype=np.int32)
+                for f, d in mc.items():
+                    arr[f] = d
+                self._mono_arr = arr
+            else:
+                self._mono_arr = np.array(mc, dtype=np.int32)
+            if len(self._mono_arr) != X.shape[1]:
+                raise ValueError(f"monotone_constraints length ({len(self._mono_arr)}) must match "
+                                 f"n_features ({X.shape[1]})")
+        else:
+            self._mono_arr = None
+        self._categorical_set = set()
+        self._is_categorical = np.zeros(X.shape[1], dtype=bool)
+        if not np.issubdtype(X.dtype, np.floating) or X.dtype == np.float16:
+            X = X.astype(np.float64)
+        if X_val is not None:
+            X_val = np.asarray(X_val)
+            if not np.issubdtype(X_val.dtype, np.floating) or X_val.dtype == np.float16:
+                X_val = X_val.astype(np.float64)
+        self._compute_adaptive_hyperparameters(X, y)
+        sample_weight = None
+        if self.scale_pos_weight is not None and self.objective == 'binary':
+            sample_weight = np.ones(len(y), dtype=np.float64)
+            sample_weight[y == 1] = self.scale_pos_weight
+        t0 = time.perf_counter()
+        self.bin_edges, self.feature_bin_counts, self._nan_bin_id = binning.build_bin_edges(
+            X, self.n_bins, None, sample_weight)
+        self._max_bins = int(np.max(self.feature_bin_counts))
+        X_bin = binning.bin_features(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id)
+        self.times['binning'] = (time.perf_counter() - t0) * 1000
+        X_val_bin = None
+        if X_val is not None and y_val is not None:
+            X_val_bin = binning.bin_features(X_val, self.bin_edges, self.feature_bin_counts,
+                                             self._nan_bin_id)
+        t0 = time.perf_counter()
+        self._fit_binary_device(X_bin, y, X_val_bin, y_val)
+        self.times['training'] = (time.perf_counter() - t0) * 1000
+        self._pack_trees()
+        self._compute_feature_importances()
+        if self.verbose:
+            print(f"\n  Training complete! ({self.n_trees_fitted_} trees)")
+            print(f"    Binning:  {self.times['binning']:.2f} ms")
+            print(f"    Training: {self.times['training']:.2f} ms")
+        return self
+
+    def fit_binned(self, X_bin, y01, counts, X_val_bin=None, y_val=None):
+        """Train on a pre-binned matrix (bin ids per feature, ``counts`` bins each).
+
+        The reference's own loop can be driven the same way
+        (``_fit_binary`` on ``X_bin``, E:2825).  Hyper-parameters are used as
+        given ('auto' values must already be resolved).
+        """
+        self._check_supported()
+        y01 = np.asarray(y01).astype(np.int64)
+        self.classes_ = np.array([0, 1])
+        self.n_classes_ = 2
+        self._is_multiclass = False
+        self.n_features_in_ = X_bin.shape[1]
+        self.feature_bin_counts = np.asarray(counts, dtype=np.int32)
+        self._max_bins = int(np.max(self.feature_bin_counts))
+        self._nan_bin_id = np.full(X_bin.shape[1], -1, dtype=np.int32)
+        self._mono_arr = None
+        self.trees = []
+        self.train_loss_history_ = []
+        self.val_loss_history_ = []
+        t0 = time.perf_counter()
+        self._fit_binary_device(X_bin, y01, X_val_bin, y_val)
+        self.times['training'] = (time.perf_counter() - t0) * 1000
+        self._pack_trees()
+        self._compute_feature_importances()
+        return self
+
+    def _fit_binary_device(self, X_bin, y, X_val_bin, y_val):
+        """The reference's ``_fit_binary`` loop (E:2825-2944) with every round on the GPU."""
+        n, p = X_bin.shape
+        w2 = self._class_weight_pair(y)
+        sw = w2[y]
+        p0 = np.clip(np.average(y, weights=sw), 1e-7, 1.0 - 1e-7)
+        self.base_score_ = float(np.log(p0 / (1.0 - p0)))
+        n_sub = max(1, int(n * self.subsample))
+        n_feat = max(1, int(p * self.colsample_bytree))
+        seed = self.random_state
+        if seed is None:
+            seed = int.from_bytes(os.urandom(4), "little")
+        if not (0 <= int(seed) <= 0xFFFFFFFF):
+            raise ValueError("Seed must be between 0 and 2**32 - 1")
+        sampler = Sampler(int(seed), n, p, n_sub, n_feat, self.subsample < 1.0,
+                          self.colsample_bytree < 1.0, look_ahead=2)
+        eng = self._get_engine()
+        dist = _dist()
+        lo, hi = 0, n
+        if dist is not None:
+            ws, rk = dist.get_world_size(), dist.get_rank()
+            lo, hi = (n * rk) // ws, (n * (rk + 1)) // ws
+            uid = [Engine.nccl_unique_id() if rk == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            eng.init_comm(uid[0], ws, rk)
+        Xd = binning.device_bins(X_bin[lo:hi], self.feature_bin_counts)
+        eng.upload_bins(Xd, self.feature_bin_counts)
+        eng.upload_labels(y[lo:hi].astype(np.uint8), w2, self.base_score_, n_global=n)
+        self.scale_bits_ = eng.scale_bits()
+        params = self._params_struct()
+        cap = self._tree_capacity()
+        F_val = np.full(len(y_val), self.base_score_) if y_val is not None else None
+        best_val = np.inf
+        no_improve = 0
+        try:
+            for m in range(self.n_estimators):
+                _, mask, fidx = sampler.next()
+                tree, loss, _ = eng.round(mask[lo:hi], fidx, params, cap)
+                self.trees.append(tree)
+                self.train_loss_history_.append(loss)
+                val_loss = None
+                if X_val_bin is not None:
+                    F_val += self.learning_rate * _predict_tree_host(X_val_bin, tree)
+                    val_loss = _logloss(y_val, F_val)
+                    self.val_loss_history_.append(val_loss)
+                if self.verbose and ((m + 1) % 20 == 0 or m == 0):
+                    msg = f"  Tree {m + 1:>3}/{self.n_estimators}  |  train-loss: {loss:.6f}"
+                    if val_loss is not None:
+                        msg += f"  |  val-loss: {val_loss:.6f}"
+                    print(msg)
+                if self.early_stopping_rounds is not None and val_loss is not None:
+                    if val_loss < best_val:
+                        best_val = val_loss
+                        self.best_iteration_ = m
+                        no_improve = 0
+                    else:
+                        no_improve += 1
+                        if no_improve >= self.early_stopping_rounds:
+                            self.trees = self.trees[:self.best_iteration_ + 1]
+                            break
+        finally:
+            sampler.close()
+        self.n_trees_fitted_ = len(self.trees)
+
+    # ------------------------------------------------------------------
+    # packing, importances (E:2192-2236, E:2343-2363)
+    # ------------------------------------------------------------------
+    def _pack_trees(self):
+        total = sum(t[5] for t in self.trees)
+        feats = np.empty(total, dtype=np.int16)
+        thr = np.empty(total, dtype=np.int64)
+        vals = np.empty(total, dtype=np.float64)
+        left = np.empty(total, dtype=np.int32)
+        right = np.empty(total, dtype=np.int32)
+        offs = np.empty(len(self.trees) + 1, dtype=np.int32)
+        o = 0
+        for t, (tf, tt, tv, tl, tr, nc, _) in enumerate(self.trees):
+            offs[t] = o
+            feats[o:o + nc] = tf[:nc]
+            thr[o:o + nc] = tt[:nc]
+            vals[o:o + nc] = tv[:nc]
+            left[o:o + nc] = tl[:nc]
+            right[o:o + nc] = tr[:nc]
+            o += nc
+        offs[len(self.trees)] = o
+        self._packed_features, self._packed_thresholds = feats, thr
+        self._packed_values, self._packed_left, self._packed_right = vals, left, right
+        self._tree_offsets = offs
+
+    def _compute_feature_importances(self):
+        gain = np.zeros(self.n_features_in_, dtype=np.float64)
+        cnt = np.zeros(self.n_features_in_, dtype=np.int64)
+        for tf, tt, tv, tl, tr, nc, sg in self.trees:
+            for k in range(nc):
+                f = tf[k]
+                if f >= 0:
+                    gain[f] += sg[k]
+                    cnt[f] += 1
+        tot = gain.sum()
+        self.feature_importances_ = gain / tot if tot > 0 else np.zeros(self.n_features_in_)
+        self.feature_split_counts_ = cnt
+
+    # ------------------------------------------------------------------
+    # predict (E:3274-3368)
+    # ------------------------------------------------------------------
+    def _packed(self):
+        return {"features": self._packed_features, "thresholds": self._packed_thresholds,
+                "values": self._packed_values, "left": self._packed_left,
+                "right": self._packed_right, "offsets": self._tree_offsets}
+
+    def predict_proba(self, X):
+        try:
+            import scipy.sparse
+            if scipy.sparse.issparse(X):
+                X = X.toarray()
+        except ImportError:
+            pass
+        if getattr(self, 'n_features_in_', None) is None:
+            raise ValueError("This HybridHistGBMNumbaV1_0_1 instance is not fitted yet.")
+        X = np.asarray(X)
+        if not np.issubdtype(X.dtype, np.floating) or X.dtype == np.float16:
+            X = X.astype(np.float64)
+        X_bin = binning.bin_features(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id)
+        return self.predict_proba_binned(X_bin)
+
+    def predict_proba_binned(self, X_bin):
+        """``predict_proba`` on bin ids already produced with this model's edges."""
+        t0 = time.perf_counter()
+        eng = self._get_engine()
+        Xd = binning.device_bins(X_bin, self.feature_bin_counts)
+        _, proba = eng.predict(Xd, self._packed(), len(self.trees), self.learning_rate,
+                               getattr(self, 'base_score_', 0.0), want_F=False, want_proba=True)
+        self.times['inference'] = (time.perf_counter() - t0) * 1000
+        return np.column_stack([1 - proba, proba])
+
+    def predict(self, X):
+        proba = self.predict_proba(X)
+        return self.classes_[(proba[:, 1] > 0.5).astype(int)]
+
+    def production_info(self):
+        return {"engine": "libgbm_b200 (sm_100a)", "device": self.device,
+                "n_trees": self.n_trees_fitted_, "n_features": self.n_features_in_}
+
+
+def _predict_tree_host(X_bin, tree):
+    """Values of one tree for every row (host, used for the small validation set)."""
+    tf, tt, tv, tl, tr, nc, _ = tree
+    node = np.zeros(X_bin.shape[0], dtype=np.int64)
+    rows = np.arange(X_bin.shape[0])
+    while True:
+        f = tf[node]
+        act = f >= 0
+        if not act.any():
+            break
+        ff = np.where(act, f, 0)
+        go_left = X_bin[rows, ff].astype(np.int64) <= tt[node]
+        node = np.where(act, np.where(go_left, tl[node], tr[node]), node)
+    return tv[node]
+
+
+def _logloss(y, F):
+    p = 1.0 / (1.0 + np.exp(-np.clip(F, -500, 500)))
+    p = np.clip(p, 1e-15, 1 - 1e-15)
+    return -np.mean(y * np.log(p) + (1 - y) * np.log(1 - p))

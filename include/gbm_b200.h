@@ -1,0 +1,208 @@
+/*
+ * gbm_b200.h -- C ABI of libgbm_b200.so, the B200 engine behind the
+ * reference's HybridHistGBMNumbaV1_0_1 binary-logloss hot path.
+ *
+ * Plain pointers and sizes only.  Every call returns GBM_OK (0) or an error
+ * code; gbm_last_error() gives the message.  No C++ exception crosses this
+ * boundary.  The caller owns every host buffer; the context owns all device
+ * memory and communicators.  One context per host thread; calls on one
+ * context are serialised by the caller.
+ *
+ * Reference interfaces each entry point replaces (paths inside the
+ * reference project, src/bsscl_gbm/estimator_v1_0_1.py = E):
+ *   gbm_round           the loop body of _fit_binary, E:2849-2905:
+ *                       gradients (E:2861, E:2873-2874), _build_one_tree
+ *                       (E:2891 -> E:2397-2459 -> _build_tree_leafwise
+ *                       E:517-823 or _build_tree_v25 E:233-508),
+ *                       _post_prune_tree_jit (E:827-841),
+ *                       _enforce_monotonicity (E:2461-2499), the F update
+ *                       (E:2896-2897 -> predict_batch_jit E:843-861) and
+ *                       the train logloss (E:2905 -> E:2320-2325).
+ *   gbm_predict         predict_all_trees_jit (E:863-884) + the sigmoid of
+ *                       predict_proba (E:3318-3336).
+ *   gbm_sampler_*       _get_subsample_indices (E:2502-2517) on the
+ *                       RandomState(random_state) stream (E:3159).
+ */
+#ifndef GBM_B200_H
+#define GBM_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    GBM_OK = 0,
+    GBM_ERR_ARG = 1,      /* invalid argument or size */
+    GBM_ERR_ALLOC = 2,    /* host or device allocation failed */
+    GBM_ERR_CUDA = 3,     /* a CUDA runtime call or kernel failed */
+    GBM_ERR_STATE = 4,    /* call out of order (e.g. round before upload) */
+    GBM_ERR_COMM = 5,     /* NCCL communicator error */
+    GBM_ERR_TIMEOUT = 6,  /* a bounded wait ran out */
+    GBM_ERR_UNSUPPORTED = 7
+};
+
+typedef struct gbm_ctx gbm_ctx;
+typedef struct gbm_sampler gbm_sampler;
+
+/* Growth and regularisation parameters of one tree (the resolved values of
+ * the reference's constructor / adaptive hyper-parameters, E:1925-2029). */
+typedef struct {
+    double reg_lambda;        /* lambda in -G/(H+lambda) and in the gain */
+    double gamma;             /* split selection needs gain > gamma (E:646) */
+    double min_child_weight;  /* HL, HR >= mcw to split (E:610) */
+    double learning_rate;     /* F += lr * leaf value (E:2897) */
+    int32_t min_samples_leaf; /* both children need >= msl rows (E:678) */
+    int32_t max_depth;
+    int32_t max_leaves;       /* best-first stops after max_leaves-1 splits */
+    int32_t grow_policy;      /* 0 = leaf-wise best-first, 1 = depth-wise */
+    const int32_t *monotone;  /* NULL, or per-feature -1/0/+1 (E:2461-2499) */
+} gbm_params;
+
+/* One tree in the reference's tuple layout (E:528-537):
+ * features int32, thresholds int64 (bin ids), values f64, left/right int32
+ * (-1 at leaves), split gains f64.  `capacity` entries per array; the
+ * leaf-wise builder needs 2*max_leaves+2, the depth-wise one
+ * 2^(max_depth+1)-1. */
+typedef struct {
+    int32_t capacity;
+    int32_t *tf;
+    int64_t *tt;
+    double *tv;
+    int32_t *tl;
+    int32_t *tr;
+    double *sg;
+    int32_t n_nodes;          /* out: node_count */
+    int32_t *leaf_of_row;     /* optional [n]: leaf node id of every row */
+} gbm_tree_out;
+
+/* A packed ensemble, as _pack_tree_list builds it (E:2192-2216). */
+typedef struct {
+    const int16_t *features;   /* [total_nodes], -1 at leaves */
+    const int64_t *thresholds; /* [total_nodes] bin ids */
+    const double *values;      /* [total_nodes] */
+    const int32_t *left;       /* [total_nodes] tree-local ids */
+    const int32_t *right;      /* [total_nodes] */
+    const int32_t *offsets;    /* [n_trees+1] */
+    int32_t n_trees;
+} gbm_packed;
+
+/* ---- context ---------------------------------------------------------- */
+
+/* Create a context on CUDA device `device`.  Fails with GBM_ERR_CUDA when
+ * no such device exists (there is no CPU fallback). */
+int gbm_ctx_create(int32_t device, gbm_ctx **out);
+void gbm_ctx_destroy(gbm_ctx *ctx);
+const char *gbm_last_error(const gbm_ctx *ctx);
+
+/* Join an NCCL communicator of `nranks` processes (one per GPU).  `uid` is
+ * the 128-byte ncclUniqueId made by rank 0 and shared by the caller.
+ * Histograms are then summed over ranks (exact int64 words), so every rank
+ * builds the identical tree from its own row shard.  `timeout_ms` bounds
+ * communicator creation and every collective wait. */
+int gbm_ctx_init_comm(gbm_ctx *ctx, const void *uid, int32_t nranks, int32_t rank,
+                      int32_t timeout_ms);
+int gbm_nccl_unique_id(void *uid_out /* 128 bytes */);
+
+/* ---- training --------------------------------------------------------- */
+
+/* Upload this rank's rows of the binned matrix.  `xbin` is row-major
+ * uint8 [n][p]; ids >= bin_counts[j] are read as bin_counts[j]-1 (the
+ * reference clamps them the same way in its histograms, E:593-594, and no
+ * threshold can separate them, E:604).  Rows are stored column-blocked on
+ * the device ([ceil(p/16)][n][16] bytes). */
+int gbm_upload_bins(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p,
+                    const int32_t *bin_counts);
+
+/* Labels (0/1) of this rank's rows, the two class weights of
+ * _compute_class_weights (E:2570-2603) and the base score (E:2829-2835).
+ * Resets F to base_score and computes round-0 gradients.  `n_global` is the
+ * row count over all ranks (the logloss divisor; 0 = this rank's n). */
+int gbm_upload_labels(gbm_ctx *ctx, const uint8_t *y, const double class_w[2],
+                      double base_score, int64_t n_global);
+
+/* One boosting round.  `inbag_mask` [n] marks this rank's in-bag rows
+ * (the subsample); `feat_idx` [nfeat] the sorted column subsample.  Writes
+ * the pruned tree to `out`, updates F on the device and returns the train
+ * logloss over all rows of all ranks. */
+int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
+              const gbm_params *params, gbm_tree_out *out, double *train_loss);
+
+/* One tree from caller-supplied float64 gradients and hessians [n] (this
+ * rank's rows): the reference's internal seam _build_one_tree(X_bin, grad,
+ * hess, sample_idx, feat_idx, n_features) (E:2397-2459), including the
+ * post-prune and monotone clipping.  F is not touched; call
+ * gbm_upload_labels again before the next gbm_round. */
+int gbm_build_tree(gbm_ctx *ctx, const double *grad, const double *hess, const uint8_t *inbag_mask,
+                   const int32_t *feat_idx, int32_t nfeat, const gbm_params *params,
+                   gbm_tree_out *out);
+
+/* Fixed-point exponent S of the current fit: every g and h is rounded once
+ * to the grid 2^-S and all sums are exact integer sums. */
+int32_t gbm_scale_bits(const gbm_ctx *ctx);
+
+/* Copy device state to the host (for parity checks): F [n], and the f64
+ * gradient/hessian of the NEXT round's inputs [n]. */
+int gbm_get_F(gbm_ctx *ctx, double *F_out);
+int gbm_get_grad(gbm_ctx *ctx, double *g_out, double *h_out);
+
+/* ---- predict ---------------------------------------------------------- */
+
+/* F[i] = base + sum_t lr * values[leaf_t(i)] and proba = sigmoid(clip(F))
+ * for row-major uint8 bins [n][p].  Either output may be NULL. */
+int gbm_predict(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p,
+                const gbm_packed *model, double learning_rate, double base_score,
+                double *F_out, double *proba_out);
+
+/* Device-resident predict: upload the ensemble and the bins once, then run
+ * on the device copies (outputs stay on the device until fetched). */
+int gbm_predict_set_model(gbm_ctx *ctx, const gbm_packed *model, int32_t n_features);
+int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p);
+int gbm_predict_run(gbm_ctx *ctx, double learning_rate, double base_score);
+int gbm_predict_fetch(gbm_ctx *ctx, double *F_out, double *proba_out);
+
+/* Synchronise the context's stream; returns the first asynchronous error. */
+int gbm_sync(gbm_ctx *ctx);
+
+/* ---- instrumentation -------------------------------------------------- */
+
+typedef struct {
+    int64_t kernel_launches;   /* every kernel this context launched */
+    int64_t hist_launches;     /* histogram kernel launches */
+    int64_t hist_rows;         /* rows the histogram kernel read */
+    int64_t waves;             /* batched node expansions */
+    double hist_ms;            /* summed CUDA-event time of the histogram
+                                  launches (only while profiling is on) */
+    double hist_alg_bytes;     /* algorithmic bytes of the histograms the
+                                  reference builds: rows x (nfeat + 8) of the
+                                  root and of the smaller child of every
+                                  executed split */
+} gbm_stats;
+
+int gbm_set_profiling(gbm_ctx *ctx, int32_t on);
+int gbm_get_stats(gbm_ctx *ctx, gbm_stats *out);
+int gbm_reset_stats(gbm_ctx *ctx);
+/* CUDA events on the context's stream (slots 0..15), for timing regions. */
+int gbm_event_record(gbm_ctx *ctx, int32_t slot);
+int gbm_event_elapsed(gbm_ctx *ctx, int32_t a, int32_t b, float *ms);
+
+/* ---- sampler (host) --------------------------------------------------- */
+
+/* The reference's RandomState(seed) row/feature subsample stream
+ * (E:2502-2517): every call reproduces the next round's sample_idx (first
+ * n_sub of the cumulatively shuffled arange(n)) and sorted feat_idx.
+ * `look_ahead` > 0 runs that many rounds ahead on a host thread. */
+int gbm_sampler_create(uint32_t seed, int64_t n, int32_t p, int64_t n_sub, int32_t n_feat,
+                       int32_t subsample_on, int32_t colsample_on, int32_t look_ahead,
+                       gbm_sampler **out);
+/* Any output may be NULL: sample_idx [n_sub] (reference order),
+ * inbag_mask [n] (1 = in bag), feat_idx [n_feat]. */
+int gbm_sampler_next(gbm_sampler *s, int64_t *sample_idx, uint8_t *inbag_mask, int32_t *feat_idx);
+void gbm_sampler_destroy(gbm_sampler *s);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GBM_B200_H */

@@ -1,0 +1,254 @@
+"""ctypes bindings and a boosting driver for the CPU oracle (liboracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU legs as the checker.  The product package never imports it.
+
+``fit_binary`` restates the reference's binary boosting loop
+(src/bsscl_gbm/estimator_v1_0_1.py, ``_fit_binary`` E:2825-2944) around the
+C builders: class weights (E:2570-2603), weighted-mean base score
+(E:2829-2835), p = sigmoid(clip(F)) / g / h (E:2861, E:2873-2874), the
+cumulative ``RandomState.shuffle`` sampler (E:2502-2517, using NumPy's own
+legacy generator), tree build + post-prune (E:2397-2459), the F update
+``F += lr * tree(X)`` (E:2896-2897) and the train logloss (E:2905).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+MODE_REF = 0
+MODE_EXACT = 1
+
+_lib = None
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        P = C.c_void_p
+        i32, i64, f64 = C.c_int32, C.c_int64, C.c_double
+        L.or_bin_matrix.argtypes = [P, i64, i32, P, i32, P, P, i32, i32, P]
+        L.or_build_leafwise.argtypes = [P, i64, i32, P, P, P, i64, P, i32, P, i32, i32, i32,
+                                        i32, f64, f64, f64, i32, i32, P, P, P, P, P, P, P]
+        L.or_build_depthwise.argtypes = [P, i64, i32, P, P, P, i64, P, i32, P, i32, i32, i32,
+                                         f64, f64, f64, i32, i32, P, P, P, P, P, P, P]
+        L.or_post_prune.argtypes = [P, P, P, P, f64, i32]
+        L.or_leaf_ids.argtypes = [P, i64, i32, P, P, P, P, P]
+        L.or_predict_packed.argtypes = [P, i64, i32, P, P, P, P, P, P, i32, f64, P]
+        L.or_grad_hess.argtypes = [P, P, P, i64, P, P]
+        L.or_logloss.argtypes = [P, P, i64]
+        L.or_logloss.restype = C.c_double
+        L.or_num_threads.restype = C.c_int
+        L.or_i128_to_double.argtypes = [C.c_int64, C.c_uint64]
+        L.or_i128_to_double.restype = C.c_double
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def i128_to_double(v):
+    """The oracle's conversion of a Python int in [-2^127, 2^127) to float64."""
+    hi = v >> 64
+    lo = v & ((1 << 64) - 1)
+    return lib().or_i128_to_double(hi, lo)
+
+
+def num_threads():
+    return lib().or_num_threads()
+
+
+def bin_matrix(X, edges, counts, nan_bin_id, hybrid):
+    X = np.ascontiguousarray(X, dtype=np.float64)
+    n, p = X.shape
+    edges = np.ascontiguousarray(edges, dtype=np.float64)
+    counts = np.ascontiguousarray(counts, dtype=np.int32)
+    nan_bin_id = np.ascontiguousarray(nan_bin_id, dtype=np.int32)
+    out = np.empty((n, p), dtype=np.uint16)
+    has_any = int(np.any(nan_bin_id >= 0))
+    lib().or_bin_matrix(_p(X), n, p, _p(edges), edges.shape[1], _p(counts), _p(nan_bin_id),
+                        has_any, int(bool(hybrid)), _p(out))
+    return out
+
+
+def build_tree(X_bin, g, h, sample_idx, feat_idx, counts, *, max_leaves=63, max_depth=6,
+               msl=5, mcw=1.0, lam=1.0, gamma=0.0, mode=MODE_REF, scale_bits=0,
+               policy="leaf"):
+    """One tree.  Returns ``(tf, tt, tv, tl, tr, nc, sg)`` like the reference."""
+    Xb = np.ascontiguousarray(X_bin, dtype=np.uint16)
+    n, p = Xb.shape
+    g = np.ascontiguousarray(g, dtype=np.float64)
+    h = np.ascontiguousarray(h, dtype=np.float64)
+    sidx = np.ascontiguousarray(sample_idx, dtype=np.int64)
+    fidx = np.ascontiguousarray(feat_idx, dtype=np.int32)
+    counts = np.ascontiguousarray(counts, dtype=np.int32)
+    max_bins = int(counts.max())
+    if policy == "leaf":
+        M = 2 * max_leaves + 2
+    else:
+        M = (1 << (max_depth + 1)) - 1
+    tf = np.empty(M, np.int32); tt = np.empty(M, np.int64); tv = np.empty(M, np.float64)
+    tl = np.empty(M, np.int32); tr = np.empty(M, np.int32); sg = np.empty(M, np.float64)
+    nc = C.c_int32(0)
+    if policy == "leaf":
+        rc = lib().or_build_leafwise(_p(Xb), n, p, _p(g), _p(h), _p(sidx), len(sidx), _p(fidx),
+                                     len(fidx), _p(counts), max_bins, max_leaves, max_depth,
+                                     msl, mcw, lam, gamma, mode, scale_bits, _p(tf), _p(tt),
+                                     _p(tv), _p(tl), _p(tr), _p(sg), C.byref(nc))
+    else:
+        rc = lib().or_build_depthwise(_p(Xb), n, p, _p(g), _p(h), _p(sidx), len(sidx),
+                                      _p(fidx), len(fidx), _p(counts), max_bins, max_depth,
+                                      msl, mcw, lam, gamma, mode, scale_bits, _p(tf), _p(tt),
+                                      _p(tv), _p(tl), _p(tr), _p(sg), C.byref(nc))
+    if rc != 0:
+        raise MemoryError("oracle builder failed to allocate")
+    return tf, tt, tv, tl, tr, int(nc.value), sg
+
+
+def post_prune(tf, tl, tr, sg, gamma, nc):
+    lib().or_post_prune(_p(tf), _p(tl), _p(tr), _p(sg), float(gamma), int(nc))
+
+
+def leaf_ids(X_bin, tf, tt, tl, tr):
+    Xb = np.ascontiguousarray(X_bin, dtype=np.uint16)
+    n, p = Xb.shape
+    out = np.empty(n, np.int32)
+    lib().or_leaf_ids(_p(Xb), n, p, _p(np.ascontiguousarray(tf, np.int32)),
+                      _p(np.ascontiguousarray(tt, np.int64)), _p(np.ascontiguousarray(tl, np.int32)),
+                      _p(np.ascontiguousarray(tr, np.int32)), _p(out))
+    return out
+
+
+def predict_packed(X_bin, packed, n_trees, lr):
+    Xb = np.ascontiguousarray(X_bin, dtype=np.uint16)
+    n, p = Xb.shape
+    F = np.empty(n, np.float64)
+    a = {k: np.ascontiguousarray(v) for k, v in packed.items()}
+    lib().or_predict_packed(_p(Xb), n, p, _p(a["features"].astype(np.int16)),
+                            _p(a["thresholds"].astype(np.int64)), _p(a["values"].astype(np.float64)),
+                            _p(a["left"].astype(np.int32)), _p(a["right"].astype(np.int32)),
+                            _p(a["offsets"].astype(np.int32)), int(n_trees), float(lr), _p(F))
+    return F
+
+
+def grad_hess(F, y01, w2):
+    F = np.ascontiguousarray(F, np.float64)
+    y = np.ascontiguousarray(y01, np.uint8)
+    w2 = np.ascontiguousarray(w2, np.float64)
+    g = np.empty_like(F); h = np.empty_like(F)
+    lib().or_grad_hess(_p(F), _p(y), _p(w2), len(F), _p(g), _p(h))
+    return g, h
+
+
+def logloss(F, y01):
+    F = np.ascontiguousarray(F, np.float64)
+    y = np.ascontiguousarray(y01, np.uint8)
+    return lib().or_logloss(_p(F), _p(y), len(F))
+
+
+# ----------------------------------------------------------------------------
+# Boosting driver
+# ----------------------------------------------------------------------------
+
+def class_weights(y01, class_weight, scale_pos_weight=None, objective="auto"):
+    """Per-class weights ``w[2]`` (E:2570-2603).  ``scale_pos_weight`` only acts
+    when ``objective == 'binary'`` (E:2572)."""
+    n = len(y01)
+    if scale_pos_weight is not None and objective == "binary":
+        return np.array([1.0, float(scale_pos_weight)])
+    if class_weight not in ("balanced", "balanced_sqrt"):
+        return np.array([1.0, 1.0])
+    w = np.ones(2)
+    for k in range(2):
+        nk = int(np.sum(y01 == k))
+        wk = n / (2 * max(nk, 1))
+        if class_weight == "balanced_sqrt":
+            wk = wk ** 0.35
+        w[k] = wk
+    return w
+
+
+def base_score(y01, w2):
+    sw = w2[y01]
+    p0 = np.clip(np.average(y01, weights=sw), 1e-7, 1.0 - 1e-7)
+    return float(np.log(p0 / (1.0 - p0)))
+
+
+def fit_binary(X_bin, y01, counts, *, n_estimators, learning_rate, max_leaves, max_depth,
+               min_samples_leaf, min_child_weight, reg_lambda, gamma, subsample,
+               colsample, class_weight, random_state, mode=MODE_REF, scale_bits=None,
+               grow_policy="leaf", record=None):
+    """The reference's ``_fit_binary`` loop on the oracle builders.
+
+    ``scale_bits=None`` in MODE_EXACT picks S per round the way the engine
+    does (``engine_scale_bits``).  Returns a dict with trees, base score,
+    final F and the train-loss history.
+    """
+    y01 = np.asarray(y01).astype(np.int64)
+    n, p = X_bin.shape
+    w2 = class_weights(y01, class_weight)
+    base = base_score(y01, w2)
+    F = np.full(n, base)
+    n_sub = max(1, int(n * subsample))
+    n_feat = max(1, int(p * colsample))
+    rng = np.random.RandomState(random_state)
+    all_r = np.arange(n, dtype=np.int64)
+    all_f = np.arange(p, dtype=np.int32)
+    trees, losses = [], []
+    y8 = y01.astype(np.uint8)
+    for m in range(n_estimators):
+        g, h = grad_hess(F, y8, w2)
+        if subsample < 1.0:
+            rng.shuffle(all_r)
+            sidx = all_r[:n_sub].copy()
+        else:
+            sidx = all_r.copy()
+        if colsample < 1.0:
+            rng.shuffle(all_f)
+            fidx = np.sort(all_f[:n_feat]).copy()
+        else:
+            fidx = all_f.copy()
+        S = scale_bits
+        if mode == MODE_EXACT and S is None:
+            S = engine_scale_bits(len(sidx), w2)
+        t = build_tree(X_bin, g, h, sidx, fidx, counts, max_leaves=max_leaves,
+                       max_depth=max_depth, msl=min_samples_leaf, mcw=min_child_weight,
+                       lam=reg_lambda, gamma=gamma, mode=mode, scale_bits=S or 0,
+                       policy=grow_policy)
+        tf, tt, tv, tl, tr, nc, sg = t
+        post_prune(tf, tl, tr, sg, gamma, nc)
+        if record is not None:
+            record.append(dict(g=g, h=h, sample=sidx, feat=fidx))
+        leaf = leaf_ids(X_bin, tf, tt, tl, tr)
+        F = F + learning_rate * tv[leaf]
+        losses.append(logloss(F, y8))
+        trees.append((tf, tt, tv, tl, tr, nc, sg))
+    return dict(trees=trees, base_score=base, F=F, train_loss=np.array(losses), w2=w2)
+
+
+def engine_scale_bits(n_rows, w2, word_bits=126):
+    """Fixed-point exponent S the CUDA engine uses for a round.
+
+    Every |g| <= max(w) and every h <= max(w)/4, so with
+    ``S = word_bits - 1 - ceil(log2(n_rows * max(w)))`` no partial sum of
+    ``n_rows`` quantised values can reach 2^(word_bits-1).
+    """
+    wmax = float(np.max(w2))
+    need = int(np.ceil(np.log2(max(1.0, n_rows * wmax)))) + 1
+    return word_bits - 1 - need

@@ -1,0 +1,186 @@
+"""CUDA engine parity, through the C ABI (libgbm_b200.so), on a B200.
+
+* gbm_build_tree on every golden tree case == the oracle's EXACT builder,
+  bit for bit (topology, values, gains), and == the reference's topology.
+* gbm_round, round after round: tree == oracle EXACT on the engine's own
+  gradients (bit for bit), per-row leaf ids, F update and train loss.
+* Full fits through the estimator vs the reference's recorded fits:
+  identical trees until a divergence, which must be an exact tie; leaf
+  values and predict_proba within 1e-6.
+* Predict on a packed ensemble vs the reference's predict_all_trees_jit.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import audit as A
+import oracle as O
+from conftest import GOLDEN
+from helpers import fit_inputs, fit_params, golden, golden_trees, same_topology
+
+pytestmark = pytest.mark.gpu
+
+TREE_CASES = sorted(os.path.basename(f)[5:-4] for f in glob.glob(os.path.join(GOLDEN, "tree_*.npz")))
+
+
+def _params(max_leaves=63, max_depth=6, msl=5, mcw=1.0, lam=1.0, gamma=0.0, lr=0.1, policy="leaf"):
+    from bsscl_gbm_b200 import GbmParams
+    return GbmParams(float(lam), float(gamma), float(mcw), float(lr), int(msl), int(max_depth),
+                     int(max_leaves), 0 if policy == "leaf" else 1, None)
+
+
+def _cap(max_leaves, max_depth, policy):
+    return 2 * max_leaves + 2 if policy == "leaf" else (1 << (max_depth + 1)) - 1
+
+
+def _assert_tree_equal(a, b, what=""):
+    nc = a[5]
+    assert nc == b[5], f"{what}: node count {nc} vs {b[5]}"
+    for i, k in [(0, "tf"), (1, "tt"), (2, "tv"), (3, "tl"), (4, "tr"), (6, "sg")]:
+        x, y = np.asarray(a[i])[:nc], np.asarray(b[i])[:nc]
+        assert np.array_equal(x, y), f"{what}: {k} differs at {np.nonzero(x != y)[0][:5]}"
+
+
+@pytest.mark.parametrize("case", TREE_CASES)
+def test_build_tree_matches_oracle_exact(engine, case):
+    from bsscl_gbm_b200 import binning
+    d = golden("tree_" + case)
+    counts = d["counts"]
+    Xb = d["X_bin"]
+    n = Xb.shape[0]
+    engine.upload_bins(binning.device_bins(Xb, counts), counts)
+    mask = np.zeros(n, np.uint8)
+    mask[d["sample_idx"]] = 1
+    pol = str(d["policy"])
+    kw = dict(max_leaves=int(d["max_leaves"]), max_depth=int(d["max_depth"]), msl=int(d["msl"]),
+              mcw=float(d["mcw"]), lam=float(d["lam"]), gamma=float(d["gamma"]))
+    t = engine.build_tree(d["g"], d["h"], mask, d["feat_idx"], _params(policy=pol, **kw),
+                          _cap(kw["max_leaves"], kw["max_depth"], pol))
+    S = engine.scale_bits()
+    o = O.build_tree(Xb, d["g"], d["h"], d["sample_idx"], d["feat_idx"], counts, mode=O.MODE_EXACT,
+                     scale_bits=S, policy=pol, **kw)
+    O.post_prune(o[0], o[3], o[4], o[6], kw["gamma"], o[5])
+    _assert_tree_equal(t, o, case)
+    ref = (d["tf_pruned"], d["tt"], d["tv"], d["tl_pruned"], d["tr_pruned"], int(d["nc"]), d["sg"])
+    assert same_topology(t, ref)
+    nc = t[5]
+    assert np.abs(t[2][:nc] - d["tv"][:nc]).max() <= 1e-9
+
+
+def test_build_tree_empty_inbag(engine):
+    """No in-bag rows: the root is a leaf with value -0/(0+lambda), like the reference."""
+    from bsscl_gbm_b200 import binning
+    d = golden("tree_basic")
+    engine.upload_bins(binning.device_bins(d["X_bin"], d["counts"]), d["counts"])
+    mask = np.zeros(d["X_bin"].shape[0], np.uint8)
+    t = engine.build_tree(d["g"], d["h"], mask, d["feat_idx"], _params(), 128)
+    assert t[5] == 1 and t[0][0] == -1 and t[2][0] == 0.0
+
+
+def _cfg1_engine(engine, n=10_000):
+    from bsscl_gbm_b200 import binning
+    d = golden("fit_cfg1")
+    X, y, _ = fit_inputs("cfg1")
+    Xb = binning.bin_features(X, d["edges"], d["counts"], d["nan_bin_id"])
+    w2 = O.class_weights(y, None)
+    base = O.base_score(y, w2)
+    engine.upload_bins(binning.device_bins(Xb, d["counts"]), d["counts"])
+    engine.upload_labels(y.astype(np.uint8), w2, base, n_global=len(y))
+    return d, Xb, y, w2, base
+
+
+@pytest.mark.parametrize("policy", ["leaf", "level"])
+def test_rounds_match_oracle_exact(engine, policy):
+    from bsscl_gbm_b200 import Sampler
+    d, Xb, y, w2, base = _cfg1_engine(engine)
+    n, p = Xb.shape
+    lr = 0.1
+    kw = dict(max_leaves=31, max_depth=6 if policy == "leaf" else 5, msl=5, mcw=2.0, lam=1.0,
+              gamma=0.0)
+    prm = _params(lr=lr, policy=policy, **kw)
+    cap = _cap(kw["max_leaves"], kw["max_depth"], policy)
+    s = Sampler(0, n, p, int(n * 0.8), int(p * 0.8), True, True)
+    F_prev = engine.get_F()
+    assert np.all(F_prev == base)
+    S = engine.scale_bits()
+    y8 = y.astype(np.uint8)
+    for r in range(6):
+        g, h = engine.get_grad()
+        og, oh = O.grad_hess(F_prev, y8, w2)
+        # CUDA's exp and the C library's differ by at most an ulp or two
+        assert np.abs(g - og).max() <= 1e-14 and np.abs(h - oh).max() <= 1e-14
+        smp, mask, feat = s.next(want_sample=True, want_mask=True)
+        tree, loss, leaf = engine.round(mask, feat, prm, cap, want_leaf=True)
+        o = O.build_tree(Xb, g, h, smp, feat, d["counts"], mode=O.MODE_EXACT, scale_bits=S,
+                         policy=policy, **kw)
+        O.post_prune(o[0], o[3], o[4], o[6], kw["gamma"], o[5])
+        _assert_tree_equal(tree, o, f"round {r}")
+        nc = tree[5]
+        assert np.array_equal(leaf, O.leaf_ids(Xb, tree[0][:nc], tree[1][:nc], tree[3][:nc],
+                                               tree[4][:nc]))
+        F = engine.get_F()
+        assert np.array_equal(F, F_prev + lr * tree[2][leaf])
+        assert abs(loss - O.logloss(F, y8)) <= 1e-12 * max(1.0, abs(loss))
+        F_prev = F
+    s.close()
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg1_level", "cfg2_small", "cfg3_small", "cfg4_small"])
+def test_fit_matches_reference(name):
+    """The estimator on the GPU vs the reference's own recorded fit."""
+    from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
+    d = golden("fit_" + name)
+    X, y, Xte = fit_inputs(name)
+    m = M(verbose=False, **fit_params(d)).fit(X, y)
+    assert m.base_score_ == float(d["base_score"])
+    ref = golden_trees(d)
+    assert len(m.trees) == len(ref)
+    div = A.first_divergence(ref, m.trees)
+    upto = len(ref) if div is None else div[0]
+    for t in range(upto):
+        nc = ref[t][5]
+        assert np.abs(m.trees[t][2][:nc] - ref[t][2][:nc]).max() <= 1e-6, f"values tree {t}"
+    if div is None:
+        assert np.abs(m.predict_proba(Xte) - d["proba_test"]).max() <= 1e-6
+        assert np.abs(np.array(m.train_loss_history_) - d["train_loss"]).max() <= 1e-9
+        return
+    # a divergence must be an exact tie of the reference's own round inputs
+    t = div[0]
+    assert f"r{t}_g" in d.files, f"divergence at tree {t} beyond the recorded rounds"
+    from bsscl_gbm_b200 import binning
+    Xb = binning.bin_features(X, d["edges"], d["counts"], d["nan_bin_id"])
+    res = A.audit_node(Xb, d[f"r{t}_g"], d[f"r{t}_h"], d[f"r{t}_sample"], d["counts"], ref[t],
+                       m.trees[t], div[1], float(d["reg_lambda"]), float(d["min_child_weight"]))
+    assert A.explained(res), res
+
+
+def test_fit_is_deterministic():
+    from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
+    X, y, Xte = fit_inputs("cfg3_small")
+    kw = dict(n_estimators=8, max_depth=6, class_weight="balanced_sqrt", n_bins=255,
+              random_state=5, verbose=False)
+    a = M(**kw).fit(X, y)
+    b = M(**kw).fit(X, y)
+    for ta, tb in zip(a.trees, b.trees):
+        _assert_tree_equal(ta, tb)
+    assert np.array_equal(a.predict_proba(Xte), b.predict_proba(Xte))
+
+
+def test_predict_matches_reference_ensemble(engine):
+    d = golden("predict_ensemble")
+    packed = {k: d[k] for k in ("features", "thresholds", "values", "left", "right", "offsets")}
+    F, P = engine.predict(d["X_bin"].astype(np.uint8), packed, 40, float(d["lr"]), 0.0)
+    assert np.abs(F - d["F"]).max() <= 1e-12
+    assert np.abs(P - 1.0 / (1.0 + np.exp(-d["F"]))).max() <= 1e-12
+
+
+def test_predict_proba_matches_oracle_random_forest(engine):
+    """A larger random ensemble (full depth-8 trees) against the oracle."""
+    from bsscl_gbm_b200 import datasets as D
+    ens = D.config5_ensemble(n_trees=60, depth=8, p=40, seed=9)
+    Xb = np.random.default_rng(9).integers(0, 255, size=(50_000, 40)).astype(np.uint8)
+    F, _ = engine.predict(Xb, ens, 60, 0.08, -1.5, want_proba=False)
+    Fo = O.predict_packed(Xb, ens, 60, 0.08) + (-1.5)
+    assert np.abs(F - Fo).max() <= 1e-12

@@ -1,0 +1,164 @@
+"""Host-side logic that needs no GPU: binning, sampler, the C-ABI library's
+exports, estimator argument handling, and that nothing falls back to a CPU
+path when no device is present."""
+import glob
+import hashlib
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, ROOT
+from helpers import fit_inputs, golden
+
+
+@pytest.mark.parametrize("case", sorted(os.path.basename(f)[:-4]
+                                        for f in glob.glob(os.path.join(GOLDEN, "bin_*.npz"))))
+def test_host_edges_and_bins_match_reference(case):
+    from bsscl_gbm_b200 import binning
+    d = golden(case)
+    e, c, nb = binning.build_bin_edges(d["X"], int(d["n_bins"]))
+    assert np.array_equal(e, d["edges"])
+    assert np.array_equal(c, d["counts"])
+    assert np.array_equal(nb, d["nan_bin_id"])
+    Xb = binning.bin_features(d["X"], d["edges"], d["counts"], d["nan_bin_id"])
+    assert np.array_equal(Xb, d["X_bin"])
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg2_small", "cfg3_small", "cfg4_small"])
+def test_host_binning_of_fit_inputs(name):
+    from bsscl_gbm_b200 import binning
+    d = golden("fit_" + name)
+    X, _, _ = fit_inputs(name)
+    e, c, nb = binning.build_bin_edges(X, int(d["n_bins"]))
+    assert np.array_equal(e, d["edges"]) and np.array_equal(c, d["counts"])
+    Xb = binning.bin_features(X, e, c, nb)
+    assert hashlib.sha256(Xb.astype(np.uint16).tobytes()).hexdigest() == str(d["X_bin_sha"])
+
+
+def test_device_bins_clamp_is_lossless():
+    """ids >= bin_count (the float32 max-edge quirk) clamp to bin_count-1."""
+    import oracle as O
+    from bsscl_gbm_b200 import binning
+    rng = np.random.default_rng(3)
+    X = rng.integers(0, 7, size=(2000, 3)).astype(np.float32)    # few levels, float32
+    X[rng.random((2000, 3)) < 0.2] = np.nan                        # NaN bin on every column
+    e, counts, nb = binning.build_bin_edges(X, 255)
+    raw = binning.bin_features(X, e, counts, nb)
+    assert np.array_equal(raw, O.bin_matrix(X, e, counts, nb, False))
+    assert (raw >= counts[None, :]).any()           # the quirk is present
+    dev = binning.device_bins(raw, counts)
+    assert dev.dtype == np.uint8
+    assert np.array_equal(dev, np.minimum(raw, counts - 1))
+    # every threshold the reference can pick (<= nb-2) routes raw and clamped ids alike
+    for j in range(raw.shape[1]):
+        for thr in range(max(0, counts[j] - 1)):
+            assert np.array_equal(raw[:, j] <= thr, dev[:, j] <= thr)
+
+
+def test_sampler_matches_numpy_randomstate(built_lib):
+    from bsscl_gbm_b200 import Sampler
+    d = np.load(os.path.join(GOLDEN, "sampler.npz"))
+    for seed, n, p, frac, fc, rounds in [(0, 1000, 30, 0.8, 0.8, 5), (7, 70000, 100, 0.75, 0.7, 3),
+                                         (4294967295, 17, 3, 0.5, 0.5, 4)]:
+        ns, nf = max(1, int(n * frac)), max(1, int(p * fc))
+        for ahead in (0, 2):
+            s = Sampler(seed, n, p, ns, nf, True, True, look_ahead=ahead)
+            for r in range(rounds):
+                smp, mask, feat = s.next(want_sample=True, want_mask=True)
+                assert np.array_equal(smp, d[f"s{seed}_n{n}_r{r}_sample"])
+                assert np.array_equal(feat, d[f"s{seed}_n{n}_r{r}_feat"])
+                assert mask.sum() == ns and mask[smp].all()
+            s.close()
+
+
+def test_sampler_matches_fit_stream(built_lib):
+    """The per-round sample hashes the reference recorded during its fit."""
+    from bsscl_gbm_b200 import Sampler
+    d = golden("fit_cfg1")
+    n = 10_000
+    s = Sampler(0, n, 30, int(n * float(d["subsample"])), int(30 * float(d["colsample"])), True, True)
+    for t in range(int(d["n_trees"])):
+        smp, _, _ = s.next(want_sample=True, want_mask=False)
+        assert hashlib.sha256(smp.tobytes()).hexdigest() == str(d["sample_sha"][t])
+    s.close()
+
+
+def test_library_exports_every_declared_symbol(built_lib):
+    import ctypes
+    from bsscl_gbm_b200 import _lib
+    hdr = open(os.path.join(ROOT, "include", "gbm_b200.h")).read()
+    declared = set(re.findall(r"\b(gbm_[A-Za-z0-9_]+)\s*\(", hdr))
+    assert declared, "no declarations parsed"
+    L = ctypes.CDLL(built_lib)
+    missing = [s for s in sorted(declared) if not hasattr(L, s)]
+    assert not missing, missing
+    assert declared == set(_lib.EXPORTS)
+
+
+def test_no_device_raises_instead_of_falling_back(built_lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from bsscl_gbm_b200 import Engine, HybridHistGBMNumbaV1_0_1
+    with pytest.raises(RuntimeError):
+        Engine(0)
+    X = np.random.default_rng(0).standard_normal((200, 4))
+    y = (X[:, 0] > 0).astype(int)
+    with pytest.raises(RuntimeError):
+        HybridHistGBMNumbaV1_0_1(n_estimators=2, verbose=False, random_state=0).fit(X, y)
+
+
+def test_estimator_argument_errors():
+    from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
+    X = np.random.default_rng(0).standard_normal((100, 5))
+    y = np.random.default_rng(1).integers(0, 2, 100)
+    with pytest.raises(ValueError):
+        M(max_depth=-5, verbose=False).fit(X, y)
+    with pytest.raises(ValueError):
+        M(learning_rate=-0.1, verbose=False).fit(X, y)
+    with pytest.raises(ValueError):
+        M(n_estimators=0, verbose=False).fit(X, y)
+    with pytest.raises(ValueError):
+        M(verbose=False).fit(X, y[:99])
+    with pytest.raises(ValueError):
+        M(verbose=False).predict(X)
+    with pytest.raises(ValueError):
+        M(device="cpu")
+    with pytest.raises(NotImplementedError):
+        M(objective="regression", verbose=False).fit(X, y)
+    with pytest.raises(NotImplementedError):
+        M(sampling_method="goss", verbose=False).fit(X, y)
+    with pytest.raises(NotImplementedError):
+        M(verbose=False).fit(X, np.arange(100) % 3)
+
+
+def test_adaptive_hyperparameters_follow_reference():
+    """'auto' resolution, checked against the values the reference recorded."""
+    from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
+    for name in ("cfg1", "cfg2_small", "cfg3_small", "cfg4_small"):
+        d = golden("fit_" + name)
+        X, y, _ = fit_inputs(name)
+        from helpers import fit_params
+        m = M(verbose=False, **fit_params(d))
+        m._compute_adaptive_hyperparameters(X, y)
+        assert m.learning_rate == float(d["learning_rate"])
+        assert m.max_leaves == int(d["max_leaves"])
+        assert m.max_depth == int(d["max_depth"])
+        assert m.min_child_weight == float(d["min_child_weight"])
+        assert m.subsample == float(d["subsample"])
+        assert m.colsample_bytree == float(d["colsample"])
+        assert m.reg_lambda == float(d["reg_lambda"])
+        assert m.binning_strategy == str(d["binning_strategy"])
+
+
+def test_get_set_params_roundtrip():
+    from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
+    m = M(n_estimators=7, max_depth=3, verbose=False)
+    p = m.get_params()
+    assert p["n_estimators"] == 7 and p["max_depth"] == 3 and p["device"] == "b200"
+    m.set_params(learning_rate=0.3)
+    assert m.learning_rate == 0.3
+    with pytest.raises(ValueError):
+        m.set_params(bogus=1)

@@ -1,0 +1,143 @@
+"""The CPU oracle pinned against the reference's own outputs (tests/golden).
+
+REF mode must reproduce the reference bit-for-bit (trees, values, gains,
+bins, sampler-driven fits).  EXACT mode (the engine's arithmetic) must give
+the same topology wherever the reference's choice is not an exact tie, and
+every divergence must be explained by the exact-rational tie audit.
+"""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import audit as A
+import oracle as O
+from conftest import GOLDEN
+from helpers import (engine_scale_bits, fit_inputs, golden, golden_trees, oracle_fit_kwargs,
+                     same_topology)
+
+TREE_CASES = sorted(os.path.basename(f)[5:-4] for f in glob.glob(os.path.join(GOLDEN, "tree_*.npz")))
+BIN_CASES = sorted(os.path.basename(f)[:-4] for f in glob.glob(os.path.join(GOLDEN, "bin_*.npz")))
+
+
+def _tree_kwargs(d):
+    return dict(max_leaves=int(d["max_leaves"]), max_depth=int(d["max_depth"]), msl=int(d["msl"]),
+                mcw=float(d["mcw"]), lam=float(d["lam"]), gamma=float(d["gamma"]),
+                policy=str(d["policy"]))
+
+
+@pytest.mark.parametrize("case", TREE_CASES)
+def test_ref_builder_bit_exact(case):
+    d = golden("tree_" + case)
+    tf, tt, tv, tl, tr, nc, sg = O.build_tree(d["X_bin"], d["g"], d["h"], d["sample_idx"],
+                                              d["feat_idx"], d["counts"], **_tree_kwargs(d))
+    assert nc == int(d["nc"])
+    for a, k in [(tf, "tf"), (tt, "tt"), (tv, "tv"), (tl, "tl"), (tr, "tr"), (sg, "sg")]:
+        assert np.array_equal(a, d[k]), k
+    O.post_prune(tf, tl, tr, sg, float(d["gamma"]), nc)
+    assert np.array_equal(tf, d["tf_pruned"])
+    leaf = O.leaf_ids(d["X_bin"], tf[:nc], tt[:nc], tl[:nc], tr[:nc])
+    assert np.array_equal(leaf, d["leaf_of_row"])
+
+
+@pytest.mark.parametrize("case", TREE_CASES)
+def test_exact_builder_topology(case):
+    d = golden("tree_" + case)
+    m = max(np.abs(d["g"]).max(), np.abs(d["h"]).max())
+    S = engine_scale_bits(m)
+    t = O.build_tree(d["X_bin"], d["g"], d["h"], d["sample_idx"], d["feat_idx"], d["counts"],
+                     mode=O.MODE_EXACT, scale_bits=S, **_tree_kwargs(d))
+    ref = (d["tf"], d["tt"], d["tv"], d["tl"], d["tr"], int(d["nc"]), d["sg"])
+    if not same_topology(t, ref):
+        div = A.first_divergence([ref], [t])
+        res = A.audit_node(d["X_bin"], d["g"], d["h"], d["sample_idx"], d["counts"], ref, t,
+                           div[1], float(d["lam"]), float(d["mcw"]))
+        assert A.explained(res), res
+    else:
+        nc = t[5]
+        assert np.abs(t[2][:nc] - d["tv"][:nc]).max() < 1e-9
+
+
+@pytest.mark.parametrize("case", BIN_CASES)
+def test_ref_binning_bit_exact(case):
+    d = golden(case)
+    Xb = O.bin_matrix(d["X"], d["edges"], d["counts"], d["nan_bin_id"], str(d["strategy"]) == "hybrid")
+    assert np.array_equal(Xb, d["X_bin"])
+
+
+def test_ref_predict_ensemble():
+    d = golden("predict_ensemble")
+    packed = {k: d[k] for k in ("features", "thresholds", "values", "left", "right", "offsets")}
+    F = O.predict_packed(d["X_bin"], packed, 40, float(d["lr"]))
+    assert np.abs(F - d["F"]).max() < 1e-12
+
+
+def _binned(name, d):
+    from bsscl_gbm_b200 import binning
+    X, y, _ = fit_inputs(name)
+    Xb = O.bin_matrix(X, d["edges"], d["counts"], d["nan_bin_id"],
+                      str(d["binning_strategy"]) == "hybrid")
+    return Xb, y
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg1_level", "cfg2_small", "cfg3_small", "cfg4_small"])
+def test_ref_fit_bit_exact(name):
+    """The oracle's boosting loop (NumPy sampler + REF builder) == the reference's fit."""
+    d = golden("fit_" + name)
+    Xb, y = _binned(name, d)
+    import hashlib
+    assert hashlib.sha256(Xb.astype(np.uint16).tobytes()).hexdigest() == str(d["X_bin_sha"])
+    rec = []
+    r = O.fit_binary(Xb, y, d["counts"], mode=O.MODE_REF, record=rec, **oracle_fit_kwargs(d))
+    assert r["base_score"] == float(d["base_score"])
+    for t, (a, b) in enumerate(zip(r["trees"], golden_trees(d))):
+        assert same_topology(a, b), f"tree {t}"
+        nc = a[5]
+        assert np.abs(a[2][:nc] - b[2][:nc]).max() < 1e-12, f"values tree {t}"
+    for t, rr in enumerate(rec):
+        assert hashlib.sha256(rr["sample"].tobytes()).hexdigest() == str(d["sample_sha"][t])
+    assert np.abs(r["train_loss"] - d["train_loss"]).max() < 1e-12
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg1_level", "cfg2_small", "cfg3_small", "cfg4_small"])
+def test_exact_fit_ties_explained(name):
+    """EXACT-mode fit: same trees as the reference up to the first divergence,
+    and that divergence is an exact (or sub-resolution) tie."""
+    d = golden("fit_" + name)
+    Xb, y = _binned(name, d)
+    kw = oracle_fit_kwargs(d)
+    rec = []
+    ref = O.fit_binary(Xb, y, d["counts"], mode=O.MODE_REF, record=rec, **kw)
+    S = engine_scale_bits(ref["w2"].max())
+    ex = O.fit_binary(Xb, y, d["counts"], mode=O.MODE_EXACT, scale_bits=S, **kw)
+    div = A.first_divergence(ref["trees"], ex["trees"])
+    if div is None:
+        return
+    t, _ = div
+    rr = rec[t]
+    te = O.build_tree(Xb, rr["g"], rr["h"], rr["sample"], rr["feat"], d["counts"],
+                      max_leaves=kw["max_leaves"], max_depth=kw["max_depth"],
+                      msl=kw["min_samples_leaf"], mcw=kw["min_child_weight"], lam=kw["reg_lambda"],
+                      gamma=kw["gamma"], mode=O.MODE_EXACT, scale_bits=S, policy=kw["grow_policy"])
+    O.post_prune(te[0], te[3], te[4], te[6], kw["gamma"], te[5])
+    dv = A.first_divergence([ref["trees"][t]], [te])
+    assert dv is not None
+    res = A.audit_node(Xb, rr["g"], rr["h"], rr["sample"], d["counts"], ref["trees"][t], te, dv[1],
+                       kw["reg_lambda"], kw["min_child_weight"])
+    assert A.explained(res), res
+
+
+def test_i128_conversion_rounds_to_nearest():
+    """The oracle's 128-bit -> float64 conversion rounds to nearest-even, like
+    Python's int -> float (and like the engine's device conversion)."""
+    rng = np.random.default_rng(0)
+    vals = [0, 1, -1, 2**53 + 1, 2**64 + 2**11, -(2**100) - 2**47 - 1, 2**126 - 1, -(2**126)]
+    for _ in range(2000):
+        bits = int(rng.integers(1, 126))
+        v = int(rng.integers(0, 2**62)) << max(0, bits - 62)
+        v |= int(rng.integers(0, 2**min(bits, 62)))
+        vals.append(v if rng.random() < 0.5 else -v)
+        vals.append((1 << bits) + (1 << max(0, bits - 53)))   # exact halfway cases
+    for v in vals:
+        assert O.i128_to_double(v) == float(v), v
