@@ -1,0 +1,193 @@
+// gbm_common.cuh -- constants, device helpers and the structures shared by
+// the engine's kernels (gbm_kernels.cuh) and its host code (gbm_b200.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+namespace gbm {
+
+constexpr int kBins = 256;          // uint8 bin ids
+constexpr int kBlk = 16;            // features per column block (one 16-byte load)
+constexpr int kWords = 4;           // g_hi, g_lo, h_hi, h_lo per histogram cell
+constexpr int kTotWords = 4;        // node totals (G hi/lo, H hi/lo) after the cells
+constexpr int kChunk = 16384;       // max rows one CTA adds into one cell (R_max)
+constexpr int kHistThreads = 512;
+constexpr int kDig = 17;            // low/mid digit width of the shared-memory accumulators
+constexpr int kAccWords = 6 * kBlk * kBins;   // [g0 g1 g2 h0 h1 h2][16][256] uint32
+constexpr int kPartTile = 4096;     // rows per partition CTA
+constexpr int kPartThreads = 256;
+constexpr int kSplitWarps = 8;      // features per split CTA (one warp each)
+constexpr int kUpdThreads = 256;
+constexpr int kCompTile = 4096;     // rows per in-bag compaction CTA
+
+typedef __int128 i128;
+
+__host__ __device__ __forceinline__ int64_t slot_words_for(int nf) {
+    return (int64_t)nf * kBins * kWords + kTotWords;
+}
+
+// ---------------------------------------------------------------------------
+// structures
+// ---------------------------------------------------------------------------
+
+// One node of the tree being grown, as known to the device.  Histogram
+// slot of node i is pool slot i.
+struct DNode {
+    long long begin, end;   // this rank's rows: rows[begin, end)
+    long long n;            // rows over all ranks
+    long long nl, gnl;      // rows sent left (this rank / all ranks) once expanded
+    double G, H;            // exact totals, each rounded once to float64
+    double gain;            // best split gain (meaningful when feat >= 0)
+    int feat, bin;          // best split; feat = -1: none, or the node may not split
+    int depth, parent;
+    int kid0, kid1;         // children (-1 = not expanded)
+    int left_small;         // 1 if the left child's histogram was built directly
+    int expanded;           // 1 once both children's results are final
+};
+
+struct HistTask {           // rows[begin, end) -> staging histogram `stage`
+    long long begin, end;
+    int stage;
+    int left_small;
+};
+
+struct PartTask {           // stable partition of rows[begin, end) on bin(feat) <= thr
+    long long begin, end;
+    int feat, thr;
+    int tile0, ntile;       // tiles of this task in the level's tile numbering
+};
+
+struct FBest {              // best bin of one feature for one node
+    double gain;
+    int bin;
+    int valid;
+};
+
+struct TreeDev {            // a pruned tree in the reference's layout
+    int n;
+    int feat[256];
+    int thr[256];
+    int left[256];
+    int right[256];
+    double val[256];
+};
+
+struct PNode {              // predict: 8 bytes per node
+    int16_t feat;           // -1 = leaf
+    uint8_t thr;
+    uint8_t pad;
+    int16_t left, right;    // tree-local ids
+};
+
+// ---------------------------------------------------------------------------
+// device helpers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ double pow2(int e) {
+    return __longlong_as_double((long long)(1023 + e) << 52);
+}
+
+// Correctly rounded (nearest-even) 128-bit integer -> double.
+__device__ __forceinline__ double i128_to_double(i128 v) {
+    bool neg = v < 0;
+    unsigned __int128 m = neg ? (unsigned __int128)(-v) : (unsigned __int128)v;
+    unsigned long long hi = (unsigned long long)(m >> 64);
+    unsigned long long lo = (unsigned long long)m;
+    double r;
+    if (hi == 0) {
+        r = __ull2double_rn(lo);
+    } else {
+        int sh = 64 - __clzll((long long)hi);                  // 1..64
+        unsigned long long top = (unsigned long long)(m >> sh); // bit 63 set
+        unsigned long long rest = (sh == 64) ? lo : (lo & ((1ull << sh) - 1ull));
+        if (rest) top |= 1ull;                                  // sticky
+        r = __dmul_rn(__ull2double_rn(top), pow2(sh));
+    }
+    return neg ? -r : r;
+}
+
+// A histogram cell stores a 128-bit sum as two int64 words: hi * 2^32 + lo.
+__device__ __forceinline__ i128 cell(long long hi, long long lo) {
+    return ((i128)hi << 32) + (i128)lo;
+}
+
+// p = 1/(1+exp(-clip(F,-500,500))), g = w(p-y), h = (w p)(1-p)   (E:2861, E:2873-2874)
+__device__ __forceinline__ void grad_hess(double F, int y, double w, double &g, double &h, double &p) {
+    double f = fmin(fmax(F, -500.0), 500.0);
+    p = __ddiv_rn(1.0, __dadd_rn(1.0, exp(-f)));
+    g = __dmul_rn(w, __dsub_rn(p, (double)y));
+    h = __dmul_rn(__dmul_rn(w, p), __dsub_rn(1.0, p));
+}
+
+// logloss term with p clipped to [1e-15, 1-1e-15]   (E:2320-2325)
+__device__ __forceinline__ double loss_term(double p, int y) {
+    double pc = fmin(fmax(p, 1e-15), 1.0 - 1e-15);
+    return y ? log(pc) : log(__dsub_rn(1.0, pc));
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum(T v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ i128 shfl_up_i128(i128 v, int o) {
+    long long lo = (long long)(unsigned long long)v;
+    long long hi = (long long)(v >> 64);
+    lo = __shfl_up_sync(0xffffffffu, lo, o);
+    hi = __shfl_up_sync(0xffffffffu, hi, o);
+    return ((i128)hi << 64) | (i128)(unsigned long long)lo;
+}
+
+__device__ __forceinline__ i128 shfl_xor_i128(i128 v, int m) {
+    long long lo = (long long)(unsigned long long)v;
+    long long hi = (long long)(v >> 64);
+    lo = __shfl_xor_sync(0xffffffffu, lo, m);
+    hi = __shfl_xor_sync(0xffffffffu, hi, m);
+    return ((i128)hi << 64) | (i128)(unsigned long long)lo;
+}
+
+// Block-wide exclusive scan of one int per thread; returns the block total.
+__device__ __forceinline__ int block_excl_scan(int v, int *s_w, int &total) {
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int x = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        int t = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += t;
+    }
+    if (lane == 31) s_w[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int y = lane < nw ? s_w[lane] : 0;
+        for (int o = 1; o < 32; o <<= 1) {
+            int t = __shfl_up_sync(0xffffffffu, y, o);
+            if (lane >= o) y += t;
+        }
+        if (lane < nw) s_w[lane] = y;
+    }
+    __syncthreads();
+    int excl = x - v + (w ? s_w[w - 1] : 0);
+    total = s_w[nw - 1];
+    __syncthreads();
+    return excl;
+}
+
+__device__ __forceinline__ int bin_of(const uint8_t *__restrict__ xb, int64_t n, int64_t row, int f) {
+    return __ldg(xb + (((int64_t)(f >> 4) * n + row) << 4) + (f & 15));
+}
+
+// a beats b: larger gain; equal gains -> lower feature position, then lower bin
+// (the reference's strict '>' scan over ascending features and bins).
+__device__ __forceinline__ bool better(double ga, int ja, int ba, double gb, int jb, int bb) {
+    if (ja < 0) return false;
+    if (jb < 0) return true;
+    if (ga > gb) return true;
+    if (gb > ga) return false;
+    if (ja != jb) return ja < jb;
+    return ba < bb;
+}
+
+}  // namespace gbm

@@ -1,0 +1,869 @@
+// gbm_kernels.cuh -- the engine's CUDA kernels (sm_100a).
+//
+// Reference: src/bsscl_gbm/estimator_v1_0_1.py ("E").  Each kernel notes the
+// reference lines whose computation it performs.
+#pragma once
+
+#include "gbm_common.cuh"
+
+namespace gbm {
+
+// ===========================================================================
+// layout, gradients, F update
+// ===========================================================================
+
+// Row-major uint8 [rows][p] -> column blocks [nblk][n][16], ids clamped to
+// bin_count-1 (E:593-594 clamps the same way; E:604 never splits above).
+__global__ void k_pack_bins(const uint8_t *__restrict__ src, int64_t rows, int p, int64_t row0,
+                            int64_t n, int nblk, const int32_t *__restrict__ counts,
+                            uint8_t *__restrict__ xb) {
+    int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= rows * nblk) return;
+    int64_t r = t / nblk;
+    int b = (int)(t % nblk);
+    uint8_t v[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) {
+        int f = b * kBlk + k;
+        uint8_t x = 0;
+        if (f < p) {
+            int c = src[r * p + f];
+            int lim = counts[f] - 1;
+            x = (uint8_t)(c > lim ? lim : c);
+        }
+        v[k] = x;
+    }
+    uint4 o;
+    memcpy(&o, v, 16);
+    reinterpret_cast<uint4 *>(xb)[(int64_t)b * n + row0 + r] = o;
+}
+
+// Bin occupancy of every feature over this rank's rows.
+__global__ void k_bincount(const uint8_t *__restrict__ xb, int64_t n, int nblk,
+                           unsigned long long *__restrict__ cnt) {
+    __shared__ unsigned s[kBlk * kBins];
+    int blk = blockIdx.y;
+    for (int k = threadIdx.x; k < kBlk * kBins; k += blockDim.x) s[k] = 0u;
+    __syncthreads();
+    const uint4 *xv = reinterpret_cast<const uint4 *>(xb) + (int64_t)blk * n;
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n;
+         r += (int64_t)gridDim.x * blockDim.x) {
+        uint4 v = xv[r];
+        unsigned w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < kBlk; k++) atomicAdd(&s[k * kBins + ((w[k >> 2] >> ((k & 3) * 8)) & 0xff)], 1u);
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < kBlk * kBins; k += blockDim.x)
+        if (s[k]) atomicAdd(&cnt[(int64_t)blk * kBlk * kBins + k], (unsigned long long)s[k]);
+}
+
+__global__ void k_init_grad(const double *__restrict__ F, const uint8_t *__restrict__ y, int64_t n,
+                            double w0, double w1, double scale, longlong2 *__restrict__ q) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int yi = y[i];
+    double g, h, p;
+    grad_hess(F[i], yi, yi ? w1 : w0, g, h, p);
+    q[i] = make_longlong2(__double2ll_rn(__dmul_rn(g, scale)), __double2ll_rn(__dmul_rn(h, scale)));
+}
+
+__global__ void k_quant(const double *__restrict__ g, const double *__restrict__ h, int64_t n, double scale,
+                        longlong2 *__restrict__ q) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    q[i] = make_longlong2(__double2ll_rn(__dmul_rn(g[i], scale)), __double2ll_rn(__dmul_rn(h[i], scale)));
+}
+
+__global__ void k_export_grad(const double *__restrict__ F, const uint8_t *__restrict__ y, int64_t n,
+                              double w0, double w1, double *__restrict__ g, double *__restrict__ h) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int yi = y[i];
+    double gg, hh, p;
+    grad_hess(F[i], yi, yi ? w1 : w0, gg, hh, p);
+    g[i] = gg;
+    h[i] = hh;
+}
+
+// One pass over all rows: traverse the round's tree (E:843-861), F += lr * v
+// with two separately rounded operations like NumPy's F += lr * pred
+// (E:2896-2897), the logloss term of the updated F (E:2905) and the next
+// round's quantised (g, h) (E:2861, E:2873-2874).
+__global__ void __launch_bounds__(kUpdThreads)
+k_update(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64_t n,
+         const uint8_t *__restrict__ y, double w0, double w1, double lr, double scale,
+         double *__restrict__ F, longlong2 *__restrict__ q, int32_t *__restrict__ leaf_out,
+         double *__restrict__ loss_part) {
+    __shared__ int s_feat[256], s_thr[256], s_left[256], s_right[256];
+    __shared__ double s_val[256];
+    __shared__ double s_red[kUpdThreads / 32];
+    int nn = tree->n;
+    for (int k = threadIdx.x; k < nn; k += blockDim.x) {
+        s_feat[k] = tree->feat[k];
+        s_thr[k] = tree->thr[k];
+        s_left[k] = tree->left[k];
+        s_right[k] = tree->right[k];
+        s_val[k] = tree->val[k];
+    }
+    __syncthreads();
+    double acc = 0.0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int node = 0;
+        while (s_feat[node] >= 0) {
+            int b = bin_of(xb, n, i, s_feat[node]);
+            node = (b <= s_thr[node]) ? s_left[node] : s_right[node];
+        }
+        if (leaf_out) leaf_out[i] = node;
+        double f = __dadd_rn(F[i], __dmul_rn(lr, s_val[node]));
+        F[i] = f;
+        int yi = y[i];
+        double g, h, p;
+        grad_hess(f, yi, yi ? w1 : w0, g, h, p);
+        acc += loss_term(p, yi);
+        q[i] = make_longlong2(__double2ll_rn(__dmul_rn(g, scale)), __double2ll_rn(__dmul_rn(h, scale)));
+    }
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int w = 0; w < kUpdThreads / 32; w++) s += s_red[w];
+        loss_part[blockIdx.x] = s;
+    }
+}
+
+// Fixed-order sum of the per-block loss partials (deterministic).
+__global__ void k_sum_partials(const double *__restrict__ part, int m, double *__restrict__ out) {
+    __shared__ double s[256];
+    double a = 0.0;
+    for (int k = threadIdx.x; k < m; k += blockDim.x) a += part[k];
+    s[threadIdx.x] = a;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < (int)blockDim.x; k++) t += s[k];
+        *out = t;
+    }
+}
+
+// ===========================================================================
+// in-bag compaction: mask -> ascending row ids
+// ===========================================================================
+
+__global__ void k_comp_count(const uint8_t *__restrict__ mask, int64_t n, int32_t *__restrict__ cnt) {
+    __shared__ int s[32];
+    int64_t base = (int64_t)blockIdx.x * kCompTile;
+    int c = 0;
+    for (int k = threadIdx.x; k < kCompTile; k += blockDim.x) {
+        int64_t i = base + k;
+        if (i < n && mask[i]) c++;
+    }
+    c = warp_sum(c);
+    if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int t = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += s[w];
+        cnt[blockIdx.x] = t;
+    }
+}
+
+// Exclusive scan of m ints by one CTA; *total = sum.
+__global__ void k_scan_small(const int32_t *__restrict__ in, int m, int32_t *__restrict__ out,
+                             int32_t *__restrict__ total) {
+    __shared__ int s_w[32];
+    int carry = 0;
+    for (int base = 0; base < m; base += blockDim.x) {
+        int k = base + threadIdx.x;
+        int v = k < m ? in[k] : 0;
+        int tot;
+        int e = block_excl_scan(v, s_w, tot);
+        if (k < m) out[k] = carry + e;
+        carry += tot;
+    }
+    if (threadIdx.x == 0 && total) *total = carry;
+}
+
+__global__ void k_comp_scatter(const uint8_t *__restrict__ mask, int64_t n, const int32_t *__restrict__ off,
+                               int32_t *__restrict__ rows) {
+    __shared__ int s_w[32];
+    int64_t base = (int64_t)blockIdx.x * kCompTile;
+    int carry = off[blockIdx.x];
+    for (int k0 = 0; k0 < kCompTile; k0 += blockDim.x) {
+        int64_t i = base + k0 + threadIdx.x;
+        int f = (i < n && mask[i]) ? 1 : 0;
+        int tot;
+        int e = block_excl_scan(f, s_w, tot);
+        if (f) rows[carry + e] = (int32_t)i;
+        carry += tot;
+    }
+}
+
+__global__ void k_count64(const int32_t *__restrict__ in, long long *__restrict__ out) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) *out = *in;
+}
+
+// ===========================================================================
+// histograms
+// ===========================================================================
+
+// grid: x = chunk id over all tasks (prefix[ntask] valid chunks), y = feature block.
+//
+// Each row's q (int64) is split into three digits, q = top*2^34 + mid*2^17 +
+// low with low, mid in [0, 2^17) and top signed, and each digit is summed in
+// its own 32-bit shared-memory word: at most kChunk = 2^14 rows per CTA keep
+// every digit sum inside 32 bits, and native 32-bit shared atomics are much
+// faster than 64-bit ones.  Each feature skips its most frequent bin (the
+// NaN bin, typically); that cell is rebuilt exactly by the split kernel as
+// node total - sum(other cells).  A task of one chunk stores its cells; a
+// task spread over several CTAs adds (hi, lo) words atomically into a zeroed
+// staging histogram.  blockIdx.y == 0 also accumulates the node totals.
+// (E:582-596 root, E:723-737 smaller child.)
+__global__ void __launch_bounds__(kHistThreads, 2)
+k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows,
+       const HistTask *__restrict__ tasks, const int32_t *__restrict__ prefix,
+       const int *__restrict__ ntask_p, const int32_t *__restrict__ blist,
+       const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
+       const longlong2 *__restrict__ q, long long *__restrict__ stage_hist) {
+    extern __shared__ unsigned acc[];   // [6][16][256]
+    __shared__ int s_task;
+    __shared__ long long s_tot[2][kHistThreads / 32];
+    const int ntask = *ntask_p;
+    int cid = blockIdx.x;
+    if (ntask <= 0 || cid >= prefix[ntask]) return;
+    if (threadIdx.x == 0) {
+        int lo = 0, hi = ntask - 1;
+        while (lo < hi) {   // last task with prefix[t] <= cid
+            int mid = (lo + hi + 1) >> 1;
+            if (prefix[mid] <= cid) lo = mid; else hi = mid - 1;
+        }
+        s_task = lo;
+    }
+    for (int k = threadIdx.x; k < kAccWords; k += blockDim.x) acc[k] = 0u;
+    __syncthreads();
+    const int t = s_task;
+    const HistTask tk = tasks[t];
+    const bool single = (prefix[t + 1] - prefix[t]) == 1;
+    const int blk = blist[blockIdx.y];
+    long long r0 = tk.begin + (long long)(cid - prefix[t]) * kChunk;
+    long long r1 = min(r0 + (long long)kChunk, tk.end);
+    unsigned mask = 0;
+    int skip[kBlk];
+#pragma unroll
+    for (int k = 0; k < kBlk; k++) {
+        bool sel = fpos[blk * kBlk + k] >= 0;
+        mask |= (sel ? 1u : 0u) << k;
+        skip[k] = sel ? (int)skipb[blk * kBlk + k] : -1;
+    }
+    const uint4 *xv = reinterpret_cast<const uint4 *>(xb) + (int64_t)blk * n;
+    long long tg = 0, th = 0;
+    for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+        int row = rows[r];
+        uint4 v = __ldg(xv + row);
+        longlong2 qq = __ldg(q + row);
+        tg += qq.x;
+        th += qq.y;
+        unsigned g0 = (unsigned)qq.x & 0x1ffffu, g1 = (unsigned)(qq.x >> kDig) & 0x1ffffu;
+        unsigned g2 = (unsigned)(int)(qq.x >> (2 * kDig));
+        unsigned h0 = (unsigned)qq.y & 0x1ffffu, h1 = (unsigned)(qq.y >> kDig) & 0x1ffffu;
+        unsigned h2 = (unsigned)(int)(qq.y >> (2 * kDig));
+        unsigned w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < kBlk; k++) {
+            if (mask & (1u << k)) {
+                int b = (w[k >> 2] >> ((k & 3) * 8)) & 0xff;
+                if (b != skip[k]) {
+                    unsigned *c = acc + k * kBins + b;
+                    atomicAdd(c + 0 * kBlk * kBins, g0);
+                    atomicAdd(c + 1 * kBlk * kBins, g1);
+                    atomicAdd(c + 2 * kBlk * kBins, g2);
+                    atomicAdd(c + 3 * kBlk * kBins, h0);
+                    atomicAdd(c + 4 * kBlk * kBins, h1);
+                    atomicAdd(c + 5 * kBlk * kBins, h2);
+                }
+            }
+        }
+    }
+    if (blockIdx.y == 0) {
+        tg = warp_sum(tg);
+        th = warp_sum(th);
+        if ((threadIdx.x & 31) == 0) {
+            s_tot[0][threadIdx.x >> 5] = tg;
+            s_tot[1][threadIdx.x >> 5] = th;
+        }
+    }
+    __syncthreads();
+    long long *dst = stage_hist + (int64_t)tk.stage * slot_words_for(nf);
+    if (blockIdx.y == 0 && threadIdx.x < 2) {
+        long long tot = 0;
+        for (int w2 = 0; w2 < kHistThreads / 32; w2++) tot += s_tot[threadIdx.x][w2];
+        long long *o = dst + (int64_t)nf * kBins * kWords + 2 * threadIdx.x;
+        if (single) {
+            o[0] = tot >> 32;
+            o[1] = tot & 0xffffffffll;
+        } else if (tot) {
+            atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(tot >> 32));
+            atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(tot & 0xffffffffll));
+        }
+    }
+    for (int idx = threadIdx.x; idx < kBlk * kBins; idx += blockDim.x) {
+        int k = idx >> 8, b = idx & 255;
+        int jj = fpos[blk * kBlk + k];
+        if (jj < 0) continue;
+        long long gv = ((long long)(int)acc[2 * kBlk * kBins + idx] << (2 * kDig)) +
+                       ((long long)acc[1 * kBlk * kBins + idx] << kDig) + (long long)acc[idx];
+        long long hv = ((long long)(int)acc[5 * kBlk * kBins + idx] << (2 * kDig)) +
+                       ((long long)acc[4 * kBlk * kBins + idx] << kDig) +
+                       (long long)acc[3 * kBlk * kBins + idx];
+        long long *o = dst + ((int64_t)jj * kBins + b) * kWords;
+        if (single) {
+            reinterpret_cast<longlong2 *>(o)[0] = make_longlong2(gv >> 32, gv & 0xffffffffll);
+            reinterpret_cast<longlong2 *>(o)[1] = make_longlong2(hv >> 32, hv & 0xffffffffll);
+        } else {
+            if (gv) {
+                atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(gv >> 32));
+                atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(gv & 0xffffffffll));
+            }
+            if (hv) {
+                atomicAdd((unsigned long long *)(o + 2), (unsigned long long)(hv >> 32));
+                atomicAdd((unsigned long long *)(o + 3), (unsigned long long)(hv & 0xffffffffll));
+            }
+        }
+    }
+}
+
+// Zero the staging histograms of tasks that span several CTAs (their CTAs
+// add atomically) or none (an empty side); single-chunk tasks store every
+// word themselves.
+__global__ void k_zero_multi(const int32_t *__restrict__ prefix, const int *__restrict__ ntask_p,
+                             long long *__restrict__ stage, int64_t words) {
+    int t = blockIdx.y;
+    if (t >= *ntask_p) return;
+    if (prefix[t + 1] - prefix[t] == 1) return;
+    long long *p = stage + (int64_t)t * words;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < words;
+         i += (int64_t)gridDim.x * blockDim.x)
+        p[i] = 0;
+}
+
+// ===========================================================================
+// level planning (device side: no host round trip inside a tree)
+// ===========================================================================
+
+__device__ __forceinline__ DNode fresh_node(int depth, int parent) {
+    DNode d;
+    d.begin = d.end = d.n = d.nl = d.gnl = 0;
+    d.G = d.H = 0.0;
+    d.gain = -1.0;
+    d.feat = -1;
+    d.bin = 0;
+    d.depth = depth;
+    d.parent = parent;
+    d.kid0 = d.kid1 = -1;
+    d.left_small = 0;
+    d.expanded = 0;
+    return d;
+}
+
+// Root: node 0 holds all in-bag rows; one histogram task over them.
+__global__ void k_root_plan(const int32_t *__restrict__ n_local, const long long *__restrict__ n_global,
+                            DNode *__restrict__ nodes, HistTask *__restrict__ ht,
+                            int32_t *__restrict__ prefix, int *__restrict__ node_count) {
+    if (threadIdx.x || blockIdx.x) return;
+    long long ns = *n_local;
+    DNode d = fresh_node(0, -1);
+    d.begin = 0;
+    d.end = ns;
+    d.n = n_global ? *n_global : ns;
+    nodes[0] = d;
+    HistTask t;
+    t.begin = 0;
+    t.end = ns;
+    t.stage = 0;
+    t.left_small = 1;
+    ht[0] = t;
+    prefix[0] = 0;
+    prefix[1] = (int32_t)((ns + kChunk - 1) / kChunk);
+    *node_count = 1;
+}
+
+// Partition tasks for the parents lvl[0..W) and node ids for their children
+// (children of lvl[k] are base+2k (left) and base+2k+1 (right)).  W is cut
+// to the level's launch bound and to the node capacity; parents cut off stay
+// unexpanded (the host expands them on demand if the replay needs them).
+__global__ void k_lvl_plan(DNode *__restrict__ nodes, const int *__restrict__ lvl, int *__restrict__ lvl_count,
+                           int *__restrict__ node_count, PartTask *__restrict__ pt,
+                           int *__restrict__ tiles_total, int nmax, int w_max) {
+    __shared__ int s_w[32];
+    __shared__ int s_W, s_base;
+    if (threadIdx.x == 0) {
+        int W = *lvl_count, base = *node_count;
+        int cap = (nmax - base) / 2;
+        if (W > w_max) W = w_max;          // the launch bounds of this level
+        if (W > cap) W = cap < 0 ? 0 : cap;
+        s_W = W;
+        s_base = base;
+    }
+    __syncthreads();
+    const int W = s_W, base = s_base;
+    int carry = 0;
+    for (int b0 = 0; b0 < W; b0 += blockDim.x) {
+        int k = b0 + threadIdx.x;
+        int nt = 0;
+        int i = -1;
+        if (k < W) {
+            i = lvl[k];
+            long long sz = nodes[i].end - nodes[i].begin;
+            nt = (int)((sz + kPartTile - 1) / kPartTile);
+            if (nt < 1) nt = 1;
+        }
+        int tot;
+        int e = block_excl_scan(nt, s_w, tot);
+        if (k < W) {
+            DNode &p = nodes[i];
+            PartTask t;
+            t.begin = p.begin;
+            t.end = p.end;
+            t.feat = p.feat;
+            t.thr = p.bin;
+            t.tile0 = carry + e;
+            t.ntile = nt;
+            pt[k] = t;
+            int c0 = base + 2 * k;
+            p.kid0 = c0;
+            p.kid1 = c0 + 1;
+            nodes[c0] = fresh_node(p.depth + 1, i);
+            nodes[c0 + 1] = fresh_node(p.depth + 1, i);
+        }
+        carry += tot;
+    }
+    if (threadIdx.x == 0) {
+        *lvl_count = W;
+        *node_count = base + 2 * W;
+        *tiles_total = carry;
+    }
+}
+
+__device__ __forceinline__ int find_task_by_tile(const PartTask *tasks, int ntask, int tile) {
+    int lo = 0, hi = ntask - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (tasks[mid].tile0 <= tile) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// Stable partition (E:663-674 decides the same sides; the row order inside
+// a side does not matter to exact sums): count, scan, scatter, copy back.
+__global__ void __launch_bounds__(kPartThreads)
+k_part_count(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows,
+             const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
+             const int *__restrict__ tiles_total, int32_t *__restrict__ tile_cnt) {
+    __shared__ int s[32];
+    int tile = blockIdx.x;
+    if (tile >= *tiles_total) return;
+    int t = find_task_by_tile(tasks, *ntask_p, tile);
+    PartTask tk = tasks[t];
+    long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
+    long long r1 = min(r0 + kPartTile, tk.end);
+    int c = 0;
+    for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x)
+        c += bin_of(xb, n, rows[r], tk.feat) <= tk.thr;
+    c = warp_sum(c);
+    if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int tot = 0;
+        for (int w = 0; w < kPartThreads / 32; w++) tot += s[w];
+        tile_cnt[tile] = tot;
+    }
+}
+
+// One CTA per task: exclusive scan of its tiles' left counts; n_left.
+__global__ void k_part_scan(const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
+                            const int32_t *__restrict__ tile_cnt, int32_t *__restrict__ tile_off,
+                            long long *__restrict__ n_left) {
+    __shared__ int s_w[32];
+    if ((int)blockIdx.x >= *ntask_p) return;
+    PartTask tk = tasks[blockIdx.x];
+    int carry = 0;
+    for (int b = 0; b < tk.ntile; b += blockDim.x) {
+        int k = b + threadIdx.x;
+        int v = k < tk.ntile ? tile_cnt[tk.tile0 + k] : 0;
+        int tot;
+        int e = block_excl_scan(v, s_w, tot);
+        if (k < tk.ntile) tile_off[tk.tile0 + k] = carry + e;
+        carry += tot;
+    }
+    if (threadIdx.x == 0) n_left[blockIdx.x] = carry;
+}
+
+__global__ void __launch_bounds__(kPartThreads)
+k_part_scatter(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows,
+               const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
+               const int *__restrict__ tiles_total, const int32_t *__restrict__ tile_off,
+               const long long *__restrict__ n_left, int32_t *__restrict__ tmp) {
+    __shared__ int s_w[32];
+    int tile = blockIdx.x;
+    if (tile >= *tiles_total) return;
+    int t = find_task_by_tile(tasks, *ntask_p, tile);
+    PartTask tk = tasks[t];
+    long long tstart = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
+    long long r1 = min(tstart + kPartTile, tk.end);
+    long long nl = n_left[t];
+    long long lcar = tile_off[tile];                         // lefts before this tile
+    long long rcar = (tstart - tk.begin) - lcar;             // rights before this tile
+    for (long long r0 = tstart; r0 < r1; r0 += blockDim.x) {
+        long long r = r0 + threadIdx.x;
+        int row = 0, f = 0;
+        bool in = r < r1;
+        if (in) {
+            row = rows[r];
+            f = bin_of(xb, n, row, tk.feat) <= tk.thr;
+        }
+        int tot;
+        int e = block_excl_scan(f, s_w, tot);
+        if (in) {
+            int pos_in_chunk = (int)(r - r0);
+            if (f) tmp[tk.begin + lcar + e] = row;
+            else tmp[tk.begin + nl + rcar + (pos_in_chunk - e)] = row;
+        }
+        int cnt = (int)min((long long)blockDim.x, r1 - r0);
+        lcar += tot;
+        rcar += cnt - tot;
+    }
+}
+
+__global__ void k_part_copyback(const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
+                                const int *__restrict__ tiles_total, const int32_t *__restrict__ tmp,
+                                int32_t *__restrict__ rows) {
+    int tile = blockIdx.x;
+    if (tile >= *tiles_total) return;
+    int t = find_task_by_tile(tasks, *ntask_p, tile);
+    PartTask tk = tasks[t];
+    long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
+    long long r1 = min(r0 + kPartTile, tk.end);
+    for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x) rows[r] = tmp[r];
+}
+
+// After the partition: children's row ranges and global counts; the
+// globally smaller side (E:701-709, n_left <= n_right -> left) becomes the
+// histogram task of staging slot k.  `gl` are the left counts summed over
+// ranks (== nl on one GPU).
+__global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ lvl,
+                            const int *__restrict__ lvl_count, const long long *__restrict__ nl_local,
+                            const long long *__restrict__ gl, HistTask *__restrict__ ht,
+                            int32_t *__restrict__ prefix) {
+    __shared__ int s_w[32];
+    const int W = *lvl_count;
+    int carry = 0;
+    for (int b0 = 0; b0 < W; b0 += blockDim.x) {
+        int k = b0 + threadIdx.x;
+        int ch = 0;
+        if (k < W) {
+            int i = lvl[k];
+            DNode &p = nodes[i];
+            long long nl = nl_local[k], gnl = gl[k], gtot = p.n;
+            bool ls = gnl <= gtot - gnl;
+            HistTask t;
+            t.begin = ls ? p.begin : p.begin + nl;
+            t.end = ls ? p.begin + nl : p.end;
+            t.stage = k;
+            t.left_small = ls ? 1 : 0;
+            ht[k] = t;
+            ch = (int)((t.end - t.begin + kChunk - 1) / kChunk);
+            p.nl = nl;
+            p.gnl = gnl;
+            p.left_small = t.left_small;
+            DNode &a = nodes[p.kid0];
+            DNode &c = nodes[p.kid1];
+            a.begin = p.begin;
+            a.end = p.begin + nl;
+            a.n = gnl;
+            c.begin = p.begin + nl;
+            c.end = p.end;
+            c.n = gtot - gnl;
+        }
+        int tot;
+        int e = block_excl_scan(ch, s_w, tot);
+        if (k < W) prefix[k] = carry + e;
+        carry += tot;
+    }
+    if (threadIdx.x == 0) prefix[W] = carry;
+}
+
+// ===========================================================================
+// split search
+// ===========================================================================
+
+// Best bin of feature position jj for one node whose cells start at `hf`
+// (256 cells x 4 words) with exact totals (TG, TH).  The reference's scan
+// (E:602-621, E:780-801): bins 0..nb-2 as a running prefix, HL<mcw or
+// HR<mcw skipped, gain = GL^2/(HL+l) + GR^2/(HR+l) - G^2/(H+l), first
+// maximum wins.  Every operation rounds separately, as in the reference.
+__device__ __forceinline__ void feature_best(const long long *__restrict__ hf, i128 TG, i128 TH, int nb,
+                                             int sb, int S, double lam, double mcw, double parent,
+                                             double &best_gain, int &best_bin) {
+    const int lane = threadIdx.x & 31;
+    const double sc = pow2(-S);
+    i128 g[8], h[8];
+    i128 lg = 0, lh = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const longlong2 *c = reinterpret_cast<const longlong2 *>(hf + (int64_t)(lane * 8 + k) * kWords);
+        longlong2 a = c[0], b = c[1];
+        g[k] = cell(a.x, a.y);
+        h[k] = cell(b.x, b.y);
+        lg += g[k];
+        lh += h[k];
+    }
+    // the skipped bin holds node total - all other cells
+    i128 ag = lg, ah = lh;
+    for (int o = 16; o > 0; o >>= 1) {
+        ag += shfl_xor_i128(ag, o);
+        ah += shfl_xor_i128(ah, o);
+    }
+    if ((sb >> 3) == lane) {
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            if ((sb & 7) == k) { g[k] += TG - ag; h[k] += TH - ah; }
+        lg += TG - ag;
+        lh += TH - ah;
+    }
+    // exclusive prefix of the lane sums
+    i128 xg = lg, xh = lh;
+    for (int o = 1; o < 32; o <<= 1) {
+        i128 tg2 = shfl_up_i128(xg, o), th2 = shfl_up_i128(xh, o);
+        if (lane >= o) { xg += tg2; xh += th2; }
+    }
+    i128 pg = xg - lg, ph = xh - lh;
+    double bg = -1e9;
+    int bb = -1;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        int b = lane * 8 + k;
+        pg += g[k];
+        ph += h[k];
+        if (b <= nb - 2) {
+            double GL = __dmul_rn(i128_to_double(pg), sc);
+            double HL = __dmul_rn(i128_to_double(ph), sc);
+            double GR = __dmul_rn(i128_to_double(TG - pg), sc);
+            double HR = __dmul_rn(i128_to_double(TH - ph), sc);
+            if (!(HL < mcw || HR < mcw)) {
+                double gain = __dsub_rn(
+                    __dadd_rn(__ddiv_rn(__dmul_rn(GL, GL), __dadd_rn(HL, lam)),
+                              __ddiv_rn(__dmul_rn(GR, GR), __dadd_rn(HR, lam))),
+                    parent);
+                if (gain > bg) { bg = gain; bb = b; }
+            }
+        }
+    }
+    // warp argmax, ties -> lower bin
+    for (int o = 16; o > 0; o >>= 1) {
+        double og = __shfl_xor_sync(0xffffffffu, bg, o);
+        int ob = __shfl_xor_sync(0xffffffffu, bb, o);
+        if (better(og, ob < 0 ? -1 : 0, ob, bg, bb < 0 ? -1 : 0, bb)) { bg = og; bb = ob; }
+    }
+    best_gain = bg;
+    best_bin = bb;
+}
+
+// One warp per (parent k, feature position jj): the smaller child's cells
+// come from staging slot k, the larger child's are parent - smaller
+// (E:740-745, exact); both are written to the children's pool slots, and
+// both children's best bins for feature jj are found.  ROOT: node 0 from
+// staging slot 0.  fbest[(2k + side) * nf + jj], side 0 = left child.
+template <bool ROOT>
+__global__ void __launch_bounds__(32 * kSplitWarps)
+k_split_feat(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const int *__restrict__ lvl_count,
+             const HistTask *__restrict__ ht, const long long *__restrict__ stage, long long *__restrict__ pool,
+             int nf, const int32_t *__restrict__ fidx, const int32_t *__restrict__ counts,
+             const int16_t *__restrict__ skipb, int S, double lam, double mcw, long long msl, int max_depth,
+             FBest *__restrict__ fbest) {
+    const int k = blockIdx.y;
+    if (!ROOT && k >= *lvl_count) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int jj = blockIdx.x * kSplitWarps + warp;
+    if (jj >= nf) return;
+    const int64_t words = slot_words_for(nf);
+    const long long *st = stage + (int64_t)k * words;
+    int parent = -1, small = 0, large = -1, c0 = 0, c1 = -1;
+    if (!ROOT) {
+        parent = lvl[k];
+        c0 = nodes[parent].kid0;
+        c1 = nodes[parent].kid1;
+        bool ls = ht[k].left_small != 0;
+        small = ls ? c0 : c1;
+        large = ls ? c1 : c0;
+    }
+    const long long *st_tot = st + (int64_t)nf * kBins * kWords;
+    const i128 TGs = cell(st_tot[0], st_tot[1]), THs = cell(st_tot[2], st_tot[3]);
+    i128 TGl = 0, THl = 0;
+    const long long *par = ROOT ? nullptr : pool + (int64_t)parent * words;
+    long long *ps = pool + (int64_t)small * words;
+    long long *pl = ROOT ? nullptr : pool + (int64_t)large * words;
+    if (!ROOT) {
+        const long long *pt = par + (int64_t)nf * kBins * kWords;
+        TGl = cell(pt[0] - st_tot[0], pt[1] - st_tot[1]);
+        THl = cell(pt[2] - st_tot[2], pt[3] - st_tot[3]);
+    }
+    if (jj == 0 && lane < kTotWords) {
+        const int64_t o = (int64_t)nf * kBins * kWords + lane;
+        ps[o] = st_tot[lane];
+        if (!ROOT) pl[o] = par[o] - st_tot[lane];
+    }
+    // cells of feature jj: lane owns bins 8*lane .. 8*lane+7 (32 words)
+    const int64_t base = (int64_t)jj * kBins * kWords + (int64_t)lane * 8 * kWords;
+#pragma unroll
+    for (int v = 0; v < 8 * kWords; v += 2) {
+        longlong2 s = *reinterpret_cast<const longlong2 *>(st + base + v);
+        *reinterpret_cast<longlong2 *>(ps + base + v) = s;
+        if (!ROOT) {
+            longlong2 p = *reinterpret_cast<const longlong2 *>(par + base + v);
+            *reinterpret_cast<longlong2 *>(pl + base + v) = make_longlong2(p.x - s.x, p.y - s.y);
+        }
+    }
+    const int f = fidx[jj];
+    const int nb = counts[f];
+    const int sb = skipb[f];
+    const double sc = pow2(-S);
+    for (int side = 0; side < (ROOT ? 1 : 2); side++) {
+        const bool is_small = ROOT || (side == 0) == (small == c0);
+        const int ch = ROOT ? 0 : (side == 0 ? c0 : c1);
+        const i128 TG = is_small ? TGs : TGl, TH = is_small ? THs : THl;
+        const long long *cells = (is_small ? ps : pl) + (int64_t)jj * kBins * kWords;
+        const double Gd = __dmul_rn(i128_to_double(TG), sc), Hd = __dmul_rn(i128_to_double(TH), sc);
+        const DNode nd = nodes[ch];
+        const bool eval = nd.depth < max_depth && nd.n >= msl && Hd >= mcw && nb >= 2;
+        double bg = -1e9;
+        int bb = -1;
+        if (eval) {
+            double parent_term = __ddiv_rn(__dmul_rn(Gd, Gd), __dadd_rn(Hd, lam));
+            feature_best(cells, TG, TH, nb, sb, S, lam, mcw, parent_term, bg, bb);
+        }
+        if (lane == 0) {
+            FBest o;
+            o.gain = bg;
+            o.bin = bb < 0 ? 0 : bb;
+            o.valid = bb >= 0 ? 1 : 0;
+            fbest[(int64_t)(2 * k + side) * nf + jj] = o;
+        }
+    }
+}
+
+// Per child: the first best over feature positions (ties -> lower position),
+// its totals as float64, and the parent marked expanded.
+template <bool ROOT>
+__global__ void k_split_reduce(DNode *__restrict__ nodes, const int *__restrict__ lvl,
+                               const int *__restrict__ lvl_count, const long long *__restrict__ pool, int nf,
+                               const int32_t *__restrict__ fidx, const FBest *__restrict__ fbest, int S) {
+    const int c = blockIdx.x;
+    int ch = 0, parent = -1;
+    if (!ROOT) {
+        const int k = c >> 1;
+        if (k >= *lvl_count) return;
+        parent = lvl[k];
+        ch = (c & 1) ? nodes[parent].kid1 : nodes[parent].kid0;
+    }
+    const FBest *fb = fbest + (int64_t)c * nf;
+    double bg = -1e9;
+    int bj = -1, bb = 0;
+    for (int jj = threadIdx.x; jj < nf; jj += 32) {
+        FBest o = fb[jj];
+        if (o.valid && better(o.gain, jj, o.bin, bg, bj, bb)) { bg = o.gain; bj = jj; bb = o.bin; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        double og = __shfl_xor_sync(0xffffffffu, bg, o);
+        int oj = __shfl_xor_sync(0xffffffffu, bj, o);
+        int ob = __shfl_xor_sync(0xffffffffu, bb, o);
+        if (better(og, oj, ob, bg, bj, bb)) { bg = og; bj = oj; bb = ob; }
+    }
+    if (threadIdx.x == 0) {
+        const long long *t = pool + (int64_t)ch * slot_words_for(nf) + (int64_t)nf * kBins * kWords;
+        const double sc = pow2(-S);
+        DNode &d = nodes[ch];
+        d.G = __dmul_rn(i128_to_double(cell(t[0], t[1])), sc);
+        d.H = __dmul_rn(i128_to_double(cell(t[2], t[3])), sc);
+        d.feat = bj >= 0 ? fidx[bj] : -1;
+        d.bin = bj >= 0 ? bb : 0;
+        d.gain = bj >= 0 ? bg : -1.0;
+        if (!ROOT && (c & 1) == 0) nodes[parent].expanded = 1;
+    }
+}
+
+// Next level: among the children of lvl[0..W) (ROOT: node 0 alone), the ones
+// with a split (and gain > gamma when use_gamma), ranked by gain (ties ->
+// lower node id), at most min(M, capacity) of them.
+template <bool ROOT>
+__global__ void k_next_level(const DNode *__restrict__ nodes, const int *__restrict__ lvl,
+                             const int *__restrict__ lvl_count, int *__restrict__ out,
+                             int *__restrict__ out_count, const int *__restrict__ node_count, int nmax,
+                             int M, double gamma, int use_gamma) {
+    __shared__ double s_g[1024];
+    __shared__ int s_id[1024];
+    __shared__ int s_cnt;
+    const int W = ROOT ? 0 : *lvl_count;
+    const int C = ROOT ? 1 : 2 * W;
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        int id = ROOT ? 0 : ((c & 1) ? nodes[lvl[c >> 1]].kid1 : nodes[lvl[c >> 1]].kid0);
+        const DNode &d = nodes[id];
+        bool ok = d.feat >= 0 && (!use_gamma || d.gain > gamma);
+        s_g[c] = d.gain;
+        s_id[c] = ok ? id : -1;
+    }
+    __syncthreads();
+    int cap = (nmax - *node_count) / 2;
+    int Mc = M < cap ? M : cap;
+    if (Mc < 0) Mc = 0;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        if (s_id[c] < 0) continue;
+        int rank = 0;
+        for (int o = 0; o < C; o++) {
+            if (s_id[o] < 0 || o == c) continue;
+            if (s_g[o] > s_g[c] || (s_g[o] == s_g[c] && s_id[o] < s_id[c])) rank++;
+        }
+        if (rank < Mc) {
+            out[rank] = s_id[c];
+            atomicAdd(&s_cnt, 1);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *out_count = s_cnt;
+}
+
+// ===========================================================================
+// predict (ensemble traversal, E:863-884)
+// ===========================================================================
+
+__global__ void __launch_bounds__(256)
+k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const PNode *__restrict__ nodes,
+          const double *__restrict__ vals, const int32_t *__restrict__ off, int ntree, double lr,
+          double base, double *__restrict__ F, double *__restrict__ proba) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint8_t *row = xr + i * p;
+    double acc = 0.0;
+    for (int t = 0; t < ntree; t++) {
+        int o = __ldg(off + t);
+        int node = 0;
+        PNode nd = nodes[o];
+        while (nd.feat >= 0) {
+            int b = __ldg(row + nd.feat);
+            node = b <= nd.thr ? nd.left : nd.right;
+            nd = nodes[o + node];
+        }
+        acc = __dadd_rn(acc, __dmul_rn(lr, __ldg(vals + o + node)));
+    }
+    double f = __dadd_rn(acc, base);
+    if (F) F[i] = f;
+    if (proba) {
+        double c = fmin(fmax(f, -500.0), 500.0);
+        proba[i] = __ddiv_rn(1.0, __dadd_rn(1.0, exp(-c)));
+    }
+}
+
+}  // namespace gbm
