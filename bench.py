@@ -199,8 +199,7 @@ def run_engine(args):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
 
     def step():
-        _, mask, feat = sampler.next()
-        return eng.round(mask[lo:hi], feat, prm, cap)
+        return eng.round_sampled(sampler, lo, prm, cap)
 
     for _ in range(args.warmup):
         step()

@@ -27,7 +27,8 @@ EXPORTS = (
     "gbm_nccl_unique_id", "gbm_upload_bins", "gbm_upload_labels", "gbm_round", "gbm_build_tree",
     "gbm_scale_bits", "gbm_get_F", "gbm_get_grad", "gbm_predict", "gbm_predict_set_model",
     "gbm_predict_upload", "gbm_predict_run", "gbm_predict_fetch", "gbm_sync",
-    "gbm_sampler_create", "gbm_sampler_next", "gbm_sampler_destroy",
+    "gbm_sampler_create", "gbm_sampler_next", "gbm_sampler_destroy", "gbm_sampler_next_rows",
+    "gbm_sampler_n_sub", "gbm_sampler_n_feat", "gbm_round_sampled",
     "gbm_set_profiling", "gbm_get_stats", "gbm_reset_stats", "gbm_event_record",
     "gbm_event_elapsed",
 )
@@ -105,6 +106,13 @@ def lib():
     L.gbm_sampler_create.argtypes = [C.c_uint32, i64, i32, i64, i32, i32, i32, i32,
                                      C.POINTER(C.c_void_p)]
     L.gbm_sampler_next.argtypes = [P, P, P, P]
+    L.gbm_sampler_next_rows.argtypes = [P, P, P]
+    L.gbm_sampler_n_sub.argtypes = [P]
+    L.gbm_sampler_n_sub.restype = i64
+    L.gbm_sampler_n_feat.argtypes = [P]
+    L.gbm_sampler_n_feat.restype = i32
+    L.gbm_round_sampled.argtypes = [P, P, i64, C.POINTER(GbmParams), C.POINTER(GbmTreeOut),
+                                    C.POINTER(C.c_double)]
     L.gbm_sampler_destroy.argtypes = [P]
     L.gbm_sampler_destroy.restype = None
     L.gbm_set_profiling.argtypes = [P, i32]
@@ -193,6 +201,19 @@ class Engine:
         loss = C.c_double(0.0)
         self.check(self._L.gbm_round(self._h, ptr(mask), ptr(fidx), len(fidx), C.byref(params),
                                      C.byref(out), C.byref(loss)), "gbm_round")
+        return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value), leaf
+
+    def round_sampled(self, sampler, row_offset, params: GbmParams, capacity, want_leaf=False):
+        """gbm_round with the subsample drawn by `sampler` (global row ids)."""
+        tf = np.empty(capacity, np.int32); tt = np.empty(capacity, np.int64)
+        tv = np.empty(capacity, np.float64); tl = np.empty(capacity, np.int32)
+        tr = np.empty(capacity, np.int32); sg = np.empty(capacity, np.float64)
+        leaf = np.empty(self.n, np.int32) if want_leaf else None
+        out = GbmTreeOut(capacity, ptr(tf), ptr(tt), ptr(tv), ptr(tl), ptr(tr), ptr(sg), 0,
+                         ptr(leaf))
+        loss = C.c_double(0.0)
+        self.check(self._L.gbm_round_sampled(self._h, sampler._h, int(row_offset), C.byref(params),
+                                             C.byref(out), C.byref(loss)), "gbm_round_sampled")
         return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value), leaf
 
     def build_tree(self, grad, hess, inbag_mask, feat_idx, params: GbmParams, capacity):

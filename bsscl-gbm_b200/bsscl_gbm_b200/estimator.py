@@ -443,7 +443,7 @@ class HybridHistGBMNumbaV1_0_1:
         if not (0 <= int(seed) <= 0xFFFFFFFF):
             raise ValueError("Seed must be between 0 and 2**32 - 1")
         sampler = Sampler(int(seed), n, p, n_sub, n_feat, self.subsample < 1.0,
-                          self.colsample_bytree < 1.0, look_ahead=2)
+                          self.colsample_bytree < 1.0, look_ahead=3)
         eng = self._get_engine()
         dist = _dist()
         lo, hi = 0, n
@@ -464,8 +464,7 @@ class HybridHistGBMNumbaV1_0_1:
         no_improve = 0
         try:
             for m in range(self.n_estimators):
-                _, mask, fidx = sampler.next()
-                tree, loss, _ = eng.round(mask[lo:hi], fidx, params, cap)
+                tree, loss, _ = eng.round_sampled(sampler, lo, params, cap)
                 self.trees.append(tree)
                 self.train_loss_history_.append(loss)
                 val_loss = None

@@ -97,6 +97,9 @@ struct gbm_ctx {
     int *h_list = nullptr;
     double *h_loss = nullptr;
     uint8_t *h_mask = nullptr;
+    int32_t *h_sample = nullptr, *d_sample = nullptr;   // gbm_round_sampled staging
+    int64_t sample_cap = 0;
+    std::vector<int32_t> feat_buf;
 
     // predict
     uint8_t *d_px = nullptr;
@@ -691,14 +694,17 @@ int check_tree_args(gbm_ctx *ctx, int32_t nfeat, const gbm_params *P, const gbm_
 }
 
 // In-bag compaction, level-wise device growth, host replay, prune, monotone.
+// `inbag_mask` NULL: the device mask was already built (gbm_round_sampled).
 int grow_tree(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
               const gbm_params *P, HostTree &T) {
     CK(cudaSetDevice(ctx->dev));
     TRY(ensure_round_buffers(ctx, nfeat, P));
     RoundFeat rf;
     TRY(setup_features(ctx, feat_idx, nfeat, rf));
-    std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
-    CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    if (inbag_mask) {
+        std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
+        CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    }
     int ntile = (int)((ctx->n + kCompTile - 1) / kCompTile);
     k_comp_count<<<ntile, 256, 0, ctx->st>>>(ctx->d_mask, ctx->n, ctx->d_cnt);
     CKL();
@@ -786,9 +792,9 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
                         ctx->d_ptask, ctx->d_tile_cnt, ctx->d_tile_off, ctx->d_nleft, ctx->d_nleft_g,
                         ctx->d_count64, ctx->d_nodes, ctx->d_lvl[0], ctx->d_lvl[1], ctx->d_ints, ctx->d_tree,
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
-                        ctx->d_poff, ctx->d_pF, ctx->d_pP};
+                        ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_sample};
     for (void *p : dev_ptrs) if (p) cudaFree(p);
-    void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask};
+    void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_sample};
     for (void *p : host_ptrs) if (p) cudaFreeHost(p);
     for (cudaEvent_t e : ctx->hist_ev) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->mark) if (e) cudaEventDestroy(e);
@@ -941,9 +947,9 @@ int gbm_build_tree(gbm_ctx *ctx, const double *grad, const double *hess, const u
     return GBM_OK;
 }
 
-int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
-              const gbm_params *P, gbm_tree_out *out, double *train_loss) {
-    if (!ctx || !inbag_mask || !feat_idx || !P || !out) return GBM_ERR_ARG;
+static int round_body(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
+                      const gbm_params *P, gbm_tree_out *out, double *train_loss) {
+    if (!ctx || !feat_idx || !P || !out) return GBM_ERR_ARG;
     if (!ctx->have_labels) return fail(ctx, GBM_ERR_STATE, "upload bins and labels before gbm_round");
     TRY(check_tree_args(ctx, nfeat, P, out));
     HostTree T;
@@ -978,6 +984,35 @@ int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, 
     if (train_loss) *train_loss = -ctx->h_loss[0] / (double)ctx->n_global;
     write_tree(T, need, out);
     return GBM_OK;
+}
+
+int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
+              const gbm_params *P, gbm_tree_out *out, double *train_loss) {
+    if (!inbag_mask) return GBM_ERR_ARG;
+    return round_body(ctx, inbag_mask, feat_idx, nfeat, P, out, train_loss);
+}
+
+int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *P,
+                      gbm_tree_out *out, double *train_loss) {
+    if (!ctx || !sampler || !P || !out || row_offset < 0) return GBM_ERR_ARG;
+    if (!ctx->have_labels) return fail(ctx, GBM_ERR_STATE, "upload bins and labels before gbm_round_sampled");
+    CK(cudaSetDevice(ctx->dev));
+    int64_t m = gbm_sampler_n_sub(sampler);
+    int32_t nf = gbm_sampler_n_feat(sampler);
+    if (m > ctx->sample_cap) {
+        TRY(halloc(ctx, &ctx->h_sample, (size_t)m));
+        TRY(dalloc(ctx, &ctx->d_sample, (size_t)m));
+        ctx->sample_cap = m;
+    }
+    ctx->feat_buf.resize((size_t)nf);
+    // the previous round's copy out of h_sample finished at that round's sync
+    int rc = gbm_sampler_next_rows(sampler, ctx->h_sample, ctx->feat_buf.data());
+    if (rc != GBM_OK) return fail(ctx, rc, "gbm_sampler_next_rows failed");
+    CK(cudaMemcpyAsync(ctx->d_sample, ctx->h_sample, sizeof(int32_t) * m, cudaMemcpyHostToDevice, ctx->st));
+    CK(cudaMemsetAsync(ctx->d_mask, 0, (size_t)ctx->n, ctx->st));
+    k_mask_from_rows<<<grid_for(m, 256), 256, 0, ctx->st>>>(ctx->d_sample, m, row_offset, ctx->n, ctx->d_mask);
+    CKL();
+    return round_body(ctx, nullptr, ctx->feat_buf.data(), nf, P, out, train_loss);
 }
 
 // ---- predict ------------------------------------------------------------------

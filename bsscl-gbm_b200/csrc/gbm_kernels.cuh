@@ -201,6 +201,15 @@ __global__ void k_comp_scatter(const uint8_t *__restrict__ mask, int64_t n, cons
     }
 }
 
+// In-bag mask of this rank's rows [row0, row0 + n) from global row ids.
+__global__ void k_mask_from_rows(const int32_t *__restrict__ rows, int64_t m, int64_t row0, int64_t n,
+                                 uint8_t *__restrict__ mask) {
+    int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= m) return;
+    int64_t r = (int64_t)rows[k] - row0;
+    if (r >= 0 && r < n) mask[r] = 1;
+}
+
 __global__ void k_count64(const int32_t *__restrict__ in, long long *__restrict__ out) {
     if (threadIdx.x == 0 && blockIdx.x == 0) *out = *in;
 }

@@ -129,6 +129,13 @@ int gbm_upload_labels(gbm_ctx *ctx, const uint8_t *y, const double class_w[2],
 int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
               const gbm_params *params, gbm_tree_out *out, double *train_loss);
 
+/* gbm_round with the round's subsample taken from `sampler` (over the
+ * global row ids of all ranks): the next draw's row ids are copied to the
+ * device and this rank's in-bag mask (rows row_offset .. row_offset+n-1) is
+ * built there.  Same results as gbm_round with the equivalent mask. */
+int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *params,
+                      gbm_tree_out *out, double *train_loss);
+
 /* One tree from caller-supplied float64 gradients and hessians [n] (this
  * rank's rows): the reference's internal seam _build_one_tree(X_bin, grad,
  * hess, sample_idx, feat_idx, n_features) (E:2397-2459), including the
@@ -192,13 +199,18 @@ int gbm_event_elapsed(gbm_ctx *ctx, int32_t a, int32_t b, float *ms);
 /* The reference's RandomState(seed) row/feature subsample stream
  * (E:2502-2517): every call reproduces the next round's sample_idx (first
  * n_sub of the cumulatively shuffled arange(n)) and sorted feat_idx.
- * `look_ahead` > 0 runs that many rounds ahead on a host thread. */
+ * `look_ahead` > 0 keeps that many rounds ready, drawn by two host threads
+ * (swap targets / swaps) while the caller trains. */
 int gbm_sampler_create(uint32_t seed, int64_t n, int32_t p, int64_t n_sub, int32_t n_feat,
                        int32_t subsample_on, int32_t colsample_on, int32_t look_ahead,
                        gbm_sampler **out);
 /* Any output may be NULL: sample_idx [n_sub] (reference order),
  * inbag_mask [n] (1 = in bag), feat_idx [n_feat]. */
 int gbm_sampler_next(gbm_sampler *s, int64_t *sample_idx, uint8_t *inbag_mask, int32_t *feat_idx);
+/* The next round as int32 row ids [n_sub] (reference order) + feat_idx. */
+int gbm_sampler_next_rows(gbm_sampler *s, int32_t *sample_rows, int32_t *feat_idx);
+int64_t gbm_sampler_n_sub(const gbm_sampler *s);
+int32_t gbm_sampler_n_feat(const gbm_sampler *s);
 void gbm_sampler_destroy(gbm_sampler *s);
 
 #ifdef __cplusplus

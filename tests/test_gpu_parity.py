@@ -184,3 +184,26 @@ def test_predict_proba_matches_oracle_random_forest(engine):
     F, _ = engine.predict(Xb, ens, 60, 0.08, -1.5, want_proba=False)
     Fo = O.predict_packed(Xb, ens, 60, 0.08) + (-1.5)
     assert np.abs(F - Fo).max() <= 1e-12
+
+
+def test_round_sampled_equals_round_with_mask(engine):
+    """gbm_round_sampled (device-built mask) == gbm_round with the same draw."""
+    from bsscl_gbm_b200 import Sampler
+    d, Xb, y, w2, base = _cfg1_engine(engine)
+    n, p = Xb.shape
+    prm = _params(max_leaves=31, max_depth=6, mcw=2.0)
+    s1 = Sampler(0, n, p, int(n * 0.8), int(p * 0.8), True, True, look_ahead=2)
+    trees_a = []
+    for _ in range(4):
+        t, _, _ = engine.round_sampled(s1, 0, prm, 64)
+        trees_a.append(t)
+    Fa = engine.get_F()
+    s1.close()
+    engine.upload_labels(y.astype(np.uint8), w2, base, n_global=len(y))
+    s2 = Sampler(0, n, p, int(n * 0.8), int(p * 0.8), True, True, look_ahead=0)
+    for r in range(4):
+        _, mask, feat = s2.next(want_sample=False, want_mask=True)
+        t, _, _ = engine.round(mask, feat, prm, 64)
+        _assert_tree_equal(trees_a[r], t, f"round {r}")
+    assert np.array_equal(engine.get_F(), Fa)
+    s2.close()
