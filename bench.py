@@ -299,6 +299,12 @@ def run_engine(args):
                          "frac": achieved / peak if peak else None, "traffic": None,
                          "hist_launches": st["hist_launches"], "hist_ms": st["hist_ms"],
                          "alg_bytes": st["hist_alg_bytes"]},
+            "breakdown_ms_per_round": {
+                "hist_kernel": st["hist_ms"] / args.steps,
+                "host_wait_sampler": st["host_sample_ms"] / args.steps,
+                "host_wait_device": st["host_sync_ms"] / args.steps,
+                "host_replay": st["host_replay_ms"] / args.steps,
+                "waves": st["waves"] / args.steps},
             "e2e": {"value": e2e, "unit": "rounds/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": st["kernel_launches"],

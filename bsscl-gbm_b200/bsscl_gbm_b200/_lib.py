@@ -57,7 +57,8 @@ class GbmPacked(C.Structure):
 class GbmStats(C.Structure):
     _fields_ = [("kernel_launches", C.c_int64), ("hist_launches", C.c_int64),
                 ("hist_rows", C.c_int64), ("waves", C.c_int64), ("hist_ms", C.c_double),
-                ("hist_alg_bytes", C.c_double)]
+                ("hist_alg_bytes", C.c_double), ("host_sample_ms", C.c_double),
+                ("host_sync_ms", C.c_double), ("host_replay_ms", C.c_double)]
 
 
 _lib = None

@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdarg>
 #include <cstdint>
@@ -119,6 +120,7 @@ struct gbm_ctx {
     bool profiling = false;
     long long hist_launches = 0, hist_rows = 0, waves = 0;
     double hist_ms = 0.0, alg_bytes = 0.0;
+    double host_sample_ms = 0.0, host_sync_ms = 0.0, host_replay_ms = 0.0;
     std::vector<cudaEvent_t> hist_ev;  // pairs recorded around k_hist launches
     int hist_ev_used = 0;
     cudaEvent_t mark[16] = {};
@@ -197,10 +199,21 @@ int scale_bits_for(double wmax) {
     return 62 - need;
 }
 
+double ms_since(std::chrono::steady_clock::time_point t0) {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+
 int sync_stream(gbm_ctx *ctx) {
-    if (ctx->comm) return gbm_comm_sync(ctx->comm, ctx->st, ctx->timeout_ms, ctx->err);
-    CK(cudaStreamSynchronize(ctx->st));
-    return GBM_OK;
+    auto t0 = std::chrono::steady_clock::now();
+    int rc = GBM_OK;
+    if (ctx->comm) {
+        rc = gbm_comm_sync(ctx->comm, ctx->st, ctx->timeout_ms, ctx->err);
+    } else {
+        cudaError_t e = cudaStreamSynchronize(ctx->st);
+        if (e != cudaSuccess) rc = fail(ctx, GBM_ERR_CUDA, "stream sync: %s", cudaGetErrorString(e));
+    }
+    ctx->host_sync_ms += ms_since(t0);
+    return rc;
 }
 
 // ---- per-round feature tables ---------------------------------------------
@@ -275,7 +288,17 @@ int ensure_round_buffers(gbm_ctx *ctx, int nf, const gbm_params *P) {
 
 // ---- launches -----------------------------------------------------------------
 
-int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int max_chunks) {
+// Rows per histogram CTA: about two waves of 2 CTAs per SM over the feature
+// blocks, a power of two in [1024, kChunk].
+int hist_chunk(int64_t rows, int nblocks) {
+    int64_t target = 148 * 2 * 2;
+    int64_t c = (rows * std::max(1, nblocks) + target - 1) / target;
+    int chunk = 1024;
+    while (chunk < c && chunk < kChunk) chunk <<= 1;
+    return chunk;
+}
+
+int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int max_chunks, int chunk) {
     if (max_chunks <= 0 || rf.blist.empty()) return GBM_OK;
     dim3 grid((unsigned)max_chunks, (unsigned)rf.blist.size());
     size_t smem = (size_t)kAccWords * sizeof(unsigned);
@@ -295,7 +318,7 @@ int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int max_c
     }
     k_hist<<<grid, kHistThreads, smem, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_htask,
                                                    ctx->d_hprefix, ntask_p, ctx->d_blist, ctx->d_fpos,
-                                                   ctx->d_skipb, rf.nf, ctx->d_q, ctx->d_stage);
+                                                   ctx->d_skipb, rf.nf, chunk, ctx->d_q, ctx->d_stage);
     CKL();
     if (ctx->profiling) CK(cudaEventRecord(e1, ctx->st));
     ctx->hist_launches++;
@@ -325,13 +348,14 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_count64, 1, ctx->st, ctx->timeout_ms, ctx->err));
         ng = ctx->d_count64;
     }
+    const int chunk = hist_chunk(ctx->n, (int)rf.blist.size());
     k_root_plan<<<1, 1, 0, ctx->st>>>(ctx->d_total, ng, ctx->d_nodes, ctx->d_htask, ctx->d_hprefix,
-                                      ints(ctx, I_NODES));
+                                      ints(ctx, I_NODES), chunk);
     CKL();
     k_zero_multi<<<dim3(grid_for(words, 256, 64), 1), 256, 0, ctx->st>>>(ctx->d_hprefix, ints(ctx, I_ONE),
                                                                          ctx->d_stage, words);
     CKL();
-    TRY(launch_hist(ctx, rf, ints(ctx, I_ONE), (int)((ctx->n + kChunk - 1) / kChunk)));
+    TRY(launch_hist(ctx, rf, ints(ctx, I_ONE), (int)((ctx->n + chunk - 1) / chunk), chunk));
     if (ctx->comm)
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words, ctx->st, ctx->timeout_ms, ctx->err));
     int fx = (rf.nf + kSplitWarps - 1) / kSplitWarps;
@@ -385,13 +409,15 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_nleft_g, W_ub, ctx->st, ctx->timeout_ms, ctx->err));
         gl = ctx->d_nleft_g;
     }
-    k_plan_hist<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ctx->d_nleft, gl, ctx->d_htask, ctx->d_hprefix);
+    int64_t chunk_rows = ctx->comm ? ctx->n : (ctx->n + 1) / 2;
+    const int chunk = hist_chunk(chunk_rows, (int)rf.blist.size());
+    k_plan_hist<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ctx->d_nleft, gl, ctx->d_htask, ctx->d_hprefix,
+                                        chunk);
     CKL();
     k_zero_multi<<<dim3(grid_for(words, 256, 64), W_ub), 256, 0, ctx->st>>>(ctx->d_hprefix, lvl_cnt, ctx->d_stage,
                                                                             words);
     CKL();
-    int64_t chunk_rows = ctx->comm ? ctx->n : (ctx->n + 1) / 2;
-    TRY(launch_hist(ctx, rf, lvl_cnt, (int)((chunk_rows + kChunk - 1) / kChunk) + W_ub));
+    TRY(launch_hist(ctx, rf, lvl_cnt, (int)((chunk_rows + chunk - 1) / chunk) + W_ub, chunk));
     if (ctx->comm)
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words * W_ub, ctx->st, ctx->timeout_ms, ctx->err));
     int fx = (rf.nf + kSplitWarps - 1) / kSplitWarps;
@@ -724,8 +750,11 @@ int grow_tree(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, 
     TRY(fetch_nodes(ctx));
     ctx->alg_bytes += (double)ctx->h_nodes[0].n * (rf.nf + 8);
     ctx->hist_rows += ctx->h_nodes[0].end;
+    auto t_rep = std::chrono::steady_clock::now();
+    double sync_before = ctx->host_sync_ms;
     if (P->grow_policy == 0) TRY(replay_leafwise(ctx, rf, P, T));
     else TRY(replay_depthwise(ctx, rf, P, T));
+    ctx->host_replay_ms += ms_since(t_rep) - (ctx->host_sync_ms - sync_before);
     post_prune(T, P->gamma);
     enforce_monotone(T, P->monotone);
     return GBM_OK;
@@ -1006,7 +1035,9 @@ int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, co
     }
     ctx->feat_buf.resize((size_t)nf);
     // the previous round's copy out of h_sample finished at that round's sync
+    auto t_s = std::chrono::steady_clock::now();
     int rc = gbm_sampler_next_rows(sampler, ctx->h_sample, ctx->feat_buf.data());
+    ctx->host_sample_ms += ms_since(t_s);
     if (rc != GBM_OK) return fail(ctx, rc, "gbm_sampler_next_rows failed");
     CK(cudaMemcpyAsync(ctx->d_sample, ctx->h_sample, sizeof(int32_t) * m, cudaMemcpyHostToDevice, ctx->st));
     CK(cudaMemsetAsync(ctx->d_mask, 0, (size_t)ctx->n, ctx->st));
@@ -1122,6 +1153,9 @@ int gbm_get_stats(gbm_ctx *ctx, gbm_stats *out) {
     out->waves = ctx->waves;
     out->hist_ms = ctx->hist_ms;
     out->hist_alg_bytes = ctx->alg_bytes;
+    out->host_sample_ms = ctx->host_sample_ms;
+    out->host_sync_ms = ctx->host_sync_ms;
+    out->host_replay_ms = ctx->host_replay_ms;
     return GBM_OK;
 }
 
@@ -1129,6 +1163,7 @@ int gbm_reset_stats(gbm_ctx *ctx) {
     if (!ctx) return GBM_ERR_ARG;
     ctx->launches = ctx->hist_launches = ctx->hist_rows = ctx->waves = 0;
     ctx->hist_ms = ctx->alg_bytes = 0.0;
+    ctx->host_sample_ms = ctx->host_sync_ms = ctx->host_replay_ms = 0.0;
     return GBM_OK;
 }
 

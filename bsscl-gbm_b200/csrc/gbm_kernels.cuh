@@ -224,7 +224,8 @@ __global__ void k_count64(const int32_t *__restrict__ in, long long *__restrict_
 // low with low, mid in [0, 2^17) and top signed, and each digit is summed in
 // its own 32-bit shared-memory word: at most kChunk = 2^14 rows per CTA keep
 // every digit sum inside 32 bits, and native 32-bit shared atomics are much
-// faster than 64-bit ones.  Each feature skips its most frequent bin (the
+// faster than 64-bit ones.  `chunk` (<= kChunk) rows per CTA is chosen per
+// launch to spread the work over every SM.  Each feature skips its most frequent bin (the
 // NaN bin, typically); that cell is rebuilt exactly by the split kernel as
 // node total - sum(other cells).  A task of one chunk stores its cells; a
 // task spread over several CTAs adds (hi, lo) words atomically into a zeroed
@@ -234,7 +235,7 @@ __global__ void __launch_bounds__(kHistThreads, 2)
 k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows,
        const HistTask *__restrict__ tasks, const int32_t *__restrict__ prefix,
        const int *__restrict__ ntask_p, const int32_t *__restrict__ blist,
-       const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
+       const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf, int chunk,
        const longlong2 *__restrict__ q, long long *__restrict__ stage_hist) {
     extern __shared__ unsigned acc[];   // [6][16][256]
     __shared__ int s_task;
@@ -256,8 +257,8 @@ k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ ro
     const HistTask tk = tasks[t];
     const bool single = (prefix[t + 1] - prefix[t]) == 1;
     const int blk = blist[blockIdx.y];
-    long long r0 = tk.begin + (long long)(cid - prefix[t]) * kChunk;
-    long long r1 = min(r0 + (long long)kChunk, tk.end);
+    long long r0 = tk.begin + (long long)(cid - prefix[t]) * chunk;
+    long long r1 = min(r0 + (long long)chunk, tk.end);
     unsigned mask = 0;
     int skip[kBlk];
 #pragma unroll
@@ -267,30 +268,38 @@ k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ ro
         skip[k] = sel ? (int)skipb[blk * kBlk + k] : -1;
     }
     const uint4 *xv = reinterpret_cast<const uint4 *>(xb) + (int64_t)blk * n;
+    const int lane = threadIdx.x & 31;
     long long tg = 0, th = 0;
-    for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
-        int row = rows[r];
-        uint4 v = __ldg(xv + row);
-        longlong2 qq = __ldg(q + row);
+    for (long long rb = r0 + (threadIdx.x & ~31); rb < r1; rb += blockDim.x) {
+        const long long r = rb + lane;
+        const bool valid = r < r1;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        longlong2 qq = make_longlong2(0, 0);
+        if (valid) {
+            int row = rows[r];
+            v = __ldg(xv + row);
+            qq = __ldg(q + row);
+        }
         tg += qq.x;
         th += qq.y;
-        unsigned g0 = (unsigned)qq.x & 0x1ffffu, g1 = (unsigned)(qq.x >> kDig) & 0x1ffffu;
-        unsigned g2 = (unsigned)(int)(qq.x >> (2 * kDig));
-        unsigned h0 = (unsigned)qq.y & 0x1ffffu, h1 = (unsigned)(qq.y >> kDig) & 0x1ffffu;
-        unsigned h2 = (unsigned)(int)(qq.y >> (2 * kDig));
+        unsigned dg[3] = {(unsigned)qq.x & 0x1ffffu, (unsigned)(qq.x >> kDig) & 0x1ffffu,
+                          (unsigned)(int)(qq.x >> (2 * kDig))};
+        unsigned dh[3] = {(unsigned)qq.y & 0x1ffffu, (unsigned)(qq.y >> kDig) & 0x1ffffu,
+                          (unsigned)(int)(qq.y >> (2 * kDig))};
         unsigned w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int k = 0; k < kBlk; k++) {
             if (mask & (1u << k)) {
                 int b = (w[k >> 2] >> ((k & 3) * 8)) & 0xff;
-                if (b != skip[k]) {
+                bool use = valid && b != skip[k];
+                if (use) {
                     unsigned *c = acc + k * kBins + b;
-                    atomicAdd(c + 0 * kBlk * kBins, g0);
-                    atomicAdd(c + 1 * kBlk * kBins, g1);
-                    atomicAdd(c + 2 * kBlk * kBins, g2);
-                    atomicAdd(c + 3 * kBlk * kBins, h0);
-                    atomicAdd(c + 4 * kBlk * kBins, h1);
-                    atomicAdd(c + 5 * kBlk * kBins, h2);
+                    atomicAdd(c + 0 * kBlk * kBins, dg[0]);
+                    atomicAdd(c + 1 * kBlk * kBins, dg[1]);
+                    atomicAdd(c + 2 * kBlk * kBins, dg[2]);
+                    atomicAdd(c + 3 * kBlk * kBins, dh[0]);
+                    atomicAdd(c + 4 * kBlk * kBins, dh[1]);
+                    atomicAdd(c + 5 * kBlk * kBins, dh[2]);
                 }
             }
         }
@@ -379,7 +388,7 @@ __device__ __forceinline__ DNode fresh_node(int depth, int parent) {
 // Root: node 0 holds all in-bag rows; one histogram task over them.
 __global__ void k_root_plan(const int32_t *__restrict__ n_local, const long long *__restrict__ n_global,
                             DNode *__restrict__ nodes, HistTask *__restrict__ ht,
-                            int32_t *__restrict__ prefix, int *__restrict__ node_count) {
+                            int32_t *__restrict__ prefix, int *__restrict__ node_count, int chunk) {
     if (threadIdx.x || blockIdx.x) return;
     long long ns = *n_local;
     DNode d = fresh_node(0, -1);
@@ -394,7 +403,7 @@ __global__ void k_root_plan(const int32_t *__restrict__ n_local, const long long
     t.left_small = 1;
     ht[0] = t;
     prefix[0] = 0;
-    prefix[1] = (int32_t)((ns + kChunk - 1) / kChunk);
+    prefix[1] = (int32_t)((ns + chunk - 1) / chunk);
     *node_count = 1;
 }
 
@@ -564,7 +573,7 @@ __global__ void k_part_copyback(const PartTask *__restrict__ tasks, const int *_
 __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ lvl,
                             const int *__restrict__ lvl_count, const long long *__restrict__ nl_local,
                             const long long *__restrict__ gl, HistTask *__restrict__ ht,
-                            int32_t *__restrict__ prefix) {
+                            int32_t *__restrict__ prefix, int chunk) {
     __shared__ int s_w[32];
     const int W = *lvl_count;
     int carry = 0;
@@ -582,7 +591,7 @@ __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ l
             t.stage = k;
             t.left_small = ls ? 1 : 0;
             ht[k] = t;
-            ch = (int)((t.end - t.begin + kChunk - 1) / kChunk);
+            ch = (int)((t.end - t.begin + chunk - 1) / chunk);
             p.nl = nl;
             p.gnl = gnl;
             p.left_small = t.left_small;

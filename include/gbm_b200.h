@@ -185,6 +185,9 @@ typedef struct {
                                   reference builds: rows x (nfeat + 8) of the
                                   root and of the smaller child of every
                                   executed split */
+    double host_sample_ms;     /* host time waiting for the sampler's draws */
+    double host_sync_ms;       /* host time waiting for the device */
+    double host_replay_ms;     /* host time in the best-first replay */
 } gbm_stats;
 
 int gbm_set_profiling(gbm_ctx *ctx, int32_t on);
