@@ -30,7 +30,7 @@ EXPORTS = (
     "gbm_sampler_create", "gbm_sampler_next", "gbm_sampler_destroy", "gbm_sampler_next_rows",
     "gbm_sampler_n_sub", "gbm_sampler_n_feat", "gbm_round_sampled",
     "gbm_set_profiling", "gbm_get_stats", "gbm_reset_stats", "gbm_event_record",
-    "gbm_event_elapsed",
+    "gbm_event_elapsed", "gbm_predict_noalloc",
 )
 
 
@@ -121,6 +121,8 @@ def lib():
     L.gbm_reset_stats.argtypes = [P]
     L.gbm_event_record.argtypes = [P, i32]
     L.gbm_event_elapsed.argtypes = [P, i32, i32, C.POINTER(C.c_float)]
+    L.gbm_predict_noalloc.argtypes = [P, i64, i32, P, P, P, P, P, P, i32, i32, f64, f64, P, P, P,
+                                      C.c_char_p, i32]
     _lib = L
     return L
 

@@ -34,6 +34,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -1182,6 +1183,150 @@ int gbm_event_elapsed(gbm_ctx *ctx, int32_t a, int32_t b, float *ms) {
     CK(cudaSetDevice(ctx->dev));
     CK(cudaEventSynchronize(ctx->mark[b]));
     CK(cudaEventElapsedTime(ms, ctx->mark[a], ctx->mark[b]));
+    return GBM_OK;
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// Predict that allocates nothing
+// ===========================================================================
+//
+// Some callers cannot call cudaMalloc: a serving process whose device memory
+// is one arena handed out by its own allocator, a framework that owns the
+// whole GPU, or a latency-bound path where an allocation (which may
+// synchronise the device) is not allowed.  gbm_predict_noalloc takes every
+// input and output as a device pointer the caller already owns and keeps its
+// only scratch -- the ensemble rewritten as 8-byte nodes, which the traversal
+// reads far better than the reference's 18-byte packed arrays -- in the
+// fixed device array below.  Every GPU that loads this library holds that
+// array (4 MiB) until the process exits.
+
+namespace {
+
+constexpr int kNoAllocMaxNodes = 1 << 19;   // 524,288 nodes: 1000 full depth-8 trees fit
+
+struct NoAllocScratch {
+    PNode nodes[kNoAllocMaxNodes];
+    int bad;          // set by the conversion kernel when the model is malformed
+};
+
+static __device__ __align__(256) NoAllocScratch g_noalloc;
+
+// Host-side addresses of g_noalloc, one per device.  In host code the name
+// g_noalloc is only a stand-in for the symbol, so the device address is
+// looked up once per device (with that device current) and cached.
+std::mutex g_noalloc_mu;
+NoAllocScratch *g_noalloc_ptr[64] = {};
+
+// Packed ensemble (device arrays) -> 8-byte nodes in the scratch array, with
+// the checks that make the traversal safe: features < p, thresholds in
+// [0, 255], children inside their tree and after their parent (so every
+// path ends), offsets non-decreasing and within the node count.
+__global__ void k_noalloc_pack(const int16_t *__restrict__ feat, const int64_t *__restrict__ thr,
+                               const int32_t *__restrict__ left, const int32_t *__restrict__ right,
+                               const int32_t *__restrict__ off, int32_t n_trees, int32_t n_nodes, int32_t p,
+                               NoAllocScratch *__restrict__ sc) {
+    int t = blockIdx.x;
+    if (t >= n_trees) return;
+    int o = off[t], o1 = off[t + 1];
+    if (o < 0 || o1 < o || o1 > n_nodes || o1 - o > 32767) {
+        if (threadIdx.x == 0) sc->bad = 1;
+        return;
+    }
+    if (o1 == o) {   // an empty tree would be read at its node 0
+        if (threadIdx.x == 0) sc->bad = 1;
+        return;
+    }
+    const int sz = o1 - o;
+    for (int k = threadIdx.x; k < sz; k += blockDim.x) {
+        int f = feat[o + k];
+        PNode nd;
+        nd.feat = (int16_t)f;
+        nd.pad = 0;
+        nd.thr = 0;
+        nd.left = nd.right = 0;
+        if (f >= 0) {
+            long long th = thr[o + k];
+            int l = left[o + k], r = right[o + k];
+            bool ok = f < p && th >= 0 && th <= 255 && l > k && l < sz && r > k && r < sz;
+            if (!ok) {
+                sc->bad = 1;
+                nd.feat = -1;
+            } else {
+                nd.thr = (uint8_t)th;
+                nd.left = (int16_t)l;
+                nd.right = (int16_t)r;
+            }
+        }
+        sc->nodes[o + k] = nd;
+    }
+}
+
+int noalloc_fail(char *errbuf, int32_t errlen, int code, const char *msg) {
+    if (errbuf && errlen > 0) {
+        std::strncpy(errbuf, msg, (size_t)errlen - 1);
+        errbuf[errlen - 1] = '\0';
+    }
+    return code;
+}
+
+}  // namespace
+
+extern "C" {
+
+// See include/gbm_b200.h.
+int gbm_predict_noalloc(const uint8_t *xbin_dev, int64_t n, int32_t p, const int16_t *features_dev,
+                        const int64_t *thresholds_dev, const double *values_dev, const int32_t *left_dev,
+                        const int32_t *right_dev, const int32_t *offsets_dev, int32_t n_trees, int32_t n_nodes,
+                        double learning_rate, double base_score, double *F_dev, double *proba_dev, void *stream,
+                        char *errbuf, int32_t errlen) {
+    if (!xbin_dev || n <= 0 || p <= 0 || n_trees <= 0 || !features_dev || !thresholds_dev || !values_dev ||
+        !left_dev || !right_dev || !offsets_dev || (!F_dev && !proba_dev))
+        return noalloc_fail(errbuf, errlen, GBM_ERR_ARG, "gbm_predict_noalloc: null pointer or empty size");
+    if (n_nodes <= 0 || n_nodes > kNoAllocMaxNodes) {
+        char m[160];
+        snprintf(m, sizeof m, "gbm_predict_noalloc: %d nodes; the fixed scratch holds at most %d", n_nodes,
+                 kNoAllocMaxNodes);
+        return noalloc_fail(errbuf, errlen, GBM_ERR_ARG, m);
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return noalloc_fail(errbuf, errlen, GBM_ERR_CUDA, "gbm_predict_noalloc: no current CUDA device");
+    NoAllocScratch *sc = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void *ptr = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc);
+            if (e != cudaSuccess || !ptr)
+                return noalloc_fail(errbuf, errlen, GBM_ERR_CUDA,
+                                    "gbm_predict_noalloc: cudaGetSymbolAddress of the scratch array failed");
+            g_noalloc_ptr[dev] = static_cast<NoAllocScratch *>(ptr);
+        }
+        sc = g_noalloc_ptr[dev];
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the array keeps the previous call's contents: clear the error flag
+    cudaError_t e = cudaMemsetAsync(&sc->bad, 0, sizeof(int), st);
+    if (e == cudaSuccess) {
+        k_noalloc_pack<<<n_trees, 256, 0, st>>>(features_dev, thresholds_dev, left_dev, right_dev, offsets_dev,
+                                                 n_trees, n_nodes, p, sc);
+        e = cudaGetLastError();
+    }
+    int bad = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&bad, &sc->bad, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return noalloc_fail(errbuf, errlen, GBM_ERR_CUDA, cudaGetErrorString(e));
+    if (bad)
+        return noalloc_fail(errbuf, errlen, GBM_ERR_ARG,
+                            "gbm_predict_noalloc: malformed ensemble (offsets, feature, threshold or child out "
+                            "of range, or a child not after its parent)");
+    k_predict<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(xbin_dev, n, p, sc->nodes, values_dev, offsets_dev,
+                                                          n_trees, learning_rate, base_score, F_dev, proba_dev);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return noalloc_fail(errbuf, errlen, GBM_ERR_CUDA, cudaGetErrorString(e));
     return GBM_OK;
 }
 

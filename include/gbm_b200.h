@@ -169,6 +169,33 @@ int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p);
 int gbm_predict_run(gbm_ctx *ctx, double learning_rate, double base_score);
 int gbm_predict_fetch(gbm_ctx *ctx, double *F_out, double *proba_out);
 
+/* Ensemble predict that allocates nothing.  No counterpart in the reference:
+ * this entry point exists for callers that cannot allocate device memory --
+ * a serving process whose GPU memory is one arena handed out by its own
+ * allocator, a framework that owns the whole device, or a latency-bound
+ * path where cudaMalloc (which can synchronise the device) is not allowed.
+ * Every input and output is a device pointer the caller owns: bins
+ * row-major uint8 [n][p] (ids clamped to bin_count-1, as gbm_predict
+ * reads them), the packed ensemble of _pack_tree_list (features int16,
+ * thresholds int64, values f64, left/right int32 [n_nodes], offsets int32
+ * [n_trees+1]), and F and/or proba f64 [n].  The only scratch -- the
+ * ensemble rewritten as 8-byte nodes -- lives in one fixed device array of
+ * at most 524,288 nodes (4 MiB) inside this library; every GPU that loads
+ * the library holds that array until the process exits.  Larger ensembles
+ * are rejected with GBM_ERR_ARG, as are malformed ones (a child that is not
+ * after its parent, a feature >= p, a threshold outside 0..255).  The
+ * first call on a device looks up the array's device address; make that
+ * first call before any stream capture.  All calls share the array, so
+ * calls that overlap on the GPU race: serialise them (one stream, or wait
+ * between calls).  The call runs on `stream` (a cudaStream_t, NULL = the
+ * default stream) of the current device and returns when the outputs are
+ * written.  `errbuf` (optional, `errlen` bytes) receives a message. */
+int gbm_predict_noalloc(const uint8_t *xbin_dev, int64_t n, int32_t p, const int16_t *features_dev,
+                        const int64_t *thresholds_dev, const double *values_dev, const int32_t *left_dev,
+                        const int32_t *right_dev, const int32_t *offsets_dev, int32_t n_trees,
+                        int32_t n_nodes, double learning_rate, double base_score, double *F_dev,
+                        double *proba_dev, void *stream, char *errbuf, int32_t errlen);
+
 /* Synchronise the context's stream; returns the first asynchronous error. */
 int gbm_sync(gbm_ctx *ctx);
 
