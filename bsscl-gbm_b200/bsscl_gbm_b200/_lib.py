@@ -30,7 +30,8 @@ EXPORTS = (
     "gbm_sampler_create", "gbm_sampler_next", "gbm_sampler_destroy", "gbm_sampler_next_rows",
     "gbm_sampler_n_sub", "gbm_sampler_n_feat", "gbm_round_sampled",
     "gbm_set_profiling", "gbm_get_stats", "gbm_reset_stats", "gbm_event_record",
-    "gbm_event_elapsed", "gbm_predict_noalloc",
+    "gbm_event_elapsed", "gbm_predict_noalloc", "gbm_fit_rounds", "gbm_upload_bins_u16",
+    "gbm_set_l2_flush",
 )
 
 
@@ -58,7 +59,8 @@ class GbmStats(C.Structure):
     _fields_ = [("kernel_launches", C.c_int64), ("hist_launches", C.c_int64),
                 ("hist_rows", C.c_int64), ("waves", C.c_int64), ("hist_ms", C.c_double),
                 ("hist_alg_bytes", C.c_double), ("host_sample_ms", C.c_double),
-                ("host_sync_ms", C.c_double), ("host_replay_ms", C.c_double)]
+                ("host_sync_ms", C.c_double), ("host_replay_ms", C.c_double),
+                ("flush_ms", C.c_double)]
 
 
 _lib = None
@@ -114,6 +116,10 @@ def lib():
     L.gbm_sampler_n_feat.restype = i32
     L.gbm_round_sampled.argtypes = [P, P, i64, C.POINTER(GbmParams), C.POINTER(GbmTreeOut),
                                     C.POINTER(C.c_double)]
+    L.gbm_upload_bins_u16.argtypes = [P, P, i64, i32, P]
+    L.gbm_set_l2_flush.argtypes = [P, i64]
+    L.gbm_fit_rounds.argtypes = [P, P, i64, C.POINTER(GbmParams), i32, C.POINTER(GbmTreeOut),
+                                 P]
     L.gbm_sampler_destroy.argtypes = [P]
     L.gbm_sampler_destroy.restype = None
     L.gbm_set_profiling.argtypes = [P, i32]
@@ -179,12 +185,24 @@ class Engine:
                                              timeout_ms), "gbm_ctx_init_comm")
 
     # -- training --
-    def upload_bins(self, xbin_u8, counts):
-        xb = np.ascontiguousarray(xbin_u8, dtype=np.uint8)
+    def upload_bins(self, xbin, counts):
+        """Bins [n][p] as uint8 (gbm_upload_bins) or the reference's uint16
+        (gbm_upload_bins_u16, narrowed on the device)."""
         cnt = np.ascontiguousarray(counts, dtype=np.int32)
-        n, p = xb.shape
+        if np.asarray(xbin).dtype == np.uint16:
+            xb = np.ascontiguousarray(xbin)
+            n, p = xb.shape
+            rc = self._L.gbm_upload_bins_u16(self._h, ptr(xb), n, p, ptr(cnt))
+        else:
+            xb = np.ascontiguousarray(xbin, dtype=np.uint8)
+            n, p = xb.shape
+            rc = self._L.gbm_upload_bins(self._h, ptr(xb), n, p, ptr(cnt))
         self.n, self.p = n, p
-        self.check(self._L.gbm_upload_bins(self._h, ptr(xb), n, p, ptr(cnt)), "gbm_upload_bins")
+        self.check(rc, "gbm_upload_bins")
+
+    def set_l2_flush(self, nbytes):
+        """Benchmark aid: evict L2 at the start of every round (0 = off)."""
+        self.check(self._L.gbm_set_l2_flush(self._h, int(nbytes)), "gbm_set_l2_flush")
 
     def upload_labels(self, y01, w2, base_score, n_global=0):
         y = np.ascontiguousarray(y01, dtype=np.uint8)
@@ -218,6 +236,28 @@ class Engine:
         self.check(self._L.gbm_round_sampled(self._h, sampler._h, int(row_offset), C.byref(params),
                                              C.byref(out), C.byref(loss)), "gbm_round_sampled")
         return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value), leaf
+
+    def fit_rounds(self, sampler, row_offset, params: GbmParams, capacity, n_rounds):
+        """n_rounds rounds queued back to back (gbm_fit_rounds): a list of
+        (tree, train_loss), the same as n_rounds round_sampled calls."""
+        n_rounds = int(n_rounds)
+        arrays = []
+        outs = (GbmTreeOut * max(1, n_rounds))()
+        for r in range(n_rounds):
+            a = (np.empty(capacity, np.int32), np.empty(capacity, np.int64),
+                 np.empty(capacity, np.float64), np.empty(capacity, np.int32),
+                 np.empty(capacity, np.int32), np.empty(capacity, np.float64))
+            arrays.append(a)
+            outs[r] = GbmTreeOut(capacity, ptr(a[0]), ptr(a[1]), ptr(a[2]), ptr(a[3]), ptr(a[4]),
+                                 ptr(a[5]), 0, None)
+        losses = np.zeros(max(1, n_rounds), np.float64)
+        self.check(self._L.gbm_fit_rounds(self._h, sampler._h, int(row_offset), C.byref(params),
+                                          n_rounds, outs, ptr(losses)), "gbm_fit_rounds")
+        res = []
+        for r in range(n_rounds):
+            tf, tt, tv, tl, tr, sg = arrays[r]
+            res.append(((tf, tt, tv, tl, tr, int(outs[r].n_nodes), sg), float(losses[r])))
+        return res
 
     def build_tree(self, grad, hess, inbag_mask, feat_idx, params: GbmParams, capacity):
         """One tree from given gradients (the reference's _build_one_tree seam)."""

@@ -453,8 +453,14 @@ class HybridHistGBMNumbaV1_0_1:
             uid = [Engine.nccl_unique_id() if rk == 0 else None]
             dist.broadcast_object_list(uid, src=0)
             eng.init_comm(uid[0], ws, rk)
-        Xd = binning.device_bins(X_bin[lo:hi], self.feature_bin_counts)
-        eng.upload_bins(Xd, self.feature_bin_counts)
+        if int(np.max(self.feature_bin_counts)) > 256:
+            binning.device_bins(X_bin[:1], self.feature_bin_counts)   # raises the ValueError
+        # uint16 (the reference's bin dtype) and uint8 ids go up as they are;
+        # the device clamps and narrows them
+        Xr = X_bin[lo:hi]
+        if Xr.dtype not in (np.uint8, np.uint16):
+            Xr = binning.device_bins(Xr, self.feature_bin_counts)
+        eng.upload_bins(Xr, self.feature_bin_counts)
         eng.upload_labels(y[lo:hi].astype(np.uint8), w2, self.base_score_, n_global=n)
         self.scale_bits_ = eng.scale_bits()
         params = self._params_struct()
@@ -462,31 +468,41 @@ class HybridHistGBMNumbaV1_0_1:
         F_val = np.full(len(y_val), self.base_score_) if y_val is not None else None
         best_val = np.inf
         no_improve = 0
+        # Rounds are queued on the GPU in batches (gbm_fit_rounds); the
+        # per-round bookkeeping below runs on each batch's results in order.
+        # With early stopping a batch may train a few rounds past the stop;
+        # they are dropped, so the kept trees are the reference's.
+        batch = self.n_estimators if X_val_bin is None else 32
         try:
-            for m in range(self.n_estimators):
-                tree, loss, _ = eng.round_sampled(sampler, lo, params, cap)
-                self.trees.append(tree)
-                self.train_loss_history_.append(loss)
-                val_loss = None
-                if X_val_bin is not None:
-                    F_val += self.learning_rate * _predict_tree_host(X_val_bin, tree)
-                    val_loss = _logloss(y_val, F_val)
-                    self.val_loss_history_.append(val_loss)
-                if self.verbose and ((m + 1) % 20 == 0 or m == 0):
-                    msg = f"  Tree {m + 1:>3}/{self.n_estimators}  |  train-loss: {loss:.6f}"
-                    if val_loss is not None:
-                        msg += f"  |  val-loss: {val_loss:.6f}"
-                    print(msg)
-                if self.early_stopping_rounds is not None and val_loss is not None:
-                    if val_loss < best_val:
-                        best_val = val_loss
-                        self.best_iteration_ = m
-                        no_improve = 0
-                    else:
-                        no_improve += 1
-                        if no_improve >= self.early_stopping_rounds:
-                            self.trees = self.trees[:self.best_iteration_ + 1]
-                            break
+            m = 0
+            stop = False
+            while m < self.n_estimators and not stop:
+                k = min(batch, self.n_estimators - m)
+                for tree, loss in eng.fit_rounds(sampler, lo, params, cap, k):
+                    self.trees.append(tree)
+                    self.train_loss_history_.append(loss)
+                    val_loss = None
+                    if X_val_bin is not None:
+                        F_val += self.learning_rate * _predict_tree_host(X_val_bin, tree)
+                        val_loss = _logloss(y_val, F_val)
+                        self.val_loss_history_.append(val_loss)
+                    if self.verbose and ((m + 1) % 20 == 0 or m == 0):
+                        msg = f"  Tree {m + 1:>3}/{self.n_estimators}  |  train-loss: {loss:.6f}"
+                        if val_loss is not None:
+                            msg += f"  |  val-loss: {val_loss:.6f}"
+                        print(msg)
+                    if self.early_stopping_rounds is not None and val_loss is not None:
+                        if val_loss < best_val:
+                            best_val = val_loss
+                            self.best_iteration_ = m
+                            no_improve = 0
+                        else:
+                            no_improve += 1
+                            if no_improve >= self.early_stopping_rounds:
+                                self.trees = self.trees[:self.best_iteration_ + 1]
+                                stop = True
+                                break
+                    m += 1
         finally:
             sampler.close()
         self.n_trees_fitted_ = len(self.trees)

@@ -184,6 +184,29 @@ int gbm_comm_sync(gbm_comm *c, cudaStream_t st, int timeout_ms, std::string &err
     }
 }
 
+int gbm_comm_wait_event(gbm_comm *c, cudaEvent_t ev, int timeout_ms, std::string &err) {
+    auto t0 = clk::now();
+    for (;;) {
+        cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return GBM_OK;
+        if (e != cudaErrorNotReady) {
+            err = std::string("stream error: ") + cudaGetErrorString(e);
+            return GBM_ERR_CUDA;
+        }
+        if (c) {
+            ncclResult_t s = ncclSuccess;
+            if (api().CommGetAsyncError(c->comm, &s) == ncclSuccess && s != ncclSuccess && s != ncclInProgress)
+                return comm_fail(c, err, GBM_ERR_COMM, "collective", s);
+        }
+        if (std::chrono::duration_cast<std::chrono::milliseconds>(clk::now() - t0).count() > timeout_ms) {
+            if (c) return comm_fail(c, err, GBM_ERR_TIMEOUT, "event wait (a peer may have left)", ncclInProgress);
+            err = "event wait timed out";
+            return GBM_ERR_TIMEOUT;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(c ? 20 : 5));
+    }
+}
+
 int gbm_comm_check_alive(gbm_comm *c, int timeout_ms, std::string &err) {
     if (!c) return GBM_OK;
     if (c->broken) {

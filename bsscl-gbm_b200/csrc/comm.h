@@ -23,6 +23,8 @@ int gbm_comm_allreduce_f64(gbm_comm *c, double *buf, int64_t count, cudaStream_t
                            std::string &err);
 // Bounded stream synchronisation that also watches the communicator.
 int gbm_comm_sync(gbm_comm *c, cudaStream_t st, int timeout_ms, std::string &err);
+// The same for one event (c may be NULL: a bounded wait only).
+int gbm_comm_wait_event(gbm_comm *c, cudaEvent_t ev, int timeout_ms, std::string &err);
 int gbm_comm_check_alive(gbm_comm *c, int timeout_ms, std::string &err);
 int gbm_comm_rank(const gbm_comm *c);
 int gbm_comm_size(const gbm_comm *c);

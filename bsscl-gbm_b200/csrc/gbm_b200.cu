@@ -41,6 +41,7 @@
 
 #include "../../include/gbm_b200.h"
 #include "comm.h"
+#include "sampler_internal.h"
 #include "gbm_kernels.cuh"
 
 using namespace gbm;
@@ -99,9 +100,34 @@ struct gbm_ctx {
     int *h_list = nullptr;
     double *h_loss = nullptr;
     uint8_t *h_mask = nullptr;
-    int32_t *h_sample = nullptr, *d_sample = nullptr;   // gbm_round_sampled staging
-    int64_t sample_cap = 0;
     std::vector<int32_t> feat_buf;
+
+    // Rounds in flight: per-slot pinned staging (so no copy waits for the
+    // stream) and a completion event.  gbm_round* use slot 0 and wait at the
+    // end; gbm_fit_rounds keeps up to kRing rounds queued.
+    struct Slot {
+        int32_t *h_tg = nullptr, *d_tg = nullptr;   // the round's row swap targets
+        int32_t *h_feat = nullptr;     // fidx [p] | blist [nblk]
+        int16_t *h_fpos = nullptr;     // [nblk * 16]
+        TreeOut *h_tout = nullptr;
+        double *h_loss = nullptr;
+        cudaEvent_t copied = nullptr, done = nullptr;
+    };
+    static constexpr int kRing = 4;
+    Slot slot[kRing];
+    bool slots_ready = false;
+    cudaStream_t cst = nullptr;        // the samplers' copies and row shuffles
+    // The bound sampler's row permutation lives here: round r turns its swap
+    // targets into a shuffle and composes perm[r % 5] = perm[(r-1) % 5][S]
+    // on cst, ahead of the round's growth.
+    gbm_sampler *samp = nullptr;
+    int64_t samp_taken = 0;
+    int64_t shuf_n = 0;
+    int32_t *d_perm[kRing + 1] = {};
+    int32_t *d_head = nullptr, *d_nxt = nullptr, *d_m = nullptr, *d_mp = nullptr;
+    TreeOut *d_tout = nullptr;
+    int32_t *d_mono = nullptr, *h_mono = nullptr;
+    int replay_smem = 0;               // dynamic shared memory the replay kernels may use
 
     // predict
     uint8_t *d_px = nullptr;
@@ -124,6 +150,13 @@ struct gbm_ctx {
     double host_sample_ms = 0.0, host_sync_ms = 0.0, host_replay_ms = 0.0;
     std::vector<cudaEvent_t> hist_ev;  // pairs recorded around k_hist launches
     int hist_ev_used = 0;
+    // benchmark aid: an L2 eviction at the start of every round
+    uint8_t *d_flush = nullptr;
+    size_t flush_bytes = 0;
+    unsigned flush_count = 0;
+    double flush_ms = 0.0;
+    std::vector<cudaEvent_t> flush_ev;
+    int flush_ev_used = 0;
     cudaEvent_t mark[16] = {};
 };
 
@@ -225,7 +258,45 @@ struct RoundFeat {
     std::vector<int16_t> fpos;
 };
 
-int setup_features(gbm_ctx *ctx, const int32_t *fidx, int nf, RoundFeat &rf) {
+// Per-slot pinned staging, sized for the data.
+int ensure_slots(gbm_ctx *ctx) {
+    if (!ctx->slots_ready) {   // once per gbm_upload_bins (sizes follow p)
+        for (auto &s : ctx->slot) {
+            TRY(halloc(ctx, &s.h_feat, (size_t)ctx->p + ctx->nblk));
+            TRY(halloc(ctx, &s.h_fpos, (size_t)ctx->nblk * kBlk));
+            TRY(halloc(ctx, &s.h_tout, 1));
+            TRY(halloc(ctx, &s.h_loss, 1));
+            if (!s.copied) CK(cudaEventCreateWithFlags(&s.copied, cudaEventDisableTiming));
+            if (!s.done) CK(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+        }
+        TRY(dalloc(ctx, &ctx->d_tout, 1));
+        TRY(dalloc(ctx, &ctx->d_mono, (size_t)ctx->p));
+        TRY(halloc(ctx, &ctx->h_mono, (size_t)ctx->p));
+        ctx->slots_ready = true;
+    }
+    return GBM_OK;
+}
+
+// Row shuffle buffers for a sampler over N global rows.
+int ensure_shuffle(gbm_ctx *ctx, int64_t N) {
+    if (N <= ctx->shuf_n) return GBM_OK;
+    for (auto &s : ctx->slot) {
+        TRY(halloc(ctx, &s.h_tg, (size_t)N + 8));
+        TRY(dalloc(ctx, &s.d_tg, (size_t)N + 8));
+    }
+    for (auto &q : ctx->d_perm) TRY(dalloc(ctx, &q, (size_t)N));
+    TRY(dalloc(ctx, &ctx->d_head, (size_t)N));
+    TRY(dalloc(ctx, &ctx->d_nxt, (size_t)N));
+    TRY(dalloc(ctx, &ctx->d_m, (size_t)N));
+    TRY(dalloc(ctx, &ctx->d_mp, (size_t)N));
+    ctx->shuf_n = N;
+    return GBM_OK;
+}
+
+// The round's feature tables, built in the slot's pinned buffers and copied
+// on the engine stream (the previous round's kernels have read theirs).
+int setup_features(gbm_ctx *ctx, int si, const int32_t *fidx, int nf, RoundFeat &rf) {
+    gbm_ctx::Slot &s = ctx->slot[si];
     rf.nf = nf;
     rf.fpos.assign((size_t)ctx->nblk * kBlk, (int16_t)-1);
     for (int jj = 0; jj < nf; jj++) {
@@ -240,17 +311,32 @@ int setup_features(gbm_ctx *ctx, const int32_t *fidx, int nf, RoundFeat &rf) {
         for (int k = 0; k < kBlk; k++) any |= rf.fpos[(size_t)b * kBlk + k] >= 0;
         if (any) rf.blist.push_back(b);
     }
-    CK(cudaMemcpyAsync(ctx->d_fidx, fidx, sizeof(int32_t) * nf, cudaMemcpyHostToDevice, ctx->st));
-    CK(cudaMemcpyAsync(ctx->d_fpos, rf.fpos.data(), sizeof(int16_t) * rf.fpos.size(), cudaMemcpyHostToDevice, ctx->st));
-    CK(cudaMemcpyAsync(ctx->d_blist, rf.blist.data(), sizeof(int32_t) * rf.blist.size(), cudaMemcpyHostToDevice, ctx->st));
+    std::memcpy(s.h_feat, fidx, sizeof(int32_t) * nf);
+    std::memcpy(s.h_feat + ctx->p, rf.blist.data(), sizeof(int32_t) * rf.blist.size());
+    std::memcpy(s.h_fpos, rf.fpos.data(), sizeof(int16_t) * rf.fpos.size());
+    CK(cudaMemcpyAsync(ctx->d_fidx, s.h_feat, sizeof(int32_t) * nf, cudaMemcpyHostToDevice, ctx->st));
+    CK(cudaMemcpyAsync(ctx->d_fpos, s.h_fpos, sizeof(int16_t) * rf.fpos.size(), cudaMemcpyHostToDevice, ctx->st));
+    CK(cudaMemcpyAsync(ctx->d_blist, s.h_feat + ctx->p, sizeof(int32_t) * rf.blist.size(), cudaMemcpyHostToDevice,
+                       ctx->st));
     return GBM_OK;
 }
 
-// Level widths: level L expands at most min(2^L, M) parents, M = max_leaves-1
-// for best-first growth (no tree uses more splits), 2^(D-1) for depth-wise.
+// Level widths: level L expands at most min(2^L, M) parents.  Depth-wise
+// growth and best-first growth up to depth kSpecDepth use M = 2^(D-1), so
+// every node that can split is expanded and the tree is replayed on the
+// device with no host round trip.  Deeper best-first trees use M =
+// max_leaves - 1 (no tree uses more splits) and expand on demand what the
+// ranking left out.
+constexpr int kSpecDepth = 9;
+constexpr int kReplaySmemMax = 160 * 1024;   // node table copy of the replay kernels
+
+bool full_spec(const gbm_params *P) { return P->grow_policy == 1 || P->max_depth <= kSpecDepth; }
+
 int level_cap(const gbm_params *P) {
-    if (P->grow_policy == 0) return std::max(1, P->max_leaves - 1);
-    return 1 << std::min(P->max_depth - 1, 12);
+    if (P->grow_policy == 1) return 1 << std::min(P->max_depth - 1, 12);
+    int m = std::max(1, P->max_leaves - 1);
+    if (full_spec(P)) m = std::max(m, 1 << (P->max_depth - 1));
+    return m;
 }
 
 int level_width(const gbm_params *P, int L) {
@@ -283,8 +369,17 @@ int ensure_round_buffers(gbm_ctx *ctx, int nf, const gbm_params *P) {
         TRY(dalloc(ctx, &ctx->d_ptask, (size_t)ctx->stage_slots));
         TRY(dalloc(ctx, &ctx->d_nleft, (size_t)ctx->stage_slots));
         TRY(dalloc(ctx, &ctx->d_nleft_g, (size_t)ctx->stage_slots));
+        int smem = (int)(sizeof(RNode) * (size_t)ctx->nmax);
+        ctx->replay_smem = 0;
+        if (smem <= kReplaySmemMax) ctx->replay_smem = smem;
     }
     return GBM_OK;
+}
+
+// The tree can be replayed on the device: every node it can need is
+// expanded, and the node table fits the replay's shared-memory copy.
+bool device_replay(const gbm_ctx *ctx, const gbm_params *P) {
+    return full_spec(P) && ctx->replay_smem > 0 && ctx->replay_smem >= (int)(sizeof(RNode) * (size_t)ctx->nmax);
 }
 
 // ---- launches -----------------------------------------------------------------
@@ -326,7 +421,7 @@ int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int max_c
     return GBM_OK;
 }
 
-// Fold the k_hist event pairs recorded since the last sync into the totals.
+// Fold the event pairs recorded since the last wait into the totals.
 int collect_hist_events(gbm_ctx *ctx) {
     for (int k = 0; k + 1 < ctx->hist_ev_used; k += 2) {
         float ms = 0.f;
@@ -334,6 +429,32 @@ int collect_hist_events(gbm_ctx *ctx) {
         ctx->hist_ms += ms;
     }
     ctx->hist_ev_used = 0;
+    for (int k = 0; k + 1 < ctx->flush_ev_used; k += 2) {
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, ctx->flush_ev[k], ctx->flush_ev[k + 1]));
+        ctx->flush_ms += ms;
+    }
+    ctx->flush_ev_used = 0;
+    return GBM_OK;
+}
+
+// The L2 eviction of gbm_set_l2_flush: a write of the scratch buffer on the
+// engine stream before the round's growth (timed when profiling).
+int flush_l2(gbm_ctx *ctx) {
+    if (!ctx->flush_bytes) return GBM_OK;
+    cudaEvent_t e1 = nullptr;
+    if (ctx->profiling) {
+        while ((int)ctx->flush_ev.size() < ctx->flush_ev_used + 2) {
+            cudaEvent_t e;
+            CK(cudaEventCreate(&e));
+            ctx->flush_ev.push_back(e);
+        }
+        CK(cudaEventRecord(ctx->flush_ev[ctx->flush_ev_used], ctx->st));
+        e1 = ctx->flush_ev[ctx->flush_ev_used + 1];
+        ctx->flush_ev_used += 2;
+    }
+    CK(cudaMemsetAsync(ctx->d_flush, (int)(++ctx->flush_count & 0xff), ctx->flush_bytes, ctx->st));
+    if (e1) CK(cudaEventRecord(e1, ctx->st));
     return GBM_OK;
 }
 
@@ -720,18 +841,14 @@ int check_tree_args(gbm_ctx *ctx, int32_t nfeat, const gbm_params *P, const gbm_
     return GBM_OK;
 }
 
-// In-bag compaction, level-wise device growth, host replay, prune, monotone.
-// `inbag_mask` NULL: the device mask was already built (gbm_round_sampled).
-int grow_tree(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
-              const gbm_params *P, HostTree &T) {
-    CK(cudaSetDevice(ctx->dev));
-    TRY(ensure_round_buffers(ctx, nfeat, P));
-    RoundFeat rf;
-    TRY(setup_features(ctx, feat_idx, nfeat, rf));
-    if (inbag_mask) {
-        std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
-        CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
-    }
+int tree_need(const gbm_params *P) {
+    return P->grow_policy == 0 ? 2 * P->max_leaves + 2 : (1 << (P->max_depth + 1)) - 1;
+}
+
+// Enqueue the in-bag compaction and the level-wise growth; the round's
+// in-bag mask is on the device and its feature tables are staged.
+int enqueue_grow(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
+    TRY(flush_l2(ctx));
     int ntile = (int)((ctx->n + kCompTile - 1) / kCompTile);
     k_comp_count<<<ntile, 256, 0, ctx->st>>>(ctx->d_mask, ctx->n, ctx->d_cnt);
     CKL();
@@ -748,8 +865,15 @@ int grow_tree(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, 
                          ints(ctx, I_LVL0 + 1 - cur), W));
         cur = 1 - cur;
     }
+    return GBM_OK;
+}
+
+// The host replay, for best-first trees deeper than kSpecDepth: one node
+// table fetch, on-demand expansion of what the level ranking left out,
+// post-prune and monotone clipping.
+int replay_on_host(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, HostTree &T) {
     TRY(fetch_nodes(ctx));
-    ctx->alg_bytes += (double)ctx->h_nodes[0].n * (rf.nf + 8);
+    ctx->alg_bytes += (double)(ctx->h_nodes[0].end - ctx->h_nodes[0].begin) * (rf.nf + 8);
     ctx->hist_rows += ctx->h_nodes[0].end;
     auto t_rep = std::chrono::steady_clock::now();
     double sync_before = ctx->host_sync_ms;
@@ -758,6 +882,85 @@ int grow_tree(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, 
     ctx->host_replay_ms += ms_since(t_rep) - (ctx->host_sync_ms - sync_before);
     post_prune(T, P->gamma);
     enforce_monotone(T, P->monotone);
+    return GBM_OK;
+}
+
+// Monotone constraints of this call -> the device (before any round of the
+// call is queued; every earlier call has finished).
+int stage_mono(gbm_ctx *ctx, const gbm_params *P) {
+    if (!P->monotone) return GBM_OK;
+    std::memcpy(ctx->h_mono, P->monotone, sizeof(int32_t) * ctx->p);
+    CK(cudaMemcpyAsync(ctx->d_mono, ctx->h_mono, sizeof(int32_t) * ctx->p, cudaMemcpyHostToDevice, ctx->st));
+    return GBM_OK;
+}
+
+// Enqueue the device replay: the tree into d_tout (host layout) and d_tree
+// (the F update's layout).
+int enqueue_replay(gbm_ctx *ctx, const gbm_params *P) {
+    RParams R;
+    R.lam = P->reg_lambda;
+    R.gamma = P->gamma;
+    R.mcw = P->min_child_weight;
+    R.msl = P->min_samples_leaf;
+    R.max_depth = P->max_depth;
+    R.max_leaves = P->max_leaves;
+    R.policy = P->grow_policy;
+    R.has_mono = P->monotone != nullptr;
+    size_t smem = sizeof(RNode) * (size_t)ctx->nmax;
+    if (P->grow_policy == 0)
+        k_replay_leaf<<<1, 32, smem, ctx->st>>>(ctx->d_nodes, ints(ctx, I_NODES), R, ctx->d_mono, ctx->d_tout,
+                                                ctx->d_tree);
+    else
+        k_replay_depth<<<1, 32, smem, ctx->st>>>(ctx->d_nodes, ints(ctx, I_NODES), R, ctx->d_mono, ctx->d_tout,
+                                                 ctx->d_tree);
+    CKL();
+    return GBM_OK;
+}
+
+// Enqueue the F update, the next gradients and the train loss of the tree
+// in d_tree; the loss goes to the slot's pinned buffer.
+int enqueue_update(gbm_ctx *ctx, const gbm_params *P, bool want_leaf, double *h_loss) {
+    double scale = std::ldexp(1.0, ctx->S);
+    k_update<<<ctx->upd_blocks, kUpdThreads, 0, ctx->st>>>(
+        ctx->d_tree, ctx->d_xb, ctx->n, ctx->d_y, ctx->w[0], ctx->w[1], P->learning_rate, scale, ctx->d_F,
+        ctx->d_q, want_leaf ? ctx->d_leaf : nullptr, ctx->d_loss_part);
+    CKL();
+    k_sum_partials<<<1, 256, 0, ctx->st>>>(ctx->d_loss_part, ctx->upd_blocks, ctx->d_loss);
+    CKL();
+    if (ctx->comm) TRY(gbm_comm_allreduce_f64(ctx->comm, ctx->d_loss, 1, ctx->st, ctx->timeout_ms, ctx->err));
+    CK(cudaMemcpyAsync(h_loss, ctx->d_loss, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
+    return GBM_OK;
+}
+
+// Wait (bounded, watching the communicator) for a slot's round to finish.
+int wait_slot(gbm_ctx *ctx, int si) {
+    auto t0 = std::chrono::steady_clock::now();
+    int rc = gbm_comm_wait_event(ctx->comm, ctx->slot[si].done, ctx->timeout_ms, ctx->err);
+    ctx->host_sync_ms += ms_since(t0);
+    return rc;
+}
+
+void write_tree_dev(const TreeOut &T, int need, gbm_tree_out *out) {
+    for (int k = 0; k < need; k++) {
+        bool in = k < 256;
+        out->tf[k] = in ? T.tf[k] : -1;
+        out->tt[k] = in ? T.tt[k] : 0;
+        out->tv[k] = in ? T.tv[k] : 0.0;
+        out->tl[k] = in ? T.tl[k] : -1;
+        out->tr[k] = in ? T.tr[k] : -1;
+        out->sg[k] = in ? T.sg[k] : 0.0;
+    }
+    out->n_nodes = T.nc;
+}
+
+// A finished slot -> the caller's tree and loss, and the statistics.
+int harvest(gbm_ctx *ctx, int si, int nf, const gbm_params *P, gbm_tree_out *out, double *train_loss) {
+    const TreeOut &T = *ctx->slot[si].h_tout;
+    if (T.status != 0) return fail(ctx, GBM_ERR_STATE, "internal: the device replay reached an unexpanded node");
+    ctx->alg_bytes += (double)T.alg_rows * (nf + 8);
+    ctx->hist_rows += T.root_rows;
+    write_tree_dev(T, tree_need(P), out);
+    if (train_loss) *train_loss = -ctx->slot[si].h_loss[0] / (double)ctx->n_global;
     return GBM_OK;
 }
 
@@ -774,8 +977,111 @@ void write_tree(const HostTree &T, int need, gbm_tree_out *out) {
     out->n_nodes = T.nc;
 }
 
-int tree_need(const gbm_params *P) {
-    return P->grow_policy == 0 ? 2 * P->max_leaves + 2 : (1 << (P->max_depth + 1)) - 1;
+
+// Buffers, slots and the monotone table for a call's rounds.
+int prepare_round(gbm_ctx *ctx, int nf, const gbm_params *P) {
+    TRY(ensure_round_buffers(ctx, nf, P));
+    TRY(ensure_slots(ctx));
+    return stage_mono(ctx, P);
+}
+
+// The sampler's next round: its row swap targets go to the device on cst,
+// where the round's shuffle is built and composed into the permutation, and
+// this rank's in-bag mask is made from the first n_sub entries on the engine
+// stream.  The round's feature list is left in feat_buf.
+int stage_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset) {
+    gbm_ctx::Slot &s = ctx->slot[si];
+    const int64_t N = gbm_sampler_rows(sampler);
+    const int64_t m = gbm_sampler_n_sub(sampler);
+    const bool rows_on = gbm_sampler_shuffles_rows(sampler) != 0;
+    const int64_t r = gbm_sampler_taken(sampler);
+    constexpr int R1 = gbm_ctx::kRing + 1;
+    if (row_offset + ctx->n > N) return fail(ctx, GBM_ERR_ARG, "rows %lld.. exceed the sampler's %lld rows",
+                                             (long long)row_offset, (long long)N);
+    if (rows_on) TRY(ensure_shuffle(ctx, N));
+    if (ctx->samp != sampler || ctx->samp_taken != r) {
+        if (r != 0)
+            return fail(ctx, GBM_ERR_STATE, "the sampler is at round %lld, which this engine did not draw",
+                        (long long)r);
+        ctx->samp = sampler;
+        ctx->samp_taken = 0;
+        if (rows_on) {
+            k_iota<<<grid_for(N, 256), 256, 0, ctx->cst>>>(ctx->d_perm[R1 - 1], N);
+            CKL();
+        }
+    }
+    ctx->feat_buf.resize((size_t)gbm_sampler_n_feat(sampler));
+    auto t_s = std::chrono::steady_clock::now();
+    int rc = gbm_sampler_take_targets(sampler, s.h_tg, ctx->feat_buf.data());
+    ctx->host_sample_ms += ms_since(t_s);
+    if (rc != GBM_OK) return fail(ctx, rc, "the sampler cannot feed an engine (already used for host draws?)");
+    ctx->samp_taken++;
+    if (!rows_on) {   // sample_idx is every row (E:2508-2509)
+        CK(cudaMemsetAsync(ctx->d_mask, 1, (size_t)ctx->n, ctx->st));
+        return GBM_OK;
+    }
+    int32_t *pin = ctx->d_perm[(r + R1 - 1) % R1], *pout = ctx->d_perm[r % R1];
+    CK(cudaMemcpyAsync(s.d_tg, s.h_tg, sizeof(int32_t) * (size_t)(N - 1), cudaMemcpyHostToDevice, ctx->cst));
+    CK(cudaMemsetAsync(ctx->d_head, 0xff, sizeof(int32_t) * (size_t)N, ctx->cst));
+    k_shuf_link<<<grid_for(N - 1, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_head, ctx->d_nxt);
+    CKL();
+    k_shuf_min<<<grid_for(N, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp);
+    CKL();
+    k_shuf_compose<<<grid_for(N, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_m, ctx->d_mp, pin, pout);
+    CKL();
+    CK(cudaEventRecord(s.copied, ctx->cst));
+    CK(cudaStreamWaitEvent(ctx->st, s.copied, 0));
+    CK(cudaMemsetAsync(ctx->d_mask, 0, (size_t)ctx->n, ctx->st));
+    k_mask_from_rows<<<grid_for(m, 256), 256, 0, ctx->st>>>(pout, m, row_offset, ctx->n, ctx->d_mask);
+    CKL();
+    return GBM_OK;
+}
+
+// Row-major bins [n][p] of type T -> column blocks on the device, clamped
+// to bin_count - 1.
+template <typename T>
+int upload_bins_t(gbm_ctx *ctx, const T *xbin, int64_t n, int32_t p, const int32_t *bin_counts) {
+    if (!ctx || !xbin || !bin_counts || n <= 0 || p <= 0 || n > 0x7fffffffLL) return GBM_ERR_ARG;
+    if (ctx->dev < 0) return GBM_ERR_STATE;
+    for (int j = 0; j < p; j++)
+        if (bin_counts[j] < 1 || bin_counts[j] > kBins)
+            return fail(ctx, GBM_ERR_UNSUPPORTED, "feature %d has %d bins; the device path holds 1..256 bins",
+                        j, bin_counts[j]);
+    CK(cudaSetDevice(ctx->dev));
+    ctx->n = n; ctx->p = p; ctx->nblk = (p + kBlk - 1) / kBlk;
+    ctx->slots_ready = false;
+    ctx->counts.assign(bin_counts, bin_counts + p);
+    TRY(dalloc(ctx, &ctx->d_xb, (size_t)ctx->nblk * n * kBlk));
+    TRY(dalloc(ctx, &ctx->d_counts, (size_t)p));
+    CK(cudaMemcpyAsync(ctx->d_counts, bin_counts, sizeof(int32_t) * p, cudaMemcpyHostToDevice, ctx->st));
+    // stream row chunks through a staging buffer and transpose to column blocks
+    int64_t chunk_rows = std::max<int64_t>(1, (int64_t)(64 << 20) / ((int64_t)p * (int64_t)sizeof(T)));
+    chunk_rows = std::min(chunk_rows, n);
+    T *stage = nullptr;
+    TRY(dalloc(ctx, &stage, (size_t)(chunk_rows * p)));
+    int rc = GBM_OK;
+    for (int64_t r0 = 0; r0 < n && rc == GBM_OK; r0 += chunk_rows) {
+        int64_t rows = std::min(chunk_rows, n - r0);
+        cudaError_t e = cudaMemcpyAsync(stage, xbin + r0 * p, sizeof(T) * (size_t)(rows * p), cudaMemcpyHostToDevice,
+                                        ctx->st);
+        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "bin upload: %s", cudaGetErrorString(e)); break; }
+        k_pack_bins<T><<<grid_for(rows * ctx->nblk, 256), 256, 0, ctx->st>>>(stage, rows, p, r0, n, ctx->nblk,
+                                                                           ctx->d_counts, ctx->d_xb);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "k_pack_bins: %s", cudaGetErrorString(e)); break; }
+        e = cudaStreamSynchronize(ctx->st);
+        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "bin upload sync: %s", cudaGetErrorString(e)); break; }
+    }
+    cudaFree(stage);
+    if (rc != GBM_OK) return rc;
+    TRY(choose_skip_bins(ctx));
+    TRY(alloc_round_fixed(ctx));
+    TRY(dalloc(ctx, &ctx->d_y, (size_t)n));
+    TRY(dalloc(ctx, &ctx->d_F, (size_t)n));
+    TRY(dalloc(ctx, &ctx->d_q, (size_t)n));
+    ctx->have_bins = true;
+    ctx->have_labels = false;
+    return GBM_OK;
 }
 
 }  // namespace
@@ -802,8 +1108,13 @@ int gbm_ctx_create(int32_t device, gbm_ctx **out) {
     *out = ctx;
     CK(cudaSetDevice(device));
     CK(cudaStreamCreateWithFlags(&ctx->st, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&ctx->cst, cudaStreamNonBlocking));
     CK(cudaFuncSetAttribute(k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             kAccWords * (int)sizeof(unsigned)));
+    // a function attribute is shared by every context of the process: set
+    // the largest node-table copy any context may launch with
+    CK(cudaFuncSetAttribute(k_replay_leaf, cudaFuncAttributeMaxDynamicSharedMemorySize, kReplaySmemMax));
+    CK(cudaFuncSetAttribute(k_replay_depth, cudaFuncAttributeMaxDynamicSharedMemorySize, kReplaySmemMax));
     return GBM_OK;
 }
 
@@ -814,6 +1125,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     if (ctx->dev >= 0) {
         cudaSetDevice(ctx->dev);
         if (ctx->st) cudaStreamSynchronize(ctx->st);
+        if (ctx->cst) cudaStreamSynchronize(ctx->cst);
     }
     if (ctx->comm) gbm_comm_destroy(ctx->comm);
     void *dev_ptrs[] = {ctx->d_xb, ctx->d_counts, ctx->d_skipb, ctx->d_y, ctx->d_F, ctx->d_q, ctx->d_mask,
@@ -822,13 +1134,24 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
                         ctx->d_ptask, ctx->d_tile_cnt, ctx->d_tile_off, ctx->d_nleft, ctx->d_nleft_g,
                         ctx->d_count64, ctx->d_nodes, ctx->d_lvl[0], ctx->d_lvl[1], ctx->d_ints, ctx->d_tree,
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
-                        ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_sample};
+                        ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,
+                        ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp};
+    for (int32_t *q : ctx->d_perm) if (q) cudaFree(q);
     for (void *p : dev_ptrs) if (p) cudaFree(p);
-    void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_sample};
+    void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_mono};
     for (void *p : host_ptrs) if (p) cudaFreeHost(p);
+    for (auto &s : ctx->slot) {
+        if (s.d_tg) cudaFree(s.d_tg);
+        void *hp[] = {s.h_tg, s.h_feat, s.h_fpos, s.h_tout, s.h_loss};
+        for (void *p : hp) if (p) cudaFreeHost(p);
+        if (s.copied) cudaEventDestroy(s.copied);
+        if (s.done) cudaEventDestroy(s.done);
+    }
     for (cudaEvent_t e : ctx->hist_ev) cudaEventDestroy(e);
+    for (cudaEvent_t e : ctx->flush_ev) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->mark) if (e) cudaEventDestroy(e);
     if (ctx->st) cudaStreamDestroy(ctx->st);
+    if (ctx->cst) cudaStreamDestroy(ctx->cst);
     delete ctx;
 }
 
@@ -850,45 +1173,11 @@ int gbm_ctx_init_comm(gbm_ctx *ctx, const void *uid, int32_t nranks, int32_t ran
 int gbm_nccl_unique_id(void *uid_out) { return gbm_comm_unique_id(uid_out); }
 
 int gbm_upload_bins(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p, const int32_t *bin_counts) {
-    if (!ctx || !xbin || !bin_counts || n <= 0 || p <= 0 || n > 0x7fffffffLL) return GBM_ERR_ARG;
-    if (ctx->dev < 0) return GBM_ERR_STATE;
-    for (int j = 0; j < p; j++)
-        if (bin_counts[j] < 1 || bin_counts[j] > kBins)
-            return fail(ctx, GBM_ERR_UNSUPPORTED, "feature %d has %d bins; the device path holds 1..256 bins",
-                        j, bin_counts[j]);
-    CK(cudaSetDevice(ctx->dev));
-    ctx->n = n; ctx->p = p; ctx->nblk = (p + kBlk - 1) / kBlk;
-    ctx->counts.assign(bin_counts, bin_counts + p);
-    TRY(dalloc(ctx, &ctx->d_xb, (size_t)ctx->nblk * n * kBlk));
-    TRY(dalloc(ctx, &ctx->d_counts, (size_t)p));
-    CK(cudaMemcpyAsync(ctx->d_counts, bin_counts, sizeof(int32_t) * p, cudaMemcpyHostToDevice, ctx->st));
-    // stream row chunks through a staging buffer and transpose to column blocks
-    int64_t chunk_rows = std::max<int64_t>(1, (int64_t)(64 << 20) / p);
-    chunk_rows = std::min(chunk_rows, n);
-    uint8_t *stage = nullptr;
-    TRY(dalloc(ctx, &stage, (size_t)(chunk_rows * p)));
-    int rc = GBM_OK;
-    for (int64_t r0 = 0; r0 < n && rc == GBM_OK; r0 += chunk_rows) {
-        int64_t rows = std::min(chunk_rows, n - r0);
-        cudaError_t e = cudaMemcpyAsync(stage, xbin + r0 * p, (size_t)(rows * p), cudaMemcpyHostToDevice, ctx->st);
-        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "bin upload: %s", cudaGetErrorString(e)); break; }
-        k_pack_bins<<<grid_for(rows * ctx->nblk, 256), 256, 0, ctx->st>>>(stage, rows, p, r0, n, ctx->nblk,
-                                                                           ctx->d_counts, ctx->d_xb);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "k_pack_bins: %s", cudaGetErrorString(e)); break; }
-        e = cudaStreamSynchronize(ctx->st);
-        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "bin upload sync: %s", cudaGetErrorString(e)); break; }
-    }
-    cudaFree(stage);
-    if (rc != GBM_OK) return rc;
-    TRY(choose_skip_bins(ctx));
-    TRY(alloc_round_fixed(ctx));
-    TRY(dalloc(ctx, &ctx->d_y, (size_t)n));
-    TRY(dalloc(ctx, &ctx->d_F, (size_t)n));
-    TRY(dalloc(ctx, &ctx->d_q, (size_t)n));
-    ctx->have_bins = true;
-    ctx->have_labels = false;
-    return GBM_OK;
+    return upload_bins_t(ctx, xbin, n, p, bin_counts);
+}
+
+int gbm_upload_bins_u16(gbm_ctx *ctx, const uint16_t *xbin, int64_t n, int32_t p, const int32_t *bin_counts) {
+    return upload_bins_t(ctx, xbin, n, p, bin_counts);
 }
 
 int gbm_upload_labels(gbm_ctx *ctx, const uint8_t *y, const double class_w[2], double base_score,
@@ -971,80 +1260,130 @@ int gbm_build_tree(gbm_ctx *ctx, const double *grad, const double *hess, const u
     cudaFree(dh);
     if (rc != GBM_OK) return rc;
     ctx->have_labels = false;   // the device gradients no longer follow F
+    TRY(prepare_round(ctx, nfeat, P));
+    std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
+    CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    RoundFeat rf;
+    TRY(setup_features(ctx, 0, feat_idx, nfeat, rf));
+    TRY(enqueue_grow(ctx, rf, P));
+    if (device_replay(ctx, P)) {
+        TRY(enqueue_replay(ctx, P));
+        gbm_ctx::Slot &s = ctx->slot[0];
+        CK(cudaMemcpyAsync(s.h_tout, ctx->d_tout, sizeof(TreeOut), cudaMemcpyDeviceToHost, ctx->st));
+        s.h_loss[0] = 0.0;
+        CK(cudaEventRecord(s.done, ctx->st));
+        TRY(wait_slot(ctx, 0));
+        if (ctx->profiling) TRY(collect_hist_events(ctx));
+        return harvest(ctx, 0, nfeat, P, out, nullptr);
+    }
     HostTree T;
-    TRY(grow_tree(ctx, inbag_mask, feat_idx, nfeat, P, T));
+    TRY(replay_on_host(ctx, rf, P, T));
     write_tree(T, tree_need(P), out);
     return GBM_OK;
 }
 
-static int round_body(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
-                      const gbm_params *P, gbm_tree_out *out, double *train_loss) {
-    if (!ctx || !feat_idx || !P || !out) return GBM_ERR_ARG;
-    if (!ctx->have_labels) return fail(ctx, GBM_ERR_STATE, "upload bins and labels before gbm_round");
-    TRY(check_tree_args(ctx, nfeat, P, out));
+// One round from the staged in-bag mask (on the device) and feature list:
+// growth, the tree (device replay, or host replay for capped levels), the F
+// update, the loss, and the wait for all of it.
+static int round_body(gbm_ctx *ctx, const int32_t *feat_idx, int32_t nfeat, const gbm_params *P,
+                      gbm_tree_out *out, double *train_loss) {
+    gbm_ctx::Slot &s = ctx->slot[0];
+    RoundFeat rf;
+    TRY(setup_features(ctx, 0, feat_idx, nfeat, rf));
+    TRY(enqueue_grow(ctx, rf, P));
+    const bool dev = device_replay(ctx, P);
     HostTree T;
-    TRY(grow_tree(ctx, inbag_mask, feat_idx, nfeat, P, T));
-    int need = tree_need(P);
-
-    // F update + loss + next gradients
-    TreeDev td;
-    std::memset(&td, 0, sizeof td);
-    if (T.nc > 256) return fail(ctx, GBM_ERR_UNSUPPORTED, "tree with %d nodes exceeds 256", T.nc);
-    td.n = T.nc;
-    for (int k = 0; k < T.nc; k++) {
-        td.feat[k] = T.tf[k];
-        td.thr[k] = (int)std::min<int64_t>(T.tt[k], 255);
-        td.left[k] = T.tl[k];
-        td.right[k] = T.tr[k];
-        td.val[k] = T.tv[k];
+    if (dev) {
+        TRY(enqueue_replay(ctx, P));
+        CK(cudaMemcpyAsync(s.h_tout, ctx->d_tout, sizeof(TreeOut), cudaMemcpyDeviceToHost, ctx->st));
+    } else {
+        TRY(replay_on_host(ctx, rf, P, T));
+        if (T.nc > 256) return fail(ctx, GBM_ERR_UNSUPPORTED, "tree with %d nodes exceeds 256", T.nc);
+        TreeDev td;
+        std::memset(&td, 0, sizeof td);
+        td.n = T.nc;
+        for (int k = 0; k < T.nc; k++) {
+            td.feat[k] = T.tf[k];
+            td.thr[k] = (int)std::min<int64_t>(T.tt[k], 255);
+            td.left[k] = T.tl[k];
+            td.right[k] = T.tr[k];
+            td.val[k] = T.tv[k];
+        }
+        CK(cudaMemcpyAsync(ctx->d_tree, &td, sizeof td, cudaMemcpyHostToDevice, ctx->st));
     }
-    CK(cudaMemcpyAsync(ctx->d_tree, &td, sizeof td, cudaMemcpyHostToDevice, ctx->st));
-    double scale = std::ldexp(1.0, ctx->S);
-    k_update<<<ctx->upd_blocks, kUpdThreads, 0, ctx->st>>>(
-        ctx->d_tree, ctx->d_xb, ctx->n, ctx->d_y, ctx->w[0], ctx->w[1], P->learning_rate, scale, ctx->d_F,
-        ctx->d_q, out->leaf_of_row ? ctx->d_leaf : nullptr, ctx->d_loss_part);
-    CKL();
-    k_sum_partials<<<1, 256, 0, ctx->st>>>(ctx->d_loss_part, ctx->upd_blocks, ctx->d_loss);
-    CKL();
-    if (ctx->comm) TRY(gbm_comm_allreduce_f64(ctx->comm, ctx->d_loss, 1, ctx->st, ctx->timeout_ms, ctx->err));
-    CK(cudaMemcpyAsync(ctx->h_loss, ctx->d_loss, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
+    TRY(enqueue_update(ctx, P, out->leaf_of_row != nullptr, s.h_loss));
     if (out->leaf_of_row)
         CK(cudaMemcpyAsync(out->leaf_of_row, ctx->d_leaf, sizeof(int32_t) * ctx->n, cudaMemcpyDeviceToHost, ctx->st));
-    TRY(sync_stream(ctx));
-    if (train_loss) *train_loss = -ctx->h_loss[0] / (double)ctx->n_global;
-    write_tree(T, need, out);
+    CK(cudaEventRecord(s.done, ctx->st));
+    TRY(wait_slot(ctx, 0));
+    if (ctx->profiling) TRY(collect_hist_events(ctx));
+    if (dev) return harvest(ctx, 0, nfeat, P, out, train_loss);
+    if (train_loss) *train_loss = -s.h_loss[0] / (double)ctx->n_global;
+    write_tree(T, tree_need(P), out);
     return GBM_OK;
 }
 
 int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
               const gbm_params *P, gbm_tree_out *out, double *train_loss) {
-    if (!inbag_mask) return GBM_ERR_ARG;
-    return round_body(ctx, inbag_mask, feat_idx, nfeat, P, out, train_loss);
+    if (!ctx || !inbag_mask || !feat_idx || !P || !out) return GBM_ERR_ARG;
+    if (!ctx->have_labels) return fail(ctx, GBM_ERR_STATE, "upload bins and labels before gbm_round");
+    TRY(check_tree_args(ctx, nfeat, P, out));
+    CK(cudaSetDevice(ctx->dev));
+    TRY(prepare_round(ctx, nfeat, P));
+    std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
+    CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    return round_body(ctx, feat_idx, nfeat, P, out, train_loss);
 }
 
 int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *P,
                       gbm_tree_out *out, double *train_loss) {
     if (!ctx || !sampler || !P || !out || row_offset < 0) return GBM_ERR_ARG;
     if (!ctx->have_labels) return fail(ctx, GBM_ERR_STATE, "upload bins and labels before gbm_round_sampled");
-    CK(cudaSetDevice(ctx->dev));
-    int64_t m = gbm_sampler_n_sub(sampler);
     int32_t nf = gbm_sampler_n_feat(sampler);
-    if (m > ctx->sample_cap) {
-        TRY(halloc(ctx, &ctx->h_sample, (size_t)m));
-        TRY(dalloc(ctx, &ctx->d_sample, (size_t)m));
-        ctx->sample_cap = m;
+    TRY(check_tree_args(ctx, nf, P, out));
+    CK(cudaSetDevice(ctx->dev));
+    TRY(prepare_round(ctx, nf, P));
+    TRY(stage_sample(ctx, 0, sampler, row_offset));
+    return round_body(ctx, ctx->feat_buf.data(), nf, P, out, train_loss);
+}
+
+int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *P, int32_t n_rounds,
+                   gbm_tree_out *outs, double *train_loss) {
+    if (!ctx || !sampler || !P || !outs || !train_loss || row_offset < 0 || n_rounds < 0) return GBM_ERR_ARG;
+    if (!ctx->have_labels) return fail(ctx, GBM_ERR_STATE, "upload bins and labels before gbm_fit_rounds");
+    int32_t nf = gbm_sampler_n_feat(sampler);
+    bool leaf = false;
+    for (int r = 0; r < n_rounds; r++) {
+        TRY(check_tree_args(ctx, nf, P, &outs[r]));
+        leaf |= outs[r].leaf_of_row != nullptr;
     }
-    ctx->feat_buf.resize((size_t)nf);
-    // the previous round's copy out of h_sample finished at that round's sync
-    auto t_s = std::chrono::steady_clock::now();
-    int rc = gbm_sampler_next_rows(sampler, ctx->h_sample, ctx->feat_buf.data());
-    ctx->host_sample_ms += ms_since(t_s);
-    if (rc != GBM_OK) return fail(ctx, rc, "gbm_sampler_next_rows failed");
-    CK(cudaMemcpyAsync(ctx->d_sample, ctx->h_sample, sizeof(int32_t) * m, cudaMemcpyHostToDevice, ctx->st));
-    CK(cudaMemsetAsync(ctx->d_mask, 0, (size_t)ctx->n, ctx->st));
-    k_mask_from_rows<<<grid_for(m, 256), 256, 0, ctx->st>>>(ctx->d_sample, m, row_offset, ctx->n, ctx->d_mask);
-    CKL();
-    return round_body(ctx, nullptr, ctx->feat_buf.data(), nf, P, out, train_loss);
+    CK(cudaSetDevice(ctx->dev));
+    TRY(prepare_round(ctx, nf, P));
+    if (leaf || !device_replay(ctx, P)) {
+        for (int r = 0; r < n_rounds; r++)
+            TRY(gbm_round_sampled(ctx, sampler, row_offset, P, &outs[r], &train_loss[r]));
+        return GBM_OK;
+    }
+    const int R = gbm_ctx::kRing;
+    for (int r = 0; r < n_rounds + R; r++) {
+        const int si = r % R;
+        if (r >= R) {
+            TRY(wait_slot(ctx, si));
+            TRY(harvest(ctx, si, nf, P, &outs[r - R], &train_loss[r - R]));
+        }
+        if (r >= n_rounds) continue;
+        gbm_ctx::Slot &s = ctx->slot[si];
+        TRY(stage_sample(ctx, si, sampler, row_offset));
+        RoundFeat rf;
+        TRY(setup_features(ctx, si, ctx->feat_buf.data(), nf, rf));
+        TRY(enqueue_grow(ctx, rf, P));
+        TRY(enqueue_replay(ctx, P));
+        TRY(enqueue_update(ctx, P, false, s.h_loss));
+        CK(cudaMemcpyAsync(s.h_tout, ctx->d_tout, sizeof(TreeOut), cudaMemcpyDeviceToHost, ctx->st));
+        CK(cudaEventRecord(s.done, ctx->st));
+    }
+    if (ctx->profiling) TRY(collect_hist_events(ctx));
+    return GBM_OK;
 }
 
 // ---- predict ------------------------------------------------------------------
@@ -1157,6 +1496,7 @@ int gbm_get_stats(gbm_ctx *ctx, gbm_stats *out) {
     out->host_sample_ms = ctx->host_sample_ms;
     out->host_sync_ms = ctx->host_sync_ms;
     out->host_replay_ms = ctx->host_replay_ms;
+    out->flush_ms = ctx->flush_ms;
     return GBM_OK;
 }
 
@@ -1164,7 +1504,21 @@ int gbm_reset_stats(gbm_ctx *ctx) {
     if (!ctx) return GBM_ERR_ARG;
     ctx->launches = ctx->hist_launches = ctx->hist_rows = ctx->waves = 0;
     ctx->hist_ms = ctx->alg_bytes = 0.0;
-    ctx->host_sample_ms = ctx->host_sync_ms = ctx->host_replay_ms = 0.0;
+    ctx->host_sample_ms = ctx->host_sync_ms = ctx->host_replay_ms = ctx->flush_ms = 0.0;
+    return GBM_OK;
+}
+
+int gbm_set_l2_flush(gbm_ctx *ctx, int64_t bytes) {
+    if (!ctx || bytes < 0) return GBM_ERR_ARG;
+    if (ctx->dev < 0) return GBM_ERR_STATE;
+    CK(cudaSetDevice(ctx->dev));
+    TRY(sync_stream(ctx));
+    if (ctx->d_flush) { cudaFree(ctx->d_flush); ctx->d_flush = nullptr; }
+    ctx->flush_bytes = 0;
+    if (bytes > 0) {
+        TRY(dalloc(ctx, &ctx->d_flush, (size_t)bytes));
+        ctx->flush_bytes = (size_t)bytes;
+    }
     return GBM_OK;
 }
 

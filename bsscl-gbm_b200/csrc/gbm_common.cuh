@@ -75,6 +75,27 @@ struct TreeDev {            // a pruned tree in the reference's layout
     double val[256];
 };
 
+// One finished tree in the reference's tuple layout, written by the device
+// replay and copied to the host.
+struct TreeOut {
+    int nc;
+    int status;             // 0 ok, 1 the replay needed a node that was not expanded
+    long long root_rows;    // this rank's in-bag rows
+    long long alg_rows;     // root rows + the smaller child's rows of every split (this rank)
+    int tf[256];
+    int tl[256];
+    int tr[256];
+    long long tt[256];
+    double tv[256];
+    double sg[256];
+};
+
+struct RParams {            // growth parameters the replay needs
+    double lam, gamma, mcw;
+    long long msl;
+    int max_depth, max_leaves, policy, has_mono;
+};
+
 struct PNode {              // predict: 8 bytes per node
     int16_t feat;           // -1 = leaf
     uint8_t thr;

@@ -14,7 +14,8 @@ namespace gbm {
 
 // Row-major uint8 [rows][p] -> column blocks [nblk][n][16], ids clamped to
 // bin_count-1 (E:593-594 clamps the same way; E:604 never splits above).
-__global__ void k_pack_bins(const uint8_t *__restrict__ src, int64_t rows, int p, int64_t row0,
+template <typename T>
+__global__ void k_pack_bins(const T *__restrict__ src, int64_t rows, int p, int64_t row0,
                             int64_t n, int nblk, const int32_t *__restrict__ counts,
                             uint8_t *__restrict__ xb) {
     int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -99,6 +100,7 @@ k_update(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64
     __shared__ double s_val[256];
     __shared__ double s_red[kUpdThreads / 32];
     int nn = tree->n;
+    if (nn <= 0) return;   // the replay failed; the host reports it and F is left as it was
     for (int k = threadIdx.x; k < nn; k += blockDim.x) {
         s_feat[k] = tree->feat[k];
         s_thr[k] = tree->thr[k];
@@ -208,6 +210,66 @@ __global__ void k_mask_from_rows(const int32_t *__restrict__ rows, int64_t m, in
     if (k >= m) return;
     int64_t r = (int64_t)rows[k] - row0;
     if (r >= 0 && r < n) mask[r] = 1;
+}
+
+// ---------------------------------------------------------------------------
+// The round's row shuffle from its swap targets (the sampler's NumPy legacy
+// Fisher-Yates, E:2502-2517), in parallel.  Steps run i = n-1 .. 1 and step
+// i swaps positions i and j_i <= i; position i is final after step i.  With
+//   m(q)  = min{ i > q : j_i = q }          (the last write into q before step q)
+//   mp(i) = min{ i' > i : j_i' = j_i }     (the last write into j_i before step i)
+//   P(i)  = value at position i just before step i = P(m(i)), or i if m(i) = none
+// the round's permutation of arange(n) is S[i] = P(mp(i)) or j_i, and
+// S[0] = P(m(0)) or 0.  m only increases along a chain, so every chase ends.
+// The targets arrive forward: t[k] = j_(n-1-k).
+// ---------------------------------------------------------------------------
+
+// Bucket the steps by target: a singly linked list per position.
+__global__ void k_shuf_link(const int32_t *__restrict__ t, int64_t n, int32_t *__restrict__ head,
+                            int32_t *__restrict__ nxt) {
+    int64_t i = 1 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int q = t[n - 1 - i];
+    nxt[i] = atomicExch(&head[q], (int32_t)i);
+}
+
+__device__ __forceinline__ int32_t min_above(const int32_t *__restrict__ head, const int32_t *__restrict__ nxt,
+                                             int q, int64_t floor_) {
+    int32_t best = -1;
+    for (int32_t e = head[q]; e >= 0; e = nxt[e])
+        if (e > floor_ && (best < 0 || e < best)) best = e;
+    return best;
+}
+
+__global__ void k_shuf_min(const int32_t *__restrict__ t, int64_t n, const int32_t *__restrict__ head,
+                           const int32_t *__restrict__ nxt, int32_t *__restrict__ m, int32_t *__restrict__ mp) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    m[i] = min_above(head, nxt, (int)i, i);
+    if (i >= 1) mp[i] = min_above(head, nxt, t[n - 1 - i], i);
+}
+
+// perm_out = perm_in[S] (the shuffle applied to the cumulative permutation).
+__global__ void k_shuf_compose(const int32_t *__restrict__ t, int64_t n, const int32_t *__restrict__ m,
+                               const int32_t *__restrict__ mp, const int32_t *__restrict__ perm_in,
+                               int32_t *__restrict__ perm_out) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int32_t src = i == 0 ? m[0] : mp[i];
+    int32_t s;
+    if (src < 0) {
+        s = i == 0 ? 0 : t[n - 1 - i];
+    } else {
+        int32_t r = src;
+        for (int32_t nx = m[r]; nx >= 0; nx = m[nx]) r = nx;
+        s = r;
+    }
+    perm_out[i] = perm_in[s];
+}
+
+__global__ void k_iota(int32_t *__restrict__ a, int64_t n) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) a[i] = (int32_t)i;
 }
 
 __global__ void k_count64(const int32_t *__restrict__ in, long long *__restrict__ out) {
@@ -851,6 +913,246 @@ __global__ void k_next_level(const DNode *__restrict__ nodes, const int *__restr
     }
     __syncthreads();
     if (threadIdx.x == 0) *out_count = s_cnt;
+}
+
+// ===========================================================================
+// best-first replay on the device (E:642-823), post-prune, monotone clip
+// ===========================================================================
+
+// The fields of a grown node the replay reads, cached in shared memory.
+struct RNode {
+    double G, H, gain;
+    long long n, local;     // rows over all ranks / on this rank
+    int feat, bin, kid0, kid1, expanded, pad;
+};
+
+__device__ void load_rnodes(const DNode *__restrict__ nodes, int cnt, RNode *sn) {
+    for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+        const DNode &d = nodes[i];
+        RNode r;
+        r.G = d.G; r.H = d.H; r.gain = d.gain; r.n = d.n; r.local = d.end - d.begin;
+        r.feat = d.feat; r.bin = d.bin; r.kid0 = d.kid0; r.kid1 = d.kid1; r.expanded = d.expanded; r.pad = 0;
+        sn[i] = r;
+    }
+    __syncwarp();
+}
+
+// The finished tree -> the F-update layout and the host copy.  Post-prune
+// (E:827-841) and the monotone clip (E:2461-2499) run on lane 0 first.
+__device__ void finish_tree(int nc, int *tf, int *tl, int *tr, long long *tt, double *tv, double *sg,
+                            const RParams &P, const int *__restrict__ mono, TreeOut *__restrict__ out,
+                            TreeDev *__restrict__ td, int status, long long root_rows, long long alg_rows) {
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) {
+        for (int k = nc - 1; k >= 0; k--) {
+            if (tf[k] != -1) {
+                int l = tl[k], r = tr[k];
+                if (tf[l] == -1 && tf[r] == -1 && sg[k] < P.gamma) { tf[k] = -1; tl[k] = -1; tr[k] = -1; }
+            }
+        }
+        if (P.has_mono) {
+            for (int k = 0; k < nc; k++) {
+                int f = tf[k];
+                if (f < 0) continue;
+                int c = mono[f];
+                if (c == 0) continue;
+                int l = tl[k], r = tr[k];
+                if (l < 0 || r < 0) continue;
+                double lv = tv[l], rv = tv[r];
+                if ((c == 1 && lv > rv) || (c == -1 && lv < rv)) {
+                    double m = __ddiv_rn(__dadd_rn(lv, rv), 2.0);
+                    tv[l] = m;
+                    tv[r] = m;
+                }
+            }
+        }
+        out->nc = nc;
+        out->status = status;
+        out->root_rows = root_rows;
+        out->alg_rows = alg_rows;
+        td->n = status ? 0 : nc;
+    }
+    __syncwarp();
+    for (int k = lane; k < 256; k += 32) {
+        bool in = k < nc;
+        out->tf[k] = in ? tf[k] : -1;
+        out->tl[k] = in ? tl[k] : -1;
+        out->tr[k] = in ? tr[k] : -1;
+        out->tt[k] = in ? tt[k] : 0;
+        out->tv[k] = in ? tv[k] : 0.0;
+        out->sg[k] = in ? sg[k] : 0.0;
+        if (in) {
+            td->feat[k] = tf[k];
+            td->thr[k] = (int)(tt[k] > 255 ? 255 : tt[k]);
+            td->left[k] = tl[k];
+            td->right[k] = tr[k];
+            td->val[k] = tv[k];
+        }
+    }
+}
+
+constexpr int kReplayMaxC = 130;    // candidate slots: max_leaves + 2 <= 129
+
+// One warp replays the reference's best-first loop over the grown node
+// table: the candidate slots, the strict '>' scan where the lowest slot wins
+// among equal gains, min_samples_leaf on the partition, the node numbering
+// and the reuse of the lowest free slots (E:546-823).  Every control value is
+// computed identically by all lanes; lane 0 writes.  status 1: the loop
+// reached a node that was not expanded (the caller then replays on the host).
+__global__ void __launch_bounds__(32)
+k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_count, RParams P,
+              const int *__restrict__ mono, TreeOut *__restrict__ out, TreeDev *__restrict__ td) {
+    extern __shared__ RNode sn[];
+    __shared__ int c_node[kReplayMaxC], c_nid[kReplayMaxC], c_depth[kReplayMaxC], c_feat[kReplayMaxC],
+        c_bin[kReplayMaxC], c_act[kReplayMaxC];
+    __shared__ double c_gain[kReplayMaxC], c_val[kReplayMaxC];
+    __shared__ int tf[256], tl[256], tr[256];
+    __shared__ long long tt[256];
+    __shared__ double tv[256], sg[256];
+    const int lane = threadIdx.x;
+    const unsigned full = 0xffffffffu;
+    const int MAXC = P.max_leaves + 2;
+    load_rnodes(nodes, *node_count, sn);
+    for (int k = lane; k < 256; k += 32) { tf[k] = -1; tl[k] = -1; tr[k] = -1; tt[k] = 0; tv[k] = 0.0; sg[k] = 0.0; }
+    for (int s = lane; s < kReplayMaxC; s += 32) { c_act[s] = 0; c_feat[s] = -1; c_gain[s] = -1.0; }
+    __syncwarp();
+    const RNode r0 = sn[0];
+    const double root_val = __ddiv_rn(-r0.G, __dadd_rn(r0.H, P.lam));
+    long long alg = r0.local;
+    int nc = 1, status = 0;
+    if (r0.n < P.msl || r0.H < P.mcw || r0.feat < 0) {          // E:575-579, E:634-638
+        if (lane == 0) tv[0] = root_val;
+        __syncwarp();
+        finish_tree(nc, tf, tl, tr, tt, tv, sg, P, mono, out, td, 0, r0.local, alg);
+        return;
+    }
+    if (lane == 0) {
+        c_node[0] = 0; c_nid[0] = 0; c_depth[0] = 0; c_feat[0] = r0.feat; c_bin[0] = r0.bin;
+        c_gain[0] = r0.gain; c_val[0] = root_val; c_act[0] = 1;
+    }
+    __syncwarp();
+    int n_splits = 0;
+    while (n_splits < P.max_leaves - 1) {
+        int bs = -1;
+        double bg = 0.0;
+        for (int s = lane; s < MAXC; s += 32) {
+            if (c_act[s] && c_feat[s] >= 0 && c_gain[s] > P.gamma && (bs < 0 || c_gain[s] > bg)) {
+                bg = c_gain[s];
+                bs = s;
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            double og = __shfl_xor_sync(full, bg, o);
+            int os = __shfl_xor_sync(full, bs, o);
+            if (os >= 0 && (bs < 0 || og > bg || (og == bg && os < bs))) { bg = og; bs = os; }
+        }
+        if (bs < 0) break;
+        const int ci = bs;
+        const int cur = c_node[ci];
+        const RNode pn = sn[c_nid[ci]];
+        if (!pn.expanded) { status = 1; break; }
+        const long long gnl = sn[pn.kid0].n, gnr = sn[pn.kid1].n;
+        if (gnl < P.msl || gnr < P.msl) {                        // E:678-683
+            if (lane == 0) { tf[cur] = -1; tv[cur] = c_val[ci]; c_act[ci] = 0; }
+            __syncwarp();
+            continue;
+        }
+        // the two lowest free slots other than ci (E:712-720)
+        int ss = -1, sl = -1;
+        for (int base = 0; base < MAXC && sl < 0; base += 32) {
+            int s = base + lane;
+            unsigned m = __ballot_sync(full, s < MAXC && s != ci && !c_act[s]);
+            while (m && sl < 0) {
+                int b = __ffs(m) - 1;
+                m &= m - 1;
+                if (ss < 0) ss = base + b; else sl = base + b;
+            }
+        }
+        if (ss < 0 || sl < 0) { status = 2; break; }   // cannot happen: >= 3 slots are free
+        const int lid = nc, rid = nc + 1;
+        nc += 2;
+        n_splits++;
+        const bool left_small = gnl <= gnr;
+        alg += left_small ? sn[pn.kid0].local : sn[pn.kid1].local;
+        const double cval = c_val[ci], cgain = c_gain[ci];
+        const int cfeat = c_feat[ci], cbin = c_bin[ci], cdepth = c_depth[ci];
+        __syncwarp();
+        if (lane < 2) {
+            // lane 0 fills the first free slot with the smaller child, lane 1
+            // the second with the larger one
+            const int pass = lane;
+            const int side = (pass == 0) == left_small ? 0 : 1;
+            const RNode kd = sn[side == 0 ? pn.kid0 : pn.kid1];
+            const int slot = pass == 0 ? ss : sl;
+            c_node[slot] = side == 0 ? lid : rid;
+            c_nid[slot] = side == 0 ? pn.kid0 : pn.kid1;
+            c_depth[slot] = cdepth + 1;
+            c_val[slot] = __ddiv_rn(-kd.G, __dadd_rn(kd.H, P.lam));
+            c_feat[slot] = kd.feat;
+            c_bin[slot] = kd.feat >= 0 ? kd.bin : 0;
+            c_gain[slot] = kd.feat >= 0 ? kd.gain : -1.0;
+            c_act[slot] = 1;
+            if (lane == 0) {
+                tf[cur] = cfeat; tt[cur] = cbin; tl[cur] = lid; tr[cur] = rid; tv[cur] = cval; sg[cur] = cgain;
+            }
+        }
+        if (lane == 0) c_act[ci] = 0;
+        __syncwarp();
+    }
+    if (!status && lane == 0) {
+        for (int s = 0; s < MAXC; s++)
+            if (c_act[s]) { tf[c_node[s]] = -1; tv[c_node[s]] = c_val[s]; }
+    }
+    __syncwarp();
+    finish_tree(nc, tf, tl, tr, tt, tv, sg, P, mono, out, td, status, r0.local, alg);
+}
+
+// Depth-wise growth's node numbering (E:233-508): a DFS stack where the
+// larger child is pushed first, so the smaller one is numbered first.
+__global__ void __launch_bounds__(32)
+k_replay_depth(const DNode *__restrict__ nodes, const int *__restrict__ node_count, RParams P,
+               const int *__restrict__ mono, TreeOut *__restrict__ out, TreeDev *__restrict__ td) {
+    extern __shared__ RNode sn[];
+    __shared__ int tf[256], tl[256], tr[256];
+    __shared__ long long tt[256];
+    __shared__ double tv[256], sg[256];
+    __shared__ int s_nc, s_status;
+    __shared__ long long s_alg;
+    const int lane = threadIdx.x;
+    load_rnodes(nodes, *node_count, sn);
+    for (int k = lane; k < 256; k += 32) { tf[k] = -1; tl[k] = -1; tr[k] = -1; tt[k] = 0; tv[k] = 0.0; sg[k] = 0.0; }
+    __syncwarp();
+    if (lane == 0) {
+        int st_nid[64], st_tid[64], sp = 0, nc = 0, status = 0;
+        long long alg = sn[0].local;
+        st_nid[sp] = 0; st_tid[sp] = nc++; sp++;
+        while (sp > 0) {
+            sp--;
+            const RNode x = sn[st_nid[sp]];
+            const int tid = st_tid[sp];
+            const double val = __ddiv_rn(-x.G, __dadd_rn(x.H, P.lam));
+            if (x.feat >= 0 && !x.expanded) status = 1;
+            bool split = x.feat >= 0 && x.expanded && sn[x.kid0].n >= P.msl && sn[x.kid1].n >= P.msl &&
+                         nc + 2 <= 256 && sp + 2 <= 64;
+            if (!split) { tf[tid] = -1; tv[tid] = val; continue; }
+            const int lid = nc++, rid = nc++;
+            const long long gl = sn[x.kid0].n, gr = sn[x.kid1].n;
+            alg += gl <= gr ? sn[x.kid0].local : sn[x.kid1].local;
+            tf[tid] = x.feat; tt[tid] = x.bin; tl[tid] = lid; tr[tid] = rid; tv[tid] = val; sg[tid] = x.gain;
+            if (gl <= gr) {
+                st_nid[sp] = x.kid1; st_tid[sp] = rid; sp++;
+                st_nid[sp] = x.kid0; st_tid[sp] = lid; sp++;
+            } else {
+                st_nid[sp] = x.kid0; st_tid[sp] = lid; sp++;
+                st_nid[sp] = x.kid1; st_tid[sp] = rid; sp++;
+            }
+        }
+        s_nc = nc;
+        s_status = status;
+        s_alg = alg;
+    }
+    __syncwarp();
+    finish_tree(s_nc, tf, tl, tr, tt, tv, sg, P, mono, out, td, s_status, sn[0].local, s_alg);
 }
 
 // ===========================================================================

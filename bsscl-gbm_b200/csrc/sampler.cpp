@@ -10,24 +10,27 @@
 //   * NumPy's legacy bounded integer draw for the shuffle: the smallest
 //     all-ones mask covering `max`, 32-bit words, rejection of values > max;
 //   * Fisher-Yates from the last element down to index 1.
-// The permutation is kept as int32 (n < 2^31) so the 1M-row state fits in
-// cache.  The stream does not depend on the model, so two host threads run
-// rounds ahead: one draws the next round's swap targets (the whole MT19937
-// cost), the other applies the previous round's swaps.
+// The stream does not depend on the model, so a host thread draws rounds
+// ahead.  For an engine only the swap targets leave this file: the engine
+// turns them into the round's permutation on the GPU (the sequential
+// MT19937 draw is all that stays on the host).  gbm_sampler_next applies
+// the swaps to a host copy of the permutation (int32, n < 2^31).
+#include <immintrin.h>
+
 #include <algorithm>
 #include <atomic>
 #include <condition_variable>
 #include <cstdint>
 #include <cstring>
-#include <deque>
 #include <mutex>
 #include <new>
 #include <thread>
 #include <vector>
 
 #include "../../include/gbm_b200.h"
+#include "sampler_internal.h"
 
-namespace {
+namespace gbmsamp {
 
 constexpr int kN = 624, kM = 397;
 
@@ -65,126 +68,198 @@ struct MT19937 {
     }
 };
 
-// Swap targets of NumPy's legacy shuffle for i = n-1 .. 1: each target is a
-// uniform integer in [0, i] drawn by masked rejection (the smallest
-// all-ones mask covering i, one 32-bit word per attempt, rejected if > i).
-// The mask is constant for i in [2^(k-1), 2^k - 1], and the attempt loop is
-// written without branches: every word is stored at tgt[i] and i only
-// advances when the word was accepted -- the same words in the same order.
-void draw_targets(MT19937 &r, int64_t n, int32_t *tgt) {
-    int64_t i = n - 1;
-    while (i >= 1) {
-        if (r.idx >= kN) r.refill();
-        uint32_t mask = (uint32_t)i;
-        mask |= mask >> 1; mask |= mask >> 2; mask |= mask >> 4;
-        mask |= mask >> 8; mask |= mask >> 16;
-        const int64_t stop = ((int64_t)mask + 1) >> 1;   // lowest i with this mask
-        const uint32_t *w = r.out + r.idx;
-        const int avail = kN - r.idx;
-        int k = 0;
-        while (k < avail && i >= stop) {
-            uint32_t v = w[k++] & mask;
-            tgt[i] = (int32_t)v;
-            i -= (int64_t)(v <= (uint64_t)i);
+// The compress permutations of AVX2 left-packing: entry m lists the lanes
+// whose bit is set in m, in order.
+struct CompressLut {
+    alignas(32) int32_t idx[256][8];
+    CompressLut() {
+        for (int m = 0; m < 256; m++) {
+            int k = 0;
+            for (int l = 0; l < 8; l++)
+                if (m & (1 << l)) idx[m][k++] = l;
+            for (; k < 8; k++) idx[m][k] = 0;
         }
-        r.idx += k;
+    }
+};
+const CompressLut kLut;
+
+inline uint32_t smear(uint64_t i) {
+    uint32_t m = (uint32_t)i;
+    m |= m >> 1; m |= m >> 2; m |= m >> 4; m |= m >> 8; m |= m >> 16;
+    return m;
+}
+
+// Swap targets of NumPy's legacy shuffle for i = n-1 .. 1, stored forward:
+// t[k] is the target of i = n-1-k (k = 0 .. n-2; t holds n + 8 entries).
+// Each target is a uniform integer in [0, i] drawn by masked rejection (the
+// smallest all-ones mask covering i, one 32-bit word per attempt, rejected
+// if > i).  The words are consumed in the scalar rule's order, but a block
+// of B words is decided at once when no word of it lies in (i-B+1, i]: each
+// word is then > i (rejected whatever the others do) or <= i-B+1 (accepted),
+// and i-B+1 still has the block's mask.  Accepted words are left-packed into
+// t (AVX2, 8 lanes).  Blocks of 64, then 8, then single words.
+inline void pack8(__m256i v, int nacc, int32_t *t, int64_t &pos) {
+    const int acc = ~nacc & 0xff;
+    const __m256i pm = _mm256_load_si256((const __m256i *)kLut.idx[acc]);
+    _mm256_storeu_si256((__m256i *)(t + pos), _mm256_permutevar8x32_epi32(v, pm));
+    pos += __builtin_popcount((unsigned)acc);
+}
+
+void draw_targets(MT19937 &r, int64_t n, int32_t *t) {
+    const int64_t top = n - 1;
+    int64_t pos = 0;                    // i = top - pos
+    while (top - pos >= 1) {
+        if (r.idx >= kN) r.refill();
+        int64_t i = top - pos;
+        const uint32_t mask = smear((uint64_t)i);
+        const int64_t stop = ((int64_t)mask + 1) >> 1;   // lowest i with this mask
+        const uint32_t *w = r.out;
+        int k = r.idx;
+        const __m256i vm = _mm256_set1_epi32((int)mask);
+        // 64-word blocks: eight independent compares, one store chain
+        while (k + 64 <= kN && i - 63 >= stop) {
+            const __m256i hi = _mm256_set1_epi32((int)i), lo = _mm256_set1_epi32((int)(i - 63));
+            __m256i v[8];
+            int nacc[8], amb = 0;
+            for (int b = 0; b < 8; b++) {
+                v[b] = _mm256_and_si256(_mm256_loadu_si256((const __m256i *)(w + k + 8 * b)), vm);
+                const int rej = _mm256_movemask_ps(_mm256_castsi256_ps(_mm256_cmpgt_epi32(v[b], hi)));
+                nacc[b] = _mm256_movemask_ps(_mm256_castsi256_ps(_mm256_cmpgt_epi32(v[b], lo)));
+                amb |= nacc[b] & ~rej;
+            }
+            if (amb) break;
+            for (int b = 0; b < 8; b++) pack8(v[b], nacc[b], t, pos);
+            k += 64;
+            i = top - pos;
+        }
+        // 8-word blocks (at most 8 of them before trying 64 again)
+        for (int blk = 0; blk < 8 && k + 8 <= kN && i - 7 >= stop; blk++) {
+            const __m256i v = _mm256_and_si256(_mm256_loadu_si256((const __m256i *)(w + k)), vm);
+            const int rej = _mm256_movemask_ps(_mm256_castsi256_ps(_mm256_cmpgt_epi32(v, _mm256_set1_epi32((int)i))));
+            const int nacc =
+                _mm256_movemask_ps(_mm256_castsi256_ps(_mm256_cmpgt_epi32(v, _mm256_set1_epi32((int)(i - 7)))));
+            if (nacc & ~rej) break;
+            pack8(v, nacc, t, pos);
+            k += 8;
+            i = top - pos;
+        }
+        // single words, up to 8
+        const int end = std::min(kN, k + 8);
+        while (k < end && i >= stop) {
+            const uint32_t v = w[k++] & mask;
+            t[pos] = (int32_t)v;
+            const int64_t a = (int64_t)(v <= (uint64_t)i);
+            pos += a;
+            i -= a;
+        }
+        r.idx = k;
     }
 }
 
-// Fisher-Yates from the last element down to index 1, targets prefetched.
+// Fisher-Yates from the last element down to index 1 (forward targets),
+// targets prefetched.
 template <typename T>
-void apply_swaps(T *a, int64_t n, const int32_t *tgt) {
+void apply_swaps(T *a, int64_t n, const int32_t *t) {
     constexpr int64_t kAhead = 24;
-    for (int64_t i = n - 1; i >= 1; i--) {
-        if (i > kAhead) __builtin_prefetch(&a[tgt[i - kAhead]], 1, 0);
-        int64_t j = tgt[i];
-        T t = a[i]; a[i] = a[j]; a[j] = t;
+    for (int64_t k = 0; k + 1 < n; k++) {
+        if (k + kAhead + 1 < n) __builtin_prefetch(&a[t[k + kAhead]], 1, 0);
+        const int64_t i = n - 1 - k, j = t[k];
+        T x = a[i]; a[i] = a[j]; a[j] = x;
     }
 }
 
-struct Draw {
-    std::vector<int32_t> sample;   // first n_sub of the permutation: sample_idx order
-    std::vector<int32_t> feat;     // n_feat sorted feature ids
+// One round drawn ahead: the row swap targets (the row shuffle itself is
+// applied by the consumer: on the host for gbm_sampler_next, on the device
+// for an engine) and the round's sorted feature ids.
+struct Round {
+    std::vector<int32_t> trow;          // n + 8 entries
+    std::vector<int32_t> feat;          // n_feat
+    bool ready = false;
 };
 
-struct Targets {                   // one round's swap targets
-    std::vector<int32_t> rows, feats;
-};
+enum { kModeUnset = 0, kModeHost, kModeTargets };
 
-}  // namespace
+}  // namespace gbmsamp
+
+using namespace gbmsamp;
 
 struct gbm_sampler {
     MT19937 rng;
     int64_t n = 0, n_sub = 0;
     int32_t p = 0, n_feat = 0;
     int sub_on = 0, col_on = 0;
-    std::vector<int32_t> perm;
-    std::vector<int32_t> fperm;
-    Targets tg;                    // synchronous path scratch
-    // look-ahead: stage 1 draws targets, stage 2 applies them
+    std::vector<int32_t> perm;         // host-side row permutation (kModeHost)
+    std::vector<int32_t> fperm, tfeat;
+    std::vector<int32_t> sample;
+    int mode = kModeUnset;
+    int64_t taken = 0;                 // rounds handed out
+    Round sync_round;
     int ahead = 0;
-    std::thread t_draw, t_apply;
+    std::vector<Round> ring;
+    int64_t r_draw = 0;
+    std::thread t_draw;
     std::mutex mu;
     std::condition_variable cv;
-    std::deque<Targets> tq;
-    std::deque<Draw> dq;
     bool stop = false;
 
-    void make_targets(Targets &t) {
-        if (sub_on) { t.rows.resize((size_t)n); draw_targets(rng, n, t.rows.data()); }
-        if (col_on) { t.feats.resize((size_t)p); draw_targets(rng, p, t.feats.data()); }
+    // The round's row targets, and its feature shuffle (applied here: it is
+    // cheap and must follow round order, as the draws do).
+    void draw(Round &R) {
+        if (sub_on) draw_targets(rng, n, R.trow.data());
+        if (col_on) {
+            draw_targets(rng, p, tfeat.data());
+            apply_swaps(fperm.data(), p, tfeat.data());
+        }
+        std::memcpy(R.feat.data(), fperm.data(), sizeof(int32_t) * (size_t)n_feat);
+        std::sort(R.feat.begin(), R.feat.end());
     }
-    Draw apply(const Targets &t) {
-        Draw d;
-        if (sub_on) apply_swaps(perm.data(), n, t.rows.data());
-        d.sample.assign(perm.begin(), perm.begin() + n_sub);
-        if (col_on) apply_swaps(fperm.data(), p, t.feats.data());
-        d.feat.assign(fperm.begin(), fperm.begin() + n_feat);
-        std::sort(d.feat.begin(), d.feat.end());
-        return d;
-    }
+    Round &slot(int64_t r) { return ring[(size_t)(r % (int64_t)ring.size())]; }
     void run_draw() {
         for (;;) {
+            Round *R;
             {
                 std::unique_lock<std::mutex> lk(mu);
-                cv.wait(lk, [&] { return stop || (int)tq.size() < ahead; });
+                cv.wait(lk, [&] { return stop || !slot(r_draw).ready; });
                 if (stop) return;
+                R = &slot(r_draw);
             }
-            Targets t;
-            make_targets(t);
+            draw(*R);
             std::lock_guard<std::mutex> lk(mu);
-            tq.push_back(std::move(t));
+            R->ready = true;
+            r_draw++;
             cv.notify_all();
         }
     }
-    void run_apply() {
-        for (;;) {
-            Targets t;
-            {
-                std::unique_lock<std::mutex> lk(mu);
-                cv.wait(lk, [&] { return stop || (!tq.empty() && (int)dq.size() < ahead); });
-                if (stop) return;
-                t = std::move(tq.front());
-                tq.pop_front();
-                cv.notify_all();
-            }
-            Draw d = apply(t);
-            std::lock_guard<std::mutex> lk(mu);
-            dq.push_back(std::move(d));
-            cv.notify_all();
-        }
-    }
-    Draw next() {
+    // Hand the next round to `take` (called without the lock, before the
+    // round's buffers are reused).
+    template <typename F>
+    void next(F &&take) {
         if (ahead <= 0) {
-            make_targets(tg);
-            return apply(tg);
+            draw(sync_round);
+            take(sync_round);
+            taken++;
+            return;
         }
-        std::unique_lock<std::mutex> lk(mu);
-        cv.wait(lk, [&] { return !dq.empty(); });
-        Draw d = std::move(dq.front());
-        dq.pop_front();
+        Round *R;
+        {
+            std::unique_lock<std::mutex> lk(mu);
+            cv.wait(lk, [&] { return slot(taken).ready; });
+            R = &slot(taken);
+        }
+        take(*R);
+        std::lock_guard<std::mutex> lk(mu);
+        R->ready = false;
+        taken++;
         cv.notify_all();
-        return d;
+    }
+    bool claim(int m) {
+        if (mode == kModeUnset) mode = m;
+        return mode == m;
+    }
+    // host mode: the cumulative shuffle of the rows, in place
+    void host_sample(const Round &R) {
+        if (sub_on) apply_swaps(perm.data(), n, R.trow.data());
+        std::memcpy(sample.data(), perm.data(), sizeof(int32_t) * (size_t)n_sub);
     }
 };
 
@@ -198,41 +273,75 @@ int gbm_sampler_create(uint32_t seed, int64_t n, int32_t p, int64_t n_sub, int32
         return GBM_ERR_ARG;
     gbm_sampler *s = new (std::nothrow) gbm_sampler();
     if (!s) return GBM_ERR_ALLOC;
-    s->rng.seed(seed);
-    s->n = n; s->p = p; s->n_sub = n_sub; s->n_feat = n_feat;
-    s->sub_on = subsample_on; s->col_on = colsample_on;
-    s->perm.resize((size_t)n);
-    for (int64_t i = 0; i < n; i++) s->perm[(size_t)i] = (int32_t)i;
-    s->fperm.resize((size_t)p);
-    for (int32_t i = 0; i < p; i++) s->fperm[(size_t)i] = i;
-    s->ahead = look_ahead < 0 ? 0 : look_ahead;
-    if (s->ahead > 0) {
-        s->t_draw = std::thread([s] { s->run_draw(); });
-        s->t_apply = std::thread([s] { s->run_apply(); });
+    try {
+        s->rng.seed(seed);
+        s->n = n; s->p = p; s->n_sub = n_sub; s->n_feat = n_feat;
+        s->sub_on = subsample_on; s->col_on = colsample_on;
+        s->fperm.resize((size_t)p);
+        for (int32_t i = 0; i < p; i++) s->fperm[(size_t)i] = i;
+        s->tfeat.resize((size_t)p + 8);
+        s->ahead = look_ahead < 0 ? 0 : look_ahead;
+        auto size_round = [&](Round &R) {
+            if (s->sub_on) R.trow.resize((size_t)n + 8);
+            R.feat.resize((size_t)n_feat);
+        };
+        if (s->ahead > 0) {
+            s->ring.resize((size_t)s->ahead + 1);
+            for (auto &R : s->ring) size_round(R);
+            s->t_draw = std::thread([s] { s->run_draw(); });
+        } else {
+            size_round(s->sync_round);
+        }
+    } catch (...) {
+        gbm_sampler_destroy(s);
+        return GBM_ERR_ALLOC;
     }
     *out = s;
     return GBM_OK;
 }
 
+// Host outputs: the row permutation is kept here (first call decides).
+static int host_ready(gbm_sampler *s) {
+    if (!s->claim(kModeHost)) return GBM_ERR_STATE;
+    if (s->perm.empty()) {
+        try {
+            s->perm.resize((size_t)s->n);
+            s->sample.resize((size_t)s->n_sub);
+        } catch (...) {
+            return GBM_ERR_ALLOC;
+        }
+        for (int64_t i = 0; i < s->n; i++) s->perm[(size_t)i] = (int32_t)i;
+    }
+    return GBM_OK;
+}
+
 int gbm_sampler_next(gbm_sampler *s, int64_t *sample_idx, uint8_t *inbag_mask, int32_t *feat_idx) {
     if (!s) return GBM_ERR_ARG;
-    Draw d = s->next();
-    if (sample_idx)
-        for (int64_t k = 0; k < s->n_sub; k++) sample_idx[k] = d.sample[(size_t)k];
-    if (inbag_mask) {
-        std::memset(inbag_mask, 0, (size_t)s->n);
-        for (int64_t k = 0; k < s->n_sub; k++) inbag_mask[d.sample[(size_t)k]] = 1;
-    }
-    if (feat_idx)
-        for (int32_t k = 0; k < s->n_feat; k++) feat_idx[k] = d.feat[(size_t)k];
+    int rc = host_ready(s);
+    if (rc != GBM_OK) return rc;
+    s->next([&](const Round &d) {
+        s->host_sample(d);
+        if (sample_idx)
+            for (int64_t k = 0; k < s->n_sub; k++) sample_idx[k] = s->sample[(size_t)k];
+        if (inbag_mask) {
+            std::memset(inbag_mask, 0, (size_t)s->n);
+            for (int64_t k = 0; k < s->n_sub; k++) inbag_mask[s->sample[(size_t)k]] = 1;
+        }
+        if (feat_idx)
+            for (int32_t k = 0; k < s->n_feat; k++) feat_idx[k] = d.feat[(size_t)k];
+    });
     return GBM_OK;
 }
 
 int gbm_sampler_next_rows(gbm_sampler *s, int32_t *sample_rows, int32_t *feat_idx) {
     if (!s || !sample_rows || !feat_idx) return GBM_ERR_ARG;
-    Draw d = s->next();
-    std::memcpy(sample_rows, d.sample.data(), sizeof(int32_t) * (size_t)s->n_sub);
-    std::memcpy(feat_idx, d.feat.data(), sizeof(int32_t) * (size_t)s->n_feat);
+    int rc = host_ready(s);
+    if (rc != GBM_OK) return rc;
+    s->next([&](const Round &d) {
+        s->host_sample(d);
+        std::memcpy(sample_rows, s->sample.data(), sizeof(int32_t) * (size_t)s->n_sub);
+        std::memcpy(feat_idx, d.feat.data(), sizeof(int32_t) * (size_t)s->n_feat);
+    });
     return GBM_OK;
 }
 
@@ -247,8 +356,23 @@ void gbm_sampler_destroy(gbm_sampler *s) {
     }
     s->cv.notify_all();
     if (s->t_draw.joinable()) s->t_draw.join();
-    if (s->t_apply.joinable()) s->t_apply.join();
     delete s;
 }
 
 }  // extern "C"
+
+// ---- engine side (sampler_internal.h) ----------------------------------------
+
+int gbm_sampler_take_targets(gbm_sampler *s, int32_t *row_targets, int32_t *feat_idx) {
+    if (!s || !feat_idx || (s->sub_on && !row_targets)) return GBM_ERR_ARG;
+    if (!s->claim(kModeTargets)) return GBM_ERR_STATE;
+    s->next([&](const Round &d) {
+        if (s->sub_on) std::memcpy(row_targets, d.trow.data(), sizeof(int32_t) * (size_t)(s->n - 1));
+        std::memcpy(feat_idx, d.feat.data(), sizeof(int32_t) * (size_t)s->n_feat);
+    });
+    return GBM_OK;
+}
+
+int64_t gbm_sampler_taken(const gbm_sampler *s) { return s ? s->taken : 0; }
+int64_t gbm_sampler_rows(const gbm_sampler *s) { return s ? s->n : 0; }
+int gbm_sampler_shuffles_rows(const gbm_sampler *s) { return s ? s->sub_on : 0; }

@@ -115,6 +115,12 @@ int gbm_nccl_unique_id(void *uid_out /* 128 bytes */);
 int gbm_upload_bins(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p,
                     const int32_t *bin_counts);
 
+/* The same from the reference's own uint16 bin matrix (bin_features'
+ * output dtype, E:2144-2190): the ids are clamped and narrowed to uint8 on
+ * the device, so the caller needs no host-side conversion pass. */
+int gbm_upload_bins_u16(gbm_ctx *ctx, const uint16_t *xbin, int64_t n, int32_t p,
+                        const int32_t *bin_counts);
+
 /* Labels (0/1) of this rank's rows, the two class weights of
  * _compute_class_weights (E:2570-2603) and the base score (E:2829-2835).
  * Resets F to base_score and computes round-0 gradients.  `n_global` is the
@@ -135,6 +141,16 @@ int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, 
  * built there.  Same results as gbm_round with the equivalent mask. */
 int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *params,
                       gbm_tree_out *out, double *train_loss);
+
+/* n_rounds consecutive gbm_round_sampled calls, the fit loop of
+ * _fit_binary (E:2849-2905): outs[r] and train_loss[r] get round r's tree
+ * and loss, identical to calling gbm_round_sampled n_rounds times.  When
+ * the tree is replayed on the device (depth-wise growth, or best-first with
+ * max_depth <= 9) the rounds are queued back to back with no host wait in
+ * between (up to 4 in flight); otherwise, or when any outs[r].leaf_of_row
+ * is set, the rounds run one by one. */
+int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *params,
+                   int32_t n_rounds, gbm_tree_out *outs, double *train_loss);
 
 /* One tree from caller-supplied float64 gradients and hessians [n] (this
  * rank's rows): the reference's internal seam _build_one_tree(X_bin, grad,
@@ -215,11 +231,17 @@ typedef struct {
     double host_sample_ms;     /* host time waiting for the sampler's draws */
     double host_sync_ms;       /* host time waiting for the device */
     double host_replay_ms;     /* host time in the best-first replay */
+    double flush_ms;           /* device time of the gbm_set_l2_flush writes */
 } gbm_stats;
 
 int gbm_set_profiling(gbm_ctx *ctx, int32_t on);
 int gbm_get_stats(gbm_ctx *ctx, gbm_stats *out);
 int gbm_reset_stats(gbm_ctx *ctx);
+/* Benchmark aid (no reference counterpart): with bytes > 0, every round
+ * starts with a write of `bytes` of device scratch on the context's stream,
+ * which evicts the L2 cache between timed rounds; its device time is
+ * reported in gbm_stats.flush_ms while profiling is on.  0 turns it off. */
+int gbm_set_l2_flush(gbm_ctx *ctx, int64_t bytes);
 /* CUDA events on the context's stream (slots 0..15), for timing regions. */
 int gbm_event_record(gbm_ctx *ctx, int32_t slot);
 int gbm_event_elapsed(gbm_ctx *ctx, int32_t a, int32_t b, float *ms);

@@ -69,6 +69,29 @@ def test_build_tree_matches_oracle_exact(engine, case):
     assert np.abs(t[2][:nc] - d["tv"][:nc]).max() <= 1e-9
 
 
+@pytest.mark.parametrize("case", ["basic", "few_bins", "tied", "nan_heavy", "leaves4"])
+def test_build_tree_host_replay_matches_oracle_exact(engine, case):
+    """Best-first trees deeper than 9 levels rank each level's expansions
+    (capped at max_leaves - 1) and are replayed on the host, expanding on
+    demand what the ranking left out: the same bit-exact bar."""
+    from bsscl_gbm_b200 import binning
+    d = golden("tree_" + case)
+    counts = d["counts"]
+    Xb = d["X_bin"]
+    n = Xb.shape[0]
+    engine.upload_bins(binning.device_bins(Xb, counts), counts)
+    mask = np.zeros(n, np.uint8)
+    mask[d["sample_idx"]] = 1
+    kw = dict(max_leaves=int(d["max_leaves"]), max_depth=14, msl=int(d["msl"]),
+              mcw=float(d["mcw"]), lam=float(d["lam"]), gamma=float(d["gamma"]))
+    t = engine.build_tree(d["g"], d["h"], mask, d["feat_idx"], _params(**kw),
+                          _cap(kw["max_leaves"], kw["max_depth"], "leaf"))
+    o = O.build_tree(Xb, d["g"], d["h"], d["sample_idx"], d["feat_idx"], counts, mode=O.MODE_EXACT,
+                     scale_bits=engine.scale_bits(), policy="leaf", **kw)
+    O.post_prune(o[0], o[3], o[4], o[6], kw["gamma"], o[5])
+    _assert_tree_equal(t, o, case)
+
+
 def test_build_tree_empty_inbag(engine):
     """No in-bag rows: the root is a leaf with value -0/(0+lambda), like the reference."""
     from bsscl_gbm_b200 import binning
@@ -205,5 +228,60 @@ def test_round_sampled_equals_round_with_mask(engine):
         _, mask, feat = s2.next(want_sample=False, want_mask=True)
         t, _, _ = engine.round(mask, feat, prm, 64)
         _assert_tree_equal(trees_a[r], t, f"round {r}")
+    assert np.array_equal(engine.get_F(), Fa)
+    s2.close()
+
+
+@pytest.mark.parametrize("policy,depth,leaves", [("leaf", 6, 31), ("level", 5, 31), ("leaf", 8, 15),
+                                                 ("leaf", 11, 31)])
+def test_fit_rounds_equals_round_sampled(engine, policy, depth, leaves):
+    """gbm_fit_rounds (rounds queued back to back, several in flight) gives
+    the trees, losses and F of the same number of gbm_round_sampled calls;
+    depth 11 takes the one-by-one path (host replay)."""
+    from bsscl_gbm_b200 import Sampler
+    d, Xb, y, w2, base = _cfg1_engine(engine)
+    n, p = Xb.shape
+    prm = _params(max_leaves=leaves, max_depth=depth, mcw=2.0, policy=policy)
+    cap = _cap(leaves, depth, policy)
+    rounds = 9
+    s1 = Sampler(3, n, p, int(n * 0.7), int(p * 0.6), True, True, look_ahead=2)
+    ref = [engine.round_sampled(s1, 0, prm, cap)[:2] for _ in range(rounds)]
+    Fa = engine.get_F()
+    s1.close()
+    engine.upload_labels(y.astype(np.uint8), w2, base, n_global=len(y))
+    s2 = Sampler(3, n, p, int(n * 0.7), int(p * 0.6), True, True, look_ahead=2)
+    got = engine.fit_rounds(s2, 0, prm, cap, 5) + engine.fit_rounds(s2, 0, prm, cap, rounds - 5)
+    s2.close()
+    for r in range(rounds):
+        _assert_tree_equal(ref[r][0], got[r][0], f"round {r}")
+        assert ref[r][1] == got[r][1]
+    assert np.array_equal(engine.get_F(), Fa)
+
+
+def test_device_row_shuffle_at_scale(engine):
+    """300k rows: the rounds whose in-bag rows come from the device-side
+    shuffle (gbm_round_sampled) equal the rounds given the host sampler's
+    masks (gbm_round), tree for tree and in F."""
+    from bsscl_gbm_b200 import Sampler
+    rng = np.random.default_rng(4)
+    n, p = 300_000, 20
+    Xb = rng.integers(0, 64, size=(n, p)).astype(np.uint8)
+    counts = np.full(p, 64, np.int32)
+    y = (rng.random(n) < 0.3).astype(np.uint8)
+    w2 = O.class_weights(y, None)
+    base = O.base_score(y, w2)
+    engine.upload_bins(Xb, counts)
+    engine.upload_labels(y, w2, base, n_global=n)
+    prm = _params(max_leaves=15, max_depth=4)
+    s1 = Sampler(21, n, p, int(n * 0.6), 12, True, True, look_ahead=3)
+    a = [engine.round_sampled(s1, 0, prm, 32)[0] for _ in range(3)]
+    Fa = engine.get_F()
+    s1.close()
+    engine.upload_labels(y, w2, base, n_global=n)
+    s2 = Sampler(21, n, p, int(n * 0.6), 12, True, True, look_ahead=0)
+    for r in range(3):
+        _, mask, feat = s2.next(want_sample=False, want_mask=True)
+        t, _, _ = engine.round(mask, feat, prm, 32)
+        _assert_tree_equal(a[r], t, f"round {r}")
     assert np.array_equal(engine.get_F(), Fa)
     s2.close()

@@ -73,6 +73,68 @@ def test_sampler_matches_numpy_randomstate(built_lib):
             s.close()
 
 
+def test_sampler_matches_numpy_at_full_size(built_lib):
+    """1M rows (every mask width of the bounded draw, the vectorised blocks
+    and their word-by-word fallback) against NumPy's RandomState itself."""
+    from bsscl_gbm_b200 import Sampler
+    n, p = 1_000_000, 100
+    rs = np.random.RandomState(11)
+    rows, feats = np.arange(n), np.arange(p, dtype=np.int32)
+    s = Sampler(11, n, p, 750_000, 70, True, True, look_ahead=2)
+    for _ in range(2):
+        rs.shuffle(rows)
+        rs.shuffle(feats)
+        smp, _, feat = s.next(want_sample=True, want_mask=False)
+        assert np.array_equal(smp, rows[:750_000])
+        assert np.array_equal(feat, np.sort(feats[:70]))
+    s.close()
+
+
+def _fisher_yates(n, j):
+    a = np.arange(n)
+    for i in range(n - 1, 0, -1):
+        a[i], a[j[i]] = a[j[i]], a[i]
+    return a
+
+
+def _shuffle_from_targets(n, j):
+    """The engine's parallel construction of a round's shuffle (gbm_kernels.cuh,
+    k_shuf_link / k_shuf_min / k_shuf_compose), restated with NumPy."""
+    steps = np.arange(1, n)
+    order = np.lexsort((steps, j[1:]))                 # steps grouped by target, ascending
+    tgt, st = j[1:][order], steps[order]
+    m = np.full(n, -1)                                 # m(q): smallest step > q targeting q
+    mp = np.full(n, -1)                                # mp(i): next larger step with i's target
+    same = tgt[1:] == tgt[:-1]
+    mp[st[:-1][same]] = st[1:][same]
+    above = st > tgt
+    first = np.ones(len(st), bool)
+    first[1:] = ~(same & above[:-1] & above[1:])
+    sel = above & first
+    for q, i in zip(tgt[sel], st[sel]):
+        if m[q] < 0:
+            m[q] = i
+    def root(i):
+        while m[i] >= 0:
+            i = m[i]
+        return i
+    S = np.empty(n, np.int64)
+    S[0] = root(m[0]) if m[0] >= 0 else 0
+    for i in range(1, n):
+        S[i] = root(mp[i]) if mp[i] >= 0 else j[i]
+    return S
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 17, 1000, 20000])
+def test_parallel_shuffle_construction_equals_fisher_yates(n):
+    rng = np.random.default_rng(n)
+    for _ in range(3):
+        j = np.zeros(n, np.int64)
+        for i in range(1, n):
+            j[i] = rng.integers(0, i + 1)
+        assert np.array_equal(_shuffle_from_targets(n, j), _fisher_yates(n, j))
+
+
 def test_sampler_matches_fit_stream(built_lib):
     """The per-round sample hashes the reference recorded during its fit."""
     from bsscl_gbm_b200 import Sampler
