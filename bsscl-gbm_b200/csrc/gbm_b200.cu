@@ -33,6 +33,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -74,7 +75,9 @@ struct gbm_ctx {
     int32_t *d_rows = nullptr, *d_tmp = nullptr;
     int32_t *d_cnt = nullptr, *d_off = nullptr, *d_total = nullptr;
     int32_t *d_blist = nullptr, *d_fidx = nullptr;
-    int16_t *d_fpos = nullptr;
+    int32_t *d_bwp = nullptr;          // histogram cost prefix over the active blocks
+    int16_t *d_fpos = nullptr, *d_fbi = nullptr;
+    int hist_grid = 0;                 // k_hist CTAs: one wave of 2 per SM
     int nf_cap = 0;
     long long *d_pool = nullptr;       // node histograms: slot i = node i
     long long *d_stage = nullptr;      // smaller-child histograms of one level
@@ -87,6 +90,7 @@ struct gbm_ctx {
     int32_t *d_tile_cnt = nullptr, *d_tile_off = nullptr;
     int tile_cap = 0;
     long long *d_nleft = nullptr, *d_nleft_g = nullptr, *d_count64 = nullptr;
+    long long *d_leafw = nullptr;      // last level: per-parent count and (G, H) words
     DNode *d_nodes = nullptr;
     int *d_lvl[2] = {nullptr, nullptr};
     int *d_ints = nullptr;             // [0] one, [1] node count, [2] tiles, [3..4] level counts
@@ -107,8 +111,8 @@ struct gbm_ctx {
     // end; gbm_fit_rounds keeps up to kRing rounds queued.
     struct Slot {
         int32_t *h_tg = nullptr, *d_tg = nullptr;   // the round's row swap targets
-        int32_t *h_feat = nullptr;     // fidx [p] | blist [nblk]
-        int16_t *h_fpos = nullptr;     // [nblk * 16]
+        int32_t *h_feat = nullptr;     // fidx [p] | blist [nblk] | bwp [nblk + 1]
+        int16_t *h_fpos = nullptr;     // fpos [nblk * 16] | fbi [p]
         TreeOut *h_tout = nullptr;
         double *h_loss = nullptr;
         cudaEvent_t copied = nullptr, done = nullptr;
@@ -258,12 +262,20 @@ struct RoundFeat {
     std::vector<int16_t> fpos;
 };
 
+// Histogram cost of a row in an active block: its loads (about two
+// feature updates' worth) plus one unit per selected feature.
+int block_weight(const RoundFeat &rf, int blk) {
+    int w = 2;
+    for (int k = 0; k < kBlk; k++) w += rf.fpos[(size_t)blk * kBlk + k] >= 0;
+    return w;
+}
+
 // Per-slot pinned staging, sized for the data.
 int ensure_slots(gbm_ctx *ctx) {
     if (!ctx->slots_ready) {   // once per gbm_upload_bins (sizes follow p)
         for (auto &s : ctx->slot) {
-            TRY(halloc(ctx, &s.h_feat, (size_t)ctx->p + ctx->nblk));
-            TRY(halloc(ctx, &s.h_fpos, (size_t)ctx->nblk * kBlk));
+            TRY(halloc(ctx, &s.h_feat, (size_t)ctx->p + 2 * ctx->nblk + 1));
+            TRY(halloc(ctx, &s.h_fpos, (size_t)ctx->nblk * kBlk + ctx->p));
             TRY(halloc(ctx, &s.h_tout, 1));
             TRY(halloc(ctx, &s.h_loss, 1));
             if (!s.copied) CK(cudaEventCreateWithFlags(&s.copied, cudaEventDisableTiming));
@@ -311,13 +323,24 @@ int setup_features(gbm_ctx *ctx, int si, const int32_t *fidx, int nf, RoundFeat 
         for (int k = 0; k < kBlk; k++) any |= rf.fpos[(size_t)b * kBlk + k] >= 0;
         if (any) rf.blist.push_back(b);
     }
+    const int nb = (int)rf.blist.size();
+    int32_t *h_blist = s.h_feat + ctx->p, *h_bwp = h_blist + nb;   // the device reads blist | bwp
+    int16_t *h_fbi = s.h_fpos + (size_t)ctx->nblk * kBlk;
     std::memcpy(s.h_feat, fidx, sizeof(int32_t) * nf);
-    std::memcpy(s.h_feat + ctx->p, rf.blist.data(), sizeof(int32_t) * rf.blist.size());
+    std::memcpy(h_blist, rf.blist.data(), sizeof(int32_t) * nb);
+    h_bwp[0] = 0;
+    for (int bi = 0; bi < nb; bi++) {
+        h_bwp[bi + 1] = h_bwp[bi] + block_weight(rf, rf.blist[bi]);
+        for (int k = 0; k < kBlk; k++) {
+            int jj = rf.fpos[(size_t)rf.blist[bi] * kBlk + k];
+            if (jj >= 0) h_fbi[jj] = (int16_t)bi;
+        }
+    }
     std::memcpy(s.h_fpos, rf.fpos.data(), sizeof(int16_t) * rf.fpos.size());
     CK(cudaMemcpyAsync(ctx->d_fidx, s.h_feat, sizeof(int32_t) * nf, cudaMemcpyHostToDevice, ctx->st));
     CK(cudaMemcpyAsync(ctx->d_fpos, s.h_fpos, sizeof(int16_t) * rf.fpos.size(), cudaMemcpyHostToDevice, ctx->st));
-    CK(cudaMemcpyAsync(ctx->d_blist, s.h_feat + ctx->p, sizeof(int32_t) * rf.blist.size(), cudaMemcpyHostToDevice,
-                       ctx->st));
+    CK(cudaMemcpyAsync(ctx->d_fbi, h_fbi, sizeof(int16_t) * nf, cudaMemcpyHostToDevice, ctx->st));
+    CK(cudaMemcpyAsync(ctx->d_blist, h_blist, sizeof(int32_t) * (2 * nb + 1), cudaMemcpyHostToDevice, ctx->st));
     return GBM_OK;
 }
 
@@ -369,6 +392,7 @@ int ensure_round_buffers(gbm_ctx *ctx, int nf, const gbm_params *P) {
         TRY(dalloc(ctx, &ctx->d_ptask, (size_t)ctx->stage_slots));
         TRY(dalloc(ctx, &ctx->d_nleft, (size_t)ctx->stage_slots));
         TRY(dalloc(ctx, &ctx->d_nleft_g, (size_t)ctx->stage_slots));
+        TRY(dalloc(ctx, &ctx->d_leafw, (size_t)ctx->stage_slots * kLeafWords));
         int smem = (int)(sizeof(RNode) * (size_t)ctx->nmax);
         ctx->replay_smem = 0;
         if (smem <= kReplaySmemMax) ctx->replay_smem = smem;
@@ -384,19 +408,15 @@ bool device_replay(const gbm_ctx *ctx, const gbm_params *P) {
 
 // ---- launches -----------------------------------------------------------------
 
-// Rows per histogram CTA: about two waves of 2 CTAs per SM over the feature
-// blocks, a power of two in [1024, kChunk].
-int hist_chunk(int64_t rows, int nblocks) {
-    int64_t target = 148 * 2 * 2;
-    int64_t c = (rows * std::max(1, nblocks) + target - 1) / target;
-    int chunk = 1024;
-    while (chunk < c && chunk < kChunk) chunk <<= 1;
-    return chunk;
-}
-
-int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int max_chunks, int chunk) {
-    if (max_chunks <= 0 || rf.blist.empty()) return GBM_OK;
-    dim3 grid((unsigned)max_chunks, (unsigned)rf.blist.size());
+// Zero the staging cells that are added atomically, then the histograms of
+// the tasks at *ntask_p (at most W_ub) on ctx->hist_grid equal-work CTAs.
+int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int W_ub) {
+    const int nb = (int)rf.blist.size();
+    if (W_ub <= 0 || nb == 0) return GBM_OK;
+    const int32_t *d_bwp = ctx->d_blist + nb;
+    k_zero_stage<<<dim3((unsigned)rf.nf + 1, (unsigned)W_ub), 256, 0, ctx->st>>>(
+        ctx->d_htask, ctx->d_hprefix, ntask_p, d_bwp, nb, ctx->d_fbi, rf.nf, ctx->hist_grid, ctx->d_stage);
+    CKL();
     size_t smem = (size_t)kAccWords * sizeof(unsigned);
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (ctx->profiling) {
@@ -412,9 +432,9 @@ int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int max_c
         ctx->hist_ev_used += 2;
         CK(cudaEventRecord(e0, ctx->st));
     }
-    k_hist<<<grid, kHistThreads, smem, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_htask,
-                                                   ctx->d_hprefix, ntask_p, ctx->d_blist, ctx->d_fpos,
-                                                   ctx->d_skipb, rf.nf, chunk, ctx->d_q, ctx->d_stage);
+    k_hist<<<ctx->hist_grid, kHistThreads, smem, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_htask,
+                                                           ctx->d_hprefix, ntask_p, ctx->d_blist, d_bwp, nb,
+                                                           ctx->d_fpos, ctx->d_skipb, rf.nf, ctx->d_q, ctx->d_stage);
     CKL();
     if (ctx->profiling) CK(cudaEventRecord(e1, ctx->st));
     ctx->hist_launches++;
@@ -470,14 +490,10 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_count64, 1, ctx->st, ctx->timeout_ms, ctx->err));
         ng = ctx->d_count64;
     }
-    const int chunk = hist_chunk(ctx->n, (int)rf.blist.size());
     k_root_plan<<<1, 1, 0, ctx->st>>>(ctx->d_total, ng, ctx->d_nodes, ctx->d_htask, ctx->d_hprefix,
-                                      ints(ctx, I_NODES), chunk);
+                                      ints(ctx, I_NODES));
     CKL();
-    k_zero_multi<<<dim3(grid_for(words, 256, 64), 1), 256, 0, ctx->st>>>(ctx->d_hprefix, ints(ctx, I_ONE),
-                                                                         ctx->d_stage, words);
-    CKL();
-    TRY(launch_hist(ctx, rf, ints(ctx, I_ONE), (int)((ctx->n + chunk - 1) / chunk), chunk));
+    TRY(launch_hist(ctx, rf, ints(ctx, I_ONE), 1));
     if (ctx->comm)
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words, ctx->st, ctx->timeout_ms, ctx->err));
     int fx = (rf.nf + kSplitWarps - 1) / kSplitWarps;
@@ -500,7 +516,7 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
 // smaller-child histogram, subtraction, children's splits.  When `next` is
 // given, also rank the children into the next level list.
 int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lvl, int *lvl_cnt,
-                 int *next, int *next_cnt, int W_ub) {
+                 int *next, int *next_cnt, int W_ub, bool last = false) {
     if (W_ub <= 0) return GBM_OK;
     const int64_t words = slot_words_for(rf.nf);
     k_lvl_plan<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ints(ctx, I_NODES), ctx->d_ptask,
@@ -511,6 +527,21 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
         ctx->tile_cap = tiles_ub;
         TRY(dalloc(ctx, &ctx->d_tile_cnt, (size_t)ctx->tile_cap));
         TRY(dalloc(ctx, &ctx->d_tile_off, (size_t)ctx->tile_cap));
+    }
+    if (last) {   // children at max_depth: counts and totals only
+        CK(cudaMemsetAsync(ctx->d_leafw, 0, sizeof(long long) * kLeafWords * W_ub, ctx->st));
+        CK(cudaMemsetAsync(ctx->d_nleft, 0, sizeof(long long) * W_ub, ctx->st));
+        k_leaf_totals<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_ptask, lvl_cnt,
+                                                              ints(ctx, I_TILES), ctx->d_q, ctx->d_leafw,
+                                                              ctx->d_nleft);
+        CKL();
+        if (ctx->comm)
+            TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_leafw, (int64_t)kLeafWords * W_ub, ctx->st, ctx->timeout_ms,
+                                       ctx->err));
+        k_leaf_finish<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ctx->d_leafw, ctx->d_nleft, ctx->S);
+        CKL();
+        ctx->waves++;
+        return GBM_OK;
     }
     k_part_count<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_ptask, lvl_cnt,
                                                          ints(ctx, I_TILES), ctx->d_tile_cnt);
@@ -531,15 +562,9 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_nleft_g, W_ub, ctx->st, ctx->timeout_ms, ctx->err));
         gl = ctx->d_nleft_g;
     }
-    int64_t chunk_rows = ctx->comm ? ctx->n : (ctx->n + 1) / 2;
-    const int chunk = hist_chunk(chunk_rows, (int)rf.blist.size());
-    k_plan_hist<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ctx->d_nleft, gl, ctx->d_htask, ctx->d_hprefix,
-                                        chunk);
+    k_plan_hist<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ctx->d_nleft, gl, ctx->d_htask, ctx->d_hprefix);
     CKL();
-    k_zero_multi<<<dim3(grid_for(words, 256, 64), W_ub), 256, 0, ctx->st>>>(ctx->d_hprefix, lvl_cnt, ctx->d_stage,
-                                                                            words);
-    CKL();
-    TRY(launch_hist(ctx, rf, lvl_cnt, (int)((chunk_rows + chunk - 1) / chunk) + W_ub, chunk));
+    TRY(launch_hist(ctx, rf, lvl_cnt, W_ub));
     if (ctx->comm)
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words * W_ub, ctx->st, ctx->timeout_ms, ctx->err));
     int fx = (rf.nf + kSplitWarps - 1) / kSplitWarps;
@@ -658,8 +683,11 @@ int replay_leafwise(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, Host
         T.tf[cur] = pc.feat; T.tt[cur] = pc.bin; T.tl[cur] = lid; T.tr[cur] = rid;
         T.tv[cur] = pc.val; T.sg[cur] = pc.gain;
         n_splits++;
-        ctx->alg_bytes += (double)std::min(gnl, gnr) * (rf.nf + 8);
         int nd_depth = pc.depth + 1;
+        if (nd_depth < P->max_depth) {   // the last level builds no histogram
+            const DNode &sm = nd[gnl <= gnr ? pn.kid0 : pn.kid1];
+            ctx->alg_bytes += (double)(sm.end - sm.begin) * (rf.nf + 8);
+        }
         bool left_small = gnl <= gnr;
         int ss = -1, sl = -1;                               // E:712-720
         for (int s = 0; s < MAXC; s++) {
@@ -720,7 +748,10 @@ int replay_depthwise(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, Hos
         if (!split) { T.tf[e.tid] = -1; T.tv[e.tid] = val; continue; }
         int lid = node_count++, rid = node_count++;
         long long gl = nd[x.kid0].n, gr = nd[x.kid1].n;
-        ctx->alg_bytes += (double)std::min(gl, gr) * (rf.nf + 8);
+        if (x.depth + 1 < D) {
+            const DNode &sm = nd[gl <= gr ? x.kid0 : x.kid1];
+            ctx->alg_bytes += (double)(sm.end - sm.begin) * (rf.nf + 8);
+        }
         T.tf[e.tid] = x.feat; T.tt[e.tid] = x.bin; T.tl[e.tid] = lid; T.tr[e.tid] = rid;
         T.tv[e.tid] = val; T.sg[e.tid] = x.gain;
         if (gl <= gr) {
@@ -809,7 +840,8 @@ int alloc_round_fixed(gbm_ctx *ctx) {
     TRY(dalloc(ctx, &ctx->d_off, (size_t)ntile));
     TRY(dalloc(ctx, &ctx->d_total, 1));
     TRY(dalloc(ctx, &ctx->d_count64, 1));
-    TRY(dalloc(ctx, &ctx->d_blist, (size_t)ctx->nblk));
+    TRY(dalloc(ctx, &ctx->d_blist, (size_t)2 * ctx->nblk + 1));   // blist | bwp
+    TRY(dalloc(ctx, &ctx->d_fbi, (size_t)ctx->p));
     TRY(dalloc(ctx, &ctx->d_fpos, (size_t)ctx->nblk * kBlk));
     TRY(dalloc(ctx, &ctx->d_ints, (size_t)I_COUNT));
     TRY(halloc(ctx, &ctx->h_ints, (size_t)I_COUNT));
@@ -861,8 +893,9 @@ int enqueue_grow(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
     int cur = 0;
     for (int L = 0; L < P->max_depth; L++) {
         int W = std::min(level_width(P, L), ctx->stage_slots);
+        const bool last = L == P->max_depth - 1;
         TRY(launch_level(ctx, rf, P, ctx->d_lvl[cur], ints(ctx, I_LVL0 + cur), ctx->d_lvl[1 - cur],
-                         ints(ctx, I_LVL0 + 1 - cur), W));
+                         ints(ctx, I_LVL0 + 1 - cur), W, last));
         cur = 1 - cur;
     }
     return GBM_OK;
@@ -1109,6 +1142,9 @@ int gbm_ctx_create(int32_t device, gbm_ctx **out) {
     CK(cudaSetDevice(device));
     CK(cudaStreamCreateWithFlags(&ctx->st, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&ctx->cst, cudaStreamNonBlocking));
+    int sms = 0;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    ctx->hist_grid = 2 * std::max(sms, 1);   // one wave of 2 per SM (measured best: fewer flushes)
     CK(cudaFuncSetAttribute(k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             kAccWords * (int)sizeof(unsigned)));
     // a function attribute is shared by every context of the process: set
@@ -1135,7 +1171,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
                         ctx->d_count64, ctx->d_nodes, ctx->d_lvl[0], ctx->d_lvl[1], ctx->d_ints, ctx->d_tree,
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
                         ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,
-                        ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp};
+                        ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi};
     for (int32_t *q : ctx->d_perm) if (q) cudaFree(q);
     for (void *p : dev_ptrs) if (p) cudaFree(p);
     void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_mono};

@@ -280,152 +280,209 @@ __global__ void k_count64(const int32_t *__restrict__ in, long long *__restrict_
 // histograms
 // ===========================================================================
 
-// grid: x = chunk id over all tasks (prefix[ntask] valid chunks), y = feature block.
-//
+// The histogram work of one launch is the rows of every task (node) for
+// every active feature block, laid out block-major: block bi, then task t,
+// then the task's rows.  A row of block bi costs w_bi = bwp[bi+1] - bwp[bi]
+// (2 + the block's selected features), so the launch costs T = bwp[nb] * R
+// for R rows over all tasks.  CTA c of G takes the rows whose cost position
+// lies in [B_c, B_c+1), B_c = floor(c T / G): every CTA gets the same work
+// whatever the tasks' sizes, and a launch is exactly G / (2 per SM) waves.
+// cta_of(x) is the CTA whose range holds cost position x.
+__device__ __forceinline__ long long cost_bound(long long c, long long T, long long G) { return c * T / G; }
+__device__ __forceinline__ long long cta_of(long long x, long long T, long long G) {
+    return ((x + 1) * G + T - 1) / T - 1;
+}
+__device__ __forceinline__ long long ceil_div_ll(long long a, long long b) { return (a + b - 1) / b; }
+
+// A (block, task) segment whose rows all fall in one CTA's range, and no
+// more than kChunk of them, is stored directly by that CTA; every other
+// segment is added atomically into a zeroed staging histogram.
+__device__ __forceinline__ bool segment_single(long long rows, long long first_pos, int w, long long T, long long G) {
+    if (rows <= 0 || rows > kChunk) return false;
+    return cta_of(first_pos, T, G) == cta_of(first_pos + (rows - 1) * w, T, G);
+}
+
 // Each row's q (int64) is split into three digits, q = top*2^34 + mid*2^17 +
 // low with low, mid in [0, 2^17) and top signed, and each digit is summed in
-// its own 32-bit shared-memory word: at most kChunk = 2^14 rows per CTA keep
-// every digit sum inside 32 bits, and native 32-bit shared atomics are much
-// faster than 64-bit ones.  `chunk` (<= kChunk) rows per CTA is chosen per
-// launch to spread the work over every SM.  Each feature skips its most frequent bin (the
-// NaN bin, typically); that cell is rebuilt exactly by the split kernel as
-// node total - sum(other cells).  A task of one chunk stores its cells; a
-// task spread over several CTAs adds (hi, lo) words atomically into a zeroed
-// staging histogram.  blockIdx.y == 0 also accumulates the node totals.
-// (E:582-596 root, E:723-737 smaller child.)
+// its own 32-bit shared-memory word: at most kChunk = 2^14 rows between two
+// flushes keep every digit sum inside 32 bits, and native 32-bit shared
+// atomics are much faster than 64-bit ones.  Each feature skips its most
+// frequent bin (the NaN bin, typically); that cell is rebuilt exactly by the
+// split kernel as node total - sum(other cells).  Block 0's pieces also sum
+// the node totals.  (E:582-596 root, E:723-737 smaller child.)
 __global__ void __launch_bounds__(kHistThreads, 2)
 k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows,
-       const HistTask *__restrict__ tasks, const int32_t *__restrict__ prefix,
-       const int *__restrict__ ntask_p, const int32_t *__restrict__ blist,
-       const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf, int chunk,
+       const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
+       const int *__restrict__ ntask_p, const int32_t *__restrict__ blist, const int32_t *__restrict__ bwp,
+       int nb, const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
        const longlong2 *__restrict__ q, long long *__restrict__ stage_hist) {
     extern __shared__ unsigned acc[];   // [6][16][256]
-    __shared__ int s_task;
     __shared__ long long s_tot[2][kHistThreads / 32];
     const int ntask = *ntask_p;
-    int cid = blockIdx.x;
-    if (ntask <= 0 || cid >= prefix[ntask]) return;
-    if (threadIdx.x == 0) {
-        int lo = 0, hi = ntask - 1;
-        while (lo < hi) {   // last task with prefix[t] <= cid
-            int mid = (lo + hi + 1) >> 1;
-            if (prefix[mid] <= cid) lo = mid; else hi = mid - 1;
-        }
-        s_task = lo;
-    }
-    for (int k = threadIdx.x; k < kAccWords; k += blockDim.x) acc[k] = 0u;
-    __syncthreads();
-    const int t = s_task;
-    const HistTask tk = tasks[t];
-    const bool single = (prefix[t + 1] - prefix[t]) == 1;
-    const int blk = blist[blockIdx.y];
-    long long r0 = tk.begin + (long long)(cid - prefix[t]) * chunk;
-    long long r1 = min(r0 + (long long)chunk, tk.end);
-    unsigned mask = 0;
-    int skip[kBlk];
-#pragma unroll
-    for (int k = 0; k < kBlk; k++) {
-        bool sel = fpos[blk * kBlk + k] >= 0;
-        mask |= (sel ? 1u : 0u) << k;
-        skip[k] = sel ? (int)skipb[blk * kBlk + k] : -1;
-    }
-    const uint4 *xv = reinterpret_cast<const uint4 *>(xb) + (int64_t)blk * n;
+    if (ntask <= 0) return;
+    const long long R = rpre[ntask];
+    const long long T = (long long)bwp[nb] * R;
+    if (T <= 0) return;
+    const long long G = gridDim.x;
+    const long long B0 = cost_bound(blockIdx.x, T, G), B1 = cost_bound(blockIdx.x + 1, T, G);
+    if (B0 >= B1) return;
     const int lane = threadIdx.x & 31;
-    long long tg = 0, th = 0;
-    for (long long rb = r0 + (threadIdx.x & ~31); rb < r1; rb += blockDim.x) {
-        const long long r = rb + lane;
-        const bool valid = r < r1;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        longlong2 qq = make_longlong2(0, 0);
-        if (valid) {
-            int row = rows[r];
-            v = __ldg(xv + row);
-            qq = __ldg(q + row);
-        }
-        tg += qq.x;
-        th += qq.y;
-        unsigned dg[3] = {(unsigned)qq.x & 0x1ffffu, (unsigned)(qq.x >> kDig) & 0x1ffffu,
-                          (unsigned)(int)(qq.x >> (2 * kDig))};
-        unsigned dh[3] = {(unsigned)qq.y & 0x1ffffu, (unsigned)(qq.y >> kDig) & 0x1ffffu,
-                          (unsigned)(int)(qq.y >> (2 * kDig))};
-        unsigned w[4] = {v.x, v.y, v.z, v.w};
+    const int64_t slot_words = slot_words_for(nf);
+    int bi = 0;
+    while (bi + 1 < nb && (long long)bwp[bi + 1] * R <= B0) bi++;
+    for (; bi < nb; bi++) {
+        const long long base = (long long)bwp[bi] * R;
+        if (base >= B1) break;
+        const int w = bwp[bi + 1] - bwp[bi];
+        const int k0 = (int)(B0 > base ? ceil_div_ll(B0 - base, w) : 0);
+        const int k1 = (int)min(R, ceil_div_ll(B1 - base, w));
+        if (k0 >= k1) continue;
+        const int blk = blist[bi];
+        unsigned mask = 0;
+        unsigned skipw[4] = {0u, 0u, 0u, 0u};   // the skipped bin of each feature, one byte each
 #pragma unroll
         for (int k = 0; k < kBlk; k++) {
-            if (mask & (1u << k)) {
-                int b = (w[k >> 2] >> ((k & 3) * 8)) & 0xff;
-                bool use = valid && b != skip[k];
-                if (use) {
-                    unsigned *c = acc + k * kBins + b;
-                    atomicAdd(c + 0 * kBlk * kBins, dg[0]);
-                    atomicAdd(c + 1 * kBlk * kBins, dg[1]);
-                    atomicAdd(c + 2 * kBlk * kBins, dg[2]);
-                    atomicAdd(c + 3 * kBlk * kBins, dh[0]);
-                    atomicAdd(c + 4 * kBlk * kBins, dh[1]);
-                    atomicAdd(c + 5 * kBlk * kBins, dh[2]);
+            bool sel = fpos[blk * kBlk + k] >= 0;
+            mask |= (sel ? 1u : 0u) << k;
+            skipw[k >> 2] |= (sel ? (unsigned)skipb[blk * kBlk + k] & 0xffu : 0u) << ((k & 3) * 8);
+        }
+        const uint4 *xv = reinterpret_cast<const uint4 *>(xb) + (int64_t)blk * n;
+        // the task holding row k0 (last t with rpre[t] <= k0)
+        int t;
+        {
+            int lo = 0, hi = ntask - 1;
+            while (lo < hi) {
+                int mid = (lo + hi + 1) >> 1;
+                if (rpre[mid] <= k0) lo = mid; else hi = mid - 1;
+            }
+            t = lo;
+        }
+        for (int k = k0; k < k1; t++) {
+            const int t0 = rpre[t], t1 = rpre[t + 1];
+            if (t1 <= k) continue;
+            const HistTask tk = tasks[t];
+            const int pe = min(k1, t1);
+            const bool single = k == t0 && pe == t1 && (t1 - t0) <= kChunk;
+            long long *dst = stage_hist + (int64_t)tk.stage * slot_words;
+            // the piece [k, pe) of task t, in runs of at most kChunk rows
+            for (int c0 = k; c0 < pe; c0 += kChunk) {
+                const int c1 = min(pe, c0 + kChunk);
+                for (int i = threadIdx.x; i < kAccWords; i += blockDim.x) acc[i] = 0u;
+                __syncthreads();
+                const int r0 = (int)tk.begin + (c0 - t0), r1 = (int)tk.begin + (c1 - t0);
+                long long tg = 0, th = 0;
+                for (int rb = r0 + (int)(threadIdx.x & ~31u); rb < r1; rb += blockDim.x) {
+                    const int r = rb + lane;
+                    const bool valid = r < r1;
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    longlong2 qq = make_longlong2(0, 0);
+                    if (valid) {
+                        int row = rows[r];
+                        v = __ldg(xv + row);
+                        qq = __ldg(q + row);
+                    }
+                    tg += qq.x;
+                    th += qq.y;
+                    unsigned dg[3] = {(unsigned)qq.x & 0x1ffffu, (unsigned)(qq.x >> kDig) & 0x1ffffu,
+                                      (unsigned)(int)(qq.x >> (2 * kDig))};
+                    unsigned dh[3] = {(unsigned)qq.y & 0x1ffffu, (unsigned)(qq.y >> kDig) & 0x1ffffu,
+                                      (unsigned)(int)(qq.y >> (2 * kDig))};
+                    unsigned wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int f = 0; f < kBlk; f++) {
+                        if (mask & (1u << f)) {
+                            const int b = (wv[f >> 2] >> ((f & 3) * 8)) & 0xff;
+                            const int sb = (skipw[f >> 2] >> ((f & 3) * 8)) & 0xff;
+                            if (valid && b != sb) {
+                                unsigned *cc = acc + f * kBins + b;
+                                atomicAdd(cc + 0 * kBlk * kBins, dg[0]);
+                                atomicAdd(cc + 1 * kBlk * kBins, dg[1]);
+                                atomicAdd(cc + 2 * kBlk * kBins, dg[2]);
+                                atomicAdd(cc + 3 * kBlk * kBins, dh[0]);
+                                atomicAdd(cc + 4 * kBlk * kBins, dh[1]);
+                                atomicAdd(cc + 5 * kBlk * kBins, dh[2]);
+                            }
+                        }
+                    }
                 }
+                if (bi == 0) {
+                    tg = warp_sum(tg);
+                    th = warp_sum(th);
+                    if (lane == 0) {
+                        s_tot[0][threadIdx.x >> 5] = tg;
+                        s_tot[1][threadIdx.x >> 5] = th;
+                    }
+                }
+                __syncthreads();
+                if (bi == 0 && threadIdx.x < 2) {
+                    long long tot = 0;
+                    for (int w2 = 0; w2 < kHistThreads / 32; w2++) tot += s_tot[threadIdx.x][w2];
+                    long long *o = dst + (int64_t)nf * kBins * kWords + 2 * threadIdx.x;
+                    if (single) {
+                        o[0] = tot >> 32;
+                        o[1] = tot & 0xffffffffll;
+                    } else if (tot) {
+                        atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(tot >> 32));
+                        atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(tot & 0xffffffffll));
+                    }
+                }
+                for (int idx = threadIdx.x; idx < kBlk * kBins; idx += blockDim.x) {
+                    int f = idx >> 8, b = idx & 255;
+                    int jj = fpos[blk * kBlk + f];
+                    if (jj < 0) continue;
+                    long long gv = ((long long)(int)acc[2 * kBlk * kBins + idx] << (2 * kDig)) +
+                                   ((long long)acc[1 * kBlk * kBins + idx] << kDig) + (long long)acc[idx];
+                    long long hv = ((long long)(int)acc[5 * kBlk * kBins + idx] << (2 * kDig)) +
+                                   ((long long)acc[4 * kBlk * kBins + idx] << kDig) +
+                                   (long long)acc[3 * kBlk * kBins + idx];
+                    long long *o = dst + ((int64_t)jj * kBins + b) * kWords;
+                    if (single) {
+                        reinterpret_cast<longlong2 *>(o)[0] = make_longlong2(gv >> 32, gv & 0xffffffffll);
+                        reinterpret_cast<longlong2 *>(o)[1] = make_longlong2(hv >> 32, hv & 0xffffffffll);
+                    } else {
+                        if (gv) {
+                            atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(gv >> 32));
+                            atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(gv & 0xffffffffll));
+                        }
+                        if (hv) {
+                            atomicAdd((unsigned long long *)(o + 2), (unsigned long long)(hv >> 32));
+                            atomicAdd((unsigned long long *)(o + 3), (unsigned long long)(hv & 0xffffffffll));
+                        }
+                    }
+                }
+                __syncthreads();
             }
-        }
-    }
-    if (blockIdx.y == 0) {
-        tg = warp_sum(tg);
-        th = warp_sum(th);
-        if ((threadIdx.x & 31) == 0) {
-            s_tot[0][threadIdx.x >> 5] = tg;
-            s_tot[1][threadIdx.x >> 5] = th;
-        }
-    }
-    __syncthreads();
-    long long *dst = stage_hist + (int64_t)tk.stage * slot_words_for(nf);
-    if (blockIdx.y == 0 && threadIdx.x < 2) {
-        long long tot = 0;
-        for (int w2 = 0; w2 < kHistThreads / 32; w2++) tot += s_tot[threadIdx.x][w2];
-        long long *o = dst + (int64_t)nf * kBins * kWords + 2 * threadIdx.x;
-        if (single) {
-            o[0] = tot >> 32;
-            o[1] = tot & 0xffffffffll;
-        } else if (tot) {
-            atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(tot >> 32));
-            atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(tot & 0xffffffffll));
-        }
-    }
-    for (int idx = threadIdx.x; idx < kBlk * kBins; idx += blockDim.x) {
-        int k = idx >> 8, b = idx & 255;
-        int jj = fpos[blk * kBlk + k];
-        if (jj < 0) continue;
-        long long gv = ((long long)(int)acc[2 * kBlk * kBins + idx] << (2 * kDig)) +
-                       ((long long)acc[1 * kBlk * kBins + idx] << kDig) + (long long)acc[idx];
-        long long hv = ((long long)(int)acc[5 * kBlk * kBins + idx] << (2 * kDig)) +
-                       ((long long)acc[4 * kBlk * kBins + idx] << kDig) +
-                       (long long)acc[3 * kBlk * kBins + idx];
-        long long *o = dst + ((int64_t)jj * kBins + b) * kWords;
-        if (single) {
-            reinterpret_cast<longlong2 *>(o)[0] = make_longlong2(gv >> 32, gv & 0xffffffffll);
-            reinterpret_cast<longlong2 *>(o)[1] = make_longlong2(hv >> 32, hv & 0xffffffffll);
-        } else {
-            if (gv) {
-                atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(gv >> 32));
-                atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(gv & 0xffffffffll));
-            }
-            if (hv) {
-                atomicAdd((unsigned long long *)(o + 2), (unsigned long long)(hv >> 32));
-                atomicAdd((unsigned long long *)(o + 3), (unsigned long long)(hv & 0xffffffffll));
-            }
+            k = pe;
         }
     }
 }
 
-// Zero the staging histograms of tasks that span several CTAs (their CTAs
-// add atomically) or none (an empty side); single-chunk tasks store every
-// word themselves.
-__global__ void k_zero_multi(const int32_t *__restrict__ prefix, const int *__restrict__ ntask_p,
-                             long long *__restrict__ stage, int64_t words) {
-    int t = blockIdx.y;
-    if (t >= *ntask_p) return;
-    if (prefix[t + 1] - prefix[t] == 1) return;
-    long long *p = stage + (int64_t)t * words;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < words;
-         i += (int64_t)gridDim.x * blockDim.x)
-        p[i] = 0;
+// Zero, in the staging histograms, every feature (and the totals, which go
+// with block 0) whose (block, task) segment is not stored whole by one CTA:
+// those are added atomically, and a task with no rows is read as zeros.
+// grid: x = feature position (nf = the totals), y = task.
+__global__ void k_zero_stage(const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
+                             const int *__restrict__ ntask_p, const int32_t *__restrict__ bwp, int nb,
+                             const int16_t *__restrict__ fbi, int nf, int G, long long *__restrict__ stage) {
+    const int t = blockIdx.y, jj = blockIdx.x;
+    const int ntask = *ntask_p;
+    if (t >= ntask) return;
+    const long long R = rpre[ntask];
+    const long long T = (long long)bwp[nb] * R;
+    const int bi = jj < nf ? fbi[jj] : 0;
+    const long long rows = rpre[t + 1] - rpre[t];
+    if (T > 0) {
+        const int w = bwp[bi + 1] - bwp[bi];
+        const long long first = (long long)bwp[bi] * R + (long long)rpre[t] * w;
+        if (segment_single(rows, first, w, T, G)) return;
+    }
+    long long *p = stage + (int64_t)tasks[t].stage * slot_words_for(nf);
+    if (jj < nf) {
+        p += (int64_t)jj * kBins * kWords;
+        for (int i = threadIdx.x; i < kBins * kWords; i += blockDim.x) p[i] = 0;
+    } else if (threadIdx.x < kTotWords) {
+        p[(int64_t)nf * kBins * kWords + threadIdx.x] = 0;
+    }
 }
 
 // ===========================================================================
@@ -450,7 +507,7 @@ __device__ __forceinline__ DNode fresh_node(int depth, int parent) {
 // Root: node 0 holds all in-bag rows; one histogram task over them.
 __global__ void k_root_plan(const int32_t *__restrict__ n_local, const long long *__restrict__ n_global,
                             DNode *__restrict__ nodes, HistTask *__restrict__ ht,
-                            int32_t *__restrict__ prefix, int *__restrict__ node_count, int chunk) {
+                            int32_t *__restrict__ prefix, int *__restrict__ node_count) {
     if (threadIdx.x || blockIdx.x) return;
     long long ns = *n_local;
     DNode d = fresh_node(0, -1);
@@ -465,7 +522,7 @@ __global__ void k_root_plan(const int32_t *__restrict__ n_local, const long long
     t.left_small = 1;
     ht[0] = t;
     prefix[0] = 0;
-    prefix[1] = (int32_t)((ns + chunk - 1) / chunk);
+    prefix[1] = (int32_t)ns;
     *node_count = 1;
 }
 
@@ -635,7 +692,7 @@ __global__ void k_part_copyback(const PartTask *__restrict__ tasks, const int *_
 __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ lvl,
                             const int *__restrict__ lvl_count, const long long *__restrict__ nl_local,
                             const long long *__restrict__ gl, HistTask *__restrict__ ht,
-                            int32_t *__restrict__ prefix, int chunk) {
+                            int32_t *__restrict__ prefix) {
     __shared__ int s_w[32];
     const int W = *lvl_count;
     int carry = 0;
@@ -653,7 +710,7 @@ __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ l
             t.stage = k;
             t.left_small = ls ? 1 : 0;
             ht[k] = t;
-            ch = (int)((t.end - t.begin + chunk - 1) / chunk);
+            ch = (int)(t.end - t.begin);
             p.nl = nl;
             p.gnl = gnl;
             p.left_small = t.left_small;
@@ -672,6 +729,88 @@ __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ l
         carry += tot;
     }
     if (threadIdx.x == 0) prefix[W] = carry;
+}
+
+// Last level (every child at max_depth, where no node splits, E:775-777):
+// the children need only their row counts and exact (G, H) -- no partition,
+// no histogram, no split search.  Per parent task: [gL hi lo, hL hi lo, gR hi
+// lo, hR hi lo, nL] int64 words, summed exactly over CTAs (and ranks).
+constexpr int kLeafWords = 9;
+
+__global__ void __launch_bounds__(kPartThreads)
+k_leaf_totals(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows,
+              const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
+              const int *__restrict__ tiles_total, const longlong2 *__restrict__ q,
+              long long *__restrict__ words, long long *__restrict__ n_left) {
+    __shared__ long long s[5][kPartThreads / 32];
+    const int tile = blockIdx.x;
+    if (tile >= *tiles_total) return;
+    const int t = find_task_by_tile(tasks, *ntask_p, tile);
+    const PartTask tk = tasks[t];
+    const long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
+    const long long r1 = min(r0 + kPartTile, tk.end);
+    long long v[5] = {0, 0, 0, 0, 0};   // gL hL gR hR nL; |sum| < 4096 * 2^48
+    for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+        const int row = rows[r];
+        const longlong2 qq = __ldg(q + row);
+        const bool left = bin_of(xb, n, row, tk.feat) <= tk.thr;
+        v[left ? 0 : 2] += qq.x;
+        v[left ? 1 : 3] += qq.y;
+        v[4] += left;
+    }
+#pragma unroll
+    for (int k = 0; k < 5; k++) {
+        long long x = warp_sum(v[k]);
+        if ((threadIdx.x & 31) == 0) s[k][threadIdx.x >> 5] = x;
+    }
+    __syncthreads();
+    if (threadIdx.x < 5) {
+        long long tot = 0;
+        for (int w = 0; w < kPartThreads / 32; w++) tot += s[threadIdx.x][w];
+        long long *o = words + (int64_t)t * kLeafWords;
+        if (threadIdx.x < 4) {
+            if (tot) {
+                atomicAdd((unsigned long long *)(o + 2 * threadIdx.x), (unsigned long long)(tot >> 32));
+                atomicAdd((unsigned long long *)(o + 2 * threadIdx.x + 1), (unsigned long long)(tot & 0xffffffffll));
+            }
+        } else if (tot) {
+            atomicAdd((unsigned long long *)(o + 8), (unsigned long long)tot);
+            atomicAdd((unsigned long long *)(n_left + t), (unsigned long long)tot);
+        }
+    }
+}
+
+// The last level's children from those sums (the same rounding as every
+// other node: exact integer total -> float64 -> * 2^-S).
+__global__ void k_leaf_finish(DNode *__restrict__ nodes, const int *__restrict__ lvl,
+                              const int *__restrict__ lvl_count, const long long *__restrict__ words,
+                              const long long *__restrict__ nl_local, int S) {
+    const int W = *lvl_count;
+    const double sc = pow2(-S);
+    for (int k = threadIdx.x; k < W; k += blockDim.x) {
+        const long long *o = words + (int64_t)k * kLeafWords;
+        DNode &p = nodes[lvl[k]];
+        const long long nl = nl_local[k], gnl = o[8];
+        DNode &a = nodes[p.kid0];
+        DNode &c = nodes[p.kid1];
+        a.begin = p.begin;
+        a.end = p.begin + nl;
+        a.n = gnl;
+        c.begin = p.begin + nl;
+        c.end = p.end;
+        c.n = p.n - gnl;
+        a.G = __dmul_rn(i128_to_double(cell(o[0], o[1])), sc);
+        a.H = __dmul_rn(i128_to_double(cell(o[2], o[3])), sc);
+        c.G = __dmul_rn(i128_to_double(cell(o[4], o[5])), sc);
+        c.H = __dmul_rn(i128_to_double(cell(o[6], o[7])), sc);
+        a.feat = c.feat = -1;
+        a.bin = c.bin = 0;
+        a.gain = c.gain = -1.0;
+        p.nl = nl;
+        p.gnl = gnl;
+        p.left_small = gnl <= p.n - gnl;
+        p.expanded = 1;
+    }
 }
 
 // ===========================================================================
@@ -921,33 +1060,41 @@ __global__ void k_next_level(const DNode *__restrict__ nodes, const int *__restr
 
 // The fields of a grown node the replay reads, cached in shared memory.
 struct RNode {
-    double G, H, gain;
+    double val, H, gain;    // leaf value -G/(H+lambda) (E:640, E:708-709), hessian sum, best gain
     long long n, local;     // rows over all ranks / on this rank
-    int feat, bin, kid0, kid1, expanded, pad;
+    int feat, bin, kid0, kid1, expanded, depth;
 };
 
-__device__ void load_rnodes(const DNode *__restrict__ nodes, int cnt, RNode *sn) {
+__device__ void load_rnodes(const DNode *__restrict__ nodes, int cnt, RNode *sn, double lam) {
     for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
         const DNode &d = nodes[i];
         RNode r;
-        r.G = d.G; r.H = d.H; r.gain = d.gain; r.n = d.n; r.local = d.end - d.begin;
-        r.feat = d.feat; r.bin = d.bin; r.kid0 = d.kid0; r.kid1 = d.kid1; r.expanded = d.expanded; r.pad = 0;
+        r.val = __ddiv_rn(-d.G, __dadd_rn(d.H, lam));
+        r.H = d.H; r.gain = d.gain; r.n = d.n; r.local = d.end - d.begin;
+        r.feat = d.feat; r.bin = d.bin; r.kid0 = d.kid0; r.kid1 = d.kid1; r.expanded = d.expanded; r.depth = d.depth;
         sn[i] = r;
     }
     __syncwarp();
 }
 
 // The finished tree -> the F-update layout and the host copy.  Post-prune
-// (E:827-841) and the monotone clip (E:2461-2499) run on lane 0 first.
+// (E:827-841: a split over two leaves with gain < gamma becomes a leaf,
+// children first) and the monotone clip (E:2461-2499) run on lane 0; the
+// prune pass is skipped when no split has gain < gamma.
 __device__ void finish_tree(int nc, int *tf, int *tl, int *tr, long long *tt, double *tv, double *sg,
                             const RParams &P, const int *__restrict__ mono, TreeOut *__restrict__ out,
                             TreeDev *__restrict__ td, int status, long long root_rows, long long alg_rows) {
     const int lane = threadIdx.x & 31;
+    bool prune = false;
+    for (int k = lane; k < nc; k += 32) prune |= tf[k] != -1 && sg[k] < P.gamma;
+    prune = __any_sync(0xffffffffu, prune);
     if (lane == 0) {
-        for (int k = nc - 1; k >= 0; k--) {
-            if (tf[k] != -1) {
-                int l = tl[k], r = tr[k];
-                if (tf[l] == -1 && tf[r] == -1 && sg[k] < P.gamma) { tf[k] = -1; tl[k] = -1; tr[k] = -1; }
+        if (prune) {
+            for (int k = nc - 1; k >= 0; k--) {
+                if (tf[k] != -1) {
+                    int l = tl[k], r = tr[k];
+                    if (tf[l] == -1 && tf[r] == -1 && sg[k] < P.gamma) { tf[k] = -1; tl[k] = -1; tr[k] = -1; }
+                }
             }
         }
         if (P.has_mono) {
@@ -991,117 +1138,127 @@ __device__ void finish_tree(int nc, int *tf, int *tl, int *tr, long long *tt, do
     }
 }
 
-constexpr int kReplayMaxC = 130;    // candidate slots: max_leaves + 2 <= 129
+constexpr int kReplayMaxC = 160;    // candidate slots: max_leaves + 2 <= 129, 5 per lane
+
+// A double as an unsigned key with the same order.
+__device__ __forceinline__ unsigned long long order_key(double d) {
+    unsigned long long u = (unsigned long long)__double_as_longlong(d);
+    return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
+}
 
 // One warp replays the reference's best-first loop over the grown node
 // table: the candidate slots, the strict '>' scan where the lowest slot wins
 // among equal gains, min_samples_leaf on the partition, the node numbering
-// and the reuse of the lowest free slots (E:546-823).  Every control value is
-// computed identically by all lanes; lane 0 writes.  status 1: the loop
-// reached a node that was not expanded (the caller then replays on the host).
+// and the reuse of the two lowest free slots (E:546-823).  Slot s belongs to
+// lane s % 32, which keeps its key (the gain's order key when the slot is a
+// candidate with gain > gamma, else 0) in a register; the argmax is three
+// warp reductions.  status 1: the loop reached a node that was not expanded
+// (the caller then replays on the host).
 __global__ void __launch_bounds__(32)
 k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_count, RParams P,
               const int *__restrict__ mono, TreeOut *__restrict__ out, TreeDev *__restrict__ td) {
     extern __shared__ RNode sn[];
-    __shared__ int c_node[kReplayMaxC], c_nid[kReplayMaxC], c_depth[kReplayMaxC], c_feat[kReplayMaxC],
-        c_bin[kReplayMaxC], c_act[kReplayMaxC];
-    __shared__ double c_gain[kReplayMaxC], c_val[kReplayMaxC];
+    __shared__ int c_node[kReplayMaxC], c_nid[kReplayMaxC];
     __shared__ int tf[256], tl[256], tr[256];
     __shared__ long long tt[256];
     __shared__ double tv[256], sg[256];
     const int lane = threadIdx.x;
     const unsigned full = 0xffffffffu;
     const int MAXC = P.max_leaves + 2;
-    load_rnodes(nodes, *node_count, sn);
+    load_rnodes(nodes, *node_count, sn, P.lam);
     for (int k = lane; k < 256; k += 32) { tf[k] = -1; tl[k] = -1; tr[k] = -1; tt[k] = 0; tv[k] = 0.0; sg[k] = 0.0; }
-    for (int s = lane; s < kReplayMaxC; s += 32) { c_act[s] = 0; c_feat[s] = -1; c_gain[s] = -1.0; }
     __syncwarp();
     const RNode r0 = sn[0];
-    const double root_val = __ddiv_rn(-r0.G, __dadd_rn(r0.H, P.lam));
     long long alg = r0.local;
-    int nc = 1, status = 0;
     if (r0.n < P.msl || r0.H < P.mcw || r0.feat < 0) {          // E:575-579, E:634-638
-        if (lane == 0) tv[0] = root_val;
+        if (lane == 0) tv[0] = r0.val;
         __syncwarp();
-        finish_tree(nc, tf, tl, tr, tt, tv, sg, P, mono, out, td, 0, r0.local, alg);
+        finish_tree(1, tf, tl, tr, tt, tv, sg, P, mono, out, td, 0, r0.local, alg);
         return;
     }
+    auto cand_key = [&](const RNode &x) -> unsigned long long {
+        return (x.feat >= 0 && x.gain > P.gamma) ? order_key(x.gain) : 0ull;
+    };
+    unsigned long long key[5];
+    unsigned act = 0;                                            // bit r: slot lane + 32 r is active
+#pragma unroll
+    for (int r = 0; r < 5; r++) key[r] = 0ull;
     if (lane == 0) {
-        c_node[0] = 0; c_nid[0] = 0; c_depth[0] = 0; c_feat[0] = r0.feat; c_bin[0] = r0.bin;
-        c_gain[0] = r0.gain; c_val[0] = root_val; c_act[0] = 1;
+        c_node[0] = 0;
+        c_nid[0] = 0;
+        key[0] = cand_key(r0);
+        act = 1u;
     }
     __syncwarp();
-    int n_splits = 0;
+    int nc = 1, n_splits = 0, status = 0;
     while (n_splits < P.max_leaves - 1) {
-        int bs = -1;
-        double bg = 0.0;
-        for (int s = lane; s < MAXC; s += 32) {
-            if (c_act[s] && c_feat[s] >= 0 && c_gain[s] > P.gamma && (bs < 0 || c_gain[s] > bg)) {
-                bg = c_gain[s];
-                bs = s;
-            }
-        }
-        for (int o = 16; o > 0; o >>= 1) {
-            double og = __shfl_xor_sync(full, bg, o);
-            int os = __shfl_xor_sync(full, bs, o);
-            if (os >= 0 && (bs < 0 || og > bg || (og == bg && os < bs))) { bg = og; bs = os; }
-        }
-        if (bs < 0) break;
-        const int ci = bs;
+        unsigned long long bk = 0ull;
+        unsigned bs = 0xffffffffu;
+#pragma unroll
+        for (int r = 0; r < 5; r++)
+            if (key[r] > bk) { bk = key[r]; bs = (unsigned)(lane + 32 * r); }
+        const unsigned hi = __reduce_max_sync(full, (unsigned)(bk >> 32));
+        const unsigned lo = __reduce_max_sync(full, (unsigned)(bk >> 32) == hi ? (unsigned)bk : 0u);
+        if (hi == 0u && lo == 0u) break;
+        const int ci = (int)__reduce_min_sync(full, ((unsigned)(bk >> 32) == hi && (unsigned)bk == lo) ? bs : full);
         const int cur = c_node[ci];
         const RNode pn = sn[c_nid[ci]];
         if (!pn.expanded) { status = 1; break; }
         const long long gnl = sn[pn.kid0].n, gnr = sn[pn.kid1].n;
+        const int own = ci & 31, orr = ci >> 5;
         if (gnl < P.msl || gnr < P.msl) {                        // E:678-683
-            if (lane == 0) { tf[cur] = -1; tv[cur] = c_val[ci]; c_act[ci] = 0; }
+            if (lane == 0) { tf[cur] = -1; tv[cur] = pn.val; }
+#pragma unroll
+            for (int r = 0; r < 5; r++)
+                if (lane == own && r == orr) { key[r] = 0ull; act &= ~(1u << r); }
             __syncwarp();
             continue;
         }
         // the two lowest free slots other than ci (E:712-720)
         int ss = -1, sl = -1;
-        for (int base = 0; base < MAXC && sl < 0; base += 32) {
-            int s = base + lane;
-            unsigned m = __ballot_sync(full, s < MAXC && s != ci && !c_act[s]);
+#pragma unroll
+        for (int r = 0; r < 5; r++) {
+            const int s = lane + 32 * r;
+            unsigned m = __ballot_sync(full, s < MAXC && s != ci && !((act >> r) & 1u));
             while (m && sl < 0) {
-                int b = __ffs(m) - 1;
+                const int b = __ffs(m) - 1;
                 m &= m - 1;
-                if (ss < 0) ss = base + b; else sl = base + b;
+                if (ss < 0) ss = 32 * r + b; else sl = 32 * r + b;
             }
         }
-        if (ss < 0 || sl < 0) { status = 2; break; }   // cannot happen: >= 3 slots are free
+        if (ss < 0 || sl < 0) { status = 2; break; }            // cannot happen: >= 3 slots are free
         const int lid = nc, rid = nc + 1;
         nc += 2;
         n_splits++;
         const bool left_small = gnl <= gnr;
-        alg += left_small ? sn[pn.kid0].local : sn[pn.kid1].local;
-        const double cval = c_val[ci], cgain = c_gain[ci];
-        const int cfeat = c_feat[ci], cbin = c_bin[ci], cdepth = c_depth[ci];
-        __syncwarp();
-        if (lane < 2) {
-            // lane 0 fills the first free slot with the smaller child, lane 1
-            // the second with the larger one
-            const int pass = lane;
-            const int side = (pass == 0) == left_small ? 0 : 1;
-            const RNode kd = sn[side == 0 ? pn.kid0 : pn.kid1];
-            const int slot = pass == 0 ? ss : sl;
-            c_node[slot] = side == 0 ? lid : rid;
-            c_nid[slot] = side == 0 ? pn.kid0 : pn.kid1;
-            c_depth[slot] = cdepth + 1;
-            c_val[slot] = __ddiv_rn(-kd.G, __dadd_rn(kd.H, P.lam));
-            c_feat[slot] = kd.feat;
-            c_bin[slot] = kd.feat >= 0 ? kd.bin : 0;
-            c_gain[slot] = kd.feat >= 0 ? kd.gain : -1.0;
-            c_act[slot] = 1;
-            if (lane == 0) {
-                tf[cur] = cfeat; tt[cur] = cbin; tl[cur] = lid; tr[cur] = rid; tv[cur] = cval; sg[cur] = cgain;
-            }
+        const int kid_s = left_small ? pn.kid0 : pn.kid1, kid_l = left_small ? pn.kid1 : pn.kid0;
+        if (pn.depth + 1 < P.max_depth) alg += sn[kid_s].local;   // the last level builds no histogram
+        if (lane == 0) {
+            tf[cur] = pn.feat; tt[cur] = pn.bin; tl[cur] = lid; tr[cur] = rid; tv[cur] = pn.val; sg[cur] = pn.gain;
+            c_node[ss] = left_small ? lid : rid;
+            c_nid[ss] = kid_s;
+            c_node[sl] = left_small ? rid : lid;
+            c_nid[sl] = kid_l;
         }
-        if (lane == 0) c_act[ci] = 0;
+        const unsigned long long ks = cand_key(sn[kid_s]), kl = cand_key(sn[kid_l]);
+#pragma unroll
+        for (int r = 0; r < 5; r++) {
+            const int s = lane + 32 * r;
+            if (s == ci) { key[r] = 0ull; act &= ~(1u << r); }
+            if (s == ss) { key[r] = ks; act |= 1u << r; }
+            if (s == sl) { key[r] = kl; act |= 1u << r; }
+        }
         __syncwarp();
     }
-    if (!status && lane == 0) {
-        for (int s = 0; s < MAXC; s++)
-            if (c_act[s]) { tf[c_node[s]] = -1; tv[c_node[s]] = c_val[s]; }
+    if (!status) {
+#pragma unroll
+        for (int r = 0; r < 5; r++) {
+            if ((act >> r) & 1u) {
+                const int s = lane + 32 * r;
+                tf[c_node[s]] = -1;
+                tv[c_node[s]] = sn[c_nid[s]].val;
+            }
+        }
     }
     __syncwarp();
     finish_tree(nc, tf, tl, tr, tt, tv, sg, P, mono, out, td, status, r0.local, alg);
@@ -1119,7 +1276,7 @@ k_replay_depth(const DNode *__restrict__ nodes, const int *__restrict__ node_cou
     __shared__ int s_nc, s_status;
     __shared__ long long s_alg;
     const int lane = threadIdx.x;
-    load_rnodes(nodes, *node_count, sn);
+    load_rnodes(nodes, *node_count, sn, P.lam);
     for (int k = lane; k < 256; k += 32) { tf[k] = -1; tl[k] = -1; tr[k] = -1; tt[k] = 0; tv[k] = 0.0; sg[k] = 0.0; }
     __syncwarp();
     if (lane == 0) {
@@ -1130,14 +1287,14 @@ k_replay_depth(const DNode *__restrict__ nodes, const int *__restrict__ node_cou
             sp--;
             const RNode x = sn[st_nid[sp]];
             const int tid = st_tid[sp];
-            const double val = __ddiv_rn(-x.G, __dadd_rn(x.H, P.lam));
+            const double val = x.val;
             if (x.feat >= 0 && !x.expanded) status = 1;
             bool split = x.feat >= 0 && x.expanded && sn[x.kid0].n >= P.msl && sn[x.kid1].n >= P.msl &&
                          nc + 2 <= 256 && sp + 2 <= 64;
             if (!split) { tf[tid] = -1; tv[tid] = val; continue; }
             const int lid = nc++, rid = nc++;
             const long long gl = sn[x.kid0].n, gr = sn[x.kid1].n;
-            alg += gl <= gr ? sn[x.kid0].local : sn[x.kid1].local;
+            if (x.depth + 1 < P.max_depth) alg += gl <= gr ? sn[x.kid0].local : sn[x.kid1].local;
             tf[tid] = x.feat; tt[tid] = x.bin; tl[tid] = lid; tr[tid] = rid; tv[tid] = val; sg[tid] = x.gain;
             if (gl <= gr) {
                 st_nid[sp] = x.kid1; st_tid[sp] = rid; sp++;

@@ -285,3 +285,51 @@ def test_device_row_shuffle_at_scale(engine):
         _assert_tree_equal(a[r], t, f"round {r}")
     assert np.array_equal(engine.get_F(), Fa)
     s2.close()
+
+
+def _scale_data(n, p, seed):
+    """Bins like config 4's: quantile-uniform columns, few-level columns and a
+    NaN bin on 30 % of the rows of every third column."""
+    rng = np.random.default_rng(seed)
+    counts = np.empty(p, np.int32)
+    Xb = np.empty((n, p), np.uint8)
+    for j in range(p):
+        if j % 7 == 3:                                   # integer levels
+            lv = int(rng.integers(2, 12))
+            Xb[:, j] = rng.integers(0, lv, n)
+            counts[j] = lv
+        else:
+            Xb[:, j] = rng.integers(0, 255, n)
+            counts[j] = 256 if j % 3 == 0 else 255
+            if j % 3 == 0:
+                Xb[rng.random(n) < 0.3, j] = 255         # the NaN bin
+    logit = (Xb[:, 0].astype(np.float64) - 128) / 40 + (Xb[:, 3] == 1) - 1.5
+    y = (rng.random(n) < 1 / (1 + np.exp(-logit))).astype(np.uint8)
+    return Xb, counts, y
+
+
+@pytest.mark.parametrize("n,p,drop", [(600_000, 40, range(16, 32)), (250_000, 100, range(96, 100))])
+def test_rounds_match_oracle_exact_at_scale(engine, n, p, drop):
+    """Full-size launches (equal-work histogram CTAs spanning several nodes
+    and feature blocks, nodes over 16k rows, a feature block with no
+    selected feature) stay bit-exact with the oracle's EXACT builder."""
+    Xb, counts, y = _scale_data(n, p, seed=n)
+    w2 = O.class_weights(y, "balanced_sqrt")
+    base = O.base_score(y, w2)
+    engine.upload_bins(Xb, counts)
+    engine.upload_labels(y, w2, base, n_global=n)
+    kw = dict(max_leaves=63, max_depth=6, msl=5, mcw=3.0, lam=1.0, gamma=0.0)
+    prm = _params(lr=0.08, **kw)
+    rng = np.random.default_rng(7)
+    keep = np.array([j for j in range(p) if j not in set(drop)])
+    S = engine.scale_bits()
+    for r in range(2):
+        g, h = engine.get_grad()
+        smp = rng.choice(n, int(0.75 * n), replace=False)
+        mask = np.zeros(n, np.uint8)
+        mask[smp] = 1
+        feat = np.sort(rng.choice(keep, int(0.7 * len(keep)), replace=False)).astype(np.int32)
+        tree, _, _ = engine.round(mask, feat, prm, 128)
+        o = O.build_tree(Xb, g, h, smp, feat, counts, mode=O.MODE_EXACT, scale_bits=S, **kw)
+        O.post_prune(o[0], o[3], o[4], o[6], kw["gamma"], o[5])
+        _assert_tree_equal(tree, o, f"round {r}")
