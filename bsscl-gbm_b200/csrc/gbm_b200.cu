@@ -72,7 +72,8 @@ struct gbm_ctx {
 
     // round buffers
     uint8_t *d_mask = nullptr;
-    int32_t *d_rows = nullptr, *d_tmp = nullptr;
+    int32_t *d_rows = nullptr, *d_tmp = nullptr;   // the two row-list buffers (depth parity)
+    unsigned *d_side = nullptr;                    // partition side bits, per tile
     int32_t *d_cnt = nullptr, *d_off = nullptr, *d_total = nullptr;
     int32_t *d_blist = nullptr, *d_fidx = nullptr;
     int32_t *d_bwp = nullptr;          // histogram cost prefix over the active blocks
@@ -262,10 +263,11 @@ struct RoundFeat {
     std::vector<int16_t> fpos;
 };
 
-// Histogram cost of a row in an active block: its loads (about two
-// feature updates' worth) plus one unit per selected feature.
+// Histogram cost of a row in an active block: its loads and flush share
+// (about six feature updates' worth, measured on B200 by sweeping this
+// base) plus one unit per selected feature.
 int block_weight(const RoundFeat &rf, int blk) {
-    int w = 2;
+    int w = 6;
     for (int k = 0; k < kBlk; k++) w += rf.fpos[(size_t)blk * kBlk + k] >= 0;
     return w;
 }
@@ -355,6 +357,12 @@ constexpr int kReplaySmemMax = 160 * 1024;   // node table copy of the replay ke
 
 bool full_spec(const gbm_params *P) { return P->grow_policy == 1 || P->max_depth <= kSpecDepth; }
 
+// Children below this depth keep their histogram in the pool (a future
+// parent's).  Under full speculation the nodes at depth D-1 are expanded by
+// the last level, which needs no histogram; otherwise any node may still be
+// expanded on demand.
+int pool_depth(const gbm_params *P) { return full_spec(P) ? P->max_depth - 1 : 1 << 30; }
+
 int level_cap(const gbm_params *P) {
     if (P->grow_policy == 1) return 1 << std::min(P->max_depth - 1, 12);
     int m = std::max(1, P->max_leaves - 1);
@@ -432,7 +440,7 @@ int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int W_ub)
         ctx->hist_ev_used += 2;
         CK(cudaEventRecord(e0, ctx->st));
     }
-    k_hist<<<ctx->hist_grid, kHistThreads, smem, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_htask,
+    k_hist<<<ctx->hist_grid, kHistThreads, smem, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask,
                                                            ctx->d_hprefix, ntask_p, ctx->d_blist, d_bwp, nb,
                                                            ctx->d_fpos, ctx->d_skipb, rf.nf, ctx->d_q, ctx->d_stage);
     CKL();
@@ -496,11 +504,11 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
     TRY(launch_hist(ctx, rf, ints(ctx, I_ONE), 1));
     if (ctx->comm)
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words, ctx->st, ctx->timeout_ms, ctx->err));
-    int fx = (rf.nf + kSplitWarps - 1) / kSplitWarps;
+    int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
     k_split_feat<true><<<dim3(fx, 1), 32 * kSplitWarps, 0, ctx->st>>>(
         ctx->d_nodes, nullptr, nullptr, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx,
         ctx->d_counts, ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight,
-        (long long)P->min_samples_leaf, P->max_depth, ctx->d_fbest);
+        (long long)P->min_samples_leaf, P->max_depth, pool_depth(P), ctx->d_fbest);
     CKL();
     k_split_reduce<true><<<1, 32, 0, ctx->st>>>(ctx->d_nodes, nullptr, nullptr, ctx->d_pool, rf.nf, ctx->d_fidx,
                                                  ctx->d_fbest, ctx->S);
@@ -527,11 +535,13 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
         ctx->tile_cap = tiles_ub;
         TRY(dalloc(ctx, &ctx->d_tile_cnt, (size_t)ctx->tile_cap));
         TRY(dalloc(ctx, &ctx->d_tile_off, (size_t)ctx->tile_cap));
+        TRY(dalloc(ctx, &ctx->d_side, (size_t)ctx->tile_cap * kPartWords));
     }
     if (last) {   // children at max_depth: counts and totals only
         CK(cudaMemsetAsync(ctx->d_leafw, 0, sizeof(long long) * kLeafWords * W_ub, ctx->st));
         CK(cudaMemsetAsync(ctx->d_nleft, 0, sizeof(long long) * W_ub, ctx->st));
-        k_leaf_totals<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_ptask, lvl_cnt,
+        k_leaf_totals<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp,
+                                                              ctx->d_ptask, lvl_cnt,
                                                               ints(ctx, I_TILES), ctx->d_q, ctx->d_leafw,
                                                               ctx->d_nleft);
         CKL();
@@ -543,17 +553,14 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
         ctx->waves++;
         return GBM_OK;
     }
-    k_part_count<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_ptask, lvl_cnt,
-                                                         ints(ctx, I_TILES), ctx->d_tile_cnt);
+    k_part_count<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_ptask,
+                                                         lvl_cnt, ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt);
     CKL();
     k_part_scan<<<W_ub, 256, 0, ctx->st>>>(ctx->d_ptask, lvl_cnt, ctx->d_tile_cnt, ctx->d_tile_off, ctx->d_nleft);
     CKL();
-    k_part_scatter<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_ptask, lvl_cnt,
-                                                           ints(ctx, I_TILES), ctx->d_tile_off, ctx->d_nleft,
-                                                           ctx->d_tmp);
-    CKL();
-    k_part_copyback<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_ptask, lvl_cnt, ints(ctx, I_TILES), ctx->d_tmp,
-                                                            ctx->d_rows);
+    k_part_scatter<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_rows, ctx->d_tmp, ctx->d_ptask, lvl_cnt,
+                                                           ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_off,
+                                                           ctx->d_nleft);
     CKL();
     const long long *gl = ctx->d_nleft;
     if (ctx->comm) {
@@ -567,10 +574,10 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
     TRY(launch_hist(ctx, rf, lvl_cnt, W_ub));
     if (ctx->comm)
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words * W_ub, ctx->st, ctx->timeout_ms, ctx->err));
-    int fx = (rf.nf + kSplitWarps - 1) / kSplitWarps;
+    int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
     k_split_feat<false><<<dim3(fx, W_ub), 32 * kSplitWarps, 0, ctx->st>>>(
         ctx->d_nodes, lvl, lvl_cnt, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx, ctx->d_counts,
-        ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight, (long long)P->min_samples_leaf, P->max_depth,
+        ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight, (long long)P->min_samples_leaf, P->max_depth, pool_depth(P),
         ctx->d_fbest);
     CKL();
     k_split_reduce<false><<<2 * W_ub, 32, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ctx->d_pool, rf.nf, ctx->d_fidx,
@@ -941,10 +948,10 @@ int enqueue_replay(gbm_ctx *ctx, const gbm_params *P) {
     R.has_mono = P->monotone != nullptr;
     size_t smem = sizeof(RNode) * (size_t)ctx->nmax;
     if (P->grow_policy == 0)
-        k_replay_leaf<<<1, 32, smem, ctx->st>>>(ctx->d_nodes, ints(ctx, I_NODES), R, ctx->d_mono, ctx->d_tout,
+        k_replay_leaf<<<1, kReplayLoaders, smem, ctx->st>>>(ctx->d_nodes, ints(ctx, I_NODES), R, ctx->d_mono, ctx->d_tout,
                                                 ctx->d_tree);
     else
-        k_replay_depth<<<1, 32, smem, ctx->st>>>(ctx->d_nodes, ints(ctx, I_NODES), R, ctx->d_mono, ctx->d_tout,
+        k_replay_depth<<<1, kReplayLoaders, smem, ctx->st>>>(ctx->d_nodes, ints(ctx, I_NODES), R, ctx->d_mono, ctx->d_tout,
                                                  ctx->d_tree);
     CKL();
     return GBM_OK;
@@ -1171,7 +1178,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
                         ctx->d_count64, ctx->d_nodes, ctx->d_lvl[0], ctx->d_lvl[1], ctx->d_ints, ctx->d_tree,
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
                         ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,
-                        ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi};
+                        ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi, ctx->d_side};
     for (int32_t *q : ctx->d_perm) if (q) cudaFree(q);
     for (void *p : dev_ptrs) if (p) cudaFree(p);
     void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_mono};

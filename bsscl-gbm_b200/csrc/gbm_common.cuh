@@ -18,7 +18,8 @@ constexpr int kHistThreads = 512;
 constexpr int kDig = 17;            // low/mid digit width of the shared-memory accumulators
 constexpr int kAccWords = 6 * kBlk * kBins;   // [g0 g1 g2 h0 h1 h2][16][256] uint32
 constexpr int kPartTile = 4096;     // rows per partition CTA
-constexpr int kPartThreads = 256;
+constexpr int kPartThreads = 512;   // 8 rows per thread, loads in flight together
+constexpr int kPartWords = kPartTile / 32;   // side bits of a tile
 constexpr int kSplitWarps = 8;      // features per split CTA (one warp each)
 constexpr int kUpdThreads = 256;
 constexpr int kCompTile = 4096;     // rows per in-bag compaction CTA
@@ -48,16 +49,22 @@ struct DNode {
     int expanded;           // 1 once both children's results are final
 };
 
-struct HistTask {           // rows[begin, end) -> staging histogram `stage`
+// Row lists live in two buffers: the rows of a node at depth d are in
+// buffer d & 1, and a partition writes the children into the other one.
+struct HistTask {           // rows[buf][begin, end) -> staging histogram `stage`
     long long begin, end;
     int stage;
     int left_small;
+    int buf;
+    int pad;
 };
 
-struct PartTask {           // stable partition of rows[begin, end) on bin(feat) <= thr
+struct PartTask {           // stable partition of rows[src][begin, end) on bin(feat) <= thr
     long long begin, end;
     int feat, thr;
     int tile0, ntile;       // tiles of this task in the level's tile numbering
+    int src;                // the parent's buffer; the children go to 1 - src
+    int pad;
 };
 
 struct FBest {              // best bin of one feature for one node

@@ -311,8 +311,8 @@ __device__ __forceinline__ bool segment_single(long long rows, long long first_p
 // split kernel as node total - sum(other cells).  Block 0's pieces also sum
 // the node totals.  (E:582-596 root, E:723-737 smaller child.)
 __global__ void __launch_bounds__(kHistThreads, 2)
-k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows,
-       const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
+k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
+       const int32_t *__restrict__ rows1, const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
        const int *__restrict__ ntask_p, const int32_t *__restrict__ blist, const int32_t *__restrict__ bwp,
        int nb, const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
        const longlong2 *__restrict__ q, long long *__restrict__ stage_hist) {
@@ -361,13 +361,15 @@ k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ ro
             const int t0 = rpre[t], t1 = rpre[t + 1];
             if (t1 <= k) continue;
             const HistTask tk = tasks[t];
+            const int32_t *__restrict__ rows = tk.buf ? rows1 : rows0;
             const int pe = min(k1, t1);
             const bool single = k == t0 && pe == t1 && (t1 - t0) <= kChunk;
             long long *dst = stage_hist + (int64_t)tk.stage * slot_words;
             // the piece [k, pe) of task t, in runs of at most kChunk rows
             for (int c0 = k; c0 < pe; c0 += kChunk) {
                 const int c1 = min(pe, c0 + kChunk);
-                for (int i = threadIdx.x; i < kAccWords; i += blockDim.x) acc[i] = 0u;
+                for (int i = threadIdx.x; i < kAccWords / 4; i += blockDim.x)
+                    reinterpret_cast<uint4 *>(acc)[i] = make_uint4(0u, 0u, 0u, 0u);
                 __syncthreads();
                 const int r0 = (int)tk.begin + (c0 - t0), r1 = (int)tk.begin + (c1 - t0);
                 long long tg = 0, th = 0;
@@ -426,29 +428,20 @@ k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ ro
                         atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(tot & 0xffffffffll));
                     }
                 }
-                for (int idx = threadIdx.x; idx < kBlk * kBins; idx += blockDim.x) {
-                    int f = idx >> 8, b = idx & 255;
-                    int jj = fpos[blk * kBlk + f];
-                    if (jj < 0) continue;
-                    long long gv = ((long long)(int)acc[2 * kBlk * kBins + idx] << (2 * kDig)) +
-                                   ((long long)acc[1 * kBlk * kBins + idx] << kDig) + (long long)acc[idx];
-                    long long hv = ((long long)(int)acc[5 * kBlk * kBins + idx] << (2 * kDig)) +
-                                   ((long long)acc[4 * kBlk * kBins + idx] << kDig) +
-                                   (long long)acc[3 * kBlk * kBins + idx];
-                    long long *o = dst + ((int64_t)jj * kBins + b) * kWords;
-                    if (single) {
-                        reinterpret_cast<longlong2 *>(o)[0] = make_longlong2(gv >> 32, gv & 0xffffffffll);
-                        reinterpret_cast<longlong2 *>(o)[1] = make_longlong2(hv >> 32, hv & 0xffffffffll);
-                    } else {
-                        if (gv) {
-                            atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(gv >> 32));
-                            atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(gv & 0xffffffffll));
-                        }
-                        if (hv) {
-                            atomicAdd((unsigned long long *)(o + 2), (unsigned long long)(hv >> 32));
-                            atomicAdd((unsigned long long *)(o + 3), (unsigned long long)(hv & 0xffffffffll));
-                        }
-                    }
+                // flush: lane-consecutive words (g hi, g lo, h hi, h lo of consecutive
+                // cells), so a warp writes or adds 256 contiguous bytes at a time
+                for (int i = threadIdx.x; i < kBlk * kBins * kWords; i += blockDim.x) {
+                    const int idx = i >> 2, wd = i & 3;
+                    const int f = idx >> 8, b = idx & 255;
+                    if (!((mask >> f) & 1u)) continue;
+                    const int jj = fpos[blk * kBlk + f];
+                    const unsigned *dg0 = acc + (wd >> 1) * 3 * kBlk * kBins + idx;
+                    const long long v = ((long long)(int)dg0[2 * kBlk * kBins] << (2 * kDig)) +
+                                        ((long long)dg0[kBlk * kBins] << kDig) + (long long)dg0[0];
+                    const long long x = (wd & 1) ? (v & 0xffffffffll) : (v >> 32);
+                    long long *o = dst + ((int64_t)jj * kBins + b) * kWords + wd;
+                    if (single) *o = x;
+                    else if (x) atomicAdd((unsigned long long *)o, (unsigned long long)x);
                 }
                 __syncthreads();
             }
@@ -520,6 +513,8 @@ __global__ void k_root_plan(const int32_t *__restrict__ n_local, const long long
     t.end = ns;
     t.stage = 0;
     t.left_small = 1;
+    t.buf = 0;
+    t.pad = 0;
     ht[0] = t;
     prefix[0] = 0;
     prefix[1] = (int32_t)ns;
@@ -567,6 +562,8 @@ __global__ void k_lvl_plan(DNode *__restrict__ nodes, const int *__restrict__ lv
             t.thr = p.bin;
             t.tile0 = carry + e;
             t.ntile = nt;
+            t.src = p.depth & 1;
+            t.pad = 0;
             pt[k] = t;
             int c0 = base + 2 * k;
             p.kid0 = c0;
@@ -592,24 +589,40 @@ __device__ __forceinline__ int find_task_by_tile(const PartTask *tasks, int ntas
     return lo;
 }
 
-// Stable partition (E:663-674 decides the same sides; the row order inside
-// a side does not matter to exact sums): count, scan, scatter, copy back.
+// Stable partition (E:663-674 decides the same sides): a tile of kPartTile
+// rows per CTA, 8 rows per thread with their loads in flight together.
+// Count: each warp's ballots are the tile's side bits (1 = left); scan: the
+// tiles' left offsets within a task; scatter: ranks from the side bits, rows
+// into the other row buffer.
 __global__ void __launch_bounds__(kPartThreads)
-k_part_count(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows,
-             const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
-             const int *__restrict__ tiles_total, int32_t *__restrict__ tile_cnt) {
-    __shared__ int s[32];
-    int tile = blockIdx.x;
+k_part_count(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
+             const int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
+             const int *__restrict__ tiles_total, unsigned *__restrict__ side, int32_t *__restrict__ tile_cnt) {
+    __shared__ int s[kPartThreads / 32];
+    const int tile = blockIdx.x;
     if (tile >= *tiles_total) return;
-    int t = find_task_by_tile(tasks, *ntask_p, tile);
-    PartTask tk = tasks[t];
-    long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
-    long long r1 = min(r0 + kPartTile, tk.end);
-    int c = 0;
-    for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x)
-        c += bin_of(xb, n, rows[r], tk.feat) <= tk.thr;
-    c = warp_sum(c);
-    if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = c;
+    const int t = find_task_by_tile(tasks, *ntask_p, tile);
+    const PartTask tk = tasks[t];
+    const int32_t *__restrict__ rows = tk.src ? rows1 : rows0;
+    const long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
+    const int m = (int)min((long long)kPartTile, tk.end - r0);
+    constexpr int J = kPartTile / kPartThreads;
+    int rw[J];
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+        const int o = threadIdx.x + j * kPartThreads;
+        rw[j] = o < m ? rows[r0 + o] : -1;
+    }
+    int cnt = 0;
+    unsigned *sw = side + (int64_t)tile * kPartWords;
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+        const bool left = rw[j] >= 0 && bin_of(xb, n, rw[j], tk.feat) <= tk.thr;
+        const unsigned word = __ballot_sync(0xffffffffu, left);
+        if ((threadIdx.x & 31) == 0) sw[(threadIdx.x >> 5) + j * (kPartThreads / 32)] = word;
+        cnt += __popc(word);
+    }
+    if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = cnt;
     __syncthreads();
     if (threadIdx.x == 0) {
         int tot = 0;
@@ -637,58 +650,62 @@ __global__ void k_part_scan(const PartTask *__restrict__ tasks, const int *__res
     if (threadIdx.x == 0) n_left[blockIdx.x] = carry;
 }
 
+// Row o of a tile is bit (o & 31) of side word o >> 5; the word of rows
+// [32 i, 32 i + 32) was written by warp i % 16 of the count kernel.  Each
+// warp here ranks a run of 256 consecutive rows (8 words).
 __global__ void __launch_bounds__(kPartThreads)
-k_part_scatter(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows,
-               const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
-               const int *__restrict__ tiles_total, const int32_t *__restrict__ tile_off,
-               const long long *__restrict__ n_left, int32_t *__restrict__ tmp) {
-    __shared__ int s_w[32];
-    int tile = blockIdx.x;
+k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks,
+               const int *__restrict__ ntask_p, const int *__restrict__ tiles_total,
+               const unsigned *__restrict__ side, const int32_t *__restrict__ tile_off,
+               const long long *__restrict__ n_left) {
+    __shared__ int s_l[kPartThreads / 32];
+    const int tile = blockIdx.x;
     if (tile >= *tiles_total) return;
-    int t = find_task_by_tile(tasks, *ntask_p, tile);
-    PartTask tk = tasks[t];
-    long long tstart = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
-    long long r1 = min(tstart + kPartTile, tk.end);
-    long long nl = n_left[t];
-    long long lcar = tile_off[tile];                         // lefts before this tile
-    long long rcar = (tstart - tk.begin) - lcar;             // rights before this tile
-    for (long long r0 = tstart; r0 < r1; r0 += blockDim.x) {
-        long long r = r0 + threadIdx.x;
-        int row = 0, f = 0;
-        bool in = r < r1;
-        if (in) {
-            row = rows[r];
-            f = bin_of(xb, n, row, tk.feat) <= tk.thr;
+    const int t = find_task_by_tile(tasks, *ntask_p, tile);
+    const PartTask tk = tasks[t];
+    const int32_t *__restrict__ src = tk.src ? rows1 : rows0;
+    int32_t *__restrict__ dst = tk.src ? const_cast<int32_t *>(rows0) : rows1;
+    const long long tstart = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
+    const int m = (int)min((long long)kPartTile, tk.end - tstart);
+    const unsigned *sw = side + (int64_t)tile * kPartWords;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    constexpr int WPW = kPartWords / (kPartThreads / 32);   // side words per warp
+    unsigned wd[WPW];
+    int lw = 0;
+#pragma unroll
+    for (int j = 0; j < WPW; j++) {
+        wd[j] = sw[w * WPW + j];
+        lw += __popc(wd[j]);
+    }
+    if (lane == 0) s_l[w] = lw;
+    __syncthreads();
+    int lbase = 0;
+    for (int k = 0; k < w; k++) lbase += s_l[k];
+    const long long nl = n_left[t];
+    const long long lcar = tile_off[tile];                   // lefts before this tile
+    const long long rcar = (tstart - tk.begin) - lcar;       // rights before this tile
+    long long lpos = tk.begin + lcar + lbase;
+    long long rpos = tk.begin + nl + rcar + (long long)(w * WPW * 32 - lbase);
+    const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+    for (int j = 0; j < WPW; j++) {
+        const int o = (w * WPW + j) * 32 + lane;
+        const unsigned word = wd[j];
+        const bool left = (word >> lane) & 1u;
+        const int nvalid = max(0, min(32, m - (w * WPW + j) * 32));
+        if (o < m) {
+            const int row = src[tstart + o];
+            if (left) dst[lpos + __popc(word & lt)] = row;
+            else dst[rpos + (lane - __popc(word & lt))] = row;
         }
-        int tot;
-        int e = block_excl_scan(f, s_w, tot);
-        if (in) {
-            int pos_in_chunk = (int)(r - r0);
-            if (f) tmp[tk.begin + lcar + e] = row;
-            else tmp[tk.begin + nl + rcar + (pos_in_chunk - e)] = row;
-        }
-        int cnt = (int)min((long long)blockDim.x, r1 - r0);
-        lcar += tot;
-        rcar += cnt - tot;
+        const int nlw = __popc(word);
+        lpos += nlw;
+        rpos += nvalid - nlw;
     }
 }
 
-__global__ void k_part_copyback(const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
-                                const int *__restrict__ tiles_total, const int32_t *__restrict__ tmp,
-                                int32_t *__restrict__ rows) {
-    int tile = blockIdx.x;
-    if (tile >= *tiles_total) return;
-    int t = find_task_by_tile(tasks, *ntask_p, tile);
-    PartTask tk = tasks[t];
-    long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
-    long long r1 = min(r0 + kPartTile, tk.end);
-    for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x) rows[r] = tmp[r];
-}
-
-// After the partition: children's row ranges and global counts; the
-// globally smaller side (E:701-709, n_left <= n_right -> left) becomes the
-// histogram task of staging slot k.  `gl` are the left counts summed over
-// ranks (== nl on one GPU).
+// Level plan after the partition: each parent's smaller child (by global
+// count) becomes a histogram task; the children get their row ranges.
 __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ lvl,
                             const int *__restrict__ lvl_count, const long long *__restrict__ nl_local,
                             const long long *__restrict__ gl, HistTask *__restrict__ ht,
@@ -709,6 +726,8 @@ __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ l
             t.end = ls ? p.begin + nl : p.end;
             t.stage = k;
             t.left_small = ls ? 1 : 0;
+            t.buf = (p.depth + 1) & 1;
+            t.pad = 0;
             ht[k] = t;
             ch = (int)(t.end - t.begin);
             p.nl = nl;
@@ -738,8 +757,8 @@ __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ l
 constexpr int kLeafWords = 9;
 
 __global__ void __launch_bounds__(kPartThreads)
-k_leaf_totals(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows,
-              const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
+k_leaf_totals(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
+              const int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
               const int *__restrict__ tiles_total, const longlong2 *__restrict__ q,
               long long *__restrict__ words, long long *__restrict__ n_left) {
     __shared__ long long s[5][kPartThreads / 32];
@@ -747,13 +766,22 @@ k_leaf_totals(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restri
     if (tile >= *tiles_total) return;
     const int t = find_task_by_tile(tasks, *ntask_p, tile);
     const PartTask tk = tasks[t];
+    const int32_t *__restrict__ rows = tk.src ? rows1 : rows0;
     const long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
-    const long long r1 = min(r0 + kPartTile, tk.end);
+    const int m = (int)min((long long)kPartTile, tk.end - r0);
+    constexpr int J = kPartTile / kPartThreads;
+    int rw[J];
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+        const int o = threadIdx.x + j * kPartThreads;
+        rw[j] = o < m ? rows[r0 + o] : -1;
+    }
     long long v[5] = {0, 0, 0, 0, 0};   // gL hL gR hR nL; |sum| < 4096 * 2^48
-    for (long long r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
-        const int row = rows[r];
-        const longlong2 qq = __ldg(q + row);
-        const bool left = bin_of(xb, n, row, tk.feat) <= tk.thr;
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+        if (rw[j] < 0) continue;
+        const longlong2 qq = __ldg(q + rw[j]);
+        const bool left = bin_of(xb, n, rw[j], tk.feat) <= tk.thr;
         v[left ? 0 : 2] += qq.x;
         v[left ? 1 : 3] += qq.y;
         v[4] += left;
@@ -817,41 +845,39 @@ __global__ void k_leaf_finish(DNode *__restrict__ nodes, const int *__restrict__
 // split search
 // ===========================================================================
 
-// Best bin of feature position jj for one node whose cells start at `hf`
-// (256 cells x 4 words) with exact totals (TG, TH).  The reference's scan
-// (E:602-621, E:780-801): bins 0..nb-2 as a running prefix, HL<mcw or
-// HR<mcw skipped, gain = GL^2/(HL+l) + GR^2/(HR+l) - G^2/(H+l), first
-// maximum wins.  Every operation rounds separately, as in the reference.
-__device__ __forceinline__ void feature_best(const long long *__restrict__ hf, i128 TG, i128 TH, int nb,
-                                             int sb, int S, double lam, double mcw, double parent,
-                                             double &best_gain, int &best_bin) {
+// Best bin of one feature for one node with exact totals (TG, TH): the
+// reference's scan (E:602-621, E:780-801): bins 0..nb-2 as a running
+// prefix, HL<mcw or HR<mcw skipped, gain = GL^2/(HL+l) + GR^2/(HR+l) -
+// G^2/(H+l), first maximum wins.  Every operation rounds separately, as in
+// the reference.  Lane l owns bins 8l .. 8l+7, whose exact sums come in
+// g[], h[]; the skipped bin sb holds node total - all other cells.
+__device__ __forceinline__ void feature_best(i128 (&g)[8], i128 (&h)[8], i128 TG, i128 TH, int nb, int sb,
+                                             int S, double lam, double mcw, double parent, double &best_gain,
+                                             int &best_bin) {
     const int lane = threadIdx.x & 31;
     const double sc = pow2(-S);
-    i128 g[8], h[8];
     i128 lg = 0, lh = 0;
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-        const longlong2 *c = reinterpret_cast<const longlong2 *>(hf + (int64_t)(lane * 8 + k) * kWords);
-        longlong2 a = c[0], b = c[1];
-        g[k] = cell(a.x, a.y);
-        h[k] = cell(b.x, b.y);
         lg += g[k];
         lh += h[k];
     }
-    // the skipped bin holds node total - all other cells
     i128 ag = lg, ah = lh;
     for (int o = 16; o > 0; o >>= 1) {
         ag += shfl_xor_i128(ag, o);
         ah += shfl_xor_i128(ah, o);
     }
+    const i128 fg = TG - ag, fh = TH - ah;   // the skipped bin's cell
     if ((sb >> 3) == lane) {
 #pragma unroll
-        for (int k = 0; k < 8; k++)
-            if ((sb & 7) == k) { g[k] += TG - ag; h[k] += TH - ah; }
-        lg += TG - ag;
-        lh += TH - ah;
+        for (int k = 0; k < 8; k++) {
+            const bool hit = (sb & 7) == k;
+            g[k] += hit ? fg : (i128)0;
+            h[k] += hit ? fh : (i128)0;
+        }
+        lg += fg;
+        lh += fh;
     }
-    // exclusive prefix of the lane sums
     i128 xg = lg, xh = lh;
     for (int o = 1; o < 32; o <<= 1) {
         i128 tg2 = shfl_up_i128(xg, o), th2 = shfl_up_i128(xh, o);
@@ -862,7 +888,7 @@ __device__ __forceinline__ void feature_best(const long long *__restrict__ hf, i
     int bb = -1;
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-        int b = lane * 8 + k;
+        const int b = lane * 8 + k;
         pg += g[k];
         ph += h[k];
         if (b <= nb - 2) {
@@ -889,86 +915,97 @@ __device__ __forceinline__ void feature_best(const long long *__restrict__ hf, i
     best_bin = bb;
 }
 
-// One warp per (parent k, feature position jj): the smaller child's cells
-// come from staging slot k, the larger child's are parent - smaller
-// (E:740-745, exact); both are written to the children's pool slots, and
-// both children's best bins for feature jj are found.  ROOT: node 0 from
-// staging slot 0.  fbest[(2k + side) * nf + jj], side 0 = left child.
+// One warp per (parent k, feature position jj, child side): the smaller
+// child's cells come from staging slot k, the larger child's are parent -
+// smaller (E:740-745, exact).  Each warp writes its child's pool slot (the
+// child's histogram as a future parent; the cells are skipped when that
+// child's children are handled without histograms) and finds its best bin
+// for feature jj.
+// ROOT: node 0 from staging slot 0.  fbest[(2k + side) * nf + jj], side 0 =
+// left child.
+constexpr int kSplitFeatPerCta = kSplitWarps / 2;
+
 template <bool ROOT>
 __global__ void __launch_bounds__(32 * kSplitWarps)
 k_split_feat(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const int *__restrict__ lvl_count,
              const HistTask *__restrict__ ht, const long long *__restrict__ stage, long long *__restrict__ pool,
              int nf, const int32_t *__restrict__ fidx, const int32_t *__restrict__ counts,
              const int16_t *__restrict__ skipb, int S, double lam, double mcw, long long msl, int max_depth,
-             FBest *__restrict__ fbest) {
+             int pool_depth, FBest *__restrict__ fbest) {
     const int k = blockIdx.y;
     if (!ROOT && k >= *lvl_count) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int jj = blockIdx.x * kSplitWarps + warp;
+    const int side = ROOT ? 0 : (warp & 1);
+    if (ROOT && (warp & 1)) return;
+    const int jj = blockIdx.x * kSplitFeatPerCta + (warp >> 1);
     if (jj >= nf) return;
     const int64_t words = slot_words_for(nf);
     const long long *st = stage + (int64_t)k * words;
-    int parent = -1, small = 0, large = -1, c0 = 0, c1 = -1;
+    int ch = 0, parent = -1;
+    bool is_small = true;
     if (!ROOT) {
         parent = lvl[k];
-        c0 = nodes[parent].kid0;
-        c1 = nodes[parent].kid1;
-        bool ls = ht[k].left_small != 0;
-        small = ls ? c0 : c1;
-        large = ls ? c1 : c0;
+        const DNode &pn = nodes[parent];
+        ch = side == 0 ? pn.kid0 : pn.kid1;
+        is_small = (ht[k].left_small != 0) == (side == 0);
     }
+    const DNode nd = nodes[ch];
     const long long *st_tot = st + (int64_t)nf * kBins * kWords;
-    const i128 TGs = cell(st_tot[0], st_tot[1]), THs = cell(st_tot[2], st_tot[3]);
-    i128 TGl = 0, THl = 0;
     const long long *par = ROOT ? nullptr : pool + (int64_t)parent * words;
-    long long *ps = pool + (int64_t)small * words;
-    long long *pl = ROOT ? nullptr : pool + (int64_t)large * words;
-    if (!ROOT) {
+    i128 TG, TH;
+    if (is_small) {
+        TG = cell(st_tot[0], st_tot[1]);
+        TH = cell(st_tot[2], st_tot[3]);
+    } else {
         const long long *pt = par + (int64_t)nf * kBins * kWords;
-        TGl = cell(pt[0] - st_tot[0], pt[1] - st_tot[1]);
-        THl = cell(pt[2] - st_tot[2], pt[3] - st_tot[3]);
+        TG = cell(pt[0] - st_tot[0], pt[1] - st_tot[1]);
+        TH = cell(pt[2] - st_tot[2], pt[3] - st_tot[3]);
     }
+    long long *pc = pool + (int64_t)ch * words;
+    const bool write_pool = nd.depth < pool_depth;   // the cells; the totals always (k_split_reduce)
     if (jj == 0 && lane < kTotWords) {
         const int64_t o = (int64_t)nf * kBins * kWords + lane;
-        ps[o] = st_tot[lane];
-        if (!ROOT) pl[o] = par[o] - st_tot[lane];
+        pc[o] = is_small ? st_tot[lane] : par[o] - st_tot[lane];
     }
     // cells of feature jj: lane owns bins 8*lane .. 8*lane+7 (32 words)
     const int64_t base = (int64_t)jj * kBins * kWords + (int64_t)lane * 8 * kWords;
+    i128 g[8], h[8];
 #pragma unroll
-    for (int v = 0; v < 8 * kWords; v += 2) {
-        longlong2 s = *reinterpret_cast<const longlong2 *>(st + base + v);
-        *reinterpret_cast<longlong2 *>(ps + base + v) = s;
-        if (!ROOT) {
-            longlong2 p = *reinterpret_cast<const longlong2 *>(par + base + v);
-            *reinterpret_cast<longlong2 *>(pl + base + v) = make_longlong2(p.x - s.x, p.y - s.y);
+    for (int b = 0; b < 8; b++) {
+        const longlong2 *sp = reinterpret_cast<const longlong2 *>(st + base + b * kWords);
+        longlong2 a = sp[0], d = sp[1];
+        if (!is_small) {
+            const longlong2 *pp = reinterpret_cast<const longlong2 *>(par + base + b * kWords);
+            const longlong2 pa = pp[0], pd = pp[1];
+            a = make_longlong2(pa.x - a.x, pa.y - a.y);
+            d = make_longlong2(pd.x - d.x, pd.y - d.y);
         }
+        if (write_pool) {
+            longlong2 *op = reinterpret_cast<longlong2 *>(pc + base + b * kWords);
+            op[0] = a;
+            op[1] = d;
+        }
+        g[b] = cell(a.x, a.y);
+        h[b] = cell(d.x, d.y);
     }
     const int f = fidx[jj];
     const int nb = counts[f];
     const int sb = skipb[f];
     const double sc = pow2(-S);
-    for (int side = 0; side < (ROOT ? 1 : 2); side++) {
-        const bool is_small = ROOT || (side == 0) == (small == c0);
-        const int ch = ROOT ? 0 : (side == 0 ? c0 : c1);
-        const i128 TG = is_small ? TGs : TGl, TH = is_small ? THs : THl;
-        const long long *cells = (is_small ? ps : pl) + (int64_t)jj * kBins * kWords;
-        const double Gd = __dmul_rn(i128_to_double(TG), sc), Hd = __dmul_rn(i128_to_double(TH), sc);
-        const DNode nd = nodes[ch];
-        const bool eval = nd.depth < max_depth && nd.n >= msl && Hd >= mcw && nb >= 2;
-        double bg = -1e9;
-        int bb = -1;
-        if (eval) {
-            double parent_term = __ddiv_rn(__dmul_rn(Gd, Gd), __dadd_rn(Hd, lam));
-            feature_best(cells, TG, TH, nb, sb, S, lam, mcw, parent_term, bg, bb);
-        }
-        if (lane == 0) {
-            FBest o;
-            o.gain = bg;
-            o.bin = bb < 0 ? 0 : bb;
-            o.valid = bb >= 0 ? 1 : 0;
-            fbest[(int64_t)(2 * k + side) * nf + jj] = o;
-        }
+    const double Gd = __dmul_rn(i128_to_double(TG), sc), Hd = __dmul_rn(i128_to_double(TH), sc);
+    const bool eval = nd.depth < max_depth && nd.n >= msl && Hd >= mcw && nb >= 2;
+    double bg = -1e9;
+    int bb = -1;
+    if (eval) {
+        const double parent_term = __ddiv_rn(__dmul_rn(Gd, Gd), __dadd_rn(Hd, lam));
+        feature_best(g, h, TG, TH, nb, sb, S, lam, mcw, parent_term, bg, bb);
+    }
+    if (lane == 0) {
+        FBest o;
+        o.gain = bg;
+        o.bin = bb < 0 ? 0 : bb;
+        o.valid = bb >= 0 ? 1 : 0;
+        fbest[(int64_t)(2 * k + side) * nf + jj] = o;
     }
 }
 
@@ -1074,8 +1111,10 @@ __device__ void load_rnodes(const DNode *__restrict__ nodes, int cnt, RNode *sn,
         r.feat = d.feat; r.bin = d.bin; r.kid0 = d.kid0; r.kid1 = d.kid1; r.expanded = d.expanded; r.depth = d.depth;
         sn[i] = r;
     }
-    __syncwarp();
+    __syncthreads();
 }
+
+constexpr int kReplayLoaders = 256;   // threads that load the node table; warp 0 replays
 
 // The finished tree -> the F-update layout and the host copy.  Post-prune
 // (E:827-841: a split over two leaves with gain < gamma becomes a leaf,
@@ -1154,7 +1193,7 @@ __device__ __forceinline__ unsigned long long order_key(double d) {
 // candidate with gain > gamma, else 0) in a register; the argmax is three
 // warp reductions.  status 1: the loop reached a node that was not expanded
 // (the caller then replays on the host).
-__global__ void __launch_bounds__(32)
+__global__ void __launch_bounds__(kReplayLoaders)
 k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_count, RParams P,
               const int *__restrict__ mono, TreeOut *__restrict__ out, TreeDev *__restrict__ td) {
     extern __shared__ RNode sn[];
@@ -1162,10 +1201,11 @@ k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_coun
     __shared__ int tf[256], tl[256], tr[256];
     __shared__ long long tt[256];
     __shared__ double tv[256], sg[256];
+    load_rnodes(nodes, *node_count, sn, P.lam);
+    if (threadIdx.x >= 32) return;
     const int lane = threadIdx.x;
     const unsigned full = 0xffffffffu;
     const int MAXC = P.max_leaves + 2;
-    load_rnodes(nodes, *node_count, sn, P.lam);
     for (int k = lane; k < 256; k += 32) { tf[k] = -1; tl[k] = -1; tr[k] = -1; tt[k] = 0; tv[k] = 0.0; sg[k] = 0.0; }
     __syncwarp();
     const RNode r0 = sn[0];
@@ -1266,7 +1306,7 @@ k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_coun
 
 // Depth-wise growth's node numbering (E:233-508): a DFS stack where the
 // larger child is pushed first, so the smaller one is numbered first.
-__global__ void __launch_bounds__(32)
+__global__ void __launch_bounds__(kReplayLoaders)
 k_replay_depth(const DNode *__restrict__ nodes, const int *__restrict__ node_count, RParams P,
                const int *__restrict__ mono, TreeOut *__restrict__ out, TreeDev *__restrict__ td) {
     extern __shared__ RNode sn[];
@@ -1275,8 +1315,9 @@ k_replay_depth(const DNode *__restrict__ nodes, const int *__restrict__ node_cou
     __shared__ double tv[256], sg[256];
     __shared__ int s_nc, s_status;
     __shared__ long long s_alg;
-    const int lane = threadIdx.x;
     load_rnodes(nodes, *node_count, sn, P.lam);
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
     for (int k = lane; k < 256; k += 32) { tf[k] = -1; tl[k] = -1; tr[k] = -1; tt[k] = 0; tv[k] = 0.0; sg[k] = 0.0; }
     __syncwarp();
     if (lane == 0) {
