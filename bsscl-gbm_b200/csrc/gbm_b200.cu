@@ -88,7 +88,7 @@ struct gbm_ctx {
     HistTask *d_htask = nullptr;
     int32_t *d_hprefix = nullptr;
     PartTask *d_ptask = nullptr;
-    int32_t *d_tile_cnt = nullptr, *d_tile_off = nullptr;
+    int32_t *d_tile_cnt = nullptr;
     int tile_cap = 0;
     long long *d_nleft = nullptr, *d_nleft_g = nullptr, *d_count64 = nullptr;
     long long *d_leafw = nullptr;      // last level: per-parent count and (G, H) words
@@ -416,15 +416,13 @@ bool device_replay(const gbm_ctx *ctx, const gbm_params *P) {
 
 // ---- launches -----------------------------------------------------------------
 
-// Zero the staging cells that are added atomically, then the histograms of
-// the tasks at *ntask_p (at most W_ub) on ctx->hist_grid equal-work CTAs.
-int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int W_ub) {
+// The histograms of the tasks at *ntask_p on ctx->hist_grid equal-work CTAs.
+// The staging histograms are zero here: the split search zeroes the cells
+// it reads and the level close the totals.
+int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p) {
     const int nb = (int)rf.blist.size();
-    if (W_ub <= 0 || nb == 0) return GBM_OK;
+    if (nb == 0) return GBM_OK;
     const int32_t *d_bwp = ctx->d_blist + nb;
-    k_zero_stage<<<dim3((unsigned)rf.nf + 1, (unsigned)W_ub), 256, 0, ctx->st>>>(
-        ctx->d_htask, ctx->d_hprefix, ntask_p, d_bwp, nb, ctx->d_fbi, rf.nf, ctx->hist_grid, ctx->d_stage);
-    CKL();
     size_t smem = (size_t)kAccWords * sizeof(unsigned);
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (ctx->profiling) {
@@ -488,8 +486,34 @@ int flush_l2(gbm_ctx *ctx) {
 
 int *ints(gbm_ctx *ctx, int i) { return ctx->d_ints + i; }
 
-// Root: histogram of all in-bag rows, its split, and the first level list.
-int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
+// The next level a level-synchronous close plans: its list capacity, and
+// whether it is the last level (children at max_depth).
+struct NextPlan {
+    int W_ub = 0;       // 0: no plan (the caller plans, or there is no next level)
+    bool last = false;
+};
+
+int launch_close(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, bool root, const int *lvl,
+                 const int *lvl_cnt, int *next, int *next_cnt, const NextPlan &np) {
+    PartTask *pt = np.W_ub > 0 ? ctx->d_ptask : nullptr;
+    long long *lw = np.W_ub > 0 && np.last ? ctx->d_leafw : nullptr;
+    if (root)
+        k_level_close<true><<<1, kCloseThreads, 0, ctx->st>>>(
+            ctx->d_nodes, nullptr, nullptr, ctx->d_pool, ctx->d_stage, rf.nf, ctx->d_fidx, ctx->d_fbest, ctx->S, next,
+            next_cnt, ints(ctx, I_NODES), ctx->nmax, level_cap(P), P->gamma, P->grow_policy == 0, pt,
+            ints(ctx, I_TILES), np.W_ub, lw, ctx->d_nleft);
+    else
+        k_level_close<false><<<1, kCloseThreads, 0, ctx->st>>>(
+            ctx->d_nodes, lvl, lvl_cnt, ctx->d_pool, ctx->d_stage, rf.nf, ctx->d_fidx, ctx->d_fbest, ctx->S, next,
+            next_cnt, ints(ctx, I_NODES), ctx->nmax, level_cap(P), P->gamma, P->grow_policy == 0, pt,
+            ints(ctx, I_TILES), np.W_ub, lw, ctx->d_nleft);
+    CKL();
+    return GBM_OK;
+}
+
+// Root: histogram of all in-bag rows, its split, the first level list and
+// that level's plan.
+int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, const NextPlan &np) {
     const int64_t words = slot_words_for(rf.nf);
     const long long *ng = nullptr;
     if (ctx->comm) {
@@ -501,7 +525,7 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
     k_root_plan<<<1, 1, 0, ctx->st>>>(ctx->d_total, ng, ctx->d_nodes, ctx->d_htask, ctx->d_hprefix,
                                       ints(ctx, I_NODES));
     CKL();
-    TRY(launch_hist(ctx, rf, ints(ctx, I_ONE), 1));
+    TRY(launch_hist(ctx, rf, ints(ctx, I_ONE)));
     if (ctx->comm)
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words, ctx->st, ctx->timeout_ms, ctx->err));
     int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
@@ -510,36 +534,35 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
         ctx->d_counts, ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight,
         (long long)P->min_samples_leaf, P->max_depth, pool_depth(P), ctx->d_fbest);
     CKL();
-    k_split_reduce<true><<<1, 32, 0, ctx->st>>>(ctx->d_nodes, nullptr, nullptr, ctx->d_pool, rf.nf, ctx->d_fidx,
-                                                 ctx->d_fbest, ctx->S);
-    CKL();
-    k_next_level<true><<<1, 256, 0, ctx->st>>>(ctx->d_nodes, nullptr, nullptr, ctx->d_lvl[0], ints(ctx, I_LVL0),
-                                                ints(ctx, I_NODES), ctx->nmax, level_cap(P), P->gamma,
-                                                P->grow_policy == 0);
-    CKL();
-    return GBM_OK;
+    return launch_close(ctx, rf, P, true, nullptr, nullptr, ctx->d_lvl[0], ints(ctx, I_LVL0), np);
 }
 
 // Expand the parents in `lvl` (count at *lvl_cnt, at most W_ub): partition,
-// smaller-child histogram, subtraction, children's splits.  When `next` is
-// given, also rank the children into the next level list.
+// smaller-child histogram, subtraction, children's splits.  `planned`: the
+// previous close planned this level; otherwise (on-demand expansion) it is
+// planned here.  `last`: the children are at max_depth (counts and totals
+// only).  When `next` is given, the close ranks the children into the next
+// level list and, with np.W_ub > 0, plans that level.
 int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lvl, int *lvl_cnt,
-                 int *next, int *next_cnt, int W_ub, bool last = false) {
+                 int *next, int *next_cnt, int W_ub, bool last, bool planned, const NextPlan &np) {
     if (W_ub <= 0) return GBM_OK;
     const int64_t words = slot_words_for(rf.nf);
-    k_lvl_plan<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ints(ctx, I_NODES), ctx->d_ptask,
-                                       ints(ctx, I_TILES), ctx->nmax, W_ub);
-    CKL();
+    if (!planned) {
+        k_lvl_plan<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ints(ctx, I_NODES), ctx->d_ptask,
+                                           ints(ctx, I_TILES), ctx->nmax, W_ub);
+        CKL();
+    }
     int tiles_ub = (int)((ctx->n + kPartTile - 1) / kPartTile) + W_ub;
     if (tiles_ub > ctx->tile_cap) {
         ctx->tile_cap = tiles_ub;
         TRY(dalloc(ctx, &ctx->d_tile_cnt, (size_t)ctx->tile_cap));
-        TRY(dalloc(ctx, &ctx->d_tile_off, (size_t)ctx->tile_cap));
         TRY(dalloc(ctx, &ctx->d_side, (size_t)ctx->tile_cap * kPartWords));
     }
     if (last) {   // children at max_depth: counts and totals only
-        CK(cudaMemsetAsync(ctx->d_leafw, 0, sizeof(long long) * kLeafWords * W_ub, ctx->st));
-        CK(cudaMemsetAsync(ctx->d_nleft, 0, sizeof(long long) * W_ub, ctx->st));
+        if (!planned) {
+            CK(cudaMemsetAsync(ctx->d_leafw, 0, sizeof(long long) * kLeafWords * W_ub, ctx->st));
+            CK(cudaMemsetAsync(ctx->d_nleft, 0, sizeof(long long) * W_ub, ctx->st));
+        }
         k_leaf_totals<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp,
                                                               ctx->d_ptask, lvl_cnt,
                                                               ints(ctx, I_TILES), ctx->d_q, ctx->d_leafw,
@@ -556,10 +579,8 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
     k_part_count<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_ptask,
                                                          lvl_cnt, ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt);
     CKL();
-    k_part_scan<<<W_ub, 256, 0, ctx->st>>>(ctx->d_ptask, lvl_cnt, ctx->d_tile_cnt, ctx->d_tile_off, ctx->d_nleft);
-    CKL();
     k_part_scatter<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_rows, ctx->d_tmp, ctx->d_ptask, lvl_cnt,
-                                                           ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_off,
+                                                           ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt,
                                                            ctx->d_nleft);
     CKL();
     const long long *gl = ctx->d_nleft;
@@ -571,23 +592,16 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
     }
     k_plan_hist<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ctx->d_nleft, gl, ctx->d_htask, ctx->d_hprefix);
     CKL();
-    TRY(launch_hist(ctx, rf, lvl_cnt, W_ub));
+    TRY(launch_hist(ctx, rf, lvl_cnt));
     if (ctx->comm)
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words * W_ub, ctx->st, ctx->timeout_ms, ctx->err));
     int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
     k_split_feat<false><<<dim3(fx, W_ub), 32 * kSplitWarps, 0, ctx->st>>>(
         ctx->d_nodes, lvl, lvl_cnt, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx, ctx->d_counts,
-        ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight, (long long)P->min_samples_leaf, P->max_depth, pool_depth(P),
-        ctx->d_fbest);
+        ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight, (long long)P->min_samples_leaf, P->max_depth,
+        pool_depth(P), ctx->d_fbest);
     CKL();
-    k_split_reduce<false><<<2 * W_ub, 32, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ctx->d_pool, rf.nf, ctx->d_fidx,
-                                                         ctx->d_fbest, ctx->S);
-    CKL();
-    if (next) {
-        k_next_level<false><<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, next, next_cnt, ints(ctx, I_NODES),
-                                                     ctx->nmax, level_cap(P), P->gamma, P->grow_policy == 0);
-        CKL();
-    }
+    TRY(launch_close(ctx, rf, P, false, lvl, lvl_cnt, next, next_cnt, next ? np : NextPlan()));
     ctx->waves++;
     return GBM_OK;
 }
@@ -613,7 +627,7 @@ int expand_now(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, const std
     CK(cudaMemcpyAsync(ctx->d_lvl[0], ctx->h_list, sizeof(int) * W, cudaMemcpyHostToDevice, ctx->st));
     CK(cudaMemcpyAsync(ints(ctx, I_LVL0), &ctx->h_list[ctx->stage_slots], sizeof(int), cudaMemcpyHostToDevice,
                        ctx->st));
-    TRY(launch_level(ctx, rf, P, ctx->d_lvl[0], ints(ctx, I_LVL0), nullptr, nullptr, W));
+    TRY(launch_level(ctx, rf, P, ctx->d_lvl[0], ints(ctx, I_LVL0), nullptr, nullptr, W, false, false, NextPlan()));
     return fetch_nodes(ctx);
 }
 
@@ -896,13 +910,21 @@ int enqueue_grow(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
     k_comp_scatter<<<ntile, 256, 0, ctx->st>>>(ctx->d_mask, ctx->n, ctx->d_off, ctx->d_rows);
     CKL();
     if (ctx->comm) TRY(gbm_comm_check_alive(ctx->comm, ctx->timeout_ms, ctx->err));
-    TRY(launch_root(ctx, rf, P));
+    const int D = P->max_depth;
+    auto plan_of = [&](int L) {
+        NextPlan np;
+        if (L < D) {
+            np.W_ub = std::min(level_width(P, L), ctx->stage_slots);
+            np.last = L == D - 1;
+        }
+        return np;
+    };
+    TRY(launch_root(ctx, rf, P, plan_of(0)));
     int cur = 0;
-    for (int L = 0; L < P->max_depth; L++) {
-        int W = std::min(level_width(P, L), ctx->stage_slots);
-        const bool last = L == P->max_depth - 1;
+    for (int L = 0; L < D; L++) {
+        const NextPlan me = plan_of(L);
         TRY(launch_level(ctx, rf, P, ctx->d_lvl[cur], ints(ctx, I_LVL0 + cur), ctx->d_lvl[1 - cur],
-                         ints(ctx, I_LVL0 + 1 - cur), W, last));
+                         ints(ctx, I_LVL0 + 1 - cur), me.W_ub, me.last, true, plan_of(L + 1)));
         cur = 1 - cur;
     }
     return GBM_OK;
@@ -1022,6 +1044,9 @@ void write_tree(const HostTree &T, int need, gbm_tree_out *out) {
 int prepare_round(gbm_ctx *ctx, int nf, const gbm_params *P) {
     TRY(ensure_round_buffers(ctx, nf, P));
     TRY(ensure_slots(ctx));
+    // staging histograms start every call at zero (each use zeroes what it read)
+    CK(cudaMemsetAsync(ctx->d_stage, 0, sizeof(long long) * (size_t)ctx->stage_slots * slot_words_for(ctx->nf_cap),
+                       ctx->st));
     return stage_mono(ctx, P);
 }
 
@@ -1174,7 +1199,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     void *dev_ptrs[] = {ctx->d_xb, ctx->d_counts, ctx->d_skipb, ctx->d_y, ctx->d_F, ctx->d_q, ctx->d_mask,
                         ctx->d_rows, ctx->d_tmp, ctx->d_cnt, ctx->d_off, ctx->d_total, ctx->d_blist, ctx->d_fidx,
                         ctx->d_fpos, ctx->d_pool, ctx->d_stage, ctx->d_fbest, ctx->d_htask, ctx->d_hprefix,
-                        ctx->d_ptask, ctx->d_tile_cnt, ctx->d_tile_off, ctx->d_nleft, ctx->d_nleft_g,
+                        ctx->d_ptask, ctx->d_tile_cnt, ctx->d_nleft, ctx->d_nleft_g,
                         ctx->d_count64, ctx->d_nodes, ctx->d_lvl[0], ctx->d_lvl[1], ctx->d_ints, ctx->d_tree,
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
                         ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,

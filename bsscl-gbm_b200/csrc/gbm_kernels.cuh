@@ -287,20 +287,12 @@ __global__ void k_count64(const int32_t *__restrict__ in, long long *__restrict_
 // for R rows over all tasks.  CTA c of G takes the rows whose cost position
 // lies in [B_c, B_c+1), B_c = floor(c T / G): every CTA gets the same work
 // whatever the tasks' sizes, and a launch is exactly G / (2 per SM) waves.
-// cta_of(x) is the CTA whose range holds cost position x.
-__device__ __forceinline__ long long cost_bound(long long c, long long T, long long G) { return c * T / G; }
-__device__ __forceinline__ long long cta_of(long long x, long long T, long long G) {
-    return ((x + 1) * G + T - 1) / T - 1;
-}
-__device__ __forceinline__ long long ceil_div_ll(long long a, long long b) { return (a + b - 1) / b; }
-
 // A (block, task) segment whose rows all fall in one CTA's range, and no
 // more than kChunk of them, is stored directly by that CTA; every other
-// segment is added atomically into a zeroed staging histogram.
-__device__ __forceinline__ bool segment_single(long long rows, long long first_pos, int w, long long T, long long G) {
-    if (rows <= 0 || rows > kChunk) return false;
-    return cta_of(first_pos, T, G) == cta_of(first_pos + (rows - 1) * w, T, G);
-}
+// segment is added atomically into the staging histogram, which is zero
+// between uses.
+__device__ __forceinline__ long long cost_bound(long long c, long long T, long long G) { return c * T / G; }
+__device__ __forceinline__ long long ceil_div_ll(long long a, long long b) { return (a + b - 1) / b; }
 
 // Each row's q (int64) is split into three digits, q = top*2^34 + mid*2^17 +
 // low with low, mid in [0, 2^17) and top signed, and each digit is summed in
@@ -447,34 +439,6 @@ k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ ro
             }
             k = pe;
         }
-    }
-}
-
-// Zero, in the staging histograms, every feature (and the totals, which go
-// with block 0) whose (block, task) segment is not stored whole by one CTA:
-// those are added atomically, and a task with no rows is read as zeros.
-// grid: x = feature position (nf = the totals), y = task.
-__global__ void k_zero_stage(const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
-                             const int *__restrict__ ntask_p, const int32_t *__restrict__ bwp, int nb,
-                             const int16_t *__restrict__ fbi, int nf, int G, long long *__restrict__ stage) {
-    const int t = blockIdx.y, jj = blockIdx.x;
-    const int ntask = *ntask_p;
-    if (t >= ntask) return;
-    const long long R = rpre[ntask];
-    const long long T = (long long)bwp[nb] * R;
-    const int bi = jj < nf ? fbi[jj] : 0;
-    const long long rows = rpre[t + 1] - rpre[t];
-    if (T > 0) {
-        const int w = bwp[bi + 1] - bwp[bi];
-        const long long first = (long long)bwp[bi] * R + (long long)rpre[t] * w;
-        if (segment_single(rows, first, w, T, G)) return;
-    }
-    long long *p = stage + (int64_t)tasks[t].stage * slot_words_for(nf);
-    if (jj < nf) {
-        p += (int64_t)jj * kBins * kWords;
-        for (int i = threadIdx.x; i < kBins * kWords; i += blockDim.x) p[i] = 0;
-    } else if (threadIdx.x < kTotWords) {
-        p[(int64_t)nf * kBins * kWords + threadIdx.x] = 0;
     }
 }
 
@@ -631,34 +595,17 @@ k_part_count(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restric
     }
 }
 
-// One CTA per task: exclusive scan of its tiles' left counts; n_left.
-__global__ void k_part_scan(const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
-                            const int32_t *__restrict__ tile_cnt, int32_t *__restrict__ tile_off,
-                            long long *__restrict__ n_left) {
-    __shared__ int s_w[32];
-    if ((int)blockIdx.x >= *ntask_p) return;
-    PartTask tk = tasks[blockIdx.x];
-    int carry = 0;
-    for (int b = 0; b < tk.ntile; b += blockDim.x) {
-        int k = b + threadIdx.x;
-        int v = k < tk.ntile ? tile_cnt[tk.tile0 + k] : 0;
-        int tot;
-        int e = block_excl_scan(v, s_w, tot);
-        if (k < tk.ntile) tile_off[tk.tile0 + k] = carry + e;
-        carry += tot;
-    }
-    if (threadIdx.x == 0) n_left[blockIdx.x] = carry;
-}
-
 // Row o of a tile is bit (o & 31) of side word o >> 5; the word of rows
 // [32 i, 32 i + 32) was written by warp i % 16 of the count kernel.  Each
-// warp here ranks a run of 256 consecutive rows (8 words).
+// CTA first sums its task's tile counts (the lefts before it, and n_left,
+// which the task's first tile stores); each warp then ranks a run of 256
+// consecutive rows (8 words).
 __global__ void __launch_bounds__(kPartThreads)
 k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks,
                const int *__restrict__ ntask_p, const int *__restrict__ tiles_total,
-               const unsigned *__restrict__ side, const int32_t *__restrict__ tile_off,
-               const long long *__restrict__ n_left) {
-    __shared__ int s_l[kPartThreads / 32];
+               const unsigned *__restrict__ side, const int32_t *__restrict__ tile_cnt,
+               long long *__restrict__ n_left) {
+    __shared__ int s_l[kPartThreads / 32], s_a[kPartThreads / 32], s_b[kPartThreads / 32];
     const int tile = blockIdx.x;
     if (tile >= *tiles_total) return;
     const int t = find_task_by_tile(tasks, *ntask_p, tile);
@@ -669,6 +616,18 @@ k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, c
     const int m = (int)min((long long)kPartTile, tk.end - tstart);
     const unsigned *sw = side + (int64_t)tile * kPartWords;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    // lefts of the task's earlier tiles, and of all its tiles (n_left)
+    {
+        int before = 0, all = 0;
+        for (int k = threadIdx.x; k < tk.ntile; k += blockDim.x) {
+            const int v = tile_cnt[tk.tile0 + k];
+            all += v;
+            before += tk.tile0 + k < tile ? v : 0;
+        }
+        before = warp_sum(before);
+        all = warp_sum(all);
+        if (lane == 0) { s_b[w] = before; s_a[w] = all; }
+    }
     constexpr int WPW = kPartWords / (kPartThreads / 32);   // side words per warp
     unsigned wd[WPW];
     int lw = 0;
@@ -681,8 +640,9 @@ k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, c
     __syncthreads();
     int lbase = 0;
     for (int k = 0; k < w; k++) lbase += s_l[k];
-    const long long nl = n_left[t];
-    const long long lcar = tile_off[tile];                   // lefts before this tile
+    long long nl = 0, lcar = 0;                              // lefts of the task; before this tile
+    for (int k = 0; k < kPartThreads / 32; k++) { nl += s_a[k]; lcar += s_b[k]; }
+    if (threadIdx.x == 0 && tile == tk.tile0) n_left[t] = nl;
     const long long rcar = (tstart - tk.begin) - lcar;       // rights before this tile
     long long lpos = tk.begin + lcar + lbase;
     long long rpos = tk.begin + nl + rcar + (long long)(w * WPW * 32 - lbase);
@@ -917,13 +877,14 @@ __device__ __forceinline__ void feature_best(i128 (&g)[8], i128 (&h)[8], i128 TG
 
 // One warp per (parent k, feature position jj, child side): the smaller
 // child's cells come from staging slot k, the larger child's are parent -
-// smaller (E:740-745, exact).  Each warp writes its child's pool slot (the
+// smaller (E:740-745, exact); the staging cells are zeroed after use.  Each warp writes its child's pool slot (the
 // child's histogram as a future parent; the cells are skipped when that
 // child's children are handled without histograms) and finds its best bin
 // for feature jj.
 // ROOT: node 0 from staging slot 0.  fbest[(2k + side) * nf + jj], side 0 =
 // left child.
 constexpr int kSplitFeatPerCta = kSplitWarps / 2;
+static_assert(kSplitWarps == 8, "k_split_feat names one barrier per warp pair (4 pairs)");
 
 template <bool ROOT>
 __global__ void __launch_bounds__(32 * kSplitWarps)
@@ -962,13 +923,14 @@ k_split_feat(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
         TH = cell(pt[2] - st_tot[2], pt[3] - st_tot[3]);
     }
     long long *pc = pool + (int64_t)ch * words;
-    const bool write_pool = nd.depth < pool_depth;   // the cells; the totals always (k_split_reduce)
+    const bool write_pool = nd.depth < pool_depth;   // the cells; the totals always (level close)
     if (jj == 0 && lane < kTotWords) {
         const int64_t o = (int64_t)nf * kBins * kWords + lane;
         pc[o] = is_small ? st_tot[lane] : par[o] - st_tot[lane];
     }
     // cells of feature jj: lane owns bins 8*lane .. 8*lane+7 (32 words)
     const int64_t base = (int64_t)jj * kBins * kWords + (int64_t)lane * 8 * kWords;
+    long long *stw = const_cast<long long *>(st) + base;
     i128 g[8], h[8];
 #pragma unroll
     for (int b = 0; b < 8; b++) {
@@ -987,6 +949,23 @@ k_split_feat(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
         }
         g[b] = cell(a.x, a.y);
         h[b] = cell(d.x, d.y);
+    }
+    // The staging cells are read once: zero them for the next level's atomic
+    // adds once both warps of this (task, feature) pair have read them.
+    if (ROOT) {
+        __syncwarp();
+    } else {
+        switch (warp >> 1) {   // a named barrier per warp pair (constant ids)
+            case 0: asm volatile("bar.sync 1, 64;" ::: "memory"); break;
+            case 1: asm volatile("bar.sync 2, 64;" ::: "memory"); break;
+            case 2: asm volatile("bar.sync 3, 64;" ::: "memory"); break;
+            default: asm volatile("bar.sync 4, 64;" ::: "memory"); break;
+        }
+    }
+    if (side == 0) {
+#pragma unroll
+        for (int v = 0; v < 8 * kWords; v += 2)
+            *reinterpret_cast<longlong2 *>(stw + v) = make_longlong2(0, 0);
     }
     const int f = fidx[jj];
     const int nb = counts[f];
@@ -1009,86 +988,156 @@ k_split_feat(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
     }
 }
 
-// Per child: the first best over feature positions (ties -> lower position),
-// its totals as float64, and the parent marked expanded.
-template <bool ROOT>
-__global__ void k_split_reduce(DNode *__restrict__ nodes, const int *__restrict__ lvl,
-                               const int *__restrict__ lvl_count, const long long *__restrict__ pool, int nf,
-                               const int32_t *__restrict__ fidx, const FBest *__restrict__ fbest, int S) {
-    const int c = blockIdx.x;
-    int ch = 0, parent = -1;
-    if (!ROOT) {
-        const int k = c >> 1;
-        if (k >= *lvl_count) return;
-        parent = lvl[k];
-        ch = (c & 1) ? nodes[parent].kid1 : nodes[parent].kid0;
-    }
-    const FBest *fb = fbest + (int64_t)c * nf;
-    double bg = -1e9;
-    int bj = -1, bb = 0;
-    for (int jj = threadIdx.x; jj < nf; jj += 32) {
-        FBest o = fb[jj];
-        if (o.valid && better(o.gain, jj, o.bin, bg, bj, bb)) { bg = o.gain; bj = jj; bb = o.bin; }
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        double og = __shfl_xor_sync(0xffffffffu, bg, o);
-        int oj = __shfl_xor_sync(0xffffffffu, bj, o);
-        int ob = __shfl_xor_sync(0xffffffffu, bb, o);
-        if (better(og, oj, ob, bg, bj, bb)) { bg = og; bj = oj; bb = ob; }
-    }
-    if (threadIdx.x == 0) {
-        const long long *t = pool + (int64_t)ch * slot_words_for(nf) + (int64_t)nf * kBins * kWords;
-        const double sc = pow2(-S);
-        DNode &d = nodes[ch];
-        d.G = __dmul_rn(i128_to_double(cell(t[0], t[1])), sc);
-        d.H = __dmul_rn(i128_to_double(cell(t[2], t[3])), sc);
-        d.feat = bj >= 0 ? fidx[bj] : -1;
-        d.bin = bj >= 0 ? bb : 0;
-        d.gain = bj >= 0 ? bg : -1.0;
-        if (!ROOT && (c & 1) == 0) nodes[parent].expanded = 1;
-    }
-}
+// The end of a level, in one CTA (1024 threads):
+//   1. per child (a warp each): the first best over feature positions, its
+//      totals as float64, the parent marked expanded (E:775-801);
+//   2. when `next` is given: the children with a split (and gain > gamma
+//      when use_gamma) ranked by gain (ties -> lower node id), at most
+//      min(M, capacity) of them, as the next level's list;
+//   3. when `pt` is given: that list's plan -- two fresh children per parent
+//      and the partition tasks (at most w_max parents) -- and, for a last
+//      level (`leafw`), its zeroed count/total words.
+// The staging totals of this level's tasks are zeroed (read for the last
+// time by the split search).
+constexpr int kCloseThreads = 1024;
 
-// Next level: among the children of lvl[0..W) (ROOT: node 0 alone), the ones
-// with a split (and gain > gamma when use_gamma), ranked by gain (ties ->
-// lower node id), at most min(M, capacity) of them.
 template <bool ROOT>
-__global__ void k_next_level(const DNode *__restrict__ nodes, const int *__restrict__ lvl,
-                             const int *__restrict__ lvl_count, int *__restrict__ out,
-                             int *__restrict__ out_count, const int *__restrict__ node_count, int nmax,
-                             int M, double gamma, int use_gamma) {
+__global__ void __launch_bounds__(kCloseThreads)
+k_level_close(DNode *__restrict__ nodes, const int *__restrict__ lvl, const int *__restrict__ lvl_count,
+              const long long *__restrict__ pool, long long *__restrict__ stage, int nf,
+              const int32_t *__restrict__ fidx, const FBest *__restrict__ fbest, int S,
+              int *__restrict__ next, int *__restrict__ next_count, int *__restrict__ node_count, int nmax, int M,
+              double gamma, int use_gamma, PartTask *__restrict__ pt, int *__restrict__ tiles_total, int w_max,
+              long long *__restrict__ leafw, long long *__restrict__ nleft) {
     __shared__ double s_g[1024];
     __shared__ int s_id[1024];
-    __shared__ int s_cnt;
-    const int W = ROOT ? 0 : *lvl_count;
+    __shared__ int s_cnt, s_W, s_base;
+    __shared__ int s_w[32];
+    const int W = ROOT ? 1 : *lvl_count;
     const int C = ROOT ? 1 : 2 * W;
-    if (threadIdx.x == 0) s_cnt = 0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t words = slot_words_for(nf);
+    // 1. split reduce
+    for (int cc = warp; cc < C; cc += kCloseThreads / 32) {
+        int ch = 0, parent = -1;
+        if (!ROOT) {
+            parent = lvl[cc >> 1];
+            ch = (cc & 1) ? nodes[parent].kid1 : nodes[parent].kid0;
+        }
+        const FBest *fb = fbest + (int64_t)cc * nf;
+        double bg = -1e9;
+        int bj = -1, bb = 0;
+        for (int jj = lane; jj < nf; jj += 32) {
+            FBest o = fb[jj];
+            if (o.valid && better(o.gain, jj, o.bin, bg, bj, bb)) { bg = o.gain; bj = jj; bb = o.bin; }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            double og = __shfl_xor_sync(0xffffffffu, bg, o);
+            int oj = __shfl_xor_sync(0xffffffffu, bj, o);
+            int ob = __shfl_xor_sync(0xffffffffu, bb, o);
+            if (better(og, oj, ob, bg, bj, bb)) { bg = og; bj = oj; bb = ob; }
+        }
+        if (lane == 0) {
+            const long long *t = pool + (int64_t)ch * words + (int64_t)nf * kBins * kWords;
+            const double sc = pow2(-S);
+            DNode &d = nodes[ch];
+            d.G = __dmul_rn(i128_to_double(cell(t[0], t[1])), sc);
+            d.H = __dmul_rn(i128_to_double(cell(t[2], t[3])), sc);
+            d.feat = bj >= 0 ? fidx[bj] : -1;
+            d.bin = bj >= 0 ? bb : 0;
+            d.gain = bj >= 0 ? bg : -1.0;
+            if (!ROOT && (cc & 1) == 0) nodes[parent].expanded = 1;
+        }
+    }
+    for (int i = threadIdx.x; i < W * kTotWords; i += kCloseThreads)
+        stage[(int64_t)(i / kTotWords) * words + (int64_t)nf * kBins * kWords + i % kTotWords] = 0;
+    if (!next) return;
     __syncthreads();
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        int id = ROOT ? 0 : ((c & 1) ? nodes[lvl[c >> 1]].kid1 : nodes[lvl[c >> 1]].kid0);
+    // 2. next level list
+    if (threadIdx.x == 0) s_cnt = 0;
+    for (int cc = threadIdx.x; cc < C; cc += kCloseThreads) {
+        int id = ROOT ? 0 : ((cc & 1) ? nodes[lvl[cc >> 1]].kid1 : nodes[lvl[cc >> 1]].kid0);
         const DNode &d = nodes[id];
         bool ok = d.feat >= 0 && (!use_gamma || d.gain > gamma);
-        s_g[c] = d.gain;
-        s_id[c] = ok ? id : -1;
+        s_g[cc] = d.gain;
+        s_id[cc] = ok ? id : -1;
     }
     __syncthreads();
-    int cap = (nmax - *node_count) / 2;
-    int Mc = M < cap ? M : cap;
-    if (Mc < 0) Mc = 0;
-    for (int c = threadIdx.x; c < C; c += blockDim.x) {
-        if (s_id[c] < 0) continue;
-        int rank = 0;
-        for (int o = 0; o < C; o++) {
-            if (s_id[o] < 0 || o == c) continue;
-            if (s_g[o] > s_g[c] || (s_g[o] == s_g[c] && s_id[o] < s_id[c])) rank++;
-        }
-        if (rank < Mc) {
-            out[rank] = s_id[c];
-            atomicAdd(&s_cnt, 1);
+    {
+        int cap = (nmax - *node_count) / 2;
+        int Mc = M < cap ? M : cap;
+        if (Mc < 0) Mc = 0;
+        for (int cc = threadIdx.x; cc < C; cc += kCloseThreads) {
+            if (s_id[cc] < 0) continue;
+            int rank = 0;
+            for (int o = 0; o < C; o++) {
+                if (s_id[o] < 0 || o == cc) continue;
+                if (s_g[o] > s_g[cc] || (s_g[o] == s_g[cc] && s_id[o] < s_id[cc])) rank++;
+            }
+            if (rank < Mc) {
+                next[rank] = s_id[cc];
+                atomicAdd(&s_cnt, 1);
+            }
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) *out_count = s_cnt;
+    if (!pt) {
+        if (threadIdx.x == 0) *next_count = s_cnt;
+        return;
+    }
+    // 3. plan the next level
+    if (threadIdx.x == 0) {
+        int Wn = s_cnt, base = *node_count;
+        int cap = (nmax - base) / 2;
+        if (Wn > w_max) Wn = w_max;
+        if (Wn > cap) Wn = cap < 0 ? 0 : cap;
+        s_W = Wn;
+        s_base = base;
+    }
+    __syncthreads();
+    const int Wn = s_W, base = s_base;
+    int carry = 0;
+    for (int b0 = 0; b0 < Wn; b0 += kCloseThreads) {
+        int k = b0 + threadIdx.x;
+        int ntl = 0;
+        int i = -1;
+        if (k < Wn) {
+            i = next[k];
+            long long sz = nodes[i].end - nodes[i].begin;
+            ntl = (int)((sz + kPartTile - 1) / kPartTile);
+            if (ntl < 1) ntl = 1;
+        }
+        int tot;
+        int e = block_excl_scan(ntl, s_w, tot);
+        if (k < Wn) {
+            DNode &p = nodes[i];
+            PartTask t;
+            t.begin = p.begin;
+            t.end = p.end;
+            t.feat = p.feat;
+            t.thr = p.bin;
+            t.tile0 = carry + e;
+            t.ntile = ntl;
+            t.src = p.depth & 1;
+            t.pad = 0;
+            pt[k] = t;
+            int c0 = base + 2 * k;
+            p.kid0 = c0;
+            p.kid1 = c0 + 1;
+            nodes[c0] = fresh_node(p.depth + 1, i);
+            nodes[c0 + 1] = fresh_node(p.depth + 1, i);
+        }
+        carry += tot;
+    }
+    if (leafw) {
+        for (int i = threadIdx.x; i < Wn * kLeafWords; i += kCloseThreads) leafw[i] = 0;
+        for (int i = threadIdx.x; i < Wn; i += kCloseThreads) nleft[i] = 0;
+    }
+    if (threadIdx.x == 0) {
+        *next_count = Wn;
+        *node_count = base + 2 * Wn;
+        *tiles_total = carry;
+    }
 }
 
 // ===========================================================================
