@@ -121,7 +121,8 @@ struct gbm_ctx {
     static constexpr int kRing = 4;
     Slot slot[kRing];
     bool slots_ready = false;
-    cudaStream_t cst = nullptr;        // the samplers' copies and row shuffles
+    cudaStream_t cst = nullptr;        // the samplers' copies, row shuffles and root row lists
+    cudaEvent_t rows_free = nullptr;   // recorded on st once a round is done with the row lists
     // The bound sampler's row permutation lives here: round r turns its swap
     // targets into a shuffle and composes perm[r % 5] = perm[(r-1) % 5][S]
     // on cst, ahead of the round's growth.
@@ -900,15 +901,23 @@ int tree_need(const gbm_params *P) {
 
 // Enqueue the in-bag compaction and the level-wise growth; the round's
 // in-bag mask is on the device and its feature tables are staged.
-int enqueue_grow(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
-    TRY(flush_l2(ctx));
+// In-bag mask -> ascending row list of the root (row buffer 0) and its count.
+int enqueue_compaction(gbm_ctx *ctx, cudaStream_t s) {
     int ntile = (int)((ctx->n + kCompTile - 1) / kCompTile);
-    k_comp_count<<<ntile, 256, 0, ctx->st>>>(ctx->d_mask, ctx->n, ctx->d_cnt);
+    k_comp_count<<<ntile, 256, 0, s>>>(ctx->d_mask, ctx->n, ctx->d_cnt);
     CKL();
-    k_scan_small<<<1, 1024, 0, ctx->st>>>(ctx->d_cnt, ntile, ctx->d_off, ctx->d_total);
+    k_scan_small<<<1, 1024, 0, s>>>(ctx->d_cnt, ntile, ctx->d_off, ctx->d_total);
     CKL();
-    k_comp_scatter<<<ntile, 256, 0, ctx->st>>>(ctx->d_mask, ctx->n, ctx->d_off, ctx->d_rows);
+    k_comp_scatter<<<ntile, 256, 0, s>>>(ctx->d_mask, ctx->n, ctx->d_off, ctx->d_rows);
     CKL();
+    return GBM_OK;
+}
+
+// `compacted`: the root's row list was already built (stage_sample, on the
+// sampler stream); otherwise it is built here from d_mask.
+int enqueue_grow(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, bool compacted) {
+    TRY(flush_l2(ctx));
+    if (!compacted) TRY(enqueue_compaction(ctx, ctx->st));
     if (ctx->comm) TRY(gbm_comm_check_alive(ctx->comm, ctx->timeout_ms, ctx->err));
     const int D = P->max_depth;
     auto plan_of = [&](int L) {
@@ -927,6 +936,8 @@ int enqueue_grow(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P) {
                          ints(ctx, I_LVL0 + 1 - cur), me.W_ub, me.last, true, plan_of(L + 1)));
         cur = 1 - cur;
     }
+    // the row lists are free: the next round's compaction may overwrite them
+    CK(cudaEventRecord(ctx->rows_free, ctx->st));
     return GBM_OK;
 }
 
@@ -1052,8 +1063,9 @@ int prepare_round(gbm_ctx *ctx, int nf, const gbm_params *P) {
 
 // The sampler's next round: its row swap targets go to the device on cst,
 // where the round's shuffle is built and composed into the permutation, and
-// this rank's in-bag mask is made from the first n_sub entries on the engine
-// stream.  The round's feature list is left in feat_buf.
+// this rank's in-bag mask and root row list are made from the first n_sub
+// entries.  The engine stream waits for them.  The round's feature list is
+// left in feat_buf.
 int stage_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset) {
     gbm_ctx::Slot &s = ctx->slot[si];
     const int64_t N = gbm_sampler_rows(sampler);
@@ -1081,24 +1093,32 @@ int stage_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset)
     ctx->host_sample_ms += ms_since(t_s);
     if (rc != GBM_OK) return fail(ctx, rc, "the sampler cannot feed an engine (already used for host draws?)");
     ctx->samp_taken++;
-    if (!rows_on) {   // sample_idx is every row (E:2508-2509)
-        CK(cudaMemsetAsync(ctx->d_mask, 1, (size_t)ctx->n, ctx->st));
-        return GBM_OK;
+    int32_t *pout = nullptr;
+    if (rows_on) {
+        int32_t *pin = ctx->d_perm[(r + R1 - 1) % R1];
+        pout = ctx->d_perm[r % R1];
+        CK(cudaMemcpyAsync(s.d_tg, s.h_tg, sizeof(int32_t) * (size_t)(N - 1), cudaMemcpyHostToDevice, ctx->cst));
+        CK(cudaMemsetAsync(ctx->d_head, 0xff, sizeof(int32_t) * (size_t)N, ctx->cst));
+        k_shuf_link<<<grid_for(N - 1, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_head, ctx->d_nxt);
+        CKL();
+        k_shuf_min<<<grid_for(N, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp);
+        CKL();
+        k_shuf_compose<<<grid_for(N, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_m, ctx->d_mp, pin, pout);
+        CKL();
     }
-    int32_t *pin = ctx->d_perm[(r + R1 - 1) % R1], *pout = ctx->d_perm[r % R1];
-    CK(cudaMemcpyAsync(s.d_tg, s.h_tg, sizeof(int32_t) * (size_t)(N - 1), cudaMemcpyHostToDevice, ctx->cst));
-    CK(cudaMemsetAsync(ctx->d_head, 0xff, sizeof(int32_t) * (size_t)N, ctx->cst));
-    k_shuf_link<<<grid_for(N - 1, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_head, ctx->d_nxt);
-    CKL();
-    k_shuf_min<<<grid_for(N, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp);
-    CKL();
-    k_shuf_compose<<<grid_for(N, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_m, ctx->d_mp, pin, pout);
-    CKL();
+    // mask and root row list on this stream too, once the previous round has
+    // finished with the row lists (it is at its replay or F update by then)
+    CK(cudaStreamWaitEvent(ctx->cst, ctx->rows_free, 0));
+    if (rows_on) {
+        CK(cudaMemsetAsync(ctx->d_mask, 0, (size_t)ctx->n, ctx->cst));
+        k_mask_from_rows<<<grid_for(m, 256), 256, 0, ctx->cst>>>(pout, m, row_offset, ctx->n, ctx->d_mask);
+        CKL();
+    } else {   // sample_idx is every row (E:2508-2509)
+        CK(cudaMemsetAsync(ctx->d_mask, 1, (size_t)ctx->n, ctx->cst));
+    }
+    TRY(enqueue_compaction(ctx, ctx->cst));
     CK(cudaEventRecord(s.copied, ctx->cst));
     CK(cudaStreamWaitEvent(ctx->st, s.copied, 0));
-    CK(cudaMemsetAsync(ctx->d_mask, 0, (size_t)ctx->n, ctx->st));
-    k_mask_from_rows<<<grid_for(m, 256), 256, 0, ctx->st>>>(pout, m, row_offset, ctx->n, ctx->d_mask);
-    CKL();
     return GBM_OK;
 }
 
@@ -1174,6 +1194,7 @@ int gbm_ctx_create(int32_t device, gbm_ctx **out) {
     CK(cudaSetDevice(device));
     CK(cudaStreamCreateWithFlags(&ctx->st, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&ctx->cst, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&ctx->rows_free, cudaEventDisableTiming));
     int sms = 0;
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
     ctx->hist_grid = 2 * std::max(sms, 1);   // one wave of 2 per SM (measured best: fewer flushes)
@@ -1220,6 +1241,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     for (cudaEvent_t e : ctx->mark) if (e) cudaEventDestroy(e);
     if (ctx->st) cudaStreamDestroy(ctx->st);
     if (ctx->cst) cudaStreamDestroy(ctx->cst);
+    if (ctx->rows_free) cudaEventDestroy(ctx->rows_free);
     delete ctx;
 }
 
@@ -1333,7 +1355,7 @@ int gbm_build_tree(gbm_ctx *ctx, const double *grad, const double *hess, const u
     CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
     RoundFeat rf;
     TRY(setup_features(ctx, 0, feat_idx, nfeat, rf));
-    TRY(enqueue_grow(ctx, rf, P));
+    TRY(enqueue_grow(ctx, rf, P, false));
     if (device_replay(ctx, P)) {
         TRY(enqueue_replay(ctx, P));
         gbm_ctx::Slot &s = ctx->slot[0];
@@ -1354,11 +1376,11 @@ int gbm_build_tree(gbm_ctx *ctx, const double *grad, const double *hess, const u
 // growth, the tree (device replay, or host replay for capped levels), the F
 // update, the loss, and the wait for all of it.
 static int round_body(gbm_ctx *ctx, const int32_t *feat_idx, int32_t nfeat, const gbm_params *P,
-                      gbm_tree_out *out, double *train_loss) {
+                      gbm_tree_out *out, double *train_loss, bool compacted) {
     gbm_ctx::Slot &s = ctx->slot[0];
     RoundFeat rf;
     TRY(setup_features(ctx, 0, feat_idx, nfeat, rf));
-    TRY(enqueue_grow(ctx, rf, P));
+    TRY(enqueue_grow(ctx, rf, P, compacted));
     const bool dev = device_replay(ctx, P);
     HostTree T;
     if (dev) {
@@ -1400,7 +1422,7 @@ int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, 
     TRY(prepare_round(ctx, nfeat, P));
     std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
     CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
-    return round_body(ctx, feat_idx, nfeat, P, out, train_loss);
+    return round_body(ctx, feat_idx, nfeat, P, out, train_loss, false);
 }
 
 int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *P,
@@ -1412,7 +1434,7 @@ int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, co
     CK(cudaSetDevice(ctx->dev));
     TRY(prepare_round(ctx, nf, P));
     TRY(stage_sample(ctx, 0, sampler, row_offset));
-    return round_body(ctx, ctx->feat_buf.data(), nf, P, out, train_loss);
+    return round_body(ctx, ctx->feat_buf.data(), nf, P, out, train_loss, true);
 }
 
 int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *P, int32_t n_rounds,
@@ -1444,7 +1466,7 @@ int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const
         TRY(stage_sample(ctx, si, sampler, row_offset));
         RoundFeat rf;
         TRY(setup_features(ctx, si, ctx->feat_buf.data(), nf, rf));
-        TRY(enqueue_grow(ctx, rf, P));
+        TRY(enqueue_grow(ctx, rf, P, true));
         TRY(enqueue_replay(ctx, P));
         TRY(enqueue_update(ctx, P, false, s.h_loss));
         CK(cudaMemcpyAsync(s.h_tout, ctx->d_tout, sizeof(TreeOut), cudaMemcpyDeviceToHost, ctx->st));
