@@ -183,6 +183,7 @@ class Engine:
         buf = (C.c_uint8 * 128).from_buffer_copy(uid)
         self.check(self._L.gbm_ctx_init_comm(self._h, C.cast(buf, C.c_void_p), nranks, rank,
                                              timeout_ms), "gbm_ctx_init_comm")
+        self._comm_world = (nranks, rank)
 
     # -- training --
     def upload_bins(self, xbin, counts):

@@ -450,9 +450,10 @@ class HybridHistGBMNumbaV1_0_1:
         if dist is not None:
             ws, rk = dist.get_world_size(), dist.get_rank()
             lo, hi = (n * rk) // ws, (n * (rk + 1)) // ws
-            uid = [Engine.nccl_unique_id() if rk == 0 else None]
-            dist.broadcast_object_list(uid, src=0)
-            eng.init_comm(uid[0], ws, rk)
+            if getattr(eng, "_comm_world", None) != (ws, rk):   # one communicator per engine
+                uid = [Engine.nccl_unique_id() if rk == 0 else None]
+                dist.broadcast_object_list(uid, src=0)
+                eng.init_comm(uid[0], ws, rk)
         if int(np.max(self.feature_bin_counts)) > 256:
             binning.device_bins(X_bin[:1], self.feature_bin_counts)   # raises the ValueError
         # uint16 (the reference's bin dtype) and uint8 ids go up as they are;

@@ -1256,6 +1256,11 @@ int gbm_ctx_init_comm(gbm_ctx *ctx, const void *uid, int32_t nranks, int32_t ran
     if (ctx->dev < 0) return GBM_ERR_STATE;
     CK(cudaSetDevice(ctx->dev));
     ctx->timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
+    if (ctx->comm) {   // replaced: finish its work first
+        TRY(sync_stream(ctx));
+        gbm_comm_destroy(ctx->comm);
+        ctx->comm = nullptr;
+    }
     if (nranks == 1) return GBM_OK;
     return gbm_comm_create(&ctx->comm, uid, nranks, rank, ctx->timeout_ms, ctx->err);
 }
