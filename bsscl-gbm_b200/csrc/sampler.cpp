@@ -21,6 +21,7 @@
 #include <atomic>
 #include <condition_variable>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -33,6 +34,60 @@
 namespace gbmsamp {
 
 constexpr int kN = 624, kM = 397;
+
+// AVX-512 (F, BW, VL, DQ) versions of the twist and of the target draw are
+// used when the CPU has them (the B200 hosts' Xeons do); GBM_SAMPLER_ISA=avx2
+// forces the AVX2 versions.  Both give the same words and targets.
+#define GBM_AVX512 __attribute__((target("avx512f,avx512bw,avx512vl,avx512dq")))
+
+bool use_avx512() {
+    static const bool on = [] {
+        const char *e = std::getenv("GBM_SAMPLER_ISA");
+        if (e && std::strcmp(e, "avx2") == 0) return false;
+        __builtin_cpu_init();
+        return __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
+               __builtin_cpu_supports("avx512vl") && __builtin_cpu_supports("avx512dq");
+    }();
+    return on;
+}
+
+// The MT19937 twist and tempering, 16 words at a time.  The first 227 words
+// read only old state, the next 396 read words this twist already wrote
+// (i - 227 < i), and word 623 reads the new word 0.
+GBM_AVX512 static inline __m512i mix16(__m512i a, __m512i b, __m512i c) {
+    const __m512i y = _mm512_or_si512(_mm512_and_si512(a, _mm512_set1_epi32((int)0x80000000u)),
+                                      _mm512_and_si512(b, _mm512_set1_epi32(0x7fffffff)));
+    const __m512i r = _mm512_xor_si512(c, _mm512_srli_epi32(y, 1));
+    return _mm512_mask_xor_epi32(r, _mm512_test_epi32_mask(y, _mm512_set1_epi32(1)), r,
+                                 _mm512_set1_epi32((int)0x9908b0dfu));
+}
+
+static inline uint32_t mix1(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t y = (a & 0x80000000u) | (b & 0x7fffffffu);
+    return c ^ (y >> 1) ^ ((0u - (y & 1u)) & 0x9908b0dfu);
+}
+
+GBM_AVX512 void twist_avx512(uint32_t *mt, uint32_t *out) {
+    int i = 0;
+    for (; i + 16 <= kN - kM; i += 16)
+        _mm512_storeu_si512(mt + i, mix16(_mm512_loadu_si512(mt + i), _mm512_loadu_si512(mt + i + 1),
+                                          _mm512_loadu_si512(mt + i + kM)));
+    for (; i < kN - kM; i++) mt[i] = mix1(mt[i], mt[i + 1], mt[i + kM]);
+    for (; i + 16 <= kN - 1; i += 16)
+        _mm512_storeu_si512(mt + i, mix16(_mm512_loadu_si512(mt + i), _mm512_loadu_si512(mt + i + 1),
+                                          _mm512_loadu_si512(mt + i + kM - kN)));
+    for (; i < kN - 1; i++) mt[i] = mix1(mt[i], mt[i + 1], mt[i + kM - kN]);
+    mt[kN - 1] = mix1(mt[kN - 1], mt[0], mt[kM - 1]);
+    const __m512i t1 = _mm512_set1_epi32((int)0x9d2c5680u), t2 = _mm512_set1_epi32((int)0xefc60000u);
+    for (int k = 0; k < kN; k += 16) {
+        __m512i y = _mm512_loadu_si512(mt + k);
+        y = _mm512_xor_si512(y, _mm512_srli_epi32(y, 11));
+        y = _mm512_xor_si512(y, _mm512_and_si512(_mm512_slli_epi32(y, 7), t1));
+        y = _mm512_xor_si512(y, _mm512_and_si512(_mm512_slli_epi32(y, 15), t2));
+        y = _mm512_xor_si512(y, _mm512_srli_epi32(y, 18));
+        _mm512_storeu_si512(out + k, y);
+    }
+}
 
 struct MT19937 {
     uint32_t mt[kN];
@@ -48,6 +103,11 @@ struct MT19937 {
         return c ^ (y >> 1) ^ ((0u - (y & 1u)) & 0x9908b0dfu);
     }
     void refill() {   // the standard twist (split so no index wraps), then tempering
+        if (use_avx512()) {
+            twist_avx512(mt, out);
+            idx = 0;
+            return;
+        }
         int i = 0;
         for (; i < kN - kM; i++) mt[i] = mix(mt[i], mt[i + 1], mt[i + kM]);
         for (; i < kN - 1; i++) mt[i] = mix(mt[i], mt[i + 1], mt[i + kM - kN]);
@@ -90,7 +150,7 @@ inline uint32_t smear(uint64_t i) {
 }
 
 // Swap targets of NumPy's legacy shuffle for i = n-1 .. 1, stored forward:
-// t[k] is the target of i = n-1-k (k = 0 .. n-2; t holds n + 8 entries).
+// t[k] is the target of i = n-1-k (k = 0 .. n-2).
 // Each target is a uniform integer in [0, i] drawn by masked rejection (the
 // smallest all-ones mask covering i, one 32-bit word per attempt, rejected
 // if > i).  The words are consumed in the scalar rule's order, but a block
@@ -105,7 +165,64 @@ inline void pack8(__m256i v, int nacc, int32_t *t, int64_t &pos) {
     pos += __builtin_popcount((unsigned)acc);
 }
 
-void draw_targets(MT19937 &r, int64_t n, int32_t *t) {
+GBM_AVX512 void draw_targets_avx512(MT19937 &r, int64_t n, int32_t *t) {
+    const int64_t top = n - 1;
+    int64_t pos = 0;                    // i = top - pos
+    while (top - pos >= 1) {
+        if (r.idx >= kN) r.refill();
+        int64_t i = top - pos;
+        const uint32_t mask = smear((uint64_t)i);
+        const int64_t stop = ((int64_t)mask + 1) >> 1;   // lowest i with this mask
+        const uint32_t *w = r.out;
+        int k = r.idx;
+        const __m512i vm = _mm512_set1_epi32((int)mask);
+        // 64-word blocks: four independent compares, one store chain
+        while (k + 64 <= kN && i - 63 >= stop) {
+            const __m512i hi = _mm512_set1_epi32((int)i), lo = _mm512_set1_epi32((int)(i - 63));
+            __m512i v[4];
+            __mmask16 nacc[4];
+            unsigned amb = 0;
+            for (int b = 0; b < 4; b++) {
+                v[b] = _mm512_and_si512(_mm512_loadu_si512(w + k + 16 * b), vm);
+                const __mmask16 rej = _mm512_cmpgt_epi32_mask(v[b], hi);
+                nacc[b] = _mm512_cmpgt_epi32_mask(v[b], lo);
+                amb |= (unsigned)(nacc[b] & (__mmask16)~rej);
+            }
+            if (amb) break;
+            for (int b = 0; b < 4; b++) {
+                const __mmask16 acc = (__mmask16)~nacc[b];
+                _mm512_storeu_si512(t + pos, _mm512_maskz_compress_epi32(acc, v[b]));
+                pos += __builtin_popcount((unsigned)acc);
+            }
+            k += 64;
+            i = top - pos;
+        }
+        // 16-word blocks (at most 4 of them before trying 64 again)
+        for (int blk = 0; blk < 4 && k + 16 <= kN && i - 15 >= stop; blk++) {
+            const __m512i v = _mm512_and_si512(_mm512_loadu_si512(w + k), vm);
+            const __mmask16 rej = _mm512_cmpgt_epi32_mask(v, _mm512_set1_epi32((int)i));
+            const __mmask16 nacc = _mm512_cmpgt_epi32_mask(v, _mm512_set1_epi32((int)(i - 15)));
+            if (nacc & (__mmask16)~rej) break;
+            const __mmask16 acc = (__mmask16)~nacc;
+            _mm512_storeu_si512(t + pos, _mm512_maskz_compress_epi32(acc, v));
+            pos += __builtin_popcount((unsigned)acc);
+            k += 16;
+            i = top - pos;
+        }
+        // single words, up to 16
+        const int end = std::min(kN, k + 16);
+        while (k < end && i >= stop) {
+            const uint32_t v = w[k++] & mask;
+            t[pos] = (int32_t)v;
+            const int64_t a = (int64_t)(v <= (uint64_t)i);
+            pos += a;
+            i -= a;
+        }
+        r.idx = k;
+    }
+}
+
+void draw_targets_avx2(MT19937 &r, int64_t n, int32_t *t) {
     const int64_t top = n - 1;
     int64_t pos = 0;                    // i = top - pos
     while (top - pos >= 1) {
@@ -156,6 +273,12 @@ void draw_targets(MT19937 &r, int64_t n, int32_t *t) {
     }
 }
 
+// t holds n + 16 entries (the last block store may run past n - 1).
+void draw_targets(MT19937 &r, int64_t n, int32_t *t) {
+    if (use_avx512()) draw_targets_avx512(r, n, t);
+    else draw_targets_avx2(r, n, t);
+}
+
 // Fisher-Yates from the last element down to index 1 (forward targets),
 // targets prefetched.
 template <typename T>
@@ -172,7 +295,7 @@ void apply_swaps(T *a, int64_t n, const int32_t *t) {
 // applied by the consumer: on the host for gbm_sampler_next, on the device
 // for an engine) and the round's sorted feature ids.
 struct Round {
-    std::vector<int32_t> trow;          // n + 8 entries
+    std::vector<int32_t> trow;          // n + 16 entries
     std::vector<int32_t> feat;          // n_feat
     bool ready = false;
 };
@@ -279,10 +402,10 @@ int gbm_sampler_create(uint32_t seed, int64_t n, int32_t p, int64_t n_sub, int32
         s->sub_on = subsample_on; s->col_on = colsample_on;
         s->fperm.resize((size_t)p);
         for (int32_t i = 0; i < p; i++) s->fperm[(size_t)i] = i;
-        s->tfeat.resize((size_t)p + 8);
+        s->tfeat.resize((size_t)p + 16);
         s->ahead = look_ahead < 0 ? 0 : look_ahead;
         auto size_round = [&](Round &R) {
-            if (s->sub_on) R.trow.resize((size_t)n + 8);
+            if (s->sub_on) R.trow.resize((size_t)n + 16);
             R.feat.resize((size_t)n_feat);
         };
         if (s->ahead > 0) {

@@ -90,6 +90,30 @@ def test_sampler_matches_numpy_at_full_size(built_lib):
     s.close()
 
 
+def test_sampler_avx512_and_avx2_paths_agree(built_lib):
+    """The sampler's AVX-512 twist/draw (used where the CPU has it) and its
+    AVX2 versions give the same stream: compare this process with a child
+    forced onto the AVX2 versions."""
+    import subprocess
+    import sys
+    from bsscl_gbm_b200 import Sampler
+    code = ("import sys; sys.path.insert(0, %r); import numpy as np; from bsscl_gbm_b200 import Sampler; "
+            "s = Sampler(5, 300001, 40, 200000, 30, True, True, look_ahead=2); "
+            "out = [s.next(want_sample=True, want_mask=False) for _ in range(3)]; "
+            "np.savez(sys.argv[1], *[a for o in out for a in (o[0], o[2])])" % os.path.join(ROOT, "bsscl-gbm_b200"))
+    import tempfile
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "avx2.npz")
+        env = dict(os.environ, GBM_SAMPLER_ISA="avx2")
+        subprocess.run([sys.executable, "-c", code, path], env=env, check=True, timeout=120)
+        ref = np.load(path)
+        s = Sampler(5, 300001, 40, 200000, 30, True, True, look_ahead=2)
+        got = [a for _ in range(3) for a in (lambda o: (o[0], o[2]))(s.next(want_sample=True, want_mask=False))]
+        s.close()
+        for k, a in enumerate(got):
+            assert np.array_equal(a, ref[f"arr_{k}"])
+
+
 def _fisher_yates(n, j):
     a = np.arange(n)
     for i in range(n - 1, 0, -1):
