@@ -54,7 +54,12 @@ def workload(n):
 
 
 class Clocks:
-    """nvidia-smi clock/throttle sampling during the timed region."""
+    """SM clock and throttle reasons sampled DURING the timed region: NVML
+    (read only) polled every 2 ms from a thread; nvidia-smi as a fallback."""
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -62,17 +67,71 @@ class Clocks:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.thread = None
+        self.samples = []
+        self.stop_flag = False
+        self.nv = None
+
+    def _poll(self, h):
+        nv = self.nv
+        while not self.stop_flag:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((sm, mx, rs))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def start(self):
         try:
+            import pynvml as nv
+            import threading
+            nv.nvmlInit()
+            self.nv = nv
+            uuid = None
+            try:
+                import torch
+                uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+            except Exception:
+                pass
+            h = None
+            if uuid:
+                try:
+                    h = nv.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+                except Exception:
+                    h = None
+            if h is None:
+                h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self.thread = threading.Thread(target=self._poll, args=(h,), daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nv = None
+        try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join()
+            if not self.samples:
+                return None
+            reasons = set()
+            for _, _, rs in self.samples:
+                for name, attr in self.REASONS:
+                    bit = getattr(self.nv, attr, None)
+                    if bit is not None and rs & bit:
+                        reasons.add(name)
+            return {"sm_mhz": statistics.median(s[0] for s in self.samples),
+                    "sm_max_mhz": max(s[1] for s in self.samples), "reasons": sorted(reasons),
+                    "samples": len(self.samples), "source": "NVML, every 2 ms during the timed region"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -98,7 +157,17 @@ class Clocks:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi -lms 100"}
+
+
+def profile_json(name):
+    """The ```json block of a committed profile summary (profiles/<name>), or None."""
+    try:
+        txt = open(os.path.join(ROOT, "profiles", name)).read()
+        i = txt.index("```json") + len("```json")
+        return json.loads(txt[i:txt.index("```", i)])
+    except Exception:
+        return None
 
 
 def measured_peak_hbm():
@@ -222,7 +291,6 @@ def run_engine(args):
         dist.barrier()
     st = eng.stats()
     eng.set_profiling(False)
-    eng.set_l2_flush(0)
     wall_ms = eng.elapsed_ms(0, 1)
     total_ms = wall_ms - st["flush_ms"]
     if dist is not None:
@@ -230,6 +298,29 @@ def run_engine(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
     value = args.steps / (total_ms / 1000.0)
+
+    # ---- configs[3] literally: the same data at max_depth 8 -----------------------
+    prm8 = GbmParams(c["lam"], 0.0, c["mcw"], c["lr"], c["msl"], 8, c["max_leaves"], 0, None)
+    s8 = Sampler(c["seed"], n, p, n_sub, n_feat, True, True, look_ahead=3)
+    eng.upload_labels(y[lo:hi].astype(np.uint8), w2, base, n_global=n)
+    eng.fit_rounds(s8, lo, prm8, cap, args.warmup)
+    if dist is not None:
+        dist.barrier()
+    eng.reset_stats()
+    eng.set_profiling(True)
+    eng.event(6)
+    eng.fit_rounds(s8, lo, prm8, cap, args.steps)
+    eng.event(7)
+    eng.sync()
+    st8 = eng.stats()
+    eng.set_profiling(False)
+    eng.set_l2_flush(0)
+    d8_ms = eng.elapsed_ms(6, 7) - st8["flush_ms"]
+    if dist is not None:
+        t = torch.tensor([d8_ms], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        d8_ms = float(t.item())
+    s8.close()
 
     # ---- e2e: the public estimator API from host arrays ----------------------
     m = HybridHistGBMNumbaV1_0_1(n_estimators=args.steps, max_depth=c["max_depth"],
@@ -281,6 +372,16 @@ def run_engine(args):
 
     peak, peak_kind = measured_peak_hbm()
     achieved = (st["hist_alg_bytes"] / (st["hist_ms"] / 1000.0)) / 1e9 if st["hist_ms"] > 0 else 0.0
+    traffic = profile_json("k_hist_config4_1M_traffic.md")
+    atom_peak = profile_json("smem_atomic_peak_b200.md")
+    atomics = None
+    if st["hist_ms"] > 0:
+        g = 6 * st["hist_updates"] / (st["hist_ms"] / 1000.0) / 1e9
+        atomics = {"achieved_g_per_s": g, "unit": "G shared-memory atomic adds/s",
+                   "peak_random_bins_g_per_s": atom_peak and atom_peak["random_bins_g_per_s"],
+                   "peak_conflict_free_g_per_s": atom_peak and atom_peak["conflict_free_g_per_s"],
+                   "frac_of_random_bins_peak": (g / atom_peak["random_bins_g_per_s"]) if atom_peak else None,
+                   "source": "profiles/smem_atomic_peak_b200.md (microbenchmark of k_hist's access pattern)"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v_cpu, done, cores = cpu_rounds(Xb, y, counts, rounds=50, warmup=1, budget_s=20.0)
@@ -300,9 +401,14 @@ def run_engine(args):
                              "engine stream; its device time is excluded)"},
             "roofline": {"bound": "hbm", "kernel": "k_hist", "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": achieved / peak if peak else None, "traffic": None,
+                         "frac": achieved / peak if peak else None,
+                         "traffic": traffic and traffic["dram_bytes_per_launch"],
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per k_hist launch, "
+                                           "one round (profiles/k_hist_config4_1M_traffic.md)",
+                         "alg_bytes_per_launch": st["hist_alg_bytes"] / max(1, st["hist_launches"]),
                          "hist_launches": st["hist_launches"], "hist_ms": st["hist_ms"],
-                         "alg_bytes": st["hist_alg_bytes"]},
+                         "alg_bytes": st["hist_alg_bytes"],
+                         "smem_atomics": atomics},
             "breakdown_ms_per_round": {
                 "hist_kernel": st["hist_ms"] / args.steps,
                 "host_wait_sampler": st["host_sample_ms"] / args.steps,
@@ -316,6 +422,9 @@ def run_engine(args):
             "predict": {"rows_per_s": pred_rows_s, "node_visits_per_s": pred_rows_s * 1000 * 8,
                         "ensemble": "1000 full depth-8 random trees (config 5 ensemble, p=100)"},
             "train_loss_last": losses[-1] if losses else None,
+            "config4_depth8": {"value": args.steps / (d8_ms / 1000.0), "unit": "rounds/s",
+                               "ms_per_step": d8_ms / args.steps,
+                               "config": "BASELINE configs[3] literally: same data, max_depth 8, 63 leaves"},
             "clocks": clk,
             "cpu_baseline": cpu,
         }

@@ -62,6 +62,7 @@ struct gbm_ctx {
     int32_t *d_counts = nullptr;
     std::vector<int32_t> counts;
     int16_t *d_skipb = nullptr;        // per feature: the bin the histogram skips
+    std::vector<double> skip_keep;     // per feature: share of rows outside that bin
     uint8_t *d_y = nullptr;
     double *d_F = nullptr;
     longlong2 *d_q = nullptr;
@@ -116,6 +117,7 @@ struct gbm_ctx {
         int16_t *h_fpos = nullptr;     // fpos [nblk * 16] | fbi [p]
         TreeOut *h_tout = nullptr;
         double *h_loss = nullptr;
+        double upd_per_row = 0.0;      // histogram cell updates per row of this round
         cudaEvent_t copied = nullptr, done = nullptr;
     };
     static constexpr int kRing = 4;
@@ -152,7 +154,7 @@ struct gbm_ctx {
     long long launches = 0;          // every kernel this context launched
     bool profiling = false;
     long long hist_launches = 0, hist_rows = 0, waves = 0;
-    double hist_ms = 0.0, alg_bytes = 0.0;
+    double hist_ms = 0.0, alg_bytes = 0.0, hist_updates = 0.0;
     double host_sample_ms = 0.0, host_sync_ms = 0.0, host_replay_ms = 0.0;
     std::vector<cudaEvent_t> hist_ev;  // pairs recorded around k_hist launches
     int hist_ev_used = 0;
@@ -262,6 +264,7 @@ struct RoundFeat {
     int nf;
     std::vector<int32_t> blist;
     std::vector<int16_t> fpos;
+    double upd_per_row = 0.0;   // histogram cell updates per row (selected features, skipped bins out)
 };
 
 // Histogram cost of a row in an active block: its loads and flush share
@@ -340,6 +343,9 @@ int setup_features(gbm_ctx *ctx, int si, const int32_t *fidx, int nf, RoundFeat 
         }
     }
     std::memcpy(s.h_fpos, rf.fpos.data(), sizeof(int16_t) * rf.fpos.size());
+    rf.upd_per_row = 0.0;
+    for (int jj = 0; jj < nf; jj++) rf.upd_per_row += ctx->skip_keep[(size_t)fidx[jj]];
+    s.upd_per_row = rf.upd_per_row;
     CK(cudaMemcpyAsync(ctx->d_fidx, s.h_feat, sizeof(int32_t) * nf, cudaMemcpyHostToDevice, ctx->st));
     CK(cudaMemcpyAsync(ctx->d_fpos, s.h_fpos, sizeof(int16_t) * rf.fpos.size(), cudaMemcpyHostToDevice, ctx->st));
     CK(cudaMemcpyAsync(ctx->d_fbi, h_fbi, sizeof(int16_t) * nf, cudaMemcpyHostToDevice, ctx->st));
@@ -709,6 +715,7 @@ int replay_leafwise(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, Host
         if (nd_depth < P->max_depth) {   // the last level builds no histogram
             const DNode &sm = nd[gnl <= gnr ? pn.kid0 : pn.kid1];
             ctx->alg_bytes += (double)(sm.end - sm.begin) * (rf.nf + 8);
+            ctx->hist_updates += (double)(sm.end - sm.begin) * rf.upd_per_row;
         }
         bool left_small = gnl <= gnr;
         int ss = -1, sl = -1;                               // E:712-720
@@ -773,6 +780,7 @@ int replay_depthwise(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, Hos
         if (x.depth + 1 < D) {
             const DNode &sm = nd[gl <= gr ? x.kid0 : x.kid1];
             ctx->alg_bytes += (double)(sm.end - sm.begin) * (rf.nf + 8);
+            ctx->hist_updates += (double)(sm.end - sm.begin) * rf.upd_per_row;
         }
         T.tf[e.tid] = x.feat; T.tt[e.tid] = x.bin; T.tl[e.tid] = lid; T.tr[e.tid] = rid;
         T.tv[e.tid] = val; T.sg[e.tid] = x.gain;
@@ -842,11 +850,15 @@ int choose_skip_bins(gbm_ctx *ctx) {
     cudaFree(d_cnt);
     if (rc != GBM_OK) return rc;
     std::vector<int16_t> skip((size_t)ctx->nblk * kBlk, (int16_t)0);
+    ctx->skip_keep.assign((size_t)ctx->p, 1.0);
     for (int f = 0; f < ctx->p; f++) {
         int best = 0;
+        unsigned long long tot = 0;
+        for (int b = 0; b < ctx->counts[f]; b++) tot += cnt[(size_t)f * kBins + b];
         for (int b = 1; b < ctx->counts[f]; b++)
             if (cnt[(size_t)f * kBins + b] > cnt[(size_t)f * kBins + best]) best = b;
         skip[(size_t)f] = (int16_t)best;
+        if (tot) ctx->skip_keep[(size_t)f] = 1.0 - (double)cnt[(size_t)f * kBins + best] / (double)tot;
     }
     TRY(dalloc(ctx, &ctx->d_skipb, skip.size()));
     CK(cudaMemcpyAsync(ctx->d_skipb, skip.data(), sizeof(int16_t) * skip.size(), cudaMemcpyHostToDevice, ctx->st));
@@ -947,6 +959,7 @@ int enqueue_grow(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, bool co
 int replay_on_host(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, HostTree &T) {
     TRY(fetch_nodes(ctx));
     ctx->alg_bytes += (double)(ctx->h_nodes[0].end - ctx->h_nodes[0].begin) * (rf.nf + 8);
+    ctx->hist_updates += (double)(ctx->h_nodes[0].end - ctx->h_nodes[0].begin) * rf.upd_per_row;
     ctx->hist_rows += ctx->h_nodes[0].end;
     auto t_rep = std::chrono::steady_clock::now();
     double sync_before = ctx->host_sync_ms;
@@ -1031,6 +1044,7 @@ int harvest(gbm_ctx *ctx, int si, int nf, const gbm_params *P, gbm_tree_out *out
     const TreeOut &T = *ctx->slot[si].h_tout;
     if (T.status != 0) return fail(ctx, GBM_ERR_STATE, "internal: the device replay reached an unexpanded node");
     ctx->alg_bytes += (double)T.alg_rows * (nf + 8);
+    ctx->hist_updates += (double)T.alg_rows * ctx->slot[si].upd_per_row;
     ctx->hist_rows += T.root_rows;
     write_tree_dev(T, tree_need(P), out);
     if (train_loss) *train_loss = -ctx->slot[si].h_loss[0] / (double)ctx->n_global;
@@ -1592,13 +1606,14 @@ int gbm_get_stats(gbm_ctx *ctx, gbm_stats *out) {
     out->host_sync_ms = ctx->host_sync_ms;
     out->host_replay_ms = ctx->host_replay_ms;
     out->flush_ms = ctx->flush_ms;
+    out->hist_updates = ctx->hist_updates;
     return GBM_OK;
 }
 
 int gbm_reset_stats(gbm_ctx *ctx) {
     if (!ctx) return GBM_ERR_ARG;
     ctx->launches = ctx->hist_launches = ctx->hist_rows = ctx->waves = 0;
-    ctx->hist_ms = ctx->alg_bytes = 0.0;
+    ctx->hist_ms = ctx->alg_bytes = ctx->hist_updates = 0.0;
     ctx->host_sample_ms = ctx->host_sync_ms = ctx->host_replay_ms = ctx->flush_ms = 0.0;
     return GBM_OK;
 }

@@ -232,6 +232,9 @@ typedef struct {
     double host_sync_ms;       /* host time waiting for the device */
     double host_replay_ms;     /* host time in the best-first replay */
     double flush_ms;           /* device time of the gbm_set_l2_flush writes */
+    double hist_updates;       /* histogram cell updates (row x selected feature, skipped bin
+                                  excluded) of the reference's histograms; 6 shared-memory
+                                  atomic adds each */
 } gbm_stats;
 
 int gbm_set_profiling(gbm_ctx *ctx, int32_t on);
