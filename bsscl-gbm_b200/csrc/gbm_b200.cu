@@ -38,6 +38,7 @@
 #include <mutex>
 #include <new>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/gbm_b200.h"
@@ -204,6 +205,28 @@ int fail(gbm_ctx *c, int code, const char *fmt, ...) {
         int r_ = (x);               \
         if (r_ != GBM_OK) return r_;\
     } while (0)
+
+// Kernels of a round are launched with programmatic stream serialization:
+// a kernel may be scheduled while its predecessor drains, and it waits
+// (griddep_wait, its first statement) before reading anything the
+// predecessor wrote.  That hides most of the gap between dependent launches.
+template <typename... P, typename... A>
+int launch(gbm_ctx *ctx, void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A &&...args) {
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    ctx->launches++;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...);
+    if (e != cudaSuccess) return fail(ctx, GBM_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+    return GBM_OK;
+}
 
 template <typename T>
 int dalloc(gbm_ctx *ctx, T **p, size_t count) {
@@ -445,10 +468,9 @@ int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p) {
         ctx->hist_ev_used += 2;
         CK(cudaEventRecord(e0, ctx->st));
     }
-    k_hist<<<ctx->hist_grid, kHistThreads, smem, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask,
+    TRY(launch(ctx, k_hist, dim3(ctx->hist_grid), dim3(kHistThreads), smem, ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask,
                                                            ctx->d_hprefix, ntask_p, ctx->d_blist, d_bwp, nb,
-                                                           ctx->d_fpos, ctx->d_skipb, rf.nf, ctx->d_q, ctx->d_stage);
-    CKL();
+                                                           ctx->d_fpos, ctx->d_skipb, rf.nf, ctx->d_q, ctx->d_stage));
     if (ctx->profiling) CK(cudaEventRecord(e1, ctx->st));
     ctx->hist_launches++;
     return GBM_OK;
@@ -505,16 +527,15 @@ int launch_close(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, bool ro
     PartTask *pt = np.W_ub > 0 ? ctx->d_ptask : nullptr;
     long long *lw = np.W_ub > 0 && np.last ? ctx->d_leafw : nullptr;
     if (root)
-        k_level_close<true><<<1, kCloseThreads, 0, ctx->st>>>(
+        TRY(launch(ctx, k_level_close<true>, dim3(1), dim3(kCloseThreads), 0, ctx->st,
             ctx->d_nodes, nullptr, nullptr, ctx->d_pool, ctx->d_stage, rf.nf, ctx->d_fidx, ctx->d_fbest, ctx->S, next,
             next_cnt, ints(ctx, I_NODES), ctx->nmax, level_cap(P), P->gamma, P->grow_policy == 0, pt,
-            ints(ctx, I_TILES), np.W_ub, lw, ctx->d_nleft);
+            ints(ctx, I_TILES), np.W_ub, lw, ctx->d_nleft));
     else
-        k_level_close<false><<<1, kCloseThreads, 0, ctx->st>>>(
+        TRY(launch(ctx, k_level_close<false>, dim3(1), dim3(kCloseThreads), 0, ctx->st, 
             ctx->d_nodes, lvl, lvl_cnt, ctx->d_pool, ctx->d_stage, rf.nf, ctx->d_fidx, ctx->d_fbest, ctx->S, next,
             next_cnt, ints(ctx, I_NODES), ctx->nmax, level_cap(P), P->gamma, P->grow_policy == 0, pt,
-            ints(ctx, I_TILES), np.W_ub, lw, ctx->d_nleft);
-    CKL();
+            ints(ctx, I_TILES), np.W_ub, lw, ctx->d_nleft));
     return GBM_OK;
 }
 
@@ -524,23 +545,20 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, const Ne
     const int64_t words = slot_words_for(rf.nf);
     const long long *ng = nullptr;
     if (ctx->comm) {
-        k_count64<<<1, 1, 0, ctx->st>>>(ctx->d_total, ctx->d_count64);
-        CKL();
+        TRY(launch(ctx, k_count64, dim3(1), dim3(1), 0, ctx->st, ctx->d_total, ctx->d_count64));
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_count64, 1, ctx->st, ctx->timeout_ms, ctx->err));
         ng = ctx->d_count64;
     }
-    k_root_plan<<<1, 1, 0, ctx->st>>>(ctx->d_total, ng, ctx->d_nodes, ctx->d_htask, ctx->d_hprefix,
-                                      ints(ctx, I_NODES));
-    CKL();
+    TRY(launch(ctx, k_root_plan, dim3(1), dim3(1), 0, ctx->st, ctx->d_total, ng, ctx->d_nodes, ctx->d_htask, ctx->d_hprefix,
+                                      ints(ctx, I_NODES)));
     TRY(launch_hist(ctx, rf, ints(ctx, I_ONE)));
     if (ctx->comm)
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words, ctx->st, ctx->timeout_ms, ctx->err));
     int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
-    k_split_feat<true><<<dim3(fx, 1), 32 * kSplitWarps, 0, ctx->st>>>(
+    TRY(launch(ctx, k_split_feat<true>, dim3(dim3(fx, 1)), dim3(32 * kSplitWarps), 0, ctx->st, 
         ctx->d_nodes, nullptr, nullptr, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx,
         ctx->d_counts, ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight,
-        (long long)P->min_samples_leaf, P->max_depth, pool_depth(P), ctx->d_fbest);
-    CKL();
+        (long long)P->min_samples_leaf, P->max_depth, pool_depth(P), ctx->d_fbest));
     return launch_close(ctx, rf, P, true, nullptr, nullptr, ctx->d_lvl[0], ints(ctx, I_LVL0), np);
 }
 
@@ -555,9 +573,8 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
     if (W_ub <= 0) return GBM_OK;
     const int64_t words = slot_words_for(rf.nf);
     if (!planned) {
-        k_lvl_plan<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ints(ctx, I_NODES), ctx->d_ptask,
-                                           ints(ctx, I_TILES), ctx->nmax, W_ub);
-        CKL();
+        TRY(launch(ctx, k_lvl_plan, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, lvl, lvl_cnt, ints(ctx, I_NODES), ctx->d_ptask,
+                                           ints(ctx, I_TILES), ctx->nmax, W_ub));
     }
     int tiles_ub = (int)((ctx->n + kPartTile - 1) / kPartTile) + W_ub;
     if (tiles_ub > ctx->tile_cap) {
@@ -570,26 +587,22 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
             CK(cudaMemsetAsync(ctx->d_leafw, 0, sizeof(long long) * kLeafWords * W_ub, ctx->st));
             CK(cudaMemsetAsync(ctx->d_nleft, 0, sizeof(long long) * W_ub, ctx->st));
         }
-        k_leaf_totals<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp,
+        TRY(launch(ctx, k_leaf_totals, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp,
                                                               ctx->d_ptask, lvl_cnt,
                                                               ints(ctx, I_TILES), ctx->d_q, ctx->d_leafw,
-                                                              ctx->d_nleft);
-        CKL();
+                                                              ctx->d_nleft));
         if (ctx->comm)
             TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_leafw, (int64_t)kLeafWords * W_ub, ctx->st, ctx->timeout_ms,
                                        ctx->err));
-        k_leaf_finish<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ctx->d_leafw, ctx->d_nleft, ctx->S);
-        CKL();
+        TRY(launch(ctx, k_leaf_finish, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, lvl, lvl_cnt, ctx->d_leafw, ctx->d_nleft, ctx->S));
         ctx->waves++;
         return GBM_OK;
     }
-    k_part_count<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_ptask,
-                                                         lvl_cnt, ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt);
-    CKL();
-    k_part_scatter<<<tiles_ub, kPartThreads, 0, ctx->st>>>(ctx->d_rows, ctx->d_tmp, ctx->d_ptask, lvl_cnt,
+    TRY(launch(ctx, k_part_count, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_ptask,
+                                                         lvl_cnt, ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt));
+    TRY(launch(ctx, k_part_scatter, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, ctx->d_rows, ctx->d_tmp, ctx->d_ptask, lvl_cnt,
                                                            ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt,
-                                                           ctx->d_nleft);
-    CKL();
+                                                           ctx->d_nleft));
     const long long *gl = ctx->d_nleft;
     if (ctx->comm) {
         CK(cudaMemcpyAsync(ctx->d_nleft_g, ctx->d_nleft, sizeof(long long) * W_ub, cudaMemcpyDeviceToDevice,
@@ -597,17 +610,15 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_nleft_g, W_ub, ctx->st, ctx->timeout_ms, ctx->err));
         gl = ctx->d_nleft_g;
     }
-    k_plan_hist<<<1, 256, 0, ctx->st>>>(ctx->d_nodes, lvl, lvl_cnt, ctx->d_nleft, gl, ctx->d_htask, ctx->d_hprefix);
-    CKL();
+    TRY(launch(ctx, k_plan_hist, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, lvl, lvl_cnt, ctx->d_nleft, gl, ctx->d_htask, ctx->d_hprefix));
     TRY(launch_hist(ctx, rf, lvl_cnt));
     if (ctx->comm)
         TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words * W_ub, ctx->st, ctx->timeout_ms, ctx->err));
     int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
-    k_split_feat<false><<<dim3(fx, W_ub), 32 * kSplitWarps, 0, ctx->st>>>(
+    TRY(launch(ctx, k_split_feat<false>, dim3(dim3(fx, W_ub)), dim3(32 * kSplitWarps), 0, ctx->st, 
         ctx->d_nodes, lvl, lvl_cnt, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx, ctx->d_counts,
         ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight, (long long)P->min_samples_leaf, P->max_depth,
-        pool_depth(P), ctx->d_fbest);
-    CKL();
+        pool_depth(P), ctx->d_fbest));
     TRY(launch_close(ctx, rf, P, false, lvl, lvl_cnt, next, next_cnt, next ? np : NextPlan()));
     ctx->waves++;
     return GBM_OK;
@@ -916,12 +927,9 @@ int tree_need(const gbm_params *P) {
 // In-bag mask -> ascending row list of the root (row buffer 0) and its count.
 int enqueue_compaction(gbm_ctx *ctx, cudaStream_t s) {
     int ntile = (int)((ctx->n + kCompTile - 1) / kCompTile);
-    k_comp_count<<<ntile, 256, 0, s>>>(ctx->d_mask, ctx->n, ctx->d_cnt);
-    CKL();
-    k_scan_small<<<1, 1024, 0, s>>>(ctx->d_cnt, ntile, ctx->d_off, ctx->d_total);
-    CKL();
-    k_comp_scatter<<<ntile, 256, 0, s>>>(ctx->d_mask, ctx->n, ctx->d_off, ctx->d_rows);
-    CKL();
+    TRY(launch(ctx, k_comp_count, dim3(ntile), dim3(256), 0, s, ctx->d_mask, ctx->n, ctx->d_cnt));
+    TRY(launch(ctx, k_scan_small, dim3(1), dim3(1024), 0, s, ctx->d_cnt, ntile, ctx->d_off, ctx->d_total));
+    TRY(launch(ctx, k_comp_scatter, dim3(ntile), dim3(256), 0, s, ctx->d_mask, ctx->n, ctx->d_off, ctx->d_rows));
     return GBM_OK;
 }
 
@@ -994,12 +1002,11 @@ int enqueue_replay(gbm_ctx *ctx, const gbm_params *P) {
     R.has_mono = P->monotone != nullptr;
     size_t smem = sizeof(RNode) * (size_t)ctx->nmax;
     if (P->grow_policy == 0)
-        k_replay_leaf<<<1, kReplayLoaders, smem, ctx->st>>>(ctx->d_nodes, ints(ctx, I_NODES), R, ctx->d_mono, ctx->d_tout,
-                                                ctx->d_tree);
+        TRY(launch(ctx, k_replay_leaf, dim3(1), dim3(kReplayLoaders), smem, ctx->st, ctx->d_nodes, ints(ctx, I_NODES), R,
+                   ctx->d_mono, ctx->d_tout, ctx->d_tree));
     else
-        k_replay_depth<<<1, kReplayLoaders, smem, ctx->st>>>(ctx->d_nodes, ints(ctx, I_NODES), R, ctx->d_mono, ctx->d_tout,
-                                                 ctx->d_tree);
-    CKL();
+        TRY(launch(ctx, k_replay_depth, dim3(1), dim3(kReplayLoaders), smem, ctx->st, ctx->d_nodes, ints(ctx, I_NODES), R, ctx->d_mono, ctx->d_tout,
+                                                 ctx->d_tree));
     return GBM_OK;
 }
 
@@ -1007,12 +1014,10 @@ int enqueue_replay(gbm_ctx *ctx, const gbm_params *P) {
 // in d_tree; the loss goes to the slot's pinned buffer.
 int enqueue_update(gbm_ctx *ctx, const gbm_params *P, bool want_leaf, double *h_loss) {
     double scale = std::ldexp(1.0, ctx->S);
-    k_update<<<ctx->upd_blocks, kUpdThreads, 0, ctx->st>>>(
+    TRY(launch(ctx, k_update, dim3(ctx->upd_blocks), dim3(kUpdThreads), 0, ctx->st, 
         ctx->d_tree, ctx->d_xb, ctx->n, ctx->d_y, ctx->w[0], ctx->w[1], P->learning_rate, scale, ctx->d_F,
-        ctx->d_q, want_leaf ? ctx->d_leaf : nullptr, ctx->d_loss_part);
-    CKL();
-    k_sum_partials<<<1, 256, 0, ctx->st>>>(ctx->d_loss_part, ctx->upd_blocks, ctx->d_loss);
-    CKL();
+        ctx->d_q, want_leaf ? ctx->d_leaf : nullptr, ctx->d_loss_part));
+    TRY(launch(ctx, k_sum_partials, dim3(1), dim3(256), 0, ctx->st, ctx->d_loss_part, ctx->upd_blocks, ctx->d_loss));
     if (ctx->comm) TRY(gbm_comm_allreduce_f64(ctx->comm, ctx->d_loss, 1, ctx->st, ctx->timeout_ms, ctx->err));
     CK(cudaMemcpyAsync(h_loss, ctx->d_loss, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
     return GBM_OK;
@@ -1113,20 +1118,16 @@ int stage_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset)
         pout = ctx->d_perm[r % R1];
         CK(cudaMemcpyAsync(s.d_tg, s.h_tg, sizeof(int32_t) * (size_t)(N - 1), cudaMemcpyHostToDevice, ctx->cst));
         CK(cudaMemsetAsync(ctx->d_head, 0xff, sizeof(int32_t) * (size_t)N, ctx->cst));
-        k_shuf_link<<<grid_for(N - 1, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_head, ctx->d_nxt);
-        CKL();
-        k_shuf_min<<<grid_for(N, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp);
-        CKL();
-        k_shuf_compose<<<grid_for(N, 256), 256, 0, ctx->cst>>>(s.d_tg, N, ctx->d_m, ctx->d_mp, pin, pout);
-        CKL();
+        TRY(launch(ctx, k_shuf_link, dim3(grid_for(N - 1, 256)), dim3(256), 0, ctx->cst, s.d_tg, N, ctx->d_head, ctx->d_nxt));
+        TRY(launch(ctx, k_shuf_min, dim3(grid_for(N, 256)), dim3(256), 0, ctx->cst, s.d_tg, N, ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp));
+        TRY(launch(ctx, k_shuf_compose, dim3(grid_for(N, 256)), dim3(256), 0, ctx->cst, s.d_tg, N, ctx->d_m, ctx->d_mp, pin, pout));
     }
     // mask and root row list on this stream too, once the previous round has
     // finished with the row lists (it is at its replay or F update by then)
     CK(cudaStreamWaitEvent(ctx->cst, ctx->rows_free, 0));
     if (rows_on) {
         CK(cudaMemsetAsync(ctx->d_mask, 0, (size_t)ctx->n, ctx->cst));
-        k_mask_from_rows<<<grid_for(m, 256), 256, 0, ctx->cst>>>(pout, m, row_offset, ctx->n, ctx->d_mask);
-        CKL();
+        TRY(launch(ctx, k_mask_from_rows, dim3(grid_for(m, 256)), dim3(256), 0, ctx->cst, pout, m, row_offset, ctx->n, ctx->d_mask));
     } else {   // sample_idx is every row (E:2508-2509)
         CK(cudaMemsetAsync(ctx->d_mask, 1, (size_t)ctx->n, ctx->cst));
     }

@@ -14,6 +14,11 @@ namespace gbm {
 
 // Row-major uint8 [rows][p] -> column blocks [nblk][n][16], ids clamped to
 // bin_count-1 (E:593-594 clamps the same way; E:604 never splits above).
+// A kernel launched with programmatic stream serialization may start while
+// its predecessor drains; this waits until the predecessor has finished and
+// its writes are visible (a no-op for a plain launch).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 template <typename T>
 __global__ void k_pack_bins(const T *__restrict__ src, int64_t rows, int p, int64_t row0,
                             int64_t n, int nblk, const int32_t *__restrict__ counts,
@@ -96,6 +101,7 @@ k_update(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64
          const uint8_t *__restrict__ y, double w0, double w1, double lr, double scale,
          double *__restrict__ F, longlong2 *__restrict__ q, int32_t *__restrict__ leaf_out,
          double *__restrict__ loss_part) {
+    griddep_wait();
     __shared__ int s_feat[256], s_thr[256], s_left[256], s_right[256];
     __shared__ double s_val[256];
     __shared__ double s_red[kUpdThreads / 32];
@@ -138,6 +144,7 @@ k_update(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64
 
 // Fixed-order sum of the per-block loss partials (deterministic).
 __global__ void k_sum_partials(const double *__restrict__ part, int m, double *__restrict__ out) {
+    griddep_wait();
     __shared__ double s[256];
     double a = 0.0;
     for (int k = threadIdx.x; k < m; k += blockDim.x) a += part[k];
@@ -155,6 +162,7 @@ __global__ void k_sum_partials(const double *__restrict__ part, int m, double *_
 // ===========================================================================
 
 __global__ void k_comp_count(const uint8_t *__restrict__ mask, int64_t n, int32_t *__restrict__ cnt) {
+    griddep_wait();
     __shared__ int s[32];
     int64_t base = (int64_t)blockIdx.x * kCompTile;
     int c = 0;
@@ -175,6 +183,7 @@ __global__ void k_comp_count(const uint8_t *__restrict__ mask, int64_t n, int32_
 // Exclusive scan of m ints by one CTA; *total = sum.
 __global__ void k_scan_small(const int32_t *__restrict__ in, int m, int32_t *__restrict__ out,
                              int32_t *__restrict__ total) {
+    griddep_wait();
     __shared__ int s_w[32];
     int carry = 0;
     for (int base = 0; base < m; base += blockDim.x) {
@@ -190,6 +199,7 @@ __global__ void k_scan_small(const int32_t *__restrict__ in, int m, int32_t *__r
 
 __global__ void k_comp_scatter(const uint8_t *__restrict__ mask, int64_t n, const int32_t *__restrict__ off,
                                int32_t *__restrict__ rows) {
+    griddep_wait();
     __shared__ int s_w[32];
     int64_t base = (int64_t)blockIdx.x * kCompTile;
     int carry = off[blockIdx.x];
@@ -206,6 +216,7 @@ __global__ void k_comp_scatter(const uint8_t *__restrict__ mask, int64_t n, cons
 // In-bag mask of this rank's rows [row0, row0 + n) from global row ids.
 __global__ void k_mask_from_rows(const int32_t *__restrict__ rows, int64_t m, int64_t row0, int64_t n,
                                  uint8_t *__restrict__ mask) {
+    griddep_wait();
     int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (k >= m) return;
     int64_t r = (int64_t)rows[k] - row0;
@@ -227,6 +238,7 @@ __global__ void k_mask_from_rows(const int32_t *__restrict__ rows, int64_t m, in
 // Bucket the steps by target: a singly linked list per position.
 __global__ void k_shuf_link(const int32_t *__restrict__ t, int64_t n, int32_t *__restrict__ head,
                             int32_t *__restrict__ nxt) {
+    griddep_wait();
     int64_t i = 1 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     int q = t[n - 1 - i];
@@ -243,6 +255,7 @@ __device__ __forceinline__ int32_t min_above(const int32_t *__restrict__ head, c
 
 __global__ void k_shuf_min(const int32_t *__restrict__ t, int64_t n, const int32_t *__restrict__ head,
                            const int32_t *__restrict__ nxt, int32_t *__restrict__ m, int32_t *__restrict__ mp) {
+    griddep_wait();
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     m[i] = min_above(head, nxt, (int)i, i);
@@ -253,6 +266,7 @@ __global__ void k_shuf_min(const int32_t *__restrict__ t, int64_t n, const int32
 __global__ void k_shuf_compose(const int32_t *__restrict__ t, int64_t n, const int32_t *__restrict__ m,
                                const int32_t *__restrict__ mp, const int32_t *__restrict__ perm_in,
                                int32_t *__restrict__ perm_out) {
+    griddep_wait();
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     int32_t src = i == 0 ? m[0] : mp[i];
@@ -273,6 +287,7 @@ __global__ void k_iota(int32_t *__restrict__ a, int64_t n) {
 }
 
 __global__ void k_count64(const int32_t *__restrict__ in, long long *__restrict__ out) {
+    griddep_wait();
     if (threadIdx.x == 0 && blockIdx.x == 0) *out = *in;
 }
 
@@ -308,6 +323,7 @@ k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ ro
        const int *__restrict__ ntask_p, const int32_t *__restrict__ blist, const int32_t *__restrict__ bwp,
        int nb, const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
        const longlong2 *__restrict__ q, long long *__restrict__ stage_hist) {
+    griddep_wait();
     extern __shared__ unsigned acc[];   // [6][16][256]
     __shared__ long long s_tot[2][kHistThreads / 32];
     const int ntask = *ntask_p;
@@ -465,6 +481,7 @@ __device__ __forceinline__ DNode fresh_node(int depth, int parent) {
 __global__ void k_root_plan(const int32_t *__restrict__ n_local, const long long *__restrict__ n_global,
                             DNode *__restrict__ nodes, HistTask *__restrict__ ht,
                             int32_t *__restrict__ prefix, int *__restrict__ node_count) {
+    griddep_wait();
     if (threadIdx.x || blockIdx.x) return;
     long long ns = *n_local;
     DNode d = fresh_node(0, -1);
@@ -492,6 +509,7 @@ __global__ void k_root_plan(const int32_t *__restrict__ n_local, const long long
 __global__ void k_lvl_plan(DNode *__restrict__ nodes, const int *__restrict__ lvl, int *__restrict__ lvl_count,
                            int *__restrict__ node_count, PartTask *__restrict__ pt,
                            int *__restrict__ tiles_total, int nmax, int w_max) {
+    griddep_wait();
     __shared__ int s_w[32];
     __shared__ int s_W, s_base;
     if (threadIdx.x == 0) {
@@ -562,6 +580,7 @@ __global__ void __launch_bounds__(kPartThreads)
 k_part_count(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
              const int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
              const int *__restrict__ tiles_total, unsigned *__restrict__ side, int32_t *__restrict__ tile_cnt) {
+    griddep_wait();
     __shared__ int s[kPartThreads / 32];
     const int tile = blockIdx.x;
     if (tile >= *tiles_total) return;
@@ -605,6 +624,7 @@ k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, c
                const int *__restrict__ ntask_p, const int *__restrict__ tiles_total,
                const unsigned *__restrict__ side, const int32_t *__restrict__ tile_cnt,
                long long *__restrict__ n_left) {
+    griddep_wait();
     __shared__ int s_l[kPartThreads / 32], s_a[kPartThreads / 32], s_b[kPartThreads / 32];
     const int tile = blockIdx.x;
     if (tile >= *tiles_total) return;
@@ -670,6 +690,7 @@ __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ l
                             const int *__restrict__ lvl_count, const long long *__restrict__ nl_local,
                             const long long *__restrict__ gl, HistTask *__restrict__ ht,
                             int32_t *__restrict__ prefix) {
+    griddep_wait();
     __shared__ int s_w[32];
     const int W = *lvl_count;
     int carry = 0;
@@ -721,6 +742,7 @@ k_leaf_totals(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restri
               const int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
               const int *__restrict__ tiles_total, const longlong2 *__restrict__ q,
               long long *__restrict__ words, long long *__restrict__ n_left) {
+    griddep_wait();
     __shared__ long long s[5][kPartThreads / 32];
     const int tile = blockIdx.x;
     if (tile >= *tiles_total) return;
@@ -773,6 +795,7 @@ k_leaf_totals(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restri
 __global__ void k_leaf_finish(DNode *__restrict__ nodes, const int *__restrict__ lvl,
                               const int *__restrict__ lvl_count, const long long *__restrict__ words,
                               const long long *__restrict__ nl_local, int S) {
+    griddep_wait();
     const int W = *lvl_count;
     const double sc = pow2(-S);
     for (int k = threadIdx.x; k < W; k += blockDim.x) {
@@ -893,6 +916,7 @@ k_split_feat(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
              int nf, const int32_t *__restrict__ fidx, const int32_t *__restrict__ counts,
              const int16_t *__restrict__ skipb, int S, double lam, double mcw, long long msl, int max_depth,
              int pool_depth, FBest *__restrict__ fbest) {
+    griddep_wait();
     const int k = blockIdx.y;
     if (!ROOT && k >= *lvl_count) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1009,6 +1033,7 @@ k_level_close(DNode *__restrict__ nodes, const int *__restrict__ lvl, const int 
               int *__restrict__ next, int *__restrict__ next_count, int *__restrict__ node_count, int nmax, int M,
               double gamma, int use_gamma, PartTask *__restrict__ pt, int *__restrict__ tiles_total, int w_max,
               long long *__restrict__ leafw, long long *__restrict__ nleft) {
+    griddep_wait();
     __shared__ double s_g[1024];
     __shared__ int s_id[1024];
     __shared__ int s_cnt, s_W, s_base;
@@ -1245,6 +1270,7 @@ __device__ __forceinline__ unsigned long long order_key(double d) {
 __global__ void __launch_bounds__(kReplayLoaders)
 k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_count, RParams P,
               const int *__restrict__ mono, TreeOut *__restrict__ out, TreeDev *__restrict__ td) {
+    griddep_wait();
     extern __shared__ RNode sn[];
     __shared__ int c_node[kReplayMaxC], c_nid[kReplayMaxC];
     __shared__ int tf[256], tl[256], tr[256];
@@ -1358,6 +1384,7 @@ k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_coun
 __global__ void __launch_bounds__(kReplayLoaders)
 k_replay_depth(const DNode *__restrict__ nodes, const int *__restrict__ node_count, RParams P,
                const int *__restrict__ mono, TreeOut *__restrict__ out, TreeDev *__restrict__ td) {
+    griddep_wait();
     extern __shared__ RNode sn[];
     __shared__ int tf[256], tl[256], tr[256];
     __shared__ long long tt[256];
