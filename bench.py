@@ -39,15 +39,32 @@ for _p in (os.path.join(ROOT, "bsscl-gbm_b200"), os.path.join(ROOT, "oracle")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-METRIC = "boosting rounds/sec at 1M x 100 depth 6"
-CFG = dict(n=1_000_000, max_depth=6, max_leaves=63, lr=0.08, subsample=0.75, colsample=0.7,
-           mcw=3.0, lam=1.0, msl=5, class_weight="balanced_sqrt", seed=0)
+CONFIGS = {
+    # the headline: BASELINE's metric (1M x 100 at depth 6) on configs[3]'s data
+    "4": dict(n=1_000_000, p=100, max_depth=6, max_leaves=63, lr=0.08, subsample=0.75, colsample=0.7,
+              mcw=3.0, lam=1.0, msl=5, class_weight="balanced_sqrt", seed=0,
+              metric="boosting rounds/sec at 1M x 100 depth 6",
+              workload="config4 1M x 100 f32 30% NaN, depth 6, 63 leaves",
+              data="synthetic (config 4 stand-in, seed 3)", cpu_rows=None),
+    # the box-scale case (training part) for the scaling study
+    "5": dict(n=10_000_000, p=200, max_depth=10, max_leaves=63, lr=0.08, subsample=0.5, colsample=0.7,
+              mcw=3.0, lam=5.0, msl=5, class_weight="balanced_sqrt", seed=0,
+              metric="boosting rounds/sec at 10M x 200 depth 10",
+              workload="config5 10M x 200 pre-binned uint8 U{1..254} + 10% NaN bin, depth 10, 63 leaves",
+              data="synthetic (config 5 stand-in, seed 5)", cpu_rows=1_000_000),
+}
+CFG = CONFIGS["4"]
+METRIC = CFG["metric"]
 
 
-def workload(n):
-    """config 4 data, binned exactly as the reference bins it."""
+def workload(cfg, rows=None):
+    """(X_bin, y, counts): config 4's data binned exactly as the reference bins
+    it (all rows), or config 5's pre-binned rows `rows` (default all)."""
     from bsscl_gbm_b200 import binning, datasets
-    X, y = datasets.config4(n=n)
+    if cfg is CONFIGS["5"]:
+        Xb, y = datasets.config5_bins(n=cfg["n"], p=cfg["p"], rows=rows)
+        return Xb, y, np.full(cfg["p"], 256, np.int32)
+    X, y = datasets.config4(n=cfg["n"])
     edges, counts, nanb = binning.build_bin_edges(X, 255)
     Xb = binning.bin_features(X, edges, counts, nanb)
     return Xb, y, counts
@@ -179,7 +196,8 @@ def measured_peak_hbm():
 
 
 def cpu_rounds(Xb, y, counts, rounds, warmup=1, budget_s=None):
-    """The reference's loop on the CPU oracle (REF mode): rounds/s."""
+    """The reference's loop on the CPU oracle (REF mode): rounds/s of the
+    given rows."""
     import oracle as O
     c = CFG
     kw = dict(learning_rate=c["lr"], max_leaves=c["max_leaves"], max_depth=c["max_depth"],
@@ -205,8 +223,10 @@ def run_reference(args):
     if rank != 0:
         return
     import oracle as O
-    Xb, y, counts = workload(CFG["n"])
     c = CFG
+    m = c["cpu_rows"] or c["n"]
+    Xb, y, counts = workload(c, rows=(0, m))
+    y = y[:m]
     kw = dict(learning_rate=c["lr"], max_leaves=c["max_leaves"], max_depth=c["max_depth"],
               min_samples_leaf=c["msl"], min_child_weight=c["mcw"], reg_lambda=c["lam"],
               gamma=0.0, subsample=c["subsample"], colsample=c["colsample"],
@@ -215,17 +235,20 @@ def run_reference(args):
     t0 = time.perf_counter()
     O.fit_binary(Xb, y, counts, n_estimators=args.steps, **kw)
     el = time.perf_counter() - t0
-    v = args.steps / el
+    # a row sample's rounds/s scaled to the full row count (a round's work is linear in rows)
+    v = args.steps / el * (m / c["n"])
+    sample = (f"{args.steps} rounds of the full workload" if m == c["n"] else
+              f"{args.steps} rounds on the first {m:,} of {c['n']:,} rows, rounds/s scaled by {m / c['n']:g}")
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "rounds/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000 * el / args.steps, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f64", "data": "synthetic (config 4 stand-in, seed 3)",
-        "config": {"workload": "config4 1M x 100 f32 30% NaN, depth 6, 63 leaves", "n_rows": CFG["n"],
-                   "n_features": 100, "max_depth": 6, "max_leaves": 63, "subsample": 0.75,
-                   "colsample": 0.7},
+        "ms_per_step": 1000 / v, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f64", "data": c["data"],
+        "config": {"workload": c["workload"], "n_rows": c["n"], "n_features": c["p"],
+                   "max_depth": c["max_depth"], "max_leaves": c["max_leaves"], "subsample": c["subsample"],
+                   "colsample": c["colsample"]},
         "cpu_baseline": {"value": v, "unit": "rounds/s", "cores": O.num_threads(), "kind": "port",
-                         "sample": f"{args.steps} rounds of the full workload"},
+                         "sample": sample},
         "e2e": {"value": v, "unit": "rounds/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -248,19 +271,22 @@ def run_engine(args):
                                 device_id=torch.device("cuda", local))
     c = CFG
     n = c["n"]
-    Xb, y, counts = workload(n)
-    p = Xb.shape[1]
     lo, hi = (n * rank) // world, (n * (rank + 1)) // world
+    five = c is CONFIGS["5"]
+    # config 5: each rank makes only its rows (2 GB per 10M x 200); config 4: all rows
+    Xb, y, counts = workload(c, rows=(lo, hi) if five else None)
+    Xl = Xb if five else Xb[lo:hi]            # this rank's rows
+    p = Xb.shape[1]
     w2 = O.class_weights(y, c["class_weight"])
     base = O.base_score(y, w2)
-    Xd = binning.device_bins(Xb, counts)
+    Xd = binning.device_bins(Xl, counts)
 
     eng = Engine(local)
     if world > 1:
         uid = [Engine.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         eng.init_comm(uid[0], world, rank, timeout_ms=120000)
-    eng.upload_bins(Xd[lo:hi], counts)
+    eng.upload_bins(Xl, counts)
     eng.upload_labels(y[lo:hi].astype(np.uint8), w2, base, n_global=n)
     prm = GbmParams(c["lam"], 0.0, c["mcw"], c["lr"], c["msl"], c["max_depth"], c["max_leaves"], 0,
                     None)
@@ -299,28 +325,30 @@ def run_engine(args):
         total_ms = float(t.item())
     value = args.steps / (total_ms / 1000.0)
 
-    # ---- configs[3] literally: the same data at max_depth 8 -----------------------
-    prm8 = GbmParams(c["lam"], 0.0, c["mcw"], c["lr"], c["msl"], 8, c["max_leaves"], 0, None)
-    s8 = Sampler(c["seed"], n, p, n_sub, n_feat, True, True, look_ahead=3)
-    eng.upload_labels(y[lo:hi].astype(np.uint8), w2, base, n_global=n)
-    eng.fit_rounds(s8, lo, prm8, cap, args.warmup)
-    if dist is not None:
-        dist.barrier()
-    eng.reset_stats()
-    eng.set_profiling(True)
-    eng.event(6)
-    eng.fit_rounds(s8, lo, prm8, cap, args.steps)
-    eng.event(7)
-    eng.sync()
-    st8 = eng.stats()
-    eng.set_profiling(False)
+    # ---- configs[3] literally: the same data at max_depth 8 (config 4 only) -------
+    d8_ms = None
+    if not five:
+        prm8 = GbmParams(c["lam"], 0.0, c["mcw"], c["lr"], c["msl"], 8, c["max_leaves"], 0, None)
+        s8 = Sampler(c["seed"], n, p, n_sub, n_feat, True, True, look_ahead=3)
+        eng.upload_labels(y[lo:hi].astype(np.uint8), w2, base, n_global=n)
+        eng.fit_rounds(s8, lo, prm8, cap, args.warmup)
+        if dist is not None:
+            dist.barrier()
+        eng.reset_stats()
+        eng.set_profiling(True)
+        eng.event(6)
+        eng.fit_rounds(s8, lo, prm8, cap, args.steps)
+        eng.event(7)
+        eng.sync()
+        st8 = eng.stats()
+        eng.set_profiling(False)
+        d8_ms = eng.elapsed_ms(6, 7) - st8["flush_ms"]
+        if dist is not None:
+            t = torch.tensor([d8_ms], device=f"cuda:{local}", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            d8_ms = float(t.item())
+        s8.close()
     eng.set_l2_flush(0)
-    d8_ms = eng.elapsed_ms(6, 7) - st8["flush_ms"]
-    if dist is not None:
-        t = torch.tensor([d8_ms], device=f"cuda:{local}", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        d8_ms = float(t.item())
-    s8.close()
 
     # ---- e2e: the public estimator API from host arrays ----------------------
     m = HybridHistGBMNumbaV1_0_1(n_estimators=args.steps, max_depth=c["max_depth"],
@@ -330,24 +358,26 @@ def run_engine(args):
                                  random_state=c["seed"], verbose=False)
     m.max_leaves = c["max_leaves"]
     m._engine, m._engine_dev = eng, local
-    if dist is not None:
-        dist.barrier()
-    eng.event(2)
-    t0 = time.perf_counter()
-    m.fit_binned(Xb, y, counts)
-    eng.event(3)
-    e2e_ms = eng.elapsed_ms(2, 3)
-    if dist is not None:
-        t = torch.tensor([e2e_ms], device=f"cuda:{local}", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e = args.steps / (e2e_ms / 1000.0)
+    e2e = None
+    if not (five and world > 1):   # the estimator takes every row on every rank
+        if dist is not None:
+            dist.barrier()
+        eng.event(2)
+        m.fit_binned(Xb, y, counts)
+        eng.event(3)
+        e2e_ms = eng.elapsed_ms(2, 3)
+        if dist is not None:
+            t = torch.tensor([e2e_ms], device=f"cuda:{local}", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = args.steps / (e2e_ms / 1000.0)
     rows = hi - lo
     nblk = (p + 15) // 16
-    # once per fit: uint16 bins, labels, initial F, bin counts; every round:
-    # the global row sample and the feature tables
-    once = rows * p * 2 + rows + 8 * rows + 4 * p
-    per_round = 4 * n_sub + 4 * n_feat + 2 * 16 * nblk + 4 * nblk
+    # once per fit: bins (uint16 for config 4, uint8 for config 5), labels,
+    # initial F, bin counts; every round: the global row sample's swap
+    # targets and the feature tables
+    once = rows * p * Xb.itemsize + rows + 8 * rows + 4 * p
+    per_round = 4 * (n - 1) + 4 * n_feat + 2 * 16 * nblk + 4 * nblk
     h2d = once / args.steps + per_round
     d2h = 9240 + 8                          # the tree record and the loss
 
@@ -355,7 +385,7 @@ def run_engine(args):
     from bsscl_gbm_b200 import datasets
     ens = datasets.config5_ensemble(n_trees=1000, depth=8, p=p, seed=5)
     eng.predict_set_model(ens, 1000, p)
-    eng.predict_upload(Xd[lo:hi])
+    eng.predict_upload(Xd)
     eng.predict_run(c["lr"], base)
     eng.sync()
     eng.event(4)
@@ -372,7 +402,7 @@ def run_engine(args):
 
     peak, peak_kind = measured_peak_hbm()
     achieved = (st["hist_alg_bytes"] / (st["hist_ms"] / 1000.0)) / 1e9 if st["hist_ms"] > 0 else 0.0
-    traffic = profile_json("k_hist_config4_1M_traffic.md")
+    traffic = None if five else profile_json("k_hist_config4_1M_traffic.md")
     atom_peak = profile_json("smem_atomic_peak_b200.md")
     atomics = None
     if st["hist_ms"] > 0:
@@ -384,16 +414,20 @@ def run_engine(args):
                    "source": "profiles/smem_atomic_peak_b200.md (microbenchmark of k_hist's access pattern)"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v_cpu, done, cores = cpu_rounds(Xb, y, counts, rounds=50, warmup=1, budget_s=20.0)
+        mr = c["cpu_rows"] or n
+        v_cpu, done, cores = cpu_rounds(Xb[:mr], y[:mr], counts, rounds=50, warmup=1, budget_s=20.0)
+        v_cpu *= mr / n
         cpu = {"value": v_cpu, "unit": "rounds/s", "cores": cores, "kind": "port",
-               "sample": f"{done} rounds of the full workload on the CPU oracle (REF mode)"}
+               "sample": (f"{done} rounds of the full workload on the CPU oracle (REF mode)" if mr == n else
+                          f"{done} rounds on the first {mr:,} of {n:,} rows on the CPU oracle (REF mode), "
+                          f"rounds/s scaled by {mr / n:g}")}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "rounds/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
-            "data": "synthetic (config 4 stand-in, seed 3)",
-            "config": {"workload": "config4 1M x 100 f32 30% NaN, depth 6, 63 leaves",
+            "data": c["data"],
+            "config": {"workload": c["workload"],
                        "n_rows": n, "n_features": p, "max_depth": c["max_depth"],
                        "max_leaves": c["max_leaves"], "subsample": c["subsample"],
                        "colsample": c["colsample"], "parallelism": f"rows sharded x{world}",
@@ -416,15 +450,18 @@ def run_engine(args):
                 "host_replay": st["host_replay_ms"] / args.steps,
                 "l2_flush_excluded": st["flush_ms"] / args.steps,
                 "waves": st["waves"] / args.steps},
-            "e2e": {"value": e2e, "unit": "rounds/s", "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(d2h)},
+            "e2e": ({"value": e2e, "unit": "rounds/s", "h2d_bytes_per_step": int(h2d),
+                     "d2h_bytes_per_step": int(d2h)} if e2e is not None else
+                    {"value": None, "note": "the estimator takes every row on every rank; config 5 ranks "
+                                            "hold only their own rows"}),
             "gpu_launches": st["kernel_launches"],
             "predict": {"rows_per_s": pred_rows_s, "node_visits_per_s": pred_rows_s * 1000 * 8,
-                        "ensemble": "1000 full depth-8 random trees (config 5 ensemble, p=100)"},
+                        "ensemble": f"1000 full depth-8 random trees (config 5 ensemble, p={p})"},
             "train_loss_last": losses[-1] if losses else None,
-            "config4_depth8": {"value": args.steps / (d8_ms / 1000.0), "unit": "rounds/s",
-                               "ms_per_step": d8_ms / args.steps,
-                               "config": "BASELINE configs[3] literally: same data, max_depth 8, 63 leaves"},
+            "config4_depth8": ({"value": args.steps / (d8_ms / 1000.0), "unit": "rounds/s",
+                                "ms_per_step": d8_ms / args.steps,
+                                "config": "BASELINE configs[3] literally: same data, max_depth 8, 63 leaves"}
+                               if d8_ms else None),
             "clocks": clk,
             "cpu_baseline": cpu,
         }
@@ -442,8 +479,13 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    ap.add_argument("--config", default="4", choices=sorted(CONFIGS),
+                    help="4 (default): the headline, 1M x 100 depth 6; 5: 10M x 200 depth 10")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    global CFG, METRIC
+    CFG = CONFIGS[args.config]
+    METRIC = CFG["metric"]
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -107,17 +107,26 @@ def config4(n=1_000_000, seed=3, nan_frac=0.30, positive_rate=0.01):
     return X, y
 
 
-def config5_bins(n=10_000_000, p=200, seed=5, nan_frac=0.10, positive_rate=0.05):
+def config5_bins(n=10_000_000, p=200, seed=5, nan_frac=0.10, positive_rate=0.05, rows=None):
     """Config 5: pre-binned uint8 matrix ~ U{1..254} with 10 % NaN-bin (0) entries.
 
-    Returns ``(X_bin uint8 [n, p] row-major, y int64 [n])``.  Every feature
+    Returns ``(X_bin uint8 [m, p] row-major, y int64 [n])`` where X_bin holds
+    rows ``rows = (lo, hi)`` (default: all n) and y is always every row's
+    label.  Rows are made in blocks of 2^20 from their own seeds, so any row
+    range is the same data whichever process makes it.  Every feature
     carries a NaN bin, so each has 256 bin ids (0 = NaN, 1..255 numeric).
     """
-    rng = np.random.default_rng(seed)
-    Xb = rng.integers(1, 255, size=(n, p), dtype=np.uint8)
-    nanm = rng.random((n, p), dtype=np.float32) < nan_frac
-    Xb[nanm] = 0
-    y = (rng.random(n) < positive_rate).astype(np.int64)
+    lo, hi = rows if rows is not None else (0, n)
+    blk = 1 << 20
+    Xb = np.empty((hi - lo, p), dtype=np.uint8)
+    for b0 in range((lo // blk) * blk, hi, blk):
+        r = np.random.default_rng([seed, b0 // blk])
+        m = min(blk, n - b0)
+        xb = r.integers(1, 255, size=(m, p), dtype=np.uint8)
+        xb[r.random((m, p), dtype=np.float32) < nan_frac] = 0
+        a, z = max(lo, b0), min(hi, b0 + m)
+        Xb[a - lo:z - lo] = xb[a - b0:z - b0]
+    y = (np.random.default_rng([seed, 1 << 30]).random(n) < positive_rate).astype(np.int64)
     return Xb, y
 
 

@@ -382,7 +382,7 @@ int setup_features(gbm_ctx *ctx, int si, const int32_t *fidx, int nf, RoundFeat 
 // device with no host round trip.  Deeper best-first trees use M =
 // max_leaves - 1 (no tree uses more splits) and expand on demand what the
 // ranking left out.
-constexpr int kSpecDepth = 9;
+constexpr int kSpecDepth = 10;
 constexpr int kReplaySmemMax = 160 * 1024;   // node table copy of the replay kernels
 
 bool full_spec(const gbm_params *P) { return P->grow_policy == 1 || P->max_depth <= kSpecDepth; }

@@ -146,7 +146,7 @@ int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, co
  * _fit_binary (E:2849-2905): outs[r] and train_loss[r] get round r's tree
  * and loss, identical to calling gbm_round_sampled n_rounds times.  When
  * the tree is replayed on the device (depth-wise growth, or best-first with
- * max_depth <= 9) the rounds are queued back to back with no host wait in
+ * max_depth <= 10) the rounds are queued back to back with no host wait in
  * between (up to 4 in flight); otherwise, or when any outs[r].leaf_of_row
  * is set, the rounds run one by one. */
 int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *params,

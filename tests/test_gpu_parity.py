@@ -69,11 +69,13 @@ def test_build_tree_matches_oracle_exact(engine, case):
     assert np.abs(t[2][:nc] - d["tv"][:nc]).max() <= 1e-9
 
 
+@pytest.mark.parametrize("depth", [10, 14])
 @pytest.mark.parametrize("case", ["basic", "few_bins", "tied", "nan_heavy", "leaves4"])
-def test_build_tree_host_replay_matches_oracle_exact(engine, case):
-    """Best-first trees deeper than 9 levels rank each level's expansions
-    (capped at max_leaves - 1) and are replayed on the host, expanding on
-    demand what the ranking left out: the same bit-exact bar."""
+def test_build_tree_deep_matches_oracle_exact(engine, case, depth):
+    """Depth 10 expands every level in full (512 parents at the last split
+    level) and replays on the device; depth 14 ranks each level's
+    expansions (capped at max_leaves - 1) and replays on the host, expanding
+    on demand what the ranking left out.  The same bit-exact bar."""
     from bsscl_gbm_b200 import binning
     d = golden("tree_" + case)
     counts = d["counts"]
@@ -82,7 +84,7 @@ def test_build_tree_host_replay_matches_oracle_exact(engine, case):
     engine.upload_bins(binning.device_bins(Xb, counts), counts)
     mask = np.zeros(n, np.uint8)
     mask[d["sample_idx"]] = 1
-    kw = dict(max_leaves=int(d["max_leaves"]), max_depth=14, msl=int(d["msl"]),
+    kw = dict(max_leaves=int(d["max_leaves"]), max_depth=depth, msl=int(d["msl"]),
               mcw=float(d["mcw"]), lam=float(d["lam"]), gamma=float(d["gamma"]))
     t = engine.build_tree(d["g"], d["h"], mask, d["feat_idx"], _params(**kw),
                           _cap(kw["max_leaves"], kw["max_depth"], "leaf"))
