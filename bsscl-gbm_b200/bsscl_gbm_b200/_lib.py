@@ -60,7 +60,8 @@ class GbmStats(C.Structure):
                 ("hist_rows", C.c_int64), ("waves", C.c_int64), ("hist_ms", C.c_double),
                 ("hist_alg_bytes", C.c_double), ("host_sample_ms", C.c_double),
                 ("host_sync_ms", C.c_double), ("host_replay_ms", C.c_double),
-                ("flush_ms", C.c_double), ("hist_updates", C.c_double)]
+                ("flush_ms", C.c_double), ("hist_updates", C.c_double),
+                ("host_comm_ms", C.c_double)]
 
 
 _lib = None

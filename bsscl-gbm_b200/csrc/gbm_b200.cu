@@ -114,25 +114,38 @@ struct gbm_ctx {
     // end; gbm_fit_rounds keeps up to kRing rounds queued.
     struct Slot {
         int32_t *h_tg = nullptr, *d_tg = nullptr;   // the round's row swap targets
-        int32_t *h_feat = nullptr;     // fidx [p] | blist [nblk] | bwp [nblk + 1]
+        int32_t *h_feat = nullptr;     // fidx [p] | blist [nblk] | bwp [nblk + 1] | nb
         int16_t *h_fpos = nullptr;     // fpos [nblk * 16] | fbi [p]
         TreeOut *h_tout = nullptr;
         double *h_loss = nullptr;
         double upd_per_row = 0.0;      // histogram cell updates per row of this round
         cudaEvent_t copied = nullptr, done = nullptr;
+        // timing pairs recorded by this slot's round while profiling (kind 0:
+        // k_hist, 1: L2 flush); a captured round records the same pairs every run
+        std::vector<cudaEvent_t> tev;
+        std::vector<char> tkind;
+        int tused = 0, tdone = 0;
+        // the slot's captured round (gbm_fit_rounds)
+        cudaGraphExec_t g_cst = nullptr, g_st = nullptr;
+        int g_tpairs = 0;
+        long long g_launches = 0, g_hist = 0, g_waves = 0;
     };
     static constexpr int kRing = 4;
     Slot slot[kRing];
     bool slots_ready = false;
     cudaStream_t cst = nullptr;        // the samplers' copies, row shuffles and root row lists
     cudaEvent_t rows_free = nullptr;   // recorded on st once a round is done with the row lists
+    int cur_slot = 0;                  // the slot whose round is being enqueued
+    bool capturing = false;            // enqueueing into a graph capture
+    std::string graph_key;             // what the slots' graphs were captured for
+    unsigned long long mem_gen = 0;    // bumped by every (re)allocation: graphs hold pointers
     // The bound sampler's row permutation lives here: round r turns its swap
     // targets into a shuffle and composes perm[r % 5] = perm[(r-1) % 5][S]
     // on cst, ahead of the round's growth.
     gbm_sampler *samp = nullptr;
     int64_t samp_taken = 0;
     int64_t shuf_n = 0;
-    int32_t *d_perm[kRing + 1] = {};
+    int32_t *d_perm[kRing] = {};
     int32_t *d_head = nullptr, *d_nxt = nullptr, *d_m = nullptr, *d_mp = nullptr;
     TreeOut *d_tout = nullptr;
     int32_t *d_mono = nullptr, *h_mono = nullptr;
@@ -156,16 +169,13 @@ struct gbm_ctx {
     bool profiling = false;
     long long hist_launches = 0, hist_rows = 0, waves = 0;
     double hist_ms = 0.0, alg_bytes = 0.0, hist_updates = 0.0;
-    double host_sample_ms = 0.0, host_sync_ms = 0.0, host_replay_ms = 0.0;
-    std::vector<cudaEvent_t> hist_ev;  // pairs recorded around k_hist launches
-    int hist_ev_used = 0;
+    double host_sample_ms = 0.0, host_sync_ms = 0.0, host_replay_ms = 0.0, host_comm_ms = 0.0;
     // benchmark aid: an L2 eviction at the start of every round
     uint8_t *d_flush = nullptr;
     size_t flush_bytes = 0;
     unsigned flush_count = 0;
     double flush_ms = 0.0;
-    std::vector<cudaEvent_t> flush_ev;
-    int flush_ev_used = 0;
+
     cudaEvent_t mark[16] = {};
 };
 
@@ -228,8 +238,58 @@ int launch(gbm_ctx *ctx, void (*k)(P...), dim3 grid, dim3 block, size_t smem, cu
     return GBM_OK;
 }
 
+// Event record / wait that also work inside a graph capture, where they
+// become event nodes recorded or waited on at every run of the graph.
+int record_ev(gbm_ctx *ctx, cudaEvent_t ev, cudaStream_t s) {
+    cudaError_t e = ctx->capturing ? cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal) : cudaEventRecord(ev, s);
+    if (e != cudaSuccess) return fail(ctx, GBM_ERR_CUDA, "event record: %s", cudaGetErrorString(e));
+    return GBM_OK;
+}
+
+int wait_ev(gbm_ctx *ctx, cudaStream_t s, cudaEvent_t ev) {
+    cudaError_t e = cudaStreamWaitEvent(s, ev, ctx->capturing ? cudaEventWaitExternal : 0);
+    if (e != cudaSuccess) return fail(ctx, GBM_ERR_CUDA, "event wait: %s", cudaGetErrorString(e));
+    return GBM_OK;
+}
+
+// A timing pair (start, end) of the current slot's round; kind 0: k_hist,
+// 1: the L2 flush.  Returns the pair's index.
+int timing_pair(gbm_ctx *ctx, char kind, cudaEvent_t &e0, cudaEvent_t &e1) {
+    gbm_ctx::Slot &s = ctx->slot[ctx->cur_slot];
+    while ((int)s.tev.size() < 2 * (s.tused + 1)) {
+        cudaEvent_t e;
+        CK(cudaEventCreate(&e));
+        s.tev.push_back(e);
+    }
+    if ((int)s.tkind.size() < s.tused + 1) s.tkind.resize((size_t)s.tused + 1);
+    s.tkind[(size_t)s.tused] = kind;
+    e0 = s.tev[(size_t)(2 * s.tused)];
+    e1 = s.tev[(size_t)(2 * s.tused + 1)];
+    s.tused++;
+    return GBM_OK;
+}
+
+// Fold a slot's finished timing pairs into the totals (each pair once).
+int collect_slot_timing(gbm_ctx *ctx, int si) {
+    gbm_ctx::Slot &s = ctx->slot[si];
+    for (int k = s.tdone; k < s.tused; k++) {
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, s.tev[(size_t)(2 * k)], s.tev[(size_t)(2 * k + 1)]));
+        (s.tkind[(size_t)k] ? ctx->flush_ms : ctx->hist_ms) += ms;
+    }
+    s.tdone = s.tused;
+    return GBM_OK;
+}
+
+// A round is about to be enqueued on slot si (outside a capture).
+void begin_round(gbm_ctx *ctx, int si) {
+    ctx->cur_slot = si;
+    ctx->slot[si].tused = ctx->slot[si].tdone = 0;
+}
+
 template <typename T>
 int dalloc(gbm_ctx *ctx, T **p, size_t count) {
+    ctx->mem_gen++;
     if (*p) { cudaFree(*p); *p = nullptr; }
     if (count == 0) count = 1;
     cudaError_t e = cudaMalloc((void **)p, count * sizeof(T));
@@ -241,6 +301,7 @@ int dalloc(gbm_ctx *ctx, T **p, size_t count) {
 
 template <typename T>
 int halloc(gbm_ctx *ctx, T **p, size_t count) {
+    ctx->mem_gen++;
     if (*p) { cudaFreeHost(*p); *p = nullptr; }
     if (count == 0) count = 1;
     cudaError_t e = cudaMallocHost((void **)p, count * sizeof(T));
@@ -281,6 +342,21 @@ int sync_stream(gbm_ctx *ctx) {
     return rc;
 }
 
+// In-place sums over the ranks on the engine stream, host time counted.
+int allreduce_i64(gbm_ctx *ctx, long long *buf, int64_t count) {
+    auto t0 = std::chrono::steady_clock::now();
+    int rc = gbm_comm_allreduce_i64(ctx->comm, buf, count, ctx->st, ctx->timeout_ms, ctx->err);
+    ctx->host_comm_ms += ms_since(t0);
+    return rc;
+}
+
+int allreduce_f64(gbm_ctx *ctx, double *buf, int64_t count) {
+    auto t0 = std::chrono::steady_clock::now();
+    int rc = gbm_comm_allreduce_f64(ctx->comm, buf, count, ctx->st, ctx->timeout_ms, ctx->err);
+    ctx->host_comm_ms += ms_since(t0);
+    return rc;
+}
+
 // ---- per-round feature tables ---------------------------------------------
 
 struct RoundFeat {
@@ -303,7 +379,7 @@ int block_weight(const RoundFeat &rf, int blk) {
 int ensure_slots(gbm_ctx *ctx) {
     if (!ctx->slots_ready) {   // once per gbm_upload_bins (sizes follow p)
         for (auto &s : ctx->slot) {
-            TRY(halloc(ctx, &s.h_feat, (size_t)ctx->p + 2 * ctx->nblk + 1));
+            TRY(halloc(ctx, &s.h_feat, (size_t)ctx->p + 2 * ctx->nblk + 2));
             TRY(halloc(ctx, &s.h_fpos, (size_t)ctx->nblk * kBlk + ctx->p));
             TRY(halloc(ctx, &s.h_tout, 1));
             TRY(halloc(ctx, &s.h_loss, 1));
@@ -334,8 +410,7 @@ int ensure_shuffle(gbm_ctx *ctx, int64_t N) {
     return GBM_OK;
 }
 
-// The round's feature tables, built in the slot's pinned buffers and copied
-// on the engine stream (the previous round's kernels have read theirs).
+// The round's feature tables, built in the slot's pinned buffers (host).
 int setup_features(gbm_ctx *ctx, int si, const int32_t *fidx, int nf, RoundFeat &rf) {
     gbm_ctx::Slot &s = ctx->slot[si];
     rf.nf = nf;
@@ -353,7 +428,7 @@ int setup_features(gbm_ctx *ctx, int si, const int32_t *fidx, int nf, RoundFeat 
         if (any) rf.blist.push_back(b);
     }
     const int nb = (int)rf.blist.size();
-    int32_t *h_blist = s.h_feat + ctx->p, *h_bwp = h_blist + nb;   // the device reads blist | bwp
+    int32_t *h_blist = s.h_feat + ctx->p, *h_bwp = h_blist + ctx->nblk;
     int16_t *h_fbi = s.h_fpos + (size_t)ctx->nblk * kBlk;
     std::memcpy(s.h_feat, fidx, sizeof(int32_t) * nf);
     std::memcpy(h_blist, rf.blist.data(), sizeof(int32_t) * nb);
@@ -365,14 +440,25 @@ int setup_features(gbm_ctx *ctx, int si, const int32_t *fidx, int nf, RoundFeat 
             if (jj >= 0) h_fbi[jj] = (int16_t)bi;
         }
     }
+    h_bwp[ctx->nblk + 1] = nb;   // the count, after the longest bwp
     std::memcpy(s.h_fpos, rf.fpos.data(), sizeof(int16_t) * rf.fpos.size());
     rf.upd_per_row = 0.0;
     for (int jj = 0; jj < nf; jj++) rf.upd_per_row += ctx->skip_keep[(size_t)fidx[jj]];
     s.upd_per_row = rf.upd_per_row;
+    return GBM_OK;
+}
+
+// ...and their copies to the device, on the engine stream (fixed sizes, so
+// a captured round copies whatever the slot holds when it runs).
+int enqueue_features(gbm_ctx *ctx, int si, int nf) {
+    gbm_ctx::Slot &s = ctx->slot[si];
     CK(cudaMemcpyAsync(ctx->d_fidx, s.h_feat, sizeof(int32_t) * nf, cudaMemcpyHostToDevice, ctx->st));
-    CK(cudaMemcpyAsync(ctx->d_fpos, s.h_fpos, sizeof(int16_t) * rf.fpos.size(), cudaMemcpyHostToDevice, ctx->st));
-    CK(cudaMemcpyAsync(ctx->d_fbi, h_fbi, sizeof(int16_t) * nf, cudaMemcpyHostToDevice, ctx->st));
-    CK(cudaMemcpyAsync(ctx->d_blist, h_blist, sizeof(int32_t) * (2 * nb + 1), cudaMemcpyHostToDevice, ctx->st));
+    CK(cudaMemcpyAsync(ctx->d_fpos, s.h_fpos, sizeof(int16_t) * (size_t)ctx->nblk * kBlk, cudaMemcpyHostToDevice,
+                       ctx->st));
+    CK(cudaMemcpyAsync(ctx->d_fbi, s.h_fpos + (size_t)ctx->nblk * kBlk, sizeof(int16_t) * nf, cudaMemcpyHostToDevice,
+                       ctx->st));
+    CK(cudaMemcpyAsync(ctx->d_blist, s.h_feat + ctx->p, sizeof(int32_t) * (2 * (size_t)ctx->nblk + 2),
+                       cudaMemcpyHostToDevice, ctx->st));
     return GBM_OK;
 }
 
@@ -435,6 +521,12 @@ int ensure_round_buffers(gbm_ctx *ctx, int nf, const gbm_params *P) {
         ctx->replay_smem = 0;
         if (smem <= kReplaySmemMax) ctx->replay_smem = smem;
     }
+    const int tiles = (int)((ctx->n + kPartTile - 1) / kPartTile) + ctx->stage_slots;
+    if (tiles > ctx->tile_cap) {
+        ctx->tile_cap = tiles;
+        TRY(dalloc(ctx, &ctx->d_tile_cnt, (size_t)ctx->tile_cap));
+        TRY(dalloc(ctx, &ctx->d_side, (size_t)ctx->tile_cap * kPartWords));
+    }
     return GBM_OK;
 }
 
@@ -450,66 +542,34 @@ bool device_replay(const gbm_ctx *ctx, const gbm_params *P) {
 // The staging histograms are zero here: the split search zeroes the cells
 // it reads and the level close the totals.
 int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p) {
-    const int nb = (int)rf.blist.size();
-    if (nb == 0) return GBM_OK;
-    const int32_t *d_bwp = ctx->d_blist + nb;
+    // d_blist holds blist [nblk] | bwp [nblk + 1] | nb
+    const int32_t *d_bwp = ctx->d_blist + ctx->nblk, *d_nb = ctx->d_blist + 2 * ctx->nblk + 1;
     size_t smem = (size_t)kAccWords * sizeof(unsigned);
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (ctx->profiling) {
-        if ((int)ctx->hist_ev.size() < ctx->hist_ev_used + 2) {
-            for (int k = 0; k < 2; k++) {
-                cudaEvent_t e;
-                CK(cudaEventCreate(&e));
-                ctx->hist_ev.push_back(e);
-            }
-        }
-        e0 = ctx->hist_ev[ctx->hist_ev_used];
-        e1 = ctx->hist_ev[ctx->hist_ev_used + 1];
-        ctx->hist_ev_used += 2;
-        CK(cudaEventRecord(e0, ctx->st));
+        TRY(timing_pair(ctx, 0, e0, e1));
+        TRY(record_ev(ctx, e0, ctx->st));
     }
-    TRY(launch(ctx, k_hist, dim3(ctx->hist_grid), dim3(kHistThreads), smem, ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask,
-                                                           ctx->d_hprefix, ntask_p, ctx->d_blist, d_bwp, nb,
-                                                           ctx->d_fpos, ctx->d_skipb, rf.nf, ctx->d_q, ctx->d_stage));
-    if (ctx->profiling) CK(cudaEventRecord(e1, ctx->st));
+    TRY(launch(ctx, k_hist, dim3(ctx->hist_grid), dim3(kHistThreads), smem, ctx->st, ctx->d_xb, ctx->n, ctx->d_rows,
+               ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p, ctx->d_blist, d_bwp, d_nb, ctx->d_fpos,
+               ctx->d_skipb, rf.nf, ctx->d_q, ctx->d_stage));
+    if (e1) TRY(record_ev(ctx, e1, ctx->st));
     ctx->hist_launches++;
     return GBM_OK;
 }
 
-// Fold the event pairs recorded since the last wait into the totals.
-int collect_hist_events(gbm_ctx *ctx) {
-    for (int k = 0; k + 1 < ctx->hist_ev_used; k += 2) {
-        float ms = 0.f;
-        CK(cudaEventElapsedTime(&ms, ctx->hist_ev[k], ctx->hist_ev[k + 1]));
-        ctx->hist_ms += ms;
-    }
-    ctx->hist_ev_used = 0;
-    for (int k = 0; k + 1 < ctx->flush_ev_used; k += 2) {
-        float ms = 0.f;
-        CK(cudaEventElapsedTime(&ms, ctx->flush_ev[k], ctx->flush_ev[k + 1]));
-        ctx->flush_ms += ms;
-    }
-    ctx->flush_ev_used = 0;
-    return GBM_OK;
-}
 
 // The L2 eviction of gbm_set_l2_flush: a write of the scratch buffer on the
 // engine stream before the round's growth (timed when profiling).
 int flush_l2(gbm_ctx *ctx) {
     if (!ctx->flush_bytes) return GBM_OK;
-    cudaEvent_t e1 = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (ctx->profiling) {
-        while ((int)ctx->flush_ev.size() < ctx->flush_ev_used + 2) {
-            cudaEvent_t e;
-            CK(cudaEventCreate(&e));
-            ctx->flush_ev.push_back(e);
-        }
-        CK(cudaEventRecord(ctx->flush_ev[ctx->flush_ev_used], ctx->st));
-        e1 = ctx->flush_ev[ctx->flush_ev_used + 1];
-        ctx->flush_ev_used += 2;
+        TRY(timing_pair(ctx, 1, e0, e1));
+        TRY(record_ev(ctx, e0, ctx->st));
     }
     CK(cudaMemsetAsync(ctx->d_flush, (int)(++ctx->flush_count & 0xff), ctx->flush_bytes, ctx->st));
-    if (e1) CK(cudaEventRecord(e1, ctx->st));
+    if (e1) TRY(record_ev(ctx, e1, ctx->st));
     return GBM_OK;
 }
 
@@ -546,14 +606,14 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, const Ne
     const long long *ng = nullptr;
     if (ctx->comm) {
         TRY(launch(ctx, k_count64, dim3(1), dim3(1), 0, ctx->st, ctx->d_total, ctx->d_count64));
-        TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_count64, 1, ctx->st, ctx->timeout_ms, ctx->err));
+        TRY(allreduce_i64(ctx, ctx->d_count64, 1));
         ng = ctx->d_count64;
     }
     TRY(launch(ctx, k_root_plan, dim3(1), dim3(1), 0, ctx->st, ctx->d_total, ng, ctx->d_nodes, ctx->d_htask, ctx->d_hprefix,
                                       ints(ctx, I_NODES)));
     TRY(launch_hist(ctx, rf, ints(ctx, I_ONE)));
     if (ctx->comm)
-        TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words, ctx->st, ctx->timeout_ms, ctx->err));
+        TRY(allreduce_i64(ctx, ctx->d_stage, words));
     int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
     TRY(launch(ctx, k_split_feat<true>, dim3(dim3(fx, 1)), dim3(32 * kSplitWarps), 0, ctx->st, 
         ctx->d_nodes, nullptr, nullptr, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx,
@@ -577,11 +637,8 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
                                            ints(ctx, I_TILES), ctx->nmax, W_ub));
     }
     int tiles_ub = (int)((ctx->n + kPartTile - 1) / kPartTile) + W_ub;
-    if (tiles_ub > ctx->tile_cap) {
-        ctx->tile_cap = tiles_ub;
-        TRY(dalloc(ctx, &ctx->d_tile_cnt, (size_t)ctx->tile_cap));
-        TRY(dalloc(ctx, &ctx->d_side, (size_t)ctx->tile_cap * kPartWords));
-    }
+    if (tiles_ub > ctx->tile_cap)   // ensure_round_buffers sized them
+        return fail(ctx, GBM_ERR_STATE, "internal: %d partition tiles > %d", tiles_ub, ctx->tile_cap);
     if (last) {   // children at max_depth: counts and totals only
         if (!planned) {
             CK(cudaMemsetAsync(ctx->d_leafw, 0, sizeof(long long) * kLeafWords * W_ub, ctx->st));
@@ -592,8 +649,7 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
                                                               ints(ctx, I_TILES), ctx->d_q, ctx->d_leafw,
                                                               ctx->d_nleft));
         if (ctx->comm)
-            TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_leafw, (int64_t)kLeafWords * W_ub, ctx->st, ctx->timeout_ms,
-                                       ctx->err));
+            TRY(allreduce_i64(ctx, ctx->d_leafw, (int64_t)kLeafWords * W_ub));
         TRY(launch(ctx, k_leaf_finish, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, lvl, lvl_cnt, ctx->d_leafw, ctx->d_nleft, ctx->S));
         ctx->waves++;
         return GBM_OK;
@@ -607,13 +663,13 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
     if (ctx->comm) {
         CK(cudaMemcpyAsync(ctx->d_nleft_g, ctx->d_nleft, sizeof(long long) * W_ub, cudaMemcpyDeviceToDevice,
                            ctx->st));
-        TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_nleft_g, W_ub, ctx->st, ctx->timeout_ms, ctx->err));
+        TRY(allreduce_i64(ctx, ctx->d_nleft_g, W_ub));
         gl = ctx->d_nleft_g;
     }
     TRY(launch(ctx, k_plan_hist, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, lvl, lvl_cnt, ctx->d_nleft, gl, ctx->d_htask, ctx->d_hprefix));
     TRY(launch_hist(ctx, rf, lvl_cnt));
     if (ctx->comm)
-        TRY(gbm_comm_allreduce_i64(ctx->comm, ctx->d_stage, words * W_ub, ctx->st, ctx->timeout_ms, ctx->err));
+        TRY(allreduce_i64(ctx, ctx->d_stage, words * W_ub));
     int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
     TRY(launch(ctx, k_split_feat<false>, dim3(dim3(fx, W_ub)), dim3(32 * kSplitWarps), 0, ctx->st, 
         ctx->d_nodes, lvl, lvl_cnt, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx, ctx->d_counts,
@@ -629,7 +685,7 @@ int fetch_nodes(gbm_ctx *ctx) {
     CK(cudaMemcpyAsync(ctx->h_ints, ctx->d_ints, sizeof(int) * I_COUNT, cudaMemcpyDeviceToHost, ctx->st));
     CK(cudaMemcpyAsync(ctx->h_nodes, ctx->d_nodes, sizeof(DNode) * ctx->nmax, cudaMemcpyDeviceToHost, ctx->st));
     TRY(sync_stream(ctx));
-    if (ctx->profiling) TRY(collect_hist_events(ctx));
+    if (ctx->profiling) TRY(collect_slot_timing(ctx, ctx->cur_slot));
     return GBM_OK;
 }
 
@@ -851,7 +907,7 @@ int choose_skip_bins(gbm_ctx *ctx) {
         e = cudaGetLastError();
         if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "k_bincount: %s", cudaGetErrorString(e)); break; }
         if (ctx->comm) {
-            rc = gbm_comm_allreduce_i64(ctx->comm, (long long *)d_cnt, cells, ctx->st, ctx->timeout_ms, ctx->err);
+            rc = allreduce_i64(ctx, (long long *)d_cnt, cells);
             if (rc != GBM_OK) break;
         }
         e = cudaMemcpyAsync(cnt.data(), d_cnt, sizeof(unsigned long long) * cells, cudaMemcpyDeviceToHost, ctx->st);
@@ -885,7 +941,7 @@ int alloc_round_fixed(gbm_ctx *ctx) {
     TRY(dalloc(ctx, &ctx->d_off, (size_t)ntile));
     TRY(dalloc(ctx, &ctx->d_total, 1));
     TRY(dalloc(ctx, &ctx->d_count64, 1));
-    TRY(dalloc(ctx, &ctx->d_blist, (size_t)2 * ctx->nblk + 1));   // blist | bwp
+    TRY(dalloc(ctx, &ctx->d_blist, (size_t)2 * ctx->nblk + 2));   // blist | bwp | nb
     TRY(dalloc(ctx, &ctx->d_fbi, (size_t)ctx->p));
     TRY(dalloc(ctx, &ctx->d_fpos, (size_t)ctx->nblk * kBlk));
     TRY(dalloc(ctx, &ctx->d_ints, (size_t)I_COUNT));
@@ -957,7 +1013,7 @@ int enqueue_grow(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, bool co
         cur = 1 - cur;
     }
     // the row lists are free: the next round's compaction may overwrite them
-    CK(cudaEventRecord(ctx->rows_free, ctx->st));
+    TRY(record_ev(ctx, ctx->rows_free, ctx->st));
     return GBM_OK;
 }
 
@@ -1018,7 +1074,7 @@ int enqueue_update(gbm_ctx *ctx, const gbm_params *P, bool want_leaf, double *h_
         ctx->d_tree, ctx->d_xb, ctx->n, ctx->d_y, ctx->w[0], ctx->w[1], P->learning_rate, scale, ctx->d_F,
         ctx->d_q, want_leaf ? ctx->d_leaf : nullptr, ctx->d_loss_part));
     TRY(launch(ctx, k_sum_partials, dim3(1), dim3(256), 0, ctx->st, ctx->d_loss_part, ctx->upd_blocks, ctx->d_loss));
-    if (ctx->comm) TRY(gbm_comm_allreduce_f64(ctx->comm, ctx->d_loss, 1, ctx->st, ctx->timeout_ms, ctx->err));
+    if (ctx->comm) TRY(allreduce_f64(ctx, ctx->d_loss, 1));
     CK(cudaMemcpyAsync(h_loss, ctx->d_loss, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
     return GBM_OK;
 }
@@ -1046,6 +1102,7 @@ void write_tree_dev(const TreeOut &T, int need, gbm_tree_out *out) {
 
 // A finished slot -> the caller's tree and loss, and the statistics.
 int harvest(gbm_ctx *ctx, int si, int nf, const gbm_params *P, gbm_tree_out *out, double *train_loss) {
+    if (ctx->profiling) TRY(collect_slot_timing(ctx, si));
     const TreeOut &T = *ctx->slot[si].h_tout;
     if (T.status != 0) return fail(ctx, GBM_ERR_STATE, "internal: the device replay reached an unexpanded node");
     ctx->alg_bytes += (double)T.alg_rows * (nf + 8);
@@ -1080,20 +1137,19 @@ int prepare_round(gbm_ctx *ctx, int nf, const gbm_params *P) {
     return stage_mono(ctx, P);
 }
 
-// The sampler's next round: its row swap targets go to the device on cst,
-// where the round's shuffle is built and composed into the permutation, and
-// this rank's in-bag mask and root row list are made from the first n_sub
-// entries.  The engine stream waits for them.  The round's feature list is
-// left in feat_buf.
-int stage_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset) {
+// The sampler's next round (host side): its row swap targets into slot
+// si's pinned buffer and its features into feat_buf.  A sampler at its
+// first round is bound here: the previous permutation becomes arange(N).
+// Slot si must be the round's index modulo kRing (the permutation chain).
+int take_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset) {
     gbm_ctx::Slot &s = ctx->slot[si];
     const int64_t N = gbm_sampler_rows(sampler);
-    const int64_t m = gbm_sampler_n_sub(sampler);
     const bool rows_on = gbm_sampler_shuffles_rows(sampler) != 0;
     const int64_t r = gbm_sampler_taken(sampler);
-    constexpr int R1 = gbm_ctx::kRing + 1;
+    constexpr int R = gbm_ctx::kRing;
     if (row_offset + ctx->n > N) return fail(ctx, GBM_ERR_ARG, "rows %lld.. exceed the sampler's %lld rows",
                                              (long long)row_offset, (long long)N);
+    if (si != (int)(r % R)) return fail(ctx, GBM_ERR_STATE, "internal: slot %d for round %lld", si, (long long)r);
     if (rows_on) TRY(ensure_shuffle(ctx, N));
     if (ctx->samp != sampler || ctx->samp_taken != r) {
         if (r != 0)
@@ -1101,10 +1157,7 @@ int stage_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset)
                         (long long)r);
         ctx->samp = sampler;
         ctx->samp_taken = 0;
-        if (rows_on) {
-            k_iota<<<grid_for(N, 256), 256, 0, ctx->cst>>>(ctx->d_perm[R1 - 1], N);
-            CKL();
-        }
+        if (rows_on) TRY(launch(ctx, k_iota, dim3(grid_for(N, 256)), dim3(256), 0, ctx->cst, ctx->d_perm[R - 1], N));
     }
     ctx->feat_buf.resize((size_t)gbm_sampler_n_feat(sampler));
     auto t_s = std::chrono::steady_clock::now();
@@ -1112,28 +1165,40 @@ int stage_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset)
     ctx->host_sample_ms += ms_since(t_s);
     if (rc != GBM_OK) return fail(ctx, rc, "the sampler cannot feed an engine (already used for host draws?)");
     ctx->samp_taken++;
+    return GBM_OK;
+}
+
+// The round's shuffle (composed into the permutation), this rank's in-bag
+// mask and the root's row list, on the sampler stream (cst); ends with
+// slot si's `copied` event, which the engine stream waits for.
+int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int64_t row_offset) {
+    gbm_ctx::Slot &s = ctx->slot[si];
+    constexpr int R = gbm_ctx::kRing;
     int32_t *pout = nullptr;
     if (rows_on) {
-        int32_t *pin = ctx->d_perm[(r + R1 - 1) % R1];
-        pout = ctx->d_perm[r % R1];
+        int32_t *pin = ctx->d_perm[(si + R - 1) % R];
+        pout = ctx->d_perm[si];
         CK(cudaMemcpyAsync(s.d_tg, s.h_tg, sizeof(int32_t) * (size_t)(N - 1), cudaMemcpyHostToDevice, ctx->cst));
         CK(cudaMemsetAsync(ctx->d_head, 0xff, sizeof(int32_t) * (size_t)N, ctx->cst));
-        TRY(launch(ctx, k_shuf_link, dim3(grid_for(N - 1, 256)), dim3(256), 0, ctx->cst, s.d_tg, N, ctx->d_head, ctx->d_nxt));
-        TRY(launch(ctx, k_shuf_min, dim3(grid_for(N, 256)), dim3(256), 0, ctx->cst, s.d_tg, N, ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp));
-        TRY(launch(ctx, k_shuf_compose, dim3(grid_for(N, 256)), dim3(256), 0, ctx->cst, s.d_tg, N, ctx->d_m, ctx->d_mp, pin, pout));
+        TRY(launch(ctx, k_shuf_link, dim3(grid_for(N - 1, 256)), dim3(256), 0, ctx->cst, s.d_tg, N, ctx->d_head,
+                   ctx->d_nxt));
+        TRY(launch(ctx, k_shuf_min, dim3(grid_for(N, 256)), dim3(256), 0, ctx->cst, s.d_tg, N, ctx->d_head,
+                   ctx->d_nxt, ctx->d_m, ctx->d_mp));
+        TRY(launch(ctx, k_shuf_compose, dim3(grid_for(N, 256)), dim3(256), 0, ctx->cst, s.d_tg, N, ctx->d_m,
+                   ctx->d_mp, pin, pout));
     }
-    // mask and root row list on this stream too, once the previous round has
-    // finished with the row lists (it is at its replay or F update by then)
-    CK(cudaStreamWaitEvent(ctx->cst, ctx->rows_free, 0));
+    // mask and root row list once the previous round is done with the row
+    // lists (it is at its replay or F update by then)
+    TRY(wait_ev(ctx, ctx->cst, ctx->rows_free));
     if (rows_on) {
         CK(cudaMemsetAsync(ctx->d_mask, 0, (size_t)ctx->n, ctx->cst));
-        TRY(launch(ctx, k_mask_from_rows, dim3(grid_for(m, 256)), dim3(256), 0, ctx->cst, pout, m, row_offset, ctx->n, ctx->d_mask));
+        TRY(launch(ctx, k_mask_from_rows, dim3(grid_for(m, 256)), dim3(256), 0, ctx->cst, pout, m, row_offset,
+                   ctx->n, ctx->d_mask));
     } else {   // sample_idx is every row (E:2508-2509)
         CK(cudaMemsetAsync(ctx->d_mask, 1, (size_t)ctx->n, ctx->cst));
     }
     TRY(enqueue_compaction(ctx, ctx->cst));
-    CK(cudaEventRecord(s.copied, ctx->cst));
-    CK(cudaStreamWaitEvent(ctx->st, s.copied, 0));
+    TRY(record_ev(ctx, s.copied, ctx->cst));
     return GBM_OK;
 }
 
@@ -1186,6 +1251,82 @@ int upload_bins_t(gbm_ctx *ctx, const T *xbin, int64_t n, int32_t p, const int32
 
 }  // namespace
 
+namespace {
+
+// Everything a captured round depends on besides the contents of its
+// slot's pinned buffers.
+std::string graph_key(const gbm_ctx *ctx, const gbm_params *P, int nf, int64_t N, int64_t m, bool rows_on,
+                      int64_t row_offset) {
+    char buf[512];
+    snprintf(buf, sizeof buf, "%a/%a/%a/%a/%d/%d/%d/%d/%p|%d/%lld/%lld/%lld/%d/%lld|%d/%zu/%llu/%p",
+             P->reg_lambda, P->gamma, P->min_child_weight, P->learning_rate, P->min_samples_leaf, P->max_depth,
+             P->max_leaves, P->grow_policy, (const void *)P->monotone, nf, (long long)N, (long long)m,
+             (long long)ctx->n, (int)rows_on, (long long)row_offset, (int)ctx->profiling, ctx->flush_bytes,
+             ctx->mem_gen, (const void *)ctx->comm);
+    return buf;
+}
+
+void drop_graphs(gbm_ctx *ctx) {
+    for (auto &s : ctx->slot) {
+        if (s.g_cst) cudaGraphExecDestroy(s.g_cst);
+        if (s.g_st) cudaGraphExecDestroy(s.g_st);
+        s.g_cst = s.g_st = nullptr;
+    }
+    ctx->graph_key.clear();
+}
+
+// Capture one stream's part of a round into an executable graph.
+template <typename F>
+int capture(gbm_ctx *ctx, cudaStream_t st, cudaGraphExec_t *out, F &&enqueue) {
+    CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    ctx->capturing = true;
+    int rc = enqueue();
+    ctx->capturing = false;
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (rc == GBM_OK && e != cudaSuccess) rc = fail(ctx, GBM_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+    if (rc == GBM_OK) {
+        e = cudaGraphInstantiate(out, g, 0);
+        if (e != cudaSuccess) rc = fail(ctx, GBM_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    }
+    if (g) cudaGraphDestroy(g);
+    return rc;
+}
+
+// Slot si's round as two graphs: the sampler stream's part (targets,
+// shuffle, mask, root row list) and the engine stream's (features, growth,
+// replay, F update, tree and loss copies).  The host fills the slot's pinned
+// buffers before each launch.
+int capture_round(gbm_ctx *ctx, int si, int nf, const gbm_params *P, int64_t N, int64_t m, bool rows_on,
+                  int64_t row_offset) {
+    gbm_ctx::Slot &s = ctx->slot[si];
+    const long long l0 = ctx->launches, h0 = ctx->hist_launches, w0 = ctx->waves;
+    ctx->cur_slot = si;
+    s.tused = s.tdone = 0;
+    TRY(capture(ctx, ctx->cst, &s.g_cst, [&] { return enqueue_sample(ctx, si, N, m, rows_on, row_offset); }));
+    TRY(capture(ctx, ctx->st, &s.g_st, [&] {
+        TRY(wait_ev(ctx, ctx->st, s.copied));
+        TRY(enqueue_features(ctx, si, nf));
+        RoundFeat rf;
+        rf.nf = nf;
+        TRY(enqueue_grow(ctx, rf, P, true));
+        TRY(enqueue_replay(ctx, P));
+        TRY(enqueue_update(ctx, P, false, s.h_loss));
+        CK(cudaMemcpyAsync(s.h_tout, ctx->d_tout, sizeof(TreeOut), cudaMemcpyDeviceToHost, ctx->st));
+        return record_ev(ctx, s.done, ctx->st);
+    }));
+    s.g_tpairs = s.tused;
+    s.g_launches = ctx->launches - l0;
+    s.g_hist = ctx->hist_launches - h0;
+    s.g_waves = ctx->waves - w0;
+    ctx->launches = l0;   // counted when the graphs run
+    ctx->hist_launches = h0;
+    ctx->waves = w0;
+    return GBM_OK;
+}
+
+}  // namespace
+
 // ===========================================================================
 // C ABI
 // ===========================================================================
@@ -1231,6 +1372,9 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
         if (ctx->st) cudaStreamSynchronize(ctx->st);
         if (ctx->cst) cudaStreamSynchronize(ctx->cst);
     }
+    drop_graphs(ctx);   // graphs may hold collectives: release them first
+    for (auto &s : ctx->slot)
+        for (cudaEvent_t e : s.tev) cudaEventDestroy(e);
     if (ctx->comm) gbm_comm_destroy(ctx->comm);
     void *dev_ptrs[] = {ctx->d_xb, ctx->d_counts, ctx->d_skipb, ctx->d_y, ctx->d_F, ctx->d_q, ctx->d_mask,
                         ctx->d_rows, ctx->d_tmp, ctx->d_cnt, ctx->d_off, ctx->d_total, ctx->d_blist, ctx->d_fidx,
@@ -1251,8 +1395,6 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
         if (s.copied) cudaEventDestroy(s.copied);
         if (s.done) cudaEventDestroy(s.done);
     }
-    for (cudaEvent_t e : ctx->hist_ev) cudaEventDestroy(e);
-    for (cudaEvent_t e : ctx->flush_ev) cudaEventDestroy(e);
     for (cudaEvent_t e : ctx->mark) if (e) cudaEventDestroy(e);
     if (ctx->st) cudaStreamDestroy(ctx->st);
     if (ctx->cst) cudaStreamDestroy(ctx->cst);
@@ -1373,8 +1515,10 @@ int gbm_build_tree(gbm_ctx *ctx, const double *grad, const double *hess, const u
     TRY(prepare_round(ctx, nfeat, P));
     std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
     CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    begin_round(ctx, 0);
     RoundFeat rf;
     TRY(setup_features(ctx, 0, feat_idx, nfeat, rf));
+    TRY(enqueue_features(ctx, 0, nfeat));
     TRY(enqueue_grow(ctx, rf, P, false));
     if (device_replay(ctx, P)) {
         TRY(enqueue_replay(ctx, P));
@@ -1383,7 +1527,6 @@ int gbm_build_tree(gbm_ctx *ctx, const double *grad, const double *hess, const u
         s.h_loss[0] = 0.0;
         CK(cudaEventRecord(s.done, ctx->st));
         TRY(wait_slot(ctx, 0));
-        if (ctx->profiling) TRY(collect_hist_events(ctx));
         return harvest(ctx, 0, nfeat, P, out, nullptr);
     }
     HostTree T;
@@ -1395,11 +1538,12 @@ int gbm_build_tree(gbm_ctx *ctx, const double *grad, const double *hess, const u
 // One round from the staged in-bag mask (on the device) and feature list:
 // growth, the tree (device replay, or host replay for capped levels), the F
 // update, the loss, and the wait for all of it.
-static int round_body(gbm_ctx *ctx, const int32_t *feat_idx, int32_t nfeat, const gbm_params *P,
+static int round_body(gbm_ctx *ctx, int si, const int32_t *feat_idx, int32_t nfeat, const gbm_params *P,
                       gbm_tree_out *out, double *train_loss, bool compacted) {
-    gbm_ctx::Slot &s = ctx->slot[0];
+    gbm_ctx::Slot &s = ctx->slot[si];
     RoundFeat rf;
-    TRY(setup_features(ctx, 0, feat_idx, nfeat, rf));
+    TRY(setup_features(ctx, si, feat_idx, nfeat, rf));
+    TRY(enqueue_features(ctx, si, nfeat));
     TRY(enqueue_grow(ctx, rf, P, compacted));
     const bool dev = device_replay(ctx, P);
     HostTree T;
@@ -1425,9 +1569,9 @@ static int round_body(gbm_ctx *ctx, const int32_t *feat_idx, int32_t nfeat, cons
     if (out->leaf_of_row)
         CK(cudaMemcpyAsync(out->leaf_of_row, ctx->d_leaf, sizeof(int32_t) * ctx->n, cudaMemcpyDeviceToHost, ctx->st));
     CK(cudaEventRecord(s.done, ctx->st));
-    TRY(wait_slot(ctx, 0));
-    if (ctx->profiling) TRY(collect_hist_events(ctx));
-    if (dev) return harvest(ctx, 0, nfeat, P, out, train_loss);
+    TRY(wait_slot(ctx, si));
+    if (dev) return harvest(ctx, si, nfeat, P, out, train_loss);
+    if (ctx->profiling) TRY(collect_slot_timing(ctx, si));
     if (train_loss) *train_loss = -s.h_loss[0] / (double)ctx->n_global;
     write_tree(T, tree_need(P), out);
     return GBM_OK;
@@ -1442,7 +1586,8 @@ int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, 
     TRY(prepare_round(ctx, nfeat, P));
     std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
     CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
-    return round_body(ctx, feat_idx, nfeat, P, out, train_loss, false);
+    begin_round(ctx, 0);
+    return round_body(ctx, 0, feat_idx, nfeat, P, out, train_loss, false);
 }
 
 int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *P,
@@ -1453,8 +1598,13 @@ int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, co
     TRY(check_tree_args(ctx, nf, P, out));
     CK(cudaSetDevice(ctx->dev));
     TRY(prepare_round(ctx, nf, P));
-    TRY(stage_sample(ctx, 0, sampler, row_offset));
-    return round_body(ctx, ctx->feat_buf.data(), nf, P, out, train_loss, true);
+    const int si = (int)(gbm_sampler_taken(sampler) % gbm_ctx::kRing);
+    begin_round(ctx, si);
+    TRY(take_sample(ctx, si, sampler, row_offset));
+    TRY(enqueue_sample(ctx, si, gbm_sampler_rows(sampler), gbm_sampler_n_sub(sampler),
+                       gbm_sampler_shuffles_rows(sampler) != 0, row_offset));
+    TRY(wait_ev(ctx, ctx->st, ctx->slot[si].copied));
+    return round_body(ctx, si, ctx->feat_buf.data(), nf, P, out, train_loss, true);
 }
 
 int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *P, int32_t n_rounds,
@@ -1475,24 +1625,58 @@ int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const
         return GBM_OK;
     }
     const int R = gbm_ctx::kRing;
-    for (int r = 0; r < n_rounds + R; r++) {
-        const int si = r % R;
-        if (r >= R) {
-            TRY(wait_slot(ctx, si));
-            TRY(harvest(ctx, si, nf, P, &outs[r - R], &train_loss[r - R]));
+    const int64_t N = gbm_sampler_rows(sampler), m = gbm_sampler_n_sub(sampler);
+    const bool rows_on = gbm_sampler_shuffles_rows(sampler) != 0;
+    if (rows_on) TRY(ensure_shuffle(ctx, N));   // before any capture: no allocation inside one
+    // With several ranks a round is replayed from graphs: each round's ~13
+    // collective enqueues cost the host more than the GPU needs for the
+    // round.  One GPU launches eagerly (programmatic dependent launch
+    // already hides the gaps there, and capturing costs a first fit time).
+    const bool graphs = ctx->comm != nullptr;
+    if (graphs) {
+        const std::string key = graph_key(ctx, P, nf, N, m, rows_on, row_offset);
+        if (key != ctx->graph_key) {
+            drop_graphs(ctx);
+            for (int si = 0; si < R; si++) TRY(capture_round(ctx, si, nf, P, N, m, rows_on, row_offset));
+            ctx->graph_key = key;
         }
-        if (r >= n_rounds) continue;
+    }
+    const int64_t r0 = gbm_sampler_taken(sampler);
+    for (int k = 0; k < n_rounds + R; k++) {
+        const int si = (int)((r0 + k) % R);
+        if (k >= R) {
+            TRY(wait_slot(ctx, si));
+            TRY(harvest(ctx, si, nf, P, &outs[k - R], &train_loss[k - R]));
+        }
+        if (k >= n_rounds) continue;
         gbm_ctx::Slot &s = ctx->slot[si];
-        TRY(stage_sample(ctx, si, sampler, row_offset));
+        if (!graphs) {
+            begin_round(ctx, si);
+            TRY(take_sample(ctx, si, sampler, row_offset));
+            TRY(enqueue_sample(ctx, si, N, m, rows_on, row_offset));
+            TRY(wait_ev(ctx, ctx->st, s.copied));
+            RoundFeat rf;
+            TRY(setup_features(ctx, si, ctx->feat_buf.data(), nf, rf));
+            TRY(enqueue_features(ctx, si, nf));
+            TRY(enqueue_grow(ctx, rf, P, true));
+            TRY(enqueue_replay(ctx, P));
+            TRY(enqueue_update(ctx, P, false, s.h_loss));
+            CK(cudaMemcpyAsync(s.h_tout, ctx->d_tout, sizeof(TreeOut), cudaMemcpyDeviceToHost, ctx->st));
+            CK(cudaEventRecord(s.done, ctx->st));
+            continue;
+        }
+        ctx->cur_slot = si;
+        TRY(take_sample(ctx, si, sampler, row_offset));
         RoundFeat rf;
         TRY(setup_features(ctx, si, ctx->feat_buf.data(), nf, rf));
-        TRY(enqueue_grow(ctx, rf, P, true));
-        TRY(enqueue_replay(ctx, P));
-        TRY(enqueue_update(ctx, P, false, s.h_loss));
-        CK(cudaMemcpyAsync(s.h_tout, ctx->d_tout, sizeof(TreeOut), cudaMemcpyDeviceToHost, ctx->st));
-        CK(cudaEventRecord(s.done, ctx->st));
+        s.tused = s.g_tpairs;
+        s.tdone = 0;
+        CK(cudaGraphLaunch(s.g_cst, ctx->cst));
+        CK(cudaGraphLaunch(s.g_st, ctx->st));
+        ctx->launches += s.g_launches;
+        ctx->hist_launches += s.g_hist;
+        ctx->waves += s.g_waves;
     }
-    if (ctx->profiling) TRY(collect_hist_events(ctx));
     return GBM_OK;
 }
 
@@ -1608,6 +1792,7 @@ int gbm_get_stats(gbm_ctx *ctx, gbm_stats *out) {
     out->host_replay_ms = ctx->host_replay_ms;
     out->flush_ms = ctx->flush_ms;
     out->hist_updates = ctx->hist_updates;
+    out->host_comm_ms = ctx->host_comm_ms;
     return GBM_OK;
 }
 
@@ -1615,7 +1800,7 @@ int gbm_reset_stats(gbm_ctx *ctx) {
     if (!ctx) return GBM_ERR_ARG;
     ctx->launches = ctx->hist_launches = ctx->hist_rows = ctx->waves = 0;
     ctx->hist_ms = ctx->alg_bytes = ctx->hist_updates = 0.0;
-    ctx->host_sample_ms = ctx->host_sync_ms = ctx->host_replay_ms = ctx->flush_ms = 0.0;
+    ctx->host_sample_ms = ctx->host_sync_ms = ctx->host_replay_ms = ctx->flush_ms = ctx->host_comm_ms = 0.0;
     return GBM_OK;
 }
 

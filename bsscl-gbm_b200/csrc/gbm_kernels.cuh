@@ -321,13 +321,14 @@ __global__ void __launch_bounds__(kHistThreads, 2)
 k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
        const int32_t *__restrict__ rows1, const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
        const int *__restrict__ ntask_p, const int32_t *__restrict__ blist, const int32_t *__restrict__ bwp,
-       int nb, const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
+       const int32_t *__restrict__ nb_p, const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
        const longlong2 *__restrict__ q, long long *__restrict__ stage_hist) {
     griddep_wait();
     extern __shared__ unsigned acc[];   // [6][16][256]
     __shared__ long long s_tot[2][kHistThreads / 32];
     const int ntask = *ntask_p;
-    if (ntask <= 0) return;
+    const int nb = *nb_p;
+    if (ntask <= 0 || nb <= 0) return;
     const long long R = rpre[ntask];
     const long long T = (long long)bwp[nb] * R;
     if (T <= 0) return;

@@ -147,8 +147,10 @@ int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, co
  * and loss, identical to calling gbm_round_sampled n_rounds times.  When
  * the tree is replayed on the device (depth-wise growth, or best-first with
  * max_depth <= 10) the rounds are queued back to back with no host wait in
- * between (up to 4 in flight); otherwise, or when any outs[r].leaf_of_row
- * is set, the rounds run one by one. */
+ * between (up to 4 in flight; with a communicator, each round is replayed
+ * from a CUDA graph captured on the first call with these parameters);
+ * otherwise, or when any outs[r].leaf_of_row is set, the rounds run one by
+ * one. */
 int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *params,
                    int32_t n_rounds, gbm_tree_out *outs, double *train_loss);
 
@@ -235,6 +237,7 @@ typedef struct {
     double hist_updates;       /* histogram cell updates (row x selected feature, skipped bin
                                   excluded) of the reference's histograms; 6 shared-memory
                                   atomic adds each */
+    double host_comm_ms;       /* host time in the collective calls (enqueue) */
 } gbm_stats;
 
 int gbm_set_profiling(gbm_ctx *ctx, int32_t on);
