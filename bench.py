@@ -70,6 +70,30 @@ def workload(cfg, rows=None):
     return Xb, y, counts
 
 
+def bin_on_gpu(eng, X, lo, hi):
+    """Config 4's edges and bins made on the GPU: gbm_bin_edges over all rows,
+    gbm_upload_binned_rows for this rank's rows (the training matrix), and
+    gbm_bin_features for the host copy of the ids that the estimator arm and
+    the CPU baseline use.  Host wall times of each step (edges include the
+    host -> device copy of X); the edges run twice and the second is kept."""
+    t0 = time.perf_counter()
+    eng.bin_edges(X, 255)
+    t1 = time.perf_counter()
+    edges, counts, nanb = eng.bin_edges(X, 255)
+    t2 = time.perf_counter()
+    eng.upload_binned_rows(lo, hi, edges, counts, nanb)
+    eng.sync()
+    t3 = time.perf_counter()
+    Xb = eng.bin_features(X, edges, counts, nanb)
+    t4 = time.perf_counter()
+    stats = {"edges_ms": (t2 - t1) * 1e3, "edges_first_call_ms": (t1 - t0) * 1e3,
+             "bin_into_engine_ms": (t3 - t2) * 1e3, "raw_ids_to_host_ms": (t4 - t3) * 1e3,
+             "x_bytes": int(X.nbytes), "rows": int(X.shape[0]), "features": int(X.shape[1]),
+             "note": "host wall times of gbm_bin_edges (sample_weight=None, n_bins 255), "
+                     "gbm_upload_binned_rows and gbm_bin_features (uint16 ids to host)"}
+    return Xb, counts, stats
+
+
 class Clocks:
     """SM clock and throttle reasons sampled DURING the timed region: NVML
     (read only) polled every 2 ms from a thread; nvidia-smi as a fallback."""
@@ -273,20 +297,28 @@ def run_engine(args):
     n = c["n"]
     lo, hi = (n * rank) // world, (n * (rank + 1)) // world
     five = c is CONFIGS["5"]
-    # config 5: each rank makes only its rows (2 GB per 10M x 200); config 4: all rows
-    Xb, y, counts = workload(c, rows=(lo, hi) if five else None)
-    Xl = Xb if five else Xb[lo:hi]            # this rank's rows
-    p = Xb.shape[1]
-    w2 = O.class_weights(y, c["class_weight"])
-    base = O.base_score(y, w2)
-    Xd = binning.device_bins(Xl, counts)
-
     eng = Engine(local)
     if world > 1:
         uid = [Engine.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         eng.init_comm(uid[0], world, rank, timeout_ms=120000)
-    eng.upload_bins(Xl, counts)
+    bin_stats = None
+    X = None
+    if five:
+        # each rank makes only its rows (2 GB per 10M x 200)
+        Xb, y, counts = workload(c, rows=(lo, hi))
+        Xl = Xb
+        eng.upload_bins(Xl, counts)
+    else:
+        # config 4: raw float32 rows, binned on the GPU
+        from bsscl_gbm_b200 import datasets
+        X, y = datasets.config4(n=n)
+        Xb, counts, bin_stats = bin_on_gpu(eng, X, lo, hi)
+        Xl = Xb[lo:hi]
+    p = Xb.shape[1]
+    w2 = O.class_weights(y, c["class_weight"])
+    base = O.base_score(y, w2)
+    Xd = binning.device_bins(Xl, counts)
     eng.upload_labels(y[lo:hi].astype(np.uint8), w2, base, n_global=n)
     prm = GbmParams(c["lam"], 0.0, c["mcw"], c["lr"], c["msl"], c["max_depth"], c["max_leaves"], 0,
                     None)
@@ -371,12 +403,30 @@ def run_engine(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
         e2e = args.steps / (e2e_ms / 1000.0)
+    # ---- the whole public fit from raw float32 rows (binning on the GPU) -------
+    fit_raw = None
+    if X is not None:
+        m2 = HybridHistGBMNumbaV1_0_1(n_estimators=args.steps, max_depth=c["max_depth"],
+                                      learning_rate=c["lr"], min_child_weight=c["mcw"],
+                                      subsample=c["subsample"], colsample_bytree=c["colsample"],
+                                      reg_lambda=c["lam"], class_weight=c["class_weight"], n_bins=255,
+                                      random_state=c["seed"], verbose=False)
+        m2._engine, m2._engine_dev = eng, local
+        if dist is not None:
+            dist.barrier()
+        t0 = time.perf_counter()
+        m2.fit(X, y)
+        fit_s = time.perf_counter() - t0
+        fit_raw = {"seconds": fit_s, "rounds": args.steps, "binning_ms": m2.times["binning"],
+                   "training_ms": m2.times["training"],
+                   "note": "HybridHistGBMNumbaV1_0_1.fit(X float32 [n, p], y) wall time on this rank: "
+                           "adaptive hyper-parameters, GPU edges and bins, labels, the rounds"}
     rows = hi - lo
     nblk = (p + 15) // 16
-    # once per fit: bins (uint16 for config 4, uint8 for config 5), labels,
-    # initial F, bin counts; every round: the global row sample's swap
-    # targets and the feature tables
-    once = rows * p * Xb.itemsize + rows + 8 * rows + 4 * p
+    # once per fit: bins (1 byte per id: uint16 ids are narrowed on the host
+    # as they stream through the pinned buffers), labels, bin counts; every
+    # round: the global row sample's swap targets and the feature tables
+    once = rows * p + rows + 4 * p
     per_round = 4 * (n - 1) + 4 * n_feat + 2 * 16 * nblk + 4 * nblk
     h2d = once / args.steps + per_round
     d2h = 9240 + 8                          # the tree record and the loss
@@ -464,6 +514,8 @@ def run_engine(args):
                                 "config": "BASELINE configs[3] literally: same data, max_depth 8, 63 leaves"}
                                if d8_ms else None),
             "clocks": clk,
+            "binning": bin_stats,
+            "fit_from_raw": fit_raw,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

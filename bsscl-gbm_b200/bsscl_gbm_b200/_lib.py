@@ -31,7 +31,8 @@ EXPORTS = (
     "gbm_sampler_n_sub", "gbm_sampler_n_feat", "gbm_round_sampled",
     "gbm_set_profiling", "gbm_get_stats", "gbm_reset_stats", "gbm_event_record",
     "gbm_event_elapsed", "gbm_predict_noalloc", "gbm_fit_rounds", "gbm_upload_bins_u16",
-    "gbm_set_l2_flush",
+    "gbm_set_l2_flush", "gbm_bin_edges", "gbm_upload_binned_rows", "gbm_bin_features",
+    "gbm_predict_upload_raw", "gbm_predict_raw",
 )
 
 
@@ -128,6 +129,12 @@ def lib():
     L.gbm_reset_stats.argtypes = [P]
     L.gbm_event_record.argtypes = [P, i32]
     L.gbm_event_elapsed.argtypes = [P, i32, i32, C.POINTER(C.c_float)]
+    L.gbm_bin_edges.argtypes = [P, P, i64, i32, i32, i32, P, P, i32, P, P, P]
+    L.gbm_upload_binned_rows.argtypes = [P, i64, i64, P, i32, P, P]
+    L.gbm_bin_features.argtypes = [P, P, i64, i32, i32, P, i32, P, P, P]
+    L.gbm_predict_upload_raw.argtypes = [P, P, i64, i32, i32, P, i32, P, P]
+    L.gbm_predict_raw.argtypes = [P, P, i64, i32, i32, P, i32, P, P, C.POINTER(GbmPacked), f64,
+                                  f64, P, P]
     L.gbm_predict_noalloc.argtypes = [P, i64, i32, P, P, P, P, P, P, i32, i32, f64, f64, P, P, P,
                                       C.c_char_p, i32]
     _lib = L
@@ -201,6 +208,81 @@ class Engine:
             rc = self._L.gbm_upload_bins(self._h, ptr(xb), n, p, ptr(cnt))
         self.n, self.p = n, p
         self.check(rc, "gbm_upload_bins")
+
+    # -- binning on the device --
+    @staticmethod
+    def _raw(X):
+        """(contiguous float32/float64 matrix, dtype code) of a raw matrix."""
+        X = np.asarray(X)
+        if X.dtype != np.float32:
+            X = np.asarray(X, dtype=np.float64)
+        return np.ascontiguousarray(X), (0 if X.dtype == np.float32 else 1)
+
+    @staticmethod
+    def _tables(edges, counts, nan_bin):
+        e = np.ascontiguousarray(edges, dtype=np.float64)
+        return (e, np.ascontiguousarray(counts, dtype=np.int32),
+                np.ascontiguousarray(nan_bin, dtype=np.int32))
+
+    def bin_edges(self, X, n_bins, categorical=None):
+        """``_build_bin_edges`` (sample_weight=None) on the GPU:
+        ``(edges_2d [p, max_b] float64, counts int32 [p], nan_bin_id int32 [p])``.
+        The matrix stays on the device for :meth:`upload_binned_rows`."""
+        Xc, dt = self._raw(X)
+        n, p = Xc.shape
+        stride = max(int(n_bins) + 2, 65)
+        edges = np.empty((p, stride), np.float64)
+        counts = np.empty(p, np.int32)
+        nanb = np.empty(p, np.int32)
+        maxb = C.c_int32(0)
+        cat = None
+        if categorical is not None:
+            cat = np.zeros(p, np.uint8)
+            cat[list(categorical)] = 1
+        self.check(self._L.gbm_bin_edges(self._h, ptr(Xc), n, p, dt, int(n_bins), ptr(cat), ptr(edges),
+                                         stride, ptr(counts), ptr(nanb), C.byref(maxb)),
+                   "gbm_bin_edges")
+        self._binned = (n, p)
+        return np.ascontiguousarray(edges[:, :maxb.value]), counts, nanb
+
+    def upload_binned_rows(self, lo, hi, edges, counts, nan_bin):
+        """Training bins from rows [lo, hi) of the matrix given to :meth:`bin_edges`."""
+        e, cnt, nb = self._tables(edges, counts, nan_bin)
+        self.check(self._L.gbm_upload_binned_rows(self._h, int(lo), int(hi), ptr(e), e.shape[1],
+                                                  ptr(cnt), ptr(nb)), "gbm_upload_binned_rows")
+        self.n, self.p = hi - lo, e.shape[0]
+
+    def bin_features(self, X, edges, counts, nan_bin):
+        """The reference's raw bin ids (``_bin_features``), uint16 [n, p], computed on the GPU."""
+        Xc, dt = self._raw(X)
+        n, p = Xc.shape
+        e, cnt, nb = self._tables(edges, counts, nan_bin)
+        out = np.empty((n, p), np.uint16)
+        self.check(self._L.gbm_bin_features(self._h, ptr(Xc), n, p, dt, ptr(e), e.shape[1], ptr(cnt),
+                                            ptr(nb), ptr(out)), "gbm_bin_features")
+        return out
+
+    def predict_raw(self, X, edges, counts, nan_bin, packed, n_trees, lr, base, want_F=True,
+                    want_proba=True):
+        """Predict from a raw matrix: binned on the GPU, then the ensemble."""
+        Xc, dt = self._raw(X)
+        n, p = Xc.shape
+        e, cnt, nb = self._tables(edges, counts, nan_bin)
+        s, keep = self.packed_struct(packed, n_trees)
+        F = np.empty(n, np.float64) if want_F else None
+        P = np.empty(n, np.float64) if want_proba else None
+        self.check(self._L.gbm_predict_raw(self._h, ptr(Xc), n, p, dt, ptr(e), e.shape[1], ptr(cnt),
+                                           ptr(nb), C.byref(s), float(lr), float(base), ptr(F),
+                                           ptr(P)), "gbm_predict_raw")
+        return F, P
+
+    def predict_upload_raw(self, X, edges, counts, nan_bin):
+        Xc, dt = self._raw(X)
+        e, cnt, nb = self._tables(edges, counts, nan_bin)
+        self._pn = Xc.shape[0]
+        self.check(self._L.gbm_predict_upload_raw(self._h, ptr(Xc), Xc.shape[0], Xc.shape[1], dt,
+                                                  ptr(e), e.shape[1], ptr(cnt), ptr(nb)),
+                   "gbm_predict_upload_raw")
 
     def set_l2_flush(self, nbytes):
         """Benchmark aid: evict L2 at the start of every round (0 = off)."""

@@ -292,6 +292,12 @@ class HybridHistGBMNumbaV1_0_1:
                          float(self.learning_rate), int(self.min_samples_leaf), int(self.max_depth),
                          int(self.max_leaves), policy, mono_ptr)
 
+    def _check_device_bins(self):
+        mx = int(np.max(self.feature_bin_counts))
+        if mx > 256:
+            raise ValueError("the device path holds at most 256 bins per feature "
+                             f"(feature with {mx} bins); use n_bins <= 255")
+
     def _tree_capacity(self):
         if self.grow_policy == 'leaf':
             return 2 * int(self.max_leaves) + 2
@@ -344,10 +350,14 @@ class HybridHistGBMNumbaV1_0_1:
         if self.n_classes_ > 2:
             raise NotImplementedError("multi-class softmax is not on the B200 engine")
         self._is_multiclass = False
-        label_map = {c: i for i, c in enumerate(self.classes_)}
-        y = np.array([label_map[v] for v in y], dtype=np.int64)
+        # class index of every label (classes_ is sorted and unique)
+        y = np.searchsorted(self.classes_, y).astype(np.int64)
         if y_val is not None:
-            y_val = np.array([label_map[v] for v in y_val], dtype=np.int64)
+            y_val = np.asarray(y_val)
+            yv = np.searchsorted(self.classes_, y_val)
+            if np.any(yv >= len(self.classes_)) or np.any(self.classes_[np.minimum(yv, len(self.classes_) - 1)] != y_val):
+                raise KeyError("y_val holds a label that is not in y")
+            y_val = yv.astype(np.int64)
         self.trees = []
         self.mc_trees = None
         self.train_loss_history_ = []
@@ -381,15 +391,34 @@ class HybridHistGBMNumbaV1_0_1:
             sample_weight = np.ones(len(y), dtype=np.float64)
             sample_weight[y == 1] = self.scale_pos_weight
         t0 = time.perf_counter()
-        self.bin_edges, self.feature_bin_counts, self._nan_bin_id = binning.build_bin_edges(
-            X, self.n_bins, None, sample_weight)
+        # Edges and bins are computed on the GPU (gbm_bin_edges /
+        # gbm_upload_binned_rows) unless the edges are weighted
+        # (scale_pos_weight), whose cumulative weights the host restatement
+        # computes in NumPy's own summation order.
+        on_device = sample_weight is None and 2 <= int(self.n_bins) <= 1023
+        if on_device:
+            eng = self._get_engine()
+            self.bin_edges, self.feature_bin_counts, self._nan_bin_id = eng.bin_edges(X, self.n_bins)
+        else:
+            self.bin_edges, self.feature_bin_counts, self._nan_bin_id = binning.build_bin_edges(
+                X, self.n_bins, None, sample_weight)
         self._max_bins = int(np.max(self.feature_bin_counts))
-        X_bin = binning.bin_features(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id)
+        self._check_device_bins()
+        if on_device:
+            lo, hi = _rank_rows(X.shape[0])
+            eng.upload_binned_rows(lo, hi, self.bin_edges, self.feature_bin_counts, self._nan_bin_id)
+            X_bin = _BinsOnDevice(X.shape)
+        else:
+            X_bin = binning.bin_features(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id)
         self.times['binning'] = (time.perf_counter() - t0) * 1000
         X_val_bin = None
         if X_val is not None and y_val is not None:
-            X_val_bin = binning.bin_features(X_val, self.bin_edges, self.feature_bin_counts,
+            if on_device:
+                X_val_bin = eng.bin_features(X_val, self.bin_edges, self.feature_bin_counts,
                                              self._nan_bin_id)
+            else:
+                X_val_bin = binning.bin_features(X_val, self.bin_edges, self.feature_bin_counts,
+                                                 self._nan_bin_id)
         t0 = time.perf_counter()
         self._fit_binary_device(X_bin, y, X_val_bin, y_val)
         self.times['training'] = (time.perf_counter() - t0) * 1000
@@ -446,22 +475,21 @@ class HybridHistGBMNumbaV1_0_1:
                           self.colsample_bytree < 1.0, look_ahead=3)
         eng = self._get_engine()
         dist = _dist()
-        lo, hi = 0, n
+        lo, hi = _rank_rows(n)
         if dist is not None:
             ws, rk = dist.get_world_size(), dist.get_rank()
-            lo, hi = (n * rk) // ws, (n * (rk + 1)) // ws
             if getattr(eng, "_comm_world", None) != (ws, rk):   # one communicator per engine
                 uid = [Engine.nccl_unique_id() if rk == 0 else None]
                 dist.broadcast_object_list(uid, src=0)
                 eng.init_comm(uid[0], ws, rk)
-        if int(np.max(self.feature_bin_counts)) > 256:
-            binning.device_bins(X_bin[:1], self.feature_bin_counts)   # raises the ValueError
-        # uint16 (the reference's bin dtype) and uint8 ids go up as they are;
-        # the device clamps and narrows them
-        Xr = X_bin[lo:hi]
-        if Xr.dtype not in (np.uint8, np.uint16):
-            Xr = binning.device_bins(Xr, self.feature_bin_counts)
-        eng.upload_bins(Xr, self.feature_bin_counts)
+        self._check_device_bins()
+        if not isinstance(X_bin, _BinsOnDevice):
+            # uint16 (the reference's bin dtype) and uint8 ids go up as they
+            # are; the device clamps and narrows them
+            Xr = X_bin[lo:hi]
+            if Xr.dtype not in (np.uint8, np.uint16):
+                Xr = binning.device_bins(Xr, self.feature_bin_counts)
+            eng.upload_bins(Xr, self.feature_bin_counts)
         eng.upload_labels(y[lo:hi].astype(np.uint8), w2, self.base_score_, n_global=n)
         self.scale_bits_ = eng.scale_bits()
         params = self._params_struct()
@@ -566,8 +594,17 @@ class HybridHistGBMNumbaV1_0_1:
         X = np.asarray(X)
         if not np.issubdtype(X.dtype, np.floating) or X.dtype == np.float16:
             X = X.astype(np.float64)
-        X_bin = binning.bin_features(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id)
-        return self.predict_proba_binned(X_bin)
+        if X.ndim != 2 or X.shape[1] != self.n_features_in_:
+            raise ValueError(f"X has shape {X.shape}; the model has {self.n_features_in_} features")
+        self._check_device_bins()
+        # rows are binned on the GPU (gbm_predict_raw) and go straight to the ensemble
+        t0 = time.perf_counter()
+        eng = self._get_engine()
+        _, proba = eng.predict_raw(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id,
+                                   self._packed(), len(self.trees), self.learning_rate,
+                                   getattr(self, 'base_score_', 0.0), want_F=False, want_proba=True)
+        self.times['inference'] = (time.perf_counter() - t0) * 1000
+        return np.column_stack([1 - proba, proba])
 
     def predict_proba_binned(self, X_bin):
         """``predict_proba`` on bin ids already produced with this model's edges."""
@@ -586,6 +623,22 @@ class HybridHistGBMNumbaV1_0_1:
     def production_info(self):
         return {"engine": "libgbm_b200 (sm_100a)", "device": self.device,
                 "n_trees": self.n_trees_fitted_, "n_features": self.n_features_in_}
+
+
+class _BinsOnDevice:
+    """Stands for a training matrix that was binned straight into the engine."""
+
+    def __init__(self, shape):
+        self.shape = shape
+
+
+def _rank_rows(n):
+    """This rank's contiguous block of rows (all rows without torch.distributed)."""
+    dist = _dist()
+    if dist is None:
+        return 0, n
+    ws, rk = dist.get_world_size(), dist.get_rank()
+    return (n * rk) // ws, (n * (rk + 1)) // ws
 
 
 def _predict_tree_host(X_bin, tree):

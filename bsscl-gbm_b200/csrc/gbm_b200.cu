@@ -42,7 +42,9 @@
 #include <vector>
 
 #include "../../include/gbm_b200.h"
+#include "binning_internal.h"
 #include "comm.h"
+#include "h2d.h"
 #include "sampler_internal.h"
 #include "gbm_kernels.cuh"
 
@@ -163,6 +165,11 @@ struct gbm_ctx {
     int32_t p_trees_cap = 0;
     int32_t p_nfeat = 0;
     double *d_pF = nullptr, *d_pP = nullptr;
+
+    // uploads and binning
+    gbmh2d::Stager *stager = nullptr;  // pinned ring + copy threads for host -> device streams
+    uint8_t *d_upstage = nullptr;      // device side of one upload chunk
+    gbmbin::Work *bw = nullptr;        // the raw matrix as order keys, sort buffers, tables
 
     // instrumentation
     long long launches = 0;          // every kernel this context launched
@@ -1204,9 +1211,9 @@ int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int
 
 // Row-major bins [n][p] of type T -> column blocks on the device, clamped
 // to bin_count - 1.
-template <typename T>
-int upload_bins_t(gbm_ctx *ctx, const T *xbin, int64_t n, int32_t p, const int32_t *bin_counts) {
-    if (!ctx || !xbin || !bin_counts || n <= 0 || p <= 0 || n > 0x7fffffffLL) return GBM_ERR_ARG;
+// Sizes, bin counts and the training matrix buffer for n rows x p features.
+int begin_bins(gbm_ctx *ctx, int64_t n, int32_t p, const int32_t *bin_counts) {
+    if (!ctx || !bin_counts || n <= 0 || p <= 0 || n > 0x7fffffffLL) return GBM_ERR_ARG;
     if (ctx->dev < 0) return GBM_ERR_STATE;
     for (int j = 0; j < p; j++)
         if (bin_counts[j] < 1 || bin_counts[j] > kBins)
@@ -1215,38 +1222,58 @@ int upload_bins_t(gbm_ctx *ctx, const T *xbin, int64_t n, int32_t p, const int32
     CK(cudaSetDevice(ctx->dev));
     ctx->n = n; ctx->p = p; ctx->nblk = (p + kBlk - 1) / kBlk;
     ctx->slots_ready = false;
+    ctx->have_bins = ctx->have_labels = false;
     ctx->counts.assign(bin_counts, bin_counts + p);
     TRY(dalloc(ctx, &ctx->d_xb, (size_t)ctx->nblk * n * kBlk));
     TRY(dalloc(ctx, &ctx->d_counts, (size_t)p));
     CK(cudaMemcpyAsync(ctx->d_counts, bin_counts, sizeof(int32_t) * p, cudaMemcpyHostToDevice, ctx->st));
-    // stream row chunks through a staging buffer and transpose to column blocks
-    int64_t chunk_rows = std::max<int64_t>(1, (int64_t)(64 << 20) / ((int64_t)p * (int64_t)sizeof(T)));
-    chunk_rows = std::min(chunk_rows, n);
-    T *stage = nullptr;
-    TRY(dalloc(ctx, &stage, (size_t)(chunk_rows * p)));
-    int rc = GBM_OK;
-    for (int64_t r0 = 0; r0 < n && rc == GBM_OK; r0 += chunk_rows) {
-        int64_t rows = std::min(chunk_rows, n - r0);
-        cudaError_t e = cudaMemcpyAsync(stage, xbin + r0 * p, sizeof(T) * (size_t)(rows * p), cudaMemcpyHostToDevice,
-                                        ctx->st);
-        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "bin upload: %s", cudaGetErrorString(e)); break; }
-        k_pack_bins<T><<<grid_for(rows * ctx->nblk, 256), 256, 0, ctx->st>>>(stage, rows, p, r0, n, ctx->nblk,
-                                                                           ctx->d_counts, ctx->d_xb);
-        e = cudaGetLastError();
-        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "k_pack_bins: %s", cudaGetErrorString(e)); break; }
-        e = cudaStreamSynchronize(ctx->st);
-        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "bin upload sync: %s", cudaGetErrorString(e)); break; }
-    }
-    cudaFree(stage);
-    if (rc != GBM_OK) return rc;
+    return GBM_OK;
+}
+
+// Everything that depends on the bins once they are on the device.
+int finish_bins(gbm_ctx *ctx) {
+    TRY(sync_stream(ctx));
     TRY(choose_skip_bins(ctx));
     TRY(alloc_round_fixed(ctx));
-    TRY(dalloc(ctx, &ctx->d_y, (size_t)n));
-    TRY(dalloc(ctx, &ctx->d_F, (size_t)n));
-    TRY(dalloc(ctx, &ctx->d_q, (size_t)n));
+    TRY(dalloc(ctx, &ctx->d_y, (size_t)ctx->n));
+    TRY(dalloc(ctx, &ctx->d_F, (size_t)ctx->n));
+    TRY(dalloc(ctx, &ctx->d_q, (size_t)ctx->n));
     ctx->have_bins = true;
     ctx->have_labels = false;
     return GBM_OK;
+}
+
+int ensure_uploads(gbm_ctx *ctx) {
+    if (!ctx->stager) ctx->stager = gbmh2d::stager_create();
+    if (!ctx->d_upstage) TRY(dalloc(ctx, &ctx->d_upstage, gbmh2d::chunk_bytes()));
+    if (!ctx->bw) ctx->bw = gbmbin::work_create();
+    return GBM_OK;
+}
+
+// Row-major uint8/uint16 ids -> column blocks: rows stream through pinned
+// buffers (uint16 narrowed to uint8 on the host, halving the copy), each
+// chunk is transposed and clamped to bin_count - 1 on the device.
+template <typename T>
+int upload_bins_t(gbm_ctx *ctx, const T *xbin, int64_t n, int32_t p, const int32_t *bin_counts) {
+    if (!xbin) return GBM_ERR_ARG;
+    TRY(begin_bins(ctx, n, p, bin_counts));
+    TRY(ensure_uploads(ctx));
+    uint8_t *stage = ctx->d_upstage;
+    const int nblk = ctx->nblk;
+    auto dst = [stage](int64_t, int64_t) { return static_cast<void *>(stage); };
+    auto after = [&](int64_t r0, int64_t nr, const void *) -> int {
+        k_pack_bins<uint8_t><<<grid_for(nr * nblk, 256), 256, 0, ctx->st>>>(stage, nr, p, r0, n, nblk,
+                                                                           ctx->d_counts, ctx->d_xb);
+        cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) return 0;
+        ctx->err = std::string("k_pack_bins: ") + cudaGetErrorString(e);
+        return GBM_ERR_CUDA;
+    };
+    std::string err;
+    const gbmh2d::Pack pk = sizeof(T) == 2 ? gbmh2d::Pack::U16toU8 : gbmh2d::Pack::Copy;
+    if (gbmh2d::stream_rows(ctx->stager, ctx->st, xbin, n, sizeof(T) * (size_t)p, pk, 0, dst, after, err))
+        return fail(ctx, GBM_ERR_CUDA, "bin upload: %s", err.empty() ? ctx->err.c_str() : err.c_str());
+    return finish_bins(ctx);
 }
 
 }  // namespace
@@ -1373,6 +1400,8 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
         if (ctx->cst) cudaStreamSynchronize(ctx->cst);
     }
     drop_graphs(ctx);   // graphs may hold collectives: release them first
+    gbmh2d::stager_destroy(ctx->stager);
+    gbmbin::work_destroy(ctx->bw);
     for (auto &s : ctx->slot)
         for (cudaEvent_t e : s.tev) cudaEventDestroy(e);
     if (ctx->comm) gbm_comm_destroy(ctx->comm);
@@ -1383,7 +1412,8 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
                         ctx->d_count64, ctx->d_nodes, ctx->d_lvl[0], ctx->d_lvl[1], ctx->d_ints, ctx->d_tree,
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
                         ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,
-                        ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi, ctx->d_side};
+                        ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi, ctx->d_side,
+                        ctx->d_upstage};
     for (int32_t *q : ctx->d_perm) if (q) cudaFree(q);
     for (void *p : dev_ptrs) if (p) cudaFree(p);
     void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_mono};
@@ -1432,6 +1462,55 @@ int gbm_upload_bins_u16(gbm_ctx *ctx, const uint16_t *xbin, int64_t n, int32_t p
     return upload_bins_t(ctx, xbin, n, p, bin_counts);
 }
 
+// ---- binning on the device ------------------------------------------------------
+
+static int bin_fail(gbm_ctx *ctx, const std::string &err) {
+    const bool arg = err.rfind("binning:", 0) == 0;
+    return fail(ctx, arg ? GBM_ERR_ARG : GBM_ERR_CUDA, "%s", err.c_str());
+}
+
+int gbm_bin_edges(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t dtype, int32_t n_bins,
+                  const uint8_t *is_cat, double *edges_out, int32_t stride, int32_t *counts_out,
+                  int32_t *nan_bin_out, int32_t *max_b_out) {
+    if (!ctx || !X || !edges_out || !counts_out || !nan_bin_out || n <= 0 || p <= 0) return GBM_ERR_ARG;
+    if (ctx->dev < 0) return GBM_ERR_STATE;
+    CK(cudaSetDevice(ctx->dev));
+    TRY(ensure_uploads(ctx));
+    std::string err;
+    if (gbmbin::load(ctx->bw, ctx->stager, ctx->st, X, n, p, dtype, err)) return bin_fail(ctx, err);
+    if (gbmbin::edges(ctx->bw, ctx->st, n_bins, is_cat, edges_out, stride, counts_out, nan_bin_out, max_b_out, err))
+        return bin_fail(ctx, err);
+    return GBM_OK;
+}
+
+int gbm_upload_binned_rows(gbm_ctx *ctx, int64_t row_lo, int64_t row_hi, const double *edges, int32_t stride,
+                           const int32_t *counts, const int32_t *nan_bin) {
+    if (!ctx || !edges || !counts || !nan_bin) return GBM_ERR_ARG;
+    int64_t n = 0;
+    int p = 0;
+    if (!ctx->bw || !gbmbin::shape(ctx->bw, n, p)) return fail(ctx, GBM_ERR_STATE, "call gbm_bin_edges first");
+    if (row_lo < 0 || row_hi > n || row_hi <= row_lo) return fail(ctx, GBM_ERR_ARG, "bad row range");
+    TRY(begin_bins(ctx, row_hi - row_lo, p, counts));
+    std::string err;
+    if (gbmbin::bin_blocks(ctx->bw, ctx->st, row_lo, row_hi, edges, stride, counts, nan_bin, ctx->d_xb, err))
+        return bin_fail(ctx, err);
+    TRY(finish_bins(ctx));
+    gbmbin::release(ctx->bw);   // the keys and sort buffers are not needed after the upload
+    return GBM_OK;
+}
+
+int gbm_bin_features(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t dtype, const double *edges,
+                     int32_t stride, const int32_t *counts, const int32_t *nan_bin, uint16_t *out) {
+    if (!ctx || !X || !edges || !counts || !nan_bin || !out || n <= 0 || p <= 0) return GBM_ERR_ARG;
+    if (ctx->dev < 0) return GBM_ERR_STATE;
+    CK(cudaSetDevice(ctx->dev));
+    TRY(ensure_uploads(ctx));
+    std::string err;
+    if (gbmbin::bin_rows(ctx->bw, ctx->stager, ctx->st, X, n, p, dtype, edges, stride, counts, nan_bin, 1, out, err))
+        return bin_fail(ctx, err);
+    return sync_stream(ctx);
+}
+
 int gbm_upload_labels(gbm_ctx *ctx, const uint8_t *y, const double class_w[2], double base_score,
                       int64_t n_global) {
     if (!ctx || !y || !class_w) return GBM_ERR_ARG;
@@ -1444,10 +1523,8 @@ int gbm_upload_labels(gbm_ctx *ctx, const uint8_t *y, const double class_w[2], d
     ctx->n_global = n_global > 0 ? n_global : ctx->n;
     ctx->S = scale_bits_for(std::max(class_w[0], class_w[1]));
     CK(cudaMemcpyAsync(ctx->d_y, y, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
-    std::vector<double> F0((size_t)ctx->n, base_score);
-    CK(cudaMemcpyAsync(ctx->d_F, F0.data(), sizeof(double) * ctx->n, cudaMemcpyHostToDevice, ctx->st));
     double scale = std::ldexp(1.0, ctx->S);
-    k_init_grad<<<grid_for(ctx->n, 256), 256, 0, ctx->st>>>(ctx->d_F, ctx->d_y, ctx->n, ctx->w[0], ctx->w[1],
+    k_init_grad<<<grid_for(ctx->n, 256), 256, 0, ctx->st>>>(ctx->d_F, ctx->d_y, ctx->n, base_score, ctx->w[0], ctx->w[1],
                                                              scale, ctx->d_q);
     CKL();
     TRY(sync_stream(ctx));
@@ -1728,8 +1805,7 @@ int gbm_predict_set_model(gbm_ctx *ctx, const gbm_packed *m, int32_t n_features)
     return sync_stream(ctx);
 }
 
-int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p) {
-    if (!ctx || !xbin || n <= 0 || p <= 0) return GBM_ERR_ARG;
+static int predict_alloc(gbm_ctx *ctx, int64_t n, int32_t p) {
     if (ctx->dev < 0) return GBM_ERR_STATE;
     if (ctx->p_nfeat && p != ctx->p_nfeat) return fail(ctx, GBM_ERR_ARG, "X has %d features, model %d", p, ctx->p_nfeat);
     CK(cudaSetDevice(ctx->dev));
@@ -1739,10 +1815,41 @@ int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p) 
     }
     TRY(dalloc(ctx, &ctx->d_pF, (size_t)n));
     TRY(dalloc(ctx, &ctx->d_pP, (size_t)n));
-    CK(cudaMemcpyAsync(ctx->d_px, xbin, (size_t)(n * p), cudaMemcpyHostToDevice, ctx->st));
+    TRY(ensure_uploads(ctx));
     ctx->pn = n;
     ctx->pp = p;
     return GBM_OK;
+}
+
+int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p) {
+    if (!ctx || !xbin || n <= 0 || p <= 0) return GBM_ERR_ARG;
+    TRY(predict_alloc(ctx, n, p));
+    uint8_t *px = ctx->d_px;
+    auto dst = [px, p](int64_t r0, int64_t) { return static_cast<void *>(px + r0 * p); };
+    std::string err;
+    if (gbmh2d::stream_rows(ctx->stager, ctx->st, xbin, n, (size_t)p, gbmh2d::Pack::Copy, 0, dst, nullptr, err))
+        return fail(ctx, GBM_ERR_CUDA, "predict upload: %s", err.c_str());
+    return GBM_OK;
+}
+
+int gbm_predict_upload_raw(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t dtype, const double *edges,
+                           int32_t stride, const int32_t *counts, const int32_t *nan_bin) {
+    if (!ctx || !X || !edges || !counts || !nan_bin || n <= 0 || p <= 0) return GBM_ERR_ARG;
+    TRY(predict_alloc(ctx, n, p));
+    std::string err;
+    if (gbmbin::bin_rows(ctx->bw, ctx->stager, ctx->st, X, n, p, dtype, edges, stride, counts, nan_bin, 0,
+                         ctx->d_px, err))
+        return bin_fail(ctx, err);
+    return GBM_OK;
+}
+
+int gbm_predict_raw(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t dtype, const double *edges,
+                    int32_t stride, const int32_t *counts, const int32_t *nan_bin, const gbm_packed *model,
+                    double lr, double base, double *F_out, double *proba_out) {
+    TRY(gbm_predict_set_model(ctx, model, p));
+    TRY(gbm_predict_upload_raw(ctx, X, n, p, dtype, edges, stride, counts, nan_bin));
+    TRY(gbm_predict_run(ctx, lr, base));
+    return gbm_predict_fetch(ctx, F_out, proba_out);
 }
 
 int gbm_predict_run(gbm_ctx *ctx, double lr, double base) {

@@ -64,13 +64,15 @@ __global__ void k_bincount(const uint8_t *__restrict__ xb, int64_t n, int nblk,
         if (s[k]) atomicAdd(&cnt[(int64_t)blk * kBlk * kBins + k], (unsigned long long)s[k]);
 }
 
-__global__ void k_init_grad(const double *__restrict__ F, const uint8_t *__restrict__ y, int64_t n,
+// F = base score for every row (E:2837), and the first round's quantised (g, h).
+__global__ void k_init_grad(double *__restrict__ F, const uint8_t *__restrict__ y, int64_t n, double base,
                             double w0, double w1, double scale, longlong2 *__restrict__ q) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
+    F[i] = base;
     int yi = y[i];
     double g, h, p;
-    grad_hess(F[i], yi, yi ? w1 : w0, g, h, p);
+    grad_hess(base, yi, yi ? w1 : w0, g, h, p);
     q[i] = make_longlong2(__double2ll_rn(__dmul_rn(g, scale)), __double2ll_rn(__dmul_rn(h, scale)));
 }
 

@@ -22,6 +22,8 @@
  *                       predict_proba (E:3318-3336).
  *   gbm_sampler_*       _get_subsample_indices (E:2502-2517) on the
  *                       RandomState(random_state) stream (E:3159).
+ *   gbm_bin_edges       _build_bin_edges (E:2073-2141), sample_weight=None.
+ *   gbm_bin_features    _bin_features (E:2144-2189).
  */
 #ifndef GBM_B200_H
 #define GBM_B200_H
@@ -121,6 +123,40 @@ int gbm_upload_bins(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p,
 int gbm_upload_bins_u16(gbm_ctx *ctx, const uint16_t *xbin, int64_t n, int32_t p,
                         const int32_t *bin_counts);
 
+/* ---- binning on the device --------------------------------------------- */
+
+/* Bin edges of a raw feature matrix, computed on the GPU exactly as
+ * _build_bin_edges (E:2073-2141) computes them for sample_weight=None:
+ * NaN bin 0 for features with NaN, the sorted distinct values when there
+ * are at most n_bins (- 1 with a NaN bin) of them, else np.percentile at
+ * linspace(0, 1, k) (NumPy's 'linear' arithmetic) made unique, then the
+ * appended e[-1] + 1e-8 in the values' dtype.  X is host row-major [n][p],
+ * dtype 0 = float32, 1 = float64.  is_cat: NULL or [p] flags of categorical
+ * features (edges arange(-0.5, 64.5), 64 bins, E:2086-2090).  edges_out is
+ * [p][stride] float64 with stride >= max(n_bins + 2, 65); each row is padded
+ * with its last edge, so edges_out[:, :max_b] is the reference's edges_2d,
+ * counts_out its bin_counts, nan_bin_out its _nan_bin_id (0 or -1) and
+ * *max_b_out = max(counts) + 1.  n_bins in 2..1023.  The matrix stays on the
+ * device for gbm_upload_binned_rows. */
+int gbm_bin_edges(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t dtype, int32_t n_bins,
+                  const uint8_t *is_cat, double *edges_out, int32_t stride, int32_t *counts_out,
+                  int32_t *nan_bin_out, int32_t *max_b_out);
+
+/* The training matrix from rows [row_lo, row_hi) of the matrix last given to
+ * gbm_bin_edges, binned on the GPU with the given edges (_bin_features,
+ * E:2144-2189) and stored like gbm_upload_bins stores its rows (bin counts
+ * <= 256).  Replaces the host binning + gbm_upload_bins of a raw matrix;
+ * frees the matrix kept by gbm_bin_edges. */
+int gbm_upload_binned_rows(gbm_ctx *ctx, int64_t row_lo, int64_t row_hi, const double *edges,
+                           int32_t stride, const int32_t *counts, const int32_t *nan_bin);
+
+/* The reference's raw bin ids of a host matrix (_bin_features, E:2144-2189),
+ * computed on the GPU: out is host uint16 [n][p].  edges/counts/nan_bin as
+ * gbm_bin_edges returns them (bin counts <= 1024). */
+int gbm_bin_features(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t dtype,
+                     const double *edges, int32_t stride, const int32_t *counts,
+                     const int32_t *nan_bin, uint16_t *out);
+
 /* Labels (0/1) of this rank's rows, the two class weights of
  * _compute_class_weights (E:2570-2603) and the base score (E:2829-2835).
  * Resets F to base_score and computes round-0 gradients.  `n_global` is the
@@ -186,6 +222,18 @@ int gbm_predict_set_model(gbm_ctx *ctx, const gbm_packed *model, int32_t n_featu
 int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p);
 int gbm_predict_run(gbm_ctx *ctx, double learning_rate, double base_score);
 int gbm_predict_fetch(gbm_ctx *ctx, double *F_out, double *proba_out);
+
+/* predict_proba from a raw host matrix (E:3274-3336): the rows are binned on
+ * the GPU (_bin_features, E:2144-2189) into the predict input, then the
+ * ensemble runs as in gbm_predict.  gbm_predict_upload_raw is the upload
+ * step of the device-resident sequence above. */
+int gbm_predict_upload_raw(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t dtype,
+                           const double *edges, int32_t stride, const int32_t *counts,
+                           const int32_t *nan_bin);
+int gbm_predict_raw(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t dtype,
+                    const double *edges, int32_t stride, const int32_t *counts,
+                    const int32_t *nan_bin, const gbm_packed *model, double learning_rate,
+                    double base_score, double *F_out, double *proba_out);
 
 /* Ensemble predict that allocates nothing.  No counterpart in the reference:
  * this entry point exists for callers that cannot allocate device memory --
