@@ -620,6 +620,118 @@ class HybridHistGBMNumbaV1_0_1:
         proba = self.predict_proba(X)
         return self.classes_[(proba[:, 1] > 0.5).astype(int)]
 
+    # ------------------------------------------------------------------
+    # model JSON (E:4035-4205)
+    # ------------------------------------------------------------------
+    _RESOLVED = ('n_estimators', 'max_depth', 'learning_rate', 'n_bins', 'min_child_weight', 'gamma',
+                 'subsample', 'colsample_bytree', 'max_leaves', 'reg_lambda', 'binning_strategy')
+
+    def save_model(self, filepath):
+        """JSON in the reference's layout (``save_model``, E:4035-4107), plus
+        two keys the reference does not write: ``_nan_bin_id`` (the reference
+        drops it and reloads every feature as NaN-free, E:4198-4200, which
+        bins NaN rows differently after a reload) and ``resolved_params``
+        (the hyper-parameters 'auto' resolved to, so a reloaded model predicts
+        with the learning rate it was trained with).  The reference's
+        ``load_model`` ignores both."""
+        import json
+        data = {
+            'version': '1.2.2',
+            'params': {},
+            'n_classes_': int(self.n_classes_),
+            'classes_': self.classes_.tolist() if self.classes_ is not None else None,
+            'n_features_in_': int(self.n_features_in_) if self.n_features_in_ is not None else None,
+            'objective': self.objective,
+            '_is_multiclass': self._is_multiclass,
+            'init_score_': float(self.init_score_),
+            'base_score_': float(getattr(self, 'base_score_', 0.0)),
+            'n_trees_fitted_': int(self.n_trees_fitted_),
+            'best_iteration_': int(self.best_iteration_),
+            'train_loss_history_': [float(x) for x in self.train_loss_history_],
+            'val_loss_history_': [float(x) for x in self.val_loss_history_],
+            '_max_bins': int(self._max_bins),
+        }
+        for k, v in self.get_params().items():
+            if not callable(v):
+                data['params'][k] = v
+        if self.bin_edges is not None:
+            data['bin_edges'] = np.asarray(self.bin_edges).tolist()
+        if self.feature_bin_counts is not None:
+            data['feature_bin_counts'] = np.asarray(self.feature_bin_counts).tolist()
+        data['trees'] = [{
+            'features': np.asarray(t[0]).tolist(), 'thresholds': np.asarray(t[1]).tolist(),
+            'values': np.asarray(t[2]).tolist(), 'left': np.asarray(t[3]).tolist(),
+            'right': np.asarray(t[4]).tolist(), 'node_count': int(t[5]),
+            'split_gains': np.asarray(t[6]).tolist() if len(t) > 6 else [],
+        } for t in self.trees]
+        if self.feature_importances_ is not None:
+            data['feature_importances_'] = np.asarray(self.feature_importances_).tolist()
+        if self.feature_split_counts_ is not None:
+            data['feature_split_counts_'] = np.asarray(self.feature_split_counts_).tolist()
+        data['_categorical_set'] = list(self._categorical_set) if hasattr(self, '_categorical_set') else []
+        if getattr(self, '_is_categorical', None) is not None:
+            data['_is_categorical'] = np.asarray(self._is_categorical).tolist()
+        if self._nan_bin_id is not None:
+            data['_nan_bin_id'] = np.asarray(self._nan_bin_id).tolist()
+        data['resolved_params'] = {k: getattr(self, k) for k in self._RESOLVED}
+        with open(filepath, 'w') as f:
+            json.dump(data, f)
+
+    @classmethod
+    def load_model(cls, filepath):
+        """Loads a model written by :meth:`save_model` or by the reference's
+        own ``save_model`` (``load_model``, E:4109-4205).  Without
+        ``_nan_bin_id`` every feature is taken as NaN-free, as the reference
+        does."""
+        import json
+        with open(filepath) as f:
+            data = json.load(f)
+        model = cls(**data['params'])
+        model.n_classes_ = data['n_classes_']
+        model.classes_ = np.array(data['classes_']) if data['classes_'] is not None else None
+        model.n_features_in_ = data['n_features_in_']
+        model.objective = data['objective']
+        model._is_multiclass = data['_is_multiclass']
+        if model._is_multiclass or 'mc_trees' in data:
+            raise NotImplementedError("multi-class softmax is not on the B200 engine")
+        model.init_score_ = data['init_score_']
+        model.base_score_ = data.get('base_score_', 0.0)
+        model.n_trees_fitted_ = data['n_trees_fitted_']
+        model.best_iteration_ = data['best_iteration_']
+        model.train_loss_history_ = data['train_loss_history_']
+        model.val_loss_history_ = data['val_loss_history_']
+        model._max_bins = data['_max_bins']
+        if 'bin_edges' in data:
+            model.bin_edges = np.array(data['bin_edges'], dtype=np.float64)
+        if 'feature_bin_counts' in data:
+            model.feature_bin_counts = np.array(data['feature_bin_counts'], dtype=np.int32)
+        model.trees = []
+        for td in data.get('trees', []):
+            sg = np.array(td.get('split_gains', [0.0] * td['node_count']), dtype=np.float64)
+            model.trees.append((np.array(td['features'], dtype=np.int32),
+                                np.array(td['thresholds'], dtype=np.int64),
+                                np.array(td['values'], dtype=np.float64),
+                                np.array(td['left'], dtype=np.int32),
+                                np.array(td['right'], dtype=np.int32),
+                                int(td['node_count']), sg))
+        if 'feature_importances_' in data:
+            model.feature_importances_ = np.array(data['feature_importances_'])
+        if 'feature_split_counts_' in data:
+            model.feature_split_counts_ = np.array(data['feature_split_counts_'])
+        model._categorical_set = set(data.get('_categorical_set', []))
+        if data.get('_is_categorical') is not None:
+            model._is_categorical = np.array(data['_is_categorical'], dtype=np.bool_)
+        model.binning_strategy = (model.binning_strategy_init if model.binning_strategy_init != 'auto'
+                                  else 'standard')
+        for k, v in data.get('resolved_params', {}).items():
+            setattr(model, k, v)
+        if data.get('_nan_bin_id') is not None:
+            model._nan_bin_id = np.array(data['_nan_bin_id'], dtype=np.int32)
+        elif model.n_features_in_ is not None:
+            model._nan_bin_id = np.full(model.n_features_in_, -1, dtype=np.int32)
+        model._pack_trees()
+        return model
+
     def production_info(self):
         return {"engine": "libgbm_b200 (sm_100a)", "device": self.device,
                 "n_trees": self.n_trees_fitted_, "n_features": self.n_features_in_}

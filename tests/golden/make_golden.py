@@ -29,12 +29,34 @@ def sha(a):
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
 
-def main(ref_src):
+def model_json_case(E, D):
+    """A reference fit saved with its own save_model (E:4035-4107), plus the
+    reference's predict_proba before and after its own load_model."""
+    X, y = D.config3(n=25_000)
+    m = E.HybridHistGBMNumbaV1_0_1(n_estimators=12, max_depth=6, learning_rate=0.1,
+                                   class_weight="balanced_sqrt", n_bins=255, random_state=0,
+                                   verbose=False)
+    m.fit(X[:20_000], y[:20_000])
+    path = os.path.join(HERE, "model_ref_cfg3.json")
+    m.save_model(path)
+    back = E.HybridHistGBMNumbaV1_0_1.load_model(path)
+    np.savez_compressed(os.path.join(HERE, "model_ref_cfg3.npz"),
+                        proba_test=m.predict_proba(X[20_000:]),
+                        proba_test_loaded=back.predict_proba(X[20_000:]))
+    return {"model_ref_cfg3": (len(m.trees),)}
+
+
+def main(ref_src, only=None):
     sys.path.insert(0, ref_src)
     import bsscl_gbm.estimator_v1_0_1 as E
     from bsscl_gbm_b200 import datasets as D
 
     out = {}
+    if only == "model":
+        out.update(model_json_case(E, D))
+        for k, v in out.items():
+            print(k, v)
+        return
 
     # ------------------------------------------------------------------
     # 1. Bin edges + binning (E:2073-2189, E:155-226)
@@ -265,10 +287,14 @@ def main(ref_src):
     fit_case("cfg1_level", Xtr[:4000], ytr[:4000], Xte,
              dict(n_estimators=20, max_depth=4, learning_rate=0.1, n_bins=64,
                   class_weight="balanced", random_state=3, grow_policy="level"))
+    out.update(model_json_case(E, D))
 
     for k, v in out.items():
         print(k, v)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    # python make_golden.py <reference>/src [model]   ('model': only the save_model fixture)
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference>/src [model]")
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else None)
