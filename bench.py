@@ -499,6 +499,8 @@ def run_engine(args):
                 "host_wait_device": st["host_sync_ms"] / args.steps,
                 "host_replay": st["host_replay_ms"] / args.steps,
                 "host_collective_calls": st["host_comm_ms"] / args.steps,
+                "collectives_device": st["comm_ms"] / args.steps,
+                "collective_mb": st["comm_bytes"] / args.steps / 1e6,
                 "l2_flush_excluded": st["flush_ms"] / args.steps,
                 "waves": st["waves"] / args.steps},
             "e2e": ({"value": e2e, "unit": "rounds/s", "h2d_bytes_per_step": int(h2d),

@@ -406,6 +406,7 @@ class HybridHistGBMNumbaV1_0_1:
         self._check_device_bins()
         if on_device:
             lo, hi = _rank_rows(X.shape[0])
+            _ensure_comm(eng)   # the upload all-reduces the bin occupancy (the skipped bin)
             eng.upload_binned_rows(lo, hi, self.bin_edges, self.feature_bin_counts, self._nan_bin_id)
             X_bin = _BinsOnDevice(X.shape)
         else:
@@ -474,14 +475,8 @@ class HybridHistGBMNumbaV1_0_1:
         sampler = Sampler(int(seed), n, p, n_sub, n_feat, self.subsample < 1.0,
                           self.colsample_bytree < 1.0, look_ahead=3)
         eng = self._get_engine()
-        dist = _dist()
         lo, hi = _rank_rows(n)
-        if dist is not None:
-            ws, rk = dist.get_world_size(), dist.get_rank()
-            if getattr(eng, "_comm_world", None) != (ws, rk):   # one communicator per engine
-                uid = [Engine.nccl_unique_id() if rk == 0 else None]
-                dist.broadcast_object_list(uid, src=0)
-                eng.init_comm(uid[0], ws, rk)
+        _ensure_comm(eng)
         self._check_device_bins()
         if not isinstance(X_bin, _BinsOnDevice):
             # uint16 (the reference's bin dtype) and uint8 ids go up as they
@@ -742,6 +737,19 @@ class _BinsOnDevice:
 
     def __init__(self, shape):
         self.shape = shape
+
+
+def _ensure_comm(eng):
+    """One NCCL communicator per engine across fits, made when torch.distributed
+    runs more than one rank (before any upload: the bin upload all-reduces)."""
+    dist = _dist()
+    if dist is None:
+        return
+    ws, rk = dist.get_world_size(), dist.get_rank()
+    if getattr(eng, "_comm_world", None) != (ws, rk):
+        uid = [Engine.nccl_unique_id() if rk == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        eng.init_comm(uid[0], ws, rk)
 
 
 def _rank_rows(n):

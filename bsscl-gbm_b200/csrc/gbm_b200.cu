@@ -131,6 +131,7 @@ struct gbm_ctx {
         cudaGraphExec_t g_cst = nullptr, g_st = nullptr;
         int g_tpairs = 0;
         long long g_launches = 0, g_hist = 0, g_waves = 0;
+        double g_comm_bytes = 0.0;
     };
     static constexpr int kRing = 4;
     Slot slot[kRing];
@@ -177,6 +178,7 @@ struct gbm_ctx {
     long long hist_launches = 0, hist_rows = 0, waves = 0;
     double hist_ms = 0.0, alg_bytes = 0.0, hist_updates = 0.0;
     double host_sample_ms = 0.0, host_sync_ms = 0.0, host_replay_ms = 0.0, host_comm_ms = 0.0;
+    double comm_ms = 0.0, comm_bytes = 0.0;   // collectives: device time (profiling), bytes per rank
     // benchmark aid: an L2 eviction at the start of every round
     uint8_t *d_flush = nullptr;
     size_t flush_bytes = 0;
@@ -260,7 +262,7 @@ int wait_ev(gbm_ctx *ctx, cudaStream_t s, cudaEvent_t ev) {
 }
 
 // A timing pair (start, end) of the current slot's round; kind 0: k_hist,
-// 1: the L2 flush.  Returns the pair's index.
+// 1: the L2 flush, 2: a collective.
 int timing_pair(gbm_ctx *ctx, char kind, cudaEvent_t &e0, cudaEvent_t &e1) {
     gbm_ctx::Slot &s = ctx->slot[ctx->cur_slot];
     while ((int)s.tev.size() < 2 * (s.tused + 1)) {
@@ -282,7 +284,8 @@ int collect_slot_timing(gbm_ctx *ctx, int si) {
     for (int k = s.tdone; k < s.tused; k++) {
         float ms = 0.f;
         CK(cudaEventElapsedTime(&ms, s.tev[(size_t)(2 * k)], s.tev[(size_t)(2 * k + 1)]));
-        (s.tkind[(size_t)k] ? ctx->flush_ms : ctx->hist_ms) += ms;
+        const char kind = s.tkind[(size_t)k];
+        (kind == 0 ? ctx->hist_ms : kind == 1 ? ctx->flush_ms : ctx->comm_ms) += ms;
     }
     s.tdone = s.tused;
     return GBM_OK;
@@ -349,18 +352,33 @@ int sync_stream(gbm_ctx *ctx) {
     return rc;
 }
 
-// In-place sums over the ranks on the engine stream, host time counted.
+// In-place sums over the ranks on the engine stream; host time counted, and
+// device time (waiting for the peers included) when profiling.
 int allreduce_i64(gbm_ctx *ctx, long long *buf, int64_t count) {
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (ctx->profiling) {
+        TRY(timing_pair(ctx, 2, e0, e1));
+        TRY(record_ev(ctx, e0, ctx->st));
+    }
     auto t0 = std::chrono::steady_clock::now();
     int rc = gbm_comm_allreduce_i64(ctx->comm, buf, count, ctx->st, ctx->timeout_ms, ctx->err);
     ctx->host_comm_ms += ms_since(t0);
+    if (rc == GBM_OK && e1) TRY(record_ev(ctx, e1, ctx->st));
+    ctx->comm_bytes += 8.0 * (double)count;
     return rc;
 }
 
 int allreduce_f64(gbm_ctx *ctx, double *buf, int64_t count) {
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (ctx->profiling) {
+        TRY(timing_pair(ctx, 2, e0, e1));
+        TRY(record_ev(ctx, e0, ctx->st));
+    }
     auto t0 = std::chrono::steady_clock::now();
     int rc = gbm_comm_allreduce_f64(ctx->comm, buf, count, ctx->st, ctx->timeout_ms, ctx->err);
     ctx->host_comm_ms += ms_since(t0);
+    if (rc == GBM_OK && e1) TRY(record_ev(ctx, e1, ctx->st));
+    ctx->comm_bytes += 8.0 * (double)count;
     return rc;
 }
 
@@ -1328,6 +1346,7 @@ int capture_round(gbm_ctx *ctx, int si, int nf, const gbm_params *P, int64_t N, 
                   int64_t row_offset) {
     gbm_ctx::Slot &s = ctx->slot[si];
     const long long l0 = ctx->launches, h0 = ctx->hist_launches, w0 = ctx->waves;
+    const double b0 = ctx->comm_bytes;
     ctx->cur_slot = si;
     s.tused = s.tdone = 0;
     TRY(capture(ctx, ctx->cst, &s.g_cst, [&] { return enqueue_sample(ctx, si, N, m, rows_on, row_offset); }));
@@ -1346,9 +1365,11 @@ int capture_round(gbm_ctx *ctx, int si, int nf, const gbm_params *P, int64_t N, 
     s.g_launches = ctx->launches - l0;
     s.g_hist = ctx->hist_launches - h0;
     s.g_waves = ctx->waves - w0;
+    s.g_comm_bytes = ctx->comm_bytes - b0;
     ctx->launches = l0;   // counted when the graphs run
     ctx->hist_launches = h0;
     ctx->waves = w0;
+    ctx->comm_bytes = b0;
     return GBM_OK;
 }
 
@@ -1443,13 +1464,18 @@ int gbm_ctx_init_comm(gbm_ctx *ctx, const void *uid, int32_t nranks, int32_t ran
     if (ctx->dev < 0) return GBM_ERR_STATE;
     CK(cudaSetDevice(ctx->dev));
     ctx->timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
-    if (ctx->comm) {   // replaced: finish its work first
+    if (ctx->comm) {   // replaced: finish its work and drop the graphs that call it first
         TRY(sync_stream(ctx));
+        drop_graphs(ctx);
         gbm_comm_destroy(ctx->comm);
         ctx->comm = nullptr;
     }
     if (nranks == 1) return GBM_OK;
-    return gbm_comm_create(&ctx->comm, uid, nranks, rank, ctx->timeout_ms, ctx->err);
+    TRY(gbm_comm_create(&ctx->comm, uid, nranks, rank, ctx->timeout_ms, ctx->err));
+    // bins uploaded before the communicator chose their skipped bins from this
+    // rank's rows alone: choose again from the occupancy of all ranks
+    if (ctx->have_bins) TRY(choose_skip_bins(ctx));
+    return GBM_OK;
 }
 
 int gbm_nccl_unique_id(void *uid_out) { return gbm_comm_unique_id(uid_out); }
@@ -1753,6 +1779,7 @@ int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const
         ctx->launches += s.g_launches;
         ctx->hist_launches += s.g_hist;
         ctx->waves += s.g_waves;
+        ctx->comm_bytes += s.g_comm_bytes;
     }
     return GBM_OK;
 }
@@ -1900,6 +1927,8 @@ int gbm_get_stats(gbm_ctx *ctx, gbm_stats *out) {
     out->flush_ms = ctx->flush_ms;
     out->hist_updates = ctx->hist_updates;
     out->host_comm_ms = ctx->host_comm_ms;
+    out->comm_ms = ctx->comm_ms;
+    out->comm_bytes = ctx->comm_bytes;
     return GBM_OK;
 }
 
@@ -1908,6 +1937,7 @@ int gbm_reset_stats(gbm_ctx *ctx) {
     ctx->launches = ctx->hist_launches = ctx->hist_rows = ctx->waves = 0;
     ctx->hist_ms = ctx->alg_bytes = ctx->hist_updates = 0.0;
     ctx->host_sample_ms = ctx->host_sync_ms = ctx->host_replay_ms = ctx->flush_ms = ctx->host_comm_ms = 0.0;
+    ctx->comm_ms = ctx->comm_bytes = 0.0;
     return GBM_OK;
 }
 

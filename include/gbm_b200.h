@@ -102,7 +102,9 @@ const char *gbm_last_error(const gbm_ctx *ctx);
  * the 128-byte ncclUniqueId made by rank 0 and shared by the caller.
  * Histograms are then summed over ranks (exact int64 words), so every rank
  * builds the identical tree from its own row shard.  `timeout_ms` bounds
- * communicator creation and every collective wait. */
+ * communicator creation and every collective wait.  Bins uploaded before
+ * this call are re-scanned with an all-reduce, so every rank must have
+ * uploaded its rows before it, or none. */
 int gbm_ctx_init_comm(gbm_ctx *ctx, const void *uid, int32_t nranks, int32_t rank,
                       int32_t timeout_ms);
 int gbm_nccl_unique_id(void *uid_out /* 128 bytes */);
@@ -286,6 +288,8 @@ typedef struct {
                                   excluded) of the reference's histograms; 6 shared-memory
                                   atomic adds each */
     double host_comm_ms;       /* host time in the collective calls (enqueue) */
+    double comm_ms;            /* device time of the collectives (profiling), waits for peers included */
+    double comm_bytes;         /* bytes this rank all-reduced */
 } gbm_stats;
 
 int gbm_set_profiling(gbm_ctx *ctx, int32_t on);
