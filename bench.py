@@ -339,7 +339,11 @@ def run_engine(args):
     # the K rounds are queued back to back (gbm_fit_rounds: the host waits
     # only for the round four places back); CUDA events on the engine stream
     eng.event(0)
+    # an NVTX range around the timed rounds: ncu --nvtx --nvtx-include "bench_timed_rounds/"
+    # captures only their launches
+    torch.cuda.nvtx.range_push("bench_timed_rounds")
     res = eng.fit_rounds(sampler, lo, prm, cap, args.steps)
+    torch.cuda.nvtx.range_pop()
     eng.event(1)
     eng.sync()
     torch.cuda.synchronize()
