@@ -395,6 +395,7 @@ def run_engine(args):
     m.max_leaves = c["max_leaves"]
     m._engine, m._engine_dev = eng, local
     e2e = None
+    e2e_parts = None
     if not (five and world > 1):   # the estimator takes every row on every rank
         if dist is not None:
             dist.barrier()
@@ -407,6 +408,8 @@ def run_engine(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
         e2e = args.steps / (e2e_ms / 1000.0)
+        e2e_parts = {"total_ms": e2e_ms, "upload_ms": m.times["upload"], "rounds_ms": m.times["rounds"],
+                     "training_ms": m.times["training"]}
     # ---- the whole public fit from raw float32 rows (binning on the GPU) -------
     fit_raw = None
     if X is not None:
@@ -508,7 +511,7 @@ def run_engine(args):
                 "l2_flush_excluded": st["flush_ms"] / args.steps,
                 "waves": st["waves"] / args.steps},
             "e2e": ({"value": e2e, "unit": "rounds/s", "h2d_bytes_per_step": int(h2d),
-                     "d2h_bytes_per_step": int(d2h)} if e2e is not None else
+                     "d2h_bytes_per_step": int(d2h), "parts_ms": e2e_parts} if e2e is not None else
                     {"value": None, "note": "the estimator takes every row on every rank; config 5 ranks "
                                             "hold only their own rows"}),
             "gpu_launches": st["kernel_launches"],

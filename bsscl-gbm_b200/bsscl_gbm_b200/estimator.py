@@ -124,7 +124,7 @@ class HybridHistGBMNumbaV1_0_1:
         self.val_loss_history_ = []
         self.n_trees_fitted_ = 0
         self.best_iteration_ = 0
-        self.times = {'binning': 0.0, 'training': 0.0, 'inference': 0.0}
+        self.times = {'binning': 0.0, 'training': 0.0, 'inference': 0.0, 'upload': 0.0, 'rounds': 0.0}
         self._packed_features = None
         self._packed_thresholds = None
         self._packed_values = None
@@ -478,6 +478,7 @@ class HybridHistGBMNumbaV1_0_1:
         lo, hi = _rank_rows(n)
         _ensure_comm(eng)
         self._check_device_bins()
+        t_up = time.perf_counter()
         if not isinstance(X_bin, _BinsOnDevice):
             # uint16 (the reference's bin dtype) and uint8 ids go up as they
             # are; the device clamps and narrows them
@@ -486,7 +487,9 @@ class HybridHistGBMNumbaV1_0_1:
                 Xr = binning.device_bins(Xr, self.feature_bin_counts)
             eng.upload_bins(Xr, self.feature_bin_counts)
         eng.upload_labels(y[lo:hi].astype(np.uint8), w2, self.base_score_, n_global=n)
+        self.times['upload'] = (time.perf_counter() - t_up) * 1000
         self.scale_bits_ = eng.scale_bits()
+        t_rounds = time.perf_counter()
         params = self._params_struct()
         cap = self._tree_capacity()
         F_val = np.full(len(y_val), self.base_score_) if y_val is not None else None
@@ -529,6 +532,7 @@ class HybridHistGBMNumbaV1_0_1:
                     m += 1
         finally:
             sampler.close()
+        self.times['rounds'] = (time.perf_counter() - t_rounds) * 1000
         self.n_trees_fitted_ = len(self.trees)
 
     # ------------------------------------------------------------------
