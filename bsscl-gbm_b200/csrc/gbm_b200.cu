@@ -85,6 +85,8 @@ struct gbm_ctx {
     int hist_grid = 0;                 // k_hist CTAs: one wave of 2 per SM
     int nf_cap = 0;
     long long *d_pool = nullptr;       // node histograms: slot i = node i
+    long long *d_lpool = nullptr;      // several ranks: this rank's partial histograms, slot i = node i
+    int64_t lpool_words = 0;
     long long *d_stage = nullptr;      // smaller-child histograms of one level
     int stage_slots = 0;
     int nmax = 0;                      // node capacity of the tree table
@@ -546,6 +548,13 @@ int ensure_round_buffers(gbm_ctx *ctx, int nf, const gbm_params *P) {
         ctx->replay_smem = 0;
         if (smem <= kReplaySmemMax) ctx->replay_smem = smem;
     }
+    if (ctx->comm) {
+        const int64_t lw = (int64_t)ctx->nmax * slot_words_for(ctx->nf_cap);
+        if (lw > ctx->lpool_words) {
+            TRY(dalloc(ctx, &ctx->d_lpool, (size_t)lw));
+            ctx->lpool_words = lw;
+        }
+    }
     const int tiles = (int)((ctx->n + kPartTile - 1) / kPartTile) + ctx->stage_slots;
     if (tiles > ctx->tile_cap) {
         ctx->tile_cap = tiles;
@@ -626,19 +635,24 @@ int launch_close(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, bool ro
 
 // Root: histogram of all in-bag rows, its split, the first level list and
 // that level's plan.
+// Several ranks: one all-reduce per histogram level.  The root's row count
+// travels in its staging slot's count word; each level's left counts in the
+// slots' count words (k_stage_left / k_fill_counts), so the partition needs
+// no collective of its own.
 int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, const NextPlan &np) {
     const int64_t words = slot_words_for(rf.nf);
-    const long long *ng = nullptr;
-    if (ctx->comm) {
-        TRY(launch(ctx, k_count64, dim3(1), dim3(1), 0, ctx->st, ctx->d_total, ctx->d_count64));
-        TRY(allreduce_i64(ctx, ctx->d_count64, 1));
-        ng = ctx->d_count64;
-    }
-    TRY(launch(ctx, k_root_plan, dim3(1), dim3(1), 0, ctx->st, ctx->d_total, ng, ctx->d_nodes, ctx->d_htask, ctx->d_hprefix,
-                                      ints(ctx, I_NODES)));
+    long long *cw = ctx->comm ? ctx->d_stage + (int64_t)rf.nf * kBins * kWords + kCountWord : nullptr;
+    TRY(launch(ctx, k_root_plan, dim3(1), dim3(1), 0, ctx->st, ctx->d_total, (const long long *)nullptr, ctx->d_nodes,
+               ctx->d_htask, ctx->d_hprefix, ints(ctx, I_NODES), cw));
     TRY(launch_hist(ctx, rf, ints(ctx, I_ONE)));
-    if (ctx->comm)
+    if (ctx->comm) {
+        // this rank's root partial, for the first level's subtractions
+        CK(cudaMemcpyAsync(ctx->d_lpool, ctx->d_stage, sizeof(long long) * (size_t)words, cudaMemcpyDeviceToDevice,
+                           ctx->st));
         TRY(allreduce_i64(ctx, ctx->d_stage, words));
+        TRY(launch(ctx, k_fill_counts, dim3(1), dim3(32), 0, ctx->st, ctx->d_nodes, (const int *)nullptr,
+                   (const int *)nullptr, (const long long *)ctx->d_stage, rf.nf));
+    }
     int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
     TRY(launch(ctx, k_split_feat<true>, dim3(dim3(fx, 1)), dim3(32 * kSplitWarps), 0, ctx->st, 
         ctx->d_nodes, nullptr, nullptr, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx,
@@ -684,17 +698,17 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
     TRY(launch(ctx, k_part_scatter, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, ctx->d_rows, ctx->d_tmp, ctx->d_ptask, lvl_cnt,
                                                            ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt,
                                                            ctx->d_nleft));
-    const long long *gl = ctx->d_nleft;
-    if (ctx->comm) {
-        CK(cudaMemcpyAsync(ctx->d_nleft_g, ctx->d_nleft, sizeof(long long) * W_ub, cudaMemcpyDeviceToDevice,
-                           ctx->st));
-        TRY(allreduce_i64(ctx, ctx->d_nleft_g, W_ub));
-        gl = ctx->d_nleft_g;
-    }
+    const long long *gl = ctx->comm ? nullptr : ctx->d_nleft;   // several ranks: the locally smaller child
     TRY(launch(ctx, k_plan_hist, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, lvl, lvl_cnt, ctx->d_nleft, gl, ctx->d_htask, ctx->d_hprefix));
     TRY(launch_hist(ctx, rf, lvl_cnt));
-    if (ctx->comm)
+    if (ctx->comm) {
+        const int cx = std::max(1, (2 * ctx->hist_grid + W_ub - 1) / W_ub);
+        TRY(launch(ctx, k_stage_left, dim3(cx, W_ub), dim3(256), 0, ctx->st, (const DNode *)ctx->d_nodes, lvl, lvl_cnt,
+                   ctx->d_htask, ctx->d_stage, ctx->d_lpool, rf.nf, pool_depth(P)));
         TRY(allreduce_i64(ctx, ctx->d_stage, words * W_ub));
+        TRY(launch(ctx, k_fill_counts, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, (const int *)lvl, lvl_cnt,
+                   (const long long *)ctx->d_stage, rf.nf));
+    }
     int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
     TRY(launch(ctx, k_split_feat<false>, dim3(dim3(fx, W_ub)), dim3(32 * kSplitWarps), 0, ctx->st, 
         ctx->d_nodes, lvl, lvl_cnt, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx, ctx->d_counts,
@@ -1428,7 +1442,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     if (ctx->comm) gbm_comm_destroy(ctx->comm);
     void *dev_ptrs[] = {ctx->d_xb, ctx->d_counts, ctx->d_skipb, ctx->d_y, ctx->d_F, ctx->d_q, ctx->d_mask,
                         ctx->d_rows, ctx->d_tmp, ctx->d_cnt, ctx->d_off, ctx->d_total, ctx->d_blist, ctx->d_fidx,
-                        ctx->d_fpos, ctx->d_pool, ctx->d_stage, ctx->d_fbest, ctx->d_htask, ctx->d_hprefix,
+                        ctx->d_fpos, ctx->d_pool, ctx->d_lpool, ctx->d_stage, ctx->d_fbest, ctx->d_htask, ctx->d_hprefix,
                         ctx->d_ptask, ctx->d_tile_cnt, ctx->d_nleft, ctx->d_nleft_g,
                         ctx->d_count64, ctx->d_nodes, ctx->d_lvl[0], ctx->d_lvl[1], ctx->d_ints, ctx->d_tree,
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,

@@ -12,7 +12,8 @@ namespace gbm {
 constexpr int kBins = 256;          // uint8 bin ids
 constexpr int kBlk = 16;            // features per column block (one 16-byte load)
 constexpr int kWords = 4;           // g_hi, g_lo, h_hi, h_lo per histogram cell
-constexpr int kTotWords = 4;        // node totals (G hi/lo, H hi/lo) after the cells
+constexpr int kTotWords = 6;        // after the cells: totals (G hi/lo, H hi/lo), left count, pad
+constexpr int kCountWord = 4;       // the slot's left-count word (multi-rank staging)
 constexpr int kChunk = 16384;       // max rows one CTA adds into one cell (R_max)
 constexpr int kHistThreads = 512;
 constexpr int kDig = 17;            // low/mid digit width of the shared-memory accumulators

@@ -481,12 +481,17 @@ __device__ __forceinline__ DNode fresh_node(int depth, int parent) {
 }
 
 // Root: node 0 holds all in-bag rows; one histogram task over them.
+// With several ranks (stage_count != null) node 0's count is this rank's
+// until k_fill_counts puts the all-reduced one in; the rank's count goes into
+// the root staging slot's count word, summed with the histogram.
 __global__ void k_root_plan(const int32_t *__restrict__ n_local, const long long *__restrict__ n_global,
                             DNode *__restrict__ nodes, HistTask *__restrict__ ht,
-                            int32_t *__restrict__ prefix, int *__restrict__ node_count) {
+                            int32_t *__restrict__ prefix, int *__restrict__ node_count,
+                            long long *__restrict__ stage_count) {
     griddep_wait();
     if (threadIdx.x || blockIdx.x) return;
     long long ns = *n_local;
+    if (stage_count) *stage_count = ns;
     DNode d = fresh_node(0, -1);
     d.begin = 0;
     d.end = ns;
@@ -689,6 +694,9 @@ k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, c
 
 // Level plan after the partition: each parent's smaller child (by global
 // count) becomes a histogram task; the children get their row ranges.
+// gl == null (several ranks): each rank histograms its locally smaller child;
+// k_stage_left turns that into the left child's partial before the all-reduce
+// and k_fill_counts sets the children's global counts after it.
 __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ lvl,
                             const int *__restrict__ lvl_count, const long long *__restrict__ nl_local,
                             const long long *__restrict__ gl, HistTask *__restrict__ ht,
@@ -703,7 +711,8 @@ __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ l
         if (k < W) {
             int i = lvl[k];
             DNode &p = nodes[i];
-            long long nl = nl_local[k], gnl = gl[k], gtot = p.n;
+            long long nl = nl_local[k];
+            long long gnl = gl ? gl[k] : nl, gtot = gl ? p.n : p.end - p.begin;
             bool ls = gnl <= gtot - gnl;
             HistTask t;
             t.begin = ls ? p.begin : p.begin + nl;
@@ -732,6 +741,65 @@ __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ l
         carry += tot;
     }
     if (threadIdx.x == 0) prefix[W] = carry;
+}
+
+// Several ranks, before the staging all-reduce: slot k holds this rank's
+// partial histogram of the child it built (the locally smaller one).  Make it
+// the LEFT child's partial -- parent - right when the right child was built,
+// from this rank's own partials of earlier levels (lpool) -- so that every
+// rank contributes the same child, store both children's partials in lpool
+// (children that will be parents only), and put this rank's left count in the
+// slot's count word.  Integer words throughout: exact.
+__global__ void k_stage_left(const DNode *__restrict__ nodes, const int *__restrict__ lvl,
+                             const int *__restrict__ lvl_count, HistTask *__restrict__ ht,
+                             long long *__restrict__ stage, long long *__restrict__ lpool, int nf, int pool_depth) {
+    griddep_wait();
+    const int k = blockIdx.y;
+    if (k >= *lvl_count) return;
+    const int64_t words = slot_words_for(nf);
+    const int64_t data = (int64_t)nf * kBins * kWords + 4;   // cells and totals
+    const int parent = lvl[k];
+    const DNode &p = nodes[parent];
+    const bool built_left = p.left_small != 0;
+    const bool keep = nodes[p.kid0].depth < pool_depth;
+    long long *st = stage + (int64_t)k * words;
+    const long long *par = lpool + (int64_t)parent * words;
+    long long *lk = lpool + (int64_t)p.kid0 * words, *rk = lpool + (int64_t)p.kid1 * words;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < data; i += (int64_t)gridDim.x * blockDim.x) {
+        const long long s = st[i], pv = par[i];
+        const long long left = built_left ? s : pv - s;
+        st[i] = left;
+        if (keep) {
+            lk[i] = left;
+            rk[i] = pv - left;
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        st[(int64_t)nf * kBins * kWords + kCountWord] = p.nl;
+        ht[k].left_small = 1;   // the split search reads the slot as the left child
+    }
+}
+
+// Several ranks, after the staging all-reduce: the global counts from the
+// slots' count words.  lvl == null: the root (slot 0).
+__global__ void k_fill_counts(DNode *__restrict__ nodes, const int *__restrict__ lvl,
+                              const int *__restrict__ lvl_count, const long long *__restrict__ stage, int nf) {
+    griddep_wait();
+    const int64_t words = slot_words_for(nf);
+    const int64_t cw = (int64_t)nf * kBins * kWords + kCountWord;
+    if (!lvl) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) nodes[0].n = stage[cw];
+        return;
+    }
+    const int W = *lvl_count;
+    for (int k = threadIdx.x; k < W; k += blockDim.x) {
+        DNode &p = nodes[lvl[k]];
+        const long long gnl = stage[(int64_t)k * words + cw];
+        p.gnl = gnl;
+        p.left_small = 1;
+        nodes[p.kid0].n = gnl;
+        nodes[p.kid1].n = p.n - gnl;
+    }
 }
 
 // Last level (every child at max_depth, where no node splits, E:775-777):
