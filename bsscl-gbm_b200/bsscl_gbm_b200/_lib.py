@@ -32,7 +32,7 @@ EXPORTS = (
     "gbm_set_profiling", "gbm_get_stats", "gbm_reset_stats", "gbm_event_record",
     "gbm_event_elapsed", "gbm_predict_noalloc", "gbm_fit_rounds", "gbm_upload_bins_u16",
     "gbm_set_l2_flush", "gbm_bin_edges", "gbm_upload_binned_rows", "gbm_bin_features",
-    "gbm_predict_upload_raw", "gbm_predict_raw",
+    "gbm_predict_upload_raw", "gbm_predict_raw", "gbm_test_peer_wait",
 )
 
 
@@ -135,6 +135,7 @@ def lib():
     L.gbm_predict_upload_raw.argtypes = [P, P, i64, i32, i32, P, i32, P, P]
     L.gbm_predict_raw.argtypes = [P, P, i64, i32, i32, P, i32, P, P, C.POINTER(GbmPacked), f64,
                                   f64, P, P]
+    L.gbm_test_peer_wait.argtypes = [i32, i32]
     L.gbm_predict_noalloc.argtypes = [P, i64, i32, P, P, P, P, P, P, i32, i32, f64, f64, P, P, P,
                                       C.c_char_p, i32]
     _lib = L

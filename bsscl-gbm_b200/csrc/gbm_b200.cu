@@ -87,6 +87,17 @@ struct gbm_ctx {
     long long *d_pool = nullptr;       // node histograms: slot i = node i
     long long *d_lpool = nullptr;      // several ranks: this rank's partial histograms, slot i = node i
     int64_t lpool_words = 0;
+    // Several ranks, peer exchange of the staging slots over NVLink (CUDA IPC;
+    // gbm_kernels.cuh, "the staging exchange").  Off: one NCCL all-reduce per level.
+    bool p2p = false;
+    int64_t p2p_tried_stride = 0;      // the staging size the last setup was made for
+    int p2p_rank = 0, p2p_n = 1;
+    long long *d_pst = nullptr;        // two parity buffers of stage_slots slots (IPC-exported)
+    int64_t pst_stride = 0;            // words per parity buffer
+    unsigned long long *d_sync = nullptr;   // [N) signals from each rank, then kSyncLocal local words (IPC-exported)
+    long long **d_peer_pst = nullptr;       // every rank's d_pst (own at [rank]), device table
+    unsigned long long **d_peer_sync = nullptr;
+    std::vector<void *> ipc_opened;    // peer mappings to close
     long long *d_stage = nullptr;      // smaller-child histograms of one level
     int stage_slots = 0;
     int nmax = 0;                      // node capacity of the tree table
@@ -409,7 +420,7 @@ int ensure_slots(gbm_ctx *ctx) {
             TRY(halloc(ctx, &s.h_feat, (size_t)ctx->p + 2 * ctx->nblk + 2));
             TRY(halloc(ctx, &s.h_fpos, (size_t)ctx->nblk * kBlk + ctx->p));
             TRY(halloc(ctx, &s.h_tout, 1));
-            TRY(halloc(ctx, &s.h_loss, 1));
+            TRY(halloc(ctx, &s.h_loss, 2));   // [0] loss, [1] the peer exchange's error word
             if (!s.copied) CK(cudaEventCreateWithFlags(&s.copied, cudaEventDisableTiming));
             if (!s.done) CK(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
         }
@@ -518,6 +529,133 @@ int level_width(const gbm_params *P, int L) {
     return std::min(w, level_cap(P));
 }
 
+// ---- peer exchange setup (several ranks) -----------------------------------------
+
+// Unmaps the peers' buffers and frees this rank's.  `collective`: the ranks
+// first agree (an all-reduce) that nobody reads them any more.
+int p2p_teardown(gbm_ctx *ctx, bool collective) {
+    if (!ctx->d_pst && !ctx->d_sync && ctx->ipc_opened.empty()) return GBM_OK;
+    if (ctx->st) cudaStreamSynchronize(ctx->st);
+    if (collective && ctx->comm) {
+        TRY(allreduce_i64(ctx, ctx->d_count64, 1));
+        TRY(sync_stream(ctx));
+    }
+    for (void *q : ctx->ipc_opened) cudaIpcCloseMemHandle(q);
+    ctx->ipc_opened.clear();
+    if (collective && ctx->comm) {   // every rank has unmapped this rank's buffers
+        TRY(allreduce_i64(ctx, ctx->d_count64, 1));
+        TRY(sync_stream(ctx));
+    }
+    void *ptrs[] = {ctx->d_pst, ctx->d_sync, ctx->d_peer_pst, ctx->d_peer_sync};
+    for (void *q : ptrs) if (q) cudaFree(q);
+    ctx->d_pst = nullptr;
+    ctx->d_sync = nullptr;
+    ctx->d_peer_pst = nullptr;
+    ctx->d_peer_sync = nullptr;
+    ctx->pst_stride = 0;
+    ctx->p2p = false;
+    ctx->mem_gen++;
+    return GBM_OK;
+}
+
+// Collective: every rank calls it at the same point.  Allocates the two
+// parity staging buffers and the sync words, exchanges their CUDA IPC
+// handles through the communicator (an all-reduce of a zeroed table into
+// which each rank writes its own row) and maps every peer's.  If any rank
+// cannot export or map, all ranks stay on the NCCL all-reduce.
+// GBM_PEER_EXCHANGE=0 turns the exchange off.
+int p2p_setup(gbm_ctx *ctx, int64_t stride) {
+    TRY(p2p_teardown(ctx, true));
+    const char *env = std::getenv("GBM_PEER_EXCHANGE");
+    if (env && env[0] == '0') return GBM_OK;
+    const int N = gbm_comm_size(ctx->comm), rank = gbm_comm_rank(ctx->comm);
+    ctx->p2p_n = N;
+    ctx->p2p_rank = rank;
+    int ok = 1;
+    if (cudaMalloc(&ctx->d_pst, sizeof(long long) * (size_t)(2 * stride)) != cudaSuccess ||
+        cudaMalloc(&ctx->d_sync, sizeof(unsigned long long) * (size_t)(N + kSyncLocal)) != cudaSuccess ||
+        cudaMalloc(&ctx->d_peer_pst, sizeof(long long *) * (size_t)N) != cudaSuccess ||
+        cudaMalloc(&ctx->d_peer_sync, sizeof(unsigned long long *) * (size_t)N) != cudaSuccess)
+        return fail(ctx, GBM_ERR_ALLOC, "peer exchange buffers");
+    ctx->mem_gen++;
+    CK(cudaMemsetAsync(ctx->d_pst, 0, sizeof(long long) * (size_t)(2 * stride), ctx->st));
+    CK(cudaMemsetAsync(ctx->d_sync, 0, sizeof(unsigned long long) * (size_t)(N + kSyncLocal), ctx->st));
+    // the handle table: per rank 2 handles of 64 bytes = 16 int64 words
+    constexpr int kHW = (int)(2 * sizeof(cudaIpcMemHandle_t) / 8);
+    static_assert(2 * sizeof(cudaIpcMemHandle_t) == 8 * kHW, "handle size");
+    std::vector<long long> tab((size_t)N * kHW + 1, 0);
+    cudaIpcMemHandle_t h[2];
+    if (cudaIpcGetMemHandle(&h[0], ctx->d_pst) != cudaSuccess || cudaIpcGetMemHandle(&h[1], ctx->d_sync) != cudaSuccess) {
+        cudaGetLastError();
+        ok = 0;
+    } else {
+        std::memcpy(&tab[(size_t)rank * kHW], h, sizeof h);
+    }
+    tab[(size_t)N * kHW] = ok ? 0 : 1;   // ranks that failed
+    long long *d_tab = nullptr;
+    TRY(dalloc(ctx, &d_tab, tab.size()));
+    CK(cudaMemcpyAsync(d_tab, tab.data(), sizeof(long long) * tab.size(), cudaMemcpyHostToDevice, ctx->st));
+    int rc = allreduce_i64(ctx, d_tab, (int64_t)tab.size());
+    if (rc == GBM_OK) rc = cudaMemcpyAsync(tab.data(), d_tab, sizeof(long long) * tab.size(), cudaMemcpyDeviceToHost,
+                                           ctx->st) == cudaSuccess ? sync_stream(ctx) : GBM_ERR_CUDA;
+    cudaFree(d_tab);
+    if (rc != GBM_OK) return rc;
+    std::vector<long long *> pst((size_t)N, nullptr);
+    std::vector<unsigned long long *> sy((size_t)N, nullptr);
+    pst[(size_t)rank] = ctx->d_pst;
+    sy[(size_t)rank] = ctx->d_sync;
+    if (tab[(size_t)N * kHW] == 0) {
+        for (int q = 0; q < N && ok; q++) {
+            if (q == rank) continue;
+            cudaIpcMemHandle_t hq[2];
+            std::memcpy(hq, &tab[(size_t)q * kHW], sizeof hq);
+            void *a = nullptr, *b = nullptr;
+            if (cudaIpcOpenMemHandle(&a, hq[0], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = 0;
+                break;
+            }
+            ctx->ipc_opened.push_back(a);
+            if (cudaIpcOpenMemHandle(&b, hq[1], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = 0;
+                break;
+            }
+            ctx->ipc_opened.push_back(b);
+            pst[(size_t)q] = static_cast<long long *>(a);
+            sy[(size_t)q] = static_cast<unsigned long long *>(b);
+        }
+    }
+    // every rank must map every peer, or nobody uses the exchange
+    CK(cudaMemsetAsync(ctx->d_count64, 0, sizeof(long long), ctx->st));
+    if (!ok) {
+        long long one = 1;
+        CK(cudaMemcpyAsync(ctx->d_count64, &one, sizeof one, cudaMemcpyHostToDevice, ctx->st));
+    }
+    TRY(allreduce_i64(ctx, ctx->d_count64, 1));
+    long long bad = 0;
+    CK(cudaMemcpyAsync(&bad, ctx->d_count64, sizeof bad, cudaMemcpyDeviceToHost, ctx->st));
+    TRY(sync_stream(ctx));
+    if (bad || tab[(size_t)N * kHW]) return p2p_teardown(ctx, true);
+    CK(cudaMemcpyAsync(ctx->d_peer_pst, pst.data(), sizeof(long long *) * (size_t)N, cudaMemcpyHostToDevice, ctx->st));
+    CK(cudaMemcpyAsync(ctx->d_peer_sync, sy.data(), sizeof(unsigned long long *) * (size_t)N, cudaMemcpyHostToDevice,
+                       ctx->st));
+    TRY(sync_stream(ctx));
+    ctx->pst_stride = stride;
+    ctx->p2p = true;
+    return GBM_OK;
+}
+
+// A round's exchange ran out of time on this rank (the flag copied into the
+// slot's pinned words with the round).
+int p2p_check(gbm_ctx *ctx, int si) {
+    if (!ctx->p2p) return GBM_OK;
+    unsigned long long e = 0;
+    std::memcpy(&e, &ctx->slot[si].h_loss[1], sizeof e);
+    if (e) return fail(ctx, GBM_ERR_TIMEOUT, "peer exchange: a peer did not reach a level in time (a rank may have left)");
+    return GBM_OK;
+}
+
 int ensure_round_buffers(gbm_ctx *ctx, int nf, const gbm_params *P) {
     int need_nf = std::max(nf, 1);
     int stage = std::max(level_cap(P), P->grow_policy == 0 ? P->max_leaves + 2 : 1);
@@ -554,6 +692,11 @@ int ensure_round_buffers(gbm_ctx *ctx, int nf, const gbm_params *P) {
             TRY(dalloc(ctx, &ctx->d_lpool, (size_t)lw));
             ctx->lpool_words = lw;
         }
+        const int64_t stride = (int64_t)ctx->stage_slots * slot_words_for(ctx->nf_cap);
+        if (stride != ctx->p2p_tried_stride) {
+            ctx->p2p_tried_stride = stride;
+            TRY(p2p_setup(ctx, stride));
+        }
     }
     const int tiles = (int)((ctx->n + kPartTile - 1) / kPartTile) + ctx->stage_slots;
     if (tiles > ctx->tile_cap) {
@@ -586,7 +729,9 @@ int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p) {
     }
     TRY(launch(ctx, k_hist, dim3(ctx->hist_grid), dim3(kHistThreads), smem, ctx->st, ctx->d_xb, ctx->n, ctx->d_rows,
                ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p, ctx->d_blist, d_bwp, d_nb, ctx->d_fpos,
-               ctx->d_skipb, rf.nf, ctx->d_q, ctx->d_stage));
+               ctx->d_skipb, rf.nf, ctx->d_q, ctx->p2p ? ctx->d_pst : ctx->d_stage,
+               (const unsigned long long *)(ctx->p2p ? ctx->d_sync + ctx->p2p_n + kSyncLevel : nullptr),
+               ctx->pst_stride));
     if (e1) TRY(record_ev(ctx, e1, ctx->st));
     ctx->hist_launches++;
     return GBM_OK;
@@ -635,23 +780,55 @@ int launch_close(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, bool ro
 
 // Root: histogram of all in-bag rows, its split, the first level list and
 // that level's plan.
-// Several ranks: one all-reduce per histogram level.  The root's row count
+// The limit of one level's wait for the peers: the communicator's timeout,
+// at most GBM_PEER_WAIT_MS (default 10 s; a level takes milliseconds).
+long long peer_wait_ns(const gbm_ctx *ctx) {
+    long long ms = 10000;
+    if (const char *e = std::getenv("GBM_PEER_WAIT_MS")) ms = std::max(1ll, std::atoll(e));
+    return std::min<long long>(ms, ctx->timeout_ms) * 1000000ll;
+}
+
+// The sum over ranks of the level's staging slots into d_stage: the peer
+// exchange (k_peer_sum), or an NCCL all-reduce in place.
+int exchange_stage(gbm_ctx *ctx, const int *lvl_cnt, int W_ub, int nf) {
+    const int64_t words = slot_words_for(nf);
+    if (!ctx->p2p) return allreduce_i64(ctx, ctx->d_stage, words * W_ub);
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (ctx->profiling) {
+        TRY(timing_pair(ctx, 2, e0, e1));
+        TRY(record_ev(ctx, e0, ctx->st));
+    }
+    const int64_t n2 = (int64_t)W_ub * words / 2;
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n2 + 255) / 256, 2 * ctx->hist_grid));
+    TRY(launch(ctx, k_peer_sum, dim3(grid), dim3(256), 0, ctx->st, (const long long *const *)ctx->d_peer_pst,
+               ctx->pst_stride, ctx->d_sync, ctx->p2p_rank, ctx->p2p_n, lvl_cnt, nf, ctx->d_stage, ctx->d_pst,
+               peer_wait_ns(ctx)));
+    if (e1) TRY(record_ev(ctx, e1, ctx->st));
+    ctx->comm_bytes += 8.0 * (double)(words * W_ub) * (ctx->p2p_n - 1);
+    return GBM_OK;
+}
+
+// Several ranks: one exchange per histogram level.  The root's row count
 // travels in its staging slot's count word; each level's left counts in the
 // slots' count words (k_stage_left / k_fill_counts), so the partition needs
 // no collective of its own.
 int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, const NextPlan &np) {
-    const int64_t words = slot_words_for(rf.nf);
-    long long *cw = ctx->comm ? ctx->d_stage + (int64_t)rf.nf * kBins * kWords + kCountWord : nullptr;
+    long long *sbase = ctx->p2p ? ctx->d_pst : ctx->d_stage;
+    unsigned long long *sync = ctx->p2p ? ctx->d_sync : nullptr;
+    const unsigned long long *par = sync ? sync + ctx->p2p_n + kSyncLevel : nullptr;
+    long long *cw = ctx->comm ? sbase + (int64_t)rf.nf * kBins * kWords + kCountWord : nullptr;
     TRY(launch(ctx, k_root_plan, dim3(1), dim3(1), 0, ctx->st, ctx->d_total, (const long long *)nullptr, ctx->d_nodes,
-               ctx->d_htask, ctx->d_hprefix, ints(ctx, I_NODES), cw));
+               ctx->d_htask, ctx->d_hprefix, ints(ctx, I_NODES), cw, par, ctx->pst_stride));
     TRY(launch_hist(ctx, rf, ints(ctx, I_ONE)));
     if (ctx->comm) {
-        // this rank's root partial, for the first level's subtractions
-        CK(cudaMemcpyAsync(ctx->d_lpool, ctx->d_stage, sizeof(long long) * (size_t)words, cudaMemcpyDeviceToDevice,
-                           ctx->st));
-        TRY(allreduce_i64(ctx, ctx->d_stage, words));
+        // this rank's root partial into lpool[0], for the first level's subtractions
+        TRY(launch(ctx, k_stage_left, dim3(std::max(1, 2 * ctx->hist_grid / 8), 1), dim3(256), 0, ctx->st,
+                   (const DNode *)ctx->d_nodes, (const int *)nullptr, (const int *)nullptr, ctx->d_htask, sbase,
+                   ctx->pst_stride, ctx->d_lpool, rf.nf, pool_depth(P), sync,
+                   (unsigned long long *const *)ctx->d_peer_sync, ctx->p2p_rank, ctx->p2p_n));
+        TRY(exchange_stage(ctx, nullptr, 1, rf.nf));
         TRY(launch(ctx, k_fill_counts, dim3(1), dim3(32), 0, ctx->st, ctx->d_nodes, (const int *)nullptr,
-                   (const int *)nullptr, (const long long *)ctx->d_stage, rf.nf));
+                   (const int *)nullptr, (const long long *)ctx->d_stage, rf.nf, sync, ctx->p2p_n));
     }
     int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
     TRY(launch(ctx, k_split_feat<true>, dim3(dim3(fx, 1)), dim3(32 * kSplitWarps), 0, ctx->st, 
@@ -703,11 +880,14 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
     TRY(launch_hist(ctx, rf, lvl_cnt));
     if (ctx->comm) {
         const int cx = std::max(1, (2 * ctx->hist_grid + W_ub - 1) / W_ub);
-        TRY(launch(ctx, k_stage_left, dim3(cx, W_ub), dim3(256), 0, ctx->st, (const DNode *)ctx->d_nodes, lvl, lvl_cnt,
-                   ctx->d_htask, ctx->d_stage, ctx->d_lpool, rf.nf, pool_depth(P)));
-        TRY(allreduce_i64(ctx, ctx->d_stage, words * W_ub));
+        unsigned long long *sync = ctx->p2p ? ctx->d_sync : nullptr;
+        TRY(launch(ctx, k_stage_left, dim3(cx, W_ub), dim3(256), 0, ctx->st, (const DNode *)ctx->d_nodes,
+                   (const int *)lvl, (const int *)lvl_cnt, ctx->d_htask, ctx->p2p ? ctx->d_pst : ctx->d_stage,
+                   ctx->pst_stride, ctx->d_lpool, rf.nf, pool_depth(P), sync,
+                   (unsigned long long *const *)ctx->d_peer_sync, ctx->p2p_rank, ctx->p2p_n));
+        TRY(exchange_stage(ctx, lvl_cnt, W_ub, rf.nf));
         TRY(launch(ctx, k_fill_counts, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, (const int *)lvl, lvl_cnt,
-                   (const long long *)ctx->d_stage, rf.nf));
+                   (const long long *)ctx->d_stage, rf.nf, sync, ctx->p2p_n));
     }
     int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
     TRY(launch(ctx, k_split_feat<false>, dim3(dim3(fx, W_ub)), dim3(32 * kSplitWarps), 0, ctx->st, 
@@ -723,7 +903,11 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
 int fetch_nodes(gbm_ctx *ctx) {
     CK(cudaMemcpyAsync(ctx->h_ints, ctx->d_ints, sizeof(int) * I_COUNT, cudaMemcpyDeviceToHost, ctx->st));
     CK(cudaMemcpyAsync(ctx->h_nodes, ctx->d_nodes, sizeof(DNode) * ctx->nmax, cudaMemcpyDeviceToHost, ctx->st));
+    if (ctx->p2p)
+        CK(cudaMemcpyAsync(&ctx->slot[ctx->cur_slot].h_loss[1], ctx->d_sync + ctx->p2p_n + kSyncErr,
+                           sizeof(unsigned long long), cudaMemcpyDeviceToHost, ctx->st));
     TRY(sync_stream(ctx));
+    TRY(p2p_check(ctx, ctx->cur_slot));
     if (ctx->profiling) TRY(collect_slot_timing(ctx, ctx->cur_slot));
     return GBM_OK;
 }
@@ -1053,6 +1237,9 @@ int enqueue_grow(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, bool co
     }
     // the row lists are free: the next round's compaction may overwrite them
     TRY(record_ev(ctx, ctx->rows_free, ctx->st));
+    if (ctx->p2p)   // the exchange's error word travels with the round
+        CK(cudaMemcpyAsync(&ctx->slot[ctx->cur_slot].h_loss[1], ctx->d_sync + ctx->p2p_n + kSyncErr,
+                           sizeof(unsigned long long), cudaMemcpyDeviceToHost, ctx->st));
     return GBM_OK;
 }
 
@@ -1142,6 +1329,7 @@ void write_tree_dev(const TreeOut &T, int need, gbm_tree_out *out) {
 // A finished slot -> the caller's tree and loss, and the statistics.
 int harvest(gbm_ctx *ctx, int si, int nf, const gbm_params *P, gbm_tree_out *out, double *train_loss) {
     if (ctx->profiling) TRY(collect_slot_timing(ctx, si));
+    TRY(p2p_check(ctx, si));
     const TreeOut &T = *ctx->slot[si].h_tout;
     if (T.status != 0) return fail(ctx, GBM_ERR_STATE, "internal: the device replay reached an unexpanded node");
     ctx->alg_bytes += (double)T.alg_rows * (nf + 8);
@@ -1435,6 +1623,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
         if (ctx->cst) cudaStreamSynchronize(ctx->cst);
     }
     drop_graphs(ctx);   // graphs may hold collectives: release them first
+    p2p_teardown(ctx, false);
     gbmh2d::stager_destroy(ctx->stager);
     gbmbin::work_destroy(ctx->bw);
     for (auto &s : ctx->slot)
@@ -1481,9 +1670,11 @@ int gbm_ctx_init_comm(gbm_ctx *ctx, const void *uid, int32_t nranks, int32_t ran
     if (ctx->comm) {   // replaced: finish its work and drop the graphs that call it first
         TRY(sync_stream(ctx));
         drop_graphs(ctx);
+        TRY(p2p_teardown(ctx, true));
         gbm_comm_destroy(ctx->comm);
         ctx->comm = nullptr;
     }
+    ctx->p2p_tried_stride = 0;
     if (nranks == 1) return GBM_OK;
     TRY(gbm_comm_create(&ctx->comm, uid, nranks, rank, ctx->timeout_ms, ctx->err));
     // bins uploaded before the communicator chose their skipped bins from this
@@ -1688,6 +1879,7 @@ static int round_body(gbm_ctx *ctx, int si, const int32_t *feat_idx, int32_t nfe
     CK(cudaEventRecord(s.done, ctx->st));
     TRY(wait_slot(ctx, si));
     if (dev) return harvest(ctx, si, nfeat, P, out, train_loss);
+    TRY(p2p_check(ctx, si));
     if (ctx->profiling) TRY(collect_slot_timing(ctx, si));
     if (train_loss) *train_loss = -s.h_loss[0] / (double)ctx->n_global;
     write_tree(T, tree_need(P), out);
@@ -1796,6 +1988,45 @@ int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const
         ctx->comm_bytes += s.g_comm_bytes;
     }
     return GBM_OK;
+}
+
+// ---- failure detection self test ----------------------------------------------
+
+int gbm_test_peer_wait(int32_t device, int32_t timeout_ms) {
+    if (timeout_ms <= 0 || timeout_ms > 10000) return GBM_ERR_ARG;
+    if (cudaSetDevice(device) != cudaSuccess) return GBM_ERR_CUDA;
+    const int N = 2, nf = 1;
+    const int64_t words = slot_words_for(nf);
+    long long *pst = nullptr, *out = nullptr, **peers = nullptr;
+    unsigned long long *sync = nullptr;
+    int rc = GBM_OK;
+    if (cudaMalloc(&pst, sizeof(long long) * (size_t)(2 * words)) != cudaSuccess ||
+        cudaMalloc(&out, sizeof(long long) * (size_t)words) != cudaSuccess ||
+        cudaMalloc(&peers, sizeof(long long *) * N) != cudaSuccess ||
+        cudaMalloc(&sync, sizeof(unsigned long long) * (N + kSyncLocal)) != cudaSuccess)
+        rc = GBM_ERR_ALLOC;
+    if (rc == GBM_OK) {
+        // rank 0 of 2 has signalled one level; rank 1 never will
+        std::vector<unsigned long long> s0((size_t)(N + kSyncLocal), 0ull);
+        s0[(size_t)(N + kSyncSent)] = 1;
+        long long *pp[2] = {pst, pst};
+        unsigned long long err = 0;
+        if (cudaMemset(pst, 0, sizeof(long long) * (size_t)(2 * words)) != cudaSuccess ||
+            cudaMemcpy(sync, s0.data(), sizeof(unsigned long long) * s0.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(peers, pp, sizeof pp, cudaMemcpyHostToDevice) != cudaSuccess) {
+            rc = GBM_ERR_CUDA;
+        } else {
+            k_peer_sum<<<1, 256>>>(peers, words, sync, 0, N, nullptr, nf, out, pst, (long long)timeout_ms * 1000000ll);
+            if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+                cudaMemcpy(&err, sync + N + kSyncErr, sizeof err, cudaMemcpyDeviceToHost) != cudaSuccess)
+                rc = GBM_ERR_CUDA;
+            else
+                rc = err ? GBM_ERR_TIMEOUT : GBM_OK;
+        }
+    }
+    void *ptrs[] = {pst, out, peers, sync};
+    for (void *q : ptrs) if (q) cudaFree(q);
+    return rc;
 }
 
 // ---- predict ------------------------------------------------------------------

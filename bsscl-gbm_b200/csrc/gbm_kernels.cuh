@@ -324,8 +324,10 @@ k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ ro
        const int32_t *__restrict__ rows1, const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
        const int *__restrict__ ntask_p, const int32_t *__restrict__ blist, const int32_t *__restrict__ bwp,
        const int32_t *__restrict__ nb_p, const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
-       const longlong2 *__restrict__ q, long long *__restrict__ stage_hist) {
+       const longlong2 *__restrict__ q, long long *__restrict__ stage_hist,
+       const unsigned long long *__restrict__ par_word, int64_t par_stride) {
     griddep_wait();
+    if (par_word) stage_hist += (int64_t)(*par_word & 1ull) * par_stride;   // peer exchange: this level's buffer
     extern __shared__ unsigned acc[];   // [6][16][256]
     __shared__ long long s_tot[2][kHistThreads / 32];
     const int ntask = *ntask_p;
@@ -487,11 +489,12 @@ __device__ __forceinline__ DNode fresh_node(int depth, int parent) {
 __global__ void k_root_plan(const int32_t *__restrict__ n_local, const long long *__restrict__ n_global,
                             DNode *__restrict__ nodes, HistTask *__restrict__ ht,
                             int32_t *__restrict__ prefix, int *__restrict__ node_count,
-                            long long *__restrict__ stage_count) {
+                            long long *__restrict__ stage_count, const unsigned long long *__restrict__ par_word,
+                            int64_t par_stride) {
     griddep_wait();
     if (threadIdx.x || blockIdx.x) return;
     long long ns = *n_local;
-    if (stage_count) *stage_count = ns;
+    if (stage_count) stage_count[par_word ? (int64_t)(*par_word & 1ull) * par_stride : 0] = ns;
     DNode d = fresh_node(0, -1);
     d.begin = 0;
     d.end = ns;
@@ -743,62 +746,178 @@ __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ l
     if (threadIdx.x == 0) prefix[W] = carry;
 }
 
-// Several ranks, before the staging all-reduce: slot k holds this rank's
-// partial histogram of the child it built (the locally smaller one).  Make it
-// the LEFT child's partial -- parent - right when the right child was built,
-// from this rank's own partials of earlier levels (lpool) -- so that every
-// rank contributes the same child, store both children's partials in lpool
-// (children that will be parents only), and put this rank's left count in the
-// slot's count word.  Integer words throughout: exact.
+// ---------------------------------------------------------------------------
+// several ranks: the staging exchange
+//
+// Every histogram level ends with the sum over ranks of the staging slots.
+// With NCCL that is one all-reduce of the slots.  With the peer exchange
+// each rank keeps two local staging buffers (level parity, from the level
+// counter in its sync words) that all ranks map through CUDA IPC: a rank
+// converts its partials in place and signals every peer (k_stage_left); each
+// rank then waits for every peer's signal and pulls the level's slots from
+// all ranks over NVLink, summing them into its own d_stage (k_peer_sum).  A
+// level's buffer is written again two levels later, after the next level's
+// signals prove that every peer has finished reading it; k_peer_sum zeroes it
+// then.  Sync words of a rank (unsigned 64-bit): [0, N) signals received from
+// each rank (written by the peers), then kSyncSent (signals this rank sent),
+// kSyncCta (CTAs done, for the last-CTA signal), kSyncLevel (levels done),
+// kSyncErr (a wait ran out), kSyncPrevW (slots of the previous level).
+// ---------------------------------------------------------------------------
+constexpr int kSyncSent = 0, kSyncCta = 1, kSyncLevel = 2, kSyncErr = 3, kSyncPrevW = 4, kSyncLocal = 8;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Slot k holds this rank's partial histogram of the child it built (the
+// locally smaller one).  Make it the LEFT child's partial -- parent - right
+// when the right child was built, from this rank's own partials of earlier
+// levels (lpool) -- so that every rank contributes the same child; store both
+// children's partials in lpool (children that will be parents only) and this
+// rank's left count in the slot's count word.  lvl == null: the root, whose
+// partial is copied to lpool[0].  Integer words throughout: exact.  With the
+// peer exchange (sync != null) the slots are in this level's parity buffer,
+// and the last CTA to finish signals every peer.
 __global__ void k_stage_left(const DNode *__restrict__ nodes, const int *__restrict__ lvl,
                              const int *__restrict__ lvl_count, HistTask *__restrict__ ht,
-                             long long *__restrict__ stage, long long *__restrict__ lpool, int nf, int pool_depth) {
+                             long long *__restrict__ stage, int64_t par_stride, long long *__restrict__ lpool, int nf,
+                             int pool_depth, unsigned long long *__restrict__ sync,
+                             unsigned long long *const *__restrict__ peer_sync, int rank, int nranks) {
     griddep_wait();
+    if (sync) stage += (int64_t)(sync[nranks + kSyncLevel] & 1ull) * par_stride;
     const int k = blockIdx.y;
-    if (k >= *lvl_count) return;
     const int64_t words = slot_words_for(nf);
     const int64_t data = (int64_t)nf * kBins * kWords + 4;   // cells and totals
-    const int parent = lvl[k];
-    const DNode &p = nodes[parent];
-    const bool built_left = p.left_small != 0;
-    const bool keep = nodes[p.kid0].depth < pool_depth;
-    long long *st = stage + (int64_t)k * words;
-    const long long *par = lpool + (int64_t)parent * words;
-    long long *lk = lpool + (int64_t)p.kid0 * words, *rk = lpool + (int64_t)p.kid1 * words;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < data; i += (int64_t)gridDim.x * blockDim.x) {
-        const long long s = st[i], pv = par[i];
-        const long long left = built_left ? s : pv - s;
-        st[i] = left;
-        if (keep) {
-            lk[i] = left;
-            rk[i] = pv - left;
+    const bool active = lvl ? k < *lvl_count : k == 0;
+    if (active) {
+        long long *st = stage + (int64_t)k * words;
+        if (!lvl) {
+            for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < data;
+                 i += (int64_t)gridDim.x * blockDim.x)
+                lpool[i] = st[i];
+        } else {
+            const int parent = lvl[k];
+            const DNode &p = nodes[parent];
+            const bool built_left = p.left_small != 0;
+            const bool keep = nodes[p.kid0].depth < pool_depth;
+            const long long *par = lpool + (int64_t)parent * words;
+            long long *lk = lpool + (int64_t)p.kid0 * words, *rk = lpool + (int64_t)p.kid1 * words;
+            for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < data;
+                 i += (int64_t)gridDim.x * blockDim.x) {
+                const long long s = st[i], pv = par[i];
+                const long long left = built_left ? s : pv - s;
+                st[i] = left;
+                if (keep) {
+                    lk[i] = left;
+                    rk[i] = pv - left;
+                }
+            }
+            if (blockIdx.x == 0 && threadIdx.x == 0) {
+                st[(int64_t)nf * kBins * kWords + kCountWord] = p.nl;
+                ht[k].left_small = 1;   // the split search reads the slot as the left child
+            }
         }
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        st[(int64_t)nf * kBins * kWords + kCountWord] = p.nl;
-        ht[k].left_small = 1;   // the split search reads the slot as the left child
+    if (!sync) return;
+    // the last CTA to finish tells every peer that this rank's slots are final
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long *ctr = sync + nranks + kSyncCta;
+        const unsigned long long total = (unsigned long long)gridDim.x * gridDim.y;
+        if (atomicAdd(ctr, 1ull) == total - 1) {
+            *ctr = 0;
+            __threadfence_system();
+            const unsigned long long e = sync[nranks + kSyncSent] + 1;
+            sync[nranks + kSyncSent] = e;
+            // word `rank` of a peer's sync words has this rank as its only writer
+            for (int q = 0; q < nranks; q++)
+                if (q != rank) *reinterpret_cast<volatile unsigned long long *>(peer_sync[q] + rank) = e;
+            __threadfence_system();
+        }
     }
 }
 
-// Several ranks, after the staging all-reduce: the global counts from the
-// slots' count words.  lvl == null: the root (slot 0).
+// Peer exchange: wait (bounded) until every peer has signalled this level,
+// then out[i] = sum over ranks r of rank r's slot word i, read from each
+// rank's parity buffer (peers over NVLink), for the level's slots; zero this
+// rank's other parity buffer (the previous level's, read by every peer by
+// now).  A wait that runs out sets kSyncErr and the sums are not used.
+__global__ void __launch_bounds__(256) k_peer_sum(const long long *const *__restrict__ peers, int64_t par_stride,
+                                                  unsigned long long *__restrict__ sync, int rank, int nranks,
+                                                  const int *__restrict__ lvl_count, int nf, long long *__restrict__ out,
+                                                  long long *__restrict__ own, long long timeout_ns) {
+    griddep_wait();
+    __shared__ int s_ok;
+    const unsigned long long level = sync[nranks + kSyncLevel];
+    if (threadIdx.x == 0) {
+        const unsigned long long want = sync[nranks + kSyncSent];
+        const unsigned long long t0 = global_ns();
+        int ok = sync[nranks + kSyncErr] == 0;   // after one failed wait the rank's exchange is broken
+        for (int q = 0; q < nranks && ok; q++) {
+            if (q == rank) continue;
+            volatile unsigned long long *f = sync + q;
+            while (*f < want) {
+                if (global_ns() - t0 > (unsigned long long)timeout_ns) {
+                    ok = 0;
+                    atomicExch(sync + nranks + kSyncErr, 1ull);
+                    break;
+                }
+                __nanosleep(200);
+            }
+        }
+        __threadfence_system();
+        s_ok = ok;
+    }
+    __syncthreads();
+    const int64_t words = slot_words_for(nf);
+    const int W = lvl_count ? *lvl_count : 1;
+    const int64_t pr = (int64_t)(level & 1ull) * par_stride, po = (int64_t)((level & 1ull) ^ 1ull) * par_stride;
+    const int64_t n2 = (int64_t)W * words / 2;   // longlong2 per level (slot words are even)
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, dt = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = t0; i < n2; i += dt) {
+        long long x = 0, y = 0;
+        if (s_ok) {
+            for (int r = 0; r < nranks; r++) {
+                const longlong2 v = __ldcv(reinterpret_cast<const longlong2 *>(peers[r] + pr) + i);
+                x += v.x;
+                y += v.y;
+            }
+        }
+        reinterpret_cast<longlong2 *>(out)[i] = make_longlong2(x, y);   // zeros after a failed wait
+    }
+    const int64_t z2 = (int64_t)sync[nranks + kSyncPrevW] * words / 2;
+    for (int64_t i = t0; i < z2; i += dt) reinterpret_cast<longlong2 *>(own + po)[i] = make_longlong2(0, 0);
+}
+
+// Several ranks, after the staging sum: the global counts from the slots'
+// count words.  lvl == null: the root (slot 0).  With the peer exchange
+// (sync != null) the level is closed: its slot count is kept for the next
+// level's zeroing and the level counter advances.
 __global__ void k_fill_counts(DNode *__restrict__ nodes, const int *__restrict__ lvl,
-                              const int *__restrict__ lvl_count, const long long *__restrict__ stage, int nf) {
+                              const int *__restrict__ lvl_count, const long long *__restrict__ stage, int nf,
+                              unsigned long long *__restrict__ sync, int nranks) {
     griddep_wait();
     const int64_t words = slot_words_for(nf);
     const int64_t cw = (int64_t)nf * kBins * kWords + kCountWord;
+    const int W = lvl ? *lvl_count : 1;
     if (!lvl) {
-        if (threadIdx.x == 0 && blockIdx.x == 0) nodes[0].n = stage[cw];
-        return;
+        if (threadIdx.x == 0) nodes[0].n = stage[cw];
+    } else {
+        for (int k = threadIdx.x; k < W; k += blockDim.x) {
+            DNode &p = nodes[lvl[k]];
+            const long long gnl = stage[(int64_t)k * words + cw];
+            p.gnl = gnl;
+            p.left_small = 1;
+            nodes[p.kid0].n = gnl;
+            nodes[p.kid1].n = p.n - gnl;
+        }
     }
-    const int W = *lvl_count;
-    for (int k = threadIdx.x; k < W; k += blockDim.x) {
-        DNode &p = nodes[lvl[k]];
-        const long long gnl = stage[(int64_t)k * words + cw];
-        p.gnl = gnl;
-        p.left_small = 1;
-        nodes[p.kid0].n = gnl;
-        nodes[p.kid1].n = p.n - gnl;
+    if (sync && threadIdx.x == 0) {
+        sync[nranks + kSyncPrevW] = (unsigned long long)W;
+        sync[nranks + kSyncLevel] += 1;
     }
 }
 

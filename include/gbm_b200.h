@@ -210,6 +210,15 @@ int32_t gbm_scale_bits(const gbm_ctx *ctx);
 int gbm_get_F(gbm_ctx *ctx, double *F_out);
 int gbm_get_grad(gbm_ctx *ctx, double *g_out, double *h_out);
 
+/* Failure-detection self test; no reference counterpart.  With several
+ * ranks each histogram level waits, on the device and with a time limit, for
+ * every peer's signal (the peer exchange of the staging histograms); a wait
+ * that runs out is reported as GBM_ERR_TIMEOUT by the round.  This runs that
+ * wait on `device` for a signal no rank will send, limited to `timeout_ms`
+ * (1..10000), and returns GBM_ERR_TIMEOUT when the wait ran out and said so.
+ * One GPU; nothing is left waiting. */
+int gbm_test_peer_wait(int32_t device, int32_t timeout_ms);
+
 /* ---- predict ---------------------------------------------------------- */
 
 /* F[i] = base + sum_t lr * values[leaf_t(i)] and proba = sigmoid(clip(F))
