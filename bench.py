@@ -508,6 +508,7 @@ def run_engine(args):
                 "host_collective_calls": st["host_comm_ms"] / args.steps,
                 "collectives_device": st["comm_ms"] / args.steps,
                 "collective_mb": st["comm_bytes"] / args.steps / 1e6,
+                "peer_wait": st["peer_wait_ms"] / args.steps,
                 "l2_flush_excluded": st["flush_ms"] / args.steps,
                 "waves": st["waves"] / args.steps},
             "e2e": ({"value": e2e, "unit": "rounds/s", "h2d_bytes_per_step": int(h2d),

@@ -192,6 +192,7 @@ struct gbm_ctx {
     double hist_ms = 0.0, alg_bytes = 0.0, hist_updates = 0.0;
     double host_sample_ms = 0.0, host_sync_ms = 0.0, host_replay_ms = 0.0, host_comm_ms = 0.0;
     double comm_ms = 0.0, comm_bytes = 0.0;   // collectives: device time (profiling), bytes per rank
+    double peer_wait_base_ms = 0.0;           // the peer exchange's wait counter at the last stats reset
     // benchmark aid: an L2 eviction at the start of every round
     uint8_t *d_flush = nullptr;
     size_t flush_bytes = 0;
@@ -567,8 +568,10 @@ int p2p_teardown(gbm_ctx *ctx, bool collective) {
 int p2p_setup(gbm_ctx *ctx, int64_t stride) {
     TRY(p2p_teardown(ctx, true));
     const char *env = std::getenv("GBM_PEER_EXCHANGE");
-    if (env && env[0] == '0') return GBM_OK;
     const int N = gbm_comm_size(ctx->comm), rank = gbm_comm_rank(ctx->comm);
+    // default: on for 2 ranks (the configuration its parity tests run on);
+    // GBM_PEER_EXCHANGE=1 turns it on for any count, 0 off
+    if (env ? env[0] == '0' : N != 2) return GBM_OK;
     ctx->p2p_n = N;
     ctx->p2p_rank = rank;
     int ok = 1;
@@ -2174,6 +2177,12 @@ int gbm_get_stats(gbm_ctx *ctx, gbm_stats *out) {
     out->host_comm_ms = ctx->host_comm_ms;
     out->comm_ms = ctx->comm_ms;
     out->comm_bytes = ctx->comm_bytes;
+    out->peer_wait_ms = 0.0;
+    if (ctx->p2p && ctx->d_sync && cudaSetDevice(ctx->dev) == cudaSuccess) {
+        unsigned long long ns = 0;
+        if (cudaMemcpy(&ns, ctx->d_sync + ctx->p2p_n + kSyncWaitNs, sizeof ns, cudaMemcpyDeviceToHost) == cudaSuccess)
+            out->peer_wait_ms = (double)ns * 1e-6 - ctx->peer_wait_base_ms;
+    }
     return GBM_OK;
 }
 
@@ -2183,6 +2192,11 @@ int gbm_reset_stats(gbm_ctx *ctx) {
     ctx->hist_ms = ctx->alg_bytes = ctx->hist_updates = 0.0;
     ctx->host_sample_ms = ctx->host_sync_ms = ctx->host_replay_ms = ctx->flush_ms = ctx->host_comm_ms = 0.0;
     ctx->comm_ms = ctx->comm_bytes = 0.0;
+    if (ctx->p2p && ctx->d_sync && cudaSetDevice(ctx->dev) == cudaSuccess) {   // the counter only grows
+        unsigned long long ns = 0;
+        if (cudaMemcpy(&ns, ctx->d_sync + ctx->p2p_n + kSyncWaitNs, sizeof ns, cudaMemcpyDeviceToHost) == cudaSuccess)
+            ctx->peer_wait_base_ms = (double)ns * 1e-6;
+    }
     return GBM_OK;
 }
 

@@ -761,9 +761,11 @@ __global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ l
 // then.  Sync words of a rank (unsigned 64-bit): [0, N) signals received from
 // each rank (written by the peers), then kSyncSent (signals this rank sent),
 // kSyncCta (CTAs done, for the last-CTA signal), kSyncLevel (levels done),
-// kSyncErr (a wait ran out), kSyncPrevW (slots of the previous level).
+// kSyncErr (a wait ran out), kSyncPrevW (slots of the previous level),
+// kSyncWaitNs (time CTA 0 of k_peer_sum spent waiting for the peers).
 // ---------------------------------------------------------------------------
-constexpr int kSyncSent = 0, kSyncCta = 1, kSyncLevel = 2, kSyncErr = 3, kSyncPrevW = 4, kSyncLocal = 8;
+constexpr int kSyncSent = 0, kSyncCta = 1, kSyncLevel = 2, kSyncErr = 3, kSyncPrevW = 4, kSyncWaitNs = 5,
+              kSyncLocal = 8;
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -869,6 +871,7 @@ __global__ void __launch_bounds__(256) k_peer_sum(const long long *const *__rest
             }
         }
         __threadfence_system();
+        if (blockIdx.x == 0) sync[nranks + kSyncWaitNs] += global_ns() - t0;
         s_ok = ok;
     }
     __syncthreads();

@@ -298,7 +298,8 @@ typedef struct {
                                   atomic adds each */
     double host_comm_ms;       /* host time in the collective calls (enqueue) */
     double comm_ms;            /* device time of the collectives (profiling), waits for peers included */
-    double comm_bytes;         /* bytes this rank all-reduced */
+    double comm_bytes;         /* bytes this rank all-reduced or pulled from peers */
+    double peer_wait_ms;       /* peer exchange: time spent waiting for the peers' signals */
 } gbm_stats;
 
 int gbm_set_profiling(gbm_ctx *ctx, int32_t on);
