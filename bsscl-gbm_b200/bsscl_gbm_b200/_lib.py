@@ -32,7 +32,8 @@ EXPORTS = (
     "gbm_set_profiling", "gbm_get_stats", "gbm_reset_stats", "gbm_event_record",
     "gbm_event_elapsed", "gbm_predict_noalloc", "gbm_fit_rounds", "gbm_upload_bins_u16",
     "gbm_set_l2_flush", "gbm_bin_edges", "gbm_upload_binned_rows", "gbm_bin_features",
-    "gbm_predict_upload_raw", "gbm_predict_raw", "gbm_test_peer_wait",
+    "gbm_predict_upload_raw", "gbm_predict_raw", "gbm_test_peer_wait", "gbm_upload_labels_mc",
+    "gbm_round_mc", "gbm_get_F_mc", "gbm_get_grad_mc",
 )
 
 
@@ -137,6 +138,10 @@ def lib():
     L.gbm_predict_raw.argtypes = [P, P, i64, i32, i32, P, i32, P, P, C.POINTER(GbmPacked), f64,
                                   f64, P, P]
     L.gbm_test_peer_wait.argtypes = [i32, i32]
+    L.gbm_upload_labels_mc.argtypes = [P, P, i32, P, i64]
+    L.gbm_round_mc.argtypes = [P, P, P, i32, C.POINTER(GbmParams), C.POINTER(GbmTreeOut), C.POINTER(C.c_double)]
+    L.gbm_get_F_mc.argtypes = [P, P]
+    L.gbm_get_grad_mc.argtypes = [P, i32, P, P]
     L.gbm_predict_noalloc.argtypes = [P, i64, i32, P, P, P, P, P, P, i32, i32, f64, f64, P, P, P,
                                       C.c_char_p, i32]
     _lib = L
@@ -309,6 +314,46 @@ class Engine:
         self.check(self._L.gbm_round(self._h, ptr(mask), ptr(fidx), len(fidx), C.byref(params),
                                      C.byref(out), C.byref(loss)), "gbm_round")
         return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value), leaf
+
+    # -- multi-class softmax --
+    def upload_labels_mc(self, y, n_classes, class_w, n_global=0):
+        yy = np.ascontiguousarray(y, dtype=np.uint8)
+        w = np.ascontiguousarray(class_w, dtype=np.float64)
+        self.K = int(n_classes)
+        self.check(self._L.gbm_upload_labels_mc(self._h, ptr(yy), self.K, ptr(w), int(n_global)),
+                   "gbm_upload_labels_mc")
+
+    def round_mc(self, inbag_mask, feat_idx, params: GbmParams, capacity, want_leaf=False):
+        """gbm_round_mc: K trees (one per class) and the round's train loss."""
+        mask = np.ascontiguousarray(inbag_mask, dtype=np.uint8)
+        fidx = np.ascontiguousarray(feat_idx, dtype=np.int32)
+        K = self.K
+        arrs, leaves = [], []
+        outs = (GbmTreeOut * K)()
+        for k in range(K):
+            a = (np.empty(capacity, np.int32), np.empty(capacity, np.int64), np.empty(capacity, np.float64),
+                 np.empty(capacity, np.int32), np.empty(capacity, np.int32), np.empty(capacity, np.float64))
+            leaf = np.empty(self.n, np.int32) if want_leaf else None
+            arrs.append(a)
+            leaves.append(leaf)
+            outs[k] = GbmTreeOut(capacity, ptr(a[0]), ptr(a[1]), ptr(a[2]), ptr(a[3]), ptr(a[4]),
+                                 ptr(a[5]), 0, ptr(leaf))
+        loss = C.c_double(0.0)
+        self.check(self._L.gbm_round_mc(self._h, ptr(mask), ptr(fidx), len(fidx), C.byref(params), outs,
+                                        C.byref(loss)), "gbm_round_mc")
+        trees = [(a[0], a[1], a[2], a[3], a[4], int(outs[k].n_nodes), a[5]) for k, a in enumerate(arrs)]
+        return trees, float(loss.value), leaves
+
+    def get_F_mc(self):
+        F = np.empty((self.K, self.n), np.float64)
+        self.check(self._L.gbm_get_F_mc(self._h, ptr(F)), "gbm_get_F_mc")
+        return F
+
+    def get_grad_mc(self, k):
+        g = np.empty(self.n, np.float64)
+        h = np.empty(self.n, np.float64)
+        self.check(self._L.gbm_get_grad_mc(self._h, int(k), ptr(g), ptr(h)), "gbm_get_grad_mc")
+        return g, h
 
     def round_sampled(self, sampler, row_offset, params: GbmParams, capacity, want_leaf=False):
         """gbm_round with the subsample drawn by `sampler` (global row ids)."""

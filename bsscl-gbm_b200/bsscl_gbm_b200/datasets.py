@@ -158,3 +158,16 @@ def config5_ensemble(n_trees=1000, depth=8, p=200, seed=5, max_threshold=253):
         "values": val.reshape(-1), "left": left.reshape(-1),
         "right": right.reshape(-1), "offsets": offsets,
     }
+
+
+def multiclass(n=8_000, p=12, K=4, seed=7, nan_frac=0.05):
+    """A K-class stand-in for the reference's multi-class path (E:2949-3065):
+    Gaussian class clusters in p dimensions with unequal class sizes (class k
+    has weight proportional to 1 / (k + 1)), NaN in the last three columns."""
+    rng = np.random.default_rng(seed)
+    pri = 1.0 / np.arange(1, K + 1)
+    y = rng.choice(K, size=n, p=pri / pri.sum())
+    centres = rng.standard_normal((K, p)) * 1.2
+    X = centres[y] + rng.standard_normal((n, p))
+    X[:, -3:][rng.random((n, 3)) < nan_frac] = np.nan
+    return X, y.astype(np.int64)

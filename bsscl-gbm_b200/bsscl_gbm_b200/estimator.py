@@ -347,9 +347,9 @@ class HybridHistGBMNumbaV1_0_1:
             raise ValueError("X is empty")
         self.classes_ = np.unique(y)
         self.n_classes_ = len(self.classes_)
-        if self.n_classes_ > 2:
-            raise NotImplementedError("multi-class softmax is not on the B200 engine")
-        self._is_multiclass = False
+        if self.n_classes_ > 64:
+            raise NotImplementedError("the B200 engine holds at most 64 classes")
+        self._is_multiclass = self.n_classes_ > 2
         # class index of every label (classes_ is sorted and unique)
         y = np.searchsorted(self.classes_, y).astype(np.int64)
         if y_val is not None:
@@ -421,7 +421,10 @@ class HybridHistGBMNumbaV1_0_1:
                 X_val_bin = binning.bin_features(X_val, self.bin_edges, self.feature_bin_counts,
                                                  self._nan_bin_id)
         t0 = time.perf_counter()
-        self._fit_binary_device(X_bin, y, X_val_bin, y_val)
+        if self._is_multiclass:
+            self._fit_multiclass_device(X_bin, y, X_val_bin, y_val)
+        else:
+            self._fit_binary_device(X_bin, y, X_val_bin, y_val)
         self.times['training'] = (time.perf_counter() - t0) * 1000
         self._pack_trees()
         self._compute_feature_importances()
@@ -535,10 +538,95 @@ class HybridHistGBMNumbaV1_0_1:
         self.times['rounds'] = (time.perf_counter() - t_rounds) * 1000
         self.n_trees_fitted_ = len(self.trees)
 
+    def _class_weights_mc(self, y):
+        """Per-class weights of ``_compute_class_weights`` (E:2570-2603) for K classes."""
+        K = self.n_classes_
+        n = len(y)
+        w = np.ones(K, dtype=np.float64)
+        if self.class_weight in ('balanced', 'balanced_sqrt'):
+            for k in range(K):
+                w_k = n / (K * max(int(np.sum(y == k)), 1))
+                if self.class_weight == 'balanced_sqrt':
+                    w_k = w_k ** 0.35
+                w[k] = w_k
+        return w
+
+    def _fit_multiclass_device(self, X_bin, y, X_val_bin, y_val):
+        """The reference's ``_fit_multiclass`` loop (E:2949-3065): per round one
+        shared subsample and K trees, all on the GPU (gbm_round_mc)."""
+        n, p = X_bin.shape
+        K = self.n_classes_
+        w = self._class_weights_mc(y)
+        n_sub = max(1, int(n * self.subsample))
+        n_feat = max(1, int(p * self.colsample_bytree))
+        seed = self.random_state
+        if seed is None:
+            seed = int.from_bytes(os.urandom(4), "little")
+        if not (0 <= int(seed) <= 0xFFFFFFFF):
+            raise ValueError("Seed must be between 0 and 2**32 - 1")
+        sampler = Sampler(int(seed), n, p, n_sub, n_feat, self.subsample < 1.0,
+                          self.colsample_bytree < 1.0, look_ahead=3)
+        eng = self._get_engine()
+        lo, hi = _rank_rows(n)
+        _ensure_comm(eng)
+        self._check_device_bins()
+        t_up = time.perf_counter()
+        if not isinstance(X_bin, _BinsOnDevice):
+            Xr = X_bin[lo:hi]
+            if Xr.dtype not in (np.uint8, np.uint16):
+                Xr = binning.device_bins(Xr, self.feature_bin_counts)
+            eng.upload_bins(Xr, self.feature_bin_counts)
+        eng.upload_labels_mc(y[lo:hi].astype(np.uint8), K, w, n_global=n)
+        self.times['upload'] = (time.perf_counter() - t_up) * 1000
+        self.scale_bits_ = eng.scale_bits()
+        self.base_score_ = 0.0
+        params = self._params_struct()
+        cap = self._tree_capacity()
+        self.mc_trees = [[] for _ in range(K)]
+        F_val = np.zeros((len(y_val), K)) if y_val is not None else None
+        yv_onehot = np.eye(K, dtype=np.float64)[y_val] if y_val is not None else None
+        best_val, no_improve = np.inf, 0
+        t_rounds = time.perf_counter()
+        try:
+            for m in range(self.n_estimators):
+                _, mask, feat = sampler.next(want_sample=False, want_mask=True)
+                trees, loss, _ = eng.round_mc(mask[lo:hi], feat, params, cap)
+                for k in range(K):
+                    self.mc_trees[k].append(trees[k])
+                    if F_val is not None:
+                        F_val[:, k] += self.learning_rate * _predict_tree_host(X_val_bin, trees[k])
+                self.train_loss_history_.append(loss)
+                val_loss = None
+                if F_val is not None:
+                    val_loss = _mc_logloss(yv_onehot, F_val)
+                    self.val_loss_history_.append(val_loss)
+                if self.verbose and ((m + 1) % 20 == 0 or m == 0):
+                    msg = f"  Round {m + 1:>3}/{self.n_estimators}  |  {K} trees  |  train-loss: {loss:.6f}"
+                    if val_loss is not None:
+                        msg += f"  |  val-loss: {val_loss:.6f}"
+                    print(msg)
+                if self.early_stopping_rounds is not None and val_loss is not None:
+                    if val_loss < best_val:
+                        best_val, self.best_iteration_, no_improve = val_loss, m, 0
+                    else:
+                        no_improve += 1
+                        if no_improve >= self.early_stopping_rounds:
+                            for k in range(K):
+                                self.mc_trees[k] = self.mc_trees[k][:self.best_iteration_ + 1]
+                            break
+        finally:
+            sampler.close()
+        self.times['rounds'] = (time.perf_counter() - t_rounds) * 1000
+        self.trees = []
+        self.n_trees_fitted_ = sum(len(t) for t in self.mc_trees)
+
     # ------------------------------------------------------------------
     # packing, importances (E:2192-2236, E:2343-2363)
     # ------------------------------------------------------------------
     def _pack_trees(self):
+        if self._is_multiclass:
+            self._mc_packed = [_pack_list(ts) for ts in self.mc_trees]
+            return
         total = sum(t[5] for t in self.trees)
         feats = np.empty(total, dtype=np.int16)
         thr = np.empty(total, dtype=np.int64)
@@ -563,7 +651,8 @@ class HybridHistGBMNumbaV1_0_1:
     def _compute_feature_importances(self):
         gain = np.zeros(self.n_features_in_, dtype=np.float64)
         cnt = np.zeros(self.n_features_in_, dtype=np.int64)
-        for tf, tt, tv, tl, tr, nc, sg in self.trees:
+        all_trees = [t for ts in self.mc_trees for t in ts] if self._is_multiclass else self.trees
+        for tf, tt, tv, tl, tr, nc, sg in all_trees:
             for k in range(nc):
                 f = tf[k]
                 if f >= 0:
@@ -599,6 +688,16 @@ class HybridHistGBMNumbaV1_0_1:
         # rows are binned on the GPU (gbm_predict_raw) and go straight to the ensemble
         t0 = time.perf_counter()
         eng = self._get_engine()
+        if self._is_multiclass:
+            # K ensembles over the same binned rows, then the softmax (E:3290-3310, E:2328-2332)
+            eng.predict_upload_raw(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id)
+            F = np.zeros((X.shape[0], self.n_classes_))
+            for k in range(self.n_classes_):
+                eng.predict_set_model(self._mc_packed[k], len(self.mc_trees[k]), X.shape[1])
+                eng.predict_run(self.learning_rate, 0.0)
+                F[:, k] = eng.predict_fetch(want_F=True, want_proba=False)[0]
+            self.times['inference'] = (time.perf_counter() - t0) * 1000
+            return _softmax(F)
         _, proba = eng.predict_raw(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id,
                                    self._packed(), len(self.trees), self.learning_rate,
                                    getattr(self, 'base_score_', 0.0), want_F=False, want_proba=True)
@@ -617,6 +716,8 @@ class HybridHistGBMNumbaV1_0_1:
 
     def predict(self, X):
         proba = self.predict_proba(X)
+        if self._is_multiclass:
+            return self.classes_[np.argmax(proba, axis=1)]
         return self.classes_[(proba[:, 1] > 0.5).astype(int)]
 
     # ------------------------------------------------------------------
@@ -657,12 +758,15 @@ class HybridHistGBMNumbaV1_0_1:
             data['bin_edges'] = np.asarray(self.bin_edges).tolist()
         if self.feature_bin_counts is not None:
             data['feature_bin_counts'] = np.asarray(self.feature_bin_counts).tolist()
-        data['trees'] = [{
-            'features': np.asarray(t[0]).tolist(), 'thresholds': np.asarray(t[1]).tolist(),
-            'values': np.asarray(t[2]).tolist(), 'left': np.asarray(t[3]).tolist(),
-            'right': np.asarray(t[4]).tolist(), 'node_count': int(t[5]),
-            'split_gains': np.asarray(t[6]).tolist() if len(t) > 6 else [],
-        } for t in self.trees]
+        def tree_json(t):
+            return {'features': np.asarray(t[0]).tolist(), 'thresholds': np.asarray(t[1]).tolist(),
+                    'values': np.asarray(t[2]).tolist(), 'left': np.asarray(t[3]).tolist(),
+                    'right': np.asarray(t[4]).tolist(), 'node_count': int(t[5]),
+                    'split_gains': np.asarray(t[6]).tolist() if len(t) > 6 else []}
+        if self._is_multiclass:
+            data['mc_trees'] = [[tree_json(t) for t in ts] for ts in self.mc_trees]
+        else:
+            data['trees'] = [tree_json(t) for t in self.trees]
         if self.feature_importances_ is not None:
             data['feature_importances_'] = np.asarray(self.feature_importances_).tolist()
         if self.feature_split_counts_ is not None:
@@ -691,8 +795,6 @@ class HybridHistGBMNumbaV1_0_1:
         model.n_features_in_ = data['n_features_in_']
         model.objective = data['objective']
         model._is_multiclass = data['_is_multiclass']
-        if model._is_multiclass or 'mc_trees' in data:
-            raise NotImplementedError("multi-class softmax is not on the B200 engine")
         model.init_score_ = data['init_score_']
         model.base_score_ = data.get('base_score_', 0.0)
         model.n_trees_fitted_ = data['n_trees_fitted_']
@@ -704,15 +806,14 @@ class HybridHistGBMNumbaV1_0_1:
             model.bin_edges = np.array(data['bin_edges'], dtype=np.float64)
         if 'feature_bin_counts' in data:
             model.feature_bin_counts = np.array(data['feature_bin_counts'], dtype=np.int32)
-        model.trees = []
-        for td in data.get('trees', []):
+        def tree_of(td):
             sg = np.array(td.get('split_gains', [0.0] * td['node_count']), dtype=np.float64)
-            model.trees.append((np.array(td['features'], dtype=np.int32),
-                                np.array(td['thresholds'], dtype=np.int64),
-                                np.array(td['values'], dtype=np.float64),
-                                np.array(td['left'], dtype=np.int32),
-                                np.array(td['right'], dtype=np.int32),
-                                int(td['node_count']), sg))
+            return (np.array(td['features'], dtype=np.int32), np.array(td['thresholds'], dtype=np.int64),
+                    np.array(td['values'], dtype=np.float64), np.array(td['left'], dtype=np.int32),
+                    np.array(td['right'], dtype=np.int32), int(td['node_count']), sg)
+        model.trees = [tree_of(td) for td in data.get('trees', [])]
+        if 'mc_trees' in data:
+            model.mc_trees = [[tree_of(td) for td in ts] for ts in data['mc_trees']]
         if 'feature_importances_' in data:
             model.feature_importances_ = np.array(data['feature_importances_'])
         if 'feature_split_counts_' in data:
@@ -734,6 +835,38 @@ class HybridHistGBMNumbaV1_0_1:
     def production_info(self):
         return {"engine": "libgbm_b200 (sm_100a)", "device": self.device,
                 "n_trees": self.n_trees_fitted_, "n_features": self.n_features_in_}
+
+
+def _softmax(F):
+    """``_softmax`` (E:2328-2332)."""
+    Fs = F - F.max(axis=1, keepdims=True)
+    e = np.exp(Fs)
+    return e / e.sum(axis=1, keepdims=True)
+
+
+def _mc_logloss(y_onehot, F):
+    """``_compute_multiclass_logloss`` (E:2335-2341)."""
+    proba = np.clip(_softmax(F), 1e-15, 1 - 1e-15)
+    return -np.mean(np.sum(y_onehot * np.log(proba), axis=1))
+
+
+def _pack_list(trees):
+    """``_pack_tree_list`` (E:2192-2216): one packed ensemble."""
+    total = sum(t[5] for t in trees)
+    out = {"features": np.empty(total, np.int16), "thresholds": np.empty(total, np.int64),
+           "values": np.empty(total, np.float64), "left": np.empty(total, np.int32),
+           "right": np.empty(total, np.int32), "offsets": np.empty(len(trees) + 1, np.int32)}
+    o = 0
+    for t, (tf, tt, tv, tl, tr, nc, _) in enumerate(trees):
+        out["offsets"][t] = o
+        out["features"][o:o + nc] = tf[:nc]
+        out["thresholds"][o:o + nc] = tt[:nc]
+        out["values"][o:o + nc] = tv[:nc]
+        out["left"][o:o + nc] = tl[:nc]
+        out["right"][o:o + nc] = tr[:nc]
+        o += nc
+    out["offsets"][len(trees)] = o
+    return out
 
 
 class _BinsOnDevice:

@@ -167,6 +167,12 @@ struct gbm_ctx {
     int32_t *d_mono = nullptr, *h_mono = nullptr;
     int replay_smem = 0;               // dynamic shared memory the replay kernels may use
 
+    // multi-class softmax: K classes, F and q class-major ([k][n])
+    int K = 0;
+    bool have_labels_mc = false;
+    double *d_Fmc = nullptr, *d_wmc = nullptr;
+    longlong2 *d_qmc = nullptr;
+
     // predict
     uint8_t *d_px = nullptr;
     int64_t pn = 0, pn_cap = 0;
@@ -1640,7 +1646,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
                         ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,
                         ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi, ctx->d_side,
-                        ctx->d_upstage};
+                        ctx->d_upstage, ctx->d_Fmc, ctx->d_wmc, ctx->d_qmc};
     for (int32_t *q : ctx->d_perm) if (q) cudaFree(q);
     for (void *p : dev_ptrs) if (p) cudaFree(p);
     void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_mono};
@@ -1886,6 +1892,146 @@ static int round_body(gbm_ctx *ctx, int si, const int32_t *feat_idx, int32_t nfe
     if (ctx->profiling) TRY(collect_slot_timing(ctx, si));
     if (train_loss) *train_loss = -s.h_loss[0] / (double)ctx->n_global;
     write_tree(T, tree_need(P), out);
+    return GBM_OK;
+}
+
+// ---- multi-class softmax (E:2949-3065) ---------------------------------------
+
+int gbm_upload_labels_mc(gbm_ctx *ctx, const uint8_t *y, int32_t n_classes, const double *class_w,
+                         int64_t n_global) {
+    if (!ctx || !y || !class_w || n_classes < 3 || n_classes > kMaxClasses) return GBM_ERR_ARG;
+    if (!ctx->have_bins) return fail(ctx, GBM_ERR_STATE, "upload bins before labels");
+    double wmax = 0.0;
+    for (int k = 0; k < n_classes; k++) {
+        if (!(class_w[k] > 0.0) || !std::isfinite(class_w[k]))
+            return fail(ctx, GBM_ERR_ARG, "class weights must be finite and > 0");
+        wmax = std::max(wmax, class_w[k]);
+    }
+    for (int64_t i = 0; i < ctx->n; i++)
+        if (y[i] >= n_classes) return fail(ctx, GBM_ERR_ARG, "label %d of row %lld >= %d classes", (int)y[i], (long long)i,
+                                           n_classes);
+    CK(cudaSetDevice(ctx->dev));
+    ctx->K = n_classes;
+    ctx->n_global = n_global > 0 ? n_global : ctx->n;
+    // |g| <= w and h <= w/4 for every class, as in the binary case
+    ctx->S = scale_bits_for(wmax);
+    TRY(dalloc(ctx, &ctx->d_Fmc, (size_t)ctx->n * n_classes));
+    TRY(dalloc(ctx, &ctx->d_qmc, (size_t)ctx->n * n_classes));
+    TRY(dalloc(ctx, &ctx->d_wmc, (size_t)n_classes));
+    CK(cudaMemsetAsync(ctx->d_Fmc, 0, sizeof(double) * (size_t)ctx->n * n_classes, ctx->st));   // F starts at 0 (E:2959)
+    CK(cudaMemcpyAsync(ctx->d_wmc, class_w, sizeof(double) * n_classes, cudaMemcpyHostToDevice, ctx->st));
+    CK(cudaMemcpyAsync(ctx->d_y, y, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    k_softmax_grad<<<ctx->upd_blocks, kUpdThreads, 0, ctx->st>>>(ctx->d_Fmc, ctx->d_y, ctx->n, n_classes, ctx->d_wmc,
+                                                                 std::ldexp(1.0, ctx->S), ctx->d_qmc, ctx->d_loss_part);
+    CKL();
+    TRY(sync_stream(ctx));
+    ctx->have_labels = false;   // the binary state no longer follows
+    ctx->have_labels_mc = true;
+    return GBM_OK;
+}
+
+int gbm_round_mc(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
+                 const gbm_params *P, gbm_tree_out *outs, double *train_loss) {
+    if (!ctx || !inbag_mask || !feat_idx || !P || !outs) return GBM_ERR_ARG;
+    if (!ctx->have_labels_mc) return fail(ctx, GBM_ERR_STATE, "upload bins and gbm_upload_labels_mc first");
+    const int K = ctx->K;
+    for (int k = 0; k < K; k++) TRY(check_tree_args(ctx, nfeat, P, &outs[k]));
+    CK(cudaSetDevice(ctx->dev));
+    TRY(prepare_round(ctx, nfeat, P));
+    std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
+    CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    longlong2 *const q_bin = ctx->d_q;
+    int rc = GBM_OK;
+    // K trees on the same sample and features, each from its class's
+    // gradients of the round's start (E:2995-3006)
+    for (int k = 0; k < K && rc == GBM_OK; k++) {
+        ctx->d_q = ctx->d_qmc + (int64_t)k * ctx->n;
+        gbm_ctx::Slot &s = ctx->slot[0];
+        begin_round(ctx, 0);
+        RoundFeat rf;
+        rc = setup_features(ctx, 0, feat_idx, nfeat, rf);
+        if (rc == GBM_OK) rc = enqueue_features(ctx, 0, nfeat);
+        if (rc == GBM_OK) rc = enqueue_grow(ctx, rf, P, false);   // the row list from the mask, per tree
+        if (rc != GBM_OK) break;
+        if (device_replay(ctx, P)) {
+            rc = enqueue_replay(ctx, P);
+            if (rc == GBM_OK && cudaMemcpyAsync(s.h_tout, ctx->d_tout, sizeof(TreeOut), cudaMemcpyDeviceToHost,
+                                                ctx->st) != cudaSuccess)
+                rc = fail(ctx, GBM_ERR_CUDA, "tree copy");
+            if (rc == GBM_OK && cudaEventRecord(s.done, ctx->st) != cudaSuccess) rc = fail(ctx, GBM_ERR_CUDA, "event");
+            if (rc == GBM_OK) rc = wait_slot(ctx, 0);
+            if (rc == GBM_OK) rc = harvest(ctx, 0, nfeat, P, &outs[k], nullptr);
+        } else {
+            HostTree T;
+            rc = replay_on_host(ctx, rf, P, T);
+            if (rc == GBM_OK && T.nc > 256) rc = fail(ctx, GBM_ERR_UNSUPPORTED, "tree with %d nodes exceeds 256", T.nc);
+            if (rc == GBM_OK) {
+                TreeDev td;
+                std::memset(&td, 0, sizeof td);
+                td.n = T.nc;
+                for (int j = 0; j < T.nc; j++) {
+                    td.feat[j] = T.tf[j];
+                    td.thr[j] = (int)std::min<int64_t>(T.tt[j], 255);
+                    td.left[j] = T.tl[j];
+                    td.right[j] = T.tr[j];
+                    td.val[j] = T.tv[j];
+                }
+                if (cudaMemcpyAsync(ctx->d_tree, &td, sizeof td, cudaMemcpyHostToDevice, ctx->st) != cudaSuccess ||
+                    cudaStreamSynchronize(ctx->st) != cudaSuccess)
+                    rc = fail(ctx, GBM_ERR_CUDA, "tree upload");
+                write_tree(T, tree_need(P), &outs[k]);
+            }
+        }
+        if (rc == GBM_OK)
+            rc = launch(ctx, k_update_class, dim3(ctx->upd_blocks), dim3(kUpdThreads), 0, ctx->st,
+                        (const TreeDev *)ctx->d_tree, (const uint8_t *)ctx->d_xb, ctx->n, P->learning_rate,
+                        ctx->d_Fmc + (int64_t)k * ctx->n,
+                        outs[k].leaf_of_row ? ctx->d_leaf : (int32_t *)nullptr);
+        if (rc == GBM_OK && outs[k].leaf_of_row &&
+            (cudaMemcpyAsync(outs[k].leaf_of_row, ctx->d_leaf, sizeof(int32_t) * ctx->n, cudaMemcpyDeviceToHost,
+                             ctx->st) != cudaSuccess || cudaStreamSynchronize(ctx->st) != cudaSuccess))
+            rc = fail(ctx, GBM_ERR_CUDA, "leaf copy");
+    }
+    ctx->d_q = q_bin;
+    TRY(rc);
+    // the next round's gradients of every class and this round's loss (E:3008)
+    TRY(launch(ctx, k_softmax_grad, dim3(ctx->upd_blocks), dim3(kUpdThreads), 0, ctx->st, (const double *)ctx->d_Fmc,
+               (const uint8_t *)ctx->d_y, ctx->n, K, (const double *)ctx->d_wmc, std::ldexp(1.0, ctx->S), ctx->d_qmc,
+               ctx->d_loss_part));
+    TRY(launch(ctx, k_sum_partials, dim3(1), dim3(256), 0, ctx->st, ctx->d_loss_part, ctx->upd_blocks, ctx->d_loss));
+    if (ctx->comm) TRY(allreduce_f64(ctx, ctx->d_loss, 1));
+    double loss = 0.0;
+    CK(cudaMemcpyAsync(ctx->slot[0].h_loss, ctx->d_loss, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
+    TRY(sync_stream(ctx));
+    loss = ctx->slot[0].h_loss[0];
+    if (train_loss) *train_loss = -loss / (double)ctx->n_global;
+    return GBM_OK;
+}
+
+int gbm_get_F_mc(gbm_ctx *ctx, double *F_out) {
+    if (!ctx || !F_out) return GBM_ERR_ARG;
+    if (!ctx->have_labels_mc) return GBM_ERR_STATE;
+    CK(cudaSetDevice(ctx->dev));
+    CK(cudaMemcpyAsync(F_out, ctx->d_Fmc, sizeof(double) * (size_t)ctx->n * ctx->K, cudaMemcpyDeviceToHost, ctx->st));
+    return sync_stream(ctx);
+}
+
+int gbm_get_grad_mc(gbm_ctx *ctx, int32_t k, double *g_out, double *h_out) {
+    if (!ctx || !g_out || !h_out) return GBM_ERR_ARG;
+    if (!ctx->have_labels_mc || k < 0 || k >= ctx->K) return GBM_ERR_STATE;
+    CK(cudaSetDevice(ctx->dev));
+    double *dg = nullptr, *dh = nullptr;
+    TRY(dalloc(ctx, &dg, (size_t)ctx->n));
+    int rc = dalloc(ctx, &dh, (size_t)ctx->n);
+    if (rc != GBM_OK) { cudaFree(dg); return rc; }
+    k_export_q<<<grid_for(ctx->n, 256), 256, 0, ctx->st>>>(ctx->d_qmc + (int64_t)k * ctx->n, ctx->n,
+                                                           std::ldexp(1.0, -ctx->S), dg, dh);
+    cudaMemcpyAsync(g_out, dg, sizeof(double) * ctx->n, cudaMemcpyDeviceToHost, ctx->st);
+    cudaMemcpyAsync(h_out, dh, sizeof(double) * ctx->n, cudaMemcpyDeviceToHost, ctx->st);
+    cudaError_t e = cudaStreamSynchronize(ctx->st);
+    cudaFree(dg);
+    cudaFree(dh);
+    if (e != cudaSuccess) return fail(ctx, GBM_ERR_CUDA, "gbm_get_grad_mc: %s", cudaGetErrorString(e));
     return GBM_OK;
 }
 

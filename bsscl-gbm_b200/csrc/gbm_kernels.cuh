@@ -144,6 +144,113 @@ k_update(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64
     }
 }
 
+// ---------------------------------------------------------------------------
+// multi-class softmax (E:2949-3065): K trees per round on one shared sample
+// ---------------------------------------------------------------------------
+
+// NumPy's sum of a short contiguous row (pairwise_sum for n <= 128: a plain
+// loop from 0 below 8 terms, else 8 running sums combined pairwise, then the
+// remainder) -- the order of exp_F.sum(axis=1) in _softmax (E:2331).
+__device__ __forceinline__ double np_row_sum(const double *a, int n) {
+    if (n < 8) {
+        double r = 0.0;
+        for (int i = 0; i < n; i++) r = __dadd_rn(r, a[i]);
+        return r;
+    }
+    double r[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) r[j] = a[j];
+    int i = 8;
+    for (; i < n - (n % 8); i += 8)
+#pragma unroll
+        for (int j = 0; j < 8; j++) r[j] = __dadd_rn(r[j], a[i + j]);
+    double res = __dadd_rn(__dadd_rn(__dadd_rn(r[0], r[1]), __dadd_rn(r[2], r[3])),
+                           __dadd_rn(__dadd_rn(r[4], r[5]), __dadd_rn(r[6], r[7])));
+    for (; i < n; i++) res = __dadd_rn(res, a[i]);
+    return res;
+}
+
+constexpr int kMaxClasses = 64;
+
+// Per row: p = softmax(F[:, i]) (E:2328-2332), then for every class k
+// g = w_y (p_k - [y == k]), h = max(w_y p_k (1 - p_k), 1e-8) (E:2991-2992,
+// E:2997), quantised to the 2^-S grid; and the row's logloss term
+// log(clip(p_y, 1e-15, 1 - 1e-15)) (E:2335-2341).  F and q are class-major
+// ([k][n]).
+__global__ void __launch_bounds__(kUpdThreads)
+k_softmax_grad(const double *__restrict__ F, const uint8_t *__restrict__ y, int64_t n, int K,
+               const double *__restrict__ w, double scale, longlong2 *__restrict__ q,
+               double *__restrict__ loss_part) {
+    griddep_wait();
+    __shared__ double s_red[kUpdThreads / 32];
+    double acc = 0.0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        double e[kMaxClasses];
+        double m = F[i];
+        for (int k = 1; k < K; k++) m = fmax(m, F[(int64_t)k * n + i]);
+        for (int k = 0; k < K; k++) e[k] = exp(__dsub_rn(F[(int64_t)k * n + i], m));
+        const double s = np_row_sum(e, K);
+        const int yi = y[i];
+        const double wi = w[yi];
+        for (int k = 0; k < K; k++) {
+            const double pk = __ddiv_rn(e[k], s);
+            const double g = __dmul_rn(wi, __dsub_rn(pk, k == yi ? 1.0 : 0.0));
+            const double h = fmax(__dmul_rn(__dmul_rn(wi, pk), __dsub_rn(1.0, pk)), 1e-8);
+            q[(int64_t)k * n + i] = make_longlong2(__double2ll_rn(__dmul_rn(g, scale)), __double2ll_rn(__dmul_rn(h, scale)));
+            if (k == yi) acc += log(fmin(fmax(pk, 1e-15), 1.0 - 1e-15));
+        }
+    }
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int w2 = 0; w2 < kUpdThreads / 32; w2++) s += s_red[w2];
+        loss_part[blockIdx.x] = s;
+    }
+}
+
+// F_k += lr * value(leaf) for one class's tree (E:3001-3002); the gradients
+// of the next round come from k_softmax_grad once all K trees are in.
+__global__ void __launch_bounds__(kUpdThreads)
+k_update_class(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64_t n, double lr,
+               double *__restrict__ F, int32_t *__restrict__ leaf_out) {
+    griddep_wait();
+    __shared__ int s_feat[256], s_thr[256], s_left[256], s_right[256];
+    __shared__ double s_val[256];
+    const int nn = tree->n;
+    if (nn <= 0) return;
+    for (int k = threadIdx.x; k < nn; k += blockDim.x) {
+        s_feat[k] = tree->feat[k];
+        s_thr[k] = tree->thr[k];
+        s_left[k] = tree->left[k];
+        s_right[k] = tree->right[k];
+        s_val[k] = tree->val[k];
+    }
+    __syncthreads();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int node = 0;
+        while (s_feat[node] >= 0) {
+            const int b = bin_of(xb, n, i, s_feat[node]);
+            node = (b <= s_thr[node]) ? s_left[node] : s_right[node];
+        }
+        if (leaf_out) leaf_out[i] = node;
+        F[i] = __dadd_rn(F[i], __dmul_rn(lr, s_val[node]));
+    }
+}
+
+// The quantised (g, h) of n rows as float64 (exact: |q| < 2^53).
+__global__ void k_export_q(const longlong2 *__restrict__ q, int64_t n, double inv_scale, double *__restrict__ g,
+                           double *__restrict__ h) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const longlong2 v = q[i];
+    g[i] = __dmul_rn((double)v.x, inv_scale);
+    h[i] = __dmul_rn((double)v.y, inv_scale);
+}
+
 // Fixed-order sum of the per-block loss partials (deterministic).
 __global__ void k_sum_partials(const double *__restrict__ part, int m, double *__restrict__ out) {
     griddep_wait();

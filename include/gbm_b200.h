@@ -166,6 +166,27 @@ int gbm_bin_features(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t 
 int gbm_upload_labels(gbm_ctx *ctx, const uint8_t *y, const double class_w[2],
                       double base_score, int64_t n_global);
 
+/* ---- multi-class softmax (E:2949-3065) --------------------------------- */
+
+/* Labels 0..n_classes-1 (3 <= n_classes <= 64) of this rank's rows and the
+ * per-class weights of _compute_class_weights (E:2570-2603).  F starts at 0
+ * for every class (E:2959); the first round's gradients are computed here. */
+int gbm_upload_labels_mc(gbm_ctx *ctx, const uint8_t *y, int32_t n_classes, const double *class_w,
+                         int64_t n_global);
+
+/* One multi-class round: K = n_classes trees on the same in-bag rows and
+ * features, tree k from the softmax gradients of class k at the round's
+ * start (E:2989-3006; hessians floored at 1e-8), F of class k updated after
+ * its tree, then the next round's gradients and the multi-class logloss
+ * (E:3008, E:2335-2341).  `outs` [n_classes]. */
+int gbm_round_mc(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
+                 const gbm_params *params, gbm_tree_out *outs, double *train_loss);
+
+/* F [n_classes][n] (class-major), and class k's current (g, h) as the engine
+ * holds them (each rounded to the 2^-S grid). */
+int gbm_get_F_mc(gbm_ctx *ctx, double *F_out);
+int gbm_get_grad_mc(gbm_ctx *ctx, int32_t k, double *g_out, double *h_out);
+
 /* One boosting round.  `inbag_mask` [n] marks this rank's in-bag rows
  * (the subsample); `feat_idx` [nfeat] the sorted column subsample.  Writes
  * the pruned tree to `out`, updates F on the device and returns the train

@@ -242,6 +242,95 @@ def fit_binary(X_bin, y01, counts, *, n_estimators, learning_rate, max_leaves, m
     return dict(trees=trees, base_score=base, F=F, train_loss=np.array(losses), w2=w2)
 
 
+def softmax(F):
+    """``_softmax`` (E:2328-2332), NumPy's own arithmetic."""
+    Fs = F - F.max(axis=1, keepdims=True)
+    e = np.exp(Fs)
+    return e / e.sum(axis=1, keepdims=True)
+
+
+def mc_logloss(y_onehot, F):
+    """``_compute_multiclass_logloss`` (E:2335-2341)."""
+    proba = np.clip(softmax(F), 1e-15, 1 - 1e-15)
+    return -np.mean(np.sum(y_onehot * np.log(proba), axis=1))
+
+
+def class_weights_mc(y, K, class_weight):
+    """Per-class weights ``w[K]`` of ``_compute_class_weights`` (E:2570-2603)
+    for a K-class fit: ``n / (K max(n_k, 1))``, to the power 0.35 for
+    'balanced_sqrt', ones otherwise."""
+    y = np.asarray(y)
+    n = len(y)
+    w = np.ones(K, dtype=np.float64)
+    if class_weight in ("balanced", "balanced_sqrt"):
+        for k in range(K):
+            n_k = np.sum(y == k)
+            w_k = n / (K * max(n_k, 1))
+            if class_weight == "balanced_sqrt":
+                w_k = w_k ** 0.35
+            w[k] = w_k
+    return w
+
+
+def fit_multiclass(X_bin, y, counts, K, *, n_estimators, learning_rate, max_leaves, max_depth,
+                   min_samples_leaf, min_child_weight, reg_lambda, gamma, subsample, colsample,
+                   class_weight, random_state, mode=MODE_REF, scale_bits=None, grow_policy="leaf",
+                   record=None):
+    """The reference's ``_fit_multiclass`` loop (E:2949-3065) on the oracle
+    builders: per round one shared subsample, the softmax gradients of every
+    class from the round's start, K trees, F of class k updated after its
+    tree.  ``record`` gets per round (g [K][n], h [K][n], sample, feat)."""
+    y = np.asarray(y).astype(np.int64)
+    n, p = X_bin.shape
+    y_onehot = np.eye(K, dtype=np.float64)[y]
+    F = np.zeros((n, K), dtype=np.float64)
+    w = class_weights_mc(y, K, class_weight)
+    sw = w[y]
+    n_sub = max(1, int(n * subsample))
+    n_feat = max(1, int(p * colsample))
+    rng = np.random.RandomState(random_state)
+    all_r = np.arange(n, dtype=np.int64)
+    all_f = np.arange(p, dtype=np.int32)
+    trees = [[] for _ in range(K)]
+    losses = []
+    for m in range(n_estimators):
+        proba = softmax(F)
+        if subsample < 1.0:
+            rng.shuffle(all_r)
+            sidx = all_r[:n_sub].copy()
+        else:
+            sidx = all_r.copy()
+        if colsample < 1.0:
+            rng.shuffle(all_f)
+            fidx = np.sort(all_f[:n_feat]).copy()
+        else:
+            fidx = all_f.copy()
+        grad_all = sw[:, None] * (proba - y_onehot)
+        hess_all = sw[:, None] * proba * (1.0 - proba)
+        S = scale_bits
+        if mode == MODE_EXACT and S is None:
+            S = engine_scale_bits(len(sidx), w)
+        gs, hs = [], []
+        for k in range(K):
+            g = np.ascontiguousarray(grad_all[:, k])
+            h = np.maximum(np.ascontiguousarray(hess_all[:, k]), 1e-8)
+            t = build_tree(X_bin, g, h, sidx, fidx, counts, max_leaves=max_leaves,
+                           max_depth=max_depth, msl=min_samples_leaf, mcw=min_child_weight,
+                           lam=reg_lambda, gamma=gamma, mode=mode, scale_bits=S or 0,
+                           policy=grow_policy)
+            tf, tt, tv, tl, tr, nc, sg = t
+            post_prune(tf, tl, tr, sg, gamma, nc)
+            leaf = leaf_ids(X_bin, tf, tt, tl, tr)
+            F[:, k] += learning_rate * tv[leaf]
+            trees[k].append((tf, tt, tv, tl, tr, nc, sg))
+            gs.append(g)
+            hs.append(h)
+        if record is not None:
+            record.append(dict(g=np.array(gs), h=np.array(hs), sample=sidx, feat=fidx))
+        losses.append(mc_logloss(y_onehot, F))
+    return dict(trees=trees, F=F, train_loss=np.array(losses), w=w)
+
+
 def engine_scale_bits(n_rows, w2, word_bits=126):
     """Fixed-point exponent S the CUDA engine uses for a round.
 

@@ -46,14 +46,68 @@ def model_json_case(E, D):
     return {"model_ref_cfg3": (len(m.trees),)}
 
 
+def multiclass_case(E, D):
+    """A reference multi-class fit (E:2949-3065): its trees per class, its
+    predict_proba, train losses, and the first rounds' gradients, sample and
+    features (for tie audits)."""
+    X, y = D.multiclass()
+    Xtr, ytr, Xte = X[:6_400], y[:6_400], X[6_400:]
+    params = dict(n_estimators=10, max_depth=5, learning_rate=0.1, n_bins=64,
+                  class_weight="balanced_sqrt", random_state=0)
+    captured = []
+    cls = E.HybridHistGBMNumbaV1_0_1
+    orig = cls._build_one_tree
+
+    def spy(self, X_bin, grad, hess, sample_idx, feat_idx, n_features):
+        captured.append((grad.copy(), hess.copy(), sample_idx.copy(), feat_idx.copy()))
+        return orig(self, X_bin, grad, hess, sample_idx, feat_idx, n_features)
+
+    cls._build_one_tree = spy
+    try:
+        m = cls(verbose=False, **params)
+        m.fit(Xtr, ytr)
+    finally:
+        cls._build_one_tree = orig
+    K = m.n_classes_
+    T = len(m.mc_trees[0])
+    maxn = max(len(t[0]) for ts in m.mc_trees for t in ts)
+    arr = {k: np.full((K, T, maxn), fill, dtype=dt) for k, fill, dt in [
+        ("tf", -1, np.int32), ("tt", 0, np.int64), ("tv", 0.0, np.float64),
+        ("tl", -1, np.int32), ("tr", -1, np.int32), ("sg", 0.0, np.float64)]}
+    ncs = np.zeros((K, T), dtype=np.int32)
+    for k in range(K):
+        for t, (tf, tt, tv, tl, tr, nc, sg) in enumerate(m.mc_trees[k]):
+            for key, a in zip(("tf", "tt", "tv", "tl", "tr", "sg"), (tf, tt, tv, tl, tr, sg)):
+                arr[key][k, t, :len(a)] = a
+            ncs[k, t] = nc
+    extra = {}
+    for r_ in range(min(3, T)):
+        for k in range(K):
+            g, h, s, f = captured[r_ * K + k]
+            extra[f"r{r_}_k{k}_g"] = g
+            extra[f"r{r_}_k{k}_h"] = h
+        extra[f"r{r_}_sample"] = captured[r_ * K][2]
+        extra[f"r{r_}_feat"] = captured[r_ * K][3]
+    Xb, _ = m._bin_features(Xtr)
+    np.savez_compressed(
+        os.path.join(HERE, "fit_mc.npz"), params=np.array(repr(params)), n_classes=K, n_trees=T, nc=ncs,
+        **arr, **extra, learning_rate=m.learning_rate, max_leaves=m.max_leaves, max_depth=m.max_depth,
+        min_child_weight=m.min_child_weight, subsample=m.subsample, colsample=m.colsample_bytree,
+        reg_lambda=m.reg_lambda, gamma=m.gamma, min_samples_leaf=m.min_samples_leaf, n_bins=m.n_bins,
+        edges=m.bin_edges, counts=m.feature_bin_counts, nan_bin_id=m._nan_bin_id,
+        X_bin_sha=sha(Xb.astype(np.uint16)), train_loss=np.array(m.train_loss_history_),
+        proba_test=m.predict_proba(Xte), sample_sha=np.array([sha(c[2]) for c in captured[::K]]))
+    return {"fit_mc": (K, T)}
+
+
 def main(ref_src, only=None):
     sys.path.insert(0, ref_src)
     import bsscl_gbm.estimator_v1_0_1 as E
     from bsscl_gbm_b200 import datasets as D
 
     out = {}
-    if only == "model":
-        out.update(model_json_case(E, D))
+    if only in ("model", "multiclass"):
+        out.update(model_json_case(E, D) if only == "model" else multiclass_case(E, D))
         for k, v in out.items():
             print(k, v)
         return
@@ -288,6 +342,7 @@ def main(ref_src, only=None):
              dict(n_estimators=20, max_depth=4, learning_rate=0.1, n_bins=64,
                   class_weight="balanced", random_state=3, grow_policy="level"))
     out.update(model_json_case(E, D))
+    out.update(multiclass_case(E, D))
 
     for k, v in out.items():
         print(k, v)
@@ -296,5 +351,5 @@ def main(ref_src, only=None):
 if __name__ == "__main__":
     # python make_golden.py <reference>/src [model]   ('model': only the save_model fixture)
     if len(sys.argv) < 2:
-        sys.exit("usage: make_golden.py <reference>/src [model]")
+        sys.exit("usage: make_golden.py <reference>/src [model|multiclass]")
     main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else None)

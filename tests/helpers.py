@@ -25,6 +25,9 @@ def fit_inputs(name):
     if name == "cfg3_small":
         X, y = D.config3(n=25_000)
         return X[:20_000], y[:20_000], X[20_000:]
+    if name == "mc":
+        X, y = D.multiclass()
+        return X[:6_400], y[:6_400], X[6_400:]
     if name == "cfg4_small":
         X, y = D.config4(n=30_000)
         return X[:24_000], y[:24_000], X[24_000:]
@@ -54,6 +57,21 @@ def golden_trees(d):
         nc = int(d["nc"][t])
         out.append((d["tf"][t], d["tt"][t], d["tv"][t], d["tl"][t], d["tr"][t], nc, d["sg"][t]))
     return out
+
+
+def golden_mc_trees(d):
+    """Per class, the reference's trees of a multi-class fit fixture."""
+    K, T = int(d["n_classes"]), int(d["n_trees"])
+    return [[(d["tf"][k, t], d["tt"][k, t], d["tv"][k, t], d["tl"][k, t], d["tr"][k, t], int(d["nc"][k, t]),
+              d["sg"][k, t]) for t in range(T)] for k in range(K)]
+
+
+def mc_fit_kwargs(d):
+    return dict(n_estimators=int(d["n_trees"]), learning_rate=float(d["learning_rate"]),
+                max_leaves=int(d["max_leaves"]), max_depth=int(d["max_depth"]),
+                min_samples_leaf=int(d["min_samples_leaf"]), min_child_weight=float(d["min_child_weight"]),
+                reg_lambda=float(d["reg_lambda"]), gamma=float(d["gamma"]), subsample=float(d["subsample"]),
+                colsample=float(d["colsample"]), class_weight="balanced_sqrt", random_state=0)
 
 
 def same_topology(a, b):

@@ -141,3 +141,29 @@ def test_i128_conversion_rounds_to_nearest():
         vals.append((1 << bits) + (1 << max(0, bits - 53)))   # exact halfway cases
     for v in vals:
         assert O.i128_to_double(v) == float(v), v
+
+
+def test_ref_multiclass_fit_bit_exact():
+    """The oracle's multi-class loop (REF builder) == the reference's _fit_multiclass."""
+    import hashlib
+    from helpers import golden_mc_trees, mc_fit_kwargs
+    d = golden("fit_mc")
+    X, y, _ = fit_inputs("mc")
+    Xb = O.bin_matrix(X, d["edges"], d["counts"], d["nan_bin_id"], False)
+    assert hashlib.sha256(Xb.astype(np.uint16).tobytes()).hexdigest() == str(d["X_bin_sha"])
+    K = int(d["n_classes"])
+    rec = []
+    r = O.fit_multiclass(Xb, y, d["counts"], K, mode=O.MODE_REF, record=rec, **mc_fit_kwargs(d))
+    ref = golden_mc_trees(d)
+    for k in range(K):
+        for t, (a, b) in enumerate(zip(r["trees"][k], ref[k])):
+            assert same_topology(a, b), f"class {k} tree {t}"
+            nc = a[5]
+            assert np.abs(a[2][:nc] - b[2][:nc]).max() < 1e-12, f"values class {k} tree {t}"
+    for t, rr in enumerate(rec):
+        assert hashlib.sha256(rr["sample"].tobytes()).hexdigest() == str(d["sample_sha"][t])
+    for t in range(3):
+        for k in range(K):
+            assert np.array_equal(rec[t]["g"][k], d[f"r{t}_k{k}_g"]), (t, k)
+            assert np.array_equal(rec[t]["h"][k], d[f"r{t}_k{k}_h"]), (t, k)
+    assert np.abs(r["train_loss"] - d["train_loss"]).max() < 1e-12
