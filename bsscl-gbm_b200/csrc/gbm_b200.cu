@@ -37,6 +37,7 @@
 #include <cstring>
 #include <mutex>
 #include <new>
+#include <unordered_map>
 #include <string>
 #include <utility>
 #include <vector>
@@ -206,6 +207,7 @@ struct gbm_ctx {
     double flush_ms = 0.0;
 
     cudaEvent_t mark[16] = {};
+    std::unordered_map<void *, size_t> dcap, hcap;   // bytes of each buffer dalloc / halloc made
 };
 
 namespace {
@@ -317,27 +319,54 @@ void begin_round(gbm_ctx *ctx, int si) {
     ctx->slot[si].tused = ctx->slot[si].tdone = 0;
 }
 
+// (Re)allocation of a context buffer: one that is already big enough is
+// kept (a repeated upload of the same shape allocates nothing: cudaFree
+// synchronises the device and pinned allocations take milliseconds).  The
+// contents are not kept meaningful either way.  mem_gen counts pointer
+// changes (captured graphs hold pointers).
 template <typename T>
 int dalloc(gbm_ctx *ctx, T **p, size_t count) {
-    ctx->mem_gen++;
-    if (*p) { cudaFree(*p); *p = nullptr; }
     if (count == 0) count = 1;
-    cudaError_t e = cudaMalloc((void **)p, count * sizeof(T));
+    const size_t bytes = count * sizeof(T);
+    if (*p) {
+        auto it = ctx->dcap.find((void *)*p);
+        if (it != ctx->dcap.end() && it->second >= bytes) return GBM_OK;
+        if (it != ctx->dcap.end()) ctx->dcap.erase(it);
+        cudaFree(*p);
+        *p = nullptr;
+    }
+    ctx->mem_gen++;
+    cudaError_t e = cudaMalloc((void **)p, bytes);
     if (e != cudaSuccess)
-        return fail(ctx, GBM_ERR_ALLOC, "cudaMalloc(%zu bytes) failed: %s", count * sizeof(T),
-                    cudaGetErrorString(e));
+        return fail(ctx, GBM_ERR_ALLOC, "cudaMalloc(%zu bytes) failed: %s", bytes, cudaGetErrorString(e));
+    ctx->dcap[(void *)*p] = bytes;
     return GBM_OK;
+}
+
+// Frees a buffer dalloc made outside the context's members (a temporary).
+template <typename T>
+void dfree(gbm_ctx *ctx, T *p) {
+    if (!p) return;
+    ctx->dcap.erase((void *)p);
+    cudaFree(p);
 }
 
 template <typename T>
 int halloc(gbm_ctx *ctx, T **p, size_t count) {
-    ctx->mem_gen++;
-    if (*p) { cudaFreeHost(*p); *p = nullptr; }
     if (count == 0) count = 1;
-    cudaError_t e = cudaMallocHost((void **)p, count * sizeof(T));
+    const size_t bytes = count * sizeof(T);
+    if (*p) {
+        auto it = ctx->hcap.find((void *)*p);
+        if (it != ctx->hcap.end() && it->second >= bytes) return GBM_OK;
+        if (it != ctx->hcap.end()) ctx->hcap.erase(it);
+        cudaFreeHost(*p);
+        *p = nullptr;
+    }
+    ctx->mem_gen++;
+    cudaError_t e = cudaMallocHost((void **)p, bytes);
     if (e != cudaSuccess)
-        return fail(ctx, GBM_ERR_ALLOC, "cudaMallocHost(%zu bytes) failed: %s", count * sizeof(T),
-                    cudaGetErrorString(e));
+        return fail(ctx, GBM_ERR_ALLOC, "cudaMallocHost(%zu bytes) failed: %s", bytes, cudaGetErrorString(e));
+    ctx->hcap[(void *)*p] = bytes;
     return GBM_OK;
 }
 
@@ -607,7 +636,7 @@ int p2p_setup(gbm_ctx *ctx, int64_t stride) {
     int rc = allreduce_i64(ctx, d_tab, (int64_t)tab.size());
     if (rc == GBM_OK) rc = cudaMemcpyAsync(tab.data(), d_tab, sizeof(long long) * tab.size(), cudaMemcpyDeviceToHost,
                                            ctx->st) == cudaSuccess ? sync_stream(ctx) : GBM_ERR_CUDA;
-    cudaFree(d_tab);
+    dfree(ctx, d_tab);
     if (rc != GBM_OK) return rc;
     std::vector<long long *> pst((size_t)N, nullptr);
     std::vector<unsigned long long *> sy((size_t)N, nullptr);
@@ -1146,7 +1175,7 @@ int choose_skip_bins(gbm_ctx *ctx) {
         if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "bincount copy: %s", cudaGetErrorString(e)); break; }
         rc = sync_stream(ctx);
     } while (0);
-    cudaFree(d_cnt);
+    dfree(ctx, d_cnt);
     if (rc != GBM_OK) return rc;
     std::vector<int16_t> skip((size_t)ctx->nblk * kBlk, (int16_t)0);
     ctx->skip_keep.assign((size_t)ctx->p, 1.0);
@@ -1789,13 +1818,13 @@ int gbm_get_grad(gbm_ctx *ctx, double *g_out, double *h_out) {
     double *dg = nullptr, *dh = nullptr;
     TRY(dalloc(ctx, &dg, (size_t)ctx->n));
     int rc = dalloc(ctx, &dh, (size_t)ctx->n);
-    if (rc != GBM_OK) { cudaFree(dg); return rc; }
+    if (rc != GBM_OK) { dfree(ctx, dg); return rc; }
     k_export_grad<<<grid_for(ctx->n, 256), 256, 0, ctx->st>>>(ctx->d_F, ctx->d_y, ctx->n, ctx->w[0], ctx->w[1], dg, dh);
     cudaMemcpyAsync(g_out, dg, sizeof(double) * ctx->n, cudaMemcpyDeviceToHost, ctx->st);
     cudaMemcpyAsync(h_out, dh, sizeof(double) * ctx->n, cudaMemcpyDeviceToHost, ctx->st);
     cudaError_t e = cudaStreamSynchronize(ctx->st);
-    cudaFree(dg);
-    cudaFree(dh);
+    dfree(ctx, dg);
+    dfree(ctx, dh);
     if (e != cudaSuccess) return fail(ctx, GBM_ERR_CUDA, "gbm_get_grad: %s", cudaGetErrorString(e));
     return GBM_OK;
 }
@@ -1825,8 +1854,8 @@ int gbm_build_tree(gbm_ctx *ctx, const double *grad, const double *hess, const u
         if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->st);
         if (e != cudaSuccess) rc = fail(ctx, GBM_ERR_CUDA, "gbm_build_tree upload: %s", cudaGetErrorString(e));
     }
-    cudaFree(dg);
-    cudaFree(dh);
+    dfree(ctx, dg);
+    dfree(ctx, dh);
     if (rc != GBM_OK) return rc;
     ctx->have_labels = false;   // the device gradients no longer follow F
     TRY(prepare_round(ctx, nfeat, P));
@@ -2023,14 +2052,14 @@ int gbm_get_grad_mc(gbm_ctx *ctx, int32_t k, double *g_out, double *h_out) {
     double *dg = nullptr, *dh = nullptr;
     TRY(dalloc(ctx, &dg, (size_t)ctx->n));
     int rc = dalloc(ctx, &dh, (size_t)ctx->n);
-    if (rc != GBM_OK) { cudaFree(dg); return rc; }
+    if (rc != GBM_OK) { dfree(ctx, dg); return rc; }
     k_export_q<<<grid_for(ctx->n, 256), 256, 0, ctx->st>>>(ctx->d_qmc + (int64_t)k * ctx->n, ctx->n,
                                                            std::ldexp(1.0, -ctx->S), dg, dh);
     cudaMemcpyAsync(g_out, dg, sizeof(double) * ctx->n, cudaMemcpyDeviceToHost, ctx->st);
     cudaMemcpyAsync(h_out, dh, sizeof(double) * ctx->n, cudaMemcpyDeviceToHost, ctx->st);
     cudaError_t e = cudaStreamSynchronize(ctx->st);
-    cudaFree(dg);
-    cudaFree(dh);
+    dfree(ctx, dg);
+    dfree(ctx, dh);
     if (e != cudaSuccess) return fail(ctx, GBM_ERR_CUDA, "gbm_get_grad_mc: %s", cudaGetErrorString(e));
     return GBM_OK;
 }
@@ -2351,7 +2380,7 @@ int gbm_set_l2_flush(gbm_ctx *ctx, int64_t bytes) {
     if (ctx->dev < 0) return GBM_ERR_STATE;
     CK(cudaSetDevice(ctx->dev));
     TRY(sync_stream(ctx));
-    if (ctx->d_flush) { cudaFree(ctx->d_flush); ctx->d_flush = nullptr; }
+    if (ctx->d_flush) { dfree(ctx, ctx->d_flush); ctx->d_flush = nullptr; }
     ctx->flush_bytes = 0;
     if (bytes > 0) {
         TRY(dalloc(ctx, &ctx->d_flush, (size_t)bytes));
