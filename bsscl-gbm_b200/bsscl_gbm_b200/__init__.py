@@ -5,8 +5,8 @@
 round and every predict runs in libgbm_b200.so on an NVIDIA B200.
 """
 
-from .estimator import HybridHistGBMNumbaV1_0_1
+from .estimator import HybridHistGBMNumbaV1_0_1, HybridHistGBMRegressorV1_0_1
 from ._lib import Engine, Sampler, GbmParams, build, lib
 
-__all__ = ["HybridHistGBMNumbaV1_0_1", "Engine", "Sampler", "GbmParams", "build", "lib"]
+__all__ = ["HybridHistGBMNumbaV1_0_1", "HybridHistGBMRegressorV1_0_1", "Engine", "Sampler", "GbmParams", "build", "lib"]
 __version__ = "0.1.0"

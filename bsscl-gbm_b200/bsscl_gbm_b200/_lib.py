@@ -33,7 +33,7 @@ EXPORTS = (
     "gbm_event_elapsed", "gbm_predict_noalloc", "gbm_fit_rounds", "gbm_upload_bins_u16",
     "gbm_set_l2_flush", "gbm_bin_edges", "gbm_upload_binned_rows", "gbm_bin_features",
     "gbm_predict_upload_raw", "gbm_predict_raw", "gbm_test_peer_wait", "gbm_upload_labels_mc",
-    "gbm_round_mc", "gbm_get_F_mc", "gbm_get_grad_mc",
+    "gbm_round_mc", "gbm_get_F_mc", "gbm_get_grad_mc", "gbm_upload_targets", "gbm_round_reg",
 )
 
 
@@ -142,6 +142,8 @@ def lib():
     L.gbm_round_mc.argtypes = [P, P, P, i32, C.POINTER(GbmParams), C.POINTER(GbmTreeOut), C.POINTER(C.c_double)]
     L.gbm_get_F_mc.argtypes = [P, P]
     L.gbm_get_grad_mc.argtypes = [P, i32, P, P]
+    L.gbm_upload_targets.argtypes = [P, P, f64, i32, i64]
+    L.gbm_round_reg.argtypes = [P, P, P, i32, C.POINTER(GbmParams), C.POINTER(GbmTreeOut), C.POINTER(C.c_double)]
     L.gbm_predict_noalloc.argtypes = [P, i64, i32, P, P, P, P, P, P, i32, i32, f64, f64, P, P, P,
                                       C.c_char_p, i32]
     _lib = L
@@ -313,6 +315,25 @@ class Engine:
         loss = C.c_double(0.0)
         self.check(self._L.gbm_round(self._h, ptr(mask), ptr(fidx), len(fidx), C.byref(params),
                                      C.byref(out), C.byref(loss)), "gbm_round")
+        return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value), leaf
+
+    # -- regression --
+    def upload_targets(self, y, init_score, loss="mse", n_global=0):
+        yy = np.ascontiguousarray(y, dtype=np.float64)
+        self.check(self._L.gbm_upload_targets(self._h, ptr(yy), float(init_score), 0 if loss == "mse" else 1,
+                                              int(n_global)), "gbm_upload_targets")
+
+    def round_reg(self, inbag_mask, feat_idx, params: GbmParams, capacity, want_leaf=False):
+        mask = np.ascontiguousarray(inbag_mask, dtype=np.uint8)
+        fidx = np.ascontiguousarray(feat_idx, dtype=np.int32)
+        tf = np.empty(capacity, np.int32); tt = np.empty(capacity, np.int64)
+        tv = np.empty(capacity, np.float64); tl = np.empty(capacity, np.int32)
+        tr = np.empty(capacity, np.int32); sg = np.empty(capacity, np.float64)
+        leaf = np.empty(self.n, np.int32) if want_leaf else None
+        out = GbmTreeOut(capacity, ptr(tf), ptr(tt), ptr(tv), ptr(tl), ptr(tr), ptr(sg), 0, ptr(leaf))
+        loss = C.c_double(0.0)
+        self.check(self._L.gbm_round_reg(self._h, ptr(mask), ptr(fidx), len(fidx), C.byref(params),
+                                         C.byref(out), C.byref(loss)), "gbm_round_reg")
         return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value), leaf
 
     # -- multi-class softmax --

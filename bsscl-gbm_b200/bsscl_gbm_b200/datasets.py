@@ -171,3 +171,15 @@ def multiclass(n=8_000, p=12, K=4, seed=7, nan_frac=0.05):
     X = centres[y] + rng.standard_normal((n, p))
     X[:, -3:][rng.random((n, 3)) < nan_frac] = np.nan
     return X, y.astype(np.int64)
+
+
+def regression(n=8_000, p=10, seed=9, nan_frac=0.05, scale=100.0):
+    """A stand-in for the reference's regression path (E:2607-2705): targets
+    ``scale * (sin(x0) + x1 * x2 / 2 + 0.3 x3^2) + N(0, scale / 10)``, NaN in
+    the last two columns."""
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((n, p))
+    y = scale * (np.sin(X[:, 0]) + 0.5 * X[:, 1] * X[:, 2] + 0.3 * X[:, 3] ** 2) \
+        + rng.standard_normal(n) * (scale / 10.0)
+    X[:, -2:][rng.random((n, 2)) < nan_frac] = np.nan
+    return X, y

@@ -307,9 +307,11 @@ class HybridHistGBMNumbaV1_0_1:
     # fit
     # ------------------------------------------------------------------
     def _check_supported(self):
-        if self.objective not in ('auto', 'binary'):
+        if self.objective not in ('auto', 'binary', 'regression'):
             raise NotImplementedError(f"objective={self.objective!r}: the B200 engine trains "
-                                      "binary log-loss only")
+                                      "log-loss (binary, multi-class) and regression")
+        if self.objective == 'regression' and self.loss not in ('mse', 'mae'):
+            raise NotImplementedError(f"loss={self.loss!r}: regression takes 'mse' or 'mae'")
         if self.sampling_method != 'uniform':
             raise NotImplementedError("sampling_method='goss' is not on the B200 engine")
         if self.boosting_type != 'gbdt':
@@ -345,14 +347,23 @@ class HybridHistGBMNumbaV1_0_1:
             raise ValueError(f"X has {X.shape[0]} rows but y has {len(y)}")
         if X.shape[0] == 0:
             raise ValueError("X is empty")
-        self.classes_ = np.unique(y)
-        self.n_classes_ = len(self.classes_)
-        if self.n_classes_ > 64:
-            raise NotImplementedError("the B200 engine holds at most 64 classes")
-        self._is_multiclass = self.n_classes_ > 2
-        # class index of every label (classes_ is sorted and unique)
-        y = np.searchsorted(self.classes_, y).astype(np.int64)
-        if y_val is not None:
+        regression = self.objective == 'regression'
+        if regression:   # E:3113-3119
+            self._is_multiclass = False
+            self.classes_ = None
+            self.n_classes_ = 1
+            y = np.array(y, dtype=np.float64)
+            if y_val is not None:
+                y_val = np.array(y_val, dtype=np.float64)
+        else:
+            self.classes_ = np.unique(y)
+            self.n_classes_ = len(self.classes_)
+            if self.n_classes_ > 64:
+                raise NotImplementedError("the B200 engine holds at most 64 classes")
+            self._is_multiclass = self.n_classes_ > 2
+            # class index of every label (classes_ is sorted and unique)
+            y = np.searchsorted(self.classes_, y).astype(np.int64)
+        if y_val is not None and not regression:
             y_val = np.asarray(y_val)
             yv = np.searchsorted(self.classes_, y_val)
             if np.any(yv >= len(self.classes_)) or np.any(self.classes_[np.minimum(yv, len(self.classes_) - 1)] != y_val):
@@ -421,7 +432,9 @@ class HybridHistGBMNumbaV1_0_1:
                 X_val_bin = binning.bin_features(X_val, self.bin_edges, self.feature_bin_counts,
                                                  self._nan_bin_id)
         t0 = time.perf_counter()
-        if self._is_multiclass:
+        if regression:
+            self._fit_regression_device(X_bin, y, X_val_bin, y_val)
+        elif self._is_multiclass:
             self._fit_multiclass_device(X_bin, y, X_val_bin, y_val)
         else:
             self._fit_binary_device(X_bin, y, X_val_bin, y_val)
@@ -533,6 +546,69 @@ class HybridHistGBMNumbaV1_0_1:
                                 stop = True
                                 break
                     m += 1
+        finally:
+            sampler.close()
+        self.times['rounds'] = (time.perf_counter() - t_rounds) * 1000
+        self.n_trees_fitted_ = len(self.trees)
+
+    def _fit_regression_device(self, X_bin, y, X_val_bin, y_val):
+        """The reference's ``_fit_regression`` loop (E:2607-2705) with every round
+        on the GPU (gbm_round_reg): F from mean(y), g = F - y (mse) or
+        sign(F - y) (mae), h = 1."""
+        n, p = X_bin.shape
+        self.init_score_ = float(np.mean(y))
+        self.base_score_ = 0.0
+        n_sub = max(1, int(n * self.subsample))
+        n_feat = max(1, int(p * self.colsample_bytree))
+        seed = self.random_state
+        if seed is None:
+            seed = int.from_bytes(os.urandom(4), "little")
+        if not (0 <= int(seed) <= 0xFFFFFFFF):
+            raise ValueError("Seed must be between 0 and 2**32 - 1")
+        sampler = Sampler(int(seed), n, p, n_sub, n_feat, self.subsample < 1.0,
+                          self.colsample_bytree < 1.0, look_ahead=3)
+        eng = self._get_engine()
+        lo, hi = _rank_rows(n)
+        _ensure_comm(eng)
+        self._check_device_bins()
+        t_up = time.perf_counter()
+        if not isinstance(X_bin, _BinsOnDevice):
+            Xr = X_bin[lo:hi]
+            if Xr.dtype not in (np.uint8, np.uint16):
+                Xr = binning.device_bins(Xr, self.feature_bin_counts)
+            eng.upload_bins(Xr, self.feature_bin_counts)
+        eng.upload_targets(y[lo:hi], self.init_score_, self.loss, n_global=n)
+        self.times['upload'] = (time.perf_counter() - t_up) * 1000
+        params = self._params_struct()
+        cap = self._tree_capacity()
+        F_val = np.full(len(y_val), self.init_score_) if y_val is not None else None
+        best_val, no_improve = np.inf, 0
+        t_rounds = time.perf_counter()
+        try:
+            for m in range(self.n_estimators):
+                _, mask, feat = sampler.next(want_sample=False, want_mask=True)
+                tree, loss, _ = eng.round_reg(mask[lo:hi], feat, params, cap)
+                self.trees.append(tree)
+                self.train_loss_history_.append(loss)
+                val_loss = None
+                if F_val is not None:
+                    F_val += self.learning_rate * _predict_tree_host(X_val_bin, tree)
+                    val_loss = (np.mean((y_val - F_val) ** 2) if self.loss == 'mse'
+                                else np.mean(np.abs(y_val - F_val)))
+                    self.val_loss_history_.append(val_loss)
+                if self.verbose and ((m + 1) % 20 == 0 or m == 0):
+                    msg = f"  Tree {m + 1:>3}/{self.n_estimators}  |  train-loss: {loss:.6f}"
+                    if val_loss is not None:
+                        msg += f"  |  val-loss: {val_loss:.6f}"
+                    print(msg)
+                if self.early_stopping_rounds is not None and val_loss is not None:
+                    if val_loss < best_val:
+                        best_val, self.best_iteration_, no_improve = val_loss, m, 0
+                    else:
+                        no_improve += 1
+                        if no_improve >= self.early_stopping_rounds:
+                            self.trees = self.trees[:self.best_iteration_ + 1]
+                            break
         finally:
             sampler.close()
         self.times['rounds'] = (time.perf_counter() - t_rounds) * 1000
@@ -715,6 +791,16 @@ class HybridHistGBMNumbaV1_0_1:
         return np.column_stack([1 - proba, proba])
 
     def predict(self, X):
+        if self.objective == 'regression':   # init score + the ensemble (E:3352-3360)
+            X = np.asarray(X)
+            if not np.issubdtype(X.dtype, np.floating) or X.dtype == np.float16:
+                X = X.astype(np.float64)
+            self._check_device_bins()
+            eng = self._get_engine()
+            F, _ = eng.predict_raw(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id,
+                                   self._packed(), len(self.trees), self.learning_rate,
+                                   self.init_score_, want_F=True, want_proba=False)
+            return F
         proba = self.predict_proba(X)
         if self._is_multiclass:
             return self.classes_[np.argmax(proba, axis=1)]
@@ -789,7 +875,9 @@ class HybridHistGBMNumbaV1_0_1:
         import json
         with open(filepath) as f:
             data = json.load(f)
-        model = cls(**data['params'])
+        import inspect
+        accepted = inspect.signature(cls.__init__).parameters   # a subclass may take fewer
+        model = cls(**{k: v for k, v in data['params'].items() if k in accepted})
         model.n_classes_ = data['n_classes_']
         model.classes_ = np.array(data['classes_']) if data['classes_'] is not None else None
         model.n_features_in_ = data['n_features_in_']
@@ -918,3 +1006,25 @@ def _logloss(y, F):
     p = 1.0 / (1.0 + np.exp(-np.clip(F, -500, 500)))
     p = np.clip(p, 1e-15, 1 - 1e-15)
     return -np.mean(y * np.log(p) + (1 - y) * np.log(1 - p))
+
+
+class HybridHistGBMRegressorV1_0_1(HybridHistGBMNumbaV1_0_1):
+    """The reference's regressor (objective='regression', mse or mae) on the B200 engine."""
+
+    def __init__(self, n_estimators='auto', max_depth='auto', learning_rate='auto',
+                 n_bins='auto', reg_lambda=1.0, min_samples_leaf=5,
+                 min_child_weight='auto', gamma='auto',
+                 subsample='auto', colsample_bytree='auto',
+                 grow_policy='leaf', max_leaves=31, binning_strategy='auto',
+                 monotone_constraints=None, categorical_features=None,
+                 early_stopping_rounds=None, verbose=True, random_state=None,
+                 loss='mse', device='b200'):
+        super().__init__(
+            n_estimators=n_estimators, max_depth=max_depth, learning_rate=learning_rate,
+            n_bins=n_bins, reg_lambda=reg_lambda, min_samples_leaf=min_samples_leaf,
+            min_child_weight=min_child_weight, gamma=gamma, subsample=subsample,
+            colsample_bytree=colsample_bytree, class_weight=None, grow_policy=grow_policy,
+            max_leaves=max_leaves, binning_strategy=binning_strategy,
+            monotone_constraints=monotone_constraints, categorical_features=categorical_features,
+            early_stopping_rounds=early_stopping_rounds, verbose=verbose, random_state=random_state,
+            objective='regression', focal_gamma=2.0, loss=loss, device=device)

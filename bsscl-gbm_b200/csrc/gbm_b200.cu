@@ -168,6 +168,11 @@ struct gbm_ctx {
     int32_t *d_mono = nullptr, *h_mono = nullptr;
     int replay_smem = 0;               // dynamic shared memory the replay kernels may use
 
+    // regression: float64 targets, mse (0) or mae (1); S follows the largest |g| each round
+    bool have_targets = false;
+    int reg_mae = 0;
+    double *d_yr = nullptr, *d_gmax_part = nullptr, *d_gmax = nullptr;
+    long long *d_stab = nullptr;       // several ranks: the one-hot table of the proposed S
     // multi-class softmax: K classes, F and q class-major ([k][n])
     int K = 0;
     bool have_labels_mc = false;
@@ -1480,7 +1485,7 @@ int begin_bins(gbm_ctx *ctx, int64_t n, int32_t p, const int32_t *bin_counts) {
     CK(cudaSetDevice(ctx->dev));
     ctx->n = n; ctx->p = p; ctx->nblk = (p + kBlk - 1) / kBlk;
     ctx->slots_ready = false;
-    ctx->have_bins = ctx->have_labels = false;
+    ctx->have_bins = ctx->have_labels = ctx->have_labels_mc = ctx->have_targets = false;
     ctx->counts.assign(bin_counts, bin_counts + p);
     TRY(dalloc(ctx, &ctx->d_xb, (size_t)ctx->nblk * n * kBlk));
     TRY(dalloc(ctx, &ctx->d_counts, (size_t)p));
@@ -1675,7 +1680,8 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
                         ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,
                         ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi, ctx->d_side,
-                        ctx->d_upstage, ctx->d_Fmc, ctx->d_wmc, ctx->d_qmc};
+                        ctx->d_upstage, ctx->d_Fmc, ctx->d_wmc, ctx->d_qmc, ctx->d_yr,
+                        ctx->d_gmax_part, ctx->d_gmax, ctx->d_stab};
     for (int32_t *q : ctx->d_perm) if (q) cudaFree(q);
     for (void *p : dev_ptrs) if (p) cudaFree(p);
     void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_mono};
@@ -1798,6 +1804,7 @@ int gbm_upload_labels(gbm_ctx *ctx, const uint8_t *y, const double class_w[2], d
     CKL();
     TRY(sync_stream(ctx));
     ctx->have_labels = true;
+    ctx->have_targets = ctx->have_labels_mc = false;
     return GBM_OK;
 }
 
@@ -1805,7 +1812,7 @@ int32_t gbm_scale_bits(const gbm_ctx *ctx) { return ctx ? ctx->S : 0; }
 
 int gbm_get_F(gbm_ctx *ctx, double *F_out) {
     if (!ctx || !F_out) return GBM_ERR_ARG;
-    if (!ctx->have_labels) return GBM_ERR_STATE;
+    if (!ctx->have_labels && !ctx->have_targets) return GBM_ERR_STATE;
     CK(cudaSetDevice(ctx->dev));
     CK(cudaMemcpyAsync(F_out, ctx->d_F, sizeof(double) * ctx->n, cudaMemcpyDeviceToHost, ctx->st));
     return sync_stream(ctx);
@@ -1813,6 +1820,21 @@ int gbm_get_F(gbm_ctx *ctx, double *F_out) {
 
 int gbm_get_grad(gbm_ctx *ctx, double *g_out, double *h_out) {
     if (!ctx || !g_out || !h_out) return GBM_ERR_ARG;
+    if (ctx->have_targets) {   // regression: the quantised gradients as the engine holds them
+        CK(cudaSetDevice(ctx->dev));
+        double *dg = nullptr, *dh = nullptr;
+        TRY(dalloc(ctx, &dg, (size_t)ctx->n));
+        int rc = dalloc(ctx, &dh, (size_t)ctx->n);
+        if (rc != GBM_OK) { dfree(ctx, dg); return rc; }
+        k_export_q<<<grid_for(ctx->n, 256), 256, 0, ctx->st>>>(ctx->d_q, ctx->n, std::ldexp(1.0, -ctx->S), dg, dh);
+        cudaMemcpyAsync(g_out, dg, sizeof(double) * ctx->n, cudaMemcpyDeviceToHost, ctx->st);
+        cudaMemcpyAsync(h_out, dh, sizeof(double) * ctx->n, cudaMemcpyDeviceToHost, ctx->st);
+        cudaError_t e = cudaStreamSynchronize(ctx->st);
+        dfree(ctx, dg);
+        dfree(ctx, dh);
+        if (e != cudaSuccess) return fail(ctx, GBM_ERR_CUDA, "gbm_get_grad: %s", cudaGetErrorString(e));
+        return GBM_OK;
+    }
     if (!ctx->have_labels) return GBM_ERR_STATE;
     CK(cudaSetDevice(ctx->dev));
     double *dg = nullptr, *dh = nullptr;
@@ -1924,6 +1946,115 @@ static int round_body(gbm_ctx *ctx, int si, const int32_t *feat_idx, int32_t nfe
     return GBM_OK;
 }
 
+// ---- regression (E:2607-2705) ------------------------------------------------
+
+// S for the next round from the largest |g| (every rank's: each proposes its
+// S, the all-reduce of a one-hot table gives the smallest), then the
+// quantised gradients.
+static int reg_requantize(gbm_ctx *ctx, double gmax) {
+    int S = scale_bits_for(ctx->reg_mae ? 1.0 : gmax);
+    if (ctx->comm) {
+        long long tab[128] = {};
+        const int slot = std::min(127, std::max(0, S + 64));
+        tab[slot] = 1;
+        CK(cudaMemcpyAsync(ctx->d_stab, tab, sizeof tab, cudaMemcpyHostToDevice, ctx->st));
+        TRY(allreduce_i64(ctx, ctx->d_stab, 128));
+        CK(cudaMemcpyAsync(tab, ctx->d_stab, sizeof tab, cudaMemcpyDeviceToHost, ctx->st));
+        TRY(sync_stream(ctx));
+        for (int k = 0; k < 128; k++)
+            if (tab[k]) { S = k - 64; break; }
+    }
+    ctx->S = S;
+    k_reg_quant<<<grid_for(ctx->n, 256), 256, 0, ctx->st>>>(ctx->d_F, ctx->d_yr, ctx->n, ctx->reg_mae,
+                                                            std::ldexp(1.0, S), ctx->d_q);
+    CKL();
+    return GBM_OK;
+}
+
+int gbm_upload_targets(gbm_ctx *ctx, const double *y, double init_score, int32_t loss, int64_t n_global) {
+    if (!ctx || !y || (loss != 0 && loss != 1) || !std::isfinite(init_score)) return GBM_ERR_ARG;
+    if (!ctx->have_bins) return fail(ctx, GBM_ERR_STATE, "upload bins before targets");
+    double gmax = 0.0;
+    for (int64_t i = 0; i < ctx->n; i++) {
+        if (!std::isfinite(y[i])) return fail(ctx, GBM_ERR_ARG, "target %lld is not finite", (long long)i);
+        gmax = std::max(gmax, std::fabs(init_score - y[i]));
+    }
+    CK(cudaSetDevice(ctx->dev));
+    ctx->reg_mae = loss;
+    ctx->base = init_score;
+    ctx->n_global = n_global > 0 ? n_global : ctx->n;
+    TRY(dalloc(ctx, &ctx->d_yr, (size_t)ctx->n));
+    TRY(dalloc(ctx, &ctx->d_gmax_part, (size_t)ctx->upd_blocks));
+    TRY(dalloc(ctx, &ctx->d_gmax, 1));
+    TRY(dalloc(ctx, &ctx->d_stab, 128));
+    CK(cudaMemcpyAsync(ctx->d_yr, y, sizeof(double) * (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    k_fill<<<grid_for(ctx->n, 256), 256, 0, ctx->st>>>(ctx->d_F, ctx->n, init_score);
+    CKL();
+    TRY(reg_requantize(ctx, gmax));
+    TRY(sync_stream(ctx));
+    ctx->have_labels = ctx->have_labels_mc = false;
+    ctx->have_targets = true;
+    return GBM_OK;
+}
+
+int gbm_round_reg(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
+                  const gbm_params *P, gbm_tree_out *out, double *train_loss) {
+    if (!ctx || !inbag_mask || !feat_idx || !P || !out) return GBM_ERR_ARG;
+    if (!ctx->have_targets) return fail(ctx, GBM_ERR_STATE, "upload bins and gbm_upload_targets first");
+    TRY(check_tree_args(ctx, nfeat, P, out));
+    CK(cudaSetDevice(ctx->dev));
+    TRY(prepare_round(ctx, nfeat, P));
+    std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
+    CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    gbm_ctx::Slot &s = ctx->slot[0];
+    begin_round(ctx, 0);
+    RoundFeat rf;
+    TRY(setup_features(ctx, 0, feat_idx, nfeat, rf));
+    TRY(enqueue_features(ctx, 0, nfeat));
+    TRY(enqueue_grow(ctx, rf, P, false));
+    if (device_replay(ctx, P)) {
+        TRY(enqueue_replay(ctx, P));
+        CK(cudaMemcpyAsync(s.h_tout, ctx->d_tout, sizeof(TreeOut), cudaMemcpyDeviceToHost, ctx->st));
+        CK(cudaEventRecord(s.done, ctx->st));
+        TRY(wait_slot(ctx, 0));
+        TRY(harvest(ctx, 0, nfeat, P, out, nullptr));
+    } else {
+        HostTree T;
+        TRY(replay_on_host(ctx, rf, P, T));
+        if (T.nc > 256) return fail(ctx, GBM_ERR_UNSUPPORTED, "tree with %d nodes exceeds 256", T.nc);
+        TreeDev td;
+        std::memset(&td, 0, sizeof td);
+        td.n = T.nc;
+        for (int j = 0; j < T.nc; j++) {
+            td.feat[j] = T.tf[j];
+            td.thr[j] = (int)std::min<int64_t>(T.tt[j], 255);
+            td.left[j] = T.tl[j];
+            td.right[j] = T.tr[j];
+            td.val[j] = T.tv[j];
+        }
+        CK(cudaMemcpyAsync(ctx->d_tree, &td, sizeof td, cudaMemcpyHostToDevice, ctx->st));
+        TRY(sync_stream(ctx));
+        write_tree(T, tree_need(P), out);
+    }
+    TRY(launch(ctx, k_update_reg, dim3(ctx->upd_blocks), dim3(kUpdThreads), 0, ctx->st, (const TreeDev *)ctx->d_tree,
+               (const uint8_t *)ctx->d_xb, ctx->n, P->learning_rate, ctx->d_F, (const double *)ctx->d_yr,
+               ctx->reg_mae, out->leaf_of_row ? ctx->d_leaf : (int32_t *)nullptr, ctx->d_loss_part,
+               ctx->d_gmax_part));
+    TRY(launch(ctx, k_sum_partials, dim3(1), dim3(256), 0, ctx->st, ctx->d_loss_part, ctx->upd_blocks, ctx->d_loss));
+    TRY(launch(ctx, k_max_partials, dim3(1), dim3(32), 0, ctx->st, (const double *)ctx->d_gmax_part,
+               ctx->upd_blocks, ctx->d_gmax));
+    if (ctx->comm) TRY(allreduce_f64(ctx, ctx->d_loss, 1));
+    if (out->leaf_of_row)
+        CK(cudaMemcpyAsync(out->leaf_of_row, ctx->d_leaf, sizeof(int32_t) * ctx->n, cudaMemcpyDeviceToHost, ctx->st));
+    double gmax = 0.0;
+    CK(cudaMemcpyAsync(s.h_loss, ctx->d_loss, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
+    CK(cudaMemcpyAsync(&gmax, ctx->d_gmax, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
+    TRY(sync_stream(ctx));
+    if (train_loss) *train_loss = s.h_loss[0] / (double)ctx->n_global;
+    TRY(reg_requantize(ctx, gmax));   // the next round's gradients
+    return sync_stream(ctx);
+}
+
 // ---- multi-class softmax (E:2949-3065) ---------------------------------------
 
 int gbm_upload_labels_mc(gbm_ctx *ctx, const uint8_t *y, int32_t n_classes, const double *class_w,
@@ -1954,7 +2085,7 @@ int gbm_upload_labels_mc(gbm_ctx *ctx, const uint8_t *y, int32_t n_classes, cons
                                                                  std::ldexp(1.0, ctx->S), ctx->d_qmc, ctx->d_loss_part);
     CKL();
     TRY(sync_stream(ctx));
-    ctx->have_labels = false;   // the binary state no longer follows
+    ctx->have_labels = ctx->have_targets = false;   // the other objectives' state no longer follows
     ctx->have_labels_mc = true;
     return GBM_OK;
 }

@@ -241,6 +241,93 @@ k_update_class(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb,
     }
 }
 
+// ---------------------------------------------------------------------------
+// regression (E:2607-2705): g = F - y (mse) or sign(F - y) (mae), h = 1
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ double reg_grad(double f, double y, int mae) {
+    const double d = __dsub_rn(f, y);
+    if (!mae) return d;
+    return d > 0.0 ? 1.0 : (d < 0.0 ? -1.0 : 0.0);   // np.sign
+}
+
+// F = init score (E:2613-2614).
+__global__ void k_fill(double *__restrict__ F, int64_t n, double v) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) F[i] = v;
+}
+
+// The round's quantised gradients on the grid 2^-S.
+__global__ void k_reg_quant(const double *__restrict__ F, const double *__restrict__ y, int64_t n, int mae,
+                            double scale, longlong2 *__restrict__ q) {
+    griddep_wait();
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    q[i] = make_longlong2(__double2ll_rn(__dmul_rn(reg_grad(F[i], y[i], mae), scale)), __double2ll_rn(scale));
+}
+
+// F += lr * value(leaf) (E:2660-2661); per block the loss partial
+// sum (y - F)^2 or |y - F| (E:2663) and the largest |g| of the next round.
+__global__ void __launch_bounds__(kUpdThreads)
+k_update_reg(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64_t n, double lr,
+             double *__restrict__ F, const double *__restrict__ y, int mae, int32_t *__restrict__ leaf_out,
+             double *__restrict__ loss_part, double *__restrict__ gmax_part) {
+    griddep_wait();
+    __shared__ int s_feat[256], s_thr[256], s_left[256], s_right[256];
+    __shared__ double s_val[256];
+    __shared__ double s_red[kUpdThreads / 32], s_mx[kUpdThreads / 32];
+    const int nn = tree->n;
+    if (nn <= 0) return;
+    for (int k = threadIdx.x; k < nn; k += blockDim.x) {
+        s_feat[k] = tree->feat[k];
+        s_thr[k] = tree->thr[k];
+        s_left[k] = tree->left[k];
+        s_right[k] = tree->right[k];
+        s_val[k] = tree->val[k];
+    }
+    __syncthreads();
+    double acc = 0.0, mx = 0.0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int node = 0;
+        while (s_feat[node] >= 0) {
+            const int b = bin_of(xb, n, i, s_feat[node]);
+            node = (b <= s_thr[node]) ? s_left[node] : s_right[node];
+        }
+        if (leaf_out) leaf_out[i] = node;
+        const double f = __dadd_rn(F[i], __dmul_rn(lr, s_val[node]));
+        F[i] = f;
+        const double r = __dsub_rn(y[i], f);
+        acc += mae ? fabs(r) : __dmul_rn(r, r);
+        mx = fmax(mx, fabs(reg_grad(f, y[i], mae)));
+    }
+    acc = warp_sum(acc);
+    for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_down_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) {
+        s_red[threadIdx.x >> 5] = acc;
+        s_mx[threadIdx.x >> 5] = mx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0, m = 0.0;
+        for (int w2 = 0; w2 < kUpdThreads / 32; w2++) {
+            s += s_red[w2];
+            m = fmax(m, s_mx[w2]);
+        }
+        loss_part[blockIdx.x] = s;
+        gmax_part[blockIdx.x] = m;
+    }
+}
+
+// max of the per-block partials (one thread; a few hundred values)
+__global__ void k_max_partials(const double *__restrict__ part, int m, double *__restrict__ out) {
+    griddep_wait();
+    if (threadIdx.x || blockIdx.x) return;
+    double v = 0.0;
+    for (int k = 0; k < m; k++) v = fmax(v, part[k]);
+    *out = v;
+}
+
 // The quantised (g, h) of n rows as float64 (exact: |q| < 2^53).
 __global__ void k_export_q(const longlong2 *__restrict__ q, int64_t n, double inv_scale, double *__restrict__ g,
                            double *__restrict__ h) {

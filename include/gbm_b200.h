@@ -166,6 +166,22 @@ int gbm_bin_features(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t 
 int gbm_upload_labels(gbm_ctx *ctx, const uint8_t *y, const double class_w[2],
                       double base_score, int64_t n_global);
 
+/* ---- regression (E:2607-2705) ------------------------------------------ */
+
+/* Float64 targets of this rank's rows, the initial score (the mean of all
+ * targets, E:2612) and the loss: 0 = mse (g = F - y), 1 = mae
+ * (g = sign(F - y)); h = 1.  Each round's fixed-point grid 2^-S follows the
+ * round's largest |g| (the smallest S over ranks), so the integer sums stay
+ * exact whatever the targets' scale. */
+int gbm_upload_targets(gbm_ctx *ctx, const double *y, double init_score, int32_t loss, int64_t n_global);
+
+/* One regression round (the loop body of _fit_regression, E:2625-2663): the
+ * tree from the current gradients, F += lr * value(leaf), the train loss
+ * mean((y - F)^2) or mean(|y - F|), then the next round's gradients.
+ * gbm_get_grad / gbm_get_F / gbm_scale_bits give the next round's state. */
+int gbm_round_reg(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
+                  const gbm_params *params, gbm_tree_out *out, double *train_loss);
+
 /* ---- multi-class softmax (E:2949-3065) --------------------------------- */
 
 /* Labels 0..n_classes-1 (3 <= n_classes <= 64) of this rank's rows and the

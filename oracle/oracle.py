@@ -331,6 +331,56 @@ def fit_multiclass(X_bin, y, counts, K, *, n_estimators, learning_rate, max_leav
     return dict(trees=trees, F=F, train_loss=np.array(losses), w=w)
 
 
+def reg_scale_bits(gmax):
+    """The engine's fixed-point exponent for a regression round:
+    ``62 - ceil(log2(16384 * max(1, max|g|)))``."""
+    return 62 - int(np.ceil(np.log2(16384.0 * max(1.0, float(gmax)))))
+
+
+def fit_regression(X_bin, y, counts, *, n_estimators, learning_rate, max_leaves, max_depth,
+                   min_samples_leaf, min_child_weight, reg_lambda, gamma, subsample, colsample,
+                   random_state, loss="mse", mode=MODE_REF, grow_policy="leaf", record=None):
+    """The reference's ``_fit_regression`` loop (E:2607-2705) on the oracle
+    builders: F from mean(y), g = F - y (mse) or sign(F - y) (mae), h = 1.
+    In MODE_EXACT each round's S follows its largest |g| as the engine's does."""
+    y = np.asarray(y, dtype=np.float64)
+    n, p = X_bin.shape
+    init = float(np.mean(y))
+    F = np.full(n, init, dtype=np.float64)
+    n_sub = max(1, int(n * subsample))
+    n_feat = max(1, int(p * colsample))
+    rng = np.random.RandomState(random_state)
+    all_r = np.arange(n, dtype=np.int64)
+    all_f = np.arange(p, dtype=np.int32)
+    trees, losses = [], []
+    for m in range(n_estimators):
+        g = F - y if loss == "mse" else np.sign(F - y)
+        h = np.ones(n, dtype=np.float64)
+        if subsample < 1.0:
+            rng.shuffle(all_r)
+            sidx = all_r[:n_sub].copy()
+        else:
+            sidx = all_r.copy()
+        if colsample < 1.0:
+            rng.shuffle(all_f)
+            fidx = np.sort(all_f[:n_feat]).copy()
+        else:
+            fidx = all_f.copy()
+        S = reg_scale_bits(1.0 if loss == "mae" else np.max(np.abs(g))) if mode == MODE_EXACT else 0
+        t = build_tree(X_bin, g, h, sidx, fidx, counts, max_leaves=max_leaves, max_depth=max_depth,
+                       msl=min_samples_leaf, mcw=min_child_weight, lam=reg_lambda, gamma=gamma, mode=mode,
+                       scale_bits=S, policy=grow_policy)
+        tf, tt, tv, tl, tr, nc, sg = t
+        post_prune(tf, tl, tr, sg, gamma, nc)
+        if record is not None:
+            record.append(dict(g=g, h=h, sample=sidx, feat=fidx, S=S))
+        leaf = leaf_ids(X_bin, tf, tt, tl, tr)
+        F = F + learning_rate * tv[leaf]
+        losses.append(np.mean((y - F) ** 2) if loss == "mse" else np.mean(np.abs(y - F)))
+        trees.append((tf, tt, tv, tl, tr, nc, sg))
+    return dict(trees=trees, init_score=init, F=F, train_loss=np.array(losses))
+
+
 def engine_scale_bits(n_rows, w2, word_bits=126):
     """Fixed-point exponent S the CUDA engine uses for a round.
 

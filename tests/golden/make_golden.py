@@ -100,14 +100,66 @@ def multiclass_case(E, D):
     return {"fit_mc": (K, T)}
 
 
+def regression_case(E, D, loss):
+    """A reference regression fit (E:2607-2705) with its own Regressor class:
+    trees, predictions, train losses, the first rounds' gradients and samples."""
+    X, y = D.regression()
+    Xtr, ytr, Xte = X[:6_400], y[:6_400], X[6_400:]
+    params = dict(n_estimators=10, max_depth=5, learning_rate=0.1, n_bins=64, random_state=0, loss=loss)
+    captured = []
+    cls = E.HybridHistGBMNumbaV1_0_1
+    orig = cls._build_one_tree
+
+    def spy(self, X_bin, grad, hess, sample_idx, feat_idx, n_features):
+        captured.append((grad.copy(), hess.copy(), sample_idx.copy(), feat_idx.copy()))
+        return orig(self, X_bin, grad, hess, sample_idx, feat_idx, n_features)
+
+    cls._build_one_tree = spy
+    try:
+        m = E.HybridHistGBMRegressorV1_0_1(verbose=False, **params)
+        m.fit(Xtr, ytr)
+    finally:
+        cls._build_one_tree = orig
+    T = len(m.trees)
+    maxn = max(len(t[0]) for t in m.trees)
+    arr = {k: np.full((T, maxn), fill, dtype=dt) for k, fill, dt in [
+        ("tf", -1, np.int32), ("tt", 0, np.int64), ("tv", 0.0, np.float64),
+        ("tl", -1, np.int32), ("tr", -1, np.int32), ("sg", 0.0, np.float64)]}
+    ncs = np.zeros(T, dtype=np.int32)
+    for t, (tf, tt, tv, tl, tr, nc, sg) in enumerate(m.trees):
+        for key, a in zip(("tf", "tt", "tv", "tl", "tr", "sg"), (tf, tt, tv, tl, tr, sg)):
+            arr[key][t, :len(a)] = a
+        ncs[t] = nc
+    extra = {}
+    for r_ in range(min(3, T)):
+        g, h, s, f = captured[r_]
+        extra[f"r{r_}_g"], extra[f"r{r_}_h"], extra[f"r{r_}_sample"], extra[f"r{r_}_feat"] = g, h, s, f
+    Xb, _ = m._bin_features(Xtr)
+    np.savez_compressed(
+        os.path.join(HERE, f"fit_reg_{loss}.npz"), params=np.array(repr(params)), n_trees=T, nc=ncs, **arr,
+        **extra, init_score=m.init_score_, learning_rate=m.learning_rate, max_leaves=m.max_leaves,
+        max_depth=m.max_depth, min_child_weight=m.min_child_weight, subsample=m.subsample,
+        colsample=m.colsample_bytree, reg_lambda=m.reg_lambda, gamma=m.gamma,
+        min_samples_leaf=m.min_samples_leaf, n_bins=m.n_bins, edges=m.bin_edges, counts=m.feature_bin_counts,
+        nan_bin_id=m._nan_bin_id, X_bin_sha=sha(Xb.astype(np.uint16)), train_loss=np.array(m.train_loss_history_),
+        pred_test=m.predict(Xte), sample_sha=np.array([sha(c[2]) for c in captured]))
+    return {f"fit_reg_{loss}": (T,)}
+
+
 def main(ref_src, only=None):
     sys.path.insert(0, ref_src)
     import bsscl_gbm.estimator_v1_0_1 as E
     from bsscl_gbm_b200 import datasets as D
 
     out = {}
-    if only in ("model", "multiclass"):
-        out.update(model_json_case(E, D) if only == "model" else multiclass_case(E, D))
+    if only in ("model", "multiclass", "regression"):
+        if only == "model":
+            out.update(model_json_case(E, D))
+        elif only == "multiclass":
+            out.update(multiclass_case(E, D))
+        else:
+            out.update(regression_case(E, D, "mse"))
+            out.update(regression_case(E, D, "mae"))
         for k, v in out.items():
             print(k, v)
         return
@@ -343,6 +395,8 @@ def main(ref_src, only=None):
                   class_weight="balanced", random_state=3, grow_policy="level"))
     out.update(model_json_case(E, D))
     out.update(multiclass_case(E, D))
+    out.update(regression_case(E, D, "mse"))
+    out.update(regression_case(E, D, "mae"))
 
     for k, v in out.items():
         print(k, v)
@@ -351,5 +405,5 @@ def main(ref_src, only=None):
 if __name__ == "__main__":
     # python make_golden.py <reference>/src [model]   ('model': only the save_model fixture)
     if len(sys.argv) < 2:
-        sys.exit("usage: make_golden.py <reference>/src [model|multiclass]")
+        sys.exit("usage: make_golden.py <reference>/src [model|multiclass|regression]")
     main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else None)

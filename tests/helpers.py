@@ -25,6 +25,9 @@ def fit_inputs(name):
     if name == "cfg3_small":
         X, y = D.config3(n=25_000)
         return X[:20_000], y[:20_000], X[20_000:]
+    if name == "reg":
+        X, y = D.regression()
+        return X[:6_400], y[:6_400], X[6_400:]
     if name == "mc":
         X, y = D.multiclass()
         return X[:6_400], y[:6_400], X[6_400:]
@@ -64,6 +67,14 @@ def golden_mc_trees(d):
     K, T = int(d["n_classes"]), int(d["n_trees"])
     return [[(d["tf"][k, t], d["tt"][k, t], d["tv"][k, t], d["tl"][k, t], d["tr"][k, t], int(d["nc"][k, t]),
               d["sg"][k, t]) for t in range(T)] for k in range(K)]
+
+
+def reg_fit_kwargs(d):
+    return dict(n_estimators=int(d["n_trees"]), learning_rate=float(d["learning_rate"]),
+                max_leaves=int(d["max_leaves"]), max_depth=int(d["max_depth"]),
+                min_samples_leaf=int(d["min_samples_leaf"]), min_child_weight=float(d["min_child_weight"]),
+                reg_lambda=float(d["reg_lambda"]), gamma=float(d["gamma"]), subsample=float(d["subsample"]),
+                colsample=float(d["colsample"]), random_state=0)
 
 
 def mc_fit_kwargs(d):

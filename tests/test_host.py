@@ -213,7 +213,7 @@ def test_estimator_argument_errors():
     with pytest.raises(ValueError):
         M(device="cpu")
     with pytest.raises(NotImplementedError):
-        M(objective="regression", verbose=False).fit(X, y)
+        M(objective="regression", loss="huber", verbose=False).fit(X, y)
     with pytest.raises(NotImplementedError):
         M(sampling_method="goss", verbose=False).fit(X, y)
     with pytest.raises(NotImplementedError):

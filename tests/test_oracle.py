@@ -167,3 +167,26 @@ def test_ref_multiclass_fit_bit_exact():
             assert np.array_equal(rec[t]["g"][k], d[f"r{t}_k{k}_g"]), (t, k)
             assert np.array_equal(rec[t]["h"][k], d[f"r{t}_k{k}_h"]), (t, k)
     assert np.abs(r["train_loss"] - d["train_loss"]).max() < 1e-12
+
+
+@pytest.mark.parametrize("loss", ["mse", "mae"])
+def test_ref_regression_fit_bit_exact(loss):
+    """The oracle's regression loop (REF builder) == the reference's _fit_regression."""
+    import hashlib
+    from helpers import golden_trees, reg_fit_kwargs
+    d = golden(f"fit_reg_{loss}")
+    X, y, _ = fit_inputs("reg")
+    Xb = O.bin_matrix(X, d["edges"], d["counts"], d["nan_bin_id"], False)
+    assert hashlib.sha256(Xb.astype(np.uint16).tobytes()).hexdigest() == str(d["X_bin_sha"])
+    rec = []
+    r = O.fit_regression(Xb, y, d["counts"], loss=loss, mode=O.MODE_REF, record=rec, **reg_fit_kwargs(d))
+    assert r["init_score"] == float(d["init_score"])
+    for t, (a, b) in enumerate(zip(r["trees"], golden_trees(d))):
+        assert same_topology(a, b), f"tree {t}"
+        nc = a[5]
+        assert np.abs(a[2][:nc] - b[2][:nc]).max() < 1e-9 * max(1.0, np.abs(b[2][:nc]).max()), f"values {t}"
+    for t, rr in enumerate(rec):
+        assert hashlib.sha256(rr["sample"].tobytes()).hexdigest() == str(d["sample_sha"][t])
+    for t in range(3):
+        assert np.array_equal(rec[t]["g"], d[f"r{t}_g"])
+    assert np.abs(r["train_loss"] - d["train_loss"]).max() <= 1e-9 * np.abs(d["train_loss"]).max()
