@@ -108,7 +108,7 @@ struct gbm_ctx {
     PartTask *d_ptask = nullptr;
     int32_t *d_tile_cnt = nullptr;
     int tile_cap = 0;
-    long long *d_nleft = nullptr, *d_nleft_g = nullptr, *d_count64 = nullptr;
+    long long *d_nleft = nullptr, *d_count64 = nullptr;   // d_count64: one word for small all-reduces
     long long *d_leafw = nullptr;      // last level: per-parent count and (G, H) words
     DNode *d_nodes = nullptr;
     int *d_lvl[2] = {nullptr, nullptr};
@@ -217,7 +217,9 @@ struct gbm_ctx {
 
 namespace {
 
-enum { I_ONE = 0, I_NODES = 1, I_TILES = 2, I_LVL0 = 3, I_LVL1 = 4, I_COUNT = 8 };
+// d_ints: I_DONE / I_DONE_UPD count finished CTAs of k_part_scatter / k_update
+// (the last one runs the tail and resets it)
+enum { I_ONE = 0, I_NODES = 1, I_TILES = 2, I_LVL0 = 3, I_LVL1 = 4, I_DONE = 5, I_DONE_UPD = 6, I_COUNT = 8 };
 
 int fail(gbm_ctx *c, int code, const char *fmt, ...) {
     char buf[512];
@@ -723,7 +725,6 @@ int ensure_round_buffers(gbm_ctx *ctx, int nf, const gbm_params *P) {
         TRY(dalloc(ctx, &ctx->d_hprefix, (size_t)ctx->stage_slots + 1));
         TRY(dalloc(ctx, &ctx->d_ptask, (size_t)ctx->stage_slots));
         TRY(dalloc(ctx, &ctx->d_nleft, (size_t)ctx->stage_slots));
-        TRY(dalloc(ctx, &ctx->d_nleft_g, (size_t)ctx->stage_slots));
         TRY(dalloc(ctx, &ctx->d_leafw, (size_t)ctx->stage_slots * kLeafWords));
         int smem = (int)(sizeof(RNode) * (size_t)ctx->nmax);
         ctx->replay_smem = 0;
@@ -915,11 +916,11 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
     }
     TRY(launch(ctx, k_part_count, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_ptask,
                                                          lvl_cnt, ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt));
-    TRY(launch(ctx, k_part_scatter, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, ctx->d_rows, ctx->d_tmp, ctx->d_ptask, lvl_cnt,
-                                                           ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt,
-                                                           ctx->d_nleft));
     const long long *gl = ctx->comm ? nullptr : ctx->d_nleft;   // several ranks: the locally smaller child
-    TRY(launch(ctx, k_plan_hist, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, lvl, lvl_cnt, ctx->d_nleft, gl, ctx->d_htask, ctx->d_hprefix));
+    TRY(launch(ctx, k_part_scatter, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, (const int32_t *)ctx->d_rows,
+               ctx->d_tmp, (const PartTask *)ctx->d_ptask, (const int *)lvl_cnt, (const int *)ints(ctx, I_TILES),
+               (const unsigned *)ctx->d_side, (const int32_t *)ctx->d_tile_cnt, ctx->d_nleft, ctx->d_nodes,
+               (const int *)lvl, gl, ctx->d_htask, ctx->d_hprefix, (unsigned *)ints(ctx, I_DONE)));
     TRY(launch_hist(ctx, rf, lvl_cnt));
     if (ctx->comm) {
         const int cx = std::max(1, (2 * ctx->hist_grid + W_ub - 1) / W_ub);
@@ -1341,8 +1342,8 @@ int enqueue_update(gbm_ctx *ctx, const gbm_params *P, bool want_leaf, double *h_
     double scale = std::ldexp(1.0, ctx->S);
     TRY(launch(ctx, k_update, dim3(ctx->upd_blocks), dim3(kUpdThreads), 0, ctx->st, 
         ctx->d_tree, ctx->d_xb, ctx->n, ctx->d_y, ctx->w[0], ctx->w[1], P->learning_rate, scale, ctx->d_F,
-        ctx->d_q, want_leaf ? ctx->d_leaf : nullptr, ctx->d_loss_part));
-    TRY(launch(ctx, k_sum_partials, dim3(1), dim3(256), 0, ctx->st, ctx->d_loss_part, ctx->upd_blocks, ctx->d_loss));
+        ctx->d_q, want_leaf ? ctx->d_leaf : nullptr, ctx->d_loss_part, (unsigned *)ints(ctx, I_DONE_UPD),
+        ctx->d_loss));
     if (ctx->comm) TRY(allreduce_f64(ctx, ctx->d_loss, 1));
     CK(cudaMemcpyAsync(h_loss, ctx->d_loss, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
     return GBM_OK;
@@ -1675,7 +1676,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     void *dev_ptrs[] = {ctx->d_xb, ctx->d_counts, ctx->d_skipb, ctx->d_y, ctx->d_F, ctx->d_q, ctx->d_mask,
                         ctx->d_rows, ctx->d_tmp, ctx->d_cnt, ctx->d_off, ctx->d_total, ctx->d_blist, ctx->d_fidx,
                         ctx->d_fpos, ctx->d_pool, ctx->d_lpool, ctx->d_stage, ctx->d_fbest, ctx->d_htask, ctx->d_hprefix,
-                        ctx->d_ptask, ctx->d_tile_cnt, ctx->d_nleft, ctx->d_nleft_g,
+                        ctx->d_ptask, ctx->d_tile_cnt, ctx->d_nleft,
                         ctx->d_count64, ctx->d_nodes, ctx->d_lvl[0], ctx->d_lvl[1], ctx->d_ints, ctx->d_tree,
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
                         ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,

@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kUpdThreads)
 k_update(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64_t n,
          const uint8_t *__restrict__ y, double w0, double w1, double lr, double scale,
          double *__restrict__ F, longlong2 *__restrict__ q, int32_t *__restrict__ leaf_out,
-         double *__restrict__ loss_part) {
+         double *__restrict__ loss_part, unsigned *__restrict__ done, double *__restrict__ loss_out) {
     griddep_wait();
     __shared__ int s_feat[256], s_thr[256], s_left[256], s_right[256];
     __shared__ double s_val[256];
@@ -141,6 +141,26 @@ k_update(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64
         double s = 0.0;
         for (int w = 0; w < kUpdThreads / 32; w++) s += s_red[w];
         loss_part[blockIdx.x] = s;
+    }
+    // the last block sums the partials (k_sum_partials' fixed order: thread t
+    // takes blocks t, t+256, ..., then thread 0 adds the 256 sums in order)
+    __shared__ int s_last;
+    __shared__ double s_sum[kUpdThreads];
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    double a = 0.0;
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) a += __ldcg(loss_part + b);
+    s_sum[threadIdx.x] = a;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        *done = 0;
+        double t = 0.0;
+        for (int k = 0; k < (int)blockDim.x; k++) t += s_sum[k];
+        *loss_out = t;
     }
 }
 
@@ -482,10 +502,6 @@ __global__ void k_iota(int32_t *__restrict__ a, int64_t n) {
     if (i < n) a[i] = (int32_t)i;
 }
 
-__global__ void k_count64(const int32_t *__restrict__ in, long long *__restrict__ out) {
-    griddep_wait();
-    if (threadIdx.x == 0 && blockIdx.x == 0) *out = *in;
-}
 
 // ===========================================================================
 // histograms
@@ -824,15 +840,62 @@ k_part_count(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restric
 // CTA first sums its task's tile counts (the lefts before it, and n_left,
 // which the task's first tile stores); each warp then ranks a run of 256
 // consecutive rows (8 words).
-__global__ void __launch_bounds__(kPartThreads)
-k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks,
-               const int *__restrict__ ntask_p, const int *__restrict__ tiles_total,
-               const unsigned *__restrict__ side, const int32_t *__restrict__ tile_cnt,
-               long long *__restrict__ n_left) {
-    griddep_wait();
+// Level plan after the partition: each parent's smaller child (by global
+// count) becomes a histogram task; the children get their row ranges.
+// gl == null (several ranks): each rank histograms its locally smaller child;
+// k_stage_left turns that into the left child's partial before the all-reduce
+// and k_fill_counts sets the children's global counts after it.
+// One CTA (the last of k_part_scatter to finish) runs it.
+__device__ void plan_hist_block(DNode *__restrict__ nodes, const int *__restrict__ lvl, int W,
+                                const long long *__restrict__ nl_local, const long long *__restrict__ gl,
+                                HistTask *__restrict__ ht, int32_t *__restrict__ prefix, int *s_w) {
+    int carry = 0;
+    for (int b0 = 0; b0 < W; b0 += blockDim.x) {
+        int k = b0 + threadIdx.x;
+        int ch = 0;
+        if (k < W) {
+            int i = lvl[k];
+            DNode &p = nodes[i];
+            long long nl = nl_local[k];
+            long long gnl = gl ? gl[k] : nl, gtot = gl ? p.n : p.end - p.begin;
+            bool ls = gnl <= gtot - gnl;
+            HistTask t;
+            t.begin = ls ? p.begin : p.begin + nl;
+            t.end = ls ? p.begin + nl : p.end;
+            t.stage = k;
+            t.left_small = ls ? 1 : 0;
+            t.buf = (p.depth + 1) & 1;
+            t.pad = 0;
+            ht[k] = t;
+            ch = (int)(t.end - t.begin);
+            p.nl = nl;
+            p.gnl = gnl;
+            p.left_small = t.left_small;
+            DNode &a = nodes[p.kid0];
+            DNode &c = nodes[p.kid1];
+            a.begin = p.begin;
+            a.end = p.begin + nl;
+            a.n = gnl;
+            c.begin = p.begin + nl;
+            c.end = p.end;
+            c.n = gtot - gnl;
+        }
+        int tot;
+        int e = block_excl_scan(ch, s_w, tot);
+        if (k < W) prefix[k] = carry + e;
+        carry += tot;
+    }
+    if (threadIdx.x == 0) prefix[W] = carry;
+}
+
+// One partition tile's scatter (k_part_scatter).
+__device__ __forceinline__ void part_scatter_tile(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1,
+                                                  const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
+                                                  const unsigned *__restrict__ side,
+                                                  const int32_t *__restrict__ tile_cnt,
+                                                  long long *__restrict__ n_left) {
     __shared__ int s_l[kPartThreads / 32], s_a[kPartThreads / 32], s_b[kPartThreads / 32];
     const int tile = blockIdx.x;
-    if (tile >= *tiles_total) return;
     const int t = find_task_by_tile(tasks, *ntask_p, tile);
     const PartTask tk = tasks[t];
     const int32_t *__restrict__ src = tk.src ? rows1 : rows0;
@@ -889,56 +952,30 @@ k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, c
     }
 }
 
-// Level plan after the partition: each parent's smaller child (by global
-// count) becomes a histogram task; the children get their row ranges.
-// gl == null (several ranks): each rank histograms its locally smaller child;
-// k_stage_left turns that into the left child's partial before the all-reduce
-// and k_fill_counts sets the children's global counts after it.
-__global__ void k_plan_hist(DNode *__restrict__ nodes, const int *__restrict__ lvl,
-                            const int *__restrict__ lvl_count, const long long *__restrict__ nl_local,
-                            const long long *__restrict__ gl, HistTask *__restrict__ ht,
-                            int32_t *__restrict__ prefix) {
+__global__ void __launch_bounds__(kPartThreads)
+k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks,
+               const int *__restrict__ ntask_p, const int *__restrict__ tiles_total,
+               const unsigned *__restrict__ side, const int32_t *__restrict__ tile_cnt,
+               long long *__restrict__ n_left, DNode *__restrict__ nodes, const int *__restrict__ lvl,
+               const long long *__restrict__ gl, HistTask *__restrict__ ht, int32_t *__restrict__ prefix,
+               unsigned *__restrict__ done) {
     griddep_wait();
+    if (blockIdx.x < *tiles_total) part_scatter_tile(rows0, rows1, tasks, ntask_p, side, tile_cnt, n_left);
+    // the last CTA to finish plans the children's histograms (k_plan_hist's work)
+    __shared__ int s_last;
     __shared__ int s_w[32];
-    const int W = *lvl_count;
-    int carry = 0;
-    for (int b0 = 0; b0 < W; b0 += blockDim.x) {
-        int k = b0 + threadIdx.x;
-        int ch = 0;
-        if (k < W) {
-            int i = lvl[k];
-            DNode &p = nodes[i];
-            long long nl = nl_local[k];
-            long long gnl = gl ? gl[k] : nl, gtot = gl ? p.n : p.end - p.begin;
-            bool ls = gnl <= gtot - gnl;
-            HistTask t;
-            t.begin = ls ? p.begin : p.begin + nl;
-            t.end = ls ? p.begin + nl : p.end;
-            t.stage = k;
-            t.left_small = ls ? 1 : 0;
-            t.buf = (p.depth + 1) & 1;
-            t.pad = 0;
-            ht[k] = t;
-            ch = (int)(t.end - t.begin);
-            p.nl = nl;
-            p.gnl = gnl;
-            p.left_small = t.left_small;
-            DNode &a = nodes[p.kid0];
-            DNode &c = nodes[p.kid1];
-            a.begin = p.begin;
-            a.end = p.begin + nl;
-            a.n = gnl;
-            c.begin = p.begin + nl;
-            c.end = p.end;
-            c.n = gtot - gnl;
-        }
-        int tot;
-        int e = block_excl_scan(ch, s_w, tot);
-        if (k < W) prefix[k] = carry + e;
-        carry += tot;
-    }
-    if (threadIdx.x == 0) prefix[W] = carry;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) *done = 0;
+    plan_hist_block(nodes, lvl, *ntask_p, n_left, gl, ht, prefix, s_w);
 }
+
+
+
 
 // ---------------------------------------------------------------------------
 // several ranks: the staging exchange
