@@ -1111,16 +1111,33 @@ __global__ void __launch_bounds__(256) k_peer_sum(const long long *const *__rest
     const int64_t pr = (int64_t)(level & 1ull) * par_stride, po = (int64_t)((level & 1ull) ^ 1ull) * par_stride;
     const int64_t n2 = (int64_t)W * words / 2;   // longlong2 per level (slot words are even)
     const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, dt = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = t0; i < n2; i += dt) {
-        long long x = 0, y = 0;
+    // four elements per thread and pass, their loads from every rank in flight together
+    constexpr int U = 4;
+    for (int64_t base = t0; base < n2; base += (int64_t)U * dt) {
+        long long x[U], y[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) x[u] = y[u] = 0;
         if (s_ok) {
             for (int r = 0; r < nranks; r++) {
-                const longlong2 v = __ldcv(reinterpret_cast<const longlong2 *>(peers[r] + pr) + i);
-                x += v.x;
-                y += v.y;
+                const longlong2 *src = reinterpret_cast<const longlong2 *>(peers[r] + pr);
+                longlong2 v[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int64_t i = base + (int64_t)u * dt;
+                    v[u] = i < n2 ? __ldcg(src + i) : make_longlong2(0, 0);   // L2 only: no stale L1 lines
+                }
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    x[u] += v[u].x;
+                    y[u] += v[u].y;
+                }
             }
         }
-        reinterpret_cast<longlong2 *>(out)[i] = make_longlong2(x, y);   // zeros after a failed wait
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t i = base + (int64_t)u * dt;
+            if (i < n2) reinterpret_cast<longlong2 *>(out)[i] = make_longlong2(x[u], y[u]);   // zeros after a failed wait
+        }
     }
     const int64_t z2 = (int64_t)sync[nranks + kSyncPrevW] * words / 2;
     for (int64_t i = t0; i < z2; i += dt) reinterpret_cast<longlong2 *>(own + po)[i] = make_longlong2(0, 0);
