@@ -539,8 +539,9 @@ def run_engine(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=3)
+    # 200 rounds (~0.2 s on one B200): the steady state of the pipelined rounds
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
     ap.add_argument("--config", default="4", choices=sorted(CONFIGS),
                     help="4 (default): the headline, 1M x 100 depth 6; 5: 10M x 200 depth 10")
