@@ -95,8 +95,10 @@ struct gbm_ctx {
     int p2p_rank = 0, p2p_n = 1;
     long long *d_pst = nullptr;        // two parity buffers of stage_slots slots (IPC-exported)
     int64_t pst_stride = 0;            // words per parity buffer
-    unsigned long long *d_sync = nullptr;   // [N) signals from each rank, then kSyncLocal local words (IPC-exported)
+    unsigned long long *d_sync = nullptr;   // signals from each rank and local words (IPC-exported)
+    long long *d_red = nullptr;        // two-shot exchange: this rank's summed share of a level (IPC-exported)
     long long **d_peer_pst = nullptr;       // every rank's d_pst (own at [rank]), device table
+    long long **d_peer_red = nullptr;       // every rank's d_red
     unsigned long long **d_peer_sync = nullptr;
     std::vector<void *> ipc_opened;    // peer mappings to close
     long long *d_stage = nullptr;      // smaller-child histograms of one level
@@ -589,12 +591,14 @@ int p2p_teardown(gbm_ctx *ctx, bool collective) {
         TRY(allreduce_i64(ctx, ctx->d_count64, 1));
         TRY(sync_stream(ctx));
     }
-    void *ptrs[] = {ctx->d_pst, ctx->d_sync, ctx->d_peer_pst, ctx->d_peer_sync};
+    void *ptrs[] = {ctx->d_pst, ctx->d_sync, ctx->d_red, ctx->d_peer_pst, ctx->d_peer_sync, ctx->d_peer_red};
     for (void *q : ptrs) if (q) cudaFree(q);
     ctx->d_pst = nullptr;
     ctx->d_sync = nullptr;
+    ctx->d_red = nullptr;
     ctx->d_peer_pst = nullptr;
     ctx->d_peer_sync = nullptr;
+    ctx->d_peer_red = nullptr;
     ctx->pst_stride = 0;
     ctx->p2p = false;
     ctx->mem_gen++;
@@ -611,26 +615,30 @@ int p2p_setup(gbm_ctx *ctx, int64_t stride) {
     TRY(p2p_teardown(ctx, true));
     const char *env = std::getenv("GBM_PEER_EXCHANGE");
     const int N = gbm_comm_size(ctx->comm), rank = gbm_comm_rank(ctx->comm);
-    // default: on for 2 ranks (the configuration its parity tests run on);
-    // GBM_PEER_EXCHANGE=1 turns it on for any count, 0 off
-    if (env ? env[0] == '0' : N != 2) return GBM_OK;
+    // default on; GBM_PEER_EXCHANGE=0 keeps the NCCL all-reduce
+    if (env && env[0] == '0') return GBM_OK;
     ctx->p2p_n = N;
     ctx->p2p_rank = rank;
     int ok = 1;
+    const size_t sync_words = (size_t)(2 * N + kSyncLocal);
     if (cudaMalloc(&ctx->d_pst, sizeof(long long) * (size_t)(2 * stride)) != cudaSuccess ||
-        cudaMalloc(&ctx->d_sync, sizeof(unsigned long long) * (size_t)(N + kSyncLocal)) != cudaSuccess ||
+        cudaMalloc(&ctx->d_red, sizeof(long long) * (size_t)stride) != cudaSuccess ||
+        cudaMalloc(&ctx->d_sync, sizeof(unsigned long long) * sync_words) != cudaSuccess ||
         cudaMalloc(&ctx->d_peer_pst, sizeof(long long *) * (size_t)N) != cudaSuccess ||
+        cudaMalloc(&ctx->d_peer_red, sizeof(long long *) * (size_t)N) != cudaSuccess ||
         cudaMalloc(&ctx->d_peer_sync, sizeof(unsigned long long *) * (size_t)N) != cudaSuccess)
         return fail(ctx, GBM_ERR_ALLOC, "peer exchange buffers");
     ctx->mem_gen++;
     CK(cudaMemsetAsync(ctx->d_pst, 0, sizeof(long long) * (size_t)(2 * stride), ctx->st));
-    CK(cudaMemsetAsync(ctx->d_sync, 0, sizeof(unsigned long long) * (size_t)(N + kSyncLocal), ctx->st));
-    // the handle table: per rank 2 handles of 64 bytes = 16 int64 words
-    constexpr int kHW = (int)(2 * sizeof(cudaIpcMemHandle_t) / 8);
-    static_assert(2 * sizeof(cudaIpcMemHandle_t) == 8 * kHW, "handle size");
+    CK(cudaMemsetAsync(ctx->d_sync, 0, sizeof(unsigned long long) * sync_words, ctx->st));
+    // the handle table: per rank 3 handles of 64 bytes = 24 int64 words
+    constexpr int kNH = 3;
+    constexpr int kHW = (int)(kNH * sizeof(cudaIpcMemHandle_t) / 8);
+    static_assert(kNH * sizeof(cudaIpcMemHandle_t) == 8 * kHW, "handle size");
     std::vector<long long> tab((size_t)N * kHW + 1, 0);
-    cudaIpcMemHandle_t h[2];
-    if (cudaIpcGetMemHandle(&h[0], ctx->d_pst) != cudaSuccess || cudaIpcGetMemHandle(&h[1], ctx->d_sync) != cudaSuccess) {
+    cudaIpcMemHandle_t h[kNH];
+    if (cudaIpcGetMemHandle(&h[0], ctx->d_pst) != cudaSuccess || cudaIpcGetMemHandle(&h[1], ctx->d_sync) != cudaSuccess ||
+        cudaIpcGetMemHandle(&h[2], ctx->d_red) != cudaSuccess) {
         cudaGetLastError();
         ok = 0;
     } else {
@@ -645,30 +653,28 @@ int p2p_setup(gbm_ctx *ctx, int64_t stride) {
                                            ctx->st) == cudaSuccess ? sync_stream(ctx) : GBM_ERR_CUDA;
     dfree(ctx, d_tab);
     if (rc != GBM_OK) return rc;
-    std::vector<long long *> pst((size_t)N, nullptr);
+    std::vector<long long *> pst((size_t)N, nullptr), red((size_t)N, nullptr);
     std::vector<unsigned long long *> sy((size_t)N, nullptr);
     pst[(size_t)rank] = ctx->d_pst;
     sy[(size_t)rank] = ctx->d_sync;
+    red[(size_t)rank] = ctx->d_red;
     if (tab[(size_t)N * kHW] == 0) {
         for (int q = 0; q < N && ok; q++) {
             if (q == rank) continue;
-            cudaIpcMemHandle_t hq[2];
+            cudaIpcMemHandle_t hq[kNH];
             std::memcpy(hq, &tab[(size_t)q * kHW], sizeof hq);
-            void *a = nullptr, *b = nullptr;
-            if (cudaIpcOpenMemHandle(&a, hq[0], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-                cudaGetLastError();
-                ok = 0;
-                break;
+            void *m[kNH] = {};
+            for (int k = 0; k < kNH && ok; k++) {
+                if (cudaIpcOpenMemHandle(&m[k], hq[k], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                    cudaGetLastError();
+                    ok = 0;
+                    break;
+                }
+                ctx->ipc_opened.push_back(m[k]);
             }
-            ctx->ipc_opened.push_back(a);
-            if (cudaIpcOpenMemHandle(&b, hq[1], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-                cudaGetLastError();
-                ok = 0;
-                break;
-            }
-            ctx->ipc_opened.push_back(b);
-            pst[(size_t)q] = static_cast<long long *>(a);
-            sy[(size_t)q] = static_cast<unsigned long long *>(b);
+            pst[(size_t)q] = static_cast<long long *>(m[0]);
+            sy[(size_t)q] = static_cast<unsigned long long *>(m[1]);
+            red[(size_t)q] = static_cast<long long *>(m[2]);
         }
     }
     // every rank must map every peer, or nobody uses the exchange
@@ -685,6 +691,7 @@ int p2p_setup(gbm_ctx *ctx, int64_t stride) {
     CK(cudaMemcpyAsync(ctx->d_peer_pst, pst.data(), sizeof(long long *) * (size_t)N, cudaMemcpyHostToDevice, ctx->st));
     CK(cudaMemcpyAsync(ctx->d_peer_sync, sy.data(), sizeof(unsigned long long *) * (size_t)N, cudaMemcpyHostToDevice,
                        ctx->st));
+    CK(cudaMemcpyAsync(ctx->d_peer_red, red.data(), sizeof(long long *) * (size_t)N, cudaMemcpyHostToDevice, ctx->st));
     TRY(sync_stream(ctx));
     ctx->pst_stride = stride;
     ctx->p2p = true;
@@ -843,12 +850,24 @@ int exchange_stage(gbm_ctx *ctx, const int *lvl_cnt, int W_ub, int nf) {
         TRY(record_ev(ctx, e0, ctx->st));
     }
     const int64_t n2 = (int64_t)W_ub * words / 2;
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n2 + 255) / 256, 2 * ctx->hist_grid));
-    TRY(launch(ctx, k_peer_sum, dim3(grid), dim3(256), 0, ctx->st, (const long long *const *)ctx->d_peer_pst,
-               ctx->pst_stride, ctx->d_sync, ctx->p2p_rank, ctx->p2p_n, lvl_cnt, nf, ctx->d_stage, ctx->d_pst,
-               peer_wait_ns(ctx)));
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n2 + 1023) / 1024, 2 * ctx->hist_grid));
+    const int N = ctx->p2p_n;
+    if (N == 2) {   // one-shot: pull the whole level from the other rank
+        TRY(launch(ctx, k_peer_sum, dim3(grid), dim3(256), 0, ctx->st, (const long long *const *)ctx->d_peer_pst,
+                   ctx->pst_stride, ctx->d_sync, ctx->p2p_rank, N, lvl_cnt, nf, ctx->d_stage, ctx->d_pst,
+                   peer_wait_ns(ctx)));
+        ctx->comm_bytes += 8.0 * (double)(words * W_ub);
+    } else {        // two-shot: sum this rank's share from every rank, then gather the shares
+        const int g1 = std::max(1, grid / N);
+        TRY(launch(ctx, k_peer_reduce, dim3(g1), dim3(256), 0, ctx->st, (const long long *const *)ctx->d_peer_pst,
+                   ctx->pst_stride, ctx->d_sync, (unsigned long long *const *)ctx->d_peer_sync, ctx->p2p_rank, N,
+                   lvl_cnt, nf, ctx->d_red, peer_wait_ns(ctx)));
+        TRY(launch(ctx, k_peer_gather, dim3(grid), dim3(256), 0, ctx->st, (const long long *const *)ctx->d_peer_red,
+                   ctx->d_sync, ctx->p2p_rank, N, lvl_cnt, nf, ctx->d_stage, ctx->d_pst, ctx->pst_stride,
+                   peer_wait_ns(ctx)));
+        ctx->comm_bytes += 8.0 * (double)(words * W_ub) * 2.0 * (N - 1) / N;
+    }
     if (e1) TRY(record_ev(ctx, e1, ctx->st));
-    ctx->comm_bytes += 8.0 * (double)(words * W_ub) * (ctx->p2p_n - 1);
     return GBM_OK;
 }
 

@@ -993,10 +993,18 @@ k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, c
 // each rank (written by the peers), then kSyncSent (signals this rank sent),
 // kSyncCta (CTAs done, for the last-CTA signal), kSyncLevel (levels done),
 // kSyncErr (a wait ran out), kSyncPrevW (slots of the previous level),
-// kSyncWaitNs (time CTA 0 of k_peer_sum spent waiting for the peers).
+// kSyncWaitNs (time CTA 0 of the exchange kernels spent waiting for the
+// peers), kSyncSentRed / kSyncCta2 (the two-shot exchange's second signal);
+// then [N + kSyncLocal, 2N + kSyncLocal) the second signals received.
+//
+// With more than two ranks the sum is two-shot: k_peer_reduce sums only this
+// rank's 1/N of the level's words from every rank into its IPC-visible
+// result buffer and signals again; k_peer_gather waits for those signals and
+// copies every rank's summed share into d_stage.  Per rank 2 (N-1)/N of the
+// level crosses NVLink instead of (N-1) times it.
 // ---------------------------------------------------------------------------
 constexpr int kSyncSent = 0, kSyncCta = 1, kSyncLevel = 2, kSyncErr = 3, kSyncPrevW = 4, kSyncWaitNs = 5,
-              kSyncLocal = 8;
+              kSyncSentRed = 6, kSyncCta2 = 7, kSyncLocal = 8;
 
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
@@ -1073,6 +1081,29 @@ __global__ void k_stage_left(const DNode *__restrict__ nodes, const int *__restr
     }
 }
 
+// Thread 0: wait (bounded) until flag word `first + q` of every peer q is at
+// least `want`; a wait that runs out sets kSyncErr.  Returns 1 when all came.
+__device__ int wait_peers(unsigned long long *sync, int first, unsigned long long want, int rank, int nranks,
+                          long long timeout_ns) {
+    const unsigned long long t0 = global_ns();
+    int ok = sync[nranks + kSyncErr] == 0;   // after one failed wait the rank's exchange is broken
+    for (int q = 0; q < nranks && ok; q++) {
+        if (q == rank) continue;
+        volatile unsigned long long *f = sync + first + q;
+        while (*f < want) {
+            if (global_ns() - t0 > (unsigned long long)timeout_ns) {
+                ok = 0;
+                atomicExch(sync + nranks + kSyncErr, 1ull);
+                break;
+            }
+            __nanosleep(200);
+        }
+    }
+    __threadfence_system();
+    if (blockIdx.x == 0) sync[nranks + kSyncWaitNs] += global_ns() - t0;
+    return ok;
+}
+
 // Peer exchange: wait (bounded) until every peer has signalled this level,
 // then out[i] = sum over ranks r of rank r's slot word i, read from each
 // rank's parity buffer (peers over NVLink), for the level's slots; zero this
@@ -1085,26 +1116,7 @@ __global__ void __launch_bounds__(256) k_peer_sum(const long long *const *__rest
     griddep_wait();
     __shared__ int s_ok;
     const unsigned long long level = sync[nranks + kSyncLevel];
-    if (threadIdx.x == 0) {
-        const unsigned long long want = sync[nranks + kSyncSent];
-        const unsigned long long t0 = global_ns();
-        int ok = sync[nranks + kSyncErr] == 0;   // after one failed wait the rank's exchange is broken
-        for (int q = 0; q < nranks && ok; q++) {
-            if (q == rank) continue;
-            volatile unsigned long long *f = sync + q;
-            while (*f < want) {
-                if (global_ns() - t0 > (unsigned long long)timeout_ns) {
-                    ok = 0;
-                    atomicExch(sync + nranks + kSyncErr, 1ull);
-                    break;
-                }
-                __nanosleep(200);
-            }
-        }
-        __threadfence_system();
-        if (blockIdx.x == 0) sync[nranks + kSyncWaitNs] += global_ns() - t0;
-        s_ok = ok;
-    }
+    if (threadIdx.x == 0) s_ok = wait_peers(sync, 0, sync[nranks + kSyncSent], rank, nranks, timeout_ns);
     __syncthreads();
     const int64_t words = slot_words_for(nf);
     const int W = lvl_count ? *lvl_count : 1;
@@ -1139,6 +1151,110 @@ __global__ void __launch_bounds__(256) k_peer_sum(const long long *const *__rest
             if (i < n2) reinterpret_cast<longlong2 *>(out)[i] = make_longlong2(x[u], y[u]);   // zeros after a failed wait
         }
     }
+    const int64_t z2 = (int64_t)sync[nranks + kSyncPrevW] * words / 2;
+    for (int64_t i = t0; i < z2; i += dt) reinterpret_cast<longlong2 *>(own + po)[i] = make_longlong2(0, 0);
+}
+
+// Two-shot exchange, phase 1: after every peer's first signal, this rank's
+// share [rank c, (rank+1) c) of the level's longlong2 words (c = ceil(n2/N))
+// summed over all ranks into its result buffer; the last CTA to finish
+// signals every peer again.
+__global__ void __launch_bounds__(256) k_peer_reduce(const long long *const *__restrict__ peers, int64_t par_stride,
+                                                     unsigned long long *__restrict__ sync,
+                                                     unsigned long long *const *__restrict__ peer_sync, int rank,
+                                                     int nranks, const int *__restrict__ lvl_count, int nf,
+                                                     long long *__restrict__ red, long long timeout_ns) {
+    griddep_wait();
+    __shared__ int s_ok;
+    const unsigned long long level = sync[nranks + kSyncLevel];
+    if (threadIdx.x == 0) s_ok = wait_peers(sync, 0, sync[nranks + kSyncSent], rank, nranks, timeout_ns);
+    __syncthreads();
+    const int64_t words = slot_words_for(nf);
+    const int W = lvl_count ? *lvl_count : 1;
+    const int64_t pr = (int64_t)(level & 1ull) * par_stride;
+    const int64_t n2 = (int64_t)W * words / 2;
+    const int64_t cs = (n2 + nranks - 1) / nranks;
+    const int64_t lo = min(n2, (int64_t)rank * cs), hi = min(n2, lo + cs);
+    const int64_t dt = (int64_t)gridDim.x * blockDim.x;
+    constexpr int U = 4;
+    for (int64_t base = lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < hi; base += (int64_t)U * dt) {
+        long long x[U], y[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) x[u] = y[u] = 0;
+        if (s_ok) {
+            for (int r = 0; r < nranks; r++) {
+                const longlong2 *src = reinterpret_cast<const longlong2 *>(peers[r] + pr);
+                longlong2 v[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int64_t i = base + (int64_t)u * dt;
+                    v[u] = i < hi ? __ldcg(src + i) : make_longlong2(0, 0);
+                }
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    x[u] += v[u].x;
+                    y[u] += v[u].y;
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t i = base + (int64_t)u * dt;
+            if (i < hi) reinterpret_cast<longlong2 *>(red)[i] = make_longlong2(x[u], y[u]);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long *ctr = sync + nranks + kSyncCta2;
+        if (atomicAdd(ctr, 1ull) == (unsigned long long)gridDim.x - 1) {
+            *ctr = 0;
+            __threadfence_system();
+            const unsigned long long e = sync[nranks + kSyncSentRed] + 1;
+            sync[nranks + kSyncSentRed] = e;
+            for (int q = 0; q < nranks; q++)
+                if (q != rank)
+                    *reinterpret_cast<volatile unsigned long long *>(peer_sync[q] + nranks + kSyncLocal + rank) = e;
+            __threadfence_system();
+        }
+    }
+}
+
+// Two-shot exchange, phase 2: after every peer's second signal, every rank's
+// summed share from its result buffer into d_stage; zero this rank's other
+// parity buffer, as k_peer_sum does.
+__global__ void __launch_bounds__(256) k_peer_gather(const long long *const *__restrict__ reds,
+                                                     unsigned long long *__restrict__ sync, int rank, int nranks,
+                                                     const int *__restrict__ lvl_count, int nf,
+                                                     long long *__restrict__ out, long long *__restrict__ own,
+                                                     int64_t par_stride, long long timeout_ns) {
+    griddep_wait();
+    __shared__ int s_ok;
+    const unsigned long long level = sync[nranks + kSyncLevel];
+    if (threadIdx.x == 0)
+        s_ok = wait_peers(sync, nranks + kSyncLocal, sync[nranks + kSyncSentRed], rank, nranks, timeout_ns);
+    __syncthreads();
+    const int64_t words = slot_words_for(nf);
+    const int W = lvl_count ? *lvl_count : 1;
+    const int64_t n2 = (int64_t)W * words / 2;
+    const int64_t cs = (n2 + nranks - 1) / nranks;
+    const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, dt = (int64_t)gridDim.x * blockDim.x;
+    constexpr int U = 4;
+    for (int64_t base = t0; base < n2; base += (int64_t)U * dt) {
+        longlong2 v[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t i = base + (int64_t)u * dt;
+            v[u] = (i < n2 && s_ok) ? __ldcg(reinterpret_cast<const longlong2 *>(reds[(int)(i / cs)]) + i)
+                                    : make_longlong2(0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t i = base + (int64_t)u * dt;
+            if (i < n2) reinterpret_cast<longlong2 *>(out)[i] = v[u];   // zeros after a failed wait
+        }
+    }
+    const int64_t po = (int64_t)((level & 1ull) ^ 1ull) * par_stride;
     const int64_t z2 = (int64_t)sync[nranks + kSyncPrevW] * words / 2;
     for (int64_t i = t0; i < z2; i += dt) reinterpret_cast<longlong2 *>(own + po)[i] = make_longlong2(0, 0);
 }
