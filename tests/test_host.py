@@ -248,3 +248,24 @@ def test_get_set_params_roundtrip():
     assert m.learning_rate == 0.3
     with pytest.raises(ValueError):
         m.set_params(bogus=1)
+
+
+def test_c_abi_rejects_bad_arguments_without_a_device(built_lib):
+    """Argument checks of the binning, multi-class, regression and self-test
+    entry points run before any CUDA call: on a host without a GPU they
+    answer GBM_ERR_ARG (1) for null contexts and out-of-range values."""
+    import ctypes as C
+    from bsscl_gbm_b200 import _lib
+    L = _lib.lib()
+    GBM_ERR_ARG = 1
+    assert L.gbm_bin_edges(None, None, 0, 0, 0, 255, None, None, 0, None, None, None) == GBM_ERR_ARG
+    assert L.gbm_upload_binned_rows(None, 0, 1, None, 0, None, None) == GBM_ERR_ARG
+    assert L.gbm_bin_features(None, None, 1, 1, 0, None, 0, None, None, None) == GBM_ERR_ARG
+    assert L.gbm_predict_upload_raw(None, None, 1, 1, 0, None, 0, None, None) == GBM_ERR_ARG
+    assert L.gbm_upload_labels_mc(None, None, 3, None, 0) == GBM_ERR_ARG
+    assert L.gbm_round_mc(None, None, None, 1, None, None, None) == GBM_ERR_ARG
+    assert L.gbm_upload_targets(None, None, 0.0, 0, 0) == GBM_ERR_ARG
+    assert L.gbm_round_reg(None, None, None, 1, None, None, None) == GBM_ERR_ARG
+    assert L.gbm_get_grad_mc(None, 0, None, None) == GBM_ERR_ARG
+    assert L.gbm_test_peer_wait(0, 0) == GBM_ERR_ARG          # the limit must be 1..10000 ms
+    assert L.gbm_test_peer_wait(0, 20000) == GBM_ERR_ARG
