@@ -554,7 +554,18 @@ int enqueue_features(gbm_ctx *ctx, int si, int nf) {
 constexpr int kSpecDepth = 10;
 constexpr int kReplaySmemMax = 160 * 1024;   // node table copy of the replay kernels
 
-bool full_spec(const gbm_params *P) { return P->grow_policy == 1 || P->max_depth <= kSpecDepth; }
+// The deepest best-first tree grown with full speculation: kSpecDepth, or
+// lower with GBM_SPEC_DEPTH in the environment (0: every best-first tree
+// takes capped speculation and the host replay).
+int spec_depth() {
+    static const int d = [] {
+        const char *e = std::getenv("GBM_SPEC_DEPTH");
+        return e ? std::max(0, std::min(kSpecDepth, std::atoi(e))) : kSpecDepth;
+    }();
+    return d;
+}
+
+bool full_spec(const gbm_params *P) { return P->grow_policy == 1 || P->max_depth <= spec_depth(); }
 
 // Children below this depth keep their histogram in the pool (a future
 // parent's).  Under full speculation the nodes at depth D-1 are expanded by
