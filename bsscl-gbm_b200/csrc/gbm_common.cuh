@@ -18,6 +18,7 @@ constexpr int kChunk = 16384;       // max rows one CTA adds into one cell (R_ma
 constexpr int kHistThreads = 512;
 constexpr int kDig = 17;            // low/mid digit width of the shared-memory accumulators
 constexpr int kAccWords = 6 * kBlk * kBins;   // [g0 g1 g2 h0 h1 h2][16][256] uint32
+constexpr int kHistV2Weight = 6 + kBlk;   // k_hist2's cost of a row in any block
 constexpr int kPartTile = 4096;     // rows per partition CTA
 constexpr int kPartThreads = 512;   // 8 rows per thread, loads in flight together
 constexpr int kPartWords = kPartTile / 32;   // side bits of a tile

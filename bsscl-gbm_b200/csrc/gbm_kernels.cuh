@@ -673,6 +673,205 @@ k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ ro
     }
 }
 
+// The same histograms with every shared-memory atomic free of bank
+// conflicts.  Each lane still loads its own row (as in k_hist), but in step
+// k of the row's 16 features lane l adds feature f = (l + k) mod 16, so the
+// 16 lanes of a half-warp touch 16 different features.  Each half-warp h
+// keeps its own copy of every cell, and cell (digit d, bin b, half h,
+// feature f) is the shared word ((d * kBins + b) * 2 + h) * kBlk + f: its
+// bank is 16 h + f, the 32 lanes of an atomic instruction land in 32
+// different banks whatever their bins, and the instruction is one
+// wavefront (k_hist's lanes all add the same feature at random bins, ~3
+// wavefronts).  A row costs the same 16 steps whatever the number of
+// selected features of its block, so the launch's work is split with one
+// weight per block (kHistV2Weight) instead of k_hist's per-feature weights
+// (bwp).
+// The two copies are added at the flush.  Digits, skipped bins, totals and
+// the staging layout are those of k_hist.
+constexpr int kHistV2Threads = 1024;
+constexpr int kDigV2 = kBins * 2 * kBlk;            // words between two digits
+constexpr int kAccV2Words = 6 * kDigV2;            // 192 KB
+
+// v rotated by r bytes (0 <= r < 16): byte k of the result is byte
+// (k + r) mod 16 of v (bytes little-endian, word k / 4).
+__device__ __forceinline__ uint4 rot_bytes(uint4 v, int r) {
+    unsigned a = v.x, b = v.y, c = v.z, d = v.w;
+    if (r & 8) {
+        unsigned t0 = a, t1 = b;
+        a = c; b = d; c = t0; d = t1;
+    }
+    if (r & 4) {
+        unsigned t = a;
+        a = b; b = c; c = d; d = t;
+    }
+    const unsigned sh = (unsigned)(r & 3) * 8u;
+    return make_uint4(__funnelshift_r(a, b, sh), __funnelshift_r(b, c, sh), __funnelshift_r(c, d, sh),
+                      __funnelshift_r(d, a, sh));
+}
+
+__device__ __forceinline__ unsigned byte_of(const uint4 &v, int k) {
+    const unsigned w = (k >> 2) == 0 ? v.x : (k >> 2) == 1 ? v.y : (k >> 2) == 2 ? v.z : v.w;
+    return (w >> ((k & 3) * 8)) & 0xffu;
+}
+
+__global__ void __launch_bounds__(kHistV2Threads, 1)
+k_hist2(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
+        const int32_t *__restrict__ rows1, const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
+        const int *__restrict__ ntask_p, const int32_t *__restrict__ blist, const int32_t *__restrict__ nb_p,
+        const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
+        const longlong2 *__restrict__ q, long long *__restrict__ stage_hist,
+        const unsigned long long *__restrict__ par_word, int64_t par_stride) {
+    griddep_wait();
+    if (par_word) stage_hist += (int64_t)(*par_word & 1ull) * par_stride;   // peer exchange: this level's buffer
+    extern __shared__ unsigned acc[];   // [6][256][2][16]
+    __shared__ long long s_tot[2][kHistV2Threads / 32];
+    const int ntask = *ntask_p;
+    const int nb = *nb_p;
+    if (ntask <= 0 || nb <= 0) return;
+    const long long R = rpre[ntask];
+    const long long T = (long long)kHistV2Weight * nb * R;
+    if (T <= 0) return;
+    const long long G = gridDim.x;
+    const long long B0 = cost_bound(blockIdx.x, T, G), B1 = cost_bound(blockIdx.x + 1, T, G);
+    if (B0 >= B1) return;
+    const int lane = threadIdx.x & 31, half = lane >> 4, fl = lane & 15;
+    const int warp = threadIdx.x >> 5;
+    const int64_t slot_words = slot_words_for(nf);
+    int bi = 0;
+    while (bi + 1 < nb && (long long)kHistV2Weight * (bi + 1) * R <= B0) bi++;
+    for (; bi < nb; bi++) {
+        const long long base = (long long)kHistV2Weight * bi * R;
+        if (base >= B1) break;
+        const int w = kHistV2Weight;
+        const int k0 = (int)(B0 > base ? ceil_div_ll(B0 - base, w) : 0);
+        const int k1 = (int)min(R, ceil_div_ll(B1 - base, w));
+        if (k0 >= k1) continue;
+        const int blk = blist[bi];
+        unsigned mask = 0;
+#pragma unroll
+        for (int k = 0; k < kBlk; k++) mask |= (fpos[blk * kBlk + k] >= 0 ? 1u : 0u) << k;
+        uint4 skipv;   // the skipped bin of each feature, one byte each, rotated like the rows
+        {
+            unsigned sw[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+            for (int k = 0; k < kBlk; k++)
+                sw[k >> 2] |= ((mask >> k) & 1u ? (unsigned)skipb[blk * kBlk + k] & 0xffu : 0u) << ((k & 3) * 8);
+            skipv = rot_bytes(make_uint4(sw[0], sw[1], sw[2], sw[3]), fl);
+        }
+        const unsigned mrot = ((mask | (mask << kBlk)) >> fl) & 0xffffu;   // bit k: feature (fl + k) mod 16
+        const bool fsel = (mask >> fl) & 1u;
+        const int jflush = fsel ? fpos[blk * kBlk + fl] : 0;
+        const uint4 *xv = reinterpret_cast<const uint4 *>(xb) + (int64_t)blk * n;
+        int t;
+        {
+            int lo = 0, hi = ntask - 1;
+            while (lo < hi) {
+                int mid = (lo + hi + 1) >> 1;
+                if (rpre[mid] <= k0) lo = mid; else hi = mid - 1;
+            }
+            t = lo;
+        }
+        for (int k = k0; k < k1; t++) {
+            const int t0 = rpre[t], t1 = rpre[t + 1];
+            if (t1 <= k) continue;
+            const HistTask tk = tasks[t];
+            const int32_t *__restrict__ rows = tk.buf ? rows1 : rows0;
+            const int pe = min(k1, t1);
+            const bool single = k == t0 && pe == t1 && (t1 - t0) <= kChunk;
+            long long *dst = stage_hist + (int64_t)tk.stage * slot_words;
+            for (int c0 = k; c0 < pe; c0 += kChunk) {
+                const int c1 = min(pe, c0 + kChunk);
+                for (int i = threadIdx.x; i < kAccV2Words / 4; i += blockDim.x)
+                    reinterpret_cast<uint4 *>(acc)[i] = make_uint4(0u, 0u, 0u, 0u);
+                __syncthreads();
+                const int r0 = (int)tk.begin + (c0 - t0), r1 = (int)tk.begin + (c1 - t0);
+                long long tg = 0, th = 0;
+                unsigned *my = acc + half * kBlk;
+                for (int rb = r0 + (int)(threadIdx.x & ~31u); rb < r1; rb += blockDim.x) {
+                    const int r = rb + lane;
+                    const bool valid = r < r1;
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    longlong2 qq = make_longlong2(0, 0);
+                    if (valid) {
+                        const int row = rows[r];
+                        v = __ldg(xv + row);
+                        qq = __ldg(q + row);
+                    }
+                    tg += qq.x;
+                    th += qq.y;
+                    const unsigned dg0 = (unsigned)qq.x & 0x1ffffu, dg1 = (unsigned)(qq.x >> kDig) & 0x1ffffu,
+                                   dg2 = (unsigned)(int)(qq.x >> (2 * kDig));
+                    const unsigned dh0 = (unsigned)qq.y & 0x1ffffu, dh1 = (unsigned)(qq.y >> kDig) & 0x1ffffu,
+                                   dh2 = (unsigned)(int)(qq.y >> (2 * kDig));
+                    const uint4 vr = rot_bytes(v, fl);
+                    const unsigned live = valid ? mrot : 0u;
+#pragma unroll
+                    for (int k = 0; k < kBlk; k++) {
+                        const unsigned b = byte_of(vr, k);
+                        if (((live >> k) & 1u) && b != byte_of(skipv, k)) {
+                            unsigned *cc = my + b * (2 * kBlk) + ((fl + k) & (kBlk - 1));
+                            atomicAdd(cc + 0 * kDigV2, dg0);
+                            atomicAdd(cc + 1 * kDigV2, dg1);
+                            atomicAdd(cc + 2 * kDigV2, dg2);
+                            atomicAdd(cc + 3 * kDigV2, dh0);
+                            atomicAdd(cc + 4 * kDigV2, dh1);
+                            atomicAdd(cc + 5 * kDigV2, dh2);
+                        }
+                    }
+                }
+                if (bi == 0) {
+                    tg = warp_sum(tg);
+                    th = warp_sum(th);
+                    if (lane == 0) {
+                        s_tot[0][warp] = tg;
+                        s_tot[1][warp] = th;
+                    }
+                }
+                __syncthreads();
+                if (bi == 0 && threadIdx.x < 2) {
+                    long long tot = 0;
+                    for (int w2 = 0; w2 < kHistV2Threads / 32; w2++) tot += s_tot[threadIdx.x][w2];
+                    long long *o = dst + (int64_t)nf * kBins * kWords + 2 * threadIdx.x;
+                    if (single) {
+                        o[0] = tot >> 32;
+                        o[1] = tot & 0xffffffffll;
+                    } else if (tot) {
+                        atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(tot >> 32));
+                        atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(tot & 0xffffffffll));
+                    }
+                }
+                // flush: warp w takes bins w, w + 32, ...; lane (half, fl) reads
+                // its copy of cell (bin, fl) (32 lanes, 32 banks), the two halves
+                // are added across the warp, and lane fl writes the g words,
+                // lane 16 + fl the h words of feature fl
+                for (int b = warp; b < kBins; b += kHistV2Threads / 32) {
+                    const unsigned *d = acc + (b * 2 + half) * kBlk + fl;
+                    long long vg = ((long long)(int)d[2 * kDigV2] << (2 * kDig)) +
+                                   ((long long)d[1 * kDigV2] << kDig) + (long long)d[0];
+                    long long vh = ((long long)(int)d[5 * kDigV2] << (2 * kDig)) +
+                                   ((long long)d[4 * kDigV2] << kDig) + (long long)d[3 * kDigV2];
+                    vg += __shfl_xor_sync(0xffffffffu, vg, 16);
+                    vh += __shfl_xor_sync(0xffffffffu, vh, 16);
+                    if (fsel) {
+                        const long long v = half ? vh : vg;
+                        long long *o = dst + ((int64_t)jflush * kBins + b) * kWords + 2 * half;
+                        if (single) {
+                            o[0] = v >> 32;
+                            o[1] = v & 0xffffffffll;
+                        } else {
+                            if (v >> 32) atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(v >> 32));
+                            if (v & 0xffffffffll)
+                                atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(v & 0xffffffffll));
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+            k = pe;
+        }
+    }
+}
+
 // ===========================================================================
 // level planning (device side: no host round trip inside a tree)
 // ===========================================================================
