@@ -490,12 +490,16 @@ def run_engine(args):
                        "colsample": c["colsample"], "parallelism": f"rows sharded x{world}",
                        "l2": "flushed at the start of every timed round (256 MB write on the "
                              "engine stream; its device time is excluded)"},
-            "roofline": {"bound": "hbm", "kernel": "k_hist", "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": "k_hist2 + k_hist (every histogram launch of the round: "
+                                                   "k_hist2 at the root and the next two levels, k_hist below)",
+                         "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak if peak else None,
                          "traffic": traffic and traffic["dram_bytes_per_launch"],
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per k_hist launch, "
-                                           "one round (profiles/k_hist_config4_1M_traffic.md)",
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per histogram "
+                                           "launch, one round, captured with k_hist on every level "
+                                           "(profiles/k_hist_config4_1M_traffic.md; k_hist2 issues the same "
+                                           "row loads)",
                          "alg_bytes_per_launch": st["hist_alg_bytes"] / max(1, st["hist_launches"]),
                          "hist_launches": st["hist_launches"], "hist_ms": st["hist_ms"],
                          "alg_bytes": st["hist_alg_bytes"],
