@@ -269,3 +269,50 @@ def test_c_abi_rejects_bad_arguments_without_a_device(built_lib):
     assert L.gbm_get_grad_mc(None, 0, None, None) == GBM_ERR_ARG
     assert L.gbm_test_peer_wait(0, 0) == GBM_ERR_ARG          # the limit must be 1..10000 ms
     assert L.gbm_test_peer_wait(0, 20000) == GBM_ERR_ARG
+
+
+def _rot_bytes(words, r):
+    """k_hist2's rot_bytes on four 32-bit words: byte k of the result is byte
+    (k + r) mod 16 of the input (restated with NumPy for the check below)."""
+    a, b, c, d = words
+    if r & 8:
+        a, b, c, d = c, d, a, b
+    if r & 4:
+        a, b, c, d = b, c, d, a
+    sh = (r & 3) * 8
+
+    def fsr(lo, hi):
+        return int(((hi << 32) | lo) >> sh) & 0xFFFFFFFF
+    return fsr(a, b), fsr(b, c), fsr(c, d), fsr(d, a)
+
+
+def test_hist2_layout_is_conflict_free_and_complete():
+    """The shared-memory layout of k_hist2 (csrc/gbm_kernels.cuh): in step k
+    lane l = 16 h + f adds feature (f + k) mod 16 into word
+    ((digit * 256 + bin) * 2 + h) * 16 + (f + k) mod 16.  For every step and
+    any bins, the 32 lanes use 32 different banks; over 16 steps every lane
+    adds each of the 16 features of its row exactly once; and the byte each
+    lane reads from its rotated record is that feature's bin."""
+    rng = np.random.default_rng(0)
+    kBins, kBlk, kDigV2 = 256, 16, 256 * 2 * 16
+    for _ in range(200):
+        bins = rng.integers(0, 256, size=(32, kBlk))          # the 16 bins of each lane's row
+        digit = int(rng.integers(0, 6))
+        seen = np.zeros((32, kBlk), dtype=int)
+        for k in range(kBlk):
+            banks = set()
+            for lane in range(32):
+                h, f = lane >> 4, lane & 15
+                feat = (f + k) & (kBlk - 1)
+                seen[lane, feat] += 1
+                word = digit * kDigV2 + (int(bins[lane, feat]) * 2 + h) * kBlk + feat
+                banks.add(word % 32)
+            assert len(banks) == 32
+        assert np.all(seen == 1)
+    for _ in range(300):
+        by = rng.integers(0, 256, size=16)
+        words = tuple(int(sum(int(by[4 * i + j]) << (8 * j) for j in range(4))) for i in range(4))
+        r = int(rng.integers(0, 16))
+        out = _rot_bytes(words, r)
+        for k in range(16):
+            assert (out[k >> 2] >> ((k & 3) * 8)) & 0xFF == by[(k + r) % 16]
