@@ -125,6 +125,31 @@ def post_prune(tf, tl, tr, sg, gamma, nc):
     lib().or_post_prune(_p(tf), _p(tl), _p(tr), _p(sg), float(gamma), int(nc))
 
 
+def enforce_monotone(tf, tl, tr, tv, nc, mono):
+    """The reference's post-hoc monotone clip (E:2461-2499), in place on tv:
+    nodes in index order; a split on a feature with constraint +1 (-1) whose
+    left child value is above (below) the right's sets both children to
+    (left + right) / 2.  Nodes past a pruned split are visited as well, as in
+    the reference's loop over range(nc)."""
+    if mono is None:
+        return
+    for k in range(int(nc)):
+        f = int(tf[k])
+        if f < 0:
+            continue
+        c = int(mono[f])
+        if c == 0:
+            continue
+        l, r = int(tl[k]), int(tr[k])
+        if l < 0 or r < 0:
+            continue
+        lv, rv = float(tv[l]), float(tv[r])
+        if (c == 1 and lv > rv) or (c == -1 and lv < rv):
+            m = (lv + rv) / 2.0
+            tv[l] = m
+            tv[r] = m
+
+
 def leaf_ids(X_bin, tf, tt, tl, tr):
     Xb = np.ascontiguousarray(X_bin, dtype=np.uint16)
     n, p = Xb.shape
@@ -193,12 +218,13 @@ def base_score(y01, w2):
 def fit_binary(X_bin, y01, counts, *, n_estimators, learning_rate, max_leaves, max_depth,
                min_samples_leaf, min_child_weight, reg_lambda, gamma, subsample,
                colsample, class_weight, random_state, mode=MODE_REF, scale_bits=None,
-               grow_policy="leaf", record=None):
+               grow_policy="leaf", record=None, monotone=None):
     """The reference's ``_fit_binary`` loop on the oracle builders.
 
     ``scale_bits=None`` in MODE_EXACT picks S per round the way the engine
-    does (``engine_scale_bits``).  Returns a dict with trees, base score,
-    final F and the train-loss history.
+    does (``engine_scale_bits``).  ``monotone``: int32 [p] of -1/0/+1, the
+    reference's ``_mono_arr``.  Returns a dict with trees, base score, final
+    F and the train-loss history.
     """
     y01 = np.asarray(y01).astype(np.int64)
     n, p = X_bin.shape
@@ -232,7 +258,8 @@ def fit_binary(X_bin, y01, counts, *, n_estimators, learning_rate, max_leaves, m
                        lam=reg_lambda, gamma=gamma, mode=mode, scale_bits=S or 0,
                        policy=grow_policy)
         tf, tt, tv, tl, tr, nc, sg = t
-        post_prune(tf, tl, tr, sg, gamma, nc)
+        post_prune(tf, tl, tr, sg, gamma, nc)          # E:2451-2452
+        enforce_monotone(tf, tl, tr, tv, nc, monotone)  # E:2454-2457
         if record is not None:
             record.append(dict(g=g, h=h, sample=sidx, feat=fidx))
         leaf = leaf_ids(X_bin, tf, tt, tl, tr)

@@ -146,15 +146,51 @@ def regression_case(E, D, loss):
     return {f"fit_reg_{loss}": (T,)}
 
 
+def monotone_case(E, D):
+    """A fit of config 1's data (first 3000 rows) with monotone constraints
+    on four features: the reference's trees after post-prune and the
+    monotone clip (E:2450-2457), its train loss and predict_proba."""
+    Xtr, ytr, Xte, _ = D.config1()
+    X, y = Xtr[:3000], ytr[:3000]
+    mono = [0] * X.shape[1]
+    mono[0], mono[1], mono[4], mono[7] = 1, -1, 1, -1
+    params = dict(n_estimators=20, max_depth=4, learning_rate=0.1, n_bins=64, class_weight=None,
+                  random_state=5, monotone_constraints=mono)
+    m = E.HybridHistGBMNumbaV1_0_1(verbose=False, **params)
+    m.fit(X, y)
+    T = len(m.trees)
+    maxn = max(len(t[0]) for t in m.trees)
+    arr = {k: np.full((T, maxn), fill, dtype=dt) for k, fill, dt in [
+        ("tf", -1, np.int32), ("tt", 0, np.int64), ("tv", 0.0, np.float64),
+        ("tl", -1, np.int32), ("tr", -1, np.int32), ("sg", 0.0, np.float64)]}
+    ncs = np.zeros(T, dtype=np.int32)
+    for t, (tf, tt, tv, tl, tr, nc, sg) in enumerate(m.trees):
+        for k, a in zip(("tf", "tt", "tv", "tl", "tr", "sg"), (tf, tt, tv, tl, tr, sg)):
+            arr[k][t, :len(a)] = a
+        ncs[t] = nc
+    np.savez_compressed(
+        os.path.join(HERE, "fit_mono.npz"), params=np.array(repr(params)), n_trees=T, nc=ncs, **arr,
+        mono=np.array(mono, dtype=np.int32), base_score=m.base_score_, learning_rate=m.learning_rate,
+        max_leaves=m.max_leaves, max_depth=m.max_depth, min_child_weight=m.min_child_weight,
+        subsample=m.subsample, colsample=m.colsample_bytree, reg_lambda=m.reg_lambda, gamma=m.gamma,
+        min_samples_leaf=m.min_samples_leaf, n_bins=m.n_bins, binning_strategy=m.binning_strategy,
+        edges=m.bin_edges, counts=m.feature_bin_counts, nan_bin_id=m._nan_bin_id,
+        train_loss=np.array(m.train_loss_history_),
+        proba_test=m.predict_proba(Xte))
+    return {"fit_mono": (T, int(ncs.sum()))}
+
+
 def main(ref_src, only=None):
     sys.path.insert(0, ref_src)
     import bsscl_gbm.estimator_v1_0_1 as E
     from bsscl_gbm_b200 import datasets as D
 
     out = {}
-    if only in ("model", "multiclass", "regression"):
+    if only in ("model", "multiclass", "regression", "monotone"):
         if only == "model":
             out.update(model_json_case(E, D))
+        elif only == "monotone":
+            out.update(monotone_case(E, D))
         elif only == "multiclass":
             out.update(multiclass_case(E, D))
         else:
@@ -397,6 +433,7 @@ def main(ref_src, only=None):
     out.update(multiclass_case(E, D))
     out.update(regression_case(E, D, "mse"))
     out.update(regression_case(E, D, "mae"))
+    out.update(monotone_case(E, D))
 
     for k, v in out.items():
         print(k, v)
@@ -405,5 +442,5 @@ def main(ref_src, only=None):
 if __name__ == "__main__":
     # python make_golden.py <reference>/src [model]   ('model': only the save_model fixture)
     if len(sys.argv) < 2:
-        sys.exit("usage: make_golden.py <reference>/src [model|multiclass|regression]")
+        sys.exit("usage: make_golden.py <reference>/src [model|multiclass|regression|monotone]")
     main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else None)

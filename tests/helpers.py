@@ -14,10 +14,12 @@ def golden(name):
 def fit_inputs(name):
     """(X_train, y_train, X_test) of a golden fit, regenerated from its seeds."""
     from bsscl_gbm_b200 import datasets as D
-    if name in ("cfg1", "cfg1_level"):
+    if name in ("cfg1", "cfg1_level", "mono"):
         Xtr, ytr, Xte, _ = D.config1()
         if name == "cfg1_level":
             return Xtr[:4000], ytr[:4000], Xte
+        if name == "mono":
+            return Xtr[:3000], ytr[:3000], Xte
         return Xtr, ytr, Xte
     if name == "cfg2_small":
         X, y = D.config2(n=40_000, n_pos=120)

@@ -181,6 +181,25 @@ def test_fit_matches_reference(name):
     assert A.explained(res), res
 
 
+def test_monotone_fit_matches_reference():
+    """monotone_constraints on four features: the device replay's clip after
+    the post-prune (E:2450-2457, E:2461-2499) gives the reference's recorded
+    fit (tests/golden/fit_mono.npz).  The oracle's EXACT arithmetic meets no
+    tie on this fit (tests/test_oracle.py), so every tree must match."""
+    from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
+    d = golden("fit_mono")
+    X, y, Xte = fit_inputs("mono")
+    m = M(verbose=False, **fit_params(d)).fit(X, y)
+    ref = golden_trees(d)
+    assert len(m.trees) == len(ref)
+    assert A.first_divergence(ref, m.trees) is None
+    for t in range(len(ref)):
+        nc = ref[t][5]
+        assert np.abs(m.trees[t][2][:nc] - ref[t][2][:nc]).max() <= 1e-6, f"values tree {t}"
+    assert np.abs(m.predict_proba(Xte) - d["proba_test"]).max() <= 1e-6
+    assert np.abs(np.array(m.train_loss_history_) - d["train_loss"]).max() <= 1e-9
+
+
 def test_fit_is_deterministic():
     from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
     X, y, Xte = fit_inputs("cfg3_small")

@@ -190,3 +190,38 @@ def test_ref_regression_fit_bit_exact(loss):
     for t in range(3):
         assert np.array_equal(rec[t]["g"], d[f"r{t}_g"])
     assert np.abs(r["train_loss"] - d["train_loss"]).max() <= 1e-9 * np.abs(d["train_loss"]).max()
+
+
+def test_ref_monotone_fit_bit_exact():
+    """The oracle's loop with the monotone clip (E:2461-2499 after the
+    post-prune, E:2450-2457) == the reference's fit with
+    monotone_constraints on four features (tests/golden/fit_mono.npz)."""
+    d = golden("fit_mono")
+    Xb, y = _binned("mono", d)
+    r = O.fit_binary(Xb, y, d["counts"], mode=O.MODE_REF, monotone=d["mono"], **oracle_fit_kwargs(d))
+    assert r["base_score"] == float(d["base_score"])
+    clipped = 0
+    for t, (a, b) in enumerate(zip(r["trees"], golden_trees(d))):
+        assert same_topology(a, b), f"tree {t}"
+        nc = a[5]
+        assert np.abs(a[2][:nc] - b[2][:nc]).max() < 1e-12, f"values tree {t}"
+        for k in range(nc):   # splits whose children the clip made equal
+            f = int(b[0][k])
+            if f >= 0 and d["mono"][f] != 0 and abs(b[2][b[3][k]] - b[2][b[4][k]]) == 0.0:
+                clipped += 1
+    assert clipped > 0        # the fixture exercises the clip
+    assert np.abs(r["train_loss"] - d["train_loss"]).max() < 1e-12
+
+
+def test_exact_monotone_fit_has_no_tie():
+    """The engine's fixed-point arithmetic (EXACT mode) gives every tree of
+    the monotone fit as the reference does, so the GPU test of this fit
+    compares every tree."""
+    from helpers import engine_scale_bits
+    d = golden("fit_mono")
+    Xb, y = _binned("mono", d)
+    kw = oracle_fit_kwargs(d)
+    ref = O.fit_binary(Xb, y, d["counts"], mode=O.MODE_REF, monotone=d["mono"], **kw)
+    ex = O.fit_binary(Xb, y, d["counts"], mode=O.MODE_EXACT, scale_bits=engine_scale_bits(ref["w2"].max()),
+                      monotone=d["mono"], **kw)
+    assert A.first_divergence(golden_trees(d), ex["trees"]) is None
