@@ -180,17 +180,51 @@ def monotone_case(E, D):
     return {"fit_mono": (T, int(ncs.sum()))}
 
 
+def early_stop_case(E, D):
+    """A fit of noisy config-3 data with a validation set and
+    early_stopping_rounds (E:2908-2935): the kept trees, best_iteration_,
+    n_trees_fitted_, both loss histories and predict_proba."""
+    X, y = D.config3(n=12_000)
+    Xtr, ytr, Xva, yva, Xte = X[:6000], y[:6000], X[6000:9000], y[6000:9000], X[9000:]
+    params = dict(n_estimators=80, max_depth=6, learning_rate=0.3, n_bins=128, class_weight="balanced_sqrt",
+                  random_state=7, early_stopping_rounds=5)
+    m = E.HybridHistGBMNumbaV1_0_1(verbose=False, **params)
+    m.fit(Xtr, ytr, X_val=Xva, y_val=yva)
+    T = len(m.trees)
+    maxn = max(len(t[0]) for t in m.trees)
+    arr = {k: np.full((T, maxn), fill, dtype=dt) for k, fill, dt in [
+        ("tf", -1, np.int32), ("tt", 0, np.int64), ("tv", 0.0, np.float64),
+        ("tl", -1, np.int32), ("tr", -1, np.int32), ("sg", 0.0, np.float64)]}
+    ncs = np.zeros(T, dtype=np.int32)
+    for t, (tf, tt, tv, tl, tr, nc, sg) in enumerate(m.trees):
+        for k, a in zip(("tf", "tt", "tv", "tl", "tr", "sg"), (tf, tt, tv, tl, tr, sg)):
+            arr[k][t, :len(a)] = a
+        ncs[t] = nc
+    np.savez_compressed(
+        os.path.join(HERE, "fit_early.npz"), params=np.array(repr(params)), n_trees=T, nc=ncs, **arr,
+        best_iteration=m.best_iteration_, n_trees_fitted=m.n_trees_fitted_, base_score=m.base_score_,
+        learning_rate=m.learning_rate, max_leaves=m.max_leaves, max_depth=m.max_depth,
+        min_child_weight=m.min_child_weight, subsample=m.subsample, colsample=m.colsample_bytree,
+        reg_lambda=m.reg_lambda, gamma=m.gamma, min_samples_leaf=m.min_samples_leaf, n_bins=m.n_bins,
+        binning_strategy=m.binning_strategy, edges=m.bin_edges, counts=m.feature_bin_counts,
+        nan_bin_id=m._nan_bin_id, train_loss=np.array(m.train_loss_history_),
+        val_loss=np.array(m.val_loss_history_), proba_test=m.predict_proba(Xte))
+    return {"fit_early": (T, m.best_iteration_, len(m.val_loss_history_))}
+
+
 def main(ref_src, only=None):
     sys.path.insert(0, ref_src)
     import bsscl_gbm.estimator_v1_0_1 as E
     from bsscl_gbm_b200 import datasets as D
 
     out = {}
-    if only in ("model", "multiclass", "regression", "monotone"):
+    if only in ("model", "multiclass", "regression", "monotone", "early"):
         if only == "model":
             out.update(model_json_case(E, D))
         elif only == "monotone":
             out.update(monotone_case(E, D))
+        elif only == "early":
+            out.update(early_stop_case(E, D))
         elif only == "multiclass":
             out.update(multiclass_case(E, D))
         else:
@@ -434,6 +468,7 @@ def main(ref_src, only=None):
     out.update(regression_case(E, D, "mse"))
     out.update(regression_case(E, D, "mae"))
     out.update(monotone_case(E, D))
+    out.update(early_stop_case(E, D))
 
     for k, v in out.items():
         print(k, v)
@@ -442,5 +477,5 @@ def main(ref_src, only=None):
 if __name__ == "__main__":
     # python make_golden.py <reference>/src [model]   ('model': only the save_model fixture)
     if len(sys.argv) < 2:
-        sys.exit("usage: make_golden.py <reference>/src [model|multiclass|regression|monotone]")
+        sys.exit("usage: make_golden.py <reference>/src [model|multiclass|regression|monotone|early]")
     main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else None)

@@ -98,3 +98,17 @@ def same_topology(a, b):
 def engine_scale_bits(wmax, chunk=16384):
     """Fixed-point exponent of the engine for weights up to ``wmax`` (libgbm_b200)."""
     return 62 - int(np.ceil(np.log2(chunk * max(1.0, wmax))))
+
+
+def early_inputs():
+    """(X_train, y_train, X_val, y_val, X_test) of tests/golden/fit_early.npz."""
+    from bsscl_gbm_b200 import datasets as D
+    X, y = D.config3(n=12_000)
+    return X[:6000], y[:6000], X[6000:9000], y[6000:9000], X[9000:]
+
+
+def val_loss(y, F):
+    """The reference's binary log-loss (E:2321-2325)."""
+    p = 1.0 / (1.0 + np.exp(-np.clip(F, -500, 500)))
+    p = np.clip(p, 1e-15, 1 - 1e-15)
+    return -np.mean(y * np.log(p) + (1 - y) * np.log(1 - p))

@@ -200,6 +200,30 @@ def test_monotone_fit_matches_reference():
     assert np.abs(np.array(m.train_loss_history_) - d["train_loss"]).max() <= 1e-9
 
 
+def test_early_stopping_fit_matches_reference():
+    """A validation set with early_stopping_rounds (E:2908-2935): the same
+    best iteration, kept trees, loss histories and predict_proba as the
+    reference's recorded fit (tests/golden/fit_early.npz).  Its stopping
+    decisions are clear of rounding noise and EXACT arithmetic meets no tie
+    on it (tests/test_oracle.py)."""
+    from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
+    from helpers import early_inputs
+    d = golden("fit_early")
+    Xtr, ytr, Xva, yva, Xte = early_inputs()
+    m = M(verbose=False, **fit_params(d)).fit(Xtr, ytr, X_val=Xva, y_val=yva)
+    assert m.best_iteration_ == int(d["best_iteration"])
+    assert m.n_trees_fitted_ == int(d["n_trees_fitted"])
+    ref = golden_trees(d)
+    assert len(m.trees) == len(ref)
+    assert A.first_divergence(ref, m.trees) is None
+    for t in range(len(ref)):
+        nc = ref[t][5]
+        assert np.abs(m.trees[t][2][:nc] - ref[t][2][:nc]).max() <= 1e-6, f"values tree {t}"
+    assert np.abs(np.array(m.val_loss_history_) - d["val_loss"]).max() <= 1e-9
+    assert np.abs(np.array(m.train_loss_history_) - d["train_loss"]).max() <= 1e-9
+    assert np.abs(m.predict_proba(Xte) - d["proba_test"]).max() <= 1e-6
+
+
 def test_fit_is_deterministic():
     from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
     X, y, Xte = fit_inputs("cfg3_small")

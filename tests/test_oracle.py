@@ -225,3 +225,53 @@ def test_exact_monotone_fit_has_no_tie():
     ex = O.fit_binary(Xb, y, d["counts"], mode=O.MODE_EXACT, scale_bits=engine_scale_bits(ref["w2"].max()),
                       monotone=d["mono"], **kw)
     assert A.first_divergence(golden_trees(d), ex["trees"]) is None
+
+
+def _early_fit(mode):
+    """The oracle's loop run for the rounds the reference ran, the validation
+    loss after each (E:2908-2916), and the reference's stopping rule
+    (E:2924-2935) restated: (trees kept, best iteration, val losses)."""
+    from helpers import early_inputs, val_loss, engine_scale_bits
+    d = golden("fit_early")
+    Xtr, ytr, Xva, yva, _ = early_inputs()
+    hyb = str(d["binning_strategy"]) == "hybrid"
+    Xb = O.bin_matrix(Xtr, d["edges"], d["counts"], d["nan_bin_id"], hyb)
+    Xvb = O.bin_matrix(Xva, d["edges"], d["counts"], d["nan_bin_id"], hyb)
+    kw = oracle_fit_kwargs(d)
+    kw["n_estimators"] = len(d["val_loss"])
+    S = None
+    if mode == O.MODE_EXACT:
+        w2 = O.class_weights(np.asarray(ytr), kw["class_weight"])
+        S = engine_scale_bits(w2.max())
+    r = O.fit_binary(Xb, ytr, d["counts"], mode=mode, scale_bits=S, **kw)
+    F = np.full(len(yva), r["base_score"])
+    losses, best, best_it, bad = [], np.inf, 0, 0
+    for m, (tf, tt, tv, tl, tr, nc, sg) in enumerate(r["trees"]):
+        F += kw["learning_rate"] * tv[O.leaf_ids(Xvb, tf, tt, tl, tr)]
+        v = val_loss(yva, F)
+        losses.append(v)
+        if v < best:
+            best, best_it, bad = v, m, 0
+        else:
+            bad += 1
+            if bad >= 5:
+                break
+    return r["trees"][:best_it + 1], best_it, np.array(losses), d
+
+
+@pytest.mark.parametrize("mode", [O.MODE_REF, O.MODE_EXACT])
+def test_early_stopping_fit(mode):
+    """REF and EXACT arithmetic both reproduce the reference's early-stopped
+    fit: the same validation losses (to 1e-12), the same best iteration and
+    kept trees.  Each stopping decision is clear of rounding noise, so the
+    GPU test of this fit compares the same decisions."""
+    trees, best_it, losses, d = _early_fit(mode)
+    assert best_it == int(d["best_iteration"]) and len(trees) == int(d["n_trees"])
+    assert len(losses) == len(d["val_loss"])
+    assert np.abs(losses - d["val_loss"]).max() < 1e-12
+    for t, (a, b) in enumerate(zip(trees, golden_trees(d))):
+        assert same_topology(a, b), f"tree {t}"
+        assert np.abs(a[2][:a[5]] - b[2][:b[5]]).max() < 1e-12, f"values tree {t}"
+    run_best = np.minimum.accumulate(d["val_loss"])
+    margins = np.abs(d["val_loss"][1:] - run_best[:-1])
+    assert margins.min() > 1e-9
