@@ -218,7 +218,7 @@ def base_score(y01, w2):
 def fit_binary(X_bin, y01, counts, *, n_estimators, learning_rate, max_leaves, max_depth,
                min_samples_leaf, min_child_weight, reg_lambda, gamma, subsample,
                colsample, class_weight, random_state, mode=MODE_REF, scale_bits=None,
-               grow_policy="leaf", record=None, monotone=None):
+               grow_policy="leaf", record=None, monotone=None, scale_pos_weight=None, objective="auto"):
     """The reference's ``_fit_binary`` loop on the oracle builders.
 
     ``scale_bits=None`` in MODE_EXACT picks S per round the way the engine
@@ -228,7 +228,7 @@ def fit_binary(X_bin, y01, counts, *, n_estimators, learning_rate, max_leaves, m
     """
     y01 = np.asarray(y01).astype(np.int64)
     n, p = X_bin.shape
-    w2 = class_weights(y01, class_weight)
+    w2 = class_weights(y01, class_weight, scale_pos_weight, objective)
     base = base_score(y01, w2)
     F = np.full(n, base)
     n_sub = max(1, int(n * subsample))

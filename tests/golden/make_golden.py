@@ -212,19 +212,68 @@ def early_stop_case(E, D):
     return {"fit_early": (T, m.best_iteration_, len(m.val_loss_history_))}
 
 
+def spw_case(E, D):
+    """A fit of imbalanced config-2 data with objective='binary' and
+    scale_pos_weight=3: the weighted bin edges (E:3211-3216, E:2073-2141)
+    and the class weights (E:2572-2577) both use it."""
+    X, y = D.config2(n=30_000, n_pos=150)
+    Xtr, ytr, Xte = X[:24_000], y[:24_000], X[24_000:]
+    params = dict(n_estimators=15, max_depth=5, n_bins=255, objective="binary", scale_pos_weight=3.0,
+                  random_state=11)
+    captured = []
+    cls = E.HybridHistGBMNumbaV1_0_1
+    orig = cls._build_one_tree
+
+    def spy(self, X_bin, grad, hess, sample_idx, feat_idx, n_features):
+        tree = orig(self, X_bin, grad, hess, sample_idx, feat_idx, n_features)
+        captured.append((grad.copy(), hess.copy(), sample_idx.copy(), feat_idx.copy()))
+        return tree
+
+    cls._build_one_tree = spy
+    try:
+        m = cls(verbose=False, **params)
+        m.fit(Xtr, ytr)
+    finally:
+        cls._build_one_tree = orig
+    rounds = {}
+    for r_, (g, h, smp, f) in enumerate(captured[:4]):
+        rounds.update({f"r{r_}_g": g, f"r{r_}_h": h, f"r{r_}_sample": smp, f"r{r_}_feat": f})
+    T = len(m.trees)
+    maxn = max(len(t[0]) for t in m.trees)
+    arr = {k: np.full((T, maxn), fill, dtype=dt) for k, fill, dt in [
+        ("tf", -1, np.int32), ("tt", 0, np.int64), ("tv", 0.0, np.float64),
+        ("tl", -1, np.int32), ("tr", -1, np.int32), ("sg", 0.0, np.float64)]}
+    ncs = np.zeros(T, dtype=np.int32)
+    for t, (tf, tt, tv, tl, tr, nc, sg) in enumerate(m.trees):
+        for k, a in zip(("tf", "tt", "tv", "tl", "tr", "sg"), (tf, tt, tv, tl, tr, sg)):
+            arr[k][t, :len(a)] = a
+        ncs[t] = nc
+    np.savez_compressed(
+        os.path.join(HERE, "fit_spw.npz"), params=np.array(repr(params)), n_trees=T, nc=ncs, **arr, **rounds,
+        base_score=m.base_score_, learning_rate=m.learning_rate, max_leaves=m.max_leaves,
+        max_depth=m.max_depth, min_child_weight=m.min_child_weight, subsample=m.subsample,
+        colsample=m.colsample_bytree, reg_lambda=m.reg_lambda, gamma=m.gamma,
+        min_samples_leaf=m.min_samples_leaf, n_bins=m.n_bins, binning_strategy=m.binning_strategy,
+        edges=m.bin_edges, counts=m.feature_bin_counts, nan_bin_id=m._nan_bin_id,
+        train_loss=np.array(m.train_loss_history_), proba_test=m.predict_proba(Xte))
+    return {"fit_spw": (T, float(m.base_score_))}
+
+
 def main(ref_src, only=None):
     sys.path.insert(0, ref_src)
     import bsscl_gbm.estimator_v1_0_1 as E
     from bsscl_gbm_b200 import datasets as D
 
     out = {}
-    if only in ("model", "multiclass", "regression", "monotone", "early"):
+    if only in ("model", "multiclass", "regression", "monotone", "early", "spw"):
         if only == "model":
             out.update(model_json_case(E, D))
         elif only == "monotone":
             out.update(monotone_case(E, D))
         elif only == "early":
             out.update(early_stop_case(E, D))
+        elif only == "spw":
+            out.update(spw_case(E, D))
         elif only == "multiclass":
             out.update(multiclass_case(E, D))
         else:
@@ -469,6 +518,7 @@ def main(ref_src, only=None):
     out.update(regression_case(E, D, "mae"))
     out.update(monotone_case(E, D))
     out.update(early_stop_case(E, D))
+    out.update(spw_case(E, D))
 
     for k, v in out.items():
         print(k, v)
@@ -477,5 +527,5 @@ def main(ref_src, only=None):
 if __name__ == "__main__":
     # python make_golden.py <reference>/src [model]   ('model': only the save_model fixture)
     if len(sys.argv) < 2:
-        sys.exit("usage: make_golden.py <reference>/src [model|multiclass|regression|monotone|early]")
+        sys.exit("usage: make_golden.py <reference>/src [model|multiclass|regression|monotone|early|spw]")
     main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else None)

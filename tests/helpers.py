@@ -24,6 +24,9 @@ def fit_inputs(name):
     if name == "cfg2_small":
         X, y = D.config2(n=40_000, n_pos=120)
         return X[:32_000], y[:32_000], X[32_000:]
+    if name == "spw":
+        X, y = D.config2(n=30_000, n_pos=150)
+        return X[:24_000], y[:24_000], X[24_000:]
     if name == "cfg3_small":
         X, y = D.config3(n=25_000)
         return X[:20_000], y[:20_000], X[20_000:]
@@ -53,7 +56,8 @@ def oracle_fit_kwargs(d):
                 colsample=float(d["colsample"]),
                 class_weight=params.get("class_weight", "balanced_sqrt"),
                 random_state=params["random_state"],
-                grow_policy=params.get("grow_policy", "leaf"))
+                grow_policy=params.get("grow_policy", "leaf"),
+                scale_pos_weight=params.get("scale_pos_weight"), objective=params.get("objective", "auto"))
 
 
 def golden_trees(d):

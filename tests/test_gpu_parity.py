@@ -152,7 +152,7 @@ def test_rounds_match_oracle_exact(engine, policy):
     s.close()
 
 
-@pytest.mark.parametrize("name", ["cfg1", "cfg1_level", "cfg2_small", "cfg3_small", "cfg4_small"])
+@pytest.mark.parametrize("name", ["cfg1", "cfg1_level", "cfg2_small", "cfg3_small", "cfg4_small", "spw"])
 def test_fit_matches_reference(name):
     """The estimator on the GPU vs the reference's own recorded fit."""
     from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M

@@ -100,7 +100,7 @@ def test_ref_fit_bit_exact(name):
     assert np.abs(r["train_loss"] - d["train_loss"]).max() < 1e-12
 
 
-@pytest.mark.parametrize("name", ["cfg1", "cfg1_level", "cfg2_small", "cfg3_small", "cfg4_small"])
+@pytest.mark.parametrize("name", ["cfg1", "cfg1_level", "cfg2_small", "cfg3_small", "cfg4_small", "spw"])
 def test_exact_fit_ties_explained(name):
     """EXACT-mode fit: same trees as the reference up to the first divergence,
     and that divergence is an exact (or sub-resolution) tie."""
@@ -275,3 +275,39 @@ def test_early_stopping_fit(mode):
     run_best = np.minimum.accumulate(d["val_loss"])
     margins = np.abs(d["val_loss"][1:] - run_best[:-1])
     assert margins.min() > 1e-9
+
+
+def test_spw_weighted_edges_match_reference():
+    """scale_pos_weight=3 with objective='binary': the host's weighted bin
+    edges (the reference's _build_bin_edges with sample_weight, E:3211-3216)
+    equal the reference's, and so do the class weights (E:2572-2577)."""
+    from bsscl_gbm_b200 import binning
+    d = golden("fit_spw")
+    X, y, _ = fit_inputs("spw")
+    sw = np.ones(len(y))
+    sw[y == 1] = 3.0
+    e, c, nb = binning.build_bin_edges(X, int(d["n_bins"]), None, sw)
+    assert np.array_equal(e, d["edges"]) and np.array_equal(c, d["counts"]) and np.array_equal(nb, d["nan_bin_id"])
+    assert np.array_equal(O.class_weights(y, "balanced_sqrt", 3.0, "binary"), [1.0, 3.0])
+    assert np.array_equal(O.class_weights(y, "balanced_sqrt", 3.0, "auto"),
+                          O.class_weights(y, "balanced_sqrt"))   # 'auto' ignores it (E:2572)
+
+
+def test_ref_spw_fit_bit_exact():
+    """The oracle's loop with scale_pos_weight=3 and objective='binary' (the
+    class weights of E:2572-2577) == the reference's fit; its sampler matches
+    the recorded rounds."""
+    d = golden("fit_spw")
+    Xb, y = _binned("spw", d)
+    rec = []
+    r = O.fit_binary(Xb, y, d["counts"], mode=O.MODE_REF, record=rec, **oracle_fit_kwargs(d))
+    assert r["base_score"] == float(d["base_score"])
+    for t, (a, b) in enumerate(zip(r["trees"], golden_trees(d))):
+        assert same_topology(a, b), f"tree {t}"
+        assert np.abs(a[2][:a[5]] - b[2][:b[5]]).max() < 1e-12, f"values tree {t}"
+    for t in range(4):
+        assert np.array_equal(rec[t]["sample"], d[f"r{t}_sample"]) and np.array_equal(rec[t]["feat"], d[f"r{t}_feat"])
+        # g, h to the last bits of exp (NumPy's SIMD exp vs the C library's)
+        assert np.allclose(rec[t]["g"], d[f"r{t}_g"], rtol=1e-14, atol=0)
+        assert np.allclose(rec[t]["h"], d[f"r{t}_h"], rtol=1e-14, atol=0)
+    assert np.abs(r["train_loss"] - d["train_loss"]).max() < 1e-12
