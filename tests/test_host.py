@@ -316,3 +316,27 @@ def test_hist2_layout_is_conflict_free_and_complete():
         out = _rot_bytes(words, r)
         for k in range(16):
             assert (out[k >> 2] >> ((k & 3) * 8)) & 0xFF == by[(k + r) % 16]
+
+
+@pytest.mark.parametrize("name", ["cfg1", "cfg1_level", "cfg2_small", "cfg3_small", "cfg4_small"])
+def test_packing_and_importances_match_reference(name):
+    """The estimator's packing (_pack_tree_list, E:2192-2216) and gain
+    importances (E:2343-2363), given the reference's own trees of a recorded
+    fit, equal the reference's packed arrays and feature_importances_."""
+    from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
+    from helpers import golden_trees
+    d = golden("fit_" + name)
+    X, _, _ = fit_inputs(name)
+    m = M(verbose=False)
+    m.trees = golden_trees(d)
+    m.mc_trees = None
+    m._is_multiclass = False
+    m.n_features_in_ = X.shape[1]
+    m._pack_trees()
+    m._compute_feature_importances()
+    for mine, ref in (("_packed_features", "packed_features"), ("_packed_thresholds", "packed_thresholds"),
+                      ("_packed_values", "packed_values"), ("_packed_left", "packed_left"),
+                      ("_packed_right", "packed_right"), ("_tree_offsets", "tree_offsets")):
+        assert np.array_equal(getattr(m, mine), d[ref]), mine
+        assert getattr(m, mine).dtype == d[ref].dtype, mine
+    assert np.array_equal(m.feature_importances_, d["feature_importances"])
