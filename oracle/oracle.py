@@ -8,8 +8,10 @@ bench.py's CPU legs as the checker.  The product package never imports it.
 C builders: class weights (E:2570-2603), weighted-mean base score
 (E:2829-2835), p = sigmoid(clip(F)) / g / h (E:2861, E:2873-2874), the
 cumulative ``RandomState.shuffle`` sampler (E:2502-2517, using NumPy's own
-legacy generator), tree build + post-prune (E:2397-2459), the F update
-``F += lr * tree(X)`` (E:2896-2897) and the train logloss (E:2905).
+legacy generator), tree build + post-prune (E:2397-2459), the monotone
+clip (E:2461-2499), the F update ``F += lr * tree(X)`` (E:2896-2897) and the
+train logloss (E:2905).  ``scale_pos_weight`` with ``objective='binary'``
+sets the class weights (E:2572-2577).
 """
 
 from __future__ import annotations
