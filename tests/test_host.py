@@ -218,6 +218,13 @@ def test_estimator_argument_errors():
         M(sampling_method="goss", verbose=False).fit(X, y)
     with pytest.raises(NotImplementedError):
         M(verbose=False).fit(X, np.arange(100) % 65)   # more classes than the engine holds
+    # the reference's own fuzz cases that fail before training (T:test_fuzz.py:5-31)
+    with pytest.raises((ValueError, TypeError)):
+        M(n_estimators=1, max_depth=2, verbose=False).fit(np.array([["a", "b"], ["c", "d"]]), np.array([0, 1]))
+    with pytest.raises((ValueError, IndexError)):
+        M(n_estimators=1, max_depth=2, verbose=False).fit(np.array([[]]), np.array([]))
+    with pytest.raises(ValueError):
+        M(n_estimators=1, max_depth=2, verbose=False).fit(np.zeros((0, 3)), np.zeros(0))
 
 
 def test_adaptive_hyperparameters_follow_reference():
