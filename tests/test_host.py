@@ -347,3 +347,34 @@ def test_packing_and_importances_match_reference(name):
         assert np.array_equal(getattr(m, mine), d[ref]), mine
         assert getattr(m, mine).dtype == d[ref].dtype, mine
     assert np.array_equal(m.feature_importances_, d["feature_importances"])
+
+
+def test_pickle_round_trip_of_a_fitted_model():
+    """A model holding a recorded fit survives pickle (T:test_serialization.py:9-35):
+    trees, packed arrays, edges and hyper-parameters come back equal, and the
+    device handle is not pickled."""
+    import pickle
+    from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1 as M
+    from helpers import golden_trees, fit_params
+    d = golden("fit_cfg3_small")
+    X, _, _ = fit_inputs("cfg3_small")
+    m = M(verbose=False, **fit_params(d))
+    m.trees = golden_trees(d)
+    m.mc_trees = None
+    m._is_multiclass = False
+    m.n_features_in_ = X.shape[1]
+    m.bin_edges, m.feature_bin_counts, m._nan_bin_id = d["edges"], d["counts"], d["nan_bin_id"]
+    m.base_score_ = float(d["base_score"])
+    m._pack_trees()
+    m._compute_feature_importances()
+    m._engine = object()            # stands in for a live device context
+    b = pickle.loads(pickle.dumps(m))
+    assert b._engine is None
+    assert b.get_params() == m.get_params()
+    for ta, tb in zip(m.trees, b.trees):
+        for x, y in zip(ta, tb):
+            assert np.array_equal(np.asarray(x), np.asarray(y))
+    for k in ("_packed_features", "_packed_thresholds", "_packed_values", "_packed_left", "_packed_right",
+              "_tree_offsets", "bin_edges", "feature_bin_counts", "_nan_bin_id", "feature_importances_"):
+        assert np.array_equal(getattr(m, k), getattr(b, k)), k
+    assert b.base_score_ == m.base_score_
