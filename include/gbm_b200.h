@@ -93,12 +93,16 @@ typedef struct {
 /* ---- context ---------------------------------------------------------- */
 
 /* Create a context on CUDA device `device`.  Fails with GBM_ERR_CUDA when
- * no such device exists (there is no CPU fallback). */
+ * no such device exists (there is no CPU fallback).  The reference's device
+ * switch (E:1852-1856, E:2408-2421) falls back to the CPU instead. */
 int gbm_ctx_create(int32_t device, gbm_ctx **out);
+/* Frees the context's device memory and communicator (no reference
+ * counterpart: the reference holds no device state). */
 void gbm_ctx_destroy(gbm_ctx *ctx);
 const char *gbm_last_error(const gbm_ctx *ctx);
 
-/* Join an NCCL communicator of `nranks` processes (one per GPU).  `uid` is
+/* Join an NCCL communicator of `nranks` processes (one per GPU); no reference
+ * counterpart (the reference runs on one host).  `uid` is
  * the 128-byte ncclUniqueId made by rank 0 and shared by the caller.
  * Histograms are then summed over ranks (exact int64 words), so every rank
  * builds the identical tree from its own row shard.  `timeout_ms` bounds
@@ -203,14 +207,16 @@ int gbm_round_mc(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_id
 int gbm_get_F_mc(gbm_ctx *ctx, double *F_out);
 int gbm_get_grad_mc(gbm_ctx *ctx, int32_t k, double *g_out, double *h_out);
 
-/* One boosting round.  `inbag_mask` [n] marks this rank's in-bag rows
+/* One boosting round, the body of _fit_binary's loop (E:2849-2905).
+ * `inbag_mask` [n] marks this rank's in-bag rows
  * (the subsample); `feat_idx` [nfeat] the sorted column subsample.  Writes
  * the pruned tree to `out`, updates F on the device and returns the train
  * logloss over all rows of all ranks. */
 int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
               const gbm_params *params, gbm_tree_out *out, double *train_loss);
 
-/* gbm_round with the round's subsample taken from `sampler` (over the
+/* gbm_round with the round's subsample taken from `sampler`
+ * (_get_subsample_indices, E:2502-2517) over the
  * global row ids of all ranks): the next draw's row ids are copied to the
  * device and this rank's in-bag mask (rows row_offset .. row_offset+n-1) is
  * built there.  Same results as gbm_round with the equivalent mask. */
@@ -239,11 +245,13 @@ int gbm_build_tree(gbm_ctx *ctx, const double *grad, const double *hess, const u
                    gbm_tree_out *out);
 
 /* Fixed-point exponent S of the current fit: every g and h is rounded once
- * to the grid 2^-S and all sums are exact integer sums. */
+ * to the grid 2^-S and all sums are exact integer sums (no reference
+ * counterpart: the reference sums float64 in row order, E:582-596). */
 int32_t gbm_scale_bits(const gbm_ctx *ctx);
 
-/* Copy device state to the host (for parity checks): F [n], and the f64
- * gradient/hessian of the NEXT round's inputs [n]. */
+/* Copy device state to the host (for parity checks): F [n] (the reference's
+ * F_train, E:2896-2897), and the f64 gradient/hessian of the NEXT round's
+ * inputs [n] (E:2861, E:2873-2874). */
 int gbm_get_F(gbm_ctx *ctx, double *F_out);
 int gbm_get_grad(gbm_ctx *ctx, double *g_out, double *h_out);
 
@@ -258,14 +266,17 @@ int gbm_test_peer_wait(int32_t device, int32_t timeout_ms);
 
 /* ---- predict ---------------------------------------------------------- */
 
-/* F[i] = base + sum_t lr * values[leaf_t(i)] and proba = sigmoid(clip(F))
- * for row-major uint8 bins [n][p].  Either output may be NULL. */
+/* F[i] = base + sum_t lr * values[leaf_t(i)] (predict_all_trees_jit,
+ * E:863-884) and proba = sigmoid(clip(F)) (predict_proba, E:3318-3336) for
+ * row-major uint8 bins [n][p].  Either output may be NULL. */
 int gbm_predict(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p,
                 const gbm_packed *model, double learning_rate, double base_score,
                 double *F_out, double *proba_out);
 
 /* Device-resident predict: upload the ensemble and the bins once, then run
- * on the device copies (outputs stay on the device until fetched). */
+ * on the device copies (outputs stay on the device until fetched).  The
+ * same computation as gbm_predict (E:863-884, E:3318-3336), split into its
+ * steps. */
 int gbm_predict_set_model(gbm_ctx *ctx, const gbm_packed *model, int32_t n_features);
 int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p);
 int gbm_predict_run(gbm_ctx *ctx, double learning_rate, double base_score);
@@ -310,7 +321,8 @@ int gbm_predict_noalloc(const uint8_t *xbin_dev, int64_t n, int32_t p, const int
                         int32_t n_nodes, double learning_rate, double base_score, double *F_dev,
                         double *proba_dev, void *stream, char *errbuf, int32_t errlen);
 
-/* Synchronise the context's stream; returns the first asynchronous error. */
+/* Synchronise the context's stream; returns the first asynchronous error
+ * (no reference counterpart). */
 int gbm_sync(gbm_ctx *ctx);
 
 /* ---- instrumentation -------------------------------------------------- */
@@ -339,6 +351,8 @@ typedef struct {
     double peer_wait_ms;       /* peer exchange: time spent waiting for the peers' signals */
 } gbm_stats;
 
+/* Instrumentation (no reference counterpart; the reference's times dict,
+ * E:3226-3240, holds wall times only). */
 int gbm_set_profiling(gbm_ctx *ctx, int32_t on);
 int gbm_get_stats(gbm_ctx *ctx, gbm_stats *out);
 int gbm_reset_stats(gbm_ctx *ctx);
@@ -347,7 +361,9 @@ int gbm_reset_stats(gbm_ctx *ctx);
  * which evicts the L2 cache between timed rounds; its device time is
  * reported in gbm_stats.flush_ms while profiling is on.  0 turns it off. */
 int gbm_set_l2_flush(gbm_ctx *ctx, int64_t bytes);
-/* CUDA events on the context's stream (slots 0..15), for timing regions. */
+/* CUDA events on the context's stream (slots 0..15), for timing regions
+ * (no reference counterpart; the reference times with perf_counter,
+ * E:3226-3240). */
 int gbm_event_record(gbm_ctx *ctx, int32_t slot);
 int gbm_event_elapsed(gbm_ctx *ctx, int32_t a, int32_t b, float *ms);
 
@@ -361,11 +377,14 @@ int gbm_event_elapsed(gbm_ctx *ctx, int32_t a, int32_t b, float *ms);
 int gbm_sampler_create(uint32_t seed, int64_t n, int32_t p, int64_t n_sub, int32_t n_feat,
                        int32_t subsample_on, int32_t colsample_on, int32_t look_ahead,
                        gbm_sampler **out);
-/* Any output may be NULL: sample_idx [n_sub] (reference order),
- * inbag_mask [n] (1 = in bag), feat_idx [n_feat]. */
+/* The next round's draw of _get_subsample_indices (E:2502-2517).  Any output
+ * may be NULL: sample_idx [n_sub] (reference order), inbag_mask [n] (1 = in
+ * bag), feat_idx [n_feat]. */
 int gbm_sampler_next(gbm_sampler *s, int64_t *sample_idx, uint8_t *inbag_mask, int32_t *feat_idx);
 /* The next round as int32 row ids [n_sub] (reference order) + feat_idx. */
 int gbm_sampler_next_rows(gbm_sampler *s, int32_t *sample_rows, int32_t *feat_idx);
+/* The sizes the sampler was made with (n_sub = int(n * subsample), n_feat =
+ * int(p * colsample_bytree), E:2502-2517), and its destruction. */
 int64_t gbm_sampler_n_sub(const gbm_sampler *s);
 int32_t gbm_sampler_n_feat(const gbm_sampler *s);
 void gbm_sampler_destroy(gbm_sampler *s);
