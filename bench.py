@@ -540,6 +540,37 @@ def run_engine(args):
         dist.destroy_process_group()
 
 
+def run_predict_only(args):
+    """--part predict: only the predict leg (for profiling k_predict): 1000
+    full depth-8 random trees (config 5's ensemble) over --predict-rows rows
+    of uint8 bins with the workload's feature count, rows and ensemble
+    resident on the device; prints one JSON line with rows/s."""
+    import torch
+    from bsscl_gbm_b200 import Engine, datasets
+    c = CFG
+    p = c["p"]
+    n = args.predict_rows
+    Xb = np.random.default_rng(5).integers(0, 256, size=(n, p)).astype(np.uint8)
+    eng = Engine(0)
+    ens = datasets.config5_ensemble(n_trees=1000, depth=8, p=p, seed=5)
+    eng.predict_set_model(ens, 1000, p)
+    eng.predict_upload(Xb)
+    for _ in range(max(1, args.warmup)):
+        eng.predict_run(c["lr"], 0.0)
+    eng.sync()
+    torch.cuda.nvtx.range_push("bench_predict")
+    eng.event(4)
+    for _ in range(args.steps):
+        eng.predict_run(c["lr"], 0.0)
+    eng.event(5)
+    torch.cuda.nvtx.range_pop()
+    ms = eng.elapsed_ms(4, 5) / args.steps
+    print(json.dumps({"part": "predict", "rows": n, "features": p, "trees": 1000, "depth": 8,
+                      "ms_per_launch": ms, "rows_per_s": n / (ms / 1000.0),
+                      "node_visits_per_s": n * 8000 / (ms / 1000.0)}), flush=True)
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -550,11 +581,16 @@ def main():
     ap.add_argument("--config", default="4", choices=sorted(CONFIGS),
                     help="4 (default): the headline, 1M x 100 depth 6; 5: 10M x 200 depth 10")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--part", default="all", choices=["all", "predict"],
+                    help="predict: time only the ensemble predict (k_predict), for profiling")
+    ap.add_argument("--predict-rows", type=int, default=1_000_000)
     args = ap.parse_args()
     global CFG, METRIC
     CFG = CONFIGS[args.config]
     METRIC = CFG["metric"]
-    if args.impl == "reference":
+    if args.part == "predict":
+        run_predict_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_engine(args)

@@ -34,6 +34,7 @@ EXPORTS = (
     "gbm_set_l2_flush", "gbm_bin_edges", "gbm_upload_binned_rows", "gbm_bin_features",
     "gbm_predict_upload_raw", "gbm_predict_raw", "gbm_test_peer_wait", "gbm_upload_labels_mc",
     "gbm_round_mc", "gbm_get_F_mc", "gbm_get_grad_mc", "gbm_upload_targets", "gbm_round_reg",
+    "gbm_check_model",
 )
 
 
@@ -146,12 +147,27 @@ def lib():
     L.gbm_round_reg.argtypes = [P, P, P, i32, C.POINTER(GbmParams), C.POINTER(GbmTreeOut), C.POINTER(C.c_double)]
     L.gbm_predict_noalloc.argtypes = [P, i64, i32, P, P, P, P, P, P, i32, i32, f64, f64, P, P, P,
                                       C.c_char_p, i32]
+    L.gbm_check_model.argtypes = [C.POINTER(GbmPacked), i32, C.c_char_p, i32]
     _lib = L
     return L
 
 
 def ptr(a):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def check_model(packed, n_trees, n_features):
+    """Host-side checks of a packed ensemble (gbm_check_model): raises
+    ValueError with the library's message when a walk could leave its tree
+    (offsets not starting at 0 or not increasing, a child not after its
+    parent or outside its tree, a feature >= n_features, a negative
+    threshold).  Needs no GPU."""
+    L = lib()
+    s, keep = Engine.packed_struct(packed, n_trees)
+    buf = C.create_string_buffer(256)
+    rc = L.gbm_check_model(C.byref(s), int(n_features), buf, 256)
+    if rc != GBM_OK:
+        raise ValueError(f"gbm_check_model: {buf.value.decode()} ({ERRORS.get(rc, rc)})")
 
 
 class Engine:

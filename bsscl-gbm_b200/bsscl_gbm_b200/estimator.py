@@ -746,7 +746,7 @@ class HybridHistGBMNumbaV1_0_1:
                 "values": self._packed_values, "left": self._packed_left,
                 "right": self._packed_right, "offsets": self._tree_offsets}
 
-    def predict_proba(self, X):
+    def _prep_X(self, X):
         try:
             import scipy.sparse
             if scipy.sparse.issparse(X):
@@ -761,8 +761,11 @@ class HybridHistGBMNumbaV1_0_1:
         if X.ndim != 2 or X.shape[1] != self.n_features_in_:
             raise ValueError(f"X has shape {X.shape}; the model has {self.n_features_in_} features")
         self._check_device_bins()
-        # rows are binned on the GPU (gbm_predict_raw) and go straight to the ensemble
-        t0 = time.perf_counter()
+        return X
+
+    def _proba_rows(self, X):
+        """predict_proba of the rows of X on this rank's GPU: the rows are
+        binned on the GPU (gbm_predict_raw) and go straight to the ensemble."""
         eng = self._get_engine()
         if self._is_multiclass:
             # K ensembles over the same binned rows, then the softmax (E:3290-3310, E:2328-2332)
@@ -772,13 +775,39 @@ class HybridHistGBMNumbaV1_0_1:
                 eng.predict_set_model(self._mc_packed[k], len(self.mc_trees[k]), X.shape[1])
                 eng.predict_run(self.learning_rate, 0.0)
                 F[:, k] = eng.predict_fetch(want_F=True, want_proba=False)[0]
-            self.times['inference'] = (time.perf_counter() - t0) * 1000
             return _softmax(F)
         _, proba = eng.predict_raw(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id,
                                    self._packed(), len(self.trees), self.learning_rate,
                                    getattr(self, 'base_score_', 0.0), want_F=False, want_proba=True)
-        self.times['inference'] = (time.perf_counter() - t0) * 1000
         return np.column_stack([1 - proba, proba])
+
+    def predict_proba(self, X):
+        """predict_proba (E:3274-3336).  With torch.distributed running more
+        than one rank, every rank passes the same X, predicts only its own
+        contiguous block of rows on its own GPU (the ensemble is replicated;
+        the walk needs no exchange), and the blocks are then all-gathered so
+        every rank returns every row's probabilities.  predict_proba_local
+        skips that gather."""
+        X = self._prep_X(X)
+        t0 = time.perf_counter()
+        dist = _dist()
+        if dist is None:
+            out = self._proba_rows(X)
+        else:
+            lo, hi = _rank_rows(X.shape[0])
+            out = _gather_rows(dist, self._proba_rows(X[lo:hi]), X.shape[0])
+        self.times['inference'] = (time.perf_counter() - t0) * 1000
+        return out
+
+    def predict_proba_local(self, X):
+        """This rank's block of rows of X (``_rank_rows``), predicted on this
+        rank's GPU with no communication at all: ``(lo, hi, proba[hi - lo])``.
+        The reference's parallel predict (predict_batch_parallel,
+        E:3842-3883) splits rows over worker processes the same way; without
+        torch.distributed the block is every row."""
+        X = self._prep_X(X)
+        lo, hi = _rank_rows(X.shape[0])
+        return lo, hi, self._proba_rows(X[lo:hi])
 
     def predict_proba_binned(self, X_bin):
         """``predict_proba`` on bin ids already produced with this model's edges."""
@@ -792,15 +821,14 @@ class HybridHistGBMNumbaV1_0_1:
 
     def predict(self, X):
         if self.objective == 'regression':   # init score + the ensemble (E:3352-3360)
-            X = np.asarray(X)
-            if not np.issubdtype(X.dtype, np.floating) or X.dtype == np.float16:
-                X = X.astype(np.float64)
-            self._check_device_bins()
+            X = self._prep_X(X)
             eng = self._get_engine()
-            F, _ = eng.predict_raw(X, self.bin_edges, self.feature_bin_counts, self._nan_bin_id,
+            dist = _dist()
+            lo, hi = _rank_rows(X.shape[0])   # row-sharded like predict_proba
+            F, _ = eng.predict_raw(X[lo:hi], self.bin_edges, self.feature_bin_counts, self._nan_bin_id,
                                    self._packed(), len(self.trees), self.learning_rate,
                                    self.init_score_, want_F=True, want_proba=False)
-            return F
+            return F if dist is None else _gather_rows(dist, F[:, None], X.shape[0])[:, 0]
         proba = self.predict_proba(X)
         if self._is_multiclass:
             return self.classes_[np.argmax(proba, axis=1)]
@@ -984,6 +1012,25 @@ def _rank_rows(n):
         return 0, n
     ws, rk = dist.get_world_size(), dist.get_rank()
     return (n * rk) // ws, (n * (rk + 1)) // ws
+
+
+def _gather_rows(dist, local, n):
+    """Every rank's block of rows (``_rank_rows`` order) of a float64 [m, k]
+    array, all-gathered so each rank holds all n rows.  Only the results
+    travel: blocks are padded to the largest block and exchanged as one
+    tensor (on this rank's GPU under NCCL, on the host under gloo)."""
+    import torch
+    ws = dist.get_world_size()
+    k = local.shape[1]
+    bounds = [((n * r) // ws, (n * (r + 1)) // ws) for r in range(ws)]
+    m = max(h - l for l, h in bounds)
+    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend() == "nccl" else torch.device("cpu")
+    buf = torch.zeros((m, k), dtype=torch.float64, device=dev)
+    buf[:local.shape[0]] = torch.from_numpy(np.ascontiguousarray(local)).to(dev)
+    allb = torch.empty((ws * m, k), dtype=torch.float64, device=dev)
+    dist.all_gather_into_tensor(allb, buf)
+    allb = allb.cpu().numpy()
+    return np.concatenate([allb[r * m:r * m + (h - l)] for r, (l, h) in enumerate(bounds)], axis=0)
 
 
 def _predict_tree_host(X_bin, tree):

@@ -192,9 +192,12 @@ struct gbm_ctx {
     uint8_t *d_px = nullptr;
     int64_t pn = 0, pn_cap = 0;
     int32_t pp = 0;
-    PNode *d_pnodes = nullptr;
+    uint8_t *d_pnodes = nullptr;    // PNode [total], or the 32-bit breadth-first words when p_packed
+    bool p_packed = false;
     double *d_pvals = nullptr;
     int32_t *d_poff = nullptr;
+    int4 *d_pchunk = nullptr;       // [p_trees_cap] chunks of whole trees, then the chunk count
+    int32_t *d_pdep = nullptr;      // [p_trees_cap] tree depths (the packed format)
     int32_t p_ntree = 0;
     int64_t p_nodes_cap = 0;
     int32_t p_trees_cap = 0;
@@ -384,6 +387,154 @@ int halloc(gbm_ctx *ctx, T **p, size_t count) {
         return fail(ctx, GBM_ERR_ALLOC, "cudaMallocHost(%zu bytes) failed: %s", bytes, cudaGetErrorString(e));
     ctx->hcap[(void *)*p] = bytes;
     return GBM_OK;
+}
+
+// ---- predict ---------------------------------------------------------------
+
+// A packed ensemble (_pack_tree_list's arrays, E:2192-2216) -> 8-byte nodes
+// and values, with every check that keeps the device walk inside its tree:
+// offsets start at 0 and increase (no empty tree), trees hold at most 32767
+// nodes, an internal node's feature is below n_features, its threshold is
+// not negative (above 255 it is read as 255: every uint8 bin goes left, as
+// the reference's compare does), and its children lie after it inside its
+// tree, so every walk ends.  Nothing is uploaded when a check fails.
+int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::vector<PNode> &nodes,
+               std::vector<double> &vals, std::vector<uint32_t> *n32 = nullptr, std::vector<double> *v32 = nullptr,
+               std::vector<int32_t> *dep32 = nullptr) {
+    auto bad = [&err](int code, const char *fmt, auto... a) {
+        char buf[256];
+        snprintf(buf, sizeof buf, fmt, a...);
+        err = buf;
+        return code;
+    };
+    const int32_t T = m->n_trees;
+    if (m->offsets[0] != 0) return bad(GBM_ERR_ARG, "model offsets start at %d, not 0", m->offsets[0]);
+    for (int32_t t = 0; t < T; t++) {
+        const int32_t o = m->offsets[t], o1 = m->offsets[t + 1];
+        if (o1 <= o) return bad(GBM_ERR_ARG, "tree %d is empty or its offsets decrease (%d -> %d)", t, o, o1);
+        if (o1 - o > 32767) return bad(GBM_ERR_UNSUPPORTED, "tree %d has %d nodes (at most 32767)", t, o1 - o);
+    }
+    const int64_t total = m->offsets[T];
+    if (total > 0 && (!m->features || !m->thresholds || !m->values || !m->left || !m->right))
+        return bad(GBM_ERR_ARG, "%s", "model arrays missing");
+    nodes.assign((size_t)std::max<int64_t>(total, 1), PNode{-1, 0, 0, 0, 0});
+    vals.assign((size_t)std::max<int64_t>(total, 1), 0.0);
+    for (int32_t t = 0; t < T; t++) {
+        const int32_t o = m->offsets[t], o1 = m->offsets[t + 1], sz = o1 - o;
+        for (int32_t k = o; k < o1; k++) {
+            PNode nd{-1, 0, 0, 0, 0};
+            const int f = m->features[k];
+            if (f >= 0) {
+                const int64_t th = m->thresholds[k];
+                const int32_t l = m->left[k], r = m->right[k], kk = k - o;
+                if (f >= n_features) return bad(GBM_ERR_ARG, "tree %d node %d: feature %d >= %d", t, kk, f, n_features);
+                if (th < 0) return bad(GBM_ERR_UNSUPPORTED, "tree %d node %d: negative threshold", t, kk);
+                if (l <= kk || l >= sz || r <= kk || r >= sz)
+                    return bad(GBM_ERR_ARG, "tree %d node %d: children %d/%d must lie after the node inside the "
+                                "tree (%d nodes)", t, kk, l, r, sz);
+                nd.feat = (int16_t)f;
+                nd.thr = (uint8_t)(th > 255 ? 255 : th);
+                nd.left = (int16_t)l;
+                nd.right = (int16_t)r;
+            }
+            nodes[(size_t)k] = nd;
+            vals[(size_t)k] = m->values[k];
+        }
+    }
+    if (n32 && v32 && dep32) {
+        // the 32-bit breadth-first form (k_predict's PACKED format): every
+        // tree renumbered so that a node's children are adjacent, each leaf
+        // pointing at itself with threshold 255, and the tree's depth; only
+        // when features fit 12 bits and every tree (as reached from its root)
+        // fits 4096 nodes, else *n32 stays empty
+        n32->clear();
+        v32->clear();
+        dep32->clear();
+        if (n_features > 4096) return GBM_OK;
+        std::vector<uint32_t> a((size_t)std::max<int64_t>(total, 1), 0u);
+        std::vector<double> b((size_t)std::max<int64_t>(total, 1), 0.0);
+        std::vector<int32_t> d((size_t)std::max<int32_t>(T, 1), 0);
+        std::vector<int32_t> order, nid, lev;
+        for (int32_t t = 0; t < T; t++) {
+            const int32_t o = m->offsets[t], sz = m->offsets[t + 1] - o;
+            if (sz > 4096) return GBM_OK;
+            order.assign(1, 0);
+            nid.assign(1, 0);     // nid[i]: the new id of order[i]; lev[i]: its depth
+            lev.assign(1, 0);
+            int32_t next = 1, depth = 0;
+            for (size_t h = 0; h < order.size(); h++) {
+                const int32_t k = order[h];
+                const PNode &nd = nodes[(size_t)(o + k)];
+                uint32_t w = (255u << 12) | (uint32_t)nid[h];   // a leaf: no bin is above 255
+                if (nd.feat >= 0) {
+                    if (next + 1 >= sz) return GBM_OK;   // more nodes than the tree holds (shared children)
+                    w = ((uint32_t)nd.feat << 20) | ((uint32_t)nd.thr << 12) | (uint32_t)next;
+                    order.push_back(nd.left);
+                    nid.push_back(next);
+                    lev.push_back(lev[h] + 1);
+                    order.push_back(nd.right);
+                    nid.push_back(next + 1);
+                    lev.push_back(lev[h] + 1);
+                    next += 2;
+                    depth = std::max(depth, lev[h] + 1);
+                }
+                a[(size_t)(o + nid[h])] = w;
+                b[(size_t)(o + nid[h])] = vals[(size_t)(o + k)];
+            }
+            d[(size_t)t] = depth;
+        }
+        n32->swap(a);
+        v32->swap(b);
+        dep32->swap(d);
+    }
+    return GBM_OK;
+}
+
+// k_predict's shape for p features: two rows per thread (512 per CTA) while
+// the row tile stays within 52 KB, so two CTAs share an SM; else one row per
+// thread, and fewer rows per CTA when 256 rows of p bytes do not fit.
+struct PredShape {
+    int rpt, rpc, stage_rows;
+    size_t smem;
+};
+
+PredShape predict_shape(int p, bool packed) {
+    if (predict_smem(2 * kPredThreads, p, packed) - predict_smem(0, p, packed) <= 52 * 1024)
+        return {2, 2 * kPredThreads, 1, predict_smem(2 * kPredThreads, p, packed)};
+    const size_t room = 227 * 1024 - predict_smem(0, p, packed);
+    const size_t per32 = predict_smem(32, p, packed) - predict_smem(0, p, packed);
+    const int rpc = (int)std::min<size_t>(kPredThreads, room / per32 * 32);
+    if (rpc < 32) return {1, kPredThreads, 0, predict_smem(0, p, packed)};   // rows read from global memory
+    return {1, rpc, 1, predict_smem(rpc, p, packed)};
+}
+
+template <int RPT, bool PK, bool SR>
+cudaError_t launch_predict_t(const PredShape &sh, unsigned grid, const uint8_t *xr, int64_t n, int p,
+                             const void *nodes, const double *vals, const int32_t *off, const int32_t *dep, int ntree,
+                             const int4 *cstart, const int32_t *nchunk, double lr, double base, double *F,
+                             double *P, cudaStream_t st) {
+    cudaError_t e = cudaFuncSetAttribute(k_predict<RPT, PK, SR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sh.smem);
+    if (e != cudaSuccess) return e;
+    k_predict<RPT, PK, SR><<<grid, kPredThreads, sh.smem, st>>>(xr, n, p, nodes, vals, off, dep, ntree, cstart,
+                                                                 nchunk, sh.rpc, lr, base, F, P);
+    return cudaGetLastError();
+}
+
+// The ensemble over n rows (row-major bins [n][p]); chunk starts and count
+// were written by k_pred_chunks.  `packed`: nodes are 32-bit breadth-first
+// words with per-tree depths `dep` (pack_model), else PNode (dep unused).
+// Allocates nothing.
+cudaError_t launch_predict(const uint8_t *xr, int64_t n, int p, const void *nodes, bool packed, const double *vals,
+                           const int32_t *off, const int32_t *dep, int ntree, const int4 *cstart,
+                           const int32_t *nchunk, double lr, double base, double *F, double *P, cudaStream_t st) {
+    const PredShape sh = predict_shape(p, packed);
+    const unsigned grid = (unsigned)((n + sh.rpc - 1) / sh.rpc);
+#define GBM_PRED(R, K, S) launch_predict_t<R, K, S>(sh, grid, xr, n, p, nodes, vals, off, dep, ntree, cstart, nchunk, lr, base, F, P, st)
+    if (sh.rpt == 2) return packed ? GBM_PRED(2, true, true) : GBM_PRED(2, false, true);
+    if (sh.stage_rows) return packed ? GBM_PRED(1, true, true) : GBM_PRED(1, false, true);
+    return packed ? GBM_PRED(1, true, false) : GBM_PRED(1, false, false);
+#undef GBM_PRED
 }
 
 int grid_for(int64_t work, int threads, int cap = 1 << 30) {
@@ -1729,7 +1880,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
                         ctx->d_ptask, ctx->d_tile_cnt, ctx->d_nleft,
                         ctx->d_count64, ctx->d_nodes, ctx->d_lvl[0], ctx->d_lvl[1], ctx->d_ints, ctx->d_tree,
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
-                        ctx->d_poff, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,
+                        ctx->d_poff, ctx->d_pchunk, ctx->d_pdep, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,
                         ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi, ctx->d_side,
                         ctx->d_upstage, ctx->d_Fmc, ctx->d_wmc, ctx->d_qmc, ctx->d_yr,
                         ctx->d_gmax_part, ctx->d_gmax, ctx->d_stab};
@@ -2391,47 +2542,58 @@ int gbm_test_peer_wait(int32_t device, int32_t timeout_ms) {
 
 // ---- predict ------------------------------------------------------------------
 
-int gbm_predict_set_model(gbm_ctx *ctx, const gbm_packed *m, int32_t n_features) {
-    if (!ctx || !m || m->n_trees < 0 || !m->offsets) return GBM_ERR_ARG;
-    if (ctx->dev < 0) return GBM_ERR_STATE;
-    CK(cudaSetDevice(ctx->dev));
-    int32_t T = m->n_trees;
-    int64_t total = m->offsets[T];
-    std::vector<PNode> nodes((size_t)std::max<int64_t>(total, 1));
-    std::vector<double> vals((size_t)std::max<int64_t>(total, 1));
-    for (int32_t t = 0; t < T; t++) {
-        int32_t o = m->offsets[t], o1 = m->offsets[t + 1];
-        if (o1 - o > 32767 || o1 < o) return fail(ctx, GBM_ERR_UNSUPPORTED, "tree %d has %d nodes", t, o1 - o);
-        for (int32_t k = o; k < o1; k++) {
-            PNode nd;
-            nd.feat = m->features[k];
-            int64_t th = m->thresholds[k];
-            nd.thr = (uint8_t)(th < 0 ? 0 : (th > 255 ? 255 : th));
-            nd.pad = 0;
-            nd.left = (int16_t)m->left[k];
-            nd.right = (int16_t)m->right[k];
-            if (nd.feat >= 0) {
-                if (nd.feat >= n_features) return fail(ctx, GBM_ERR_ARG, "node feature %d >= %d", nd.feat, n_features);
-                if (th < 0) return fail(ctx, GBM_ERR_UNSUPPORTED, "negative threshold");
-                if (m->left[k] < 0 || m->left[k] >= o1 - o || m->right[k] < 0 || m->right[k] >= o1 - o)
-                    return fail(ctx, GBM_ERR_ARG, "tree %d node %d has an out-of-range child", t, k - o);
-            }
-            nodes[(size_t)k] = nd;
-            vals[(size_t)k] = m->values[k];
-        }
+int gbm_check_model(const gbm_packed *m, int32_t n_features, char *errbuf, int32_t errlen) {
+    if (!m || m->n_trees < 0 || !m->offsets || n_features <= 0) {
+        if (errbuf && errlen > 0) snprintf(errbuf, (size_t)errlen, "null model or empty size");
+        return GBM_ERR_ARG;
     }
+    std::vector<PNode> nodes;
+    std::vector<double> vals;
+    std::string err;
+    int rc = pack_model(err, m, n_features, nodes, vals);
+    if (rc && errbuf && errlen > 0) snprintf(errbuf, (size_t)errlen, "%s", err.c_str());
+    return rc;
+}
+
+int gbm_predict_set_model(gbm_ctx *ctx, const gbm_packed *m, int32_t n_features) {
+    if (!ctx || !m || m->n_trees < 0 || !m->offsets || n_features <= 0) return GBM_ERR_ARG;
+    if (ctx->dev < 0) return GBM_ERR_STATE;
+    int32_t T = m->n_trees;
+    std::vector<PNode> nodes;
+    std::vector<double> vals;
+    std::vector<uint32_t> n32;
+    std::vector<double> v32;
+    std::vector<int32_t> dep;
+    std::string err;
+    if (int rc = pack_model(err, m, n_features, nodes, vals, &n32, &v32, &dep)) return fail(ctx, rc, "%s", err.c_str());
+    CK(cudaSetDevice(ctx->dev));
+    int64_t total = (int64_t)nodes.size();
     if (total > ctx->p_nodes_cap) {
-        TRY(dalloc(ctx, &ctx->d_pnodes, (size_t)total));
+        TRY(dalloc(ctx, &ctx->d_pnodes, (size_t)total * sizeof(PNode)));
         TRY(dalloc(ctx, &ctx->d_pvals, (size_t)total));
         ctx->p_nodes_cap = total;
     }
     if (T + 1 > ctx->p_trees_cap) {
         TRY(dalloc(ctx, &ctx->d_poff, (size_t)T + 1));
+        TRY(dalloc(ctx, &ctx->d_pchunk, (size_t)T + 2));   // the count sits in the last int4
+        TRY(dalloc(ctx, &ctx->d_pdep, (size_t)T + 1));
         ctx->p_trees_cap = T + 1;
     }
-    CK(cudaMemcpyAsync(ctx->d_pnodes, nodes.data(), sizeof(PNode) * total, cudaMemcpyHostToDevice, ctx->st));
-    CK(cudaMemcpyAsync(ctx->d_pvals, vals.data(), sizeof(double) * total, cudaMemcpyHostToDevice, ctx->st));
+    ctx->p_packed = !n32.empty();
+    if (ctx->p_packed) {
+        CK(cudaMemcpyAsync(ctx->d_pnodes, n32.data(), sizeof(uint32_t) * total, cudaMemcpyHostToDevice, ctx->st));
+        CK(cudaMemcpyAsync(ctx->d_pvals, v32.data(), sizeof(double) * total, cudaMemcpyHostToDevice, ctx->st));
+        if (T > 0)
+            CK(cudaMemcpyAsync(ctx->d_pdep, dep.data(), sizeof(int32_t) * T, cudaMemcpyHostToDevice, ctx->st));
+    } else {
+        CK(cudaMemcpyAsync(ctx->d_pnodes, nodes.data(), sizeof(PNode) * total, cudaMemcpyHostToDevice, ctx->st));
+        CK(cudaMemcpyAsync(ctx->d_pvals, vals.data(), sizeof(double) * total, cudaMemcpyHostToDevice, ctx->st));
+    }
     CK(cudaMemcpyAsync(ctx->d_poff, m->offsets, sizeof(int32_t) * (T + 1), cudaMemcpyHostToDevice, ctx->st));
+    // the ensemble's chunks of whole trees, cut once per model on the device
+    k_pred_chunks<<<1, 32, 0, ctx->st>>>(ctx->d_poff, T, ctx->d_pchunk,
+                                         reinterpret_cast<int32_t *>(ctx->d_pchunk + T + 1));
+    CKL();
     ctx->p_ntree = T;
     ctx->p_nfeat = n_features;
     return sync_stream(ctx);
@@ -2488,9 +2650,11 @@ int gbm_predict_run(gbm_ctx *ctx, double lr, double base) {
     if (!ctx) return GBM_ERR_ARG;
     if (!ctx->d_px || !ctx->d_poff) return fail(ctx, GBM_ERR_STATE, "upload a model and rows first");
     CK(cudaSetDevice(ctx->dev));
-    k_predict<<<grid_for(ctx->pn, 256), 256, 0, ctx->st>>>(ctx->d_px, ctx->pn, ctx->pp, ctx->d_pnodes, ctx->d_pvals,
-                                                          ctx->d_poff, ctx->p_ntree, lr, base, ctx->d_pF, ctx->d_pP);
-    CKL();
+    CK(launch_predict(ctx->d_px, ctx->pn, ctx->pp, ctx->d_pnodes, ctx->p_packed, ctx->d_pvals, ctx->d_poff,
+                      ctx->d_pdep, ctx->p_ntree, ctx->d_pchunk,
+                      reinterpret_cast<const int32_t *>(ctx->d_pchunk + ctx->p_ntree + 1), lr, base, ctx->d_pF,
+                      ctx->d_pP, ctx->st));
+    ctx->launches++;
     return GBM_OK;
 }
 
@@ -2608,9 +2772,12 @@ int gbm_event_elapsed(gbm_ctx *ctx, int32_t a, int32_t b, float *ms) {
 namespace {
 
 constexpr int kNoAllocMaxNodes = 1 << 19;   // 524,288 nodes: 1000 full depth-8 trees fit
+constexpr int kNoAllocMaxTrees = 1 << 16;   // 65,536 trees
 
 struct NoAllocScratch {
     PNode nodes[kNoAllocMaxNodes];
+    int4 chunks[kNoAllocMaxTrees + 1];      // the walk's chunks of whole trees
+    int32_t nchunk;
     int bad;          // set by the conversion kernel when the model is malformed
 };
 
@@ -2687,10 +2854,10 @@ int gbm_predict_noalloc(const uint8_t *xbin_dev, int64_t n, int32_t p, const int
     if (!xbin_dev || n <= 0 || p <= 0 || n_trees <= 0 || !features_dev || !thresholds_dev || !values_dev ||
         !left_dev || !right_dev || !offsets_dev || (!F_dev && !proba_dev))
         return noalloc_fail(errbuf, errlen, GBM_ERR_ARG, "gbm_predict_noalloc: null pointer or empty size");
-    if (n_nodes <= 0 || n_nodes > kNoAllocMaxNodes) {
-        char m[160];
-        snprintf(m, sizeof m, "gbm_predict_noalloc: %d nodes; the fixed scratch holds at most %d", n_nodes,
-                 kNoAllocMaxNodes);
+    if (n_nodes <= 0 || n_nodes > kNoAllocMaxNodes || n_trees > kNoAllocMaxTrees) {
+        char m[200];
+        snprintf(m, sizeof m, "gbm_predict_noalloc: %d trees of %d nodes; the fixed scratch holds at most %d trees "
+                 "and %d nodes", n_trees, n_nodes, kNoAllocMaxTrees, kNoAllocMaxNodes);
         return noalloc_fail(errbuf, errlen, GBM_ERR_ARG, m);
     }
     int dev = -1;
@@ -2725,9 +2892,14 @@ int gbm_predict_noalloc(const uint8_t *xbin_dev, int64_t n, int32_t p, const int
         return noalloc_fail(errbuf, errlen, GBM_ERR_ARG,
                             "gbm_predict_noalloc: malformed ensemble (offsets, feature, threshold or child out "
                             "of range, or a child not after its parent)");
-    k_predict<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(xbin_dev, n, p, sc->nodes, values_dev, offsets_dev,
-                                                          n_trees, learning_rate, base_score, F_dev, proba_dev);
+    k_pred_chunks<<<1, 32, 0, st>>>(offsets_dev, n_trees, sc->chunks, &sc->nchunk);
     e = cudaGetLastError();
+    // the walk is bounded by each tree's own size (from offsets_dev, checked
+    // above), so a call that overlaps this one and rewrites the shared nodes
+    // can make this one's output wrong but cannot send it outside the arrays
+    if (e == cudaSuccess)
+        e = launch_predict(xbin_dev, n, p, sc->nodes, false, values_dev, offsets_dev, nullptr, n_trees, sc->chunks,
+                           &sc->nchunk, learning_rate, base_score, F_dev, proba_dev, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return noalloc_fail(errbuf, errlen, GBM_ERR_CUDA, cudaGetErrorString(e));
     return GBM_OK;

@@ -2189,31 +2189,265 @@ k_replay_depth(const DNode *__restrict__ nodes, const int *__restrict__ node_cou
 // predict (ensemble traversal, E:863-884)
 // ===========================================================================
 
-__global__ void __launch_bounds__(256)
-k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const PNode *__restrict__ nodes,
-          const double *__restrict__ vals, const int32_t *__restrict__ off, int ntree, double lr,
-          double base, double *__restrict__ F, double *__restrict__ proba) {
-    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const uint8_t *row = xr + i * p;
-    double acc = 0.0;
-    for (int t = 0; t < ntree; t++) {
-        int o = __ldg(off + t);
-        int node = 0;
-        PNode nd = nodes[o];
-        while (nd.feat >= 0) {
-            int b = __ldg(row + nd.feat);
-            node = b <= nd.thr ? nd.left : nd.right;
-            nd = nodes[o + node];
+// The ensemble is walked in chunks of whole consecutive trees that fit the
+// shared-memory node buffer (kPredChunkNodes nodes, at most kPredChunkTrees
+// trees).  k_pred_chunks cuts the trees into chunks greedily with one warp
+// that tests 32 offsets per step, and writes each chunk as {first tree, end
+// tree, first node, node count}; a tree larger than the buffer is a chunk of
+// its own and is walked from global memory.
+constexpr int kPredThreads = 256;
+constexpr int kPredChunkNodes = 2048;
+constexpr int kPredChunkTrees = 512;
+
+__global__ void k_pred_chunks(const int32_t *__restrict__ off, int ntree, int4 *__restrict__ chunks,
+                              int32_t *__restrict__ nchunk) {
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    int t0 = 0, nc = 0;
+    while (t0 < ntree) {
+        const int base = __ldg(off + t0);
+        int t1 = -1;
+        for (int j = t0 + 1; t1 < 0; j += 32) {
+            const int t = j + lane;
+            // the first t that does not fit: chunk [t0, t) is then maximal
+            bool stop = t > ntree || t - t0 > kPredChunkTrees || __ldg(off + t) - base > kPredChunkNodes;
+            unsigned b = __ballot_sync(0xffffffffu, stop);
+            if (b) t1 = j + __ffs(b) - 1;
         }
-        acc = __dadd_rn(acc, __dmul_rn(lr, __ldg(vals + o + node)));
+        t1 = max(t1 - 1, t0 + 1);
+        if (lane == 0) chunks[nc] = make_int4(t0, t1, base, __ldg(off + t1) - base);
+        nc++;
+        t0 = t1;
     }
-    double f = __dadd_rn(acc, base);
-    if (F) F[i] = f;
-    if (proba) {
-        double c = fmin(fmax(f, -500.0), 500.0);
-        proba[i] = __ddiv_rn(1.0, __dadd_rn(1.0, exp(-c)));
+    if (lane == 0) *nchunk = nc;
+}
+
+__device__ __forceinline__ void cp_async4(void *sdst, const void *gsrc) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(sdst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *sdst, const void *gsrc) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(sdst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+// One tree for a thread's RPT rows, PACKED format: exactly `dep` steps (a
+// leaf points at itself with threshold 255, so no bin moves it).  `tn` and
+// the rows are shared or global memory as the caller's pointers are; each
+// call site is inlined with a known address space.
+template <int RPT, bool SROWS>
+__device__ __forceinline__ void walk_packed(const uint32_t *__restrict__ tn, int dep, int szm1, int pm1,
+                                            const uint8_t *const *rowp, int *node) {
+    for (int s = 0; s < dep; s++) {
+#pragma unroll
+        for (int j = 0; j < RPT; j++) {
+            const uint32_t w = tn[node[j]];
+            const int f = min((int)(w >> 20), pm1);
+            const int b = SROWS ? rowp[j][((f >> 2) << 7) | (f & 3)] : __ldg(rowp[j] + f);
+            node[j] = min((int)(w & 0xfffu) + (b > (int)((w >> 12) & 0xffu) ? 1 : 0), szm1);
+        }
     }
+}
+
+// The same in the 8-byte PNode format (the reference's numbering): walk
+// until every row is at a leaf, at most szm1 steps.
+template <int RPT, bool SROWS>
+__device__ __forceinline__ void walk_pnode(const PNode *__restrict__ tn, int szm1, int pm1,
+                                           const uint8_t *const *rowp, int *node) {
+    PNode nd[RPT];
+#pragma unroll
+    for (int j = 0; j < RPT; j++) nd[j] = tn[0];
+    for (int s = 0; s < szm1; s++) {
+        bool more = false;
+#pragma unroll
+        for (int j = 0; j < RPT; j++) {
+            if (nd[j].feat >= 0) {
+                const int f = min((int)nd[j].feat, pm1);
+                const int b = SROWS ? rowp[j][((f >> 2) << 7) | (f & 3)] : __ldg(rowp[j] + f);
+                node[j] = min((int)(b <= nd[j].thr ? nd[j].left : nd[j].right), szm1);
+                nd[j] = tn[node[j]];
+                more = true;
+            }
+        }
+        if (!more) break;
+    }
+}
+
+// F[i] = base + sum_t lr * value_t(leaf_t(i)), summed in tree order
+// (predict_all_trees_jit, E:863-884), and proba = sigmoid(clip(F, +-500))
+// (E:3318-3336).
+//
+// A CTA takes rpc <= RPT x 256 consecutive rows.  With SROWS their bins are
+// staged in shared memory once, swizzled so that the 32 lanes of a warp (32
+// consecutive rows) read 32 different banks whatever features they test:
+// byte f of tile row r sits at byte 4 * ((r / 32) * P4 * 32 + r % 32) +
+// 128 * (f / 4) + f % 4 (P4 = ceil(p / 4)); without SROWS (rows too wide for
+// shared memory) the bins are read from the row in global memory.  The
+// chunks of whole trees (nodes, values, offsets, depths) stream through two
+// shared-memory buffers: while the CTA walks chunk c, cp.async copies chunk
+// c + 1 into the other buffer.
+//
+// Node formats.  PACKED: one 32-bit word per node of a tree renumbered
+// breadth-first (pack_model), children adjacent: feature << 20 | threshold
+// << 12 | left child, right = left + 1, and a leaf pointing at itself with
+// threshold 255; every row takes exactly the tree's depth steps with no
+// branch.  Level d of a complete tree is 2^d consecutive words,
+// conflict-free up to level 5.  Otherwise PNode (8 bytes, the reference's
+// own numbering), walked until a leaf.
+//
+// The walk is bounded whatever the node table holds: a feature is clamped
+// below p, a child below the tree's size, and a walk stops after size - 1
+// steps (a valid tree's children come after their parent, so a real walk
+// never needs more).
+template <bool PACKED>
+struct PredBuf {
+    static constexpr int kNodeBytes = PACKED ? 4 : 8;
+    static constexpr size_t kBytes =
+        (sizeof(double) + kNodeBytes) * kPredChunkNodes + 2 * sizeof(int32_t) * (kPredChunkTrees + 4);
+};
+
+template <int RPT, bool PACKED, bool SROWS>
+__global__ void __launch_bounds__(kPredThreads)
+k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const void *__restrict__ nodes_v,
+          const double *__restrict__ vals, const int32_t *__restrict__ off, const int32_t *__restrict__ depth_g,
+          int ntree, const int4 *__restrict__ chunks, const int32_t *__restrict__ nchunk_p, int rpc, double lr,
+          double base, double *__restrict__ F, double *__restrict__ proba) {
+    extern __shared__ __align__(16) unsigned char psm[];
+    constexpr int kNodeBytes = PredBuf<PACKED>::kNodeBytes;
+    constexpr size_t kBuf = PredBuf<PACKED>::kBytes;
+    uint8_t *s_rows = psm + 2 * kBuf;
+    const int64_t r0 = (int64_t)blockIdx.x * rpc;
+    if (r0 >= n) return;
+    const int nr = (int)min(n - r0, (int64_t)min(rpc, kPredThreads * RPT));
+    const int P4 = (p + 3) >> 2;
+    const int nch = min(*nchunk_p, ntree);
+
+    // chunk c's validated bounds; staged when it fits a buffer
+    auto chunk = [&](int c, int &t0, int &t1, int &o0, int &cn) {
+        const int4 d = __ldg(chunks + c);
+        t0 = min(max(d.x, 0), ntree);
+        t1 = min(max(d.y, t0), ntree);
+        o0 = __ldg(off + t0);
+        cn = __ldg(off + t1) - o0;
+        return t1 > t0 && cn <= kPredChunkNodes && t1 - t0 <= kPredChunkTrees;
+    };
+    auto prefetch = [&](int c) {
+        int t0, t1, o0, cn;
+        if (!chunk(c, t0, t1, o0, cn)) return;
+        unsigned char *b = psm + (c & 1) * kBuf;
+        double *s_val = reinterpret_cast<double *>(b);
+        unsigned char *s_nd = b + sizeof(double) * kPredChunkNodes;
+        int32_t *s_off = reinterpret_cast<int32_t *>(s_nd + kNodeBytes * kPredChunkNodes);
+        int32_t *s_dep = s_off + kPredChunkTrees + 4;
+        for (int i = threadIdx.x; i < cn; i += kPredThreads) {
+            if (PACKED)
+                cp_async4(s_nd + 4 * i, reinterpret_cast<const uint32_t *>(nodes_v) + o0 + i);
+            else
+                cp_async8(s_nd + 8 * i, reinterpret_cast<const PNode *>(nodes_v) + o0 + i);
+            cp_async8(s_val + i, vals + o0 + i);
+        }
+        for (int i = threadIdx.x; i <= t1 - t0; i += kPredThreads) cp_async4(s_off + i, off + t0 + i);
+        if (PACKED)
+            for (int i = threadIdx.x; i < t1 - t0; i += kPredThreads) cp_async4(s_dep + i, depth_g + t0 + i);
+    };
+
+    if (nch > 0) prefetch(0);
+    cp_async_commit();
+    if (SROWS) {   // the row tile, swizzled; whole 4-byte words when p % 4 == 0
+        const uint8_t *src = xr + r0 * p;
+        if ((p & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 3) == 0) {
+            const uint32_t *s4 = reinterpret_cast<const uint32_t *>(src);
+            uint32_t *d4 = reinterpret_cast<uint32_t *>(s_rows);
+            const int words = nr * P4;
+            for (int w = threadIdx.x; w < words; w += kPredThreads) {
+                const int r = w / P4, fw = w - r * P4;
+                d4[((r >> 5) * P4 + fw) * 32 + (r & 31)] = __ldg(s4 + w);
+            }
+        } else {
+            const int bytes = nr * p;
+            for (int b = threadIdx.x; b < bytes; b += kPredThreads) {
+                const int r = b / p, f = b - r * p;
+                s_rows[(((r >> 5) * P4 + (f >> 2)) * 32 + (r & 31)) * 4 + (f & 3)] = __ldg(src + b);
+            }
+        }
+    }
+    double acc[RPT];
+    const uint8_t *rowp[RPT];   // the tile's byte base of the row (SROWS), else the row in global memory
+    bool live[RPT];
+#pragma unroll
+    for (int j = 0; j < RPT; j++) {
+        const int r = threadIdx.x + j * kPredThreads;
+        acc[j] = 0.0;
+        live[j] = r < nr;
+        const int rr = live[j] ? r : 0;   // a thread past the tile walks row 0 and writes nothing
+        rowp[j] = SROWS ? s_rows + 4 * ((rr >> 5) * P4 * 32 + (rr & 31)) : xr + (r0 + rr) * p;
+    }
+    const int pm1 = p - 1;
+    for (int c = 0; c < nch; c++) {
+        cp_async_wait_all();
+        __syncthreads();   // chunk c is in its buffer; nobody still reads chunk c - 1's
+        if (c + 1 < nch) prefetch(c + 1);
+        cp_async_commit();
+        int t0, t1, o0, cn;
+        const bool staged = chunk(c, t0, t1, o0, cn);
+        if (t1 <= t0) continue;
+        const unsigned char *b = psm + (c & 1) * kBuf;
+        const double *s_val = reinterpret_cast<const double *>(b);
+        const unsigned char *s_nd = b + sizeof(double) * kPredChunkNodes;
+        const int32_t *s_off = reinterpret_cast<const int32_t *>(s_nd + kNodeBytes * kPredChunkNodes);
+        const int32_t *s_dep = s_off + kPredChunkTrees + 4;
+        for (int t = t0; t < t1; t++) {
+            int node[RPT];
+#pragma unroll
+            for (int j = 0; j < RPT; j++) node[j] = 0;
+            double v[RPT];
+            if (staged) {
+                const int ob = s_off[t - t0] - o0, sz = s_off[t - t0 + 1] - o0 - ob;
+                if (sz <= 0) continue;
+                if (PACKED)
+                    walk_packed<RPT, SROWS>(reinterpret_cast<const uint32_t *>(s_nd) + ob, min(s_dep[t - t0], sz - 1),
+                                            sz - 1, pm1, rowp, node);
+                else
+                    walk_pnode<RPT, SROWS>(reinterpret_cast<const PNode *>(s_nd) + ob, sz - 1, pm1, rowp, node);
+#pragma unroll
+                for (int j = 0; j < RPT; j++) v[j] = s_val[ob + node[j]];
+            } else {
+                const int ob = __ldg(off + t), sz = __ldg(off + t + 1) - ob;
+                if (sz <= 0) continue;
+                if (PACKED)
+                    walk_packed<RPT, SROWS>(reinterpret_cast<const uint32_t *>(nodes_v) + ob,
+                                            min(__ldg(depth_g + t), sz - 1), sz - 1, pm1, rowp, node);
+                else
+                    walk_pnode<RPT, SROWS>(reinterpret_cast<const PNode *>(nodes_v) + ob, sz - 1, pm1, rowp, node);
+#pragma unroll
+                for (int j = 0; j < RPT; j++) v[j] = __ldg(vals + ob + node[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < RPT; j++) acc[j] = __dadd_rn(acc[j], __dmul_rn(lr, v[j]));
+        }
+    }
+    cp_async_wait_all();
+#pragma unroll
+    for (int j = 0; j < RPT; j++) {
+        if (!live[j]) continue;
+        const int64_t i = r0 + threadIdx.x + j * kPredThreads;
+        const double f = __dadd_rn(acc[j], base);
+        if (F) F[i] = f;
+        if (proba) {
+            const double cl = fmin(fmax(f, -500.0), 500.0);
+            proba[i] = __ddiv_rn(1.0, __dadd_rn(1.0, exp(-cl)));
+        }
+    }
+}
+
+// Shared memory of a k_predict launch with rows_per_cta rows of p bytes:
+// two chunk buffers, then the swizzled tile (whole 32-row groups of
+// ceil(p / 4) words).
+inline size_t predict_smem(int rows_per_cta, int p, bool packed) {
+    return 2 * (packed ? PredBuf<true>::kBytes : PredBuf<false>::kBytes) +
+           (size_t)((rows_per_cta + 31) / 32) * 32 * 4 * ((p + 3) / 4);
 }
 
 }  // namespace gbm

@@ -278,6 +278,17 @@ int gbm_predict(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p,
  * same computation as gbm_predict (E:863-884, E:3318-3336), split into its
  * steps. */
 int gbm_predict_set_model(gbm_ctx *ctx, const gbm_packed *model, int32_t n_features);
+
+/* The checks gbm_predict_set_model (and so gbm_predict / gbm_predict_raw)
+ * applies to a packed ensemble before anything is uploaded, on the host
+ * only (no device needed): offsets start at 0 and increase (no empty tree),
+ * a tree holds at most 32767 nodes, and every internal node has a feature
+ * below n_features, a threshold >= 0 and both children after it inside its
+ * tree, so every walk ends.  The reference's predict_all_trees_jit
+ * (E:863-884) trusts its arrays; a malformed model there loops or reads out
+ * of bounds.  Returns GBM_ERR_ARG / GBM_ERR_UNSUPPORTED with a message in
+ * errbuf (optional, errlen bytes). */
+int gbm_check_model(const gbm_packed *model, int32_t n_features, char *errbuf, int32_t errlen);
 int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p);
 int gbm_predict_run(gbm_ctx *ctx, double learning_rate, double base_score);
 int gbm_predict_fetch(gbm_ctx *ctx, double *F_out, double *proba_out);
@@ -304,17 +315,22 @@ int gbm_predict_raw(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t d
  * reads them), the packed ensemble of _pack_tree_list (features int16,
  * thresholds int64, values f64, left/right int32 [n_nodes], offsets int32
  * [n_trees+1]), and F and/or proba f64 [n].  The only scratch -- the
- * ensemble rewritten as 8-byte nodes -- lives in one fixed device array of
- * at most 524,288 nodes (4 MiB) inside this library; every GPU that loads
- * the library holds that array until the process exits.  Larger ensembles
- * are rejected with GBM_ERR_ARG, as are malformed ones (a child that is not
- * after its parent, a feature >= p, a threshold outside 0..255).  The
- * first call on a device looks up the array's device address; make that
- * first call before any stream capture.  All calls share the array, so
- * calls that overlap on the GPU race: serialise them (one stream, or wait
- * between calls).  The call runs on `stream` (a cudaStream_t, NULL = the
- * default stream) of the current device and returns when the outputs are
- * written.  `errbuf` (optional, `errlen` bytes) receives a message. */
+ * ensemble rewritten as 8-byte nodes, and the walk's list of tree chunks --
+ * lives in one fixed device array inside this library, sized for at most
+ * 524,288 nodes and 65,536 trees (about 4.3 MiB); every GPU that loads the
+ * library holds that array until the process exits.  Larger ensembles are
+ * rejected with GBM_ERR_ARG, as are malformed ones (offsets that do not
+ * increase or pass n_nodes, a child that is not after its parent inside its
+ * tree, a feature >= p, a threshold outside 0..255).  The first call on a
+ * device looks up the array's device address; make that first call before
+ * any stream capture.  All calls share the array, so calls that overlap on
+ * the GPU race: serialise them (one stream, or wait between calls).  The
+ * walk is bounded by each tree's size taken from the caller's own offsets,
+ * so an overlapping call can make the outputs wrong but cannot make the
+ * walk loop or read outside the arrays.  The call runs on `stream` (a
+ * cudaStream_t, NULL = the default stream) of the current device,
+ * synchronises that stream and returns when the outputs are written.
+ * `errbuf` (optional, `errlen` bytes) receives a message. */
 int gbm_predict_noalloc(const uint8_t *xbin_dev, int64_t n, int32_t p, const int16_t *features_dev,
                         const int64_t *thresholds_dev, const double *values_dev, const int32_t *left_dev,
                         const int32_t *right_dev, const int32_t *offsets_dev, int32_t n_trees,

@@ -1,0 +1,67 @@
+"""The full-size reference fixtures (tests/golden/fit_full_*.npz), checked on
+the CPU: what the GPU parity tests at the benchmark sizes rely on.
+
+* The oracle's EXACT trajectory recorded in each fixture leaves the
+  reference's trees at the recorded node only, and the audit made there
+  (exact rational gains of both splits on the reference's own round
+  inputs) found an exact tie.
+* The native sampler draws, at the full row counts, the reference's
+  per-round row and feature samples (their SHA-256 hashes).
+* Class weights and base score of the regenerated labels equal the
+  reference's base score.
+"""
+import hashlib
+import ast
+
+import numpy as np
+import pytest
+
+import audit as A
+import oracle as O
+from helpers import golden
+
+CASES = ["cfg4_d6", "cfg4_d8", "cfg2", "cfg3"]
+
+
+def _trees(d, prefix=""):
+    return [tuple(d[prefix + k][t] for k in ("tf", "tt", "tv", "tl", "tr")) + (int(d[prefix + "nc"][t]),
+                                                                              d[prefix + "sg"][t])
+            for t in range(int(d["n_trees"]))]
+
+
+def _labels(name):
+    from bsscl_gbm_b200 import datasets as D
+    if name.startswith("cfg4"):
+        return D.config4(n=1_000_000)[1], 1_000_000, 100
+    if name == "cfg2":
+        return D.config2()[1], 284_807, 30
+    return D.config3()[1], 50_000, 20
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_exact_trajectory_leaves_the_reference_only_at_an_audited_tie(name):
+    d = golden("fit_full_" + name)
+    div = A.first_divergence(_trees(d), _trees(d, "exact_"))
+    if bool(d["has_div"]):
+        assert div == (int(d["div_tree"]), int(d["div_node"]))
+        assert str(d["audit_kind"]) in ("exact_tie", "same_partition")
+    else:
+        assert div is None
+        assert np.abs(d["exact_train_loss"] - d["train_loss"]).max() <= 1e-9
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_sampler_and_base_score_at_full_size(name, built_lib):
+    from bsscl_gbm_b200 import Sampler
+    d = golden("fit_full_" + name)
+    y, n, p = _labels(name)
+    params = ast.literal_eval(str(d["params"]))
+    w2 = O.class_weights(y, params.get("class_weight", "balanced_sqrt"))
+    assert O.base_score(y, w2) == float(d["base_score"])
+    s = Sampler(params["random_state"], n, p, int(n * float(d["subsample"])), int(p * float(d["colsample"])),
+                True, True)
+    for t in range(12):
+        smp, _, feat = s.next(want_sample=True, want_mask=False)
+        assert hashlib.sha256(smp.tobytes()).hexdigest() == str(d["sample_sha"][t]), f"round {t} rows"
+        assert hashlib.sha256(np.ascontiguousarray(feat, np.int32).tobytes()).hexdigest() == str(d["feat_sha"][t])
+    s.close()

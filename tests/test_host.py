@@ -278,6 +278,32 @@ def test_c_abi_rejects_bad_arguments_without_a_device(built_lib):
     assert L.gbm_test_peer_wait(0, 20000) == GBM_ERR_ARG
 
 
+def test_malformed_models_are_rejected_on_the_host(built_lib):
+    """gbm_check_model -- the checks gbm_predict_set_model runs before any
+    upload or launch -- accepts a well-formed ensemble and rejects every
+    model whose walk could loop or leave its tree: a child at or before its
+    parent (a cycle), a child past the tree's end, offsets that start below 0,
+    an empty tree, a feature >= p and a negative threshold."""
+    from bsscl_gbm_b200 import datasets as D
+    from bsscl_gbm_b200._lib import check_model
+    good = D.config5_ensemble(n_trees=4, depth=3, p=10, seed=1)
+    check_model(good, 4, 10)
+
+    def bad(mutate, msg):
+        m = {k: v.copy() for k, v in good.items()}
+        mutate(m)
+        with pytest.raises(ValueError, match=msg):
+            check_model(m, 4, 10)
+
+    bad(lambda m: m["left"].__setitem__(15 + 2, 2), "must lie after")     # tree 1, node 2 -> itself
+    bad(lambda m: m["right"].__setitem__(0, 0), "must lie after")         # root -> root: a cycle
+    bad(lambda m: m["left"].__setitem__(3, 40), "must lie after")         # past the tree's end
+    bad(lambda m: m["offsets"].__setitem__(0, -5), "start at -5")
+    bad(lambda m: m["offsets"].__setitem__(2, m["offsets"][1]), "empty")
+    bad(lambda m: m["features"].__setitem__(1, 10), "feature 10 >= 10")
+    bad(lambda m: m["thresholds"].__setitem__(2, -1), "negative threshold")
+
+
 def _rot_bytes(words, r):
     """k_hist2's rot_bytes on four 32-bit words: byte k of the result is byte
     (k + r) mod 16 of the input (restated with NumPy for the check below)."""

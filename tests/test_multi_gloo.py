@@ -113,3 +113,30 @@ def test_sampler_union_of_rank_masks_is_the_global_draw(built_lib):
         lo, hi = _shard(n, ws, rk)
         union[lo:hi] = mask[lo:hi]                         # what rank rk uploads
     assert np.array_equal(np.nonzero(union)[0], np.sort(smp))
+
+
+def _predict_worker(rank, ws, port, n, result):
+    """Row-sharded predict's host logic: each rank scores only its own block
+    (here a stand-in score: the row index itself) and _gather_rows returns
+    every row, in order, on every rank."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        from bsscl_gbm_b200.estimator import _gather_rows, _rank_rows
+        lo, hi = _rank_rows(n)
+        local = np.stack([np.arange(lo, hi, dtype=np.float64), -np.arange(lo, hi, dtype=np.float64)], axis=1)
+        result[rank] = (lo, hi, _gather_rows(dist, local, n))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("n", [11, 4000])
+def test_sharded_predict_gathers_every_row_in_order(n):
+    mgr = mp.Manager()
+    result = mgr.dict()
+    mp.spawn(_predict_worker, args=(2, _free_port(), n, result), nprocs=2, join=True)
+    want = np.stack([np.arange(n, dtype=np.float64), -np.arange(n, dtype=np.float64)], axis=1)
+    assert result[0][:2] == (0, n // 2) and result[1][:2] == (n // 2, n)
+    for rk in range(2):
+        assert np.array_equal(result[rk][2], want)

@@ -66,6 +66,40 @@ def test_predict_noalloc_matches_predict_twice():
     eng.close()
 
 
+def test_predict_noalloc_allocates_nothing():
+    """After a first call (which looks up the scratch array's address and
+    loads the kernels), a second call leaves the device's free memory
+    exactly as it was: every buffer it touches is the caller's or the fixed
+    array."""
+    import torch
+    from bsscl_gbm_b200 import lib
+    L = lib()
+    rng = np.random.default_rng(12)
+    n, p = 30_000, 16
+    xb_t = _dev(torch, rng.integers(0, 256, size=(n, p)).astype(np.uint8))
+    ens = _ensemble(7, 40, 7, p)
+    t = {k: _dev(torch, v) for k, v in ens.items()}
+    F = torch.empty(n, dtype=torch.float64, device="cuda")
+    P = torch.empty(n, dtype=torch.float64, device="cuda")
+    err = C.create_string_buffer(256)
+
+    def call():
+        return L.gbm_predict_noalloc(
+            C.c_void_p(xb_t.data_ptr()), n, p, C.c_void_p(t["features"].data_ptr()),
+            C.c_void_p(t["thresholds"].data_ptr()), C.c_void_p(t["values"].data_ptr()),
+            C.c_void_p(t["left"].data_ptr()), C.c_void_p(t["right"].data_ptr()),
+            C.c_void_p(t["offsets"].data_ptr()), 40, int(ens["features"].shape[0]), 0.1, 0.0,
+            C.c_void_p(F.data_ptr()), C.c_void_p(P.data_ptr()), None, err, 256)
+
+    assert call() == 0, err.value
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    assert call() == 0, err.value
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+
+
 def test_predict_noalloc_rejects_oversize_and_malformed():
     import torch
     from bsscl_gbm_b200 import lib
@@ -74,7 +108,10 @@ def test_predict_noalloc_rejects_oversize_and_malformed():
     xb_t = _dev(torch, np.zeros((n, p), np.uint8))
     big = _ensemble(5, 1100, 8, p)            # 562,100 nodes > 524,288
     rc, msg, _, _ = _call(L, torch, xb_t, p, big, 1100, 0.1, 0.0, None)
-    assert rc == 1 and "at most 524288" in msg
+    assert rc == 1 and "524288 nodes" in msg
+    many = _ensemble(8, 70_000, 0, p)          # 70,000 one-leaf trees > 65,536
+    rc, msg, _, _ = _call(L, torch, xb_t, p, many, 70_000, 0.1, 0.0, None)
+    assert rc == 1 and "65536 trees" in msg
     bad = _ensemble(6, 3, 3, p)
     bad["left"][0] = 0                         # a child that is not after its parent
     rc, msg, _, _ = _call(L, torch, xb_t, p, bad, 3, 0.1, 0.0, None)
