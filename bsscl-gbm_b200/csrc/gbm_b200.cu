@@ -63,6 +63,11 @@ struct gbm_ctx {
     int64_t n_global = 0;
     int32_t p = 0, nblk = 0;
     uint8_t *d_xb = nullptr;
+    // the round's selected features packed in blocks of 16 (k_compact_feat):
+    // two buffers, round r uses [slot & 1], so the sampler stream can pack
+    // round r + 1 while round r's histograms read the other
+    uint8_t *d_xc[2] = {nullptr, nullptr};
+    const uint8_t *xc_cur = nullptr;   // the buffer of the round being enqueued
     int32_t *d_counts = nullptr;
     std::vector<int32_t> counts;
     int16_t *d_skipb = nullptr;        // per feature: the bin the histogram skips
@@ -91,6 +96,8 @@ struct gbm_ctx {
     // and flush with the other's atomics.  Measured on config 4: 3 levels
     // 1110 rounds/s, 0 levels 1077, all levels 1057.
     int hist_v2_levels = 3;
+    int hist_kernel = 3;               // 3: k_hist3 on every level; 2: k_hist2 / k_hist split by level
+    int hist_seg_cost = 150000;        // k_hist3's cost of a segment in row units (22 per row; measured)
     int nf_cap = 0;
     long long *d_pool = nullptr;       // node histograms: slot i = node i
     long long *d_lpool = nullptr;      // several ranks: this rank's partial histograms, slot i = node i
@@ -140,6 +147,8 @@ struct gbm_ctx {
     struct Slot {
         int32_t *h_tg = nullptr, *d_tg = nullptr;   // the round's row swap targets
         int32_t *h_feat = nullptr;     // fidx [p] | blist [nblk] | bwp [nblk + 1] | nb
+        int32_t *d_fidx_c = nullptr;   // the round's fidx for its feature compaction on cst
+        bool xc_on_cst = false;        // the round's packed blocks are made on cst (k_compact_feat)
         int16_t *h_fpos = nullptr;     // fpos [nblk * 16] | fbi [p]
         TreeOut *h_tout = nullptr;
         double *h_loss = nullptr;
@@ -616,11 +625,19 @@ int block_weight(const RoundFeat &rf, int blk) {
     return w;
 }
 
+// The histograms read the round's packed feature blocks (k_compact_feat):
+// the default (GBM_HIST_KERNEL unset or 3) whenever the compaction's staging
+// of 256 rows x every column block fits its shared memory (p <= 608).
+bool compact_hist(const gbm_ctx *ctx) {
+    return ctx->hist_kernel == 3 && ctx->nblk <= 38;
+}
+
 // Per-slot pinned staging, sized for the data.
 int ensure_slots(gbm_ctx *ctx) {
     if (!ctx->slots_ready) {   // once per gbm_upload_bins (sizes follow p)
         for (auto &s : ctx->slot) {
             TRY(halloc(ctx, &s.h_feat, (size_t)ctx->p + 2 * ctx->nblk + 2));
+            TRY(dalloc(ctx, &s.d_fidx_c, (size_t)ctx->p));
             TRY(halloc(ctx, &s.h_fpos, (size_t)ctx->nblk * kBlk + ctx->p));
             TRY(halloc(ctx, &s.h_tout, 1));
             TRY(halloc(ctx, &s.h_loss, 2));   // [0] loss, [1] the peer exchange's error word
@@ -689,6 +706,14 @@ int setup_features(gbm_ctx *ctx, int si, const int32_t *fidx, int nf, RoundFeat 
     return GBM_OK;
 }
 
+// The round's selected features packed into blocks of 16 (k_compact_feat),
+// on stream st.
+int enqueue_pack(gbm_ctx *ctx, cudaStream_t st, const int32_t *d_fidx, int nf, uint8_t *xc) {
+    const size_t smem = (size_t)ctx->nblk * kCompactRows * kCompactStrideW * 4 + sizeof(int32_t) * (size_t)nf;
+    return launch(ctx, k_compact_feat, dim3((unsigned)((ctx->n + kCompactRows - 1) / kCompactRows)),
+                  dim3(kCompactRows), smem, st, (const uint8_t *)ctx->d_xb, ctx->n, ctx->nblk, d_fidx, nf, xc);
+}
+
 // ...and their copies to the device, on the engine stream (fixed sizes, so
 // a captured round copies whatever the slot holds when it runs).
 int enqueue_features(gbm_ctx *ctx, int si, int nf) {
@@ -700,6 +725,16 @@ int enqueue_features(gbm_ctx *ctx, int si, int nf) {
                        ctx->st));
     CK(cudaMemcpyAsync(ctx->d_blist, s.h_feat + ctx->p, sizeof(int32_t) * (2 * (size_t)ctx->nblk + 2),
                        cudaMemcpyHostToDevice, ctx->st));
+    const bool packed_on_cst = s.xc_on_cst;
+    s.xc_on_cst = false;   // a later round in this slot may take another path
+    if (compact_hist(ctx)) {   // the round's selected features, packed for the histograms
+        if (packed_on_cst) {
+            ctx->xc_cur = ctx->d_xc[si & 1];   // packed on cst before s.copied
+        } else {
+            TRY(enqueue_pack(ctx, ctx->st, ctx->d_fidx, nf, ctx->d_xc[0]));
+            ctx->xc_cur = ctx->d_xc[0];
+        }
+    }
     return GBM_OK;
 }
 
@@ -951,7 +986,17 @@ int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int level
     long long *stage = ctx->p2p ? ctx->d_pst : ctx->d_stage;
     const unsigned long long *par = (const unsigned long long *)(ctx->p2p ? ctx->d_sync + ctx->p2p_n + kSyncLevel
                                                                           : nullptr);
-    if (level < ctx->hist_v2_levels)
+    if (compact_hist(ctx))
+        TRY(launch(ctx, k_hist3<true>, dim3(ctx->sms), dim3(kHistV3Threads), (size_t)kAccV3Words * sizeof(unsigned),
+                   ctx->st, ctx->xc_cur, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p,
+                   ctx->d_blist, d_nb, ctx->d_fpos, rf.nf, ctx->d_q, stage, par, ctx->pst_stride,
+                   ctx->hist_seg_cost));
+    else if (ctx->hist_kernel >= 3)
+        TRY(launch(ctx, k_hist3<false>, dim3(ctx->sms), dim3(kHistV3Threads), (size_t)kAccV3Words * sizeof(unsigned),
+                   ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p,
+                   ctx->d_blist, d_nb, ctx->d_fpos, rf.nf, ctx->d_q, stage, par, ctx->pst_stride,
+                   ctx->hist_seg_cost));
+    else if (level < ctx->hist_v2_levels)
         TRY(launch(ctx, k_hist2, dim3(ctx->sms), dim3(kHistV2Threads), (size_t)kAccV2Words * sizeof(unsigned),
                    ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p,
                    ctx->d_blist, d_nb, ctx->d_fpos, ctx->d_skipb, rf.nf, ctx->d_q, stage, par, ctx->pst_stride));
@@ -1639,10 +1684,19 @@ int take_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset) 
 // The round's shuffle (composed into the permutation), this rank's in-bag
 // mask and the root's row list, on the sampler stream (cst); ends with
 // slot si's `copied` event, which the engine stream waits for.
-int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int64_t row_offset) {
+int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int64_t row_offset, int nf) {
     gbm_ctx::Slot &s = ctx->slot[si];
     constexpr int R = gbm_ctx::kRing;
     int32_t *pout = nullptr;
+    // the round's packed feature blocks, made here while the previous round
+    // grows: buffer si & 1 was last read by the round two places back, whose
+    // histograms ended before the rows_free this stream waited for in the
+    // previous round's sample
+    s.xc_on_cst = nf > 0 && compact_hist(ctx);
+    if (s.xc_on_cst) {
+        CK(cudaMemcpyAsync(s.d_fidx_c, s.h_feat, sizeof(int32_t) * nf, cudaMemcpyHostToDevice, ctx->cst));
+        TRY(enqueue_pack(ctx, ctx->cst, s.d_fidx_c, nf, ctx->d_xc[si & 1]));
+    }
     if (rows_on) {
         int32_t *pin = ctx->d_perm[(si + R - 1) % R];
         pout = ctx->d_perm[si];
@@ -1686,6 +1740,8 @@ int begin_bins(gbm_ctx *ctx, int64_t n, int32_t p, const int32_t *bin_counts) {
     ctx->have_bins = ctx->have_labels = ctx->have_labels_mc = ctx->have_targets = false;
     ctx->counts.assign(bin_counts, bin_counts + p);
     TRY(dalloc(ctx, &ctx->d_xb, (size_t)ctx->nblk * n * kBlk));
+    if (compact_hist(ctx))
+        for (auto &b : ctx->d_xc) TRY(dalloc(ctx, &b, (size_t)ctx->nblk * n * kBlk));
     TRY(dalloc(ctx, &ctx->d_counts, (size_t)p));
     CK(cudaMemcpyAsync(ctx->d_counts, bin_counts, sizeof(int32_t) * p, cudaMemcpyHostToDevice, ctx->st));
     return GBM_OK;
@@ -1792,7 +1848,7 @@ int capture_round(gbm_ctx *ctx, int si, int nf, const gbm_params *P, int64_t N, 
     const double b0 = ctx->comm_bytes;
     ctx->cur_slot = si;
     s.tused = s.tdone = 0;
-    TRY(capture(ctx, ctx->cst, &s.g_cst, [&] { return enqueue_sample(ctx, si, N, m, rows_on, row_offset); }));
+    TRY(capture(ctx, ctx->cst, &s.g_cst, [&] { return enqueue_sample(ctx, si, N, m, rows_on, row_offset, nf); }));
     TRY(capture(ctx, ctx->st, &s.g_st, [&] {
         TRY(wait_ev(ctx, ctx->st, s.copied));
         TRY(enqueue_features(ctx, si, nf));
@@ -1847,6 +1903,13 @@ int gbm_ctx_create(int32_t device, gbm_ctx **out) {
     ctx->sms = std::max(sms, 1);
     ctx->hist_grid = 2 * ctx->sms;   // one wave of 2 per SM (measured best: fewer flushes)
     if (const char *e = std::getenv("GBM_HIST_V2_LEVELS")) ctx->hist_v2_levels = std::atoi(e);
+    if (const char *e = std::getenv("GBM_HIST_KERNEL")) ctx->hist_kernel = std::atoi(e);
+    if (const char *e = std::getenv("GBM_HIST_SEG_COST")) ctx->hist_seg_cost = std::max(0, std::atoi(e));
+    CK(cudaFuncSetAttribute(k_hist3<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)(kAccV3Words * sizeof(unsigned))));
+    CK(cudaFuncSetAttribute(k_hist3<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)(kAccV3Words * sizeof(unsigned))));
+    CK(cudaFuncSetAttribute(k_compact_feat, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     CK(cudaFuncSetAttribute(k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             kAccWords * (int)sizeof(unsigned)));
     CK(cudaFuncSetAttribute(k_hist2, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1874,7 +1937,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     for (auto &s : ctx->slot)
         for (cudaEvent_t e : s.tev) cudaEventDestroy(e);
     if (ctx->comm) gbm_comm_destroy(ctx->comm);
-    void *dev_ptrs[] = {ctx->d_xb, ctx->d_counts, ctx->d_skipb, ctx->d_y, ctx->d_F, ctx->d_q, ctx->d_mask,
+    void *dev_ptrs[] = {ctx->d_xb, ctx->d_xc[0], ctx->d_xc[1], ctx->d_counts, ctx->d_skipb, ctx->d_y, ctx->d_F, ctx->d_q, ctx->d_mask,
                         ctx->d_rows, ctx->d_tmp, ctx->d_cnt, ctx->d_off, ctx->d_total, ctx->d_blist, ctx->d_fidx,
                         ctx->d_fpos, ctx->d_pool, ctx->d_lpool, ctx->d_stage, ctx->d_fbest, ctx->d_htask, ctx->d_hprefix,
                         ctx->d_ptask, ctx->d_tile_cnt, ctx->d_nleft,
@@ -1890,6 +1953,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     for (void *p : host_ptrs) if (p) cudaFreeHost(p);
     for (auto &s : ctx->slot) {
         if (s.d_tg) cudaFree(s.d_tg);
+        if (s.d_fidx_c) cudaFree(s.d_fidx_c);
         void *hp[] = {s.h_tg, s.h_feat, s.h_fpos, s.h_tout, s.h_loss};
         for (void *p : hp) if (p) cudaFreeHost(p);
         if (s.copied) cudaEventDestroy(s.copied);
@@ -2422,7 +2486,7 @@ int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, co
     begin_round(ctx, si);
     TRY(take_sample(ctx, si, sampler, row_offset));
     TRY(enqueue_sample(ctx, si, gbm_sampler_rows(sampler), gbm_sampler_n_sub(sampler),
-                       gbm_sampler_shuffles_rows(sampler) != 0, row_offset));
+                       gbm_sampler_shuffles_rows(sampler) != 0, row_offset, 0));
     TRY(wait_ev(ctx, ctx->st, ctx->slot[si].copied));
     return round_body(ctx, si, ctx->feat_buf.data(), nf, P, out, train_loss, true);
 }
@@ -2473,10 +2537,10 @@ int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const
         if (!graphs) {
             begin_round(ctx, si);
             TRY(take_sample(ctx, si, sampler, row_offset));
-            TRY(enqueue_sample(ctx, si, N, m, rows_on, row_offset));
-            TRY(wait_ev(ctx, ctx->st, s.copied));
             RoundFeat rf;
-            TRY(setup_features(ctx, si, ctx->feat_buf.data(), nf, rf));
+            TRY(setup_features(ctx, si, ctx->feat_buf.data(), nf, rf));   // before the sample packs its features
+            TRY(enqueue_sample(ctx, si, N, m, rows_on, row_offset, nf));
+            TRY(wait_ev(ctx, ctx->st, s.copied));
             TRY(enqueue_features(ctx, si, nf));
             TRY(enqueue_grow(ctx, rf, P, true));
             TRY(enqueue_replay(ctx, P));

@@ -872,6 +872,275 @@ k_hist2(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ r
     }
 }
 
+// The round's selected features, packed into dense blocks of 16: block v,
+// slot s holds the bin of feature fidx[16 v + s] (0 past the last one), in
+// the same column-block layout as the bins themselves ([nvb][n][16]).  The
+// histogram then runs 16 busy lanes per block: 70 selected features of 100
+// take 5 blocks instead of 7 partly idle ones.  A CTA takes 256 rows: their
+// records of every physical block are staged in shared memory at a 20-byte
+// row stride (5 words, so 32 consecutive rows fall in 32 banks), then each
+// thread assembles its row's packed records.
+constexpr int kCompactRows = 256;
+constexpr int kCompactStrideW = 5;   // words per staged record (16 bytes + pad)
+
+__global__ void __launch_bounds__(kCompactRows)
+k_compact_feat(const uint8_t *__restrict__ xb, int64_t n, int nblk, const int32_t *__restrict__ fidx, int nf,
+               uint8_t *__restrict__ xc) {
+    griddep_wait();
+    extern __shared__ uint32_t cst[];   // [nblk][256][5] words, then fidx [nf]
+    int32_t *s_f = reinterpret_cast<int32_t *>(cst + (size_t)nblk * kCompactRows * kCompactStrideW);
+    const int64_t r0 = (int64_t)blockIdx.x * kCompactRows;
+    const int t = threadIdx.x;
+    const int64_t row = r0 + t;
+    for (int i = t; i < nf; i += kCompactRows) s_f[i] = fidx[i];
+    if (row < n) {
+        for (int b = 0; b < nblk; b++) {
+            const uint4 v = __ldg(reinterpret_cast<const uint4 *>(xb) + (int64_t)b * n + row);
+            uint32_t *d = cst + ((size_t)b * kCompactRows + t) * kCompactStrideW;
+            d[0] = v.x; d[1] = v.y; d[2] = v.z; d[3] = v.w;
+        }
+    }
+    __syncthreads();
+    if (row >= n) return;
+    const uint8_t *sb = reinterpret_cast<const uint8_t *>(cst);
+    const int nvb = (nf + kBlk - 1) / kBlk;
+    for (int v = 0; v < nvb; v++) {
+        uint32_t w[4];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; q4++) {
+            uint32_t x = 0;
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int pos = v * kBlk + q4 * 4 + k;
+                if (pos < nf) {
+                    const int f = s_f[pos];
+                    x |= (uint32_t)sb[(((size_t)(f >> 4) * kCompactRows + t) * kCompactStrideW) * 4 + (f & 15)] << (8 * k);
+                }
+            }
+            w[q4] = x;
+        }
+        reinterpret_cast<uint4 *>(xc)[(int64_t)v * n + row] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// k_hist3: the histograms of every level with the shared-memory layout of
+// k_hist2 (each half-warp its own copy, 32 lanes on 32 banks, one wavefront
+// per atomic instruction) and no branch in the update loop.
+// * Every bin is added, the skipped bin included (the split search rebuilds
+//   that cell as node total - the other cells, which returns the value
+//   stored here), so no lane idles on it.
+// * A slot whose feature the round did not select adds into a trash bin
+//   (256): its cell sits in the lane's own bank like every other cell, so
+//   the instruction stays conflict-free, and the trash row is never read.
+// * Runs of up to kChunk3 = 32768 rows between flushes: (2^17 - 1) * 2^15 <
+//   2^32 keeps the low and middle digit sums inside 32 bits, and the top
+//   digit's |sum| < 2^14 * 2^15.  At the flush a cell's 128-bit value is
+//   split into its words without forming it in 64 bits: with a = mid * 2^17
+//   + low (< 2^50), hi = 4 * top + (a >> 32) and lo = a mod 2^32.
+constexpr int kHistV3Threads = 1024;
+constexpr int kChunk3 = 32768;
+constexpr int kBinsV3 = kBins + 1;                   // + the trash bin
+constexpr int kDigV3 = kBinsV3 * 2 * kBlk;           // words between two digits
+constexpr int kAccV3Words = 6 * kDigV3;              // 197,376 bytes
+
+// COMPACT: xb is the round's packed blocks (k_compact_feat): block bi holds
+// feature positions 16 bi .. 16 bi + 15, every slot below nf selected; the
+// physical block list and feature positions are not read.
+template <bool COMPACT>
+__global__ void __launch_bounds__(kHistV3Threads, 1)
+k_hist3(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
+        const int32_t *__restrict__ rows1, const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
+        const int *__restrict__ ntask_p, const int32_t *__restrict__ blist, const int32_t *__restrict__ nb_p,
+        const int16_t *__restrict__ fpos, int nf, const longlong2 *__restrict__ q, long long *__restrict__ stage_hist,
+        const unsigned long long *__restrict__ par_word, int64_t par_stride, int seg_cost) {
+    griddep_wait();
+    if (par_word) stage_hist += (int64_t)(*par_word & 1ull) * par_stride;   // peer exchange: this level's buffer
+    extern __shared__ unsigned acc[];   // [6][257][2][16]
+    __shared__ long long s_tot[2][kHistV3Threads / 32];
+    const int ntask = *ntask_p;
+    const int nb = COMPACT ? (nf + kBlk - 1) / kBlk : *nb_p;
+    if (ntask <= 0 || nb <= 0) return;
+    // The work split.  Within a block, task t costs w per row plus seg_cost
+    // for its segment (zeroing the accumulators and the flush, whatever its
+    // rows): task t spans [w rpre[t] + C t, w rpre[t+1] + C (t+1)) of the
+    // block's Wb = w R + C ntask, its rows after its first C units.  CTA c
+    // takes [c T / G, (c+1) T / G) of T = nb Wb, so a CTA whose share covers
+    // many small tasks takes fewer rows.
+    const long long R = rpre[ntask];
+    const long long w = kHistV2Weight, C = seg_cost;
+    const long long Wb = w * R + C * ntask;
+    const long long T = (long long)nb * Wb;
+    if (T <= 0) return;
+    const long long G = gridDim.x;
+    const long long B0 = cost_bound(blockIdx.x, T, G), B1 = cost_bound(blockIdx.x + 1, T, G);
+    if (B0 >= B1) return;
+    // the first row at or after cost position y (0 <= y <= Wb) of a block
+    auto row_at = [&](long long y) -> int {
+        int lo = 0, hi = ntask;   // the last task t with w rpre[t] + C t <= y (t = ntask: past the end)
+        while (lo < hi) {
+            int mid = (lo + hi + 1) >> 1;
+            if (w * rpre[mid] + C * mid <= y) lo = mid; else hi = mid - 1;
+        }
+        if (lo >= ntask) return (int)R;
+        const long long off = y - (w * rpre[lo] + C * lo) - C;
+        const long long kk = off <= 0 ? 0 : ceil_div_ll(off, w);
+        return (int)min((long long)rpre[lo + 1], rpre[lo] + kk);
+    };
+    const int lane = threadIdx.x & 31, half = lane >> 4, fl = lane & 15;
+    const int warp = threadIdx.x >> 5;
+    const int64_t slot_words = slot_words_for(nf);
+    int bi = (int)min((long long)nb - 1, B0 / Wb);
+    for (; bi < nb; bi++) {
+        const long long base = Wb * bi;
+        if (base >= B1) break;
+        const int k0 = row_at(max(B0 - base, 0ll));
+        const int k1 = row_at(min(B1 - base, Wb));
+        if (k0 >= k1) continue;
+        const int blk = COMPACT ? bi : blist[bi];
+        unsigned mask = 0;
+        if (COMPACT) {
+            const int m = min(nf - bi * kBlk, kBlk);
+            mask = m >= kBlk ? 0xffffu : (1u << m) - 1u;
+        } else {
+#pragma unroll
+            for (int k = 0; k < kBlk; k++) mask |= (fpos[blk * kBlk + k] >= 0 ? 1u : 0u) << k;
+        }
+        // bit k set: step k's feature (fl + k) mod 16 is not selected -> trash bin
+        const unsigned unsel = ~((mask | (mask << kBlk)) >> fl) & 0xffffu;
+        const uint4 *xv = reinterpret_cast<const uint4 *>(xb) + (int64_t)blk * n;
+        int t;
+        {
+            int lo = 0, hi = ntask - 1;
+            while (lo < hi) {
+                int mid = (lo + hi + 1) >> 1;
+                if (rpre[mid] <= k0) lo = mid; else hi = mid - 1;
+            }
+            t = lo;
+        }
+        for (int k = k0; k < k1; t++) {
+            const int t0 = rpre[t], t1 = rpre[t + 1];
+            if (t1 <= k) continue;
+            const HistTask tk = tasks[t];
+            const int32_t *__restrict__ rows = tk.buf ? rows1 : rows0;
+            const int pe = min(k1, t1);
+            const bool single = k == t0 && pe == t1 && (t1 - t0) <= kChunk3;
+            long long *dst = stage_hist + (int64_t)tk.stage * slot_words;
+            for (int c0 = k; c0 < pe; c0 += kChunk3) {
+                const int c1 = min(pe, c0 + kChunk3);
+                for (int i = threadIdx.x; i < kAccV3Words / 4; i += blockDim.x)
+                    reinterpret_cast<uint4 *>(acc)[i] = make_uint4(0u, 0u, 0u, 0u);
+                __syncthreads();
+                const int r0 = (int)tk.begin + (c0 - t0), r1 = (int)tk.begin + (c1 - t0);
+                long long tg = 0, th = 0;
+                unsigned *my = acc + half * kBlk;
+                for (int rb = r0 + (int)(threadIdx.x & ~31u); rb < r1; rb += blockDim.x) {
+                    const int r = rb + lane;
+                    const bool valid = r < r1;
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    longlong2 qq = make_longlong2(0, 0);
+                    if (valid) {
+                        const int row = rows[r];
+                        v = __ldg(xv + row);
+                        qq = __ldg(q + row);
+                    }
+                    tg += qq.x;
+                    th += qq.y;
+                    // an invalid lane adds zeros (its q is 0) into real cells: harmless
+                    const unsigned dg0 = (unsigned)qq.x & 0x1ffffu, dg1 = (unsigned)(qq.x >> kDig) & 0x1ffffu,
+                                   dg2 = (unsigned)(int)(qq.x >> (2 * kDig));
+                    const unsigned dh0 = (unsigned)qq.y & 0x1ffffu, dh1 = (unsigned)(qq.y >> kDig) & 0x1ffffu,
+                                   dh2 = (unsigned)(int)(qq.y >> (2 * kDig));
+                    const uint4 vr = rot_bytes(v, fl);
+#pragma unroll
+                    for (int k = 0; k < kBlk; k++) {
+                        const unsigned b = ((unsel >> k) & 1u) ? (unsigned)kBins : byte_of(vr, k);
+                        unsigned *cc = my + b * (2 * kBlk) + ((fl + k) & (kBlk - 1));
+                        atomicAdd(cc + 0 * kDigV3, dg0);
+                        atomicAdd(cc + 1 * kDigV3, dg1);
+                        atomicAdd(cc + 2 * kDigV3, dg2);
+                        atomicAdd(cc + 3 * kDigV3, dh0);
+                        atomicAdd(cc + 4 * kDigV3, dh1);
+                        atomicAdd(cc + 5 * kDigV3, dh2);
+                    }
+                }
+                if (bi == 0) {
+                    tg = warp_sum(tg);   // <= 32 rows per lane, 1024 per warp: |sum| < 2^58
+                    th = warp_sum(th);
+                    if (lane == 0) {
+                        s_tot[0][warp] = tg;
+                        s_tot[1][warp] = th;
+                    }
+                }
+                __syncthreads();
+                if (bi == 0 && threadIdx.x < 2) {
+                    i128 tot = 0;
+                    for (int w2 = 0; w2 < kHistV3Threads / 32; w2++) tot += (i128)s_tot[threadIdx.x][w2];
+                    const long long thi = (long long)(tot >> 32), tlo = (long long)(tot & 0xffffffff);
+                    long long *o = dst + (int64_t)nf * kBins * kWords + 2 * threadIdx.x;
+                    if (single) {
+                        o[0] = thi;
+                        o[1] = tlo;
+                    } else {
+                        if (thi) atomicAdd((unsigned long long *)(o + 0), (unsigned long long)thi);
+                        if (tlo) atomicAdd((unsigned long long *)(o + 1), (unsigned long long)tlo);
+                    }
+                }
+                // flush, in two steps.  (1) warp w takes bins w, w + 32, ...: lane
+                // (half, fl) reads its copy of cell (bin, fl) (32 lanes, 32 banks),
+                // the halves' digit sums are added across the warp (a half-0 lane
+                // keeps g, a half-1 lane h) and the cell's two words are held in
+                // registers; once every warp has read its cells, they are written
+                // over the accumulators in the staging order, feature-major:
+                // word ((fl * 256 + bin) * 4 + 2 * half + {hi, lo}).  (2) the CTA
+                // adds (or stores) them into staging one feature at a time, 1024
+                // consecutive words per feature, so a warp covers 256 contiguous
+                // bytes instead of 32 features' lines.
+                long long fw[2 * (kBins / (kHistV3Threads / 32))];
+#pragma unroll
+                for (int i = 0; i < kBins / (kHistV3Threads / 32); i++) {
+                    const int b = warp + i * (kHistV3Threads / 32);
+                    const unsigned *d = acc + (b * 2 + half) * kBlk + fl;
+                    const unsigned g0 = d[0], g1 = d[kDigV3], g2 = d[2 * kDigV3];
+                    const unsigned h0 = d[3 * kDigV3], h1 = d[4 * kDigV3], h2 = d[5 * kDigV3];
+                    // send the partner what it keeps: half 0 sends h, half 1 sends g
+                    const unsigned s0 = half ? g0 : h0, s1 = half ? g1 : h1, s2 = half ? g2 : h2;
+                    const unsigned r0_ = __shfl_xor_sync(0xffffffffu, s0, 16);
+                    const unsigned r1_ = __shfl_xor_sync(0xffffffffu, s1, 16);
+                    const unsigned r2_ = __shfl_xor_sync(0xffffffffu, s2, 16);
+                    const unsigned long long lo64 = (unsigned long long)(half ? h0 : g0) + r0_;
+                    const unsigned long long mid64 = (unsigned long long)(half ? h1 : g1) + r1_;
+                    const long long top = (long long)(int)(half ? h2 : g2) + (long long)(int)r2_;
+                    const unsigned long long a = (mid64 << kDig) + lo64;
+                    fw[2 * i] = 4 * top + (long long)(a >> 32);
+                    fw[2 * i + 1] = (long long)(a & 0xffffffffull);
+                }
+                __syncthreads();   // every cell has been read: the accumulators become the buffer
+                long long *fbuf = reinterpret_cast<long long *>(acc);   // [16][256][4], 128 KB
+#pragma unroll
+                for (int i = 0; i < kBins / (kHistV3Threads / 32); i++) {
+                    const int b = warp + i * (kHistV3Threads / 32);
+                    *reinterpret_cast<longlong2 *>(fbuf + ((int64_t)fl * kBins + b) * kWords + 2 * half) =
+                        make_longlong2(fw[2 * i], fw[2 * i + 1]);
+                }
+                __syncthreads();
+                for (int f = 0; f < kBlk; f++) {
+                    if (!((mask >> f) & 1u)) continue;
+                    const int jj = COMPACT ? bi * kBlk + f : fpos[blk * kBlk + f];
+                    long long *o = dst + (int64_t)jj * kBins * kWords;
+                    const long long *src = fbuf + (int64_t)f * kBins * kWords;
+                    for (int i = threadIdx.x; i < kBins * kWords; i += kHistV3Threads) {
+                        const long long x = src[i];
+                        if (single) o[i] = x;
+                        else if (x) atomicAdd((unsigned long long *)(o + i), (unsigned long long)x);
+                    }
+                }
+                __syncthreads();
+            }
+            k = pe;
+        }
+    }
+}
+
 // ===========================================================================
 // level planning (device side: no host round trip inside a tree)
 // ===========================================================================
