@@ -1115,10 +1115,10 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, const Ne
         TRY(launch(ctx, k_fill_counts, dim3(1), dim3(32), 0, ctx->st, ctx->d_nodes, (const int *)nullptr,
                    (const int *)nullptr, (const long long *)ctx->d_stage, rf.nf, sync, ctx->p2p_n));
     }
-    int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
-    TRY(launch(ctx, k_split_feat<true>, dim3(dim3(fx, 1)), dim3(32 * kSplitWarps), 0, ctx->st, 
-        ctx->d_nodes, nullptr, nullptr, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx,
-        ctx->d_counts, ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight,
+    TRY(launch(ctx, k_split_bins<true>, dim3(rf.nf, 1), dim3(kSplitThreads), 0, ctx->st,
+        (const DNode *)ctx->d_nodes, (const int *)nullptr, (const int *)nullptr, (const HistTask *)ctx->d_htask,
+        ctx->d_stage, ctx->d_pool, rf.nf, (const int32_t *)ctx->d_fidx, (const int32_t *)ctx->d_counts,
+        (const int16_t *)ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight,
         (long long)P->min_samples_leaf, P->max_depth, pool_depth(P), ctx->d_fbest));
     return launch_close(ctx, rf, P, true, nullptr, nullptr, ctx->d_lvl[0], ints(ctx, I_LVL0), np);
 }
@@ -1174,11 +1174,11 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
         TRY(launch(ctx, k_fill_counts, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, (const int *)lvl, lvl_cnt,
                    (const long long *)ctx->d_stage, rf.nf, sync, ctx->p2p_n));
     }
-    int fx = (rf.nf + kSplitFeatPerCta - 1) / kSplitFeatPerCta;
-    TRY(launch(ctx, k_split_feat<false>, dim3(dim3(fx, W_ub)), dim3(32 * kSplitWarps), 0, ctx->st, 
-        ctx->d_nodes, lvl, lvl_cnt, ctx->d_htask, ctx->d_stage, ctx->d_pool, rf.nf, ctx->d_fidx, ctx->d_counts,
-        ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight, (long long)P->min_samples_leaf, P->max_depth,
-        pool_depth(P), ctx->d_fbest));
+    TRY(launch(ctx, k_split_bins<false>, dim3(rf.nf, W_ub), dim3(kSplitThreads), 0, ctx->st,
+        (const DNode *)ctx->d_nodes, (const int *)lvl, (const int *)lvl_cnt, (const HistTask *)ctx->d_htask,
+        ctx->d_stage, ctx->d_pool, rf.nf, (const int32_t *)ctx->d_fidx, (const int32_t *)ctx->d_counts,
+        (const int16_t *)ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight,
+        (long long)P->min_samples_leaf, P->max_depth, pool_depth(P), ctx->d_fbest));
     TRY(launch_close(ctx, rf, P, false, lvl, lvl_cnt, next, next_cnt, next ? np : NextPlan()));
     ctx->waves++;
     return GBM_OK;

@@ -22,7 +22,6 @@ constexpr int kHistV2Weight = 6 + kBlk;   // k_hist2's cost of a row in any bloc
 constexpr int kPartTile = 4096;     // rows per partition CTA
 constexpr int kPartThreads = 512;   // 8 rows per thread, loads in flight together
 constexpr int kPartWords = kPartTile / 32;   // side bits of a tile
-constexpr int kSplitWarps = 8;      // features per split CTA (one warp each)
 constexpr int kUpdThreads = 256;
 constexpr int kCompTile = 4096;     // rows per in-bag compaction CTA
 

@@ -1853,187 +1853,183 @@ __global__ void k_leaf_finish(DNode *__restrict__ nodes, const int *__restrict__
 // split search
 // ===========================================================================
 
-// Best bin of one feature for one node with exact totals (TG, TH): the
-// reference's scan (E:602-621, E:780-801): bins 0..nb-2 as a running
-// prefix, HL<mcw or HR<mcw skipped, gain = GL^2/(HL+l) + GR^2/(HR+l) -
-// G^2/(H+l), first maximum wins.  Every operation rounds separately, as in
-// the reference.  Lane l owns bins 8l .. 8l+7, whose exact sums come in
-// g[], h[]; the skipped bin sb holds node total - all other cells.
-__device__ __forceinline__ void feature_best(i128 (&g)[8], i128 (&h)[8], i128 TG, i128 TH, int nb, int sb,
-                                             int S, double lam, double mcw, double parent, double &best_gain,
-                                             int &best_bin) {
-    const int lane = threadIdx.x & 31;
-    const double sc = pow2(-S);
-    i128 lg = 0, lh = 0;
+// k_split_bins: the split search (E:602-621, E:780-801) with one CTA of 256
+// threads per (parent k, feature position jj) and one thread per bin, for both children at once
+// (ROOT: node 0 alone).  Thread b reads bin b's staging cell (the smaller
+// child, built by the histogram) and the parent's pool cell, forms both
+// children's cells (larger = parent - smaller, E:740-745, exact), writes
+// their pool slots when their own children will need them, and zeroes the
+// staging cell it alone read.  A block-wide 128-bit prefix scan over the
+// 256 bins gives every bin's left sums at once, so each thread evaluates
+// one bin's gain (the reference's formula, every operation rounded as in
+// E:602-621) and a block argmax picks the first maximum (lowest bin on a
+// tie).  The skipped-bin cell is rebuilt as node total - all other cells.
+constexpr int kSplitThreads = kBins;
+
+// Inclusive block scan of NV 128-bit values per thread (256 threads).
+template <int NV>
+__device__ __forceinline__ void block_scan_i128(i128 (&v)[NV], i128 (&tot)[NV], i128 *s_w /* [8][NV] */) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        lg += g[k];
-        lh += h[k];
-    }
-    i128 ag = lg, ah = lh;
-    for (int o = 16; o > 0; o >>= 1) {
-        ag += shfl_xor_i128(ag, o);
-        ah += shfl_xor_i128(ah, o);
-    }
-    const i128 fg = TG - ag, fh = TH - ah;   // the skipped bin's cell
-    if ((sb >> 3) == lane) {
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const bool hit = (sb & 7) == k;
-            g[k] += hit ? fg : (i128)0;
-            h[k] += hit ? fh : (i128)0;
-        }
-        lg += fg;
-        lh += fh;
-    }
-    i128 xg = lg, xh = lh;
     for (int o = 1; o < 32; o <<= 1) {
-        i128 tg2 = shfl_up_i128(xg, o), th2 = shfl_up_i128(xh, o);
-        if (lane >= o) { xg += tg2; xh += th2; }
-    }
-    i128 pg = xg - lg, ph = xh - lh;
-    double bg = -1e9;
-    int bb = -1;
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        const int b = lane * 8 + k;
-        pg += g[k];
-        ph += h[k];
-        if (b <= nb - 2) {
-            double GL = __dmul_rn(i128_to_double(pg), sc);
-            double HL = __dmul_rn(i128_to_double(ph), sc);
-            double GR = __dmul_rn(i128_to_double(TG - pg), sc);
-            double HR = __dmul_rn(i128_to_double(TH - ph), sc);
-            if (!(HL < mcw || HR < mcw)) {
-                double gain = __dsub_rn(
-                    __dadd_rn(__ddiv_rn(__dmul_rn(GL, GL), __dadd_rn(HL, lam)),
-                              __ddiv_rn(__dmul_rn(GR, GR), __dadd_rn(HR, lam))),
-                    parent);
-                if (gain > bg) { bg = gain; bb = b; }
-            }
+        for (int j = 0; j < NV; j++) {
+            const i128 t = shfl_up_i128(v[j], o);
+            if (lane >= o) v[j] += t;
         }
     }
-    // warp argmax, ties -> lower bin
-    for (int o = 16; o > 0; o >>= 1) {
-        double og = __shfl_xor_sync(0xffffffffu, bg, o);
-        int ob = __shfl_xor_sync(0xffffffffu, bb, o);
-        if (better(og, ob < 0 ? -1 : 0, ob, bg, bb < 0 ? -1 : 0, bb)) { bg = og; bb = ob; }
+    if (lane == 31) {
+#pragma unroll
+        for (int j = 0; j < NV; j++) s_w[w * NV + j] = v[j];
     }
-    best_gain = bg;
-    best_bin = bb;
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < NV; j++) {
+        i128 before = 0, all = 0;
+        for (int u = 0; u < kSplitThreads / 32; u++) {
+            const i128 x = s_w[u * NV + j];
+            if (u < w) before += x;
+            all += x;
+        }
+        v[j] += before;
+        tot[j] = all;
+    }
 }
 
-// One warp per (parent k, feature position jj, child side): the smaller
-// child's cells come from staging slot k, the larger child's are parent -
-// smaller (E:740-745, exact); the staging cells are zeroed after use.  Each warp writes its child's pool slot (the
-// child's histogram as a future parent; the cells are skipped when that
-// child's children are handled without histograms) and finds its best bin
-// for feature jj.
-// ROOT: node 0 from staging slot 0.  fbest[(2k + side) * nf + jj], side 0 =
-// left child.
-constexpr int kSplitFeatPerCta = kSplitWarps / 2;
-static_assert(kSplitWarps == 8, "k_split_feat names one barrier per warp pair (4 pairs)");
-
 template <bool ROOT>
-__global__ void __launch_bounds__(32 * kSplitWarps)
-k_split_feat(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const int *__restrict__ lvl_count,
-             const HistTask *__restrict__ ht, const long long *__restrict__ stage, long long *__restrict__ pool,
-             int nf, const int32_t *__restrict__ fidx, const int32_t *__restrict__ counts,
-             const int16_t *__restrict__ skipb, int S, double lam, double mcw, long long msl, int max_depth,
-             int pool_depth, FBest *__restrict__ fbest) {
+__global__ void __launch_bounds__(kSplitThreads)
+k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const int *__restrict__ lvl_count,
+             const HistTask *__restrict__ ht, long long *__restrict__ stage, long long *__restrict__ pool, int nf,
+             const int32_t *__restrict__ fidx, const int32_t *__restrict__ counts, const int16_t *__restrict__ skipb,
+             int S, double lam, double mcw, long long msl, int max_depth, int pool_depth,
+             FBest *__restrict__ fbest) {
     griddep_wait();
-    const int k = blockIdx.y;
+    constexpr int NS = ROOT ? 1 : 2;   // children searched
+    __shared__ i128 s_w[(kSplitThreads / 32) * 2 * NS];
+    __shared__ double s_bg[NS][kSplitThreads / 32];
+    __shared__ int s_bb[NS][kSplitThreads / 32];
+    const int k = blockIdx.y, jj = blockIdx.x;
     if (!ROOT && k >= *lvl_count) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int side = ROOT ? 0 : (warp & 1);
-    if (ROOT && (warp & 1)) return;
-    const int jj = blockIdx.x * kSplitFeatPerCta + (warp >> 1);
     if (jj >= nf) return;
+    const int b = threadIdx.x, lane = b & 31, warp = b >> 5;
     const int64_t words = slot_words_for(nf);
-    const long long *st = stage + (int64_t)k * words;
-    int ch = 0, parent = -1;
-    bool is_small = true;
+    long long *st = stage + (int64_t)k * words;
+    const long long *st_tot = st + (int64_t)nf * kBins * kWords;
+    int parent = -1, ch[2] = {0, 0};
+    bool small[2] = {true, false};
     if (!ROOT) {
         parent = lvl[k];
         const DNode &pn = nodes[parent];
-        ch = side == 0 ? pn.kid0 : pn.kid1;
-        is_small = (ht[k].left_small != 0) == (side == 0);
+        ch[0] = pn.kid0;
+        ch[1] = pn.kid1;
+        small[0] = ht[k].left_small != 0;
+        small[1] = !small[0];
     }
-    const DNode nd = nodes[ch];
-    const long long *st_tot = st + (int64_t)nf * kBins * kWords;
     const long long *par = ROOT ? nullptr : pool + (int64_t)parent * words;
-    i128 TG, TH;
-    if (is_small) {
-        TG = cell(st_tot[0], st_tot[1]);
-        TH = cell(st_tot[2], st_tot[3]);
-    } else {
-        const long long *pt = par + (int64_t)nf * kBins * kWords;
-        TG = cell(pt[0] - st_tot[0], pt[1] - st_tot[1]);
-        TH = cell(pt[2] - st_tot[2], pt[3] - st_tot[3]);
-    }
-    long long *pc = pool + (int64_t)ch * words;
-    const bool write_pool = nd.depth < pool_depth;   // the cells; the totals always (level close)
-    if (jj == 0 && lane < kTotWords) {
-        const int64_t o = (int64_t)nf * kBins * kWords + lane;
-        pc[o] = is_small ? st_tot[lane] : par[o] - st_tot[lane];
-    }
-    // cells of feature jj: lane owns bins 8*lane .. 8*lane+7 (32 words)
-    const int64_t base = (int64_t)jj * kBins * kWords + (int64_t)lane * 8 * kWords;
-    long long *stw = const_cast<long long *>(st) + base;
-    i128 g[8], h[8];
+    // this bin's cells: the smaller child from staging, the larger = parent - smaller
+    const int64_t cbase = ((int64_t)jj * kBins + b) * kWords;
+    const longlong2 sa = *reinterpret_cast<const longlong2 *>(st + cbase);
+    const longlong2 sd = *reinterpret_cast<const longlong2 *>(st + cbase + 2);
+    longlong2 ca[NS], cd[NS];
 #pragma unroll
-    for (int b = 0; b < 8; b++) {
-        const longlong2 *sp = reinterpret_cast<const longlong2 *>(st + base + b * kWords);
-        longlong2 a = sp[0], d = sp[1];
-        if (!is_small) {
-            const longlong2 *pp = reinterpret_cast<const longlong2 *>(par + base + b * kWords);
-            const longlong2 pa = pp[0], pd = pp[1];
-            a = make_longlong2(pa.x - a.x, pa.y - a.y);
-            d = make_longlong2(pd.x - d.x, pd.y - d.y);
-        }
-        if (write_pool) {
-            longlong2 *op = reinterpret_cast<longlong2 *>(pc + base + b * kWords);
-            op[0] = a;
-            op[1] = d;
-        }
-        g[b] = cell(a.x, a.y);
-        h[b] = cell(d.x, d.y);
-    }
-    // The staging cells are read once: zero them for the next level's atomic
-    // adds once both warps of this (task, feature) pair have read them.
-    if (ROOT) {
-        __syncwarp();
-    } else {
-        switch (warp >> 1) {   // a named barrier per warp pair (constant ids)
-            case 0: asm volatile("bar.sync 1, 64;" ::: "memory"); break;
-            case 1: asm volatile("bar.sync 2, 64;" ::: "memory"); break;
-            case 2: asm volatile("bar.sync 3, 64;" ::: "memory"); break;
-            default: asm volatile("bar.sync 4, 64;" ::: "memory"); break;
+    for (int s = 0; s < NS; s++) {
+        if (small[s]) {
+            ca[s] = sa;
+            cd[s] = sd;
+        } else {
+            const longlong2 pa = *reinterpret_cast<const longlong2 *>(par + cbase);
+            const longlong2 pd = *reinterpret_cast<const longlong2 *>(par + cbase + 2);
+            ca[s] = make_longlong2(pa.x - sa.x, pa.y - sa.y);
+            cd[s] = make_longlong2(pd.x - sd.x, pd.y - sd.y);
         }
     }
-    if (side == 0) {
+    // the staging cell is read by this thread only: zero it for the next level's adds
+    *reinterpret_cast<longlong2 *>(st + cbase) = make_longlong2(0, 0);
+    *reinterpret_cast<longlong2 *>(st + cbase + 2) = make_longlong2(0, 0);
+    DNode nd[NS];
+    i128 TG[NS], TH[NS];
 #pragma unroll
-        for (int v = 0; v < 8 * kWords; v += 2)
-            *reinterpret_cast<longlong2 *>(stw + v) = make_longlong2(0, 0);
+    for (int s = 0; s < NS; s++) {
+        nd[s] = nodes[ch[s]];
+        long long *pc = pool + (int64_t)ch[s] * words;
+        if (nd[s].depth < pool_depth) {   // the cells; the totals always (level close)
+            *reinterpret_cast<longlong2 *>(pc + cbase) = ca[s];
+            *reinterpret_cast<longlong2 *>(pc + cbase + 2) = cd[s];
+        }
+        long long t4[4];
+#pragma unroll
+        for (int q4 = 0; q4 < 4; q4++)
+            t4[q4] = small[s] ? st_tot[q4] : par[(int64_t)nf * kBins * kWords + q4] - st_tot[q4];
+        TG[s] = cell(t4[0], t4[1]);
+        TH[s] = cell(t4[2], t4[3]);
+        if (jj == 0 && b < kTotWords) {
+            const int64_t o = (int64_t)nf * kBins * kWords + b;
+            pc[o] = small[s] ? st_tot[b] : par[o] - st_tot[b];
+        }
     }
+    // prefix over the bins: v = {g_0, h_0, g_1, h_1}
+    i128 v[2 * NS], tot[2 * NS];
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+        v[2 * s] = cell(ca[s].x, ca[s].y);
+        v[2 * s + 1] = cell(cd[s].x, cd[s].y);
+    }
+    block_scan_i128<2 * NS>(v, tot, s_w);
     const int f = fidx[jj];
     const int nb = counts[f];
     const int sb = skipb[f];
     const double sc = pow2(-S);
-    const double Gd = __dmul_rn(i128_to_double(TG), sc), Hd = __dmul_rn(i128_to_double(TH), sc);
-    const bool eval = nd.depth < max_depth && nd.n >= msl && Hd >= mcw && nb >= 2;
-    double bg = -1e9;
-    int bb = -1;
-    if (eval) {
-        const double parent_term = __ddiv_rn(__dmul_rn(Gd, Gd), __dadd_rn(Hd, lam));
-        feature_best(g, h, TG, TH, nb, sb, S, lam, mcw, parent_term, bg, bb);
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+        // the skipped bin's cell is node total - all other cells: bins >= sb gain the difference
+        i128 pg = v[2 * s], ph = v[2 * s + 1];
+        if (b >= sb) {
+            pg += TG[s] - tot[2 * s];
+            ph += TH[s] - tot[2 * s + 1];
+        }
+        const double Gd = __dmul_rn(i128_to_double(TG[s]), sc), Hd = __dmul_rn(i128_to_double(TH[s]), sc);
+        const bool eval = nd[s].depth < max_depth && nd[s].n >= msl && Hd >= mcw && nb >= 2;
+        double bg = -1e9;
+        int bb = -1;
+        if (eval && b <= nb - 2) {
+            const double parent_term = __ddiv_rn(__dmul_rn(Gd, Gd), __dadd_rn(Hd, lam));
+            const double GL = __dmul_rn(i128_to_double(pg), sc);
+            const double HL = __dmul_rn(i128_to_double(ph), sc);
+            const double GR = __dmul_rn(i128_to_double(TG[s] - pg), sc);
+            const double HR = __dmul_rn(i128_to_double(TH[s] - ph), sc);
+            if (!(HL < mcw || HR < mcw)) {
+                bg = __dsub_rn(__dadd_rn(__ddiv_rn(__dmul_rn(GL, GL), __dadd_rn(HL, lam)),
+                                         __ddiv_rn(__dmul_rn(GR, GR), __dadd_rn(HR, lam))),
+                               parent_term);
+                bb = b;
+            }
+        }
+        // argmax: larger gain, ties -> lower bin (the reference's strict '>' over ascending bins)
+        for (int o = 16; o > 0; o >>= 1) {
+            const double og = __shfl_xor_sync(0xffffffffu, bg, o);
+            const int ob = __shfl_xor_sync(0xffffffffu, bb, o);
+            if (better(og, ob < 0 ? -1 : 0, ob, bg, bb < 0 ? -1 : 0, bb)) { bg = og; bb = ob; }
+        }
+        if (lane == 0) {
+            s_bg[s][warp] = bg;
+            s_bb[s][warp] = bb;
+        }
     }
-    if (lane == 0) {
+    __syncthreads();
+    if (b < NS) {
+        const int s = b;
+        double bg = s_bg[s][0];
+        int bb = s_bb[s][0];
+        for (int u = 1; u < kSplitThreads / 32; u++)
+            if (better(s_bg[s][u], s_bb[s][u] < 0 ? -1 : 0, s_bb[s][u], bg, bb < 0 ? -1 : 0, bb)) {
+                bg = s_bg[s][u];
+                bb = s_bb[s][u];
+            }
         FBest o;
         o.gain = bg;
         o.bin = bb < 0 ? 0 : bb;
         o.valid = bb >= 0 ? 1 : 0;
-        fbest[(int64_t)(2 * k + side) * nf + jj] = o;
+        fbest[(int64_t)(2 * k + s) * nf + jj] = o;
     }
 }
 
