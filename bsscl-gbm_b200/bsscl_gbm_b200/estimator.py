@@ -12,8 +12,9 @@ constructor and 'auto' resolution (E:1820-1923, E:1925-2029), ``fit``
 Every boosting round runs on the GPU through libgbm_b200.so (``gbm_round``);
 predict_proba runs ``gbm_predict``.  There is no CPU path: ``device`` must
 name a CUDA device ('b200', 'cuda', 'cuda:N'), and a missing device or
-library raises.  Binary log-loss only; the reference's other objectives,
-GOSS, DART and categorical features raise NotImplementedError.
+library raises.  Objectives: binary log-loss, multi-class softmax and
+regression (mse / mae); LambdaRank, focal and custom objectives, GOSS, DART
+and categorical features raise NotImplementedError.
 
 Row sharding: when ``torch.distributed`` is initialised with more than one
 rank, every rank passes the same full ``X``/``y`` and trains on its
@@ -241,15 +242,10 @@ class HybridHistGBMNumbaV1_0_1:
         else:
             self.max_leaves = 31
         if self.verbose:
-            print("  Adaptive Hyperparameters:")
-            print(f"     n_estimators:  {self.n_estimators}")
-            print(f"     max_depth:     {self.max_depth} (from {n} samples)")
-            print(f"     learning_rate: {self.learning_rate:.4f}")
-            print(f"     n_bins:        {self.n_bins} (from {p} features)")
-            print(f"     gamma:         {self.gamma:.2f}")
-            print(f"     min_child_w:   {self.min_child_weight:.1f}")
-            print(f"     subsample:     {self.subsample}")
-            print(f"     colsample:     {self.colsample_bytree}")
+            resolved = {k: getattr(self, k) for k in ('n_estimators', 'max_depth', 'learning_rate', 'n_bins',
+                                                      'gamma', 'min_child_weight', 'subsample',
+                                                      'colsample_bytree', 'max_leaves', 'reg_lambda')}
+            print(f"[bsscl-gbm-b200] {n} x {p}, resolved parameters: {resolved}")
 
     # ------------------------------------------------------------------
     # class weights and base score (E:2570-2603, E:2829-2835)

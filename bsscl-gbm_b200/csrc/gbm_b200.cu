@@ -70,8 +70,6 @@ struct gbm_ctx {
     const uint8_t *xc_cur = nullptr;   // the buffer of the round being enqueued
     int32_t *d_counts = nullptr;
     std::vector<int32_t> counts;
-    int16_t *d_skipb = nullptr;        // per feature: the bin the histogram skips
-    std::vector<double> skip_keep;     // per feature: share of rows outside that bin
     uint8_t *d_y = nullptr;
     double *d_F = nullptr;
     longlong2 *d_q = nullptr;
@@ -86,17 +84,15 @@ struct gbm_ctx {
     unsigned *d_side = nullptr;                    // partition side bits, per tile
     int32_t *d_cnt = nullptr, *d_off = nullptr, *d_total = nullptr;
     int32_t *d_blist = nullptr, *d_fidx = nullptr;
-    int32_t *d_bwp = nullptr;          // histogram cost prefix over the active blocks
     int16_t *d_fpos = nullptr, *d_fbi = nullptr;
-    int hist_grid = 0;                 // k_hist CTAs: one wave of 2 per SM
+    int hist_grid = 0;                 // 2 CTAs per SM: the grid of the multi-rank staging kernels
     int sms = 0;
     // Histogram launches of a tree, from the root, that use k_hist2 (big
     // segments: its conflict-free atomics win); the deeper, smaller
     // segments use k_hist, whose two CTAs per SM overlap one CTA's zeroing
     // and flush with the other's atomics.  Measured on config 4: 3 levels
     // 1110 rounds/s, 0 levels 1077, all levels 1057.
-    int hist_v2_levels = 3;
-    int hist_kernel = 3;               // 3: k_hist3 on every level; 2: k_hist2 / k_hist split by level
+    bool hist_compact = true;          // histograms on the round's packed feature blocks (k_compact_feat)
     int hist_seg_cost = 150000;        // k_hist3's cost of a segment in row units (22 per row; measured)
     int nf_cap = 0;
     long long *d_pool = nullptr;       // node histograms: slot i = node i
@@ -146,7 +142,7 @@ struct gbm_ctx {
     // end; gbm_fit_rounds keeps up to kRing rounds queued.
     struct Slot {
         int32_t *h_tg = nullptr, *d_tg = nullptr;   // the round's row swap targets
-        int32_t *h_feat = nullptr;     // fidx [p] | blist [nblk] | bwp [nblk + 1] | nb
+        int32_t *h_feat = nullptr;     // fidx [p] | blist [nblk] | nb
         int32_t *d_fidx_c = nullptr;   // the round's fidx for its feature compaction on cst
         bool xc_on_cst = false;        // the round's packed blocks are made on cst (k_compact_feat)
         int16_t *h_fpos = nullptr;     // fpos [nblk * 16] | fbi [p]
@@ -613,23 +609,14 @@ struct RoundFeat {
     int nf;
     std::vector<int32_t> blist;
     std::vector<int16_t> fpos;
-    double upd_per_row = 0.0;   // histogram cell updates per row (selected features, skipped bins out)
+    double upd_per_row = 0.0;   // histogram cell updates per row: the selected features
 };
 
-// Histogram cost of a row in an active block: its loads and flush share
-// (about six feature updates' worth, measured on B200 by sweeping this
-// base) plus one unit per selected feature.
-int block_weight(const RoundFeat &rf, int blk) {
-    int w = 6;
-    for (int k = 0; k < kBlk; k++) w += rf.fpos[(size_t)blk * kBlk + k] >= 0;
-    return w;
-}
-
 // The histograms read the round's packed feature blocks (k_compact_feat):
-// the default (GBM_HIST_KERNEL unset or 3) whenever the compaction's staging
+// the default (GBM_HIST_COMPACT unset or 1) whenever the compaction's staging
 // of 256 rows x every column block fits its shared memory (p <= 608).
 bool compact_hist(const gbm_ctx *ctx) {
-    return ctx->hist_kernel == 3 && ctx->nblk <= 38;
+    return ctx->hist_compact && ctx->nblk <= 38;
 }
 
 // Per-slot pinned staging, sized for the data.
@@ -686,22 +673,19 @@ int setup_features(gbm_ctx *ctx, int si, const int32_t *fidx, int nf, RoundFeat 
         if (any) rf.blist.push_back(b);
     }
     const int nb = (int)rf.blist.size();
-    int32_t *h_blist = s.h_feat + ctx->p, *h_bwp = h_blist + ctx->nblk;
+    int32_t *h_blist = s.h_feat + ctx->p;
     int16_t *h_fbi = s.h_fpos + (size_t)ctx->nblk * kBlk;
     std::memcpy(s.h_feat, fidx, sizeof(int32_t) * nf);
     std::memcpy(h_blist, rf.blist.data(), sizeof(int32_t) * nb);
-    h_bwp[0] = 0;
     for (int bi = 0; bi < nb; bi++) {
-        h_bwp[bi + 1] = h_bwp[bi] + block_weight(rf, rf.blist[bi]);
         for (int k = 0; k < kBlk; k++) {
             int jj = rf.fpos[(size_t)rf.blist[bi] * kBlk + k];
             if (jj >= 0) h_fbi[jj] = (int16_t)bi;
         }
     }
-    h_bwp[ctx->nblk + 1] = nb;   // the count, after the longest bwp
+    h_blist[ctx->nblk] = nb;   // the count, after the longest list
     std::memcpy(s.h_fpos, rf.fpos.data(), sizeof(int16_t) * rf.fpos.size());
-    rf.upd_per_row = 0.0;
-    for (int jj = 0; jj < nf; jj++) rf.upd_per_row += ctx->skip_keep[(size_t)fidx[jj]];
+    rf.upd_per_row = nf;
     s.upd_per_row = rf.upd_per_row;
     return GBM_OK;
 }
@@ -723,7 +707,7 @@ int enqueue_features(gbm_ctx *ctx, int si, int nf) {
                        ctx->st));
     CK(cudaMemcpyAsync(ctx->d_fbi, s.h_fpos + (size_t)ctx->nblk * kBlk, sizeof(int16_t) * nf, cudaMemcpyHostToDevice,
                        ctx->st));
-    CK(cudaMemcpyAsync(ctx->d_blist, s.h_feat + ctx->p, sizeof(int32_t) * (2 * (size_t)ctx->nblk + 2),
+    CK(cudaMemcpyAsync(ctx->d_blist, s.h_feat + ctx->p, sizeof(int32_t) * ((size_t)ctx->nblk + 1),
                        cudaMemcpyHostToDevice, ctx->st));
     const bool packed_on_cst = s.xc_on_cst;
     s.xc_on_cst = false;   // a later round in this slot may take another path
@@ -972,12 +956,12 @@ bool device_replay(const gbm_ctx *ctx, const gbm_params *P) {
 
 // ---- launches -----------------------------------------------------------------
 
-// The histograms of the tasks at *ntask_p on ctx->hist_grid equal-work CTAs.
+// The histograms of the tasks at *ntask_p: one k_hist3 CTA per SM.
 // The staging histograms are zero here: the split search zeroes the cells
 // it reads and the level close the totals.
-int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int level) {
-    // d_blist holds blist [nblk] | bwp [nblk + 1] | nb
-    const int32_t *d_bwp = ctx->d_blist + ctx->nblk, *d_nb = ctx->d_blist + 2 * ctx->nblk + 1;
+int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p) {
+    // d_blist holds blist [nblk] | nb
+    const int32_t *d_nb = ctx->d_blist + ctx->nblk;
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (ctx->profiling) {
         TRY(timing_pair(ctx, 0, e0, e1));
@@ -991,20 +975,11 @@ int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p, int level
                    ctx->st, ctx->xc_cur, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p,
                    ctx->d_blist, d_nb, ctx->d_fpos, rf.nf, ctx->d_q, stage, par, ctx->pst_stride,
                    ctx->hist_seg_cost));
-    else if (ctx->hist_kernel >= 3)
+    else
         TRY(launch(ctx, k_hist3<false>, dim3(ctx->sms), dim3(kHistV3Threads), (size_t)kAccV3Words * sizeof(unsigned),
                    ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p,
                    ctx->d_blist, d_nb, ctx->d_fpos, rf.nf, ctx->d_q, stage, par, ctx->pst_stride,
                    ctx->hist_seg_cost));
-    else if (level < ctx->hist_v2_levels)
-        TRY(launch(ctx, k_hist2, dim3(ctx->sms), dim3(kHistV2Threads), (size_t)kAccV2Words * sizeof(unsigned),
-                   ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p,
-                   ctx->d_blist, d_nb, ctx->d_fpos, ctx->d_skipb, rf.nf, ctx->d_q, stage, par, ctx->pst_stride));
-    else
-        TRY(launch(ctx, k_hist, dim3(ctx->hist_grid), dim3(kHistThreads), (size_t)kAccWords * sizeof(unsigned),
-                   ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p,
-                   ctx->d_blist, d_bwp, d_nb, ctx->d_fpos, ctx->d_skipb, rf.nf, ctx->d_q, stage, par,
-                   ctx->pst_stride));
     if (e1) TRY(record_ev(ctx, e1, ctx->st));
     ctx->hist_launches++;
     return GBM_OK;
@@ -1104,7 +1079,7 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, const Ne
     long long *cw = ctx->comm ? sbase + (int64_t)rf.nf * kBins * kWords + kCountWord : nullptr;
     TRY(launch(ctx, k_root_plan, dim3(1), dim3(1), 0, ctx->st, ctx->d_total, (const long long *)nullptr, ctx->d_nodes,
                ctx->d_htask, ctx->d_hprefix, ints(ctx, I_NODES), cw, par, ctx->pst_stride));
-    TRY(launch_hist(ctx, rf, ints(ctx, I_ONE), 0));
+    TRY(launch_hist(ctx, rf, ints(ctx, I_ONE)));
     if (ctx->comm) {
         // this rank's root partial into lpool[0], for the first level's subtractions
         TRY(launch(ctx, k_stage_left, dim3(std::max(1, 2 * ctx->hist_grid / 8), 1), dim3(256), 0, ctx->st,
@@ -1118,7 +1093,7 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, const Ne
     TRY(launch(ctx, k_split_bins<true>, dim3(rf.nf, 1), dim3(kSplitThreads), 0, ctx->st,
         (const DNode *)ctx->d_nodes, (const int *)nullptr, (const int *)nullptr, (const HistTask *)ctx->d_htask,
         ctx->d_stage, ctx->d_pool, rf.nf, (const int32_t *)ctx->d_fidx, (const int32_t *)ctx->d_counts,
-        (const int16_t *)ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight,
+        ctx->S, P->reg_lambda, P->min_child_weight,
         (long long)P->min_samples_leaf, P->max_depth, pool_depth(P), ctx->d_fbest));
     return launch_close(ctx, rf, P, true, nullptr, nullptr, ctx->d_lvl[0], ints(ctx, I_LVL0), np);
 }
@@ -1162,7 +1137,7 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
                ctx->d_tmp, (const PartTask *)ctx->d_ptask, (const int *)lvl_cnt, (const int *)ints(ctx, I_TILES),
                (const unsigned *)ctx->d_side, (const int32_t *)ctx->d_tile_cnt, ctx->d_nleft, ctx->d_nodes,
                (const int *)lvl, gl, ctx->d_htask, ctx->d_hprefix, (unsigned *)ints(ctx, I_DONE)));
-    TRY(launch_hist(ctx, rf, lvl_cnt, hist_level));
+    TRY(launch_hist(ctx, rf, lvl_cnt));
     if (ctx->comm) {
         const int cx = std::max(1, (2 * ctx->hist_grid + W_ub - 1) / W_ub);
         unsigned long long *sync = ctx->p2p ? ctx->d_sync : nullptr;
@@ -1177,7 +1152,7 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
     TRY(launch(ctx, k_split_bins<false>, dim3(rf.nf, W_ub), dim3(kSplitThreads), 0, ctx->st,
         (const DNode *)ctx->d_nodes, (const int *)lvl, (const int *)lvl_cnt, (const HistTask *)ctx->d_htask,
         ctx->d_stage, ctx->d_pool, rf.nf, (const int32_t *)ctx->d_fidx, (const int32_t *)ctx->d_counts,
-        (const int16_t *)ctx->d_skipb, ctx->S, P->reg_lambda, P->min_child_weight,
+        ctx->S, P->reg_lambda, P->min_child_weight,
         (long long)P->min_samples_leaf, P->max_depth, pool_depth(P), ctx->d_fbest));
     TRY(launch_close(ctx, rf, P, false, lvl, lvl_cnt, next, next_cnt, next ? np : NextPlan()));
     ctx->waves++;
@@ -1399,47 +1374,6 @@ void enforce_monotone(HostTree &T, const int32_t *mono) {   // E:2461-2499
     }
 }
 
-// The histogram kernel skips, per feature, the bin holding the most rows
-// over all ranks (ties -> lowest bin); every rank must skip the same one.
-int choose_skip_bins(gbm_ctx *ctx) {
-    int64_t cells = (int64_t)ctx->nblk * kBlk * kBins;
-    unsigned long long *d_cnt = nullptr;
-    TRY(dalloc(ctx, &d_cnt, (size_t)cells));
-    std::vector<unsigned long long> cnt((size_t)cells);
-    int rc = GBM_OK;
-    do {
-        cudaError_t e = cudaMemsetAsync(d_cnt, 0, sizeof(unsigned long long) * cells, ctx->st);
-        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "memset: %s", cudaGetErrorString(e)); break; }
-        dim3 g((unsigned)std::min<int64_t>(1024, (ctx->n + 255) / 256), (unsigned)ctx->nblk);
-        k_bincount<<<g, 256, 0, ctx->st>>>(ctx->d_xb, ctx->n, ctx->nblk, d_cnt);
-        ctx->launches++;
-        e = cudaGetLastError();
-        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "k_bincount: %s", cudaGetErrorString(e)); break; }
-        if (ctx->comm) {
-            rc = allreduce_i64(ctx, (long long *)d_cnt, cells);
-            if (rc != GBM_OK) break;
-        }
-        e = cudaMemcpyAsync(cnt.data(), d_cnt, sizeof(unsigned long long) * cells, cudaMemcpyDeviceToHost, ctx->st);
-        if (e != cudaSuccess) { rc = fail(ctx, GBM_ERR_CUDA, "bincount copy: %s", cudaGetErrorString(e)); break; }
-        rc = sync_stream(ctx);
-    } while (0);
-    dfree(ctx, d_cnt);
-    if (rc != GBM_OK) return rc;
-    std::vector<int16_t> skip((size_t)ctx->nblk * kBlk, (int16_t)0);
-    ctx->skip_keep.assign((size_t)ctx->p, 1.0);
-    for (int f = 0; f < ctx->p; f++) {
-        int best = 0;
-        unsigned long long tot = 0;
-        for (int b = 0; b < ctx->counts[f]; b++) tot += cnt[(size_t)f * kBins + b];
-        for (int b = 1; b < ctx->counts[f]; b++)
-            if (cnt[(size_t)f * kBins + b] > cnt[(size_t)f * kBins + best]) best = b;
-        skip[(size_t)f] = (int16_t)best;
-        if (tot) ctx->skip_keep[(size_t)f] = 1.0 - (double)cnt[(size_t)f * kBins + best] / (double)tot;
-    }
-    TRY(dalloc(ctx, &ctx->d_skipb, skip.size()));
-    CK(cudaMemcpyAsync(ctx->d_skipb, skip.data(), sizeof(int16_t) * skip.size(), cudaMemcpyHostToDevice, ctx->st));
-    return sync_stream(ctx);
-}
 
 int alloc_round_fixed(gbm_ctx *ctx) {
     TRY(dalloc(ctx, &ctx->d_mask, (size_t)ctx->n));
@@ -1450,7 +1384,7 @@ int alloc_round_fixed(gbm_ctx *ctx) {
     TRY(dalloc(ctx, &ctx->d_off, (size_t)ntile));
     TRY(dalloc(ctx, &ctx->d_total, 1));
     TRY(dalloc(ctx, &ctx->d_count64, 1));
-    TRY(dalloc(ctx, &ctx->d_blist, (size_t)2 * ctx->nblk + 2));   // blist | bwp | nb
+    TRY(dalloc(ctx, &ctx->d_blist, (size_t)ctx->nblk + 1));   // blist | nb
     TRY(dalloc(ctx, &ctx->d_fbi, (size_t)ctx->p));
     TRY(dalloc(ctx, &ctx->d_fpos, (size_t)ctx->nblk * kBlk));
     TRY(dalloc(ctx, &ctx->d_ints, (size_t)I_COUNT));
@@ -1750,7 +1684,6 @@ int begin_bins(gbm_ctx *ctx, int64_t n, int32_t p, const int32_t *bin_counts) {
 // Everything that depends on the bins once they are on the device.
 int finish_bins(gbm_ctx *ctx) {
     TRY(sync_stream(ctx));
-    TRY(choose_skip_bins(ctx));
     TRY(alloc_round_fixed(ctx));
     TRY(dalloc(ctx, &ctx->d_y, (size_t)ctx->n));
     TRY(dalloc(ctx, &ctx->d_F, (size_t)ctx->n));
@@ -1901,19 +1834,14 @@ int gbm_ctx_create(int32_t device, gbm_ctx **out) {
     int sms = 0;
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
     ctx->sms = std::max(sms, 1);
-    ctx->hist_grid = 2 * ctx->sms;   // one wave of 2 per SM (measured best: fewer flushes)
-    if (const char *e = std::getenv("GBM_HIST_V2_LEVELS")) ctx->hist_v2_levels = std::atoi(e);
-    if (const char *e = std::getenv("GBM_HIST_KERNEL")) ctx->hist_kernel = std::atoi(e);
+    ctx->hist_grid = 2 * ctx->sms;
+    if (const char *e = std::getenv("GBM_HIST_COMPACT")) ctx->hist_compact = std::atoi(e) != 0;
     if (const char *e = std::getenv("GBM_HIST_SEG_COST")) ctx->hist_seg_cost = std::max(0, std::atoi(e));
     CK(cudaFuncSetAttribute(k_hist3<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             (int)(kAccV3Words * sizeof(unsigned))));
     CK(cudaFuncSetAttribute(k_hist3<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             (int)(kAccV3Words * sizeof(unsigned))));
     CK(cudaFuncSetAttribute(k_compact_feat, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-    CK(cudaFuncSetAttribute(k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            kAccWords * (int)sizeof(unsigned)));
-    CK(cudaFuncSetAttribute(k_hist2, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            kAccV2Words * (int)sizeof(unsigned)));
     // a function attribute is shared by every context of the process: set
     // the largest node-table copy any context may launch with
     CK(cudaFuncSetAttribute(k_replay_leaf, cudaFuncAttributeMaxDynamicSharedMemorySize, kReplaySmemMax));
@@ -1937,7 +1865,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     for (auto &s : ctx->slot)
         for (cudaEvent_t e : s.tev) cudaEventDestroy(e);
     if (ctx->comm) gbm_comm_destroy(ctx->comm);
-    void *dev_ptrs[] = {ctx->d_xb, ctx->d_xc[0], ctx->d_xc[1], ctx->d_counts, ctx->d_skipb, ctx->d_y, ctx->d_F, ctx->d_q, ctx->d_mask,
+    void *dev_ptrs[] = {ctx->d_xb, ctx->d_xc[0], ctx->d_xc[1], ctx->d_counts, ctx->d_y, ctx->d_F, ctx->d_q, ctx->d_mask,
                         ctx->d_rows, ctx->d_tmp, ctx->d_cnt, ctx->d_off, ctx->d_total, ctx->d_blist, ctx->d_fidx,
                         ctx->d_fpos, ctx->d_pool, ctx->d_lpool, ctx->d_stage, ctx->d_fbest, ctx->d_htask, ctx->d_hprefix,
                         ctx->d_ptask, ctx->d_tile_cnt, ctx->d_nleft,
@@ -1987,9 +1915,6 @@ int gbm_ctx_init_comm(gbm_ctx *ctx, const void *uid, int32_t nranks, int32_t ran
     ctx->p2p_tried_stride = 0;
     if (nranks == 1) return GBM_OK;
     TRY(gbm_comm_create(&ctx->comm, uid, nranks, rank, ctx->timeout_ms, ctx->err));
-    // bins uploaded before the communicator chose their skipped bins from this
-    // rank's rows alone: choose again from the occupancy of all ranks
-    if (ctx->have_bins) TRY(choose_skip_bins(ctx));
     return GBM_OK;
 }
 

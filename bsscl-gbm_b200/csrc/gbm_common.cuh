@@ -14,11 +14,11 @@ constexpr int kBlk = 16;            // features per column block (one 16-byte lo
 constexpr int kWords = 4;           // g_hi, g_lo, h_hi, h_lo per histogram cell
 constexpr int kTotWords = 6;        // after the cells: totals (G hi/lo, H hi/lo), left count, pad
 constexpr int kCountWord = 4;       // the slot's left-count word (multi-rank staging)
-constexpr int kChunk = 16384;       // max rows one CTA adds into one cell (R_max)
-constexpr int kHistThreads = 512;
+// The fixed-point exponent: S = 62 - ceil(log2(kChunk * max(1, w_max))), so
+// |q| <= 2^48 for every row and 2^15 rows of q sum to less than 2^63.
+constexpr int kChunk = 16384;
 constexpr int kDig = 17;            // low/mid digit width of the shared-memory accumulators
-constexpr int kAccWords = 6 * kBlk * kBins;   // [g0 g1 g2 h0 h1 h2][16][256] uint32
-constexpr int kHistV2Weight = 6 + kBlk;   // k_hist2's cost of a row in any block
+constexpr int kRowWeight = 6 + kBlk;     // k_hist3's cost of a row of a block (its loads + 16 steps)
 constexpr int kPartTile = 4096;     // rows per partition CTA
 constexpr int kPartThreads = 512;   // 8 rows per thread, loads in flight together
 constexpr int kPartWords = kPartTile / 32;   // side bits of a tile

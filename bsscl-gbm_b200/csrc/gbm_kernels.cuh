@@ -44,25 +44,6 @@ __global__ void k_pack_bins(const T *__restrict__ src, int64_t rows, int p, int6
     reinterpret_cast<uint4 *>(xb)[(int64_t)b * n + row0 + r] = o;
 }
 
-// Bin occupancy of every feature over this rank's rows.
-__global__ void k_bincount(const uint8_t *__restrict__ xb, int64_t n, int nblk,
-                           unsigned long long *__restrict__ cnt) {
-    __shared__ unsigned s[kBlk * kBins];
-    int blk = blockIdx.y;
-    for (int k = threadIdx.x; k < kBlk * kBins; k += blockDim.x) s[k] = 0u;
-    __syncthreads();
-    const uint4 *xv = reinterpret_cast<const uint4 *>(xb) + (int64_t)blk * n;
-    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n;
-         r += (int64_t)gridDim.x * blockDim.x) {
-        uint4 v = xv[r];
-        unsigned w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int k = 0; k < kBlk; k++) atomicAdd(&s[k * kBins + ((w[k >> 2] >> ((k & 3) * 8)) & 0xff)], 1u);
-    }
-    __syncthreads();
-    for (int k = threadIdx.x; k < kBlk * kBins; k += blockDim.x)
-        if (s[k]) atomicAdd(&cnt[(int64_t)blk * kBlk * kBins + k], (unsigned long long)s[k]);
-}
 
 // F = base score for every row (E:2837), and the first round's quantised (g, h).
 __global__ void k_init_grad(double *__restrict__ F, const uint8_t *__restrict__ y, int64_t n, double base,
@@ -507,190 +488,8 @@ __global__ void k_iota(int32_t *__restrict__ a, int64_t n) {
 // histograms
 // ===========================================================================
 
-// The histogram work of one launch is the rows of every task (node) for
-// every active feature block, laid out block-major: block bi, then task t,
-// then the task's rows.  A row of block bi costs w_bi = bwp[bi+1] - bwp[bi]
-// (2 + the block's selected features), so the launch costs T = bwp[nb] * R
-// for R rows over all tasks.  CTA c of G takes the rows whose cost position
-// lies in [B_c, B_c+1), B_c = floor(c T / G): every CTA gets the same work
-// whatever the tasks' sizes, and a launch is exactly G / (2 per SM) waves.
-// A (block, task) segment whose rows all fall in one CTA's range, and no
-// more than kChunk of them, is stored directly by that CTA; every other
-// segment is added atomically into the staging histogram, which is zero
-// between uses.
 __device__ __forceinline__ long long cost_bound(long long c, long long T, long long G) { return c * T / G; }
 __device__ __forceinline__ long long ceil_div_ll(long long a, long long b) { return (a + b - 1) / b; }
-
-// Each row's q (int64) is split into three digits, q = top*2^34 + mid*2^17 +
-// low with low, mid in [0, 2^17) and top signed, and each digit is summed in
-// its own 32-bit shared-memory word: at most kChunk = 2^14 rows between two
-// flushes keep every digit sum inside 32 bits, and native 32-bit shared
-// atomics are much faster than 64-bit ones.  Each feature skips its most
-// frequent bin (the NaN bin, typically); that cell is rebuilt exactly by the
-// split kernel as node total - sum(other cells).  Block 0's pieces also sum
-// the node totals.  (E:582-596 root, E:723-737 smaller child.)
-__global__ void __launch_bounds__(kHistThreads, 2)
-k_hist(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
-       const int32_t *__restrict__ rows1, const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
-       const int *__restrict__ ntask_p, const int32_t *__restrict__ blist, const int32_t *__restrict__ bwp,
-       const int32_t *__restrict__ nb_p, const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
-       const longlong2 *__restrict__ q, long long *__restrict__ stage_hist,
-       const unsigned long long *__restrict__ par_word, int64_t par_stride) {
-    griddep_wait();
-    if (par_word) stage_hist += (int64_t)(*par_word & 1ull) * par_stride;   // peer exchange: this level's buffer
-    extern __shared__ unsigned acc[];   // [6][16][256]
-    __shared__ long long s_tot[2][kHistThreads / 32];
-    const int ntask = *ntask_p;
-    const int nb = *nb_p;
-    if (ntask <= 0 || nb <= 0) return;
-    const long long R = rpre[ntask];
-    const long long T = (long long)bwp[nb] * R;
-    if (T <= 0) return;
-    const long long G = gridDim.x;
-    const long long B0 = cost_bound(blockIdx.x, T, G), B1 = cost_bound(blockIdx.x + 1, T, G);
-    if (B0 >= B1) return;
-    const int lane = threadIdx.x & 31;
-    const int64_t slot_words = slot_words_for(nf);
-    int bi = 0;
-    while (bi + 1 < nb && (long long)bwp[bi + 1] * R <= B0) bi++;
-    for (; bi < nb; bi++) {
-        const long long base = (long long)bwp[bi] * R;
-        if (base >= B1) break;
-        const int w = bwp[bi + 1] - bwp[bi];
-        const int k0 = (int)(B0 > base ? ceil_div_ll(B0 - base, w) : 0);
-        const int k1 = (int)min(R, ceil_div_ll(B1 - base, w));
-        if (k0 >= k1) continue;
-        const int blk = blist[bi];
-        unsigned mask = 0;
-        unsigned skipw[4] = {0u, 0u, 0u, 0u};   // the skipped bin of each feature, one byte each
-#pragma unroll
-        for (int k = 0; k < kBlk; k++) {
-            bool sel = fpos[blk * kBlk + k] >= 0;
-            mask |= (sel ? 1u : 0u) << k;
-            skipw[k >> 2] |= (sel ? (unsigned)skipb[blk * kBlk + k] & 0xffu : 0u) << ((k & 3) * 8);
-        }
-        const uint4 *xv = reinterpret_cast<const uint4 *>(xb) + (int64_t)blk * n;
-        // the task holding row k0 (last t with rpre[t] <= k0)
-        int t;
-        {
-            int lo = 0, hi = ntask - 1;
-            while (lo < hi) {
-                int mid = (lo + hi + 1) >> 1;
-                if (rpre[mid] <= k0) lo = mid; else hi = mid - 1;
-            }
-            t = lo;
-        }
-        for (int k = k0; k < k1; t++) {
-            const int t0 = rpre[t], t1 = rpre[t + 1];
-            if (t1 <= k) continue;
-            const HistTask tk = tasks[t];
-            const int32_t *__restrict__ rows = tk.buf ? rows1 : rows0;
-            const int pe = min(k1, t1);
-            const bool single = k == t0 && pe == t1 && (t1 - t0) <= kChunk;
-            long long *dst = stage_hist + (int64_t)tk.stage * slot_words;
-            // the piece [k, pe) of task t, in runs of at most kChunk rows
-            for (int c0 = k; c0 < pe; c0 += kChunk) {
-                const int c1 = min(pe, c0 + kChunk);
-                for (int i = threadIdx.x; i < kAccWords / 4; i += blockDim.x)
-                    reinterpret_cast<uint4 *>(acc)[i] = make_uint4(0u, 0u, 0u, 0u);
-                __syncthreads();
-                const int r0 = (int)tk.begin + (c0 - t0), r1 = (int)tk.begin + (c1 - t0);
-                long long tg = 0, th = 0;
-                for (int rb = r0 + (int)(threadIdx.x & ~31u); rb < r1; rb += blockDim.x) {
-                    const int r = rb + lane;
-                    const bool valid = r < r1;
-                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                    longlong2 qq = make_longlong2(0, 0);
-                    if (valid) {
-                        int row = rows[r];
-                        v = __ldg(xv + row);
-                        qq = __ldg(q + row);
-                    }
-                    tg += qq.x;
-                    th += qq.y;
-                    unsigned dg[3] = {(unsigned)qq.x & 0x1ffffu, (unsigned)(qq.x >> kDig) & 0x1ffffu,
-                                      (unsigned)(int)(qq.x >> (2 * kDig))};
-                    unsigned dh[3] = {(unsigned)qq.y & 0x1ffffu, (unsigned)(qq.y >> kDig) & 0x1ffffu,
-                                      (unsigned)(int)(qq.y >> (2 * kDig))};
-                    unsigned wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int f = 0; f < kBlk; f++) {
-                        if (mask & (1u << f)) {
-                            const int b = (wv[f >> 2] >> ((f & 3) * 8)) & 0xff;
-                            const int sb = (skipw[f >> 2] >> ((f & 3) * 8)) & 0xff;
-                            if (valid && b != sb) {
-                                unsigned *cc = acc + f * kBins + b;
-                                atomicAdd(cc + 0 * kBlk * kBins, dg[0]);
-                                atomicAdd(cc + 1 * kBlk * kBins, dg[1]);
-                                atomicAdd(cc + 2 * kBlk * kBins, dg[2]);
-                                atomicAdd(cc + 3 * kBlk * kBins, dh[0]);
-                                atomicAdd(cc + 4 * kBlk * kBins, dh[1]);
-                                atomicAdd(cc + 5 * kBlk * kBins, dh[2]);
-                            }
-                        }
-                    }
-                }
-                if (bi == 0) {
-                    tg = warp_sum(tg);
-                    th = warp_sum(th);
-                    if (lane == 0) {
-                        s_tot[0][threadIdx.x >> 5] = tg;
-                        s_tot[1][threadIdx.x >> 5] = th;
-                    }
-                }
-                __syncthreads();
-                if (bi == 0 && threadIdx.x < 2) {
-                    long long tot = 0;
-                    for (int w2 = 0; w2 < kHistThreads / 32; w2++) tot += s_tot[threadIdx.x][w2];
-                    long long *o = dst + (int64_t)nf * kBins * kWords + 2 * threadIdx.x;
-                    if (single) {
-                        o[0] = tot >> 32;
-                        o[1] = tot & 0xffffffffll;
-                    } else if (tot) {
-                        atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(tot >> 32));
-                        atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(tot & 0xffffffffll));
-                    }
-                }
-                // flush: lane-consecutive words (g hi, g lo, h hi, h lo of consecutive
-                // cells), so a warp writes or adds 256 contiguous bytes at a time
-                for (int i = threadIdx.x; i < kBlk * kBins * kWords; i += blockDim.x) {
-                    const int idx = i >> 2, wd = i & 3;
-                    const int f = idx >> 8, b = idx & 255;
-                    if (!((mask >> f) & 1u)) continue;
-                    const int jj = fpos[blk * kBlk + f];
-                    const unsigned *dg0 = acc + (wd >> 1) * 3 * kBlk * kBins + idx;
-                    const long long v = ((long long)(int)dg0[2 * kBlk * kBins] << (2 * kDig)) +
-                                        ((long long)dg0[kBlk * kBins] << kDig) + (long long)dg0[0];
-                    const long long x = (wd & 1) ? (v & 0xffffffffll) : (v >> 32);
-                    long long *o = dst + ((int64_t)jj * kBins + b) * kWords + wd;
-                    if (single) *o = x;
-                    else if (x) atomicAdd((unsigned long long *)o, (unsigned long long)x);
-                }
-                __syncthreads();
-            }
-            k = pe;
-        }
-    }
-}
-
-// The same histograms with every shared-memory atomic free of bank
-// conflicts.  Each lane still loads its own row (as in k_hist), but in step
-// k of the row's 16 features lane l adds feature f = (l + k) mod 16, so the
-// 16 lanes of a half-warp touch 16 different features.  Each half-warp h
-// keeps its own copy of every cell, and cell (digit d, bin b, half h,
-// feature f) is the shared word ((d * kBins + b) * 2 + h) * kBlk + f: its
-// bank is 16 h + f, the 32 lanes of an atomic instruction land in 32
-// different banks whatever their bins, and the instruction is one
-// wavefront (k_hist's lanes all add the same feature at random bins, ~3
-// wavefronts).  A row costs the same 16 steps whatever the number of
-// selected features of its block, so the launch's work is split with one
-// weight per block (kHistV2Weight) instead of k_hist's per-feature weights
-// (bwp).
-// The two copies are added at the flush.  Digits, skipped bins, totals and
-// the staging layout are those of k_hist.
-constexpr int kHistV2Threads = 1024;
-constexpr int kDigV2 = kBins * 2 * kBlk;            // words between two digits
-constexpr int kAccV2Words = 6 * kDigV2;            // 192 KB
 
 // v rotated by r bytes (0 <= r < 16): byte k of the result is byte
 // (k + r) mod 16 of v (bytes little-endian, word k / 4).
@@ -712,164 +511,6 @@ __device__ __forceinline__ uint4 rot_bytes(uint4 v, int r) {
 __device__ __forceinline__ unsigned byte_of(const uint4 &v, int k) {
     const unsigned w = (k >> 2) == 0 ? v.x : (k >> 2) == 1 ? v.y : (k >> 2) == 2 ? v.z : v.w;
     return (w >> ((k & 3) * 8)) & 0xffu;
-}
-
-__global__ void __launch_bounds__(kHistV2Threads, 1)
-k_hist2(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
-        const int32_t *__restrict__ rows1, const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
-        const int *__restrict__ ntask_p, const int32_t *__restrict__ blist, const int32_t *__restrict__ nb_p,
-        const int16_t *__restrict__ fpos, const int16_t *__restrict__ skipb, int nf,
-        const longlong2 *__restrict__ q, long long *__restrict__ stage_hist,
-        const unsigned long long *__restrict__ par_word, int64_t par_stride) {
-    griddep_wait();
-    if (par_word) stage_hist += (int64_t)(*par_word & 1ull) * par_stride;   // peer exchange: this level's buffer
-    extern __shared__ unsigned acc[];   // [6][256][2][16]
-    __shared__ long long s_tot[2][kHistV2Threads / 32];
-    const int ntask = *ntask_p;
-    const int nb = *nb_p;
-    if (ntask <= 0 || nb <= 0) return;
-    const long long R = rpre[ntask];
-    const long long T = (long long)kHistV2Weight * nb * R;
-    if (T <= 0) return;
-    const long long G = gridDim.x;
-    const long long B0 = cost_bound(blockIdx.x, T, G), B1 = cost_bound(blockIdx.x + 1, T, G);
-    if (B0 >= B1) return;
-    const int lane = threadIdx.x & 31, half = lane >> 4, fl = lane & 15;
-    const int warp = threadIdx.x >> 5;
-    const int64_t slot_words = slot_words_for(nf);
-    int bi = 0;
-    while (bi + 1 < nb && (long long)kHistV2Weight * (bi + 1) * R <= B0) bi++;
-    for (; bi < nb; bi++) {
-        const long long base = (long long)kHistV2Weight * bi * R;
-        if (base >= B1) break;
-        const int w = kHistV2Weight;
-        const int k0 = (int)(B0 > base ? ceil_div_ll(B0 - base, w) : 0);
-        const int k1 = (int)min(R, ceil_div_ll(B1 - base, w));
-        if (k0 >= k1) continue;
-        const int blk = blist[bi];
-        unsigned mask = 0;
-#pragma unroll
-        for (int k = 0; k < kBlk; k++) mask |= (fpos[blk * kBlk + k] >= 0 ? 1u : 0u) << k;
-        uint4 skipv;   // the skipped bin of each feature, one byte each, rotated like the rows
-        {
-            unsigned sw[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-            for (int k = 0; k < kBlk; k++)
-                sw[k >> 2] |= ((mask >> k) & 1u ? (unsigned)skipb[blk * kBlk + k] & 0xffu : 0u) << ((k & 3) * 8);
-            skipv = rot_bytes(make_uint4(sw[0], sw[1], sw[2], sw[3]), fl);
-        }
-        const unsigned mrot = ((mask | (mask << kBlk)) >> fl) & 0xffffu;   // bit k: feature (fl + k) mod 16
-        const bool fsel = (mask >> fl) & 1u;
-        const int jflush = fsel ? fpos[blk * kBlk + fl] : 0;
-        const uint4 *xv = reinterpret_cast<const uint4 *>(xb) + (int64_t)blk * n;
-        int t;
-        {
-            int lo = 0, hi = ntask - 1;
-            while (lo < hi) {
-                int mid = (lo + hi + 1) >> 1;
-                if (rpre[mid] <= k0) lo = mid; else hi = mid - 1;
-            }
-            t = lo;
-        }
-        for (int k = k0; k < k1; t++) {
-            const int t0 = rpre[t], t1 = rpre[t + 1];
-            if (t1 <= k) continue;
-            const HistTask tk = tasks[t];
-            const int32_t *__restrict__ rows = tk.buf ? rows1 : rows0;
-            const int pe = min(k1, t1);
-            const bool single = k == t0 && pe == t1 && (t1 - t0) <= kChunk;
-            long long *dst = stage_hist + (int64_t)tk.stage * slot_words;
-            for (int c0 = k; c0 < pe; c0 += kChunk) {
-                const int c1 = min(pe, c0 + kChunk);
-                for (int i = threadIdx.x; i < kAccV2Words / 4; i += blockDim.x)
-                    reinterpret_cast<uint4 *>(acc)[i] = make_uint4(0u, 0u, 0u, 0u);
-                __syncthreads();
-                const int r0 = (int)tk.begin + (c0 - t0), r1 = (int)tk.begin + (c1 - t0);
-                long long tg = 0, th = 0;
-                unsigned *my = acc + half * kBlk;
-                for (int rb = r0 + (int)(threadIdx.x & ~31u); rb < r1; rb += blockDim.x) {
-                    const int r = rb + lane;
-                    const bool valid = r < r1;
-                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                    longlong2 qq = make_longlong2(0, 0);
-                    if (valid) {
-                        const int row = rows[r];
-                        v = __ldg(xv + row);
-                        qq = __ldg(q + row);
-                    }
-                    tg += qq.x;
-                    th += qq.y;
-                    const unsigned dg0 = (unsigned)qq.x & 0x1ffffu, dg1 = (unsigned)(qq.x >> kDig) & 0x1ffffu,
-                                   dg2 = (unsigned)(int)(qq.x >> (2 * kDig));
-                    const unsigned dh0 = (unsigned)qq.y & 0x1ffffu, dh1 = (unsigned)(qq.y >> kDig) & 0x1ffffu,
-                                   dh2 = (unsigned)(int)(qq.y >> (2 * kDig));
-                    const uint4 vr = rot_bytes(v, fl);
-                    const unsigned live = valid ? mrot : 0u;
-#pragma unroll
-                    for (int k = 0; k < kBlk; k++) {
-                        const unsigned b = byte_of(vr, k);
-                        if (((live >> k) & 1u) && b != byte_of(skipv, k)) {
-                            unsigned *cc = my + b * (2 * kBlk) + ((fl + k) & (kBlk - 1));
-                            atomicAdd(cc + 0 * kDigV2, dg0);
-                            atomicAdd(cc + 1 * kDigV2, dg1);
-                            atomicAdd(cc + 2 * kDigV2, dg2);
-                            atomicAdd(cc + 3 * kDigV2, dh0);
-                            atomicAdd(cc + 4 * kDigV2, dh1);
-                            atomicAdd(cc + 5 * kDigV2, dh2);
-                        }
-                    }
-                }
-                if (bi == 0) {
-                    tg = warp_sum(tg);
-                    th = warp_sum(th);
-                    if (lane == 0) {
-                        s_tot[0][warp] = tg;
-                        s_tot[1][warp] = th;
-                    }
-                }
-                __syncthreads();
-                if (bi == 0 && threadIdx.x < 2) {
-                    long long tot = 0;
-                    for (int w2 = 0; w2 < kHistV2Threads / 32; w2++) tot += s_tot[threadIdx.x][w2];
-                    long long *o = dst + (int64_t)nf * kBins * kWords + 2 * threadIdx.x;
-                    if (single) {
-                        o[0] = tot >> 32;
-                        o[1] = tot & 0xffffffffll;
-                    } else if (tot) {
-                        atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(tot >> 32));
-                        atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(tot & 0xffffffffll));
-                    }
-                }
-                // flush: warp w takes bins w, w + 32, ...; lane (half, fl) reads
-                // its copy of cell (bin, fl) (32 lanes, 32 banks), the two halves
-                // are added across the warp, and lane fl writes the g words,
-                // lane 16 + fl the h words of feature fl
-                for (int b = warp; b < kBins; b += kHistV2Threads / 32) {
-                    const unsigned *d = acc + (b * 2 + half) * kBlk + fl;
-                    long long vg = ((long long)(int)d[2 * kDigV2] << (2 * kDig)) +
-                                   ((long long)d[1 * kDigV2] << kDig) + (long long)d[0];
-                    long long vh = ((long long)(int)d[5 * kDigV2] << (2 * kDig)) +
-                                   ((long long)d[4 * kDigV2] << kDig) + (long long)d[3 * kDigV2];
-                    vg += __shfl_xor_sync(0xffffffffu, vg, 16);
-                    vh += __shfl_xor_sync(0xffffffffu, vh, 16);
-                    if (fsel) {
-                        const long long v = half ? vh : vg;
-                        long long *o = dst + ((int64_t)jflush * kBins + b) * kWords + 2 * half;
-                        if (single) {
-                            o[0] = v >> 32;
-                            o[1] = v & 0xffffffffll;
-                        } else {
-                            if (v >> 32) atomicAdd((unsigned long long *)(o + 0), (unsigned long long)(v >> 32));
-                            if (v & 0xffffffffll)
-                                atomicAdd((unsigned long long *)(o + 1), (unsigned long long)(v & 0xffffffffll));
-                        }
-                    }
-                }
-                __syncthreads();
-            }
-            k = pe;
-        }
-    }
 }
 
 // The round's selected features, packed into dense blocks of 16: block v,
@@ -923,12 +564,20 @@ k_compact_feat(const uint8_t *__restrict__ xb, int64_t n, int nblk, const int32_
     }
 }
 
-// k_hist3: the histograms of every level with the shared-memory layout of
-// k_hist2 (each half-warp its own copy, 32 lanes on 32 banks, one wavefront
-// per atomic instruction) and no branch in the update loop.
-// * Every bin is added, the skipped bin included (the split search rebuilds
-//   that cell as node total - the other cells, which returns the value
-//   stored here), so no lane idles on it.
+// k_hist3: the per-node gradient/hessian histograms of a level (the root,
+// E:582-596, then the smaller child of every split, E:723-737), exact.
+// * Fixed point: every row's (g, h) is a pair of int64 q values on the grid
+//   2^-S.  Each q is split into three digits, q = top * 2^34 + mid * 2^17 +
+//   low (low, mid in [0, 2^17), top signed), and each digit is summed in its
+//   own 32-bit shared-memory word: native 32-bit shared atomics, six per
+//   (row, feature), exact.
+// * Layout: the lanes of a warp each load their own row's 16-byte record of
+//   16 features; in step k lane l = 16 h + f adds feature (f + k) mod 16,
+//   and half-warp h keeps its own copy of every cell: cell (digit d, bin b,
+//   half h, feature f) is word ((d * 257 + b) * 2 + h) * 16 + f, whose bank
+//   is 16 h + f.  The 32 lanes of an atomic instruction hit 32 different
+//   banks whatever their bins: one wavefront per instruction.
+// * Every bin is added, the NaN bin included, so no lane idles on it.
 // * A slot whose feature the round did not select adds into a trash bin
 //   (256): its cell sits in the lane's own bank like every other cell, so
 //   the instruction stays conflict-free, and the trash row is never read.
@@ -936,7 +585,9 @@ k_compact_feat(const uint8_t *__restrict__ xb, int64_t n, int nblk, const int32_
 //   2^32 keeps the low and middle digit sums inside 32 bits, and the top
 //   digit's |sum| < 2^14 * 2^15.  At the flush a cell's 128-bit value is
 //   split into its words without forming it in 64 bits: with a = mid * 2^17
-//   + low (< 2^50), hi = 4 * top + (a >> 32) and lo = a mod 2^32.
+//   + low (< 2^50), hi = 4 * top + (a >> 32) and lo = a mod 2^32.  The
+//   staging slot sums these (hi, lo) words over the CTAs of a segment (and
+//   over ranks): value = hi * 2^32 + lo, exact.
 constexpr int kHistV3Threads = 1024;
 constexpr int kChunk3 = 32768;
 constexpr int kBinsV3 = kBins + 1;                   // + the trash bin
@@ -967,7 +618,7 @@ k_hist3(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ r
     // takes [c T / G, (c+1) T / G) of T = nb Wb, so a CTA whose share covers
     // many small tasks takes fewer rows.
     const long long R = rpre[ntask];
-    const long long w = kHistV2Weight, C = seg_cost;
+    const long long w = kRowWeight, C = seg_cost;
     const long long Wb = w * R + C * ntask;
     const long long T = (long long)nb * Wb;
     if (T <= 0) return;
@@ -1863,7 +1514,7 @@ __global__ void k_leaf_finish(DNode *__restrict__ nodes, const int *__restrict__
 // 256 bins gives every bin's left sums at once, so each thread evaluates
 // one bin's gain (the reference's formula, every operation rounded as in
 // E:602-621) and a block argmax picks the first maximum (lowest bin on a
-// tie).  The skipped-bin cell is rebuilt as node total - all other cells.
+// tie).
 constexpr int kSplitThreads = kBins;
 
 // Inclusive block scan of NV 128-bit values per thread (256 threads).
@@ -1900,7 +1551,7 @@ template <bool ROOT>
 __global__ void __launch_bounds__(kSplitThreads)
 k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const int *__restrict__ lvl_count,
              const HistTask *__restrict__ ht, long long *__restrict__ stage, long long *__restrict__ pool, int nf,
-             const int32_t *__restrict__ fidx, const int32_t *__restrict__ counts, const int16_t *__restrict__ skipb,
+             const int32_t *__restrict__ fidx, const int32_t *__restrict__ counts,
              int S, double lam, double mcw, long long msl, int max_depth, int pool_depth,
              FBest *__restrict__ fbest) {
     griddep_wait();
@@ -1977,16 +1628,10 @@ k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
     block_scan_i128<2 * NS>(v, tot, s_w);
     const int f = fidx[jj];
     const int nb = counts[f];
-    const int sb = skipb[f];
     const double sc = pow2(-S);
 #pragma unroll
     for (int s = 0; s < NS; s++) {
-        // the skipped bin's cell is node total - all other cells: bins >= sb gain the difference
-        i128 pg = v[2 * s], ph = v[2 * s + 1];
-        if (b >= sb) {
-            pg += TG[s] - tot[2 * s];
-            ph += TH[s] - tot[2 * s + 1];
-        }
+        const i128 pg = v[2 * s], ph = v[2 * s + 1];
         const double Gd = __dmul_rn(i128_to_double(TG[s]), sc), Hd = __dmul_rn(i128_to_double(TH[s]), sc);
         const bool eval = nd[s].depth < max_depth && nd[s].n >= msl && Hd >= mcw && nb >= 2;
         double bg = -1e9;

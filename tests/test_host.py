@@ -305,7 +305,7 @@ def test_malformed_models_are_rejected_on_the_host(built_lib):
 
 
 def _rot_bytes(words, r):
-    """k_hist2's rot_bytes on four 32-bit words: byte k of the result is byte
+    """k_hist3's rot_bytes on four 32-bit words: byte k of the result is byte
     (k + r) mod 16 of the input (restated with NumPy for the check below)."""
     a, b, c, d = words
     if r & 8:
@@ -319,17 +319,21 @@ def _rot_bytes(words, r):
     return fsr(a, b), fsr(b, c), fsr(c, d), fsr(d, a)
 
 
-def test_hist2_layout_is_conflict_free_and_complete():
-    """The shared-memory layout of k_hist2 (csrc/gbm_kernels.cuh): in step k
+def test_hist3_layout_is_conflict_free_and_complete():
+    """The shared-memory layout of k_hist3 (csrc/gbm_kernels.cuh): in step k
     lane l = 16 h + f adds feature (f + k) mod 16 into word
-    ((digit * 256 + bin) * 2 + h) * 16 + (f + k) mod 16.  For every step and
-    any bins, the 32 lanes use 32 different banks; over 16 steps every lane
-    adds each of the 16 features of its row exactly once; and the byte each
-    lane reads from its rotated record is that feature's bin."""
+    ((digit * 257 + bin) * 2 + h) * 16 + (f + k) mod 16, where bin is the
+    row's bin, or 256 (the trash row) when the round did not select that
+    feature.  For every step and any bins and selection, the 32 lanes use 32
+    different banks; over 16 steps every lane adds each of the 16 features
+    of its row exactly once; every word lies inside the 6 x 257 x 32-word
+    accumulator; and the byte each lane reads from its rotated record is
+    that feature's bin."""
     rng = np.random.default_rng(0)
-    kBins, kBlk, kDigV2 = 256, 16, 256 * 2 * 16
+    kBlk, kDigV3 = 16, 257 * 2 * 16
     for _ in range(200):
         bins = rng.integers(0, 256, size=(32, kBlk))          # the 16 bins of each lane's row
+        sel = rng.random(kBlk) < 0.7                          # the round's selected features of the block
         digit = int(rng.integers(0, 6))
         seen = np.zeros((32, kBlk), dtype=int)
         for k in range(kBlk):
@@ -338,7 +342,9 @@ def test_hist2_layout_is_conflict_free_and_complete():
                 h, f = lane >> 4, lane & 15
                 feat = (f + k) & (kBlk - 1)
                 seen[lane, feat] += 1
-                word = digit * kDigV2 + (int(bins[lane, feat]) * 2 + h) * kBlk + feat
+                b = int(bins[lane, feat]) if sel[feat] else 256
+                word = digit * kDigV3 + (b * 2 + h) * kBlk + feat
+                assert 0 <= word < 6 * kDigV3
                 banks.add(word % 32)
             assert len(banks) == 32
         assert np.all(seen == 1)
