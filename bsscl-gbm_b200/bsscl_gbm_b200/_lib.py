@@ -43,19 +43,30 @@ class GbmParams(C.Structure):
                 ("min_child_weight", C.c_double), ("learning_rate", C.c_double),
                 ("min_samples_leaf", C.c_int32), ("max_depth", C.c_int32),
                 ("max_leaves", C.c_int32), ("grow_policy", C.c_int32),
-                ("monotone", C.c_void_p)]
+                ("monotone", C.c_void_p), ("nan_direction", C.c_int32), ("nan_bin_id", C.c_void_p)]
+
+
+def with_nan_direction(params, nan_bin_id):
+    """params learning the NaN direction (gbm_params.nan_direction) for the
+    features whose nan_bin_id is 0; returns (params, the int32 array params
+    points at, which the caller keeps alive while params is used)."""
+    nb = np.ascontiguousarray(nan_bin_id, dtype=np.int32)
+    params.nan_direction = 1
+    params.nan_bin_id = nb.ctypes.data_as(C.c_void_p)
+    return params, nb
 
 
 class GbmTreeOut(C.Structure):
     _fields_ = [("capacity", C.c_int32), ("tf", C.c_void_p), ("tt", C.c_void_p),
                 ("tv", C.c_void_p), ("tl", C.c_void_p), ("tr", C.c_void_p),
-                ("sg", C.c_void_p), ("n_nodes", C.c_int32), ("leaf_of_row", C.c_void_p)]
+                ("sg", C.c_void_p), ("n_nodes", C.c_int32), ("leaf_of_row", C.c_void_p),
+                ("nan_right", C.c_void_p)]
 
 
 class GbmPacked(C.Structure):
     _fields_ = [("features", C.c_void_p), ("thresholds", C.c_void_p), ("values", C.c_void_p),
                 ("left", C.c_void_p), ("right", C.c_void_p), ("offsets", C.c_void_p),
-                ("n_trees", C.c_int32)]
+                ("n_trees", C.c_int32), ("nan_right", C.c_void_p)]
 
 
 class GbmStats(C.Structure):
@@ -154,6 +165,13 @@ def lib():
 
 def ptr(a):
     return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _tree(tf, tt, tv, tl, tr, nc, sg, nan_right=None):
+    """A tree in the reference's tuple layout (tf, tt, tv, tl, tr, nc, sg),
+    with the per-node NaN direction appended when the round learned it."""
+    t = (tf, tt, tv, tl, tr, int(nc), sg)
+    return t if nan_right is None else t + (nan_right,)
 
 
 def check_model(packed, n_trees, n_features):
@@ -326,12 +344,13 @@ class Engine:
         tv = np.empty(capacity, np.float64); tl = np.empty(capacity, np.int32)
         tr = np.empty(capacity, np.int32); sg = np.empty(capacity, np.float64)
         leaf = np.empty(self.n, np.int32) if want_leaf else None
+        nr = np.empty(capacity, np.int32) if params.nan_direction else None
         out = GbmTreeOut(capacity, ptr(tf), ptr(tt), ptr(tv), ptr(tl), ptr(tr), ptr(sg), 0,
-                         ptr(leaf))
+                         ptr(leaf), ptr(nr))
         loss = C.c_double(0.0)
         self.check(self._L.gbm_round(self._h, ptr(mask), ptr(fidx), len(fidx), C.byref(params),
                                      C.byref(out), C.byref(loss)), "gbm_round")
-        return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value), leaf
+        return _tree(tf, tt, tv, tl, tr, out.n_nodes, sg, nr), float(loss.value), leaf
 
     # -- regression --
     def upload_targets(self, y, init_score, loss="mse", n_global=0):
@@ -398,12 +417,13 @@ class Engine:
         tv = np.empty(capacity, np.float64); tl = np.empty(capacity, np.int32)
         tr = np.empty(capacity, np.int32); sg = np.empty(capacity, np.float64)
         leaf = np.empty(self.n, np.int32) if want_leaf else None
+        nr = np.empty(capacity, np.int32) if params.nan_direction else None
         out = GbmTreeOut(capacity, ptr(tf), ptr(tt), ptr(tv), ptr(tl), ptr(tr), ptr(sg), 0,
-                         ptr(leaf))
+                         ptr(leaf), ptr(nr))
         loss = C.c_double(0.0)
         self.check(self._L.gbm_round_sampled(self._h, sampler._h, int(row_offset), C.byref(params),
                                              C.byref(out), C.byref(loss)), "gbm_round_sampled")
-        return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value), leaf
+        return _tree(tf, tt, tv, tl, tr, out.n_nodes, sg, nr), float(loss.value), leaf
 
     def fit_rounds(self, sampler, row_offset, params: GbmParams, capacity, n_rounds):
         """n_rounds rounds queued back to back (gbm_fit_rounds): a list of
@@ -414,17 +434,18 @@ class Engine:
         for r in range(n_rounds):
             a = (np.empty(capacity, np.int32), np.empty(capacity, np.int64),
                  np.empty(capacity, np.float64), np.empty(capacity, np.int32),
-                 np.empty(capacity, np.int32), np.empty(capacity, np.float64))
+                 np.empty(capacity, np.int32), np.empty(capacity, np.float64),
+                 np.empty(capacity, np.int32) if params.nan_direction else None)
             arrays.append(a)
             outs[r] = GbmTreeOut(capacity, ptr(a[0]), ptr(a[1]), ptr(a[2]), ptr(a[3]), ptr(a[4]),
-                                 ptr(a[5]), 0, None)
+                                 ptr(a[5]), 0, None, ptr(a[6]))
         losses = np.zeros(max(1, n_rounds), np.float64)
         self.check(self._L.gbm_fit_rounds(self._h, sampler._h, int(row_offset), C.byref(params),
                                           n_rounds, outs, ptr(losses)), "gbm_fit_rounds")
         res = []
         for r in range(n_rounds):
-            tf, tt, tv, tl, tr, sg = arrays[r]
-            res.append(((tf, tt, tv, tl, tr, int(outs[r].n_nodes), sg), float(losses[r])))
+            tf, tt, tv, tl, tr, sg, nr = arrays[r]
+            res.append((_tree(tf, tt, tv, tl, tr, outs[r].n_nodes, sg, nr), float(losses[r])))
         return res
 
     def build_tree(self, grad, hess, inbag_mask, feat_idx, params: GbmParams, capacity):
@@ -436,10 +457,11 @@ class Engine:
         tf = np.empty(capacity, np.int32); tt = np.empty(capacity, np.int64)
         tv = np.empty(capacity, np.float64); tl = np.empty(capacity, np.int32)
         tr = np.empty(capacity, np.int32); sg = np.empty(capacity, np.float64)
-        out = GbmTreeOut(capacity, ptr(tf), ptr(tt), ptr(tv), ptr(tl), ptr(tr), ptr(sg), 0, None)
+        nr = np.empty(capacity, np.int32) if params.nan_direction else None
+        out = GbmTreeOut(capacity, ptr(tf), ptr(tt), ptr(tv), ptr(tl), ptr(tr), ptr(sg), 0, None, ptr(nr))
         self.check(self._L.gbm_build_tree(self._h, ptr(g), ptr(h), ptr(mask), ptr(fidx), len(fidx),
                                           C.byref(params), C.byref(out)), "gbm_build_tree")
-        return (tf, tt, tv, tl, tr, int(out.n_nodes), sg)
+        return _tree(tf, tt, tv, tl, tr, out.n_nodes, sg, nr)
 
     def scale_bits(self):
         return int(self._L.gbm_scale_bits(self._h))
@@ -465,8 +487,11 @@ class Engine:
             "right": np.ascontiguousarray(packed["right"], dtype=np.int32),
             "offsets": np.ascontiguousarray(packed["offsets"], dtype=np.int32),
         }
+        if packed.get("nan_right") is not None:
+            keep["nan_right"] = np.ascontiguousarray(packed["nan_right"], dtype=np.uint8)
         s = GbmPacked(ptr(keep["features"]), ptr(keep["thresholds"]), ptr(keep["values"]),
-                      ptr(keep["left"]), ptr(keep["right"]), ptr(keep["offsets"]), int(n_trees))
+                      ptr(keep["left"]), ptr(keep["right"]), ptr(keep["offsets"]), int(n_trees),
+                      ptr(keep.get("nan_right")))
         return s, keep
 
     def predict(self, xbin_u8, packed, n_trees, lr, base, want_F=True, want_proba=True):

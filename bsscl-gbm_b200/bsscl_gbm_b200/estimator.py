@@ -30,7 +30,7 @@ import time
 import numpy as np
 
 from . import binning
-from ._lib import Engine, GbmParams, Sampler
+from ._lib import Engine, GbmParams, Sampler, with_nan_direction
 
 
 def _device_index(device):
@@ -68,7 +68,7 @@ class HybridHistGBMNumbaV1_0_1:
                  objective='auto', focal_gamma=2.0, loss='mse', device='b200',
                  sampling_method='uniform', top_rate=0.2, other_rate=0.1,
                  scale_pos_weight=None, custom_objective=None, boosting_type='gbdt',
-                 dart_rate=0.1, interaction_constraints=None):
+                 dart_rate=0.1, interaction_constraints=None, nan_direction='left'):
         self.binning_strategy_init = binning_strategy
         self.n_estimators_init = n_estimators
         self.max_depth_init = max_depth
@@ -92,6 +92,10 @@ class HybridHistGBMNumbaV1_0_1:
         self.boosting_type = boosting_type
         self.dart_rate = dart_rate
         self.interaction_constraints = interaction_constraints
+        # 'left' (default): the reference's rule, the NaN bin always goes left
+        # (E:668).  'learn': every split also weighs sending NaN right and
+        # keeps the better direction (no reference counterpart; binary only).
+        self.nan_direction = nan_direction
         self.max_leaves = max_leaves
         self.monotone_constraints = monotone_constraints
         self.categorical_features = categorical_features
@@ -132,6 +136,8 @@ class HybridHistGBMNumbaV1_0_1:
         self._packed_left = None
         self._packed_right = None
         self._tree_offsets = None
+        self._tree_nan_right = []      # per tree: nan_right [nc] (nan_direction='learn'), else None
+        self._packed_nan_right = None
         self._mc_packed = None
         self._nan_bin_id = None
         self._engine = None
@@ -148,7 +154,7 @@ class HybridHistGBMNumbaV1_0_1:
                     'early_stopping_rounds', 'verbose', 'random_state', 'objective',
                     'focal_gamma', 'loss', 'device', 'sampling_method', 'top_rate',
                     'other_rate', 'scale_pos_weight', 'custom_objective', 'boosting_type',
-                    'dart_rate', 'interaction_constraints')
+                    'dart_rate', 'interaction_constraints', 'nan_direction')
     _INIT_ALIAS = {'n_estimators': 'n_estimators_init', 'max_depth': 'max_depth_init',
                    'learning_rate': 'learning_rate_init', 'n_bins': 'n_bins_init',
                    'min_child_weight': 'min_child_weight_init', 'gamma': 'gamma_init',
@@ -284,9 +290,13 @@ class HybridHistGBMNumbaV1_0_1:
         if self._mono_arr is not None:
             self._mono_keep = np.ascontiguousarray(self._mono_arr, dtype=np.int32)
             mono_ptr = self._mono_keep.ctypes.data
-        return GbmParams(float(self.reg_lambda), float(self.gamma), float(self.min_child_weight),
-                         float(self.learning_rate), int(self.min_samples_leaf), int(self.max_depth),
-                         int(self.max_leaves), policy, mono_ptr)
+        prm = GbmParams(float(self.reg_lambda), float(self.gamma), float(self.min_child_weight),
+                        float(self.learning_rate), int(self.min_samples_leaf), int(self.max_depth),
+                        int(self.max_leaves), policy, mono_ptr)
+        self._nan_keep = None
+        if self.nan_direction == 'learn':
+            prm, self._nan_keep = with_nan_direction(prm, self._nan_bin_id)
+        return prm
 
     def _check_device_bins(self):
         mx = int(np.max(self.feature_bin_counts))
@@ -365,7 +375,12 @@ class HybridHistGBMNumbaV1_0_1:
             if np.any(yv >= len(self.classes_)) or np.any(self.classes_[np.minimum(yv, len(self.classes_) - 1)] != y_val):
                 raise KeyError("y_val holds a label that is not in y")
             y_val = yv.astype(np.int64)
+        if self.nan_direction not in ('left', 'learn'):
+            raise ValueError(f"nan_direction must be 'left' or 'learn', got {self.nan_direction!r}")
+        if self.nan_direction == 'learn' and (regression or self._is_multiclass):
+            raise NotImplementedError("nan_direction='learn' is built for binary log-loss only")
         self.trees = []
+        self._tree_nan_right = []
         self.mc_trees = None
         self.train_loss_history_ = []
         self.val_loss_history_ = []
@@ -461,6 +476,7 @@ class HybridHistGBMNumbaV1_0_1:
         self._nan_bin_id = np.full(X_bin.shape[1], -1, dtype=np.int32)
         self._mono_arr = None
         self.trees = []
+        self._tree_nan_right = []
         self.train_loss_history_ = []
         self.val_loss_history_ = []
         t0 = time.perf_counter()
@@ -518,11 +534,12 @@ class HybridHistGBMNumbaV1_0_1:
             while m < self.n_estimators and not stop:
                 k = min(batch, self.n_estimators - m)
                 for tree, loss in eng.fit_rounds(sampler, lo, params, cap, k):
-                    self.trees.append(tree)
+                    self.trees.append(tree[:7])
+                    self._tree_nan_right.append(tree[7][:tree[5]].copy() if len(tree) > 7 else None)
                     self.train_loss_history_.append(loss)
                     val_loss = None
                     if X_val_bin is not None:
-                        F_val += self.learning_rate * _predict_tree_host(X_val_bin, tree)
+                        F_val += self.learning_rate * _predict_tree_host(X_val_bin, tree)   # NaN direction included
                         val_loss = _logloss(y_val, F_val)
                         self.val_loss_history_.append(val_loss)
                     if self.verbose and ((m + 1) % 20 == 0 or m == 0):
@@ -539,6 +556,7 @@ class HybridHistGBMNumbaV1_0_1:
                             no_improve += 1
                             if no_improve >= self.early_stopping_rounds:
                                 self.trees = self.trees[:self.best_iteration_ + 1]
+                                self._tree_nan_right = self._tree_nan_right[:self.best_iteration_ + 1]
                                 stop = True
                                 break
                     m += 1
@@ -604,6 +622,7 @@ class HybridHistGBMNumbaV1_0_1:
                         no_improve += 1
                         if no_improve >= self.early_stopping_rounds:
                             self.trees = self.trees[:self.best_iteration_ + 1]
+                            self._tree_nan_right = self._tree_nan_right[:self.best_iteration_ + 1]
                             break
         finally:
             sampler.close()
@@ -719,6 +738,14 @@ class HybridHistGBMNumbaV1_0_1:
         self._packed_features, self._packed_thresholds = feats, thr
         self._packed_values, self._packed_left, self._packed_right = vals, left, right
         self._tree_offsets = offs
+        self._packed_nan_right = None
+        nrs = getattr(self, '_tree_nan_right', [])
+        if any(x is not None for x in nrs):
+            nr = np.zeros(total, dtype=np.uint8)
+            for t, x in enumerate(nrs):
+                if x is not None:
+                    nr[offs[t]:offs[t] + len(x)] = x
+            self._packed_nan_right = nr
 
     def _compute_feature_importances(self):
         gain = np.zeros(self.n_features_in_, dtype=np.float64)
@@ -740,7 +767,8 @@ class HybridHistGBMNumbaV1_0_1:
     def _packed(self):
         return {"features": self._packed_features, "thresholds": self._packed_thresholds,
                 "values": self._packed_values, "left": self._packed_left,
-                "right": self._packed_right, "offsets": self._tree_offsets}
+                "right": self._packed_right, "offsets": self._tree_offsets,
+                "nan_right": getattr(self, '_packed_nan_right', None)}
 
     def _prep_X(self, X):
         try:
@@ -877,6 +905,9 @@ class HybridHistGBMNumbaV1_0_1:
             data['mc_trees'] = [[tree_json(t) for t in ts] for ts in self.mc_trees]
         else:
             data['trees'] = [tree_json(t) for t in self.trees]
+            nrs = getattr(self, '_tree_nan_right', [])
+            if any(x is not None for x in nrs):   # nan_direction='learn' (no reference counterpart)
+                data['nan_right'] = [[] if x is None else np.asarray(x).astype(int).tolist() for x in nrs]
         if self.feature_importances_ is not None:
             data['feature_importances_'] = np.asarray(self.feature_importances_).tolist()
         if self.feature_split_counts_ is not None:
@@ -924,6 +955,9 @@ class HybridHistGBMNumbaV1_0_1:
                     np.array(td['values'], dtype=np.float64), np.array(td['left'], dtype=np.int32),
                     np.array(td['right'], dtype=np.int32), int(td['node_count']), sg)
         model.trees = [tree_of(td) for td in data.get('trees', [])]
+        nrs = data.get('nan_right')
+        model._tree_nan_right = ([np.array(x, dtype=np.int32) if x else None for x in nrs] if nrs
+                                 else [None] * len(model.trees))
         if 'mc_trees' in data:
             model.mc_trees = [[tree_of(td) for td in ts] for ts in data['mc_trees']]
         if 'feature_importances_' in data:
@@ -1030,8 +1064,10 @@ def _gather_rows(dist, local, n):
 
 
 def _predict_tree_host(X_bin, tree):
-    """Values of one tree for every row (host, used for the small validation set)."""
-    tf, tt, tv, tl, tr, nc, _ = tree
+    """Values of one tree for every row (host, used for the small validation set);
+    a tree with an 8th element sends the NaN bin right where it is 1."""
+    tf, tt, tv, tl, tr, nc, _ = tree[:7]
+    nr = np.asarray(tree[7]) if len(tree) > 7 else np.zeros(len(tf), np.int32)
     node = np.zeros(X_bin.shape[0], dtype=np.int64)
     rows = np.arange(X_bin.shape[0])
     while True:
@@ -1040,7 +1076,8 @@ def _predict_tree_host(X_bin, tree):
         if not act.any():
             break
         ff = np.where(act, f, 0)
-        go_left = X_bin[rows, ff].astype(np.int64) <= tt[node]
+        b = X_bin[rows, ff].astype(np.int64)
+        go_left = (b <= tt[node]) & ~((nr[node] != 0) & (b == 0))
         node = np.where(act, np.where(go_left, tl[node], tr[node]), node)
     return tv[node]
 

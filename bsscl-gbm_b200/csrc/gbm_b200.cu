@@ -180,6 +180,8 @@ struct gbm_ctx {
     int32_t *d_head = nullptr, *d_nxt = nullptr, *d_m = nullptr, *d_mp = nullptr;
     TreeOut *d_tout = nullptr;
     int32_t *d_mono = nullptr, *h_mono = nullptr;
+    uint8_t *d_nanf = nullptr, *h_nanf = nullptr;   // per feature: bin 0 is a NaN bin (nan_direction)
+    bool nan_dir = false;                           // this call's rounds learn the NaN direction
     int replay_smem = 0;               // dynamic shared memory the replay kernels may use
 
     // regression: float64 targets, mse (0) or mae (1); S follows the largest |g| each round
@@ -422,7 +424,7 @@ int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::v
     const int64_t total = m->offsets[T];
     if (total > 0 && (!m->features || !m->thresholds || !m->values || !m->left || !m->right))
         return bad(GBM_ERR_ARG, "%s", "model arrays missing");
-    nodes.assign((size_t)std::max<int64_t>(total, 1), PNode{-1, 0, 0, 0, 0});
+    nodes.assign((size_t)std::max<int64_t>(total, 1), PNode{-1, 0, 0, 0, 0});   // feat, thr, nanr, left, right
     vals.assign((size_t)std::max<int64_t>(total, 1), 0.0);
     for (int32_t t = 0; t < T; t++) {
         const int32_t o = m->offsets[t], o1 = m->offsets[t + 1], sz = o1 - o;
@@ -434,11 +436,15 @@ int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::v
                 const int32_t l = m->left[k], r = m->right[k], kk = k - o;
                 if (f >= n_features) return bad(GBM_ERR_ARG, "tree %d node %d: feature %d >= %d", t, kk, f, n_features);
                 if (th < 0) return bad(GBM_ERR_UNSUPPORTED, "tree %d node %d: negative threshold", t, kk);
+                const int nr = m->nan_right && m->nan_right[k] ? 1 : 0;
+                if (nr && th < 1)
+                    return bad(GBM_ERR_ARG, "tree %d node %d: a NaN-right split needs threshold >= 1", t, kk);
                 if (l <= kk || l >= sz || r <= kk || r >= sz)
                     return bad(GBM_ERR_ARG, "tree %d node %d: children %d/%d must lie after the node inside the "
                                 "tree (%d nodes)", t, kk, l, r, sz);
                 nd.feat = (int16_t)f;
                 nd.thr = (uint8_t)(th > 255 ? 255 : th);
+                nd.nanr = (uint8_t)nr;
                 nd.left = (int16_t)l;
                 nd.right = (int16_t)r;
             }
@@ -449,13 +455,14 @@ int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::v
     if (n32 && v32 && dep32) {
         // the 32-bit breadth-first form (k_predict's PACKED format): every
         // tree renumbered so that a node's children are adjacent, each leaf
-        // pointing at itself with threshold 255, and the tree's depth; only
-        // when features fit 12 bits and every tree (as reached from its root)
-        // fits 4096 nodes, else *n32 stays empty
+        // pointing at itself with threshold 255, a NaN-right split stored with
+        // threshold - 1 and bit 31 set, and the tree's depth; only when
+        // features fit 11 bits and every tree (as reached from its root) fits
+        // 4096 nodes, else *n32 stays empty
         n32->clear();
         v32->clear();
         dep32->clear();
-        if (n_features > 4096) return GBM_OK;
+        if (n_features > 2048) return GBM_OK;
         std::vector<uint32_t> a((size_t)std::max<int64_t>(total, 1), 0u);
         std::vector<double> b((size_t)std::max<int64_t>(total, 1), 0.0);
         std::vector<int32_t> d((size_t)std::max<int32_t>(T, 1), 0);
@@ -473,7 +480,8 @@ int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::v
                 uint32_t w = (255u << 12) | (uint32_t)nid[h];   // a leaf: no bin is above 255
                 if (nd.feat >= 0) {
                     if (next + 1 >= sz) return GBM_OK;   // more nodes than the tree holds (shared children)
-                    w = ((uint32_t)nd.feat << 20) | ((uint32_t)nd.thr << 12) | (uint32_t)next;
+                    w = ((uint32_t)nd.nanr << 31) | ((uint32_t)nd.feat << 20) |
+                        ((uint32_t)(nd.nanr ? nd.thr - 1 : nd.thr) << 12) | (uint32_t)next;
                     order.push_back(nd.left);
                     nid.push_back(next);
                     lev.push_back(lev[h] + 1);
@@ -633,6 +641,8 @@ int ensure_slots(gbm_ctx *ctx) {
         }
         TRY(dalloc(ctx, &ctx->d_tout, 1));
         TRY(dalloc(ctx, &ctx->d_mono, (size_t)ctx->p));
+        TRY(dalloc(ctx, &ctx->d_nanf, (size_t)ctx->p));
+        TRY(halloc(ctx, &ctx->h_nanf, (size_t)ctx->p));
         TRY(halloc(ctx, &ctx->h_mono, (size_t)ctx->p));
         ctx->slots_ready = true;
     }
@@ -1093,7 +1103,7 @@ int launch_root(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, const Ne
     TRY(launch(ctx, k_split_bins<true>, dim3(rf.nf, 1), dim3(kSplitThreads), 0, ctx->st,
         (const DNode *)ctx->d_nodes, (const int *)nullptr, (const int *)nullptr, (const HistTask *)ctx->d_htask,
         ctx->d_stage, ctx->d_pool, rf.nf, (const int32_t *)ctx->d_fidx, (const int32_t *)ctx->d_counts,
-        ctx->S, P->reg_lambda, P->min_child_weight,
+        (const uint8_t *)(ctx->nan_dir ? ctx->d_nanf : nullptr), ctx->S, P->reg_lambda, P->min_child_weight,
         (long long)P->min_samples_leaf, P->max_depth, pool_depth(P), ctx->d_fbest));
     return launch_close(ctx, rf, P, true, nullptr, nullptr, ctx->d_lvl[0], ints(ctx, I_LVL0), np);
 }
@@ -1152,7 +1162,7 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
     TRY(launch(ctx, k_split_bins<false>, dim3(rf.nf, W_ub), dim3(kSplitThreads), 0, ctx->st,
         (const DNode *)ctx->d_nodes, (const int *)lvl, (const int *)lvl_cnt, (const HistTask *)ctx->d_htask,
         ctx->d_stage, ctx->d_pool, rf.nf, (const int32_t *)ctx->d_fidx, (const int32_t *)ctx->d_counts,
-        ctx->S, P->reg_lambda, P->min_child_weight,
+        (const uint8_t *)(ctx->nan_dir ? ctx->d_nanf : nullptr), ctx->S, P->reg_lambda, P->min_child_weight,
         (long long)P->min_samples_leaf, P->max_depth, pool_depth(P), ctx->d_fbest));
     TRY(launch_close(ctx, rf, P, false, lvl, lvl_cnt, next, next_cnt, next ? np : NextPlan()));
     ctx->waves++;
@@ -1208,7 +1218,7 @@ struct HostTree {
 struct Cand {
     int node = 0;      // tree node id (reference numbering)
     int nid = -1;      // device node table index
-    int depth = 0, feat = -1, bin = 0;
+    int depth = 0, feat = -1, bin = 0, nan_right = 0;
     double gain = -1.0, val = 0.0;
     bool active = false;
 };
@@ -1229,7 +1239,7 @@ int replay_leafwise(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, Host
     }
     std::vector<Cand> c(MAXC);
     c[0].node = root; c[0].nid = 0; c[0].depth = 0; c[0].gain = nd[0].gain; c[0].feat = nd[0].feat;
-    c[0].bin = nd[0].bin; c[0].val = root_val; c[0].active = true;
+    c[0].bin = nd[0].bin; c[0].nan_right = nd[0].nan_right; c[0].val = root_val; c[0].active = true;
     int n_splits = 0;
     while (n_splits < max_leaves - 1) {
         int ci = -1;
@@ -1259,7 +1269,7 @@ int replay_leafwise(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, Host
             continue;
         }
         int lid = node_count++, rid = node_count++;
-        T.tf[cur] = pc.feat; T.tt[cur] = pc.bin; T.tl[cur] = lid; T.tr[cur] = rid;
+        T.tf[cur] = pc.feat; T.tt[cur] = pc.bin | ((int64_t)pc.nan_right << 32); T.tl[cur] = lid; T.tr[cur] = rid;
         T.tv[cur] = pc.val; T.sg[cur] = pc.gain;
         n_splits++;
         int nd_depth = pc.depth + 1;
@@ -1288,6 +1298,7 @@ int replay_leafwise(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, Host
             x.val = -k.G / (k.H + lam);
             x.feat = k.feat;                    // -1 unless n >= msl, H >= mcw, depth < max_depth (E:775-777)
             x.bin = k.feat >= 0 ? k.bin : 0;
+            x.nan_right = k.feat >= 0 ? k.nan_right : 0;
             x.gain = k.feat >= 0 ? k.gain : -1.0;
             x.active = true;
         }
@@ -1333,7 +1344,7 @@ int replay_depthwise(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, Hos
             ctx->alg_bytes += (double)(sm.end - sm.begin) * (rf.nf + 8);
             ctx->hist_updates += (double)(sm.end - sm.begin) * rf.upd_per_row;
         }
-        T.tf[e.tid] = x.feat; T.tt[e.tid] = x.bin; T.tl[e.tid] = lid; T.tr[e.tid] = rid;
+        T.tf[e.tid] = x.feat; T.tt[e.tid] = x.bin | ((int64_t)x.nan_right << 32); T.tl[e.tid] = lid; T.tr[e.tid] = rid;
         T.tv[e.tid] = val; T.sg[e.tid] = x.gain;
         if (gl <= gr) {
             stack.push_back({x.kid1, rid});   // larger pushed first
@@ -1414,6 +1425,8 @@ int check_tree_args(gbm_ctx *ctx, int32_t nfeat, const gbm_params *P, const gbm_
         return fail(ctx, GBM_ERR_UNSUPPORTED, "max_depth > 24 is not supported");
     int need = P->grow_policy == 0 ? 2 * P->max_leaves + 2 : (1 << (P->max_depth + 1)) - 1;
     if (out->capacity < need) return fail(ctx, GBM_ERR_ARG, "tree capacity %d < %d", out->capacity, need);
+    if (P->nan_direction && !P->nan_bin_id)
+        return fail(ctx, GBM_ERR_ARG, "nan_direction needs nan_bin_id (the reference's _nan_bin_id)");
     return GBM_OK;
 }
 
@@ -1484,6 +1497,11 @@ int replay_on_host(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, HostT
 // Monotone constraints of this call -> the device (before any round of the
 // call is queued; every earlier call has finished).
 int stage_mono(gbm_ctx *ctx, const gbm_params *P) {
+    ctx->nan_dir = P->nan_direction != 0;
+    if (ctx->nan_dir) {   // which features' bin 0 is a NaN bin
+        for (int j = 0; j < ctx->p; j++) ctx->h_nanf[j] = P->nan_bin_id[j] == 0 ? 1 : 0;
+        CK(cudaMemcpyAsync(ctx->d_nanf, ctx->h_nanf, (size_t)ctx->p, cudaMemcpyHostToDevice, ctx->st));
+    }
     if (!P->monotone) return GBM_OK;
     std::memcpy(ctx->h_mono, P->monotone, sizeof(int32_t) * ctx->p);
     CK(cudaMemcpyAsync(ctx->d_mono, ctx->h_mono, sizeof(int32_t) * ctx->p, cudaMemcpyHostToDevice, ctx->st));
@@ -1542,6 +1560,7 @@ void write_tree_dev(const TreeOut &T, int need, gbm_tree_out *out) {
         out->tl[k] = in ? T.tl[k] : -1;
         out->tr[k] = in ? T.tr[k] : -1;
         out->sg[k] = in ? T.sg[k] : 0.0;
+        if (out->nan_right) out->nan_right[k] = in ? T.nr[k] : 0;
     }
     out->n_nodes = T.nc;
 }
@@ -1564,7 +1583,8 @@ void write_tree(const HostTree &T, int need, gbm_tree_out *out) {
     for (int k = 0; k < need; k++) {
         bool in = k < (int)T.tf.size();
         out->tf[k] = in ? T.tf[k] : -1;
-        out->tt[k] = in ? T.tt[k] : 0;
+        out->tt[k] = in ? (T.tt[k] & 0xffffffffll) : 0;   // the NaN direction rides in bit 32
+        if (out->nan_right) out->nan_right[k] = in ? (int32_t)(T.tt[k] >> 32) : 0;
         out->tv[k] = in ? T.tv[k] : 0.0;
         out->tl[k] = in ? T.tl[k] : -1;
         out->tr[k] = in ? T.tr[k] : -1;
@@ -1735,9 +1755,10 @@ namespace {
 std::string graph_key(const gbm_ctx *ctx, const gbm_params *P, int nf, int64_t N, int64_t m, bool rows_on,
                       int64_t row_offset) {
     char buf[512];
-    snprintf(buf, sizeof buf, "%a/%a/%a/%a/%d/%d/%d/%d/%p|%d/%lld/%lld/%lld/%d/%lld|%d/%zu/%llu/%p",
+    snprintf(buf, sizeof buf, "%a/%a/%a/%a/%d/%d/%d/%d/%p/%d/%p|%d/%lld/%lld/%lld/%d/%lld|%d/%zu/%llu/%p",
              P->reg_lambda, P->gamma, P->min_child_weight, P->learning_rate, P->min_samples_leaf, P->max_depth,
-             P->max_leaves, P->grow_policy, (const void *)P->monotone, nf, (long long)N, (long long)m,
+             P->max_leaves, P->grow_policy, (const void *)P->monotone, P->nan_direction,
+             (const void *)P->nan_bin_id, nf, (long long)N, (long long)m,
              (long long)ctx->n, (int)rows_on, (long long)row_offset, (int)ctx->profiling, ctx->flush_bytes,
              ctx->mem_gen, (const void *)ctx->comm);
     return buf;
@@ -2117,7 +2138,7 @@ static int round_body(gbm_ctx *ctx, int si, const int32_t *feat_idx, int32_t nfe
         td.n = T.nc;
         for (int k = 0; k < T.nc; k++) {
             td.feat[k] = T.tf[k];
-            td.thr[k] = (int)std::min<int64_t>(T.tt[k], 255);
+            td.thr[k] = dev_thr(T.tt[k] & 0xffffffffll, (int)(T.tt[k] >> 32));
             td.left[k] = T.tl[k];
             td.right[k] = T.tr[k];
             td.val[k] = T.tv[k];
@@ -2218,7 +2239,7 @@ int gbm_round_reg(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_i
         td.n = T.nc;
         for (int j = 0; j < T.nc; j++) {
             td.feat[j] = T.tf[j];
-            td.thr[j] = (int)std::min<int64_t>(T.tt[j], 255);
+            td.thr[j] = dev_thr(T.tt[j] & 0xffffffffll, (int)(T.tt[j] >> 32));
             td.left[j] = T.tl[j];
             td.right[j] = T.tr[j];
             td.val[j] = T.tv[j];
@@ -2322,7 +2343,7 @@ int gbm_round_mc(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_id
                 td.n = T.nc;
                 for (int j = 0; j < T.nc; j++) {
                     td.feat[j] = T.tf[j];
-                    td.thr[j] = (int)std::min<int64_t>(T.tt[j], 255);
+                    td.thr[j] = dev_thr(T.tt[j] & 0xffffffffll, (int)(T.tt[j] >> 32));
                     td.left[j] = T.tl[j];
                     td.right[j] = T.tr[j];
                     td.val[j] = T.tv[j];
@@ -2802,7 +2823,7 @@ __global__ void k_noalloc_pack(const int16_t *__restrict__ feat, const int64_t *
         int f = feat[o + k];
         PNode nd;
         nd.feat = (int16_t)f;
-        nd.pad = 0;
+        nd.nanr = 0;
         nd.thr = 0;
         nd.left = nd.right = 0;
         if (f >= 0) {

@@ -48,6 +48,8 @@ struct DNode {
     int kid0, kid1;         // children (-1 = not expanded)
     int left_small;         // 1 if the left child's histogram was built directly
     int expanded;           // 1 once both children's results are final
+    int nan_right;          // the best split sends the NaN bin (bin 0) right (learned direction)
+    int pad;
 };
 
 // Row lists live in two buffers: the rows of a node at depth d are in
@@ -60,24 +62,26 @@ struct HistTask {           // rows[buf][begin, end) -> staging histogram `stage
     int pad;
 };
 
-struct PartTask {           // stable partition of rows[src][begin, end) on bin(feat) <= thr
+struct PartTask {           // stable partition of rows[src][begin, end) on goes_left(bin(feat), thr, nan_right)
     long long begin, end;
     int feat, thr;
     int tile0, ntile;       // tiles of this task in the level's tile numbering
     int src;                // the parent's buffer; the children go to 1 - src
-    int pad;
+    int nan_right;
 };
 
 struct FBest {              // best bin of one feature for one node
     double gain;
     int bin;
     int valid;
+    int nan_right;          // the best candidate sends the NaN bin right
+    int pad;
 };
 
 struct TreeDev {            // a pruned tree in the reference's layout
     int n;
     int feat[256];
-    int thr[256];
+    int thr[256];           // threshold bin (<= 255) | nan_right << 16 (dev_thr)
     int left[256];
     int right[256];
     double val[256];
@@ -96,6 +100,7 @@ struct TreeOut {
     long long tt[256];
     double tv[256];
     double sg[256];
+    int nr[256];            // 1: the split sends the NaN bin right (learned direction)
 };
 
 struct RParams {            // growth parameters the replay needs
@@ -107,7 +112,7 @@ struct RParams {            // growth parameters the replay needs
 struct PNode {              // predict: 8 bytes per node
     int16_t feat;           // -1 = leaf
     uint8_t thr;
-    uint8_t pad;
+    uint8_t nanr;           // 1: the NaN bin (bin 0) goes right
     int16_t left, right;    // tree-local ids
 };
 
@@ -206,6 +211,20 @@ __device__ __forceinline__ int block_excl_scan(int v, int *s_w, int &total) {
 
 __device__ __forceinline__ int bin_of(const uint8_t *__restrict__ xb, int64_t n, int64_t row, int f) {
     return __ldg(xb + (((int64_t)(f >> 4) * n + row) << 4) + (f & 15));
+}
+
+// The split rule.  The reference sends bin <= thr left (E:668, E:855,
+// E:878), so the NaN bin (bin 0) always goes left.  A split learned with the
+// NaN direction (gbm_params.nan_direction) may instead send the NaN bin
+// right: then left is 1 <= bin <= thr (thr >= 1).
+__host__ __device__ __forceinline__ bool goes_left(int b, int thr, int nan_right) {
+    return b <= thr && !(nan_right && b == 0);
+}
+
+// A tree threshold as the update kernels read it: the bin (clamped to 255)
+// with the NaN direction in bit 16.
+__host__ __device__ __forceinline__ int dev_thr(long long t, int nan_right) {
+    return (int)(t > 255 ? 255 : t) | (nan_right ? 1 << 16 : 0);
 }
 
 // a beats b: larger gain; equal gains -> lower feature position, then lower bin

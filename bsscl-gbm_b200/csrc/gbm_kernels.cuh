@@ -104,7 +104,7 @@ k_update(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64
         int node = 0;
         while (s_feat[node] >= 0) {
             int b = bin_of(xb, n, i, s_feat[node]);
-            node = (b <= s_thr[node]) ? s_left[node] : s_right[node];
+            node = goes_left(b, s_thr[node] & 0xffff, s_thr[node] >> 16) ? s_left[node] : s_right[node];
         }
         if (leaf_out) leaf_out[i] = node;
         double f = __dadd_rn(F[i], __dmul_rn(lr, s_val[node]));
@@ -235,7 +235,7 @@ k_update_class(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb,
         int node = 0;
         while (s_feat[node] >= 0) {
             const int b = bin_of(xb, n, i, s_feat[node]);
-            node = (b <= s_thr[node]) ? s_left[node] : s_right[node];
+            node = goes_left(b, s_thr[node] & 0xffff, s_thr[node] >> 16) ? s_left[node] : s_right[node];
         }
         if (leaf_out) leaf_out[i] = node;
         F[i] = __dadd_rn(F[i], __dmul_rn(lr, s_val[node]));
@@ -293,7 +293,7 @@ k_update_reg(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, i
         int node = 0;
         while (s_feat[node] >= 0) {
             const int b = bin_of(xb, n, i, s_feat[node]);
-            node = (b <= s_thr[node]) ? s_left[node] : s_right[node];
+            node = goes_left(b, s_thr[node] & 0xffff, s_thr[node] >> 16) ? s_left[node] : s_right[node];
         }
         if (leaf_out) leaf_out[i] = node;
         const double f = __dadd_rn(F[i], __dmul_rn(lr, s_val[node]));
@@ -808,6 +808,8 @@ __device__ __forceinline__ DNode fresh_node(int depth, int parent) {
     d.kid0 = d.kid1 = -1;
     d.left_small = 0;
     d.expanded = 0;
+    d.nan_right = 0;
+    d.pad = 0;
     return d;
 }
 
@@ -885,7 +887,7 @@ __global__ void k_lvl_plan(DNode *__restrict__ nodes, const int *__restrict__ lv
             t.tile0 = carry + e;
             t.ntile = nt;
             t.src = p.depth & 1;
-            t.pad = 0;
+            t.nan_right = p.nan_right;
             pt[k] = t;
             int c0 = base + 2 * k;
             p.kid0 = c0;
@@ -940,7 +942,7 @@ k_part_count(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restric
     unsigned *sw = side + (int64_t)tile * kPartWords;
 #pragma unroll
     for (int j = 0; j < J; j++) {
-        const bool left = rw[j] >= 0 && bin_of(xb, n, rw[j], tk.feat) <= tk.thr;
+        const bool left = rw[j] >= 0 && goes_left(bin_of(xb, n, rw[j], tk.feat), tk.thr, tk.nan_right);
         const unsigned word = __ballot_sync(0xffffffffu, left);
         if ((threadIdx.x & 31) == 0) sw[(threadIdx.x >> 5) + j * (kPartThreads / 32)] = word;
         cnt += __popc(word);
@@ -1439,7 +1441,7 @@ k_leaf_totals(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restri
     for (int j = 0; j < J; j++) {
         if (rw[j] < 0) continue;
         const longlong2 qq = __ldg(q + rw[j]);
-        const bool left = bin_of(xb, n, rw[j], tk.feat) <= tk.thr;
+        const bool left = goes_left(bin_of(xb, n, rw[j], tk.feat), tk.thr, tk.nan_right);
         v[left ? 0 : 2] += qq.x;
         v[left ? 1 : 3] += qq.y;
         v[4] += left;
@@ -1552,13 +1554,14 @@ __global__ void __launch_bounds__(kSplitThreads)
 k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const int *__restrict__ lvl_count,
              const HistTask *__restrict__ ht, long long *__restrict__ stage, long long *__restrict__ pool, int nf,
              const int32_t *__restrict__ fidx, const int32_t *__restrict__ counts,
-             int S, double lam, double mcw, long long msl, int max_depth, int pool_depth,
-             FBest *__restrict__ fbest) {
+             const uint8_t *__restrict__ nan_feat, int S, double lam, double mcw, long long msl, int max_depth,
+             int pool_depth, FBest *__restrict__ fbest) {
     griddep_wait();
     constexpr int NS = ROOT ? 1 : 2;   // children searched
     __shared__ i128 s_w[(kSplitThreads / 32) * 2 * NS];
     __shared__ double s_bg[NS][kSplitThreads / 32];
     __shared__ int s_bb[NS][kSplitThreads / 32];
+    __shared__ i128 s_c0[NS][2];   // bin 0's cell (the NaN bin when the feature has one)
     const int k = blockIdx.y, jj = blockIdx.x;
     if (!ROOT && k >= *lvl_count) return;
     if (jj >= nf) return;
@@ -1629,35 +1632,60 @@ k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
     const int f = fidx[jj];
     const int nb = counts[f];
     const double sc = pow2(-S);
+    // the NaN-right candidates (nan_feat given: the learned NaN direction):
+    // left = bins 1..b, right = the NaN bin and bins > b
+    const bool nan_dir = nan_feat != nullptr && nan_feat[f] != 0;
+    if (nan_dir) {
+        if (b == 0) {
+#pragma unroll
+            for (int s = 0; s < NS; s++) {
+                s_c0[s][0] = v[2 * s];
+                s_c0[s][1] = v[2 * s + 1];
+            }
+        }
+        __syncthreads();
+    }
 #pragma unroll
     for (int s = 0; s < NS; s++) {
         const i128 pg = v[2 * s], ph = v[2 * s + 1];
         const double Gd = __dmul_rn(i128_to_double(TG[s]), sc), Hd = __dmul_rn(i128_to_double(TH[s]), sc);
         const bool eval = nd[s].depth < max_depth && nd[s].n >= msl && Hd >= mcw && nb >= 2;
+        // candidate c = 2 * bin + direction: ties go to the lower c, i.e. the
+        // lower bin, then NaN-left (the reference's strict '>' over ascending bins)
         double bg = -1e9;
-        int bb = -1;
+        int bc = -1;
         if (eval && b <= nb - 2) {
             const double parent_term = __ddiv_rn(__dmul_rn(Gd, Gd), __dadd_rn(Hd, lam));
-            const double GL = __dmul_rn(i128_to_double(pg), sc);
-            const double HL = __dmul_rn(i128_to_double(ph), sc);
-            const double GR = __dmul_rn(i128_to_double(TG[s] - pg), sc);
-            const double HR = __dmul_rn(i128_to_double(TH[s] - ph), sc);
-            if (!(HL < mcw || HR < mcw)) {
-                bg = __dsub_rn(__dadd_rn(__ddiv_rn(__dmul_rn(GL, GL), __dadd_rn(HL, lam)),
-                                         __ddiv_rn(__dmul_rn(GR, GR), __dadd_rn(HR, lam))),
-                               parent_term);
-                bb = b;
+            auto gain_of = [&](i128 gl, i128 hl, double &gain) {
+                const double GL = __dmul_rn(i128_to_double(gl), sc);
+                const double HL = __dmul_rn(i128_to_double(hl), sc);
+                const double GR = __dmul_rn(i128_to_double(TG[s] - gl), sc);
+                const double HR = __dmul_rn(i128_to_double(TH[s] - hl), sc);
+                if (HL < mcw || HR < mcw) return false;
+                gain = __dsub_rn(__dadd_rn(__ddiv_rn(__dmul_rn(GL, GL), __dadd_rn(HL, lam)),
+                                           __ddiv_rn(__dmul_rn(GR, GR), __dadd_rn(HR, lam))),
+                                 parent_term);
+                return true;
+            };
+            double gn;
+            if (gain_of(pg, ph, gn)) {
+                bg = gn;
+                bc = 2 * b;
+            }
+            if (nan_dir && b >= 1 && gain_of(pg - s_c0[s][0], ph - s_c0[s][1], gn) && (bc < 0 || gn > bg)) {
+                bg = gn;
+                bc = 2 * b + 1;
             }
         }
-        // argmax: larger gain, ties -> lower bin (the reference's strict '>' over ascending bins)
+        // argmax: larger gain, ties -> lower candidate
         for (int o = 16; o > 0; o >>= 1) {
             const double og = __shfl_xor_sync(0xffffffffu, bg, o);
-            const int ob = __shfl_xor_sync(0xffffffffu, bb, o);
-            if (better(og, ob < 0 ? -1 : 0, ob, bg, bb < 0 ? -1 : 0, bb)) { bg = og; bb = ob; }
+            const int oc = __shfl_xor_sync(0xffffffffu, bc, o);
+            if (better(og, oc < 0 ? -1 : 0, oc, bg, bc < 0 ? -1 : 0, bc)) { bg = og; bc = oc; }
         }
         if (lane == 0) {
             s_bg[s][warp] = bg;
-            s_bb[s][warp] = bb;
+            s_bb[s][warp] = bc;
         }
     }
     __syncthreads();
@@ -1672,8 +1700,10 @@ k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
             }
         FBest o;
         o.gain = bg;
-        o.bin = bb < 0 ? 0 : bb;
+        o.bin = bb < 0 ? 0 : bb >> 1;
         o.valid = bb >= 0 ? 1 : 0;
+        o.nan_right = bb >= 0 ? (bb & 1) : 0;
+        o.pad = 0;
         fbest[(int64_t)(2 * k + s) * nf + jj] = o;
     }
 }
@@ -1717,16 +1747,17 @@ k_level_close(DNode *__restrict__ nodes, const int *__restrict__ lvl, const int 
         }
         const FBest *fb = fbest + (int64_t)cc * nf;
         double bg = -1e9;
-        int bj = -1, bb = 0;
+        int bj = -1, bb = 0, br = 0;
         for (int jj = lane; jj < nf; jj += 32) {
             FBest o = fb[jj];
-            if (o.valid && better(o.gain, jj, o.bin, bg, bj, bb)) { bg = o.gain; bj = jj; bb = o.bin; }
+            if (o.valid && better(o.gain, jj, o.bin, bg, bj, bb)) { bg = o.gain; bj = jj; bb = o.bin; br = o.nan_right; }
         }
         for (int o = 16; o > 0; o >>= 1) {
             double og = __shfl_xor_sync(0xffffffffu, bg, o);
             int oj = __shfl_xor_sync(0xffffffffu, bj, o);
             int ob = __shfl_xor_sync(0xffffffffu, bb, o);
-            if (better(og, oj, ob, bg, bj, bb)) { bg = og; bj = oj; bb = ob; }
+            int orr = __shfl_xor_sync(0xffffffffu, br, o);
+            if (better(og, oj, ob, bg, bj, bb)) { bg = og; bj = oj; bb = ob; br = orr; }
         }
         if (lane == 0) {
             const long long *t = pool + (int64_t)ch * words + (int64_t)nf * kBins * kWords;
@@ -1737,6 +1768,7 @@ k_level_close(DNode *__restrict__ nodes, const int *__restrict__ lvl, const int 
             d.feat = bj >= 0 ? fidx[bj] : -1;
             d.bin = bj >= 0 ? bb : 0;
             d.gain = bj >= 0 ? bg : -1.0;
+            d.nan_right = bj >= 0 ? br : 0;
             if (!ROOT && (cc & 1) == 0) nodes[parent].expanded = 1;
         }
     }
@@ -1810,7 +1842,7 @@ k_level_close(DNode *__restrict__ nodes, const int *__restrict__ lvl, const int 
             t.tile0 = carry + e;
             t.ntile = ntl;
             t.src = p.depth & 1;
-            t.pad = 0;
+            t.nan_right = p.nan_right;
             pt[k] = t;
             int c0 = base + 2 * k;
             p.kid0 = c0;
@@ -1840,6 +1872,7 @@ struct RNode {
     double val, H, gain;    // leaf value -G/(H+lambda) (E:640, E:708-709), hessian sum, best gain
     long long n, local;     // rows over all ranks / on this rank
     int feat, bin, kid0, kid1, expanded, depth;
+    int nanr;               // the split sends the NaN bin right
 };
 
 __device__ void load_rnodes(const DNode *__restrict__ nodes, int cnt, RNode *sn, double lam) {
@@ -1849,6 +1882,7 @@ __device__ void load_rnodes(const DNode *__restrict__ nodes, int cnt, RNode *sn,
         r.val = __ddiv_rn(-d.G, __dadd_rn(d.H, lam));
         r.H = d.H; r.gain = d.gain; r.n = d.n; r.local = d.end - d.begin;
         r.feat = d.feat; r.bin = d.bin; r.kid0 = d.kid0; r.kid1 = d.kid1; r.expanded = d.expanded; r.depth = d.depth;
+        r.nanr = d.nan_right;
         sn[i] = r;
     }
     __syncthreads();
@@ -1904,12 +1938,14 @@ __device__ void finish_tree(int nc, int *tf, int *tl, int *tr, long long *tt, do
         out->tf[k] = in ? tf[k] : -1;
         out->tl[k] = in ? tl[k] : -1;
         out->tr[k] = in ? tr[k] : -1;
-        out->tt[k] = in ? tt[k] : 0;
+        // a replay's tt holds the bin with the NaN direction in bit 32
+        out->tt[k] = in ? (tt[k] & 0xffffffffll) : 0;
+        out->nr[k] = in ? (int)(tt[k] >> 32) : 0;
         out->tv[k] = in ? tv[k] : 0.0;
         out->sg[k] = in ? sg[k] : 0.0;
         if (in) {
             td->feat[k] = tf[k];
-            td->thr[k] = (int)(tt[k] > 255 ? 255 : tt[k]);
+            td->thr[k] = dev_thr(tt[k] & 0xffffffffll, (int)(tt[k] >> 32));
             td->left[k] = tl[k];
             td->right[k] = tr[k];
             td->val[k] = tv[k];
@@ -2015,7 +2051,7 @@ k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_coun
         const int kid_s = left_small ? pn.kid0 : pn.kid1, kid_l = left_small ? pn.kid1 : pn.kid0;
         if (pn.depth + 1 < P.max_depth) alg += sn[kid_s].local;   // the last level builds no histogram
         if (lane == 0) {
-            tf[cur] = pn.feat; tt[cur] = pn.bin; tl[cur] = lid; tr[cur] = rid; tv[cur] = pn.val; sg[cur] = pn.gain;
+            tf[cur] = pn.feat; tt[cur] = pn.bin | ((long long)pn.nanr << 32); tl[cur] = lid; tr[cur] = rid; tv[cur] = pn.val; sg[cur] = pn.gain;
             c_node[ss] = left_small ? lid : rid;
             c_nid[ss] = kid_s;
             c_node[sl] = left_small ? rid : lid;
@@ -2078,7 +2114,7 @@ k_replay_depth(const DNode *__restrict__ nodes, const int *__restrict__ node_cou
             const int lid = nc++, rid = nc++;
             const long long gl = sn[x.kid0].n, gr = sn[x.kid1].n;
             if (x.depth + 1 < P.max_depth) alg += gl <= gr ? sn[x.kid0].local : sn[x.kid1].local;
-            tf[tid] = x.feat; tt[tid] = x.bin; tl[tid] = lid; tr[tid] = rid; tv[tid] = val; sg[tid] = x.gain;
+            tf[tid] = x.feat; tt[tid] = x.bin | ((long long)x.nanr << 32); tl[tid] = lid; tr[tid] = rid; tv[tid] = val; sg[tid] = x.gain;
             if (gl <= gr) {
                 st_nid[sp] = x.kid1; st_tid[sp] = rid; sp++;
                 st_nid[sp] = x.kid0; st_tid[sp] = lid; sp++;
@@ -2154,8 +2190,10 @@ __device__ __forceinline__ void walk_packed(const uint32_t *__restrict__ tn, int
 #pragma unroll
         for (int j = 0; j < RPT; j++) {
             const uint32_t w = tn[node[j]];
-            const int f = min((int)(w >> 20), pm1);
-            const int b = SROWS ? rowp[j][((f >> 2) << 7) | (f & 3)] : __ldg(rowp[j] + f);
+            const int f = min((int)((w >> 20) & 0x7ffu), pm1);
+            const int b0 = SROWS ? rowp[j][((f >> 2) << 7) | (f & 3)] : __ldg(rowp[j] + f);
+            // a NaN-right split (bit 31, threshold stored as t - 1) compares bin - 1 mod 256: bin 0 -> 255
+            const int b = (b0 - (int)(w >> 31)) & 0xff;
             node[j] = min((int)(w & 0xfffu) + (b > (int)((w >> 12) & 0xffu) ? 1 : 0), szm1);
         }
     }
@@ -2176,7 +2214,7 @@ __device__ __forceinline__ void walk_pnode(const PNode *__restrict__ tn, int szm
             if (nd[j].feat >= 0) {
                 const int f = min((int)nd[j].feat, pm1);
                 const int b = SROWS ? rowp[j][((f >> 2) << 7) | (f & 3)] : __ldg(rowp[j] + f);
-                node[j] = min((int)(b <= nd[j].thr ? nd[j].left : nd[j].right), szm1);
+                node[j] = min((int)(goes_left(b, nd[j].thr, nd[j].nanr) ? nd[j].left : nd[j].right), szm1);
                 nd[j] = tn[node[j]];
                 more = true;
             }
@@ -2200,10 +2238,11 @@ __device__ __forceinline__ void walk_pnode(const PNode *__restrict__ tn, int szm
 // c + 1 into the other buffer.
 //
 // Node formats.  PACKED: one 32-bit word per node of a tree renumbered
-// breadth-first (pack_model), children adjacent: feature << 20 | threshold
-// << 12 | left child, right = left + 1, and a leaf pointing at itself with
-// threshold 255; every row takes exactly the tree's depth steps with no
-// branch.  Level d of a complete tree is 2^d consecutive words,
+// breadth-first (pack_model), children adjacent: nan_right << 31 | feature
+// << 20 | threshold << 12 | left child, right = left + 1 (a NaN-right split
+// holds threshold - 1 and compares bin - 1 mod 256, so the NaN bin goes
+// right), and a leaf pointing at itself with threshold 255; every row takes
+// exactly the tree's depth steps with no branch.  Level d of a complete tree is 2^d consecutive words,
 // conflict-free up to level 5.  Otherwise PNode (8 bytes, the reference's
 // own numbering), walked until a leaf.
 //

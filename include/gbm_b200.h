@@ -60,6 +60,16 @@ typedef struct {
     int32_t max_leaves;       /* best-first stops after max_leaves-1 splits */
     int32_t grow_policy;      /* 0 = leaf-wise best-first, 1 = depth-wise */
     const int32_t *monotone;  /* NULL, or per-feature -1/0/+1 (E:2461-2499) */
+    /* The NaN direction.  0 (the reference, E:602-621, E:668): every split
+     * is bin <= threshold -> left, so the NaN bin (bin 0) always goes left.
+     * 1: for every feature whose nan_bin_id[j] is 0 (its bin 0 is the NaN
+     * bin, E:2113-2127) the split search also evaluates, at every bin t >= 1,
+     * the split that sends NaN right (left = bins 1..t) and keeps whichever
+     * gains more (NaN-left on a tie); the tree then records the direction
+     * per split (gbm_tree_out.nan_right) and every partition, F update and
+     * predict honours it.  No reference counterpart: parity mode is 0. */
+    int32_t nan_direction;
+    const int32_t *nan_bin_id;   /* [p] the reference's _nan_bin_id (0 or -1); needed when nan_direction */
 } gbm_params;
 
 /* One tree in the reference's tuple layout (E:528-537):
@@ -77,6 +87,7 @@ typedef struct {
     double *sg;
     int32_t n_nodes;          /* out: node_count */
     int32_t *leaf_of_row;     /* optional [n]: leaf node id of every row */
+    int32_t *nan_right;       /* optional [capacity]: 1 where the split sends NaN right (nan_direction) */
 } gbm_tree_out;
 
 /* A packed ensemble, as _pack_tree_list builds it (E:2192-2216). */
@@ -88,6 +99,8 @@ typedef struct {
     const int32_t *right;      /* [total_nodes] */
     const int32_t *offsets;    /* [n_trees+1] */
     int32_t n_trees;
+    const uint8_t *nan_right;  /* optional [total_nodes]: 1 where the split sends the NaN bin right
+                                  (a model trained with nan_direction); NULL = the reference's NaN-left */
 } gbm_packed;
 
 /* ---- context ---------------------------------------------------------- */

@@ -133,7 +133,19 @@ static double i128_to_double(i128 v) {
 
 static inline double qd(i128 v, int S) { return ldexp(i128_to_double(v), -S); }
 
-typedef struct { int feat; int bin; double gain; } split_t;
+typedef struct { int feat; int bin; double gain; int nr; } split_t;
+
+/* The learned NaN direction (the engine's gbm_params.nan_direction; no
+ * reference counterpart): when set, nanf[j] != 0 marks the features whose
+ * bin 0 is the NaN bin, the split scan also evaluates at every bin t >= 1
+ * the split that sends NaN right (left = bins 1..t), right after the
+ * NaN-left candidate of the same bin (so NaN-left wins a tie), and a
+ * tree's thresholds carry the direction in bit 32 of tt.  NULL: the
+ * reference's NaN-left only. */
+static const uint8_t *g_nanf = NULL;
+void or_set_nan_dir(const uint8_t *nanf) { g_nanf = nanf; }
+
+static inline int goes_left(int64_t b, int64_t thr, int nr) { return b <= thr && !(nr && b == 0); }
 
 /* Split scan of one node's histogram.  E:602-621 / E:780-801: features in
  * ascending feature_indices order, bins 0..nb-2 as a running prefix, skip
@@ -141,7 +153,7 @@ typedef struct { int feat; int bin; double gain; } split_t;
 static split_t find_split(const params_t *P, const hist_t *hs, int max_bins,
                           const int32_t *fidx, int nf, const int32_t *counts,
                           i128 qG, i128 qH) {
-    split_t best = { -1, 0, -1e9 };
+    split_t best = { -1, 0, -1e9, 0 };
     for (int jj = 0; jj < nf; jj++) {
         int j = fidx[jj];
         int nb = counts[j];
@@ -151,13 +163,17 @@ static split_t find_split(const params_t *P, const hist_t *hs, int max_bins,
             double Gt = 0.0, Ht = 0.0;
             for (int b = 0; b < nb; b++) { Gt += G[b]; Ht += H[b]; }
             double GL = 0.0, HL = 0.0;
+            const int nd_ = g_nanf && g_nanf[j];
             for (int b = 0; b < nb - 1; b++) {
                 GL += G[b]; HL += H[b];
-                double GR = Gt - GL, HR = Ht - HL;
-                if (HL < P->mcw || HR < P->mcw) continue;
-                double gain = GL * GL / (HL + P->lam) + GR * GR / (HR + P->lam)
-                            - Gt * Gt / (Ht + P->lam);
-                if (gain > best.gain) { best.gain = gain; best.feat = j; best.bin = b; }
+                for (int dir = 0; dir <= (nd_ && b >= 1); dir++) {
+                    double gl_ = dir ? GL - G[0] : GL, hl_ = dir ? HL - H[0] : HL;
+                    double GR = Gt - gl_, HR = Ht - hl_;
+                    if (hl_ < P->mcw || HR < P->mcw) continue;
+                    double gain = gl_ * gl_ / (hl_ + P->lam) + GR * GR / (HR + P->lam)
+                                - Gt * Gt / (Ht + P->lam);
+                    if (gain > best.gain) { best.gain = gain; best.feat = j; best.bin = b; best.nr = dir; }
+                }
             }
         } else {
             const i128 *G = hs->QG + (int64_t)j * max_bins, *H = hs->QH + (int64_t)j * max_bins;
@@ -165,13 +181,17 @@ static split_t find_split(const params_t *P, const hist_t *hs, int max_bins,
             double Gt = qd(qG, S), Ht = qd(qH, S);
             double parent = Gt * Gt / (Ht + P->lam);
             i128 gl = 0, hl = 0;
+            const int nd_ = g_nanf && g_nanf[j];
             for (int b = 0; b < nb - 1; b++) {
                 gl += G[b]; hl += H[b];
-                double GL = qd(gl, S), HL = qd(hl, S);
-                double GR = qd(qG - gl, S), HR = qd(qH - hl, S);
-                if (HL < P->mcw || HR < P->mcw) continue;
-                double gain = GL * GL / (HL + P->lam) + GR * GR / (HR + P->lam) - parent;
-                if (gain > best.gain) { best.gain = gain; best.feat = j; best.bin = b; }
+                for (int dir = 0; dir <= (nd_ && b >= 1); dir++) {
+                    i128 gl_ = dir ? gl - G[0] : gl, hl_ = dir ? hl - H[0] : hl;
+                    double GL = qd(gl_, S), HL = qd(hl_, S);
+                    double GR = qd(qG - gl_, S), HR = qd(qH - hl_, S);
+                    if (HL < P->mcw || HR < P->mcw) continue;
+                    double gain = GL * GL / (HL + P->lam) + GR * GR / (HR + P->lam) - parent;
+                    if (gain > best.gain) { best.gain = gain; best.feat = j; best.bin = b; best.nr = dir; }
+                }
             }
         }
     }
@@ -245,13 +265,13 @@ static void node_sums(const params_t *P, const double *g, const double *h, const
 }
 
 /* In-place two-pointer partition of idx[a..b) on Xb[:, f] <= thr
- * (E:663-674).  Returns the split position. */
+ * (E:663-674), NaN bin right when nr.  Returns the split position. */
 static int64_t partition(int64_t *idx, int64_t a, int64_t b, const uint16_t *Xb, int p,
-                         int f, int64_t thr) {
+                         int f, int64_t thr, int nr) {
     int64_t lp = a, rp = b - 1;
     while (lp <= rp) {
         int64_t i = idx[lp];
-        if ((int64_t)Xb[i * p + f] <= thr) lp++;
+        if (goes_left(Xb[i * p + f], thr, nr)) lp++;
         else { idx[lp] = idx[rp]; idx[rp] = i; rp--; }
     }
     return lp;
@@ -328,7 +348,7 @@ int or_build_leafwise(const uint16_t *Xb, int64_t n_all, int32_t p, const double
         build_hist(&P, &hs[0], max_bins, Xb, p, g, h, qg, qh, idx, 0, n_sub, fidx, nf, counts);
         split_t s = find_split(&P, &hs[0], max_bins, fidx, nf, counts, qGr, qHr);
         c_node[0] = root; c_start[0] = 0; c_end[0] = n_sub; c_depth[0] = 0;
-        c_gain[0] = s.feat >= 0 ? s.gain : -1.0; c_feat[0] = s.feat; c_bin[0] = s.bin;
+        c_gain[0] = s.feat >= 0 ? s.gain : -1.0; c_feat[0] = s.feat; c_bin[0] = s.bin | (s.nr << 16);
         c_val[0] = root_val; c_active[0] = 1; c_qG[0] = qGr; c_qH[0] = qHr;
         if (s.feat < 0) { tf[root] = -1; tv[root] = root_val; done = 1; }
     }
@@ -341,14 +361,15 @@ int or_build_leafwise(const uint16_t *Xb, int64_t n_all, int32_t p, const double
         int cur = c_node[ci];
         int64_t a = c_start[ci], b = c_end[ci];
         int depth = c_depth[ci];
-        int64_t sp = partition(idx, a, b, Xb, p, c_feat[ci], c_bin[ci]);
+        int64_t sp = partition(idx, a, b, Xb, p, c_feat[ci], c_bin[ci] & 0xffff, c_bin[ci] >> 16);
         int64_t nl = sp - a, nr = b - sp;
         if (nl < msl || nr < msl) {                          /* E:678-683 */
             tf[cur] = -1; tv[cur] = c_val[ci]; c_active[ci] = 0;
             continue;
         }
         int lid = node_count++, rid = node_count++;
-        tf[cur] = c_feat[ci]; tt[cur] = c_bin[ci]; tl[cur] = lid; tr[cur] = rid;
+        tf[cur] = c_feat[ci]; tt[cur] = (c_bin[ci] & 0xffff) | ((int64_t)(c_bin[ci] >> 16) << 32);
+        tl[cur] = lid; tr[cur] = rid;
         tv[cur] = c_val[ci]; sg[cur] = c_gain[ci];
         n_splits++;
         int nd = depth + 1;
@@ -371,11 +392,11 @@ int or_build_leafwise(const uint16_t *Xb, int64_t n_all, int32_t p, const double
             double Gc, Hc; i128 qGc, qHc;
             node_sums(&P, g, h, qg, qh, idx, ca, cb, &Gc, &Hc, &qGc, &qHc);
             double val = -Gc / (Hc + lam);
-            split_t s = { -1, 0, -1e9 };
+            split_t s = { -1, 0, -1e9, 0 };
             int can = (cb - ca) >= msl && Hc >= mcw && nd < max_depth;
             if (can) s = find_split(&P, &hs[cs], max_bins, fidx, nf, counts, qGc, qHc);
             c_node[cs] = cid; c_start[cs] = ca; c_end[cs] = cb; c_depth[cs] = nd;
-            c_gain[cs] = s.feat >= 0 ? s.gain : -1.0; c_feat[cs] = s.feat; c_bin[cs] = s.bin;
+            c_gain[cs] = s.feat >= 0 ? s.gain : -1.0; c_feat[cs] = s.feat; c_bin[cs] = s.bin | (s.nr << 16);
             c_val[cs] = val; c_active[cs] = 1; c_qG[cs] = qGc; c_qH[cs] = qHc;
         }
     }
@@ -440,11 +461,11 @@ int or_build_depthwise(const uint16_t *Xb, int64_t n_all, int32_t p, const doubl
         }
         split_t s = find_split(&P, &work, max_bins, fidx, nf, counts, qG, qH);
         if (s.feat < 0) { tf[cur] = -1; tv[cur] = val; continue; }
-        int64_t spos = partition(idx, a, b, Xb, p, s.feat, s.bin);
+        int64_t spos = partition(idx, a, b, Xb, p, s.feat, s.bin, s.nr);
         int64_t nl = spos - a, nr = b - spos;
         if (nl < msl || nr < msl) { tf[cur] = -1; tv[cur] = val; continue; }
         int lid = node_count++, rid = node_count++;
-        tf[cur] = s.feat; tt[cur] = s.bin; tl[cur] = lid; tr[cur] = rid; tv[cur] = val; sg[cur] = s.gain;
+        tf[cur] = s.feat; tt[cur] = s.bin | ((int64_t)s.nr << 32); tl[cur] = lid; tr[cur] = rid; tv[cur] = val; sg[cur] = s.gain;
         int left_small = nl <= nr;
         int64_t sa = left_small ? a : spos, sb = left_small ? spos : b;
         int64_t la = left_small ? spos : a, lb = left_small ? b : spos;
@@ -486,7 +507,8 @@ void or_leaf_ids(const uint16_t *Xb, int64_t n, int32_t p, const int32_t *tf, co
     #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++) {
         int node = 0;
-        while (tf[node] >= 0) node = ((int64_t)Xb[i * p + tf[node]] <= tt[node]) ? tl[node] : tr[node];
+        while (tf[node] >= 0)
+            node = goes_left(Xb[i * p + tf[node]], tt[node] & 0xffffffffLL, (int)(tt[node] >> 32)) ? tl[node] : tr[node];
         leaf[i] = node;
     }
 }
@@ -495,7 +517,7 @@ void or_leaf_ids(const uint16_t *Xb, int64_t n, int32_t p, const int32_t *tf, co
 void or_predict_packed(const uint16_t *Xb, int64_t n, int32_t p, const int16_t *feat,
                        const int64_t *thr, const double *val, const int32_t *left,
                        const int32_t *right, const int32_t *offsets, int32_t n_trees,
-                       double lr, double *F) {
+                       double lr, const uint8_t *nanr, double *F) {
     #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++) {
         double acc = 0.0;
@@ -503,7 +525,8 @@ void or_predict_packed(const uint16_t *Xb, int64_t n, int32_t p, const int16_t *
         for (int t = 0; t < n_trees; t++) {
             int o = offsets[t], node = 0;
             while (feat[o + node] >= 0) {
-                node = ((int64_t)row[feat[o + node]] <= thr[o + node]) ? left[o + node] : right[o + node];
+                node = goes_left(row[feat[o + node]], thr[o + node], nanr ? nanr[o + node] : 0) ? left[o + node]
+                                                                                             : right[o + node];
             }
             acc += lr * val[o + node];
         }

@@ -50,7 +50,9 @@ def lib():
                                          f64, f64, f64, i32, i32, P, P, P, P, P, P, P]
         L.or_post_prune.argtypes = [P, P, P, P, f64, i32]
         L.or_leaf_ids.argtypes = [P, i64, i32, P, P, P, P, P]
-        L.or_predict_packed.argtypes = [P, i64, i32, P, P, P, P, P, P, i32, f64, P]
+        L.or_predict_packed.argtypes = [P, i64, i32, P, P, P, P, P, P, i32, f64, P, P]
+        L.or_set_nan_dir.argtypes = [P]
+        L.or_set_nan_dir.restype = None
         L.or_grad_hess.argtypes = [P, P, P, i64, P, P]
         L.or_logloss.argtypes = [P, P, i64]
         L.or_logloss.restype = C.c_double
@@ -62,7 +64,7 @@ def lib():
 
 
 def _p(a):
-    return a.ctypes.data_as(C.c_void_p)
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
 
 
 def i128_to_double(v):
@@ -91,8 +93,13 @@ def bin_matrix(X, edges, counts, nan_bin_id, hybrid):
 
 def build_tree(X_bin, g, h, sample_idx, feat_idx, counts, *, max_leaves=63, max_depth=6,
                msl=5, mcw=1.0, lam=1.0, gamma=0.0, mode=MODE_REF, scale_bits=0,
-               policy="leaf"):
-    """One tree.  Returns ``(tf, tt, tv, tl, tr, nc, sg)`` like the reference."""
+               policy="leaf", nan_bin_id=None):
+    """One tree.  Returns ``(tf, tt, tv, tl, tr, nc, sg)`` like the reference.
+
+    ``nan_bin_id`` (the reference's ``_nan_bin_id``, 0 where bin 0 is a NaN
+    bin): also evaluate the splits that send NaN right (the engine's
+    ``nan_direction``); the tree's ``tt`` then carries the direction in bit
+    32 (``split_nan_right`` separates them)."""
     Xb = np.ascontiguousarray(X_bin, dtype=np.uint16)
     n, p = Xb.shape
     g = np.ascontiguousarray(g, dtype=np.float64)
@@ -108,6 +115,8 @@ def build_tree(X_bin, g, h, sample_idx, feat_idx, counts, *, max_leaves=63, max_
     tf = np.empty(M, np.int32); tt = np.empty(M, np.int64); tv = np.empty(M, np.float64)
     tl = np.empty(M, np.int32); tr = np.empty(M, np.int32); sg = np.empty(M, np.float64)
     nc = C.c_int32(0)
+    nanf = None if nan_bin_id is None else (np.asarray(nan_bin_id) == 0).astype(np.uint8)
+    lib().or_set_nan_dir(_p(nanf))
     if policy == "leaf":
         rc = lib().or_build_leafwise(_p(Xb), n, p, _p(g), _p(h), _p(sidx), len(sidx), _p(fidx),
                                      len(fidx), _p(counts), max_bins, max_leaves, max_depth,
@@ -118,9 +127,16 @@ def build_tree(X_bin, g, h, sample_idx, feat_idx, counts, *, max_leaves=63, max_
                                       _p(fidx), len(fidx), _p(counts), max_bins, max_depth,
                                       msl, mcw, lam, gamma, mode, scale_bits, _p(tf), _p(tt),
                                       _p(tv), _p(tl), _p(tr), _p(sg), C.byref(nc))
+    lib().or_set_nan_dir(None)
     if rc != 0:
         raise MemoryError("oracle builder failed to allocate")
     return tf, tt, tv, tl, tr, int(nc.value), sg
+
+
+def split_nan_right(tt):
+    """(thresholds, nan_right) of a tree built with nan_bin_id."""
+    tt = np.asarray(tt, np.int64)
+    return tt & 0xFFFFFFFF, (tt >> 32).astype(np.int32)
 
 
 def post_prune(tf, tl, tr, sg, gamma, nc):
@@ -152,7 +168,10 @@ def enforce_monotone(tf, tl, tr, tv, nc, mono):
             tv[r] = m
 
 
-def leaf_ids(X_bin, tf, tt, tl, tr):
+def leaf_ids(X_bin, tf, tt, tl, tr, nan_right=None):
+    """Leaf id of every row; ``nan_right`` [nodes] (or bit 32 of ``tt``) sends NaN right."""
+    if nan_right is not None:
+        tt = np.asarray(tt, np.int64) | (np.asarray(nan_right, np.int64) << 32)
     Xb = np.ascontiguousarray(X_bin, dtype=np.uint16)
     n, p = Xb.shape
     out = np.empty(n, np.int32)
@@ -166,11 +185,13 @@ def predict_packed(X_bin, packed, n_trees, lr):
     Xb = np.ascontiguousarray(X_bin, dtype=np.uint16)
     n, p = Xb.shape
     F = np.empty(n, np.float64)
-    a = {k: np.ascontiguousarray(v) for k, v in packed.items()}
+    a = {k: np.ascontiguousarray(v) for k, v in packed.items() if v is not None}
+    nr = a.get("nan_right")
     lib().or_predict_packed(_p(Xb), n, p, _p(a["features"].astype(np.int16)),
                             _p(a["thresholds"].astype(np.int64)), _p(a["values"].astype(np.float64)),
                             _p(a["left"].astype(np.int32)), _p(a["right"].astype(np.int32)),
-                            _p(a["offsets"].astype(np.int32)), int(n_trees), float(lr), _p(F))
+                            _p(a["offsets"].astype(np.int32)), int(n_trees), float(lr),
+                            _p(None if nr is None else nr.astype(np.uint8)), _p(F))
     return F
 
 

@@ -311,3 +311,55 @@ def test_ref_spw_fit_bit_exact():
         assert np.allclose(rec[t]["g"], d[f"r{t}_g"], rtol=1e-14, atol=0)
         assert np.allclose(rec[t]["h"], d[f"r{t}_h"], rtol=1e-14, atol=0)
     assert np.abs(r["train_loss"] - d["train_loss"]).max() < 1e-12
+
+
+def _nan_like_high_case(seed=21, n=6000):
+    """Feature 0: NaN in 30 % of rows, whose labels follow the rows with the
+    highest values -- the split that sends NaN right separates the classes,
+    the reference's NaN-left rule cannot."""
+    from bsscl_gbm_b200 import binning
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((n, 4))
+    y = (X[:, 0] > 0.8).astype(np.int64)
+    nan = rng.random(n) < 0.3
+    y[nan] = (rng.random(nan.sum()) < 0.9).astype(np.int64)
+    X[nan, 0] = np.nan
+    X[:, 1:] += 0.3 * y[:, None] * rng.random((n, 3))
+    e, c, nb = binning.build_bin_edges(X, 64)
+    Xb = binning.bin_features(X, e, c, nb)
+    return Xb, y, c, nb
+
+
+def test_oracle_learns_nan_right_where_it_gains_more():
+    """With nan_bin_id (the engine's nan_direction) the root splits feature 0
+    sending NaN right, with a larger gain than the best NaN-left split; that
+    split's rows go as goes_left says; without nan_bin_id the tree is the
+    reference's (no direction bits)."""
+    Xb, y, counts, nanb = _nan_like_high_case()
+    assert nanb[0] == 0
+    w2 = O.class_weights(y, None)
+    F = np.full(len(y), O.base_score(y, w2))
+    g, h = O.grad_hess(F, y.astype(np.uint8), w2)
+    sidx = np.arange(len(y), dtype=np.int64)
+    fidx = np.arange(4, dtype=np.int32)
+    kw = dict(max_leaves=8, max_depth=3, msl=5, mcw=1.0, lam=1.0, mode=O.MODE_EXACT, scale_bits=40)
+    t0 = O.build_tree(Xb, g, h, sidx, fidx, counts, **kw)
+    t1 = O.build_tree(Xb, g, h, sidx, fidx, counts, nan_bin_id=nanb, **kw)
+    assert np.all((np.asarray(t0[1][:t0[5]]) >> 32) == 0)
+    thr, nr = O.split_nan_right(t1[1])
+    assert t1[0][0] == 0 and nr[0] == 1 and thr[0] >= 1
+    assert t1[6][0] > t0[6][0]
+    leaf = O.leaf_ids(Xb, t1[0], t1[1], t1[3], t1[4])
+    b0 = Xb[:, 0].astype(np.int64)
+    went_left = np.isin(leaf, _subtree(t1, int(t1[3][0])))
+    assert np.array_equal(went_left, (b0 >= 1) & (b0 <= thr[0]))
+
+
+def _subtree(t, k):
+    out, stack = [], [k]
+    while stack:
+        u = stack.pop()
+        out.append(u)
+        if t[0][u] >= 0:
+            stack += [int(t[3][u]), int(t[4][u])]
+    return out
