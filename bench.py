@@ -238,6 +238,15 @@ def parity_check(res, first_round, record):
 # bins) and 9.05 T/s conflict-free (one warp instruction per SM clock).
 SMEM_ATOMIC_PEAK = {"random_bins_g_per_s": 2968, "conflict_free_g_per_s": 9054}
 
+# The CPU port (oracle.c, REF mode) against the reference's own Numba fit,
+# measured in the build container with oracle/calibrate_port.py: config 4's
+# data at 1,000,000 x 100, bench parameters, 10 trees, 8 threads each, the
+# same tree topology.  The port is the faster of the two, so ratios against
+# the reference arm (the port) understate the speed-up over the reference.
+PORT_CALIBRATION = {"rows": 1_000_000, "trees": 10, "threads": 8, "reference_rounds_per_s": 0.942,
+                    "port_rounds_per_s": 1.359, "port_over_reference": 1.442, "same_topology": True,
+                    "how": "oracle/calibrate_port.py"}
+
 # DRAM traffic of the histogram kernel per launch on this workload, from one
 # ncu capture (dram__bytes_read.sum + dram__bytes_write.sum over the six
 # histogram launches of one round, averaged).  A constant here, since a
@@ -308,10 +317,67 @@ def run_reference(args):
                    "max_depth": c["max_depth"], "max_leaves": c["max_leaves"], "subsample": c["subsample"],
                    "colsample": c["colsample"]},
         "cpu_baseline": {"value": v, "unit": "rounds/s", "cores": O.num_threads(), "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "calibration": PORT_CALIBRATION},
         "e2e": {"value": v, "unit": "rounds/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def config5_subrecord(eng, args, world, rank, local, dist):
+    """configs[4]'s training at this run's GPU count: 10,000,000 x 200
+    pre-binned rows sharded over the ranks (each rank makes only its own
+    rows), max_depth 10, 63 leaves, subsample 0.5, colsample 0.7, lambda 5,
+    rounds queued back to back (gbm_fit_rounds), device-timed, max over
+    ranks.  Rows are drawn by the throughput-mode device sampler
+    (gbm_sampler_create_device): the reference's cumulative shuffle of 10M
+    rows costs ~7 ms of host time per round on every rank, which would cap
+    every GPU count at ~140 rounds/s.  Throughput only: no parity claim."""
+    import torch
+    from bsscl_gbm_b200 import GbmParams, Sampler
+    import oracle as O
+    c = CONFIGS["5"]
+    n = c["n"]
+    lo, hi = (n * rank) // world, (n * (rank + 1)) // world
+    Xb, y, counts = workload(c, rows=(lo, hi))
+    p = Xb.shape[1]
+    w2 = O.class_weights(y, c["class_weight"])
+    base = O.base_score(y, w2)
+    eng.upload_bins(Xb, counts)
+    del Xb
+    eng.upload_labels(y[lo:hi].astype(np.uint8), w2, base, n_global=n)
+    prm = GbmParams(c["lam"], 0.0, c["mcw"], c["lr"], c["msl"], c["max_depth"], c["max_leaves"], 0, None)
+    cap = 2 * c["max_leaves"] + 2
+    smp = Sampler.device(c["seed"], n, p, c["subsample"], int(p * c["colsample"]), True, look_ahead=3)
+    eng.set_l2_flush(256 << 20)
+    eng.set_profiling(True)
+    eng.fit_rounds(smp, lo, prm, cap, args.warmup)
+    eng.reset_stats()
+    k = args.config5_steps
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    eng.event(8)
+    res = eng.fit_rounds(smp, lo, prm, cap, k)
+    eng.event(9)
+    eng.sync()
+    st = eng.stats()
+    eng.set_profiling(False)
+    eng.set_l2_flush(0)
+    ms = eng.elapsed_ms(8, 9) - st["flush_ms"]
+    if dist is not None:
+        t = torch.tensor([ms], device=f"cuda:{local}", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    smp.close()
+    return {"value": k / (ms / 1000.0), "unit": "rounds/s", "ms_per_step": ms / k, "steps": k,
+            "scaling": "strong", "n_gpus": world, "hist_ms_per_round": st["hist_ms"] / k,
+            "collectives_device_ms_per_round": st["comm_ms"] / k,
+            "collective_mb_per_round": st["comm_bytes"] / k / 1e6,
+            "train_loss_last": res[-1][1] if res else None,
+            "sampler": "throughput-mode device sampler (each row in-bag with probability 0.5 by a "
+                       "counter-based hash; gbm_sampler_create_device), not the reference's shuffle",
+            "config": {"workload": c["workload"], "n_rows": n, "n_features": p, "max_depth": c["max_depth"],
+                       "max_leaves": c["max_leaves"], "subsample": c["subsample"], "colsample": c["colsample"]}}
 
 
 def run_engine(args):
@@ -497,6 +563,11 @@ def run_engine(args):
         pred_ms = float(t.item())
     pred_rows_s = n / (pred_ms / 1000.0)
 
+    # ---- configs[4] at this GPU count (a sub-record of every config-4 line) --------
+    c5 = None
+    if not five and not args.no_config5:
+        c5 = config5_subrecord(eng, args, world, rank, local, dist)
+
     peak, peak_kind = measured_peak_hbm()
     achieved = (st["hist_alg_bytes"] / (st["hist_ms"] / 1000.0)) / 1e9 if st["hist_ms"] > 0 else 0.0
     atomics = None
@@ -564,6 +635,7 @@ def run_engine(args):
                                 "ms_per_step": d8_ms / args.steps,
                                 "config": "BASELINE configs[3] literally: same data, max_depth 8, 63 leaves"}
                                if d8_ms else None),
+            "config5": c5,
             "clocks": clk,
             "binning": bin_stats,
             "fit_from_raw": fit_raw,
@@ -621,6 +693,9 @@ def main():
     ap.add_argument("--part", default="all", choices=["all", "predict"],
                     help="predict: time only the ensemble predict (k_predict), for profiling")
     ap.add_argument("--predict-rows", type=int, default=1_000_000)
+    ap.add_argument("--config5-steps", type=int, default=20,
+                    help="timed rounds of the configs[4] (10M x 200) sub-record")
+    ap.add_argument("--no-config5", action="store_true", help="skip the configs[4] sub-record")
     args = ap.parse_args()
     global CFG, METRIC
     CFG = CONFIGS[args.config]

@@ -34,7 +34,7 @@ EXPORTS = (
     "gbm_set_l2_flush", "gbm_bin_edges", "gbm_upload_binned_rows", "gbm_bin_features",
     "gbm_predict_upload_raw", "gbm_predict_raw", "gbm_test_peer_wait", "gbm_upload_labels_mc",
     "gbm_round_mc", "gbm_get_F_mc", "gbm_get_grad_mc", "gbm_upload_targets", "gbm_round_reg",
-    "gbm_check_model",
+    "gbm_check_model", "gbm_sampler_create_device",
 )
 
 
@@ -122,6 +122,7 @@ def lib():
     L.gbm_predict_run.argtypes = [P, f64, f64]
     L.gbm_predict_fetch.argtypes = [P, P, P]
     L.gbm_sync.argtypes = [P]
+    L.gbm_sampler_create_device.argtypes = [C.c_uint32, i64, i32, f64, i32, i32, i32, C.POINTER(C.c_void_p)]
     L.gbm_sampler_create.argtypes = [C.c_uint32, i64, i32, i64, i32, i32, i32, i32,
                                      C.POINTER(C.c_void_p)]
     L.gbm_sampler_next.argtypes = [P, P, P, P]
@@ -562,6 +563,24 @@ class Sampler:
                                         C.byref(self._h))
         if rc != GBM_OK:
             raise ValueError(f"gbm_sampler_create failed ({ERRORS.get(rc, rc)})")
+
+    @classmethod
+    def device(cls, seed, n, p, subsample, n_feat, colsample_on, look_ahead=2):
+        """A throughput-mode sampler (gbm_sampler_create_device): features as
+        the reference draws them, rows drawn on the device by a counter-based
+        hash (each row in-bag with probability `subsample`).  Off the parity
+        paths: only the engine's round calls accept it."""
+        self = cls.__new__(cls)
+        self._L = lib()
+        self._h = C.c_void_p()
+        self.n, self.p, self.n_feat = int(n), int(p), int(n_feat)
+        self.n_sub = max(1, int(self.n * float(subsample)))
+        rc = self._L.gbm_sampler_create_device(C.c_uint32(int(seed) & 0xFFFFFFFF), self.n, self.p,
+                                               float(subsample), self.n_feat, int(bool(colsample_on)),
+                                               int(look_ahead), C.byref(self._h))
+        if rc != GBM_OK:
+            raise ValueError(f"gbm_sampler_create_device failed ({ERRORS.get(rc, rc)})")
+        return self
 
     def next(self, want_sample=False, want_mask=True):
         s = np.empty(self.n_sub, np.int64) if want_sample else None

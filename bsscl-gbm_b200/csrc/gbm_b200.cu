@@ -142,6 +142,7 @@ struct gbm_ctx {
     // end; gbm_fit_rounds keeps up to kRing rounds queued.
     struct Slot {
         int32_t *h_tg = nullptr, *d_tg = nullptr;   // the round's row swap targets
+        long long *h_round = nullptr, *d_round = nullptr;   // the round's index (throughput-mode rows)
         int32_t *h_feat = nullptr;     // fidx [p] | blist [nblk] | nb
         int32_t *d_fidx_c = nullptr;   // the round's fidx for its feature compaction on cst
         bool xc_on_cst = false;        // the round's packed blocks are made on cst (k_compact_feat)
@@ -633,6 +634,8 @@ int ensure_slots(gbm_ctx *ctx) {
         for (auto &s : ctx->slot) {
             TRY(halloc(ctx, &s.h_feat, (size_t)ctx->p + 2 * ctx->nblk + 2));
             TRY(dalloc(ctx, &s.d_fidx_c, (size_t)ctx->p));
+            TRY(halloc(ctx, &s.h_round, 1));
+            TRY(dalloc(ctx, &s.d_round, 1));
             TRY(halloc(ctx, &s.h_fpos, (size_t)ctx->nblk * kBlk + ctx->p));
             TRY(halloc(ctx, &s.h_tout, 1));
             TRY(halloc(ctx, &s.h_loss, 2));   // [0] loss, [1] the peer exchange's error word
@@ -1627,6 +1630,7 @@ int take_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset) 
         if (rows_on) TRY(launch(ctx, k_iota, dim3(grid_for(N, 256)), dim3(256), 0, ctx->cst, ctx->d_perm[R - 1], N));
     }
     ctx->feat_buf.resize((size_t)gbm_sampler_n_feat(sampler));
+    s.h_round[0] = (long long)r;   // the round a throughput-mode sampler hashes its rows with
     auto t_s = std::chrono::steady_clock::now();
     int rc = gbm_sampler_take_targets(sampler, s.h_tg, ctx->feat_buf.data());
     ctx->host_sample_ms += ms_since(t_s);
@@ -1638,7 +1642,20 @@ int take_sample(gbm_ctx *ctx, int si, gbm_sampler *sampler, int64_t row_offset) 
 // The round's shuffle (composed into the permutation), this rank's in-bag
 // mask and the root's row list, on the sampler stream (cst); ends with
 // slot si's `copied` event, which the engine stream waits for.
-int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int64_t row_offset, int nf) {
+// Throughput-mode rows of a sampler (gbm_sampler_create_device), or none.
+struct DevRows {
+    bool on = false;
+    uint64_t seed = 0, thr = 0;
+};
+
+DevRows dev_rows_of(const gbm_sampler *sampler) {
+    DevRows d;
+    d.on = gbm_sampler_device_rows(sampler, &d.seed, &d.thr) != 0;
+    return d;
+}
+
+int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int64_t row_offset, int nf,
+                   const DevRows &dr) {
     gbm_ctx::Slot &s = ctx->slot[si];
     constexpr int R = gbm_ctx::kRing;
     int32_t *pout = nullptr;
@@ -1666,7 +1683,11 @@ int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int
     // mask and root row list once the previous round is done with the row
     // lists (it is at its replay or F update by then)
     TRY(wait_ev(ctx, ctx->cst, ctx->rows_free));
-    if (rows_on) {
+    if (dr.on) {   // throughput mode: this rank's rows from the hash of (seed, round, global row)
+        CK(cudaMemcpyAsync(s.d_round, s.h_round, sizeof(long long), cudaMemcpyHostToDevice, ctx->cst));
+        TRY(launch(ctx, k_mask_hash, dim3(grid_for(ctx->n, 256)), dim3(256), 0, ctx->cst, ctx->d_mask, ctx->n,
+                   row_offset, dr.seed, dr.thr, (const long long *)s.d_round));
+    } else if (rows_on) {
         CK(cudaMemsetAsync(ctx->d_mask, 0, (size_t)ctx->n, ctx->cst));
         TRY(launch(ctx, k_mask_from_rows, dim3(grid_for(m, 256)), dim3(256), 0, ctx->cst, pout, m, row_offset,
                    ctx->n, ctx->d_mask));
@@ -1796,13 +1817,13 @@ int capture(gbm_ctx *ctx, cudaStream_t st, cudaGraphExec_t *out, F &&enqueue) {
 // replay, F update, tree and loss copies).  The host fills the slot's pinned
 // buffers before each launch.
 int capture_round(gbm_ctx *ctx, int si, int nf, const gbm_params *P, int64_t N, int64_t m, bool rows_on,
-                  int64_t row_offset) {
+                  int64_t row_offset, const DevRows &dr) {
     gbm_ctx::Slot &s = ctx->slot[si];
     const long long l0 = ctx->launches, h0 = ctx->hist_launches, w0 = ctx->waves;
     const double b0 = ctx->comm_bytes;
     ctx->cur_slot = si;
     s.tused = s.tdone = 0;
-    TRY(capture(ctx, ctx->cst, &s.g_cst, [&] { return enqueue_sample(ctx, si, N, m, rows_on, row_offset, nf); }));
+    TRY(capture(ctx, ctx->cst, &s.g_cst, [&] { return enqueue_sample(ctx, si, N, m, rows_on, row_offset, nf, dr); }));
     TRY(capture(ctx, ctx->st, &s.g_st, [&] {
         TRY(wait_ev(ctx, ctx->st, s.copied));
         TRY(enqueue_features(ctx, si, nf));
@@ -1903,6 +1924,8 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     for (auto &s : ctx->slot) {
         if (s.d_tg) cudaFree(s.d_tg);
         if (s.d_fidx_c) cudaFree(s.d_fidx_c);
+        if (s.d_round) cudaFree(s.d_round);
+        if (s.h_round) cudaFreeHost(s.h_round);
         void *hp[] = {s.h_tg, s.h_feat, s.h_fpos, s.h_tout, s.h_loss};
         for (void *p : hp) if (p) cudaFreeHost(p);
         if (s.copied) cudaEventDestroy(s.copied);
@@ -2432,7 +2455,7 @@ int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, co
     begin_round(ctx, si);
     TRY(take_sample(ctx, si, sampler, row_offset));
     TRY(enqueue_sample(ctx, si, gbm_sampler_rows(sampler), gbm_sampler_n_sub(sampler),
-                       gbm_sampler_shuffles_rows(sampler) != 0, row_offset, 0));
+                       gbm_sampler_shuffles_rows(sampler) != 0, row_offset, 0, dev_rows_of(sampler)));
     TRY(wait_ev(ctx, ctx->st, ctx->slot[si].copied));
     return round_body(ctx, si, ctx->feat_buf.data(), nf, P, out, train_loss, true);
 }
@@ -2457,6 +2480,7 @@ int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const
     const int R = gbm_ctx::kRing;
     const int64_t N = gbm_sampler_rows(sampler), m = gbm_sampler_n_sub(sampler);
     const bool rows_on = gbm_sampler_shuffles_rows(sampler) != 0;
+    const DevRows dr = dev_rows_of(sampler);
     if (rows_on) TRY(ensure_shuffle(ctx, N));   // before any capture: no allocation inside one
     // With several ranks a round is replayed from graphs: each round's ~13
     // collective enqueues cost the host more than the GPU needs for the
@@ -2464,10 +2488,10 @@ int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const
     // already hides the gaps there, and capturing costs a first fit time).
     const bool graphs = ctx->comm != nullptr;
     if (graphs) {
-        const std::string key = graph_key(ctx, P, nf, N, m, rows_on, row_offset);
+        const std::string key = graph_key(ctx, P, nf, N, m, rows_on, row_offset) + (dr.on ? "/dev" : "");
         if (key != ctx->graph_key) {
             drop_graphs(ctx);
-            for (int si = 0; si < R; si++) TRY(capture_round(ctx, si, nf, P, N, m, rows_on, row_offset));
+            for (int si = 0; si < R; si++) TRY(capture_round(ctx, si, nf, P, N, m, rows_on, row_offset, dr));
             ctx->graph_key = key;
         }
     }
@@ -2485,7 +2509,7 @@ int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const
             TRY(take_sample(ctx, si, sampler, row_offset));
             RoundFeat rf;
             TRY(setup_features(ctx, si, ctx->feat_buf.data(), nf, rf));   // before the sample packs its features
-            TRY(enqueue_sample(ctx, si, N, m, rows_on, row_offset, nf));
+            TRY(enqueue_sample(ctx, si, N, m, rows_on, row_offset, nf, dr));
             TRY(wait_ev(ctx, ctx->st, s.copied));
             TRY(enqueue_features(ctx, si, nf));
             TRY(enqueue_grow(ctx, rf, P, true));

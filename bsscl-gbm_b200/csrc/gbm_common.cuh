@@ -213,6 +213,18 @@ __device__ __forceinline__ int bin_of(const uint8_t *__restrict__ xb, int64_t n,
     return __ldg(xb + (((int64_t)(f >> 4) * n + row) << 4) + (f & 15));
 }
 
+// Throughput-mode row sampling (gbm_sampler_create_device): row `row`
+// (global id) is in-bag in round `round` iff this hash is below the
+// sampler's threshold.  The mixing is the splitmix64 finalizer (Steele, Lea
+// and Flood, 2014) of seed + round * k1 + row * k2; every rank hashes its own
+// rows, so the draw is the same at any GPU count and needs no exchange.
+__host__ __device__ __forceinline__ uint64_t gbm_row_hash(uint64_t seed, uint64_t round, uint64_t row) {
+    uint64_t z = seed + round * 0xd1b54a32d192ed03ull + row * 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
 // The split rule.  The reference sends bin <= thr left (E:668, E:855,
 // E:878), so the NaN bin (bin 0) always goes left.  A split learned with the
 // NaN direction (gbm_params.nan_direction) may instead send the NaN bin

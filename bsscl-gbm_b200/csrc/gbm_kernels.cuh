@@ -478,6 +478,15 @@ __global__ void k_shuf_compose(const int32_t *__restrict__ t, int64_t n, const i
     perm_out[i] = perm_in[s];
 }
 
+// Throughput-mode in-bag mask of this rank's rows (gbm_row_hash).
+__global__ void k_mask_hash(uint8_t *__restrict__ mask, int64_t n, int64_t row0, uint64_t seed, uint64_t thr,
+                            const long long *__restrict__ round_p) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint64_t r = (uint64_t)*round_p;
+    mask[i] = thr == ~0ull ? 1 : (gbm_row_hash(seed, r, (uint64_t)(row0 + i)) < thr ? 1 : 0);
+}
+
 __global__ void k_iota(int32_t *__restrict__ a, int64_t n) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) a[i] = (int32_t)i;

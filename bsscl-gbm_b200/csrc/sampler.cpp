@@ -18,6 +18,7 @@
 #include <immintrin.h>
 
 #include <algorithm>
+#include <cmath>
 #include <atomic>
 #include <condition_variable>
 #include <cstdint>
@@ -311,6 +312,10 @@ struct gbm_sampler {
     int64_t n = 0, n_sub = 0;
     int32_t p = 0, n_feat = 0;
     int sub_on = 0, col_on = 0;
+    // throughput mode (gbm_sampler_create_device): rows are drawn on the
+    // device from a counter-based hash, in-bag iff hash < dev_thr
+    int dev_rows = 0;
+    uint64_t dev_seed = 0, dev_thr = 0;
     std::vector<int32_t> perm;         // host-side row permutation (kModeHost)
     std::vector<int32_t> fperm, tfeat;
     std::vector<int32_t> sample;
@@ -423,8 +428,23 @@ int gbm_sampler_create(uint32_t seed, int64_t n, int32_t p, int64_t n_sub, int32
     return GBM_OK;
 }
 
+int gbm_sampler_create_device(uint32_t seed, int64_t n, int32_t p, double subsample, int32_t n_feat,
+                              int32_t colsample_on, int32_t look_ahead, gbm_sampler **out) {
+    if (!out || !(subsample > 0.0 && subsample <= 1.0)) return GBM_ERR_ARG;
+    const int64_t n_sub = std::max<int64_t>(1, (int64_t)((double)n * subsample));
+    int rc = gbm_sampler_create(seed, n, p, n_sub > n ? n : n_sub, n_feat, 0, colsample_on, look_ahead, out);
+    if (rc != GBM_OK) return rc;
+    gbm_sampler *s = *out;
+    s->dev_rows = 1;
+    s->dev_seed = 0x9e3779b97f4a7c15ull * ((uint64_t)seed + 1u);
+    // in-bag iff hash < subsample * 2^64 (every row when subsample is 1)
+    s->dev_thr = subsample >= 1.0 ? ~0ull : (uint64_t)std::ldexp(subsample, 64);
+    return GBM_OK;
+}
+
 // Host outputs: the row permutation is kept here (first call decides).
 static int host_ready(gbm_sampler *s) {
+    if (s->dev_rows) return GBM_ERR_STATE;   // its rows are drawn on the device only
     if (!s->claim(kModeHost)) return GBM_ERR_STATE;
     if (s->perm.empty()) {
         try {
@@ -499,3 +519,9 @@ int gbm_sampler_take_targets(gbm_sampler *s, int32_t *row_targets, int32_t *feat
 int64_t gbm_sampler_taken(const gbm_sampler *s) { return s ? s->taken : 0; }
 int64_t gbm_sampler_rows(const gbm_sampler *s) { return s ? s->n : 0; }
 int gbm_sampler_shuffles_rows(const gbm_sampler *s) { return s ? s->sub_on : 0; }
+int gbm_sampler_device_rows(const gbm_sampler *s, uint64_t *seed, uint64_t *thr) {
+    if (!s || !s->dev_rows) return 0;
+    *seed = s->dev_seed;
+    *thr = s->dev_thr;
+    return 1;
+}

@@ -14,3 +14,6 @@ GBM_INTERNAL int gbm_sampler_take_targets(gbm_sampler *s, int32_t *row_targets, 
 GBM_INTERNAL int64_t gbm_sampler_taken(const gbm_sampler *s);
 GBM_INTERNAL int64_t gbm_sampler_rows(const gbm_sampler *s);
 GBM_INTERNAL int gbm_sampler_shuffles_rows(const gbm_sampler *s);
+// 1 for a throughput-mode sampler (gbm_sampler_create_device): round r's
+// in-bag rows are those with gbm_row_hash(seed, r, global row) < thr.
+GBM_INTERNAL int gbm_sampler_device_rows(const gbm_sampler *s, uint64_t *seed, uint64_t *thr);

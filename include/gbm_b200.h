@@ -406,6 +406,20 @@ int gbm_event_elapsed(gbm_ctx *ctx, int32_t a, int32_t b, float *ms);
 int gbm_sampler_create(uint32_t seed, int64_t n, int32_t p, int64_t n_sub, int32_t n_feat,
                        int32_t subsample_on, int32_t colsample_on, int32_t look_ahead,
                        gbm_sampler **out);
+/* A throughput-mode sampler (no reference counterpart; off the parity
+ * paths): the features are drawn as above, but each round's in-bag rows are
+ * drawn on the device by the engine -- row i (global id) is in-bag in round
+ * r iff a counter-based hash of (seed, r, i) is below subsample * 2^64, so
+ * each row is in with probability `subsample` (the in-bag count varies
+ * around n * subsample) and every rank draws its own rows with no host work
+ * and no exchange, identically at any GPU count.  The reference's sampler
+ * (_get_subsample_indices, E:2502-2517) is a cumulative shuffle whose host
+ * cost grows with n (~7 ms per round at 10M rows); this one has none.  Only
+ * the engine's round calls (gbm_round_sampled, gbm_fit_rounds) accept it;
+ * gbm_sampler_next / _next_rows answer GBM_ERR_STATE. */
+int gbm_sampler_create_device(uint32_t seed, int64_t n, int32_t p, double subsample, int32_t n_feat,
+                              int32_t colsample_on, int32_t look_ahead, gbm_sampler **out);
+
 /* The next round's draw of _get_subsample_indices (E:2502-2517).  Any output
  * may be NULL: sample_idx [n_sub] (reference order), inbag_mask [n] (1 = in
  * bag), feat_idx [n_feat]. */

@@ -87,3 +87,47 @@ def test_rank_that_leaves_ends_the_peer_collective_with_an_error():
     status, dt = result.get(0, ("missing", 0.0))
     assert status not in ("completed", "missing")
     assert dt < 30.0
+
+
+_LONELY_RANK = r"""
+import sys, time
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+from bsscl_gbm_b200 import Engine
+eng = Engine(0)
+uid = Engine.nccl_unique_id()
+t0 = time.perf_counter()
+try:
+    eng.init_comm(uid, 2, 0, timeout_ms=1500)      # rank 1 never joins
+    print("JOINED")
+except RuntimeError as e:
+    print("ERR", time.perf_counter() - t0, str(e).replace("\n", " "))
+xb = np.zeros((100, 2), np.uint8)
+packed = {"features": np.array([-1], np.int16), "thresholds": np.array([0], np.int64),
+          "values": np.array([0.5]), "left": np.array([-1], np.int32), "right": np.array([-1], np.int32),
+          "offsets": np.array([0, 1], np.int32)}
+F, _ = eng.predict(xb, packed, 1, 2.0, 0.0)
+print("PREDICT", float(F[0]))
+eng.close()
+"""
+
+
+@pytest.mark.gpu
+def test_communicator_whose_peer_never_joins_times_out():
+    """gbm_ctx_init_comm for a 2-rank world with only rank 0 present: the
+    non-blocking NCCL init is polled with the engine's time limit, runs out,
+    is aborted and reported as GBM_ERR_TIMEOUT, and the context still runs
+    kernels afterwards.  A child process (NVLS off) so that nothing of the
+    aborted communicator outlives the test."""
+    import subprocess
+    import sys
+    from conftest import ROOT
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    out = subprocess.run([sys.executable, "-c", _LONELY_RANK, os.path.join(ROOT, "bsscl-gbm_b200")], env=env,
+                         capture_output=True, text=True, timeout=180)
+    lines = out.stdout.strip().splitlines()
+    err = [ln for ln in lines if ln.startswith("ERR")]
+    assert err, out.stdout + out.stderr
+    dt = float(err[0].split()[1])
+    assert "timeout" in err[0] and 1.0 < dt < 60.0, err[0]
+    assert "PREDICT 1.0" in lines, out.stdout + out.stderr

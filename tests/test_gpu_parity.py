@@ -378,3 +378,43 @@ def test_rounds_match_oracle_exact_at_scale(engine, n, p, drop):
         o = O.build_tree(Xb, g, h, smp, feat, counts, mode=O.MODE_EXACT, scale_bits=S, **kw)
         O.post_prune(o[0], o[3], o[4], o[6], kw["gamma"], o[5])
         _assert_tree_equal(tree, o, f"round {r}")
+
+
+def _row_hash(seed, rnd, rows):
+    """gbm_row_hash (csrc/gbm_common.cuh) restated with NumPy's wrapping uint64."""
+    with np.errstate(over="ignore"):
+        z = np.uint64(seed) + np.uint64(rnd) * np.uint64(0xD1B54A32D192ED03) + \
+            rows.astype(np.uint64) * np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+
+def test_device_sampler_rows_are_the_documented_hash(engine):
+    """The throughput-mode sampler (gbm_sampler_create_device): round r's
+    in-bag rows are those whose gbm_row_hash(seed, r, row) < subsample *
+    2^64, and its features are the reference stream's feature draws alone
+    (a host sampler with row subsampling off gives the same).  Every tree
+    equals the oracle's EXACT tree on exactly those rows and features."""
+    from bsscl_gbm_b200 import Sampler
+    d, Xb, y, w2, base = _cfg1_engine(engine)
+    n, p = Xb.shape
+    seed, frac, nfeat = 7, 0.6, int(p * 0.8)
+    s = Sampler.device(seed, n, p, frac, nfeat, True)
+    twin = Sampler(seed, n, p, n, nfeat, False, True)
+    dseed = (0x9E3779B97F4A7C15 * (seed + 1)) & 0xFFFFFFFFFFFFFFFF
+    thr = np.uint64(int(np.ldexp(frac, 64)))
+    kw = dict(max_leaves=31, max_depth=6, msl=5, mcw=2.0, lam=1.0, gamma=0.0)
+    prm = _params(lr=0.1, **kw)
+    S = engine.scale_bits()
+    for r in range(4):
+        g, h = engine.get_grad()
+        tree, loss, leaf = engine.round_sampled(s, 0, prm, 64, want_leaf=True)
+        rows = np.flatnonzero(_row_hash(dseed, r, np.arange(n)) < thr).astype(np.int64)
+        assert abs(len(rows) - frac * n) < 5 * np.sqrt(n)
+        _, _, feat = twin.next(want_sample=False, want_mask=False)
+        o = O.build_tree(Xb, g, h, rows, feat, d["counts"], mode=O.MODE_EXACT, scale_bits=S, **kw)
+        O.post_prune(o[0], o[3], o[4], o[6], kw["gamma"], o[5])
+        _assert_tree_equal(tree, o, f"round {r}")
+    s.close()
+    twin.close()
