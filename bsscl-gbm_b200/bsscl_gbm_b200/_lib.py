@@ -34,7 +34,7 @@ EXPORTS = (
     "gbm_set_l2_flush", "gbm_bin_edges", "gbm_upload_binned_rows", "gbm_bin_features",
     "gbm_predict_upload_raw", "gbm_predict_raw", "gbm_test_peer_wait", "gbm_upload_labels_mc",
     "gbm_round_mc", "gbm_get_F_mc", "gbm_get_grad_mc", "gbm_upload_targets", "gbm_round_reg",
-    "gbm_check_model", "gbm_sampler_create_device",
+    "gbm_check_model", "gbm_sampler_create_device", "gbm_predict_upload_u16",
 )
 
 
@@ -119,6 +119,7 @@ def lib():
     L.gbm_predict.argtypes = [P, P, i64, i32, C.POINTER(GbmPacked), f64, f64, P, P]
     L.gbm_predict_set_model.argtypes = [P, C.POINTER(GbmPacked), i32]
     L.gbm_predict_upload.argtypes = [P, P, i64, i32]
+    L.gbm_predict_upload_u16.argtypes = [P, P, i64, i32]
     L.gbm_predict_run.argtypes = [P, f64, f64]
     L.gbm_predict_fetch.argtypes = [P, P, P]
     L.gbm_sync.argtypes = [P]
@@ -495,8 +496,16 @@ class Engine:
                       ptr(keep.get("nan_right")))
         return s, keep
 
-    def predict(self, xbin_u8, packed, n_trees, lr, base, want_F=True, want_proba=True):
-        xb = np.ascontiguousarray(xbin_u8, dtype=np.uint8)
+    def predict(self, xbin, packed, n_trees, lr, base, want_F=True, want_proba=True):
+        """gbm_predict on uint8 bins; the reference's uint16 bins (ids up to
+        256: 257-bin features) go through gbm_predict_upload_u16."""
+        if np.asarray(xbin).dtype == np.uint16:
+            xb = np.ascontiguousarray(xbin)
+            self.predict_set_model(packed, n_trees, xb.shape[1])
+            self.predict_upload(xb)
+            self.predict_run(lr, base)
+            return self.predict_fetch(want_F, want_proba)
+        xb = np.ascontiguousarray(xbin, dtype=np.uint8)
         n, p = xb.shape
         s, keep = self.packed_struct(packed, n_trees)
         F = np.empty(n, np.float64) if want_F else None
@@ -510,8 +519,16 @@ class Engine:
         self.check(self._L.gbm_predict_set_model(self._h, C.byref(s), int(n_features)),
                    "gbm_predict_set_model")
 
-    def predict_upload(self, xbin_u8):
-        xb = np.ascontiguousarray(xbin_u8, dtype=np.uint8)
+    def predict_upload(self, xbin):
+        """uint8 bins (gbm_predict_upload) or the reference's uint16
+        (gbm_predict_upload_u16)."""
+        if np.asarray(xbin).dtype == np.uint16:
+            xb = np.ascontiguousarray(xbin)
+            self._pn = xb.shape[0]
+            self.check(self._L.gbm_predict_upload_u16(self._h, ptr(xb), xb.shape[0], xb.shape[1]),
+                       "gbm_predict_upload_u16")
+            return
+        xb = np.ascontiguousarray(xbin, dtype=np.uint8)
         self._pn = xb.shape[0]
         self.check(self._L.gbm_predict_upload(self._h, ptr(xb), xb.shape[0], xb.shape[1]),
                    "gbm_predict_upload")

@@ -96,14 +96,19 @@ def bin_features(X, edges, counts, nan_bin_id):
 
 
 def device_bins(X_bin, counts):
-    """uint8 ids for the device: ``min(id, bin_count - 1)``.
+    """Ids for the device: ``min(id, bin_count - 1)``, as uint8 -- or as
+    uint16 when a feature has 257 bins (n_bins 256 with a NaN bin,
+    E:2111-2127), whose id 256 the device keeps as a row bit.
 
     Lossless for training and predict: the histogram clamps ids >= bin_count
     the same way (E:593-594), and no threshold exceeds bin_count - 2
     (E:604), so the clamped id always goes right whenever the raw one did.
     """
     lim = np.asarray(counts, dtype=np.int64) - 1
-    if int(lim.max()) > 255:
-        raise ValueError("the device path holds at most 256 bins per feature "
-                         f"(feature with {int(lim.max()) + 1} bins); use n_bins <= 255")
+    if int(lim.max()) > 256:
+        raise ValueError("the device path holds at most 257 bins per feature "
+                         f"(feature with {int(lim.max()) + 1} bins); use n_bins <= 256")
+    X_bin = np.asarray(X_bin)
+    if int(lim.max()) == 256:
+        return np.minimum(X_bin, lim[None, :].astype(X_bin.dtype)).astype(np.uint16)
     return np.minimum(X_bin, lim[None, :].astype(X_bin.dtype)).astype(np.uint8)

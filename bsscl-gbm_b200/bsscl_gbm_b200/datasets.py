@@ -183,3 +183,26 @@ def regression(n=8_000, p=10, seed=9, nan_frac=0.05, scale=100.0):
         + rng.standard_normal(n) * (scale / 10.0)
     X[:, -2:][rng.random((n, 2)) < nan_frac] = np.nan
     return X, y
+
+
+def top_bin(n=20_000, p=30, seed=21, nan_frac=0.2, n_top=60):
+    """Data for the reference's default constructor (``n_bins='auto'``:
+    256 bins once p >= 28, E:2111-2127), where every continuous feature gets
+    257 bin ids.  N(0,1) float64 features, ``nan_frac`` NaN in the first
+    ten; in features 3 (with NaN) and 12 (without) ``n_top`` rows -- fewer
+    than 1/256 of the rows, so the quantile edges stay distinct -- are set
+    to the column maximum and labelled positive, so that a threshold of 255
+    (bin 256 alone on the right) is worth a split.
+    """
+    rng = np.random.default_rng(seed)
+    X = rng.standard_normal((n, p))
+    logit = 1.2 * X[:, 0] - 0.8 * X[:, 5] + 0.6 * X[:, 12] * X[:, 7]
+    y = (rng.random(n) < _sigmoid(logit + _solve_intercept(logit, 0.15))).astype(np.int64)
+    X[:, :10][rng.random((n, 10)) < nan_frac] = np.nan
+    for j in (3, 12):
+        col = X[:, j]
+        finite = np.flatnonzero(~np.isnan(col))
+        top = rng.choice(finite, size=n_top, replace=False)
+        col[top] = np.nanmax(col)
+        y[top] = 1
+    return X, y

@@ -300,9 +300,9 @@ class HybridHistGBMNumbaV1_0_1:
 
     def _check_device_bins(self):
         mx = int(np.max(self.feature_bin_counts))
-        if mx > 256:
-            raise ValueError("the device path holds at most 256 bins per feature "
-                             f"(feature with {mx} bins); use n_bins <= 255")
+        if mx > 257:
+            raise ValueError("the device path holds at most 257 bins per feature "
+                             f"(feature with {mx} bins); use n_bins <= 256")
 
     def _tree_capacity(self):
         if self.grow_policy == 'leaf':

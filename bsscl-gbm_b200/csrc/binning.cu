@@ -361,7 +361,8 @@ __global__ void __launch_bounds__(kBinThreads) k_bin_keys(const typename Keys<T>
                                                           const double *__restrict__ edges, int stride,
                                                           const int *__restrict__ counts,
                                                           const int *__restrict__ nanb, int any_nan, int ts,
-                                                          uint8_t *__restrict__ xb) {
+                                                          uint8_t *__restrict__ xb, const int32_t *__restrict__ bigidx,
+                                                          uint32_t *__restrict__ topbits) {
     typedef typename Keys<T>::V V;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ Tab<V> tb;
@@ -375,7 +376,11 @@ __global__ void __launch_bounds__(kBinThreads) k_bin_keys(const typename Keys<T>
         uint32_t w[4] = {0u, 0u, 0u, 0u};
         for (int f = 0; f < nf; f++) {
             const V v = (V)ovalue(keys[(int64_t)(b * 16 + f) * n + lo + i]);
-            const int id = min(bin_id(tb, f, ts, any_nan, v), tb.nb[f] - 1);
+            int id = min(bin_id(tb, f, ts, any_nan, v), tb.nb[f] - 1);
+            if (id > 255) {   // bin 256 of a 257-bin feature: stored as 255, marked in the top bits
+                atomicOr(topbits + (int64_t)bigidx[b * 16 + f] * ((rows + 31) >> 5) + (i >> 5), 1u << (i & 31));
+                id = 255;
+            }
             w[f >> 2] |= (uint32_t)id << (8 * (f & 3));
         }
         *reinterpret_cast<uint4 *>(xb + ((int64_t)b * rows + i) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -389,7 +394,9 @@ __global__ void __launch_bounds__(kBinThreads) k_bin_rows(const T *__restrict__ 
                                                           const double *__restrict__ edges, int stride,
                                                           const int *__restrict__ counts,
                                                           const int *__restrict__ nanb, int any_nan, int ts,
-                                                          void *__restrict__ out) {
+                                                          void *__restrict__ out, const int32_t *__restrict__ bigidx,
+                                                          uint32_t *__restrict__ topbits, int64_t row0,
+                                                          int64_t top_words) {
     typedef typename Keys<T>::V V;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ Tab<V> tb;
@@ -403,8 +410,15 @@ __global__ void __launch_bounds__(kBinThreads) k_bin_rows(const T *__restrict__ 
         const T *x = X + i * p + b * 16;
         for (int f = 0; f < nf; f++) {
             const int id = bin_id(tb, f, ts, any_nan, (V)x[f]);
-            if (MODE == 0)
-                static_cast<uint8_t *>(out)[i * p + b * 16 + f] = (uint8_t)min(id, tb.nb[f] - 1);
+            if (MODE == 0) {
+                int c = min(id, tb.nb[f] - 1);
+                if (c > 255) {   // bin 256 of a 257-bin feature: 255, marked in the top bits
+                    const int64_t r = row0 + i;
+                    atomicOr(topbits + (int64_t)bigidx[b * 16 + f] * top_words + (r >> 5), 1u << (r & 31));
+                    c = 255;
+                }
+                static_cast<uint8_t *>(out)[i * p + b * 16 + f] = (uint8_t)c;
+            }
             else
                 static_cast<uint16_t *>(out)[i * p + b * 16 + f] = (uint16_t)id;
         }
@@ -671,7 +685,8 @@ int edges(Work *w, cudaStream_t st, int n_bins, const uint8_t *is_cat, double *e
 }
 
 int bin_blocks(Work *w, cudaStream_t st, int64_t lo, int64_t hi, const double *edges, int stride,
-               const int32_t *counts, const int32_t *nan_bin, uint8_t *d_xb, std::string &err) {
+               const int32_t *counts, const int32_t *nan_bin, uint8_t *d_xb, const int32_t *d_bigidx,
+               uint32_t *d_topbits, std::string &err) {
     if (w->dtype < 0) {
         err = "binning: no matrix loaded";
         return -1;
@@ -692,12 +707,14 @@ int bin_blocks(Work *w, cudaStream_t st, int64_t lo, int64_t hi, const double *e
         const size_t sm = 16 * (size_t)ts * sizeof(double);
         smem_opt_in(k_bin_keys<double>, sm);
         k_bin_keys<double><<<grid, kBinThreads, sm, st>>>(static_cast<const unsigned long long *>(w->keys), w->n, p,
-                                                          lo, rows, d_ed, stride, d_cnt, d_nb, any_nan, ts, d_xb);
+                                                          lo, rows, d_ed, stride, d_cnt, d_nb, any_nan, ts, d_xb,
+                                                          d_bigidx, d_topbits);
     } else {
         const size_t sm = 16 * (size_t)ts * sizeof(float);
         smem_opt_in(k_bin_keys<float>, sm);
         k_bin_keys<float><<<grid, kBinThreads, sm, st>>>(static_cast<const uint32_t *>(w->keys), w->n, p, lo, rows,
-                                                         d_ed, stride, d_cnt, d_nb, any_nan, ts, d_xb);
+                                                         d_ed, stride, d_cnt, d_nb, any_nan, ts, d_xb,
+                                                         d_bigidx, d_topbits);
     }
     BCK("k_bin_keys", cudaGetLastError());
     return 0;
@@ -705,7 +722,7 @@ int bin_blocks(Work *w, cudaStream_t st, int64_t lo, int64_t hi, const double *e
 
 int bin_rows(Work *w, gbmh2d::Stager *sg, cudaStream_t st, const void *X, int64_t n, int p, int dtype,
              const double *edges, int stride, const int32_t *counts, const int32_t *nan_bin, int out_mode, void *out,
-             std::string &err) {
+             const int32_t *d_bigidx, uint32_t *d_topbits, std::string &err) {
     if (!X || !out || n <= 0 || p <= 0 || (dtype != 0 && dtype != 1) || (out_mode != 0 && out_mode != 1)) {
         err = "binning: bad arguments";
         return -1;
@@ -741,17 +758,17 @@ int bin_rows(Work *w, gbmh2d::Stager *sg, cudaStream_t st, const void *X, int64_
         if (dtype) {
             if (out_mode == 0)
                 k_bin_rows<double, 0><<<grid, kBinThreads, sm, st>>>(static_cast<const double *>(dev), nr, p, d_ed,
-                                                                     stride, d_cnt, d_nb, any_nan, ts, o);
+                                                                     stride, d_cnt, d_nb, any_nan, ts, o, d_bigidx, d_topbits, r0, (n + 31) >> 5);
             else
                 k_bin_rows<double, 1><<<grid, kBinThreads, sm, st>>>(static_cast<const double *>(dev), nr, p, d_ed,
-                                                                     stride, d_cnt, d_nb, any_nan, ts, o);
+                                                                     stride, d_cnt, d_nb, any_nan, ts, o, d_bigidx, d_topbits, r0, (n + 31) >> 5);
         } else {
             if (out_mode == 0)
                 k_bin_rows<float, 0><<<grid, kBinThreads, sm, st>>>(static_cast<const float *>(dev), nr, p, d_ed,
-                                                                    stride, d_cnt, d_nb, any_nan, ts, o);
+                                                                    stride, d_cnt, d_nb, any_nan, ts, o, d_bigidx, d_topbits, r0, (n + 31) >> 5);
             else
                 k_bin_rows<float, 1><<<grid, kBinThreads, sm, st>>>(static_cast<const float *>(dev), nr, p, d_ed,
-                                                                    stride, d_cnt, d_nb, any_nan, ts, o);
+                                                                    stride, d_cnt, d_nb, any_nan, ts, o, d_bigidx, d_topbits, r0, (n + 31) >> 5);
         }
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_fail(err, "k_bin_rows", e);

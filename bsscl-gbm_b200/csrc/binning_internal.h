@@ -36,15 +36,21 @@ int edges(Work *w, cudaStream_t st, int n_bins, const uint8_t *is_cat, double *e
           int32_t *counts_out, int32_t *nan_bin_out, int32_t *max_b_out, std::string &err);
 
 // Bins rows [lo, hi) of the loaded matrix into the training layout: column
-// blocks uint8 [ceil(p/16)][hi-lo][16], ids clamped to bin_count - 1.
+// blocks uint8 [ceil(p/16)][hi-lo][16], ids clamped to bin_count - 1; an id
+// of 256 (a 257-bin feature) is stored as 255 and sets the row's bit in
+// d_topbits [big feature d_bigidx[j]][ceil((hi - lo) / 32)] (zeroed by the
+// caller).
 int bin_blocks(Work *w, cudaStream_t st, int64_t lo, int64_t hi, const double *edges, int stride,
-               const int32_t *counts, const int32_t *nan_bin, uint8_t *d_xb, std::string &err);
+               const int32_t *counts, const int32_t *nan_bin, uint8_t *d_xb, const int32_t *d_bigidx,
+               uint32_t *d_topbits, std::string &err);
 
 // Bins a host matrix row by row.  out_mode 0: uint8 [n][p] ids clamped to
-// bin_count - 1 into device memory `out` (the predict input); 1: the raw
-// uint16 [n][p] ids of _bin_features (E:2144-2189) into host memory `out`.
+// bin_count - 1 into device memory `out` (the predict input), an id of 256
+// stored as 255 with the row's bit set in d_topbits [d_bigidx[j]][ceil(n /
+// 32)] (zeroed by the caller); 1: the raw uint16 [n][p] ids of
+// _bin_features (E:2144-2189) into host memory `out`.
 int bin_rows(Work *w, gbmh2d::Stager *sg, cudaStream_t st, const void *X, int64_t n, int p, int dtype,
              const double *edges, int stride, const int32_t *counts, const int32_t *nan_bin, int out_mode,
-             void *out, std::string &err);
+             void *out, const int32_t *d_bigidx, uint32_t *d_topbits, std::string &err);
 
 }  // namespace gbmbin

@@ -70,6 +70,16 @@ struct gbm_ctx {
     const uint8_t *xc_cur = nullptr;   // the buffer of the round being enqueued
     int32_t *d_counts = nullptr;
     std::vector<int32_t> counts;
+    // Features with 257 bins (ids 0..256, n_bins 256: E:2111-2127) keep
+    // min(id, 255) in d_xb; the rows whose id is 256 are bits of d_topbits
+    // [nbig][ceil(n / 32)] and, as ascending row lists, d_toprows
+    // [d_topoff[b] .. d_topoff[b + 1]).  d_bigidx [p]: the feature's index
+    // among them, -1 for every other feature.
+    int nbig = 0;
+    std::vector<int32_t> bigfeat;
+    int32_t *d_bigidx = nullptr, *d_bigfeat = nullptr, *d_topoff = nullptr, *d_toprows = nullptr;
+    uint32_t *d_topbits = nullptr;
+    int64_t *d_toppairs = nullptr;   // the uint16 upload's (row, big index) pairs of id 256
     uint8_t *d_y = nullptr;
     double *d_F = nullptr;
     longlong2 *d_q = nullptr;
@@ -211,6 +221,11 @@ struct gbm_ctx {
     int32_t p_trees_cap = 0;
     int32_t p_nfeat = 0;
     double *d_pF = nullptr, *d_pP = nullptr;
+    // the predict rows' bin-256 bits, as for training (null when no feature has them)
+    int32_t *d_pbigidx = nullptr;
+    uint32_t *d_ptopbits = nullptr;
+    bool p_top = false;
+    bool p_model_top = false;   // the model has a threshold of 255 (the bits matter)
 
     // uploads and binning
     gbmh2d::Stager *stager = nullptr;  // pinned ring + copy threads for host -> device streams
@@ -403,9 +418,10 @@ int halloc(gbm_ctx *ctx, T **p, size_t count) {
 // and values, with every check that keeps the device walk inside its tree:
 // offsets start at 0 and increase (no empty tree), trees hold at most 32767
 // nodes, an internal node's feature is below n_features, its threshold is
-// not negative (above 255 it is read as 255: every uint8 bin goes left, as
-// the reference's compare does), and its children lie after it inside its
-// tree, so every walk ends.  Nothing is uploaded when a check fails.
+// not negative (above 255 it is stored as 255 with nanr bit 1: every bin,
+// 256 included, goes left, as the reference's compare does), and its
+// children lie after it inside its tree, so every walk ends.  Nothing is
+// uploaded when a check fails.
 int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::vector<PNode> &nodes,
                std::vector<double> &vals, std::vector<uint32_t> *n32 = nullptr, std::vector<double> *v32 = nullptr,
                std::vector<int32_t> *dep32 = nullptr) {
@@ -445,7 +461,7 @@ int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::v
                                 "tree (%d nodes)", t, kk, l, r, sz);
                 nd.feat = (int16_t)f;
                 nd.thr = (uint8_t)(th > 255 ? 255 : th);
-                nd.nanr = (uint8_t)nr;
+                nd.nanr = (uint8_t)(nr | (th > 255 ? 2 : 0));
                 nd.left = (int16_t)l;
                 nd.right = (int16_t)r;
             }
@@ -481,8 +497,12 @@ int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::v
                 uint32_t w = (255u << 12) | (uint32_t)nid[h];   // a leaf: no bin is above 255
                 if (nd.feat >= 0) {
                     if (next + 1 >= sz) return GBM_OK;   // more nodes than the tree holds (shared children)
-                    w = ((uint32_t)nd.nanr << 31) | ((uint32_t)nd.feat << 20) |
-                        ((uint32_t)(nd.nanr ? nd.thr - 1 : nd.thr) << 12) | (uint32_t)next;
+                    // threshold 255 exactly: bin 256 of a 257-bin feature goes right,
+                    // which needs the top bits of the 8-byte walk
+                    if (nd.thr == 255 && !(nd.nanr & 2)) return GBM_OK;
+                    const uint32_t nr = nd.nanr & 1;
+                    w = (nr << 31) | ((uint32_t)nd.feat << 20) | ((uint32_t)(nr ? nd.thr - 1 : nd.thr) << 12) |
+                        (uint32_t)next;
                     order.push_back(nd.left);
                     nid.push_back(next);
                     lev.push_back(lev[h] + 1);
@@ -526,25 +546,28 @@ template <int RPT, bool PK, bool SR>
 cudaError_t launch_predict_t(const PredShape &sh, unsigned grid, const uint8_t *xr, int64_t n, int p,
                              const void *nodes, const double *vals, const int32_t *off, const int32_t *dep, int ntree,
                              const int4 *cstart, const int32_t *nchunk, double lr, double base, double *F,
-                             double *P, cudaStream_t st) {
+                             double *P, const int32_t *bigidx, const uint32_t *topbits, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(k_predict<RPT, PK, SR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sh.smem);
     if (e != cudaSuccess) return e;
     k_predict<RPT, PK, SR><<<grid, kPredThreads, sh.smem, st>>>(xr, n, p, nodes, vals, off, dep, ntree, cstart,
-                                                                 nchunk, sh.rpc, lr, base, F, P);
+                                                                 nchunk, sh.rpc, lr, base, F, P, bigidx,
+                                                                 topbits);
     return cudaGetLastError();
 }
 
 // The ensemble over n rows (row-major bins [n][p]); chunk starts and count
 // were written by k_pred_chunks.  `packed`: nodes are 32-bit breadth-first
 // words with per-tree depths `dep` (pack_model), else PNode (dep unused).
-// Allocates nothing.
+// bigidx [p] / topbits [big][ceil(n / 32)]: the rows of bin 256 of 257-bin
+// features (null: none; only the PNode walk reads them).  Allocates nothing.
 cudaError_t launch_predict(const uint8_t *xr, int64_t n, int p, const void *nodes, bool packed, const double *vals,
                            const int32_t *off, const int32_t *dep, int ntree, const int4 *cstart,
-                           const int32_t *nchunk, double lr, double base, double *F, double *P, cudaStream_t st) {
+                           const int32_t *nchunk, double lr, double base, double *F, double *P,
+                           const int32_t *bigidx, const uint32_t *topbits, cudaStream_t st) {
     const PredShape sh = predict_shape(p, packed);
     const unsigned grid = (unsigned)((n + sh.rpc - 1) / sh.rpc);
-#define GBM_PRED(R, K, S) launch_predict_t<R, K, S>(sh, grid, xr, n, p, nodes, vals, off, dep, ntree, cstart, nchunk, lr, base, F, P, st)
+#define GBM_PRED(R, K, S) launch_predict_t<R, K, S>(sh, grid, xr, n, p, nodes, vals, off, dep, ntree, cstart, nchunk, lr, base, F, P, bigidx, topbits, st)
     if (sh.rpt == 2) return packed ? GBM_PRED(2, true, true) : GBM_PRED(2, false, true);
     if (sh.stage_rows) return packed ? GBM_PRED(1, true, true) : GBM_PRED(1, false, true);
     return packed ? GBM_PRED(1, true, false) : GBM_PRED(1, false, false);
@@ -993,6 +1016,12 @@ int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p) {
                    ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p,
                    ctx->d_blist, d_nb, ctx->d_fpos, rf.nf, ctx->d_q, stage, par, ctx->pst_stride,
                    ctx->hist_seg_cost));
+    if (ctx->nbig)   // bin 256 of the 257-bin features, into the top cells
+        TRY(launch(ctx, k_hist_top, dim3(ctx->nbig), dim3(128), 0, ctx->st, (const int32_t *)ctx->d_rows,
+                   (const int32_t *)ctx->d_tmp, (const HistTask *)ctx->d_htask, ntask_p,
+                   (const int32_t *)ctx->d_bigfeat, (const int16_t *)ctx->d_fpos, (const int32_t *)ctx->d_topoff,
+                   (const int32_t *)ctx->d_toprows, rf.nf, (const longlong2 *)ctx->d_q, stage, par,
+                   ctx->pst_stride));
     if (e1) TRY(record_ev(ctx, e1, ctx->st));
     ctx->hist_launches++;
     return GBM_OK;
@@ -1136,7 +1165,8 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
         TRY(launch(ctx, k_leaf_totals, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp,
                                                               ctx->d_ptask, lvl_cnt,
                                                               ints(ctx, I_TILES), ctx->d_q, ctx->d_leafw,
-                                                              ctx->d_nleft));
+                                                              ctx->d_nleft, (const int32_t *)ctx->d_bigidx,
+                                                              (const uint32_t *)ctx->d_topbits));
         if (ctx->comm)
             TRY(allreduce_i64(ctx, ctx->d_leafw, (int64_t)kLeafWords * W_ub));
         TRY(launch(ctx, k_leaf_finish, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, lvl, lvl_cnt, ctx->d_leafw, ctx->d_nleft, ctx->S));
@@ -1144,7 +1174,8 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
         return GBM_OK;
     }
     TRY(launch(ctx, k_part_count, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_ptask,
-                                                         lvl_cnt, ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt));
+                                                         lvl_cnt, ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt,
+                                                         (const int32_t *)ctx->d_bigidx, (const uint32_t *)ctx->d_topbits));
     const long long *gl = ctx->comm ? nullptr : ctx->d_nleft;   // several ranks: the locally smaller child
     TRY(launch(ctx, k_part_scatter, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, (const int32_t *)ctx->d_rows,
                ctx->d_tmp, (const PartTask *)ctx->d_ptask, (const int *)lvl_cnt, (const int *)ints(ctx, I_TILES),
@@ -1540,7 +1571,7 @@ int enqueue_update(gbm_ctx *ctx, const gbm_params *P, bool want_leaf, double *h_
     TRY(launch(ctx, k_update, dim3(ctx->upd_blocks), dim3(kUpdThreads), 0, ctx->st, 
         ctx->d_tree, ctx->d_xb, ctx->n, ctx->d_y, ctx->w[0], ctx->w[1], P->learning_rate, scale, ctx->d_F,
         ctx->d_q, want_leaf ? ctx->d_leaf : nullptr, ctx->d_loss_part, (unsigned *)ints(ctx, I_DONE_UPD),
-        ctx->d_loss));
+        ctx->d_loss, (const int32_t *)ctx->d_bigidx, (const uint32_t *)ctx->d_topbits));
     if (ctx->comm) TRY(allreduce_f64(ctx, ctx->d_loss, 1));
     CK(cudaMemcpyAsync(h_loss, ctx->d_loss, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
     return GBM_OK;
@@ -1699,15 +1730,14 @@ int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int
     return GBM_OK;
 }
 
-// Row-major bins [n][p] of type T -> column blocks on the device, clamped
-// to bin_count - 1.
-// Sizes, bin counts and the training matrix buffer for n rows x p features.
+// Sizes, bin counts and the training matrix buffer for n rows x p
+// features; features of 257 bins get their big index and zeroed top bits.
 int begin_bins(gbm_ctx *ctx, int64_t n, int32_t p, const int32_t *bin_counts) {
     if (!ctx || !bin_counts || n <= 0 || p <= 0 || n > 0x7fffffffLL) return GBM_ERR_ARG;
     if (ctx->dev < 0) return GBM_ERR_STATE;
     for (int j = 0; j < p; j++)
-        if (bin_counts[j] < 1 || bin_counts[j] > kBins)
-            return fail(ctx, GBM_ERR_UNSUPPORTED, "feature %d has %d bins; the device path holds 1..256 bins",
+        if (bin_counts[j] < 1 || bin_counts[j] > kBins + 1)
+            return fail(ctx, GBM_ERR_UNSUPPORTED, "feature %d has %d bins; the device path holds 1..257 bins",
                         j, bin_counts[j]);
     CK(cudaSetDevice(ctx->dev));
     ctx->n = n; ctx->p = p; ctx->nblk = (p + kBlk - 1) / kBlk;
@@ -1719,12 +1749,71 @@ int begin_bins(gbm_ctx *ctx, int64_t n, int32_t p, const int32_t *bin_counts) {
         for (auto &b : ctx->d_xc) TRY(dalloc(ctx, &b, (size_t)ctx->nblk * n * kBlk));
     TRY(dalloc(ctx, &ctx->d_counts, (size_t)p));
     CK(cudaMemcpyAsync(ctx->d_counts, bin_counts, sizeof(int32_t) * p, cudaMemcpyHostToDevice, ctx->st));
+    std::vector<int32_t> bigidx((size_t)p, -1);
+    ctx->bigfeat.clear();
+    for (int j = 0; j < p; j++)
+        if (bin_counts[j] > kBins) {
+            bigidx[(size_t)j] = (int32_t)ctx->bigfeat.size();
+            ctx->bigfeat.push_back(j);
+        }
+    ctx->nbig = (int)ctx->bigfeat.size();
+    TRY(dalloc(ctx, &ctx->d_bigidx, (size_t)p));
+    CK(cudaMemcpy(ctx->d_bigidx, bigidx.data(), sizeof(int32_t) * p, cudaMemcpyHostToDevice));
+    if (ctx->nbig) {
+        const size_t words = (size_t)ctx->nbig * (size_t)((n + 31) >> 5);
+        TRY(dalloc(ctx, &ctx->d_topbits, words));
+        CK(cudaMemsetAsync(ctx->d_topbits, 0, sizeof(uint32_t) * words, ctx->st));
+        TRY(dalloc(ctx, &ctx->d_bigfeat, (size_t)ctx->nbig));
+        CK(cudaMemcpy(ctx->d_bigfeat, ctx->bigfeat.data(), sizeof(int32_t) * ctx->nbig, cudaMemcpyHostToDevice));
+        TRY(dalloc(ctx, &ctx->d_topoff, (size_t)ctx->nbig + 1));
+    }
     return GBM_OK;
+}
+
+// The ascending row lists of the top bits (k_hist_top's input).
+int build_top_lists(gbm_ctx *ctx) {
+    if (!ctx->nbig) return GBM_OK;
+    const int64_t wp = (ctx->n + 31) >> 5;
+    TRY(launch(ctx, k_top_list<false>, dim3(ctx->nbig), dim3(256), 0, ctx->st, (const uint32_t *)ctx->d_topbits, wp,
+               ctx->n, ctx->d_topoff, (const int32_t *)nullptr, (int32_t *)nullptr));
+    std::vector<int32_t> off((size_t)ctx->nbig + 1, 0);
+    CK(cudaMemcpyAsync(off.data() + 1, ctx->d_topoff, sizeof(int32_t) * ctx->nbig, cudaMemcpyDeviceToHost, ctx->st));
+    TRY(sync_stream(ctx));
+    for (int b = 0; b < ctx->nbig; b++) off[(size_t)b + 1] += off[(size_t)b];
+    TRY(dalloc(ctx, &ctx->d_toprows, (size_t)std::max(1, off[(size_t)ctx->nbig])));
+    CK(cudaMemcpyAsync(ctx->d_topoff, off.data(), sizeof(int32_t) * (ctx->nbig + 1), cudaMemcpyHostToDevice, ctx->st));
+    TRY(launch(ctx, k_top_list<true>, dim3(ctx->nbig), dim3(256), 0, ctx->st, (const uint32_t *)ctx->d_topbits, wp,
+               ctx->n, (int32_t *)nullptr, (const int32_t *)ctx->d_topoff, ctx->d_toprows));
+    return sync_stream(ctx);
+}
+
+// Top bits from the uint16 upload's element indices (row * p + feature) of
+// ids above 255: the features of 257 bins read them as bin 256; every
+// other feature's clamp to bin_count - 1 already holds them.
+int set_top_bits(gbm_ctx *ctx, const std::vector<int64_t> &wide, int32_t p, const std::vector<int32_t> &bigidx,
+                 int64_t rows, uint32_t *bits) {
+    std::vector<int64_t> pairs;
+    for (int64_t e : wide) {
+        const int32_t b = bigidx[(size_t)(e % p)];
+        if (b >= 0) {
+            pairs.push_back(e / p);
+            pairs.push_back(b);
+        }
+    }
+    if (pairs.empty()) return GBM_OK;
+    const int64_t m = (int64_t)pairs.size() / 2;
+    TRY(dalloc(ctx, &ctx->d_toppairs, pairs.size()));
+    CK(cudaMemcpyAsync(ctx->d_toppairs, pairs.data(), sizeof(int64_t) * pairs.size(), cudaMemcpyHostToDevice,
+                       ctx->st));
+    TRY(launch(ctx, k_set_topbits, dim3(grid_for(m, 256)), dim3(256), 0, ctx->st, (const int64_t *)ctx->d_toppairs,
+               m, (rows + 31) >> 5, bits));
+    return sync_stream(ctx);   // the pairs are host memory freed on return
 }
 
 // Everything that depends on the bins once they are on the device.
 int finish_bins(gbm_ctx *ctx) {
     TRY(sync_stream(ctx));
+    TRY(build_top_lists(ctx));
     TRY(alloc_round_fixed(ctx));
     TRY(dalloc(ctx, &ctx->d_y, (size_t)ctx->n));
     TRY(dalloc(ctx, &ctx->d_F, (size_t)ctx->n));
@@ -1762,8 +1851,15 @@ int upload_bins_t(gbm_ctx *ctx, const T *xbin, int64_t n, int32_t p, const int32
     };
     std::string err;
     const gbmh2d::Pack pk = sizeof(T) == 2 ? gbmh2d::Pack::U16toU8 : gbmh2d::Pack::Copy;
-    if (gbmh2d::stream_rows(ctx->stager, ctx->st, xbin, n, sizeof(T) * (size_t)p, pk, 0, dst, after, err))
+    std::vector<int64_t> wide;   // uint16 ids above 255
+    if (gbmh2d::stream_rows(ctx->stager, ctx->st, xbin, n, sizeof(T) * (size_t)p, pk, 0, dst, after, err,
+                            ctx->nbig ? &wide : nullptr))
         return fail(ctx, GBM_ERR_CUDA, "bin upload: %s", err.empty() ? ctx->err.c_str() : err.c_str());
+    if (!wide.empty()) {
+        std::vector<int32_t> bigidx((size_t)p, -1);
+        for (int b = 0; b < ctx->nbig; b++) bigidx[(size_t)ctx->bigfeat[(size_t)b]] = b;
+        TRY(set_top_bits(ctx, wide, p, bigidx, n, ctx->d_topbits));
+    }
     return finish_bins(ctx);
 }
 
@@ -1916,10 +2012,12 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
                         ctx->d_poff, ctx->d_pchunk, ctx->d_pdep, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,
                         ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi, ctx->d_side,
                         ctx->d_upstage, ctx->d_Fmc, ctx->d_wmc, ctx->d_qmc, ctx->d_yr,
-                        ctx->d_gmax_part, ctx->d_gmax, ctx->d_stab};
+                        ctx->d_gmax_part, ctx->d_gmax, ctx->d_stab, ctx->d_leafw, ctx->d_nanf, ctx->d_bigidx,
+                        ctx->d_bigfeat, ctx->d_topoff, ctx->d_toprows, ctx->d_topbits, ctx->d_toppairs,
+                        ctx->d_pbigidx, ctx->d_ptopbits};
     for (int32_t *q : ctx->d_perm) if (q) cudaFree(q);
     for (void *p : dev_ptrs) if (p) cudaFree(p);
-    void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_mono};
+    void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_mono, ctx->h_nanf};
     for (void *p : host_ptrs) if (p) cudaFreeHost(p);
     for (auto &s : ctx->slot) {
         if (s.d_tg) cudaFree(s.d_tg);
@@ -2002,7 +2100,8 @@ int gbm_upload_binned_rows(gbm_ctx *ctx, int64_t row_lo, int64_t row_hi, const d
     if (row_lo < 0 || row_hi > n || row_hi <= row_lo) return fail(ctx, GBM_ERR_ARG, "bad row range");
     TRY(begin_bins(ctx, row_hi - row_lo, p, counts));
     std::string err;
-    if (gbmbin::bin_blocks(ctx->bw, ctx->st, row_lo, row_hi, edges, stride, counts, nan_bin, ctx->d_xb, err))
+    if (gbmbin::bin_blocks(ctx->bw, ctx->st, row_lo, row_hi, edges, stride, counts, nan_bin, ctx->d_xb,
+                           ctx->d_bigidx, ctx->d_topbits, err))
         return bin_fail(ctx, err);
     TRY(finish_bins(ctx));
     gbmbin::release(ctx->bw);   // the keys and sort buffers are not needed after the upload
@@ -2016,7 +2115,8 @@ int gbm_bin_features(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t 
     CK(cudaSetDevice(ctx->dev));
     TRY(ensure_uploads(ctx));
     std::string err;
-    if (gbmbin::bin_rows(ctx->bw, ctx->stager, ctx->st, X, n, p, dtype, edges, stride, counts, nan_bin, 1, out, err))
+    if (gbmbin::bin_rows(ctx->bw, ctx->stager, ctx->st, X, n, p, dtype, edges, stride, counts, nan_bin, 1, out,
+                         nullptr, nullptr, err))
         return bin_fail(ctx, err);
     return sync_stream(ctx);
 }
@@ -2274,7 +2374,7 @@ int gbm_round_reg(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_i
     TRY(launch(ctx, k_update_reg, dim3(ctx->upd_blocks), dim3(kUpdThreads), 0, ctx->st, (const TreeDev *)ctx->d_tree,
                (const uint8_t *)ctx->d_xb, ctx->n, P->learning_rate, ctx->d_F, (const double *)ctx->d_yr,
                ctx->reg_mae, out->leaf_of_row ? ctx->d_leaf : (int32_t *)nullptr, ctx->d_loss_part,
-               ctx->d_gmax_part));
+               ctx->d_gmax_part, (const int32_t *)ctx->d_bigidx, (const uint32_t *)ctx->d_topbits));
     TRY(launch(ctx, k_sum_partials, dim3(1), dim3(256), 0, ctx->st, ctx->d_loss_part, ctx->upd_blocks, ctx->d_loss));
     TRY(launch(ctx, k_max_partials, dim3(1), dim3(32), 0, ctx->st, (const double *)ctx->d_gmax_part,
                ctx->upd_blocks, ctx->d_gmax));
@@ -2381,7 +2481,8 @@ int gbm_round_mc(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_id
             rc = launch(ctx, k_update_class, dim3(ctx->upd_blocks), dim3(kUpdThreads), 0, ctx->st,
                         (const TreeDev *)ctx->d_tree, (const uint8_t *)ctx->d_xb, ctx->n, P->learning_rate,
                         ctx->d_Fmc + (int64_t)k * ctx->n,
-                        outs[k].leaf_of_row ? ctx->d_leaf : (int32_t *)nullptr);
+                        outs[k].leaf_of_row ? ctx->d_leaf : (int32_t *)nullptr, (const int32_t *)ctx->d_bigidx,
+                        (const uint32_t *)ctx->d_topbits);
         if (rc == GBM_OK && outs[k].leaf_of_row &&
             (cudaMemcpyAsync(outs[k].leaf_of_row, ctx->d_leaf, sizeof(int32_t) * ctx->n, cudaMemcpyDeviceToHost,
                              ctx->st) != cudaSuccess || cudaStreamSynchronize(ctx->st) != cudaSuccess))
@@ -2646,7 +2747,21 @@ static int predict_alloc(gbm_ctx *ctx, int64_t n, int32_t p) {
     TRY(ensure_uploads(ctx));
     ctx->pn = n;
     ctx->pp = p;
+    ctx->p_top = false;
     return GBM_OK;
+}
+
+// The predict rows' top-bit state for the features flagged in bigidx [p]
+// (-1: not a 257-bin feature): zeroed bits, ready for the binning to set.
+static int predict_top_alloc(gbm_ctx *ctx, const std::vector<int32_t> &bigidx, int nbig) {
+    ctx->p_top = nbig > 0;
+    if (!nbig) return GBM_OK;
+    const size_t words = (size_t)nbig * (size_t)((ctx->pn + 31) >> 5);
+    TRY(dalloc(ctx, &ctx->d_pbigidx, (size_t)ctx->pp));
+    TRY(dalloc(ctx, &ctx->d_ptopbits, words));
+    CK(cudaMemcpyAsync(ctx->d_pbigidx, bigidx.data(), sizeof(int32_t) * ctx->pp, cudaMemcpyHostToDevice, ctx->st));
+    CK(cudaMemsetAsync(ctx->d_ptopbits, 0, sizeof(uint32_t) * words, ctx->st));
+    return sync_stream(ctx);   // bigidx is host memory of the caller's frame
 }
 
 int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p) {
@@ -2660,13 +2775,38 @@ int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p) 
     return GBM_OK;
 }
 
+int gbm_predict_upload_u16(gbm_ctx *ctx, const uint16_t *xbin, int64_t n, int32_t p) {
+    if (!ctx || !xbin || n <= 0 || p <= 0) return GBM_ERR_ARG;
+    TRY(predict_alloc(ctx, n, p));
+    uint8_t *px = ctx->d_px;
+    auto dst = [px, p](int64_t r0, int64_t) { return static_cast<void *>(px + r0 * p); };
+    std::string err;
+    std::vector<int64_t> wide;   // ids above 255, read as bin 256
+    if (gbmh2d::stream_rows(ctx->stager, ctx->st, xbin, n, 2 * (size_t)p, gbmh2d::Pack::U16toU8, 0, dst, nullptr,
+                            err, &wide))
+        return fail(ctx, GBM_ERR_CUDA, "predict upload: %s", err.c_str());
+    if (wide.empty()) return sync_stream(ctx);
+    std::vector<int32_t> bigidx((size_t)p, -1);
+    int nbig = 0;
+    for (int64_t e : wide)
+        if (bigidx[(size_t)(e % p)] < 0) bigidx[(size_t)(e % p)] = nbig++;
+    TRY(sync_stream(ctx));
+    TRY(predict_top_alloc(ctx, bigidx, nbig));
+    return set_top_bits(ctx, wide, p, bigidx, n, ctx->d_ptopbits);
+}
+
 int gbm_predict_upload_raw(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t dtype, const double *edges,
                            int32_t stride, const int32_t *counts, const int32_t *nan_bin) {
     if (!ctx || !X || !edges || !counts || !nan_bin || n <= 0 || p <= 0) return GBM_ERR_ARG;
     TRY(predict_alloc(ctx, n, p));
+    std::vector<int32_t> bigidx((size_t)p, -1);
+    int nbig = 0;
+    for (int j = 0; j < p; j++)
+        if (counts[j] > kBins) bigidx[(size_t)j] = nbig++;
+    TRY(predict_top_alloc(ctx, bigidx, nbig));
     std::string err;
     if (gbmbin::bin_rows(ctx->bw, ctx->stager, ctx->st, X, n, p, dtype, edges, stride, counts, nan_bin, 0,
-                         ctx->d_px, err))
+                         ctx->d_px, nbig ? ctx->d_pbigidx : nullptr, nbig ? ctx->d_ptopbits : nullptr, err))
         return bin_fail(ctx, err);
     return GBM_OK;
 }
@@ -2687,7 +2827,8 @@ int gbm_predict_run(gbm_ctx *ctx, double lr, double base) {
     CK(launch_predict(ctx->d_px, ctx->pn, ctx->pp, ctx->d_pnodes, ctx->p_packed, ctx->d_pvals, ctx->d_poff,
                       ctx->d_pdep, ctx->p_ntree, ctx->d_pchunk,
                       reinterpret_cast<const int32_t *>(ctx->d_pchunk + ctx->p_ntree + 1), lr, base, ctx->d_pF,
-                      ctx->d_pP, ctx->st));
+                      ctx->d_pP, ctx->p_top ? ctx->d_pbigidx : nullptr, ctx->p_top ? ctx->d_ptopbits : nullptr,
+                      ctx->st));
     ctx->launches++;
     return GBM_OK;
 }
@@ -2933,7 +3074,7 @@ int gbm_predict_noalloc(const uint8_t *xbin_dev, int64_t n, int32_t p, const int
     // can make this one's output wrong but cannot send it outside the arrays
     if (e == cudaSuccess)
         e = launch_predict(xbin_dev, n, p, sc->nodes, false, values_dev, offsets_dev, nullptr, n_trees, sc->chunks,
-                           &sc->nchunk, learning_rate, base_score, F_dev, proba_dev, st);
+                           &sc->nchunk, learning_rate, base_score, F_dev, proba_dev, nullptr, nullptr, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return noalloc_fail(errbuf, errlen, GBM_ERR_CUDA, cudaGetErrorString(e));
     return GBM_OK;

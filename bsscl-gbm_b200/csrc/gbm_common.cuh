@@ -27,8 +27,27 @@ constexpr int kCompTile = 4096;     // rows per in-bag compaction CTA
 
 typedef __int128 i128;
 
+// A histogram slot: [nf][256] cells of kWords, the node's kTotWords total
+// words, then one more cell per feature position -- the top cell, the sum
+// over the rows whose bin id is 256 (features with 257 bins: stored as 255,
+// see top_cell_offset).
 __host__ __device__ __forceinline__ int64_t slot_words_for(int nf) {
-    return (int64_t)nf * kBins * kWords + kTotWords;
+    return (int64_t)nf * kBins * kWords + kTotWords + (int64_t)nf * kWords;
+}
+
+// Word offset of feature position jj's top cell in a slot.  A feature with
+// 257 bins (ids 0..256: n_bins 256, E:2111-2127) is stored with ids
+// min(id, 255), so its cell 255 holds bins 255 and 256 together, and this
+// cell holds bin 256 alone (the rows equal to the column maximum); every
+// threshold 0..255 of the reference's scan is then exact.
+__host__ __device__ __forceinline__ int64_t top_cell_offset(int nf, int jj) {
+    return (int64_t)nf * kBins * kWords + kTotWords + (int64_t)jj * kWords;
+}
+
+// Row r's bit of a top-bin matrix (bits [big feature][ceil(n / 32)] words):
+// 1 when its bin id is 256.
+__device__ __forceinline__ bool top_bit(const uint32_t *__restrict__ bits, int64_t words_per, int big, int64_t r) {
+    return big >= 0 && bits && ((__ldg(bits + (int64_t)big * words_per + (r >> 5)) >> (r & 31)) & 1u);
 }
 
 // ---------------------------------------------------------------------------
@@ -112,7 +131,8 @@ struct RParams {            // growth parameters the replay needs
 struct PNode {              // predict: 8 bytes per node
     int16_t feat;           // -1 = leaf
     uint8_t thr;
-    uint8_t nanr;           // 1: the NaN bin (bin 0) goes right
+    uint8_t nanr;           // bit 0: the NaN bin (bin 0) goes right; bit 1: the threshold is above
+                            // 255 (stored 255), so bin 256 of a 257-bin feature goes left too
     int16_t left, right;    // tree-local ids
 };
 

@@ -34,7 +34,7 @@ __global__ void k_pack_bins(const T *__restrict__ src, int64_t rows, int p, int6
         uint8_t x = 0;
         if (f < p) {
             int c = src[r * p + f];
-            int lim = counts[f] - 1;
+            int lim = min(counts[f] - 1, 255);   // a 257-bin feature's id 256 is kept in its top bits
             x = (uint8_t)(c > lim ? lim : c);
         }
         v[k] = x;
@@ -83,7 +83,8 @@ __global__ void __launch_bounds__(kUpdThreads)
 k_update(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64_t n,
          const uint8_t *__restrict__ y, double w0, double w1, double lr, double scale,
          double *__restrict__ F, longlong2 *__restrict__ q, int32_t *__restrict__ leaf_out,
-         double *__restrict__ loss_part, unsigned *__restrict__ done, double *__restrict__ loss_out) {
+         double *__restrict__ loss_part, unsigned *__restrict__ done, double *__restrict__ loss_out,
+         const int32_t *__restrict__ bigidx, const uint32_t *__restrict__ topbits) {
     griddep_wait();
     __shared__ int s_feat[256], s_thr[256], s_left[256], s_right[256];
     __shared__ double s_val[256];
@@ -104,7 +105,10 @@ k_update(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64
         int node = 0;
         while (s_feat[node] >= 0) {
             int b = bin_of(xb, n, i, s_feat[node]);
-            node = goes_left(b, s_thr[node] & 0xffff, s_thr[node] >> 16) ? s_left[node] : s_right[node];
+            const int th = s_thr[node] & 0xffff;
+            node = goes_left(b, th, s_thr[node] >> 16) &&
+                           !(th >= 255 && top_bit(topbits, (n + 31) >> 5, bigidx[s_feat[node]], i))
+                       ? s_left[node] : s_right[node];
         }
         if (leaf_out) leaf_out[i] = node;
         double f = __dadd_rn(F[i], __dmul_rn(lr, s_val[node]));
@@ -216,7 +220,8 @@ k_softmax_grad(const double *__restrict__ F, const uint8_t *__restrict__ y, int6
 // of the next round come from k_softmax_grad once all K trees are in.
 __global__ void __launch_bounds__(kUpdThreads)
 k_update_class(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64_t n, double lr,
-               double *__restrict__ F, int32_t *__restrict__ leaf_out) {
+               double *__restrict__ F, int32_t *__restrict__ leaf_out, const int32_t *__restrict__ bigidx,
+               const uint32_t *__restrict__ topbits) {
     griddep_wait();
     __shared__ int s_feat[256], s_thr[256], s_left[256], s_right[256];
     __shared__ double s_val[256];
@@ -235,7 +240,10 @@ k_update_class(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb,
         int node = 0;
         while (s_feat[node] >= 0) {
             const int b = bin_of(xb, n, i, s_feat[node]);
-            node = goes_left(b, s_thr[node] & 0xffff, s_thr[node] >> 16) ? s_left[node] : s_right[node];
+            const int th = s_thr[node] & 0xffff;
+            node = goes_left(b, th, s_thr[node] >> 16) &&
+                           !(th >= 255 && top_bit(topbits, (n + 31) >> 5, bigidx[s_feat[node]], i))
+                       ? s_left[node] : s_right[node];
         }
         if (leaf_out) leaf_out[i] = node;
         F[i] = __dadd_rn(F[i], __dmul_rn(lr, s_val[node]));
@@ -272,7 +280,8 @@ __global__ void k_reg_quant(const double *__restrict__ F, const double *__restri
 __global__ void __launch_bounds__(kUpdThreads)
 k_update_reg(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, int64_t n, double lr,
              double *__restrict__ F, const double *__restrict__ y, int mae, int32_t *__restrict__ leaf_out,
-             double *__restrict__ loss_part, double *__restrict__ gmax_part) {
+             double *__restrict__ loss_part, double *__restrict__ gmax_part, const int32_t *__restrict__ bigidx,
+             const uint32_t *__restrict__ topbits) {
     griddep_wait();
     __shared__ int s_feat[256], s_thr[256], s_left[256], s_right[256];
     __shared__ double s_val[256];
@@ -293,7 +302,10 @@ k_update_reg(const TreeDev *__restrict__ tree, const uint8_t *__restrict__ xb, i
         int node = 0;
         while (s_feat[node] >= 0) {
             const int b = bin_of(xb, n, i, s_feat[node]);
-            node = goes_left(b, s_thr[node] & 0xffff, s_thr[node] >> 16) ? s_left[node] : s_right[node];
+            const int th = s_thr[node] & 0xffff;
+            node = goes_left(b, th, s_thr[node] >> 16) &&
+                           !(th >= 255 && top_bit(topbits, (n + 31) >> 5, bigidx[s_feat[node]], i))
+                       ? s_left[node] : s_right[node];
         }
         if (leaf_out) leaf_out[i] = node;
         const double f = __dadd_rn(F[i], __dmul_rn(lr, s_val[node]));
@@ -492,6 +504,92 @@ __global__ void k_iota(int32_t *__restrict__ a, int64_t n) {
     if (i < n) a[i] = (int32_t)i;
 }
 
+
+// ===========================================================================
+// the top bin of 257-bin features
+// ===========================================================================
+
+// Top bits from a list of (row, big feature index) pairs (the uint16 upload,
+// whose ids the host narrows to uint8).
+__global__ void k_set_topbits(const int64_t *__restrict__ pairs, int64_t m, int64_t words_per,
+                              uint32_t *__restrict__ bits) {
+    griddep_wait();
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m) return;
+    const int64_t r = pairs[2 * i], b = pairs[2 * i + 1];
+    atomicOr(bits + b * words_per + (r >> 5), 1u << (r & 31));
+}
+
+// Rows with a top bit, per big feature (one CTA each), in ascending order:
+// cnt[b] first (count pass), then rows[off[b] ..] (fill pass).
+template <bool FILL>
+__global__ void __launch_bounds__(256) k_top_list(const uint32_t *__restrict__ bits, int64_t words_per, int64_t n,
+                                                  int32_t *__restrict__ cnt, const int32_t *__restrict__ off,
+                                                  int32_t *__restrict__ rows) {
+    griddep_wait();
+    __shared__ int s_w[8];
+    const int b = blockIdx.x;
+    const uint32_t *w = bits + (int64_t)b * words_per;
+    int carry = 0;
+    for (int64_t w0 = 0; w0 < words_per; w0 += 256) {
+        const int64_t wi = w0 + threadIdx.x;
+        uint32_t x = wi < words_per ? w[wi] : 0u;
+        int tot;
+        const int e = block_excl_scan(__popc(x), s_w, tot);
+        if (FILL) {
+            int o = off[b] + carry + e;
+            while (x) {
+                const int k = __ffs(x) - 1;
+                x &= x - 1;
+                const int64_t r = wi * 32 + k;
+                if (r < n) rows[o++] = (int32_t)r;
+            }
+        }
+        carry += tot;
+    }
+    if (!FILL && threadIdx.x == 0) cnt[b] = carry;
+}
+
+// The top cells of a level's histograms: one CTA per big feature b; for
+// every histogram task t of the level (when the round selected b, at
+// position jj) each row of b's top list that lies in the task's row
+// segment (ascending, so a binary search) adds its (g, h) into the task's
+// staging top cell jj, as (hi, lo) words like the cells.  Top rows are the
+// rows equal to the column maximum: few, against the segment's length.
+__global__ void __launch_bounds__(128) k_hist_top(const int32_t *__restrict__ rows0, const int32_t *__restrict__ rows1,
+                                                  const HistTask *__restrict__ tasks, const int *__restrict__ ntask_p,
+                                                  const int32_t *__restrict__ bigfeat, const int16_t *__restrict__ fpos,
+                                                  const int32_t *__restrict__ top_off,
+                                                  const int32_t *__restrict__ top_rows, int nf,
+                                                  const longlong2 *__restrict__ q, long long *__restrict__ stage_hist,
+                                                  const unsigned long long *__restrict__ par_word, int64_t par_stride) {
+    griddep_wait();
+    if (par_word) stage_hist += (int64_t)(*par_word & 1ull) * par_stride;
+    const int b = blockIdx.x;
+    const int jj = fpos[bigfeat[b]];
+    if (jj < 0) return;
+    const int ntask = *ntask_p, i0 = top_off[b], i1 = top_off[b + 1];
+    for (int t = 0; t < ntask; t++) {
+        const HistTask tk = tasks[t];
+        const int32_t *rows = tk.buf ? rows1 : rows0;
+        long long *cellp = stage_hist + (int64_t)tk.stage * slot_words_for(nf) + top_cell_offset(nf, jj);
+        for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+            const int r = top_rows[i];
+            long long lo = tk.begin, hi = tk.end;   // the first position with rows[pos] >= r
+            while (lo < hi) {
+                const long long mid = (lo + hi) >> 1;
+                if (rows[mid] < r) lo = mid + 1; else hi = mid;
+            }
+            if (lo < tk.end && rows[lo] == r) {
+                const longlong2 qq = q[r];
+                atomicAdd((unsigned long long *)(cellp + 0), (unsigned long long)(qq.x >> 32));
+                atomicAdd((unsigned long long *)(cellp + 1), (unsigned long long)(qq.x & 0xffffffffll));
+                atomicAdd((unsigned long long *)(cellp + 2), (unsigned long long)(qq.y >> 32));
+                atomicAdd((unsigned long long *)(cellp + 3), (unsigned long long)(qq.y & 0xffffffffll));
+            }
+        }
+    }
+}
 
 // ===========================================================================
 // histograms
@@ -930,7 +1028,8 @@ __device__ __forceinline__ int find_task_by_tile(const PartTask *tasks, int ntas
 __global__ void __launch_bounds__(kPartThreads)
 k_part_count(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
              const int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
-             const int *__restrict__ tiles_total, unsigned *__restrict__ side, int32_t *__restrict__ tile_cnt) {
+             const int *__restrict__ tiles_total, unsigned *__restrict__ side, int32_t *__restrict__ tile_cnt,
+             const int32_t *__restrict__ bigidx, const uint32_t *__restrict__ topbits) {
     griddep_wait();
     __shared__ int s[kPartThreads / 32];
     const int tile = blockIdx.x;
@@ -951,7 +1050,9 @@ k_part_count(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restric
     unsigned *sw = side + (int64_t)tile * kPartWords;
 #pragma unroll
     for (int j = 0; j < J; j++) {
-        const bool left = rw[j] >= 0 && goes_left(bin_of(xb, n, rw[j], tk.feat), tk.thr, tk.nan_right);
+        // threshold 255 of a 257-bin feature: the rows of bin 256 (stored as 255) go right
+        const bool left = rw[j] >= 0 && goes_left(bin_of(xb, n, rw[j], tk.feat), tk.thr, tk.nan_right) &&
+                          !(tk.thr >= 255 && top_bit(topbits, (n + 31) >> 5, bigidx[tk.feat], rw[j]));
         const unsigned word = __ballot_sync(0xffffffffu, left);
         if ((threadIdx.x & 31) == 0) sw[(threadIdx.x >> 5) + j * (kPartThreads / 32)] = word;
         cnt += __popc(word);
@@ -1161,13 +1262,16 @@ __global__ void k_stage_left(const DNode *__restrict__ nodes, const int *__restr
     const int k = blockIdx.y;
     const int64_t words = slot_words_for(nf);
     const int64_t data = (int64_t)nf * kBins * kWords + 4;   // cells and totals
+    const int64_t tops = (int64_t)nf * kWords;              // then the top cells
+    // word i of the converted range: the cells and totals, then the top cells
+    auto word = [&](int64_t i) { return i < data ? i : top_cell_offset(nf, 0) + (i - data); };
     const bool active = lvl ? k < *lvl_count : k == 0;
     if (active) {
         long long *st = stage + (int64_t)k * words;
         if (!lvl) {
-            for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < data;
+            for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < data + tops;
                  i += (int64_t)gridDim.x * blockDim.x)
-                lpool[i] = st[i];
+                lpool[word(i)] = st[word(i)];
         } else {
             const int parent = lvl[k];
             const DNode &p = nodes[parent];
@@ -1175,8 +1279,9 @@ __global__ void k_stage_left(const DNode *__restrict__ nodes, const int *__restr
             const bool keep = nodes[p.kid0].depth < pool_depth;
             const long long *par = lpool + (int64_t)parent * words;
             long long *lk = lpool + (int64_t)p.kid0 * words, *rk = lpool + (int64_t)p.kid1 * words;
-            for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < data;
-                 i += (int64_t)gridDim.x * blockDim.x) {
+            for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < data + tops;
+                 i0 += (int64_t)gridDim.x * blockDim.x) {
+                const int64_t i = word(i0);
                 const long long s = st[i], pv = par[i];
                 const long long left = built_left ? s : pv - s;
                 st[i] = left;
@@ -1428,7 +1533,8 @@ __global__ void __launch_bounds__(kPartThreads)
 k_leaf_totals(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
               const int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
               const int *__restrict__ tiles_total, const longlong2 *__restrict__ q,
-              long long *__restrict__ words, long long *__restrict__ n_left) {
+              long long *__restrict__ words, long long *__restrict__ n_left, const int32_t *__restrict__ bigidx,
+              const uint32_t *__restrict__ topbits) {
     griddep_wait();
     __shared__ long long s[5][kPartThreads / 32];
     const int tile = blockIdx.x;
@@ -1450,7 +1556,8 @@ k_leaf_totals(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restri
     for (int j = 0; j < J; j++) {
         if (rw[j] < 0) continue;
         const longlong2 qq = __ldg(q + rw[j]);
-        const bool left = goes_left(bin_of(xb, n, rw[j], tk.feat), tk.thr, tk.nan_right);
+        const bool left = goes_left(bin_of(xb, n, rw[j], tk.feat), tk.thr, tk.nan_right) &&
+                          !(tk.thr >= 255 && top_bit(topbits, (n + 31) >> 5, bigidx[tk.feat], rw[j]));
         v[left ? 0 : 2] += qq.x;
         v[left ? 1 : 3] += qq.y;
         v[4] += left;
@@ -1609,6 +1716,23 @@ k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
     // the staging cell is read by this thread only: zero it for the next level's adds
     *reinterpret_cast<longlong2 *>(st + cbase) = make_longlong2(0, 0);
     *reinterpret_cast<longlong2 *>(st + cbase + 2) = make_longlong2(0, 0);
+    // the top cell (bin 256 of a 257-bin feature; zero otherwise), formed like the cells
+    const int64_t tbase = top_cell_offset(nf, jj);
+    const longlong2 ta = *reinterpret_cast<const longlong2 *>(st + tbase);
+    const longlong2 td = *reinterpret_cast<const longlong2 *>(st + tbase + 2);
+    longlong2 tca[NS], tcd[NS];
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+        if (small[s]) {
+            tca[s] = ta;
+            tcd[s] = td;
+        } else {
+            const longlong2 pa = *reinterpret_cast<const longlong2 *>(par + tbase);
+            const longlong2 pd = *reinterpret_cast<const longlong2 *>(par + tbase + 2);
+            tca[s] = make_longlong2(pa.x - ta.x, pa.y - ta.y);
+            tcd[s] = make_longlong2(pd.x - td.x, pd.y - td.y);
+        }
+    }
     DNode nd[NS];
     i128 TG[NS], TH[NS];
 #pragma unroll
@@ -1618,6 +1742,10 @@ k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
         if (nd[s].depth < pool_depth) {   // the cells; the totals always (level close)
             *reinterpret_cast<longlong2 *>(pc + cbase) = ca[s];
             *reinterpret_cast<longlong2 *>(pc + cbase + 2) = cd[s];
+            if (b == 0) {
+                *reinterpret_cast<longlong2 *>(pc + tbase) = tca[s];
+                *reinterpret_cast<longlong2 *>(pc + tbase + 2) = tcd[s];
+            }
         }
         long long t4[4];
 #pragma unroll
@@ -1637,9 +1765,22 @@ k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
         v[2 * s] = cell(ca[s].x, ca[s].y);
         v[2 * s + 1] = cell(cd[s].x, cd[s].y);
     }
-    block_scan_i128<2 * NS>(v, tot, s_w);
+    block_scan_i128<2 * NS>(v, tot, s_w);   // (its barrier: every thread has read the top cell)
+    if (b == 0) {
+        *reinterpret_cast<longlong2 *>(st + tbase) = make_longlong2(0, 0);
+        *reinterpret_cast<longlong2 *>(st + tbase + 2) = make_longlong2(0, 0);
+    }
     const int f = fidx[jj];
     const int nb = counts[f];
+    // bin 255 of a 257-bin feature holds bins 255 and 256: the left sum at
+    // threshold 255 leaves the top cell out
+    if (nb > kBins && b == kBins - 1) {
+#pragma unroll
+        for (int s = 0; s < NS; s++) {
+            v[2 * s] -= cell(tca[s].x, tca[s].y);
+            v[2 * s + 1] -= cell(tcd[s].x, tcd[s].y);
+        }
+    }
     const double sc = pow2(-S);
     // the NaN-right candidates (nan_feat given: the learned NaN direction):
     // left = bins 1..b, right = the NaN bin and bins > b
@@ -2212,7 +2353,9 @@ __device__ __forceinline__ void walk_packed(const uint32_t *__restrict__ tn, int
 // until every row is at a leaf, at most szm1 steps.
 template <int RPT, bool SROWS>
 __device__ __forceinline__ void walk_pnode(const PNode *__restrict__ tn, int szm1, int pm1,
-                                           const uint8_t *const *rowp, int *node) {
+                                           const uint8_t *const *rowp, int *node, const int64_t *rid,
+                                           const int32_t *__restrict__ bigidx, const uint32_t *__restrict__ topbits,
+                                           int64_t top_words) {
     PNode nd[RPT];
 #pragma unroll
     for (int j = 0; j < RPT; j++) nd[j] = tn[0];
@@ -2223,7 +2366,12 @@ __device__ __forceinline__ void walk_pnode(const PNode *__restrict__ tn, int szm
             if (nd[j].feat >= 0) {
                 const int f = min((int)nd[j].feat, pm1);
                 const int b = SROWS ? rowp[j][((f >> 2) << 7) | (f & 3)] : __ldg(rowp[j] + f);
-                node[j] = min((int)(goes_left(b, nd[j].thr, nd[j].nanr) ? nd[j].left : nd[j].right), szm1);
+                // threshold 255 on a 257-bin feature: a row of bin 256 (stored as 255) goes right
+                // (unless the model's threshold is above 255: nanr bit 1)
+                const bool l = goes_left(b, nd[j].thr, nd[j].nanr & 1) &&
+                               !(!(nd[j].nanr & 2) && nd[j].thr == 255 && bigidx &&
+                                 top_bit(topbits, top_words, bigidx[f], rid[j]));
+                node[j] = min((int)(l ? nd[j].left : nd[j].right), szm1);
                 nd[j] = tn[node[j]];
                 more = true;
             }
@@ -2271,7 +2419,8 @@ __global__ void __launch_bounds__(kPredThreads)
 k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const void *__restrict__ nodes_v,
           const double *__restrict__ vals, const int32_t *__restrict__ off, const int32_t *__restrict__ depth_g,
           int ntree, const int4 *__restrict__ chunks, const int32_t *__restrict__ nchunk_p, int rpc, double lr,
-          double base, double *__restrict__ F, double *__restrict__ proba) {
+          double base, double *__restrict__ F, double *__restrict__ proba, const int32_t *__restrict__ bigidx,
+          const uint32_t *__restrict__ topbits) {
     extern __shared__ __align__(16) unsigned char psm[];
     constexpr int kNodeBytes = PredBuf<PACKED>::kNodeBytes;
     constexpr size_t kBuf = PredBuf<PACKED>::kBytes;
@@ -2333,7 +2482,9 @@ k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const void *__restri
     }
     double acc[RPT];
     const uint8_t *rowp[RPT];   // the tile's byte base of the row (SROWS), else the row in global memory
+    int64_t rid[RPT];           // the row's index (its top bits)
     bool live[RPT];
+    const int64_t top_words = (n + 31) >> 5;
 #pragma unroll
     for (int j = 0; j < RPT; j++) {
         const int r = threadIdx.x + j * kPredThreads;
@@ -2341,6 +2492,7 @@ k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const void *__restri
         live[j] = r < nr;
         const int rr = live[j] ? r : 0;   // a thread past the tile walks row 0 and writes nothing
         rowp[j] = SROWS ? s_rows + 4 * ((rr >> 5) * P4 * 32 + (rr & 31)) : xr + (r0 + rr) * p;
+        rid[j] = r0 + rr;
     }
     const int pm1 = p - 1;
     for (int c = 0; c < nch; c++) {
@@ -2368,7 +2520,8 @@ k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const void *__restri
                     walk_packed<RPT, SROWS>(reinterpret_cast<const uint32_t *>(s_nd) + ob, min(s_dep[t - t0], sz - 1),
                                             sz - 1, pm1, rowp, node);
                 else
-                    walk_pnode<RPT, SROWS>(reinterpret_cast<const PNode *>(s_nd) + ob, sz - 1, pm1, rowp, node);
+                    walk_pnode<RPT, SROWS>(reinterpret_cast<const PNode *>(s_nd) + ob, sz - 1, pm1, rowp, node, rid,
+                                           bigidx, topbits, top_words);
 #pragma unroll
                 for (int j = 0; j < RPT; j++) v[j] = s_val[ob + node[j]];
             } else {
@@ -2378,7 +2531,8 @@ k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const void *__restri
                     walk_packed<RPT, SROWS>(reinterpret_cast<const uint32_t *>(nodes_v) + ob,
                                             min(__ldg(depth_g + t), sz - 1), sz - 1, pm1, rowp, node);
                 else
-                    walk_pnode<RPT, SROWS>(reinterpret_cast<const PNode *>(nodes_v) + ob, sz - 1, pm1, rowp, node);
+                    walk_pnode<RPT, SROWS>(reinterpret_cast<const PNode *>(nodes_v) + ob, sz - 1, pm1, rowp, node, rid,
+                                           bigidx, topbits, top_words);
 #pragma unroll
                 for (int j = 0; j < RPT; j++) v[j] = __ldg(vals + ob + node[j]);
             }

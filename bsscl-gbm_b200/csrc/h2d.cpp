@@ -15,7 +15,10 @@ namespace {
 constexpr int kBufs = 3;                  // pinned buffers in the ring
 constexpr size_t kChunk = 32u << 20;      // bytes per pinned buffer
 
-void pack_range(const uint8_t *src, uint8_t *dst, size_t nsrc, Pack pk) {
+// Narrowing also records, in `wide`, the element index (first_elem + i)
+// of every value above 255 (rare: the top bin of 257-bin features).
+void pack_range(const uint8_t *src, uint8_t *dst, size_t nsrc, Pack pk, int64_t first_elem,
+                std::vector<int64_t> *wide) {
     if (pk == Pack::Copy) {
         std::memcpy(dst, src, nsrc);
         return;
@@ -24,7 +27,12 @@ void pack_range(const uint8_t *src, uint8_t *dst, size_t nsrc, Pack pk) {
     const size_t m = nsrc / 2;
     for (size_t i = 0; i < m; i++) {
         const uint16_t v = s[i];
-        dst[i] = (uint8_t)(v > 255 ? 255 : v);
+        if (v > 255) {
+            if (wide) wide->push_back(first_elem + (int64_t)i);
+            dst[i] = 255;
+        } else {
+            dst[i] = (uint8_t)v;
+        }
     }
 }
 
@@ -48,13 +56,23 @@ struct Stager {
     uint8_t *jdst = nullptr;
     size_t jn = 0;
     Pack jpk = Pack::Copy;
+    int64_t jelem = 0;                        // element index of jsrc in the whole matrix
+    std::vector<int64_t> *jwide = nullptr;    // narrowed values above 255 (element indices)
+    mutable std::mutex wmu;
 
     void part(int k) const {
         // parts start on 64-byte source boundaries (whole uint16 values)
         const size_t per = ((jn / (size_t)parts) + 63) & ~(size_t)63;
         const size_t a = std::min(jn, per * (size_t)k), b = std::min(jn, per * (size_t)(k + 1));
         const size_t div = jpk == Pack::U16toU8 ? 2 : 1;
-        if (b > a) pack_range(jsrc + a, jdst + a / div, b - a, jpk);
+        if (b > a) {
+            std::vector<int64_t> local;
+            pack_range(jsrc + a, jdst + a / div, b - a, jpk, jelem + (int64_t)(a / 2), jwide ? &local : nullptr);
+            if (!local.empty()) {
+                std::lock_guard<std::mutex> lk(wmu);
+                jwide->insert(jwide->end(), local.begin(), local.end());
+            }
+        }
     }
 
     void worker(int k) {
@@ -74,11 +92,13 @@ struct Stager {
         }
     }
 
-    void run(const uint8_t *src, uint8_t *dst, size_t n, Pack pk) {
+    void run(const uint8_t *src, uint8_t *dst, size_t n, Pack pk, int64_t elem0, std::vector<int64_t> *wide) {
         jsrc = src;
         jdst = dst;
         jn = n;
         jpk = pk;
+        jelem = elem0;
+        jwide = wide;
         if (parts == 1 || n < (1u << 20)) {
             const int saved = parts;
             parts = 1;
@@ -128,7 +148,8 @@ size_t chunk_bytes() { return kChunk; }
 
 int stream_rows(Stager *s, cudaStream_t st, const void *src, int64_t rows, size_t row_bytes, Pack pack,
                 int64_t max_chunk_rows, const std::function<void *(int64_t, int64_t)> &dst,
-                const std::function<int(int64_t, int64_t, const void *)> &after, std::string &err) {
+                const std::function<int(int64_t, int64_t, const void *)> &after, std::string &err,
+                std::vector<int64_t> *wide) {
     if (rows <= 0) return 0;
     const size_t out_row = pack == Pack::U16toU8 ? row_bytes / 2 : row_bytes;
     if (out_row == 0 || out_row > kChunk) {
@@ -160,7 +181,8 @@ int stream_rows(Stager *s, cudaStream_t st, const void *src, int64_t rows, size_
                 return -1;
             }
         }
-        s->run(base + (size_t)r0 * row_bytes, s->pin[k], (size_t)nr * row_bytes, pack);
+        s->run(base + (size_t)r0 * row_bytes, s->pin[k], (size_t)nr * row_bytes, pack,
+               (int64_t)((size_t)r0 * row_bytes / 2), pack == Pack::U16toU8 ? wide : nullptr);
         void *d = dst(r0, nr);
         cudaError_t e = cudaMemcpyAsync(d, s->pin[k], (size_t)nr * out_row, cudaMemcpyHostToDevice, st);
         if (e == cudaSuccess) e = cudaEventRecord(s->ev[k], st);

@@ -15,12 +15,13 @@
 #include <cstdint>
 #include <functional>
 #include <string>
+#include <vector>
 
 namespace gbmh2d {
 
 enum class Pack {
     Copy,      // rows are copied as they are
-    U16toU8,   // uint16 -> uint8 as min(v, 255)
+    U16toU8,   // uint16 -> uint8 as min(v, 255); values above 255 are listed in `wide`
 };
 
 struct Stager;
@@ -36,9 +37,12 @@ void stager_destroy(Stager *s);
 // to the size of a device staging buffer.  Returns 0, or -1 with `err` set.
 // When it returns 0 all host reads of `src` are complete; device work may
 // still be in flight on `st`.
+// With U16toU8 and `wide` given, the element index (row * p + feature of
+// the uint16 matrix) of every value above 255 is appended to *wide.
 int stream_rows(Stager *s, cudaStream_t st, const void *src, int64_t rows, size_t row_bytes, Pack pack,
                 int64_t max_chunk_rows, const std::function<void *(int64_t r0, int64_t nr)> &dst,
-                const std::function<int(int64_t r0, int64_t nr, const void *dev)> &after, std::string &err);
+                const std::function<int(int64_t r0, int64_t nr, const void *dev)> &after, std::string &err,
+                std::vector<int64_t> *wide = nullptr);
 
 // Bytes a chunk may hold (the pinned buffer size).
 size_t chunk_bytes();

@@ -132,13 +132,17 @@ int gbm_nccl_unique_id(void *uid_out /* 128 bytes */);
  * uint8 [n][p]; ids >= bin_counts[j] are read as bin_counts[j]-1 (the
  * reference clamps them the same way in its histograms, E:593-594, and no
  * threshold can separate them, E:604).  Rows are stored column-blocked on
- * the device ([ceil(p/16)][n][16] bytes). */
+ * the device ([ceil(p/16)][n][16] bytes).  bin_counts[j] is 1..257: n_bins
+ * 256 (the reference's default, 'auto') gives a feature with NaN up to 257
+ * bins (E:2111-2127); such a feature keeps min(id, 255) in its byte and the
+ * rows of id 256 as a bit per row (uint8 input cannot hold id 256). */
 int gbm_upload_bins(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p,
                     const int32_t *bin_counts);
 
 /* The same from the reference's own uint16 bin matrix (bin_features'
- * output dtype, E:2144-2190): the ids are clamped and narrowed to uint8 on
- * the device, so the caller needs no host-side conversion pass. */
+ * output dtype, E:2144-2190): the ids are narrowed to uint8 while they are
+ * staged and clamped on the device, so the caller needs no conversion
+ * pass; the ids of 256 of a 257-bin feature become its row bits. */
 int gbm_upload_bins_u16(gbm_ctx *ctx, const uint16_t *xbin, int64_t n, int32_t p,
                         const int32_t *bin_counts);
 
@@ -164,7 +168,7 @@ int gbm_bin_edges(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t dty
 /* The training matrix from rows [row_lo, row_hi) of the matrix last given to
  * gbm_bin_edges, binned on the GPU with the given edges (_bin_features,
  * E:2144-2189) and stored like gbm_upload_bins stores its rows (bin counts
- * <= 256).  Replaces the host binning + gbm_upload_bins of a raw matrix;
+ * <= 257).  Replaces the host binning + gbm_upload_bins of a raw matrix;
  * frees the matrix kept by gbm_bin_edges. */
 int gbm_upload_binned_rows(gbm_ctx *ctx, int64_t row_lo, int64_t row_hi, const double *edges,
                            int32_t stride, const int32_t *counts, const int32_t *nan_bin);
@@ -303,6 +307,10 @@ int gbm_predict_set_model(gbm_ctx *ctx, const gbm_packed *model, int32_t n_featu
  * errbuf (optional, errlen bytes). */
 int gbm_check_model(const gbm_packed *model, int32_t n_features, char *errbuf, int32_t errlen);
 int gbm_predict_upload(gbm_ctx *ctx, const uint8_t *xbin, int64_t n, int32_t p);
+/* The predict rows as the reference's uint16 bin ids (E:2144-2190): ids
+ * above 255 are read as bin 256 (the top bin of a 257-bin feature; a
+ * threshold of 255 sends it right, one above 255 left). */
+int gbm_predict_upload_u16(gbm_ctx *ctx, const uint16_t *xbin, int64_t n, int32_t p);
 int gbm_predict_run(gbm_ctx *ctx, double learning_rate, double base_score);
 int gbm_predict_fetch(gbm_ctx *ctx, double *F_out, double *proba_out);
 

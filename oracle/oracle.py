@@ -204,6 +204,18 @@ def grad_hess(F, y01, w2):
     return g, h
 
 
+def grad_hess_numpy(F, y01, w2):
+    """The reference's binary gradients in NumPy's own arithmetic
+    (E:2859-2868: p = 1 / (1 + np.exp(-clip(F, -500, 500))), g = w (p - y),
+    h = w p (1 - p)).  NumPy's vectorised exp can differ from the C
+    library's in the last bit, so MODE_REF uses this one to stay bit-exact
+    with the reference."""
+    y = np.asarray(y01).astype(np.int64)
+    sw = np.asarray(w2, np.float64)[y]
+    p = 1.0 / (1.0 + np.exp(-np.clip(np.asarray(F, np.float64), -500, 500)))
+    return sw * (p - y), sw * p * (1.0 - p)
+
+
 def logloss(F, y01):
     F = np.ascontiguousarray(F, np.float64)
     y = np.ascontiguousarray(y01, np.uint8)
@@ -262,7 +274,7 @@ def fit_binary(X_bin, y01, counts, *, n_estimators, learning_rate, max_leaves, m
     trees, losses = [], []
     y8 = y01.astype(np.uint8)
     for m in range(n_estimators):
-        g, h = grad_hess(F, y8, w2)
+        g, h = grad_hess_numpy(F, y01, w2) if mode == MODE_REF else grad_hess(F, y8, w2)
         if subsample < 1.0:
             rng.shuffle(all_r)
             sidx = all_r[:n_sub].copy()

@@ -14,6 +14,9 @@ no feature matrix is stored, the tests regenerate it):
 * ``cfg4_d8``  the same data at max_depth 8, 200 trees (configs[3] literally).
 * ``cfg2``     config 2 at its full 284,807 x 30, balanced_sqrt, 500 trees.
 * ``cfg3``     config 3 at its full 50,000 x 20, balanced_sqrt, 300 trees.
+* ``top257``   the reference's default constructor (n_bins 'auto' = 256 at
+  p = 30, so every feature has 257 bin ids) on ``datasets.top_bin``, 30
+  trees: splits at threshold 255, bin 256 alone on the right.
 
 Each file ``fit_full_<case>.npz`` holds the reference's trees, train-loss
 history, base score, bin edges / counts / NaN bins, a hash of its uint16 bin
@@ -73,6 +76,7 @@ CASES = {
                  random_state=0),
     "cfg3": dict(data="config3", n_estimators=300, max_depth=6, class_weight="balanced_sqrt", n_bins=255,
                  random_state=0),
+    "top257": dict(data="top_bin", n_estimators=30, random_state=0),
 }
 
 
@@ -82,6 +86,9 @@ def case_data(D, which):
     if which == "config4":
         X, y = D.config4(n=1_000_000)
         Xh, _ = D.config4(n=20_000, seed=13)
+    elif which == "top_bin":
+        X, y = D.top_bin()
+        Xh, _ = D.top_bin(n=5_000, seed=22)
     elif which == "config2":
         X, y = D.config2()
         Xh, _ = D.config2(n=20_000, seed=11, n_pos=40)

@@ -9,7 +9,9 @@ the same data recorded by ``tests/golden/make_golden_full.py``:
   trees -- bench.py's workload and its 5 warm-up + 200 timed rounds;
 * ``cfg4_d8``  the same data at max_depth 8, 200 trees (configs[3]);
 * ``cfg2``     config 2, 284,807 x 30, balanced_sqrt, 500 trees;
-* ``cfg3``     config 3, 50,000 x 20, balanced_sqrt, 300 trees.
+* ``cfg3``     config 3, 50,000 x 20, balanced_sqrt, 300 trees;
+* ``top257``   the reference's default constructor (n_bins 'auto' = 256, so
+  257 bin ids per feature) on 20,000 x 30 with splits at threshold 255.
 
 What must hold:
 
@@ -37,7 +39,7 @@ from helpers import golden
 
 pytestmark = pytest.mark.gpu
 
-CASES = ["cfg4_d6", "cfg4_d8", "cfg2", "cfg3"]
+CASES = ["cfg4_d6", "cfg4_d8", "cfg2", "cfg3", "top257"]
 
 
 def _trees(d, prefix=""):
@@ -50,7 +52,10 @@ def _trees(d, prefix=""):
 
 def _data(name):
     from bsscl_gbm_b200 import datasets as D
-    if name.startswith("cfg4"):
+    if name == "top257":
+        X, y = D.top_bin()
+        Xh, _ = D.top_bin(n=5_000, seed=22)
+    elif name.startswith("cfg4"):
         X, y = D.config4(n=1_000_000)
         Xh, _ = D.config4(n=20_000, seed=13)
     elif name == "cfg2":
