@@ -451,6 +451,21 @@ def run_engine(args):
     torch.cuda.synchronize()
     clk = clocks.stop()
     losses = [r[1] for r in res]
+    if args.part == "rounds":   # profiling aid: the timed rounds alone
+        st = eng.stats()
+        ms = eng.elapsed_ms(0, 1) - st["flush_ms"]
+        if rank == 0:
+            print(json.dumps({"part": "rounds", "workload": c["workload"], "rounds": args.steps,
+                              "ms_per_round": ms / args.steps, "rounds_per_s": args.steps / (ms / 1000.0),
+                              "hist_launches": st["hist_launches"], "hist_ms": st["hist_ms"],
+                              "hist_alg_bytes": st["hist_alg_bytes"], "kernel_launches": st["kernel_launches"]}),
+                  flush=True)
+        sampler.close()
+        eng.close()
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     # the timed rounds are rounds W .. W+K-1 of one fit: compare them with the
     # reference's own fit of this workload (config 4 at depth 6)
     parity = parity_check(res, args.warmup, "cfg4_d6") if not five else {
@@ -601,8 +616,8 @@ def run_engine(args):
                     "l2": "flushed at the start of every timed round (256 MB write on the "
                           "engine stream; its device time is excluded)"},
             "parity": parity,
-            "roofline": {"bound": "hbm", "kernel": "k_hist2 + k_hist (every histogram launch of the round: "
-                                                   "k_hist2 at the root and the next two levels, k_hist below)",
+            "roofline": {"bound": "hbm", "kernel": "k_hist3 (every histogram launch of the round, on the "
+                                                   "round's selected features packed into 16-feature blocks)",
                          "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak if peak else None,
@@ -690,8 +705,9 @@ def main():
     ap.add_argument("--config", default="4", choices=sorted(CONFIGS),
                     help="4 (default): the headline, 1M x 100 depth 6; 5: 10M x 200 depth 10")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--part", default="all", choices=["all", "predict"],
-                    help="predict: time only the ensemble predict (k_predict), for profiling")
+    ap.add_argument("--part", default="all", choices=["all", "predict", "rounds"],
+                    help="predict: time only the ensemble predict (k_predict); rounds: only the "
+                         "upload and the timed rounds (both for profiling)")
     ap.add_argument("--predict-rows", type=int, default=1_000_000)
     ap.add_argument("--config5-steps", type=int, default=20,
                     help="timed rounds of the configs[4] (10M x 200) sub-record")

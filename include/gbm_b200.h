@@ -350,7 +350,8 @@ int gbm_predict_raw(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t d
  * so an overlapping call can make the outputs wrong but cannot make the
  * walk loop or read outside the arrays.  The call runs on `stream` (a
  * cudaStream_t, NULL = the default stream) of the current device,
- * synchronises that stream and returns when the outputs are written.
+ * synchronises that stream and returns when the outputs are written, so
+ * it cannot be captured into a CUDA graph.
  * `errbuf` (optional, `errlen` bytes) receives a message. */
 int gbm_predict_noalloc(const uint8_t *xbin_dev, int64_t n, int32_t p, const int16_t *features_dev,
                         const int64_t *thresholds_dev, const double *values_dev, const int32_t *left_dev,
