@@ -89,9 +89,16 @@ struct gbm_ctx {
     bool have_bins = false, have_labels = false;
 
     // round buffers
+    // The round's in-bag mask, its two row-list buffers (depth parity) and
+    // its compaction scratch: aliases of one of two sets, by round parity
+    // (slot & 1), so the sampler stream builds round r + 1's root list
+    // while round r still partitions its own.
     uint8_t *d_mask = nullptr;
-    int32_t *d_rows = nullptr, *d_tmp = nullptr;   // the two row-list buffers (depth parity)
-    unsigned *d_side = nullptr;                    // partition side bits, per tile
+    int32_t *d_rows = nullptr, *d_tmp = nullptr;
+    uint8_t *d_maskP[2] = {};
+    int32_t *d_rowsP[2] = {}, *d_tmpP[2] = {}, *d_cntP[2] = {}, *d_offP[2] = {}, *d_totalP[2] = {};
+    cudaEvent_t rows_freeP[2] = {};
+    unsigned long long *d_tile_st = nullptr;       // k_partition's per-tile look-back words (zero between levels)
     int32_t *d_cnt = nullptr, *d_off = nullptr, *d_total = nullptr;
     int32_t *d_blist = nullptr, *d_fidx = nullptr;
     int16_t *d_fpos = nullptr, *d_fbi = nullptr;
@@ -128,7 +135,6 @@ struct gbm_ctx {
     HistTask *d_htask = nullptr;
     int32_t *d_hprefix = nullptr;
     PartTask *d_ptask = nullptr;
-    int32_t *d_tile_cnt = nullptr;
     int tile_cap = 0;
     long long *d_nleft = nullptr, *d_count64 = nullptr;   // d_count64: one word for small all-reduces
     long long *d_leafw = nullptr;      // last level: per-parent count and (G, H) words
@@ -176,7 +182,7 @@ struct gbm_ctx {
     Slot slot[kRing];
     bool slots_ready = false;
     cudaStream_t cst = nullptr;        // the samplers' copies, row shuffles and root row lists
-    cudaEvent_t rows_free = nullptr;   // recorded on st once a round is done with the row lists
+    cudaEvent_t rows_free = nullptr;   // recorded on st once a round is done with its row lists (alias by parity)
     int cur_slot = 0;                  // the slot whose round is being enqueued
     bool capturing = false;            // enqueueing into a graph capture
     std::string graph_key;             // what the slots' graphs were captured for
@@ -252,9 +258,12 @@ struct gbm_ctx {
 
 namespace {
 
-// d_ints: I_DONE / I_DONE_UPD count finished CTAs of k_part_scatter / k_update
+// d_ints: I_DONE / I_DONE_UPD count finished CTAs of k_partition / k_update;
+// I_TICKET hands out k_partition's tiles in order; I_PART_ERR records a
+// partition look-back wait that ran out
 // (the last one runs the tail and resets it)
-enum { I_ONE = 0, I_NODES = 1, I_TILES = 2, I_LVL0 = 3, I_LVL1 = 4, I_DONE = 5, I_DONE_UPD = 6, I_COUNT = 8 };
+enum { I_ONE = 0, I_NODES = 1, I_TILES = 2, I_LVL0 = 3, I_LVL1 = 4, I_DONE = 5, I_DONE_UPD = 6, I_TICKET = 7,
+       I_PART_ERR = 8, I_COUNT = 10 };
 
 int fail(gbm_ctx *c, int code, const char *fmt, ...) {
     char buf[512];
@@ -356,7 +365,19 @@ int collect_slot_timing(gbm_ctx *ctx, int si) {
 }
 
 // A round is about to be enqueued on slot si (outside a capture).
+// The buffer set of round parity q (see d_maskP).
+void use_parity(gbm_ctx *ctx, int q) {
+    ctx->d_mask = ctx->d_maskP[q];
+    ctx->d_rows = ctx->d_rowsP[q];
+    ctx->d_tmp = ctx->d_tmpP[q];
+    ctx->d_cnt = ctx->d_cntP[q];
+    ctx->d_off = ctx->d_offP[q];
+    ctx->d_total = ctx->d_totalP[q];
+    ctx->rows_free = ctx->rows_freeP[q];
+}
+
 void begin_round(gbm_ctx *ctx, int si) {
+    use_parity(ctx, si & 1);
     ctx->cur_slot = si;
     ctx->slot[si].tused = ctx->slot[si].tdone = 0;
 }
@@ -978,8 +999,8 @@ int ensure_round_buffers(gbm_ctx *ctx, int nf, const gbm_params *P) {
     const int tiles = (int)((ctx->n + kPartTile - 1) / kPartTile) + ctx->stage_slots;
     if (tiles > ctx->tile_cap) {
         ctx->tile_cap = tiles;
-        TRY(dalloc(ctx, &ctx->d_tile_cnt, (size_t)ctx->tile_cap));
-        TRY(dalloc(ctx, &ctx->d_side, (size_t)ctx->tile_cap * kPartWords));
+        TRY(dalloc(ctx, &ctx->d_tile_st, (size_t)ctx->tile_cap));
+        CK(cudaMemsetAsync(ctx->d_tile_st, 0, sizeof(unsigned long long) * ctx->tile_cap, ctx->st));
     }
     return GBM_OK;
 }
@@ -1173,14 +1194,13 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
         ctx->waves++;
         return GBM_OK;
     }
-    TRY(launch(ctx, k_part_count, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, ctx->d_xb, ctx->n, ctx->d_rows, ctx->d_tmp, ctx->d_ptask,
-                                                         lvl_cnt, ints(ctx, I_TILES), ctx->d_side, ctx->d_tile_cnt,
-                                                         (const int32_t *)ctx->d_bigidx, (const uint32_t *)ctx->d_topbits));
     const long long *gl = ctx->comm ? nullptr : ctx->d_nleft;   // several ranks: the locally smaller child
-    TRY(launch(ctx, k_part_scatter, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, (const int32_t *)ctx->d_rows,
-               ctx->d_tmp, (const PartTask *)ctx->d_ptask, (const int *)lvl_cnt, (const int *)ints(ctx, I_TILES),
-               (const unsigned *)ctx->d_side, (const int32_t *)ctx->d_tile_cnt, ctx->d_nleft, ctx->d_nodes,
-               (const int *)lvl, gl, ctx->d_htask, ctx->d_hprefix, (unsigned *)ints(ctx, I_DONE)));
+    TRY(launch(ctx, k_partition, dim3(tiles_ub), dim3(kPartThreads), 0, ctx->st, (const uint8_t *)ctx->d_xb, ctx->n,
+               ctx->d_rows, ctx->d_tmp, (const PartTask *)ctx->d_ptask, (const int *)lvl_cnt,
+               (const int *)ints(ctx, I_TILES), ctx->d_tile_st, (unsigned *)ints(ctx, I_TICKET),
+               ints(ctx, I_PART_ERR), ctx->d_nleft, (const int32_t *)ctx->d_bigidx,
+               (const uint32_t *)ctx->d_topbits, ctx->d_nodes, (const int *)lvl, gl, ctx->d_htask, ctx->d_hprefix,
+               (unsigned *)ints(ctx, I_DONE)));
     TRY(launch_hist(ctx, rf, lvl_cnt));
     if (ctx->comm) {
         const int cx = std::max(1, (2 * ctx->hist_grid + W_ub - 1) / W_ub);
@@ -1212,6 +1232,8 @@ int fetch_nodes(gbm_ctx *ctx) {
                            sizeof(unsigned long long), cudaMemcpyDeviceToHost, ctx->st));
     TRY(sync_stream(ctx));
     TRY(p2p_check(ctx, ctx->cur_slot));
+    if (ctx->h_ints[I_PART_ERR])
+        return fail(ctx, GBM_ERR_STATE, "internal: a partition tile's wait for its predecessors ran out");
     if (ctx->profiling) TRY(collect_slot_timing(ctx, ctx->cur_slot));
     return GBM_OK;
 }
@@ -1421,20 +1443,23 @@ void enforce_monotone(HostTree &T, const int32_t *mono) {   // E:2461-2499
 
 
 int alloc_round_fixed(gbm_ctx *ctx) {
-    TRY(dalloc(ctx, &ctx->d_mask, (size_t)ctx->n));
-    TRY(dalloc(ctx, &ctx->d_rows, (size_t)ctx->n));
-    TRY(dalloc(ctx, &ctx->d_tmp, (size_t)ctx->n));
     int ntile = (int)((ctx->n + kCompTile - 1) / kCompTile);
-    TRY(dalloc(ctx, &ctx->d_cnt, (size_t)ntile));
-    TRY(dalloc(ctx, &ctx->d_off, (size_t)ntile));
-    TRY(dalloc(ctx, &ctx->d_total, 1));
+    for (int q = 0; q < 2; q++) {
+        TRY(dalloc(ctx, &ctx->d_maskP[q], (size_t)ctx->n));
+        TRY(dalloc(ctx, &ctx->d_rowsP[q], (size_t)ctx->n));
+        TRY(dalloc(ctx, &ctx->d_tmpP[q], (size_t)ctx->n));
+        TRY(dalloc(ctx, &ctx->d_cntP[q], (size_t)ntile));
+        TRY(dalloc(ctx, &ctx->d_offP[q], (size_t)ntile));
+        TRY(dalloc(ctx, &ctx->d_totalP[q], 1));
+    }
+    use_parity(ctx, 0);
     TRY(dalloc(ctx, &ctx->d_count64, 1));
     TRY(dalloc(ctx, &ctx->d_blist, (size_t)ctx->nblk + 1));   // blist | nb
     TRY(dalloc(ctx, &ctx->d_fbi, (size_t)ctx->p));
     TRY(dalloc(ctx, &ctx->d_fpos, (size_t)ctx->nblk * kBlk));
     TRY(dalloc(ctx, &ctx->d_ints, (size_t)I_COUNT));
     TRY(halloc(ctx, &ctx->h_ints, (size_t)I_COUNT));
-    int init[I_COUNT] = {1, 0, 0, 0, 0, 0, 0, 0};
+    int init[I_COUNT] = {1, 0, 0, 0, 0, 0, 0, 0, 0, 0};
     CK(cudaMemcpyAsync(ctx->d_ints, init, sizeof init, cudaMemcpyHostToDevice, ctx->st));
     TRY(dalloc(ctx, &ctx->d_tree, 1));
     TRY(dalloc(ctx, &ctx->d_leaf, (size_t)ctx->n));
@@ -1502,7 +1527,8 @@ int enqueue_grow(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, bool co
                          ints(ctx, I_LVL0 + 1 - cur), me.W_ub, me.last, true, plan_of(L + 1), L + 1));
         cur = 1 - cur;
     }
-    // the row lists are free: the next round's compaction may overwrite them
+    // this parity's row lists and packed blocks are free: the round two
+    // places on may overwrite them
     TRY(record_ev(ctx, ctx->rows_free, ctx->st));
     if (ctx->p2p)   // the exchange's error word travels with the round
         CK(cudaMemcpyAsync(&ctx->slot[ctx->cur_slot].h_loss[1], ctx->d_sync + ctx->p2p_n + kSyncErr,
@@ -1554,6 +1580,7 @@ int enqueue_replay(gbm_ctx *ctx, const gbm_params *P) {
     R.max_leaves = P->max_leaves;
     R.policy = P->grow_policy;
     R.has_mono = P->monotone != nullptr;
+    R.part_err = ints(ctx, I_PART_ERR);
     size_t smem = sizeof(RNode) * (size_t)ctx->nmax;
     if (P->grow_policy == 0)
         TRY(launch(ctx, k_replay_leaf, dim3(1), dim3(kReplayLoaders), smem, ctx->st, ctx->d_nodes, ints(ctx, I_NODES), R,
@@ -1604,6 +1631,8 @@ int harvest(gbm_ctx *ctx, int si, int nf, const gbm_params *P, gbm_tree_out *out
     if (ctx->profiling) TRY(collect_slot_timing(ctx, si));
     TRY(p2p_check(ctx, si));
     const TreeOut &T = *ctx->slot[si].h_tout;
+    if (T.status == 3)
+        return fail(ctx, GBM_ERR_STATE, "internal: a partition tile's wait for its predecessors ran out");
     if (T.status != 0) return fail(ctx, GBM_ERR_STATE, "internal: the device replay reached an unexpanded node");
     ctx->alg_bytes += (double)T.alg_rows * (nf + 8);
     ctx->hist_updates += (double)T.alg_rows * ctx->slot[si].upd_per_row;
@@ -1635,6 +1664,7 @@ int prepare_round(gbm_ctx *ctx, int nf, const gbm_params *P) {
     // staging histograms start every call at zero (each use zeroes what it read)
     CK(cudaMemsetAsync(ctx->d_stage, 0, sizeof(long long) * (size_t)ctx->stage_slots * slot_words_for(ctx->nf_cap),
                        ctx->st));
+    use_parity(ctx, 0);   // the one-round calls use slot 0's buffers; begin_round picks a ring slot's
     return stage_mono(ctx, P);
 }
 
@@ -1690,10 +1720,12 @@ int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int
     gbm_ctx::Slot &s = ctx->slot[si];
     constexpr int R = gbm_ctx::kRing;
     int32_t *pout = nullptr;
-    // the round's packed feature blocks, made here while the previous round
-    // grows: buffer si & 1 was last read by the round two places back, whose
-    // histograms ended before the rows_free this stream waited for in the
-    // previous round's sample
+    // Everything this round writes here -- its packed feature blocks
+    // (d_xc[si & 1]), its mask, root row list and compaction scratch (the
+    // parity set of use_parity) -- was last used by the round two places
+    // back: wait for that round's last level, then build them while the
+    // previous round grows.
+    TRY(wait_ev(ctx, ctx->cst, ctx->rows_free));
     s.xc_on_cst = nf > 0 && compact_hist(ctx);
     if (s.xc_on_cst) {
         CK(cudaMemcpyAsync(s.d_fidx_c, s.h_feat, sizeof(int32_t) * nf, cudaMemcpyHostToDevice, ctx->cst));
@@ -1711,9 +1743,6 @@ int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int
         TRY(launch(ctx, k_shuf_compose, dim3(grid_for(N, 256)), dim3(256), 0, ctx->cst, s.d_tg, N, ctx->d_m,
                    ctx->d_mp, pin, pout));
     }
-    // mask and root row list once the previous round is done with the row
-    // lists (it is at its replay or F update by then)
-    TRY(wait_ev(ctx, ctx->cst, ctx->rows_free));
     if (dr.on) {   // throughput mode: this rank's rows from the hash of (seed, round, global row)
         CK(cudaMemcpyAsync(s.d_round, s.h_round, sizeof(long long), cudaMemcpyHostToDevice, ctx->cst));
         TRY(launch(ctx, k_mask_hash, dim3(grid_for(ctx->n, 256)), dim3(256), 0, ctx->cst, ctx->d_mask, ctx->n,
@@ -1918,6 +1947,7 @@ int capture_round(gbm_ctx *ctx, int si, int nf, const gbm_params *P, int64_t N, 
     const long long l0 = ctx->launches, h0 = ctx->hist_launches, w0 = ctx->waves;
     const double b0 = ctx->comm_bytes;
     ctx->cur_slot = si;
+    use_parity(ctx, si & 1);
     s.tused = s.tdone = 0;
     TRY(capture(ctx, ctx->cst, &s.g_cst, [&] { return enqueue_sample(ctx, si, N, m, rows_on, row_offset, nf, dr); }));
     TRY(capture(ctx, ctx->st, &s.g_st, [&] {
@@ -1966,9 +1996,16 @@ int gbm_ctx_create(int32_t device, gbm_ctx **out) {
     ctx->dev = device;
     *out = ctx;
     CK(cudaSetDevice(device));
-    CK(cudaStreamCreateWithFlags(&ctx->st, cudaStreamNonBlocking));
-    CK(cudaStreamCreateWithFlags(&ctx->cst, cudaStreamNonBlocking));
-    CK(cudaEventCreateWithFlags(&ctx->rows_free, cudaEventDisableTiming));
+    // The engine stream at the highest priority: when both streams have work
+    // pending, the round's own kernels get the SMs first and the sampler
+    // stream's (the next round's shuffle, mask and packed blocks) fill the
+    // SMs the engine leaves idle (its one-CTA replay and level close).
+    int prio_lo = 0, prio_hi = 0;
+    CK(cudaDeviceGetStreamPriorityRange(&prio_lo, &prio_hi));
+    CK(cudaStreamCreateWithPriority(&ctx->st, cudaStreamNonBlocking, prio_hi));
+    CK(cudaStreamCreateWithPriority(&ctx->cst, cudaStreamNonBlocking, prio_lo));
+    for (auto &e : ctx->rows_freeP) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    ctx->rows_free = ctx->rows_freeP[0];
     int sms = 0;
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
     ctx->sms = std::max(sms, 1);
@@ -2003,14 +2040,18 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     for (auto &s : ctx->slot)
         for (cudaEvent_t e : s.tev) cudaEventDestroy(e);
     if (ctx->comm) gbm_comm_destroy(ctx->comm);
-    void *dev_ptrs[] = {ctx->d_xb, ctx->d_xc[0], ctx->d_xc[1], ctx->d_counts, ctx->d_y, ctx->d_F, ctx->d_q, ctx->d_mask,
-                        ctx->d_rows, ctx->d_tmp, ctx->d_cnt, ctx->d_off, ctx->d_total, ctx->d_blist, ctx->d_fidx,
+    for (int q = 0; q < 2; q++) {
+        void *pq[] = {ctx->d_maskP[q], ctx->d_rowsP[q], ctx->d_tmpP[q], ctx->d_cntP[q], ctx->d_offP[q], ctx->d_totalP[q]};
+        for (void *p : pq) if (p) cudaFree(p);
+    }
+    void *dev_ptrs[] = {ctx->d_xb, ctx->d_xc[0], ctx->d_xc[1], ctx->d_counts, ctx->d_y, ctx->d_F, ctx->d_q,
+                        ctx->d_blist, ctx->d_fidx,
                         ctx->d_fpos, ctx->d_pool, ctx->d_lpool, ctx->d_stage, ctx->d_fbest, ctx->d_htask, ctx->d_hprefix,
-                        ctx->d_ptask, ctx->d_tile_cnt, ctx->d_nleft,
+                        ctx->d_ptask, ctx->d_nleft,
                         ctx->d_count64, ctx->d_nodes, ctx->d_lvl[0], ctx->d_lvl[1], ctx->d_ints, ctx->d_tree,
                         ctx->d_leaf, ctx->d_loss_part, ctx->d_loss, ctx->d_px, ctx->d_pnodes, ctx->d_pvals,
                         ctx->d_poff, ctx->d_pchunk, ctx->d_pdep, ctx->d_pF, ctx->d_pP, ctx->d_tout, ctx->d_mono, ctx->d_flush,
-                        ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi, ctx->d_side,
+                        ctx->d_head, ctx->d_nxt, ctx->d_m, ctx->d_mp, ctx->d_fbi, 
                         ctx->d_upstage, ctx->d_Fmc, ctx->d_wmc, ctx->d_qmc, ctx->d_yr,
                         ctx->d_gmax_part, ctx->d_gmax, ctx->d_stab, ctx->d_leafw, ctx->d_nanf, ctx->d_bigidx,
                         ctx->d_bigfeat, ctx->d_topoff, ctx->d_toprows, ctx->d_topbits, ctx->d_toppairs,
@@ -2032,7 +2073,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
     for (cudaEvent_t e : ctx->mark) if (e) cudaEventDestroy(e);
     if (ctx->st) cudaStreamDestroy(ctx->st);
     if (ctx->cst) cudaStreamDestroy(ctx->cst);
-    if (ctx->rows_free) cudaEventDestroy(ctx->rows_free);
+    for (auto &e : ctx->rows_freeP) if (e) cudaEventDestroy(e);
     delete ctx;
 }
 

@@ -110,7 +110,7 @@ struct TreeDev {            // a pruned tree in the reference's layout
 // replay and copied to the host.
 struct TreeOut {
     int nc;
-    int status;             // 0 ok, 1 the replay needed a node that was not expanded
+    int status;             // 0 ok, 1 the replay needed a node that was not expanded, 3 a partition wait ran out
     long long root_rows;    // this rank's in-bag rows
     long long alg_rows;     // root rows + the smaller child's rows of every split (this rank)
     int tf[256];
@@ -126,6 +126,7 @@ struct RParams {            // growth parameters the replay needs
     double lam, gamma, mcw;
     long long msl;
     int max_depth, max_leaves, policy, has_mono;
+    const int *part_err;    // set by a partition look-back wait that ran out (the tree's status 3)
 };
 
 struct PNode {              // predict: 8 bytes per node

@@ -553,8 +553,9 @@ __global__ void __launch_bounds__(256) k_top_list(const uint32_t *__restrict__ b
 // The top cells of a level's histograms: one CTA per big feature b; for
 // every histogram task t of the level (when the round selected b, at
 // position jj) each row of b's top list that lies in the task's row
-// segment (ascending, so a binary search) adds its (g, h) into the task's
-// staging top cell jj, as (hi, lo) words like the cells.  Top rows are the
+// segment (ascending or descending: k_partition keeps every node's list
+// monotonic, so a binary search) adds its (g, h) into the task's staging
+// top cell jj, as (hi, lo) words like the cells.  Top rows are the
 // rows equal to the column maximum: few, against the segment's length.
 __global__ void __launch_bounds__(128) k_hist_top(const int32_t *__restrict__ rows0, const int32_t *__restrict__ rows1,
                                                   const HistTask *__restrict__ tasks, const int *__restrict__ ntask_p,
@@ -573,12 +574,14 @@ __global__ void __launch_bounds__(128) k_hist_top(const int32_t *__restrict__ ro
         const HistTask tk = tasks[t];
         const int32_t *rows = tk.buf ? rows1 : rows0;
         long long *cellp = stage_hist + (int64_t)tk.stage * slot_words_for(nf) + top_cell_offset(nf, jj);
+        if (tk.end <= tk.begin) continue;
+        const bool asc = rows[tk.begin] <= rows[tk.end - 1];
         for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
             const int r = top_rows[i];
-            long long lo = tk.begin, hi = tk.end;   // the first position with rows[pos] >= r
+            long long lo = tk.begin, hi = tk.end;   // the first position at or past r in the list's order
             while (lo < hi) {
                 const long long mid = (lo + hi) >> 1;
-                if (rows[mid] < r) lo = mid + 1; else hi = mid;
+                if (asc ? rows[mid] < r : rows[mid] > r) lo = mid + 1; else hi = mid;
             }
             if (lo < tk.end && rows[lo] == r) {
                 const longlong2 qq = q[r];
@@ -1020,63 +1023,12 @@ __device__ __forceinline__ int find_task_by_tile(const PartTask *tasks, int ntas
     return lo;
 }
 
-// Stable partition (E:663-674 decides the same sides): a tile of kPartTile
-// rows per CTA, 8 rows per thread with their loads in flight together.
-// Count: each warp's ballots are the tile's side bits (1 = left); scan: the
-// tiles' left offsets within a task; scatter: ranks from the side bits, rows
-// into the other row buffer.
-__global__ void __launch_bounds__(kPartThreads)
-k_part_count(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
-             const int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
-             const int *__restrict__ tiles_total, unsigned *__restrict__ side, int32_t *__restrict__ tile_cnt,
-             const int32_t *__restrict__ bigidx, const uint32_t *__restrict__ topbits) {
-    griddep_wait();
-    __shared__ int s[kPartThreads / 32];
-    const int tile = blockIdx.x;
-    if (tile >= *tiles_total) return;
-    const int t = find_task_by_tile(tasks, *ntask_p, tile);
-    const PartTask tk = tasks[t];
-    const int32_t *__restrict__ rows = tk.src ? rows1 : rows0;
-    const long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
-    const int m = (int)min((long long)kPartTile, tk.end - r0);
-    constexpr int J = kPartTile / kPartThreads;
-    int rw[J];
-#pragma unroll
-    for (int j = 0; j < J; j++) {
-        const int o = threadIdx.x + j * kPartThreads;
-        rw[j] = o < m ? rows[r0 + o] : -1;
-    }
-    int cnt = 0;
-    unsigned *sw = side + (int64_t)tile * kPartWords;
-#pragma unroll
-    for (int j = 0; j < J; j++) {
-        // threshold 255 of a 257-bin feature: the rows of bin 256 (stored as 255) go right
-        const bool left = rw[j] >= 0 && goes_left(bin_of(xb, n, rw[j], tk.feat), tk.thr, tk.nan_right) &&
-                          !(tk.thr >= 255 && top_bit(topbits, (n + 31) >> 5, bigidx[tk.feat], rw[j]));
-        const unsigned word = __ballot_sync(0xffffffffu, left);
-        if ((threadIdx.x & 31) == 0) sw[(threadIdx.x >> 5) + j * (kPartThreads / 32)] = word;
-        cnt += __popc(word);
-    }
-    if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = cnt;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int tot = 0;
-        for (int w = 0; w < kPartThreads / 32; w++) tot += s[w];
-        tile_cnt[tile] = tot;
-    }
-}
-
-// Row o of a tile is bit (o & 31) of side word o >> 5; the word of rows
-// [32 i, 32 i + 32) was written by warp i % 16 of the count kernel.  Each
-// CTA first sums its task's tile counts (the lefts before it, and n_left,
-// which the task's first tile stores); each warp then ranks a run of 256
-// consecutive rows (8 words).
 // Level plan after the partition: each parent's smaller child (by global
 // count) becomes a histogram task; the children get their row ranges.
 // gl == null (several ranks): each rank histograms its locally smaller child;
 // k_stage_left turns that into the left child's partial before the all-reduce
 // and k_fill_counts sets the children's global counts after it.
-// One CTA (the last of k_part_scatter to finish) runs it.
+// One CTA (the last of k_partition to finish) runs it.
 __device__ void plan_hist_block(DNode *__restrict__ nodes, const int *__restrict__ lvl, int W,
                                 const long long *__restrict__ nl_local, const long long *__restrict__ gl,
                                 HistTask *__restrict__ ht, int32_t *__restrict__ prefix, int *s_w) {
@@ -1119,89 +1071,137 @@ __device__ void plan_hist_block(DNode *__restrict__ nodes, const int *__restrict
     if (threadIdx.x == 0) prefix[W] = carry;
 }
 
-// One partition tile's scatter (k_part_scatter).
-__device__ __forceinline__ void part_scatter_tile(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1,
-                                                  const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
-                                                  const unsigned *__restrict__ side,
-                                                  const int32_t *__restrict__ tile_cnt,
-                                                  long long *__restrict__ n_left) {
-    __shared__ int s_l[kPartThreads / 32], s_a[kPartThreads / 32], s_b[kPartThreads / 32];
-    const int tile = blockIdx.x;
-    const int t = find_task_by_tile(tasks, *ntask_p, tile);
-    const PartTask tk = tasks[t];
-    const int32_t *__restrict__ src = tk.src ? rows1 : rows0;
-    int32_t *__restrict__ dst = tk.src ? const_cast<int32_t *>(rows0) : rows1;
-    const long long tstart = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
-    const int m = (int)min((long long)kPartTile, tk.end - tstart);
-    const unsigned *sw = side + (int64_t)tile * kPartWords;
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    // lefts of the task's earlier tiles, and of all its tiles (n_left)
-    {
-        int before = 0, all = 0;
-        for (int k = threadIdx.x; k < tk.ntile; k += blockDim.x) {
-            const int v = tile_cnt[tk.tile0 + k];
-            all += v;
-            before += tk.tile0 + k < tile ? v : 0;
-        }
-        before = warp_sum(before);
-        all = warp_sum(all);
-        if (lane == 0) { s_b[w] = before; s_a[w] = all; }
-    }
-    constexpr int WPW = kPartWords / (kPartThreads / 32);   // side words per warp
-    unsigned wd[WPW];
-    int lw = 0;
-#pragma unroll
-    for (int j = 0; j < WPW; j++) {
-        wd[j] = sw[w * WPW + j];
-        lw += __popc(wd[j]);
-    }
-    if (lane == 0) s_l[w] = lw;
-    __syncthreads();
-    int lbase = 0;
-    for (int k = 0; k < w; k++) lbase += s_l[k];
-    long long nl = 0, lcar = 0;                              // lefts of the task; before this tile
-    for (int k = 0; k < kPartThreads / 32; k++) { nl += s_a[k]; lcar += s_b[k]; }
-    if (threadIdx.x == 0 && tile == tk.tile0) n_left[t] = nl;
-    const long long rcar = (tstart - tk.begin) - lcar;       // rights before this tile
-    long long lpos = tk.begin + lcar + lbase;
-    long long rpos = tk.begin + nl + rcar + (long long)(w * WPW * 32 - lbase);
-    const unsigned lt = (1u << lane) - 1u;
-#pragma unroll
-    for (int j = 0; j < WPW; j++) {
-        const int o = (w * WPW + j) * 32 + lane;
-        const unsigned word = wd[j];
-        const bool left = (word >> lane) & 1u;
-        const int nvalid = max(0, min(32, m - (w * WPW + j) * 32));
-        if (o < m) {
-            const int row = src[tstart + o];
-            if (left) dst[lpos + __popc(word & lt)] = row;
-            else dst[rpos + (lane - __popc(word & lt))] = row;
-        }
-        const int nlw = __popc(word);
-        lpos += nlw;
-        rpos += nvalid - nlw;
-    }
-}
+// The partition of a level (the sides of E:663-674: goes_left on the split's
+// feature, bin and NaN direction), in one pass.  A CTA per tile of
+// kPartTile consecutive positions of a parent's row list; tiles are taken
+// in order from a ticket, so every tile a CTA waits on has started.  Each
+// thread holds 8 rows with their loads in flight together; the ballots of
+// the tile give each row its rank among the tile's lefts, and the tile's
+// left count is published for decoupled look-back: the tile's lefts before
+// it in the task come from its predecessors' published sums.  Lefts are
+// written to the front of the parent's range in list order, rights to its
+// back in reverse order: a node's list is then ascending or descending
+// (every list stays monotonic), and the order inside a node changes no
+// result, every sum over it being exact.  The task's last tile stores the
+// task's left count.  The last CTA to finish clears the tile words and the
+// ticket for the next level and plans the children's histograms.
+// A look-back wait is bounded: past kLookbackSpins polls it records the
+// failure in *err (the round then fails on the host) and goes on.
+constexpr unsigned long long kTileAgg = 1ull << 62, kTilePre = 2ull << 62, kTileVal = (1ull << 62) - 1;
+constexpr int kLookbackSpins = 1 << 22;
 
 __global__ void __launch_bounds__(kPartThreads)
-k_part_scatter(const int32_t *__restrict__ rows0, int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks,
-               const int *__restrict__ ntask_p, const int *__restrict__ tiles_total,
-               const unsigned *__restrict__ side, const int32_t *__restrict__ tile_cnt,
-               long long *__restrict__ n_left, DNode *__restrict__ nodes, const int *__restrict__ lvl,
-               const long long *__restrict__ gl, HistTask *__restrict__ ht, int32_t *__restrict__ prefix,
-               unsigned *__restrict__ done) {
+k_partition(const uint8_t *__restrict__ xb, int64_t n, int32_t *__restrict__ rows0, int32_t *__restrict__ rows1,
+            const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p, const int *__restrict__ tiles_total,
+            unsigned long long *__restrict__ tile_st, unsigned *__restrict__ ticket, int *__restrict__ err,
+            long long *__restrict__ n_left, const int32_t *__restrict__ bigidx, const uint32_t *__restrict__ topbits,
+            DNode *__restrict__ nodes, const int *__restrict__ lvl, const long long *__restrict__ gl,
+            HistTask *__restrict__ ht, int32_t *__restrict__ prefix, unsigned *__restrict__ done) {
     griddep_wait();
-    if (blockIdx.x < *tiles_total) part_scatter_tile(rows0, rows1, tasks, ntask_p, side, tile_cnt, n_left);
-    // the last CTA to finish plans the children's histograms (k_plan_hist's work)
+    constexpr int J = kPartTile / kPartThreads;
+    constexpr int NW = kPartTile / 32;   // ballot words of a tile
+    __shared__ int s_pre[NW];             // lefts before each word of the tile
+    __shared__ int s_tile, s_tot;
+    __shared__ long long s_lcar;
     __shared__ int s_last;
     __shared__ int s_w[32];
+    if (threadIdx.x == 0) s_tile = (int)atomicAdd(ticket, 1u);
+    __syncthreads();
+    const int tile = s_tile;
+    const int ntiles = *tiles_total;
+    if (tile < ntiles) {
+        const int t = find_task_by_tile(tasks, *ntask_p, tile);
+        const PartTask tk = tasks[t];
+        const int32_t *__restrict__ src = tk.src ? rows1 : rows0;
+        int32_t *__restrict__ dst = tk.src ? rows0 : rows1;
+        const long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
+        const int m = (int)min((long long)kPartTile, tk.end - r0);
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        // position o = threadIdx.x + j * kPartThreads; word (o >> 5) = warp + j * (kPartThreads / 32)
+        int rw[J];
+#pragma unroll
+        for (int j = 0; j < J; j++) {
+            const int o = threadIdx.x + j * kPartThreads;
+            rw[j] = o < m ? src[r0 + o] : -1;
+        }
+        unsigned wd[J];
+#pragma unroll
+        for (int j = 0; j < J; j++) {
+            // threshold 255 of a 257-bin feature: the rows of bin 256 (stored as 255) go right
+            const bool left = rw[j] >= 0 && goes_left(bin_of(xb, n, rw[j], tk.feat), tk.thr, tk.nan_right) &&
+                              !(tk.thr >= 255 && top_bit(topbits, (n + 31) >> 5, bigidx[tk.feat], rw[j]));
+            wd[j] = __ballot_sync(0xffffffffu, left);
+            if (lane == 0) s_pre[warp + j * (kPartThreads / 32)] = __popc(wd[j]);
+        }
+        __syncthreads();
+        if (warp == 0) {   // exclusive scan of the NW word counts, NW / 32 per lane
+            constexpr int PER = NW / 32;
+            int v[PER], sum = 0;
+#pragma unroll
+            for (int k = 0; k < PER; k++) { v[k] = s_pre[lane * PER + k]; sum += v[k]; }
+            int incl = sum;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int x = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += x;
+            }
+            int run = incl - sum;
+#pragma unroll
+            for (int k = 0; k < PER; k++) { s_pre[lane * PER + k] = run; run += v[k]; }
+            if (lane == 31) s_tot = incl;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const long long tot = s_tot;
+            long long lcar = 0;
+            volatile unsigned long long *vst = tile_st;
+            if (tile == tk.tile0) {
+                vst[tile] = kTilePre | (unsigned long long)tot;
+            } else {
+                vst[tile] = kTileAgg | (unsigned long long)tot;
+                int j = tile - 1, spins = 0;
+                while (true) {
+                    const unsigned long long v = vst[j];
+                    if ((v >> 62) == 0ull) {
+                        if (++spins > kLookbackSpins) { atomicExch(err, 1); break; }
+                        if (spins > 64) __nanosleep(32);
+                        continue;
+                    }
+                    lcar += (long long)(v & kTileVal);
+                    if ((v >> 62) == 2ull) break;
+                    --j;
+                    spins = 0;
+                }
+                vst[tile] = kTilePre | (unsigned long long)(lcar + tot);
+            }
+            s_lcar = lcar;
+            if (tile == tk.tile0 + tk.ntile - 1) n_left[t] = lcar + tot;
+        }
+        __syncthreads();
+        const long long lcar = s_lcar;
+        const long long rcar = (r0 - tk.begin) - lcar;   // rights of the task's earlier tiles
+        const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+        for (int j = 0; j < J; j++) {
+            if (rw[j] < 0) continue;
+            const int o = threadIdx.x + j * kPartThreads;
+            const int wi = warp + j * (kPartThreads / 32);
+            const int lrank = s_pre[wi] + __popc(wd[j] & lt);   // lefts before position o in the tile
+            if ((wd[j] >> lane) & 1u) dst[tk.begin + lcar + lrank] = rw[j];
+            else dst[tk.end - 1 - rcar - (o - lrank)] = rw[j];
+        }
+    }
+    // the last CTA to finish resets the tile words and plans the children's histograms
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x - 1;
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    if (threadIdx.x == 0) *done = 0;
+    for (int i = threadIdx.x; i < ntiles; i += blockDim.x) tile_st[i] = 0ull;
+    if (threadIdx.x == 0) {
+        *done = 0;
+        *ticket = 0;
+    }
     plan_hist_block(nodes, lvl, *ntask_p, n_left, gl, ht, prefix, s_w);
 }
 
@@ -2048,6 +2048,7 @@ __device__ void finish_tree(int nc, int *tf, int *tl, int *tr, long long *tt, do
                             const RParams &P, const int *__restrict__ mono, TreeOut *__restrict__ out,
                             TreeDev *__restrict__ td, int status, long long root_rows, long long alg_rows) {
     const int lane = threadIdx.x & 31;
+    if (P.part_err && *(volatile const int *)P.part_err) status = 3;
     bool prune = false;
     for (int k = lane; k < nc; k += 32) prune |= tf[k] != -1 && sg[k] < P.gamma;
     prune = __any_sync(0xffffffffu, prune);

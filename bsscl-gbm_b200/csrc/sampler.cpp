@@ -18,12 +18,14 @@
 #include <immintrin.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <atomic>
 #include <condition_variable>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <new>
 #include <thread>
@@ -90,41 +92,105 @@ GBM_AVX512 void twist_avx512(uint32_t *mt, uint32_t *out) {
     }
 }
 
+// One twist of MT19937 state `mt`, tempered into dst[0 .. kN).
+void twist_into(uint32_t *mt, uint32_t *dst) {
+    if (use_avx512()) {
+        twist_avx512(mt, dst);
+        return;
+    }
+    int i = 0;
+    for (; i < kN - kM; i++) mt[i] = mix1(mt[i], mt[i + 1], mt[i + kM]);
+    for (; i < kN - 1; i++) mt[i] = mix1(mt[i], mt[i + 1], mt[i + kM - kN]);
+    mt[kN - 1] = mix1(mt[kN - 1], mt[0], mt[kM - 1]);
+    for (int k = 0; k < kN; k++) {
+        uint32_t y = mt[k];
+        y ^= y >> 11;
+        y ^= (y << 7) & 0x9d2c5680u;
+        y ^= (y << 15) & 0xefc60000u;
+        y ^= y >> 18;
+        dst[k] = y;
+    }
+}
+
+// The words of a stream ahead of its draws, made by a second thread.  The
+// MT19937 word stream does not depend on the draws that consume it, so a
+// generator thread twists and tempers it into a ring of chunks while the
+// draw thread decides targets from the chunks in order: the same words in
+// the same order, with the twist off the draw's critical path.
+struct WordPipe {
+    static constexpr int kTwists = 16;                 // twists per chunk
+    static constexpr int kChunkWords = kTwists * kN;   // 9984 words (39 KB)
+    static constexpr int kChunks = 48;                 // a 1.9 MB ring
+    uint32_t mt[kN];                                   // the generator's state
+    std::vector<uint32_t> ring;
+    std::atomic<int64_t> made{0}, freed{0};           // chunks written / released by the reader
+    std::atomic<bool> stop{false};
+    int64_t cur = -1;                                  // the reader's chunk
+    std::thread th;
+
+    explicit WordPipe(const uint32_t *state) : ring((size_t)kChunks * kChunkWords) {
+        std::memcpy(mt, state, sizeof mt);
+        th = std::thread([this] { run(); });
+    }
+    ~WordPipe() {
+        stop.store(true);
+        if (th.joinable()) th.join();
+    }
+    void run() {
+        int idle = 0;   // polls of a full ring in a row: spin while the reader is active, then sleep
+        while (!stop.load(std::memory_order_relaxed)) {
+            const int64_t h = made.load(std::memory_order_relaxed);
+            if (h - freed.load(std::memory_order_acquire) >= kChunks) {   // full: the reader is behind
+                if (++idle < (1 << 16)) _mm_pause();
+                else std::this_thread::sleep_for(std::chrono::microseconds(200));
+                continue;
+            }
+            idle = 0;
+            uint32_t *dst = ring.data() + (size_t)(h % kChunks) * kChunkWords;
+            for (int k = 0; k < kTwists; k++) twist_into(mt, dst + k * kN);
+            made.store(h + 1, std::memory_order_release);
+        }
+    }
+    // The reader: release the current chunk and wait for the next.
+    const uint32_t *next() {
+        if (cur >= 0) freed.store(cur + 1, std::memory_order_release);
+        cur++;
+        int spins = 0;
+        while (made.load(std::memory_order_acquire) <= cur) {
+            if (++spins < 512) _mm_pause();
+            else std::this_thread::yield();
+        }
+        return ring.data() + (size_t)(cur % kChunks) * kChunkWords;
+    }
+};
+
+// The reader's view of the stream: a window out[0 .. len) of tempered
+// words, refilled by one twist, or by the next chunk of a WordPipe.
 struct MT19937 {
     uint32_t mt[kN];
-    uint32_t out[kN];   // tempered words of the current state
-    int idx = kN;
+    uint32_t buf[kN];
+    const uint32_t *out = buf;
+    int idx = kN, len = kN;
+    WordPipe *pipe = nullptr;
     void seed(uint32_t s) {
         mt[0] = s;
         for (int i = 1; i < kN; i++) mt[i] = 1812433253u * (mt[i - 1] ^ (mt[i - 1] >> 30)) + (uint32_t)i;
-        idx = kN;
+        idx = len = kN;
+        out = buf;
     }
-    static inline uint32_t mix(uint32_t a, uint32_t b, uint32_t c) {
-        uint32_t y = (a & 0x80000000u) | (b & 0x7fffffffu);
-        return c ^ (y >> 1) ^ ((0u - (y & 1u)) & 0x9908b0dfu);
-    }
-    void refill() {   // the standard twist (split so no index wraps), then tempering
-        if (use_avx512()) {
-            twist_avx512(mt, out);
-            idx = 0;
-            return;
-        }
-        int i = 0;
-        for (; i < kN - kM; i++) mt[i] = mix(mt[i], mt[i + 1], mt[i + kM]);
-        for (; i < kN - 1; i++) mt[i] = mix(mt[i], mt[i + 1], mt[i + kM - kN]);
-        mt[kN - 1] = mix(mt[kN - 1], mt[0], mt[kM - 1]);
-        for (int k = 0; k < kN; k++) {
-            uint32_t y = mt[k];
-            y ^= y >> 11;
-            y ^= (y << 7) & 0x9d2c5680u;
-            y ^= (y << 15) & 0xefc60000u;
-            y ^= y >> 18;
-            out[k] = y;
+    void refill() {
+        if (pipe) {
+            out = pipe->next();
+            len = WordPipe::kChunkWords;
+        } else {
+            twist_into(mt, buf);
+            out = buf;
+            len = kN;
         }
         idx = 0;
     }
     inline uint32_t next32() {
-        if (idx >= kN) refill();
+        if (idx >= len) refill();
         return out[idx++];
     }
 };
@@ -170,15 +236,16 @@ GBM_AVX512 void draw_targets_avx512(MT19937 &r, int64_t n, int32_t *t) {
     const int64_t top = n - 1;
     int64_t pos = 0;                    // i = top - pos
     while (top - pos >= 1) {
-        if (r.idx >= kN) r.refill();
+        if (r.idx >= r.len) r.refill();
         int64_t i = top - pos;
         const uint32_t mask = smear((uint64_t)i);
         const int64_t stop = ((int64_t)mask + 1) >> 1;   // lowest i with this mask
         const uint32_t *w = r.out;
+        const int L = r.len;
         int k = r.idx;
         const __m512i vm = _mm512_set1_epi32((int)mask);
         // 64-word blocks: four independent compares, one store chain
-        while (k + 64 <= kN && i - 63 >= stop) {
+        while (k + 64 <= L && i - 63 >= stop) {
             const __m512i hi = _mm512_set1_epi32((int)i), lo = _mm512_set1_epi32((int)(i - 63));
             __m512i v[4];
             __mmask16 nacc[4];
@@ -199,7 +266,7 @@ GBM_AVX512 void draw_targets_avx512(MT19937 &r, int64_t n, int32_t *t) {
             i = top - pos;
         }
         // 16-word blocks (at most 4 of them before trying 64 again)
-        for (int blk = 0; blk < 4 && k + 16 <= kN && i - 15 >= stop; blk++) {
+        for (int blk = 0; blk < 4 && k + 16 <= L && i - 15 >= stop; blk++) {
             const __m512i v = _mm512_and_si512(_mm512_loadu_si512(w + k), vm);
             const __mmask16 rej = _mm512_cmpgt_epi32_mask(v, _mm512_set1_epi32((int)i));
             const __mmask16 nacc = _mm512_cmpgt_epi32_mask(v, _mm512_set1_epi32((int)(i - 15)));
@@ -211,7 +278,7 @@ GBM_AVX512 void draw_targets_avx512(MT19937 &r, int64_t n, int32_t *t) {
             i = top - pos;
         }
         // single words, up to 16
-        const int end = std::min(kN, k + 16);
+        const int end = std::min(L, k + 16);
         while (k < end && i >= stop) {
             const uint32_t v = w[k++] & mask;
             t[pos] = (int32_t)v;
@@ -227,15 +294,16 @@ void draw_targets_avx2(MT19937 &r, int64_t n, int32_t *t) {
     const int64_t top = n - 1;
     int64_t pos = 0;                    // i = top - pos
     while (top - pos >= 1) {
-        if (r.idx >= kN) r.refill();
+        if (r.idx >= r.len) r.refill();
         int64_t i = top - pos;
         const uint32_t mask = smear((uint64_t)i);
         const int64_t stop = ((int64_t)mask + 1) >> 1;   // lowest i with this mask
         const uint32_t *w = r.out;
+        const int L = r.len;
         int k = r.idx;
         const __m256i vm = _mm256_set1_epi32((int)mask);
         // 64-word blocks: eight independent compares, one store chain
-        while (k + 64 <= kN && i - 63 >= stop) {
+        while (k + 64 <= L && i - 63 >= stop) {
             const __m256i hi = _mm256_set1_epi32((int)i), lo = _mm256_set1_epi32((int)(i - 63));
             __m256i v[8];
             int nacc[8], amb = 0;
@@ -251,7 +319,7 @@ void draw_targets_avx2(MT19937 &r, int64_t n, int32_t *t) {
             i = top - pos;
         }
         // 8-word blocks (at most 8 of them before trying 64 again)
-        for (int blk = 0; blk < 8 && k + 8 <= kN && i - 7 >= stop; blk++) {
+        for (int blk = 0; blk < 8 && k + 8 <= L && i - 7 >= stop; blk++) {
             const __m256i v = _mm256_and_si256(_mm256_loadu_si256((const __m256i *)(w + k)), vm);
             const int rej = _mm256_movemask_ps(_mm256_castsi256_ps(_mm256_cmpgt_epi32(v, _mm256_set1_epi32((int)i))));
             const int nacc =
@@ -262,7 +330,7 @@ void draw_targets_avx2(MT19937 &r, int64_t n, int32_t *t) {
             i = top - pos;
         }
         // single words, up to 8
-        const int end = std::min(kN, k + 8);
+        const int end = std::min(L, k + 8);
         while (k < end && i >= stop) {
             const uint32_t v = w[k++] & mask;
             t[pos] = (int32_t)v;
@@ -309,6 +377,7 @@ using namespace gbmsamp;
 
 struct gbm_sampler {
     MT19937 rng;
+    std::unique_ptr<WordPipe> pipe;    // the words ahead (large draws drawn ahead only)
     int64_t n = 0, n_sub = 0;
     int32_t p = 0, n_feat = 0;
     int sub_on = 0, col_on = 0;
@@ -413,6 +482,12 @@ int gbm_sampler_create(uint32_t seed, int64_t n, int32_t p, int64_t n_sub, int32
             if (s->sub_on) R.trow.resize((size_t)n + 16);
             R.feat.resize((size_t)n_feat);
         };
+        // a draw of a million rows spends about half its time in the twist:
+        // drawn ahead, it gets a generator thread of its own
+        if (s->ahead > 0 && n >= (1 << 17)) {
+            s->pipe.reset(new WordPipe(s->rng.mt));
+            s->rng.pipe = s->pipe.get();
+        }
         if (s->ahead > 0) {
             s->ring.resize((size_t)s->ahead + 1);
             for (auto &R : s->ring) size_round(R);

@@ -357,6 +357,54 @@ def test_hist3_layout_is_conflict_free_and_complete():
             assert (out[k >> 2] >> ((k & 3) * 8)) & 0xFF == by[(k + r) % 16]
 
 
+def _partition_restated(rows, left, begin, end, tile=4096, threads=512):
+    """k_partition's index arithmetic for one task, restated: position o of
+    tile k is word (o >> 5) = warp + j * (threads / 32) with lane o & 31; a
+    left goes to begin + lcar + lrank, a right to end - 1 - rcar - (o - lrank)."""
+    out = np.full(len(rows), -1, dtype=np.int64)
+    lcar = 0
+    ntile = max(1, -(-(end - begin) // tile))
+    for k in range(ntile):
+        r0 = begin + k * tile
+        m = min(tile, end - r0)
+        l = np.zeros(tile, bool)
+        l[:m] = left[r0:r0 + m]
+        words = l.reshape(tile // 32, 32)
+        pre = np.concatenate([[0], np.cumsum(words.sum(axis=1))[:-1]])
+        rcar = (r0 - begin) - lcar
+        for o in range(m):
+            lrank = pre[o >> 5] + int(words[o >> 5, :(o & 31)].sum())
+            dst = begin + lcar + lrank if l[o] else end - 1 - rcar - (o - lrank)
+            assert begin <= dst < end and out[dst] == -1
+            out[dst] = rows[r0 + o]
+        lcar += int(l[:m].sum())
+    return out[begin:end], lcar
+
+
+@pytest.mark.parametrize("size", [1, 31, 4096, 4097, 20_000])
+def test_partition_index_arithmetic_is_a_monotonic_permutation(size):
+    """Every row lands once inside the task's range, the lefts first in list
+    order and the rights after them in reverse order, so an ascending list
+    gives an ascending left child and a descending right child (and a
+    monotonic list gives monotonic children at every depth)."""
+    rng = np.random.default_rng(size)
+    begin = 7
+    rows = np.concatenate([np.full(begin, -5), np.sort(rng.choice(10 * size + 10, size, replace=False)),
+                           np.full(3, -9)])
+    left = rng.random(len(rows)) < 0.4
+    out, nl = _partition_restated(rows, left, begin, begin + size)
+    seg, lseg = rows[begin:begin + size], left[begin:begin + size]
+    assert nl == int(lseg.sum())
+    assert np.array_equal(out[:nl], seg[lseg])
+    assert np.array_equal(out[nl:], seg[~lseg][::-1])
+    # the right child, partitioned again, stays monotonic (descending in, so left part descending)
+    if size - nl > 1:
+        r = out[nl:]
+        l2 = rng.random(len(r)) < 0.5
+        out2, nl2 = _partition_restated(r, l2, 0, len(r))
+        assert np.all(np.diff(out2[:nl2]) < 0) and np.all(np.diff(out2[nl2:]) > 0)
+
+
 @pytest.mark.parametrize("name", ["cfg1", "cfg1_level", "cfg2_small", "cfg3_small", "cfg4_small"])
 def test_packing_and_importances_match_reference(name):
     """The estimator's packing (_pack_tree_list, E:2192-2216) and gain
