@@ -218,6 +218,7 @@ struct gbm_ctx {
     int32_t pp = 0;
     uint8_t *d_pnodes = nullptr;    // PNode [total], or the 32-bit breadth-first words when p_packed
     bool p_packed = false;
+    bool p_packed_nr = false;       // the packed words hold NaN-right splits
     double *d_pvals = nullptr;
     int32_t *d_poff = nullptr;
     int4 *d_pchunk = nullptr;       // [p_trees_cap] chunks of whole trees, then the chunk count
@@ -445,7 +446,10 @@ int halloc(gbm_ctx *ctx, T **p, size_t count) {
 // uploaded when a check fails.
 int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::vector<PNode> &nodes,
                std::vector<double> &vals, std::vector<uint32_t> *n32 = nullptr, std::vector<double> *v32 = nullptr,
-               std::vector<int32_t> *dep32 = nullptr) {
+               std::vector<int32_t> *dep32 = nullptr, bool *has_nr = nullptr) {
+    bool nr_scratch = false;
+    if (!has_nr) has_nr = &nr_scratch;
+    *has_nr = false;
     auto bad = [&err](int code, const char *fmt, auto... a) {
         char buf[256];
         snprintf(buf, sizeof buf, fmt, a...);
@@ -491,12 +495,12 @@ int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::v
         }
     }
     if (n32 && v32 && dep32) {
-        // the 32-bit breadth-first form (k_predict's PACKED format): every
-        // tree renumbered so that a node's children are adjacent, each leaf
-        // pointing at itself with threshold 255, a NaN-right split stored with
-        // threshold - 1 and bit 31 set, and the tree's depth; only when
-        // features fit 11 bits and every tree (as reached from its root) fits
-        // 4096 nodes, else *n32 stays empty
+        // the 32-bit breadth-first form (k_predict's PACKED format, the word
+        // layout of walk_packed): every tree renumbered so that a node's
+        // children are adjacent, each leaf pointing at itself with threshold
+        // 255, a NaN-right split stored with threshold - 1 and bit 23 set,
+        // and the tree's depth; only when features fit 11 bits and every tree
+        // (as reached from its root) fits 4096 nodes, else *n32 stays empty
         n32->clear();
         v32->clear();
         dep32->clear();
@@ -515,15 +519,16 @@ int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::v
             for (size_t h = 0; h < order.size(); h++) {
                 const int32_t k = order[h];
                 const PNode &nd = nodes[(size_t)(o + k)];
-                uint32_t w = (255u << 12) | (uint32_t)nid[h];   // a leaf: no bin is above 255
+                uint32_t w = (255u << 24) | (uint32_t)nid[h];   // a leaf: no bin is above 255
                 if (nd.feat >= 0) {
                     if (next + 1 >= sz) return GBM_OK;   // more nodes than the tree holds (shared children)
                     // threshold 255 exactly: bin 256 of a 257-bin feature goes right,
                     // which needs the top bits of the 8-byte walk
                     if (nd.thr == 255 && !(nd.nanr & 2)) return GBM_OK;
-                    const uint32_t nr = nd.nanr & 1;
-                    w = (nr << 31) | ((uint32_t)nd.feat << 20) | ((uint32_t)(nr ? nd.thr - 1 : nd.thr) << 12) |
-                        (uint32_t)next;
+                    const uint32_t nr = nd.nanr & 1, f = (uint32_t)nd.feat;
+                    w = ((uint32_t)(nr ? nd.thr - 1 : nd.thr) << 24) | (nr << 23) | ((f & 3u) << 21) |
+                        ((f >> 2) << 12) | (uint32_t)next;
+                    if (nr) *has_nr = true;
                     order.push_back(nd.left);
                     nid.push_back(next);
                     lev.push_back(lev[h] + 1);
@@ -545,33 +550,36 @@ int pack_model(std::string &err, const gbm_packed *m, int32_t n_features, std::v
     return GBM_OK;
 }
 
-// k_predict's shape for p features: two rows per thread (512 per CTA) while
-// the row tile stays within 52 KB, so two CTAs share an SM; else one row per
-// thread, and fewer rows per CTA when 256 rows of p bytes do not fit.
+// k_predict's shape for p features (kPredThreads threads per CTA, one CTA
+// per SM or more when they fit): two rows per thread while that row tile
+// fits beside the two chunk buffers; else one row per thread, and fewer
+// rows per CTA when even that does not fit; rows wider than 32 rows' tile
+// are read from global memory.
 struct PredShape {
     int rpt, rpc, stage_rows;
     size_t smem;
 };
 
 PredShape predict_shape(int p, bool packed) {
-    if (predict_smem(2 * kPredThreads, p, packed) - predict_smem(0, p, packed) <= 52 * 1024)
+    constexpr size_t kSmem = 227 * 1024;
+    if (predict_smem(2 * kPredThreads, p, packed) <= kSmem)
         return {2, 2 * kPredThreads, 1, predict_smem(2 * kPredThreads, p, packed)};
-    const size_t room = 227 * 1024 - predict_smem(0, p, packed);
+    const size_t room = kSmem - predict_smem(0, p, packed);
     const size_t per32 = predict_smem(32, p, packed) - predict_smem(0, p, packed);
     const int rpc = (int)std::min<size_t>(kPredThreads, room / per32 * 32);
     if (rpc < 32) return {1, kPredThreads, 0, predict_smem(0, p, packed)};   // rows read from global memory
     return {1, rpc, 1, predict_smem(rpc, p, packed)};
 }
 
-template <int RPT, bool PK, bool SR>
+template <int RPT, bool PK, bool SR, bool NR>
 cudaError_t launch_predict_t(const PredShape &sh, unsigned grid, const uint8_t *xr, int64_t n, int p,
                              const void *nodes, const double *vals, const int32_t *off, const int32_t *dep, int ntree,
                              const int4 *cstart, const int32_t *nchunk, double lr, double base, double *F,
                              double *P, const int32_t *bigidx, const uint32_t *topbits, cudaStream_t st) {
-    cudaError_t e = cudaFuncSetAttribute(k_predict<RPT, PK, SR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_predict<RPT, PK, SR, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)sh.smem);
     if (e != cudaSuccess) return e;
-    k_predict<RPT, PK, SR><<<grid, kPredThreads, sh.smem, st>>>(xr, n, p, nodes, vals, off, dep, ntree, cstart,
+    k_predict<RPT, PK, SR, NR><<<grid, kPredThreads, sh.smem, st>>>(xr, n, p, nodes, vals, off, dep, ntree, cstart,
                                                                  nchunk, sh.rpc, lr, base, F, P, bigidx,
                                                                  topbits);
     return cudaGetLastError();
@@ -585,13 +593,18 @@ cudaError_t launch_predict_t(const PredShape &sh, unsigned grid, const uint8_t *
 cudaError_t launch_predict(const uint8_t *xr, int64_t n, int p, const void *nodes, bool packed, const double *vals,
                            const int32_t *off, const int32_t *dep, int ntree, const int4 *cstart,
                            const int32_t *nchunk, double lr, double base, double *F, double *P,
-                           const int32_t *bigidx, const uint32_t *topbits, cudaStream_t st) {
+                           const int32_t *bigidx, const uint32_t *topbits, cudaStream_t st, bool packed_nr = true) {
     const PredShape sh = predict_shape(p, packed);
     const unsigned grid = (unsigned)((n + sh.rpc - 1) / sh.rpc);
-#define GBM_PRED(R, K, S) launch_predict_t<R, K, S>(sh, grid, xr, n, p, nodes, vals, off, dep, ntree, cstart, nchunk, lr, base, F, P, bigidx, topbits, st)
-    if (sh.rpt == 2) return packed ? GBM_PRED(2, true, true) : GBM_PRED(2, false, true);
-    if (sh.stage_rows) return packed ? GBM_PRED(1, true, true) : GBM_PRED(1, false, true);
-    return packed ? GBM_PRED(1, true, false) : GBM_PRED(1, false, false);
+#define GBM_PRED(R, K, S, N) launch_predict_t<R, K, S, N>(sh, grid, xr, n, p, nodes, vals, off, dep, ntree, cstart, nchunk, lr, base, F, P, bigidx, topbits, st)
+    if (packed) {   // NaN-right splits in the packed words: the walk's extra step only when the model has some
+        if (sh.rpt == 2) return packed_nr ? GBM_PRED(2, true, true, true) : GBM_PRED(2, true, true, false);
+        if (sh.stage_rows) return packed_nr ? GBM_PRED(1, true, true, true) : GBM_PRED(1, true, true, false);
+        return packed_nr ? GBM_PRED(1, true, false, true) : GBM_PRED(1, true, false, false);
+    }
+    if (sh.rpt == 2) return GBM_PRED(2, false, true, false);
+    if (sh.stage_rows) return GBM_PRED(1, false, true, false);
+    return GBM_PRED(1, false, false, false);
 #undef GBM_PRED
 }
 
@@ -2741,7 +2754,9 @@ int gbm_predict_set_model(gbm_ctx *ctx, const gbm_packed *m, int32_t n_features)
     std::vector<double> v32;
     std::vector<int32_t> dep;
     std::string err;
-    if (int rc = pack_model(err, m, n_features, nodes, vals, &n32, &v32, &dep)) return fail(ctx, rc, "%s", err.c_str());
+    bool has_nr = false;
+    if (int rc = pack_model(err, m, n_features, nodes, vals, &n32, &v32, &dep, &has_nr))
+        return fail(ctx, rc, "%s", err.c_str());
     CK(cudaSetDevice(ctx->dev));
     int64_t total = (int64_t)nodes.size();
     if (total > ctx->p_nodes_cap) {
@@ -2756,6 +2771,7 @@ int gbm_predict_set_model(gbm_ctx *ctx, const gbm_packed *m, int32_t n_features)
         ctx->p_trees_cap = T + 1;
     }
     ctx->p_packed = !n32.empty();
+    ctx->p_packed_nr = has_nr;
     if (ctx->p_packed) {
         CK(cudaMemcpyAsync(ctx->d_pnodes, n32.data(), sizeof(uint32_t) * total, cudaMemcpyHostToDevice, ctx->st));
         CK(cudaMemcpyAsync(ctx->d_pvals, v32.data(), sizeof(double) * total, cudaMemcpyHostToDevice, ctx->st));
@@ -2864,12 +2880,15 @@ int gbm_predict_raw(gbm_ctx *ctx, const void *X, int64_t n, int32_t p, int32_t d
 int gbm_predict_run(gbm_ctx *ctx, double lr, double base) {
     if (!ctx) return GBM_ERR_ARG;
     if (!ctx->d_px || !ctx->d_poff) return fail(ctx, GBM_ERR_STATE, "upload a model and rows first");
+    // the packed walk reads a feature's byte unclamped: the rows must have the model's features
+    if (ctx->pp != ctx->p_nfeat)
+        return fail(ctx, GBM_ERR_ARG, "the rows have %d features, the model %d", ctx->pp, ctx->p_nfeat);
     CK(cudaSetDevice(ctx->dev));
     CK(launch_predict(ctx->d_px, ctx->pn, ctx->pp, ctx->d_pnodes, ctx->p_packed, ctx->d_pvals, ctx->d_poff,
                       ctx->d_pdep, ctx->p_ntree, ctx->d_pchunk,
                       reinterpret_cast<const int32_t *>(ctx->d_pchunk + ctx->p_ntree + 1), lr, base, ctx->d_pF,
                       ctx->d_pP, ctx->p_top ? ctx->d_pbigidx : nullptr, ctx->p_top ? ctx->d_ptopbits : nullptr,
-                      ctx->st));
+                      ctx->st, ctx->p_packed_nr));
     ctx->launches++;
     return GBM_OK;
 }

@@ -2292,7 +2292,7 @@ k_replay_depth(const DNode *__restrict__ nodes, const int *__restrict__ node_cou
 // that tests 32 offsets per step, and writes each chunk as {first tree, end
 // tree, first node, node count}; a tree larger than the buffer is a chunk of
 // its own and is walked from global memory.
-constexpr int kPredThreads = 256;
+constexpr int kPredThreads = 768;   // 24 warps: one CTA of 1536 rows per SM at p = 100
 constexpr int kPredChunkNodes = 2048;
 constexpr int kPredChunkTrees = 512;
 
@@ -2333,21 +2333,44 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // One tree for a thread's RPT rows, PACKED format: exactly `dep` steps (a
 // leaf points at itself with threshold 255, so no bin moves it).  `tn` and
 // the rows are shared or global memory as the caller's pointers are; each
-// call site is inlined with a known address space.
-template <int RPT, bool SROWS>
-__device__ __forceinline__ void walk_packed(const uint32_t *__restrict__ tn, int dep, int szm1, int pm1,
-                                            const uint8_t *const *rowp, int *node) {
-    for (int s = 0; s < dep; s++) {
+// call site is inlined with a known address space.  The word (pack_model):
+//   bits 24-31 threshold, 23 NaN right, 21-22 feature & 3, 12-20 feature >> 2,
+//   0-11 left child (the right child is left + 1);
+// so the feature's byte in the swizzled row tile is at
+// ((w >> 5) & 0xff80) | ((w >> 21) & 3), and the row goes right when
+// (bin << 24) > w (the bits below the threshold never reach a whole step
+// of it).  The features were checked below p and the children inside the
+// tree when the model was packed (p is the model's feature count, checked
+// again at launch), so no index is clamped here: every word comes from
+// pack_model.  NR: the model has NaN-right splits (threshold stored as t - 1;
+// the walk compares bin - 1 mod 256, so bin 0 goes right).
+template <int RPT, bool SROWS, bool NR>
+__device__ __forceinline__ void step_packed(const uint32_t *__restrict__ tn, const uint8_t *const *rowp,
+                                            int *node) {
 #pragma unroll
-        for (int j = 0; j < RPT; j++) {
-            const uint32_t w = tn[node[j]];
-            const int f = min((int)((w >> 20) & 0x7ffu), pm1);
-            const int b0 = SROWS ? rowp[j][((f >> 2) << 7) | (f & 3)] : __ldg(rowp[j] + f);
-            // a NaN-right split (bit 31, threshold stored as t - 1) compares bin - 1 mod 256: bin 0 -> 255
-            const int b = (b0 - (int)(w >> 31)) & 0xff;
-            node[j] = min((int)(w & 0xfffu) + (b > (int)((w >> 12) & 0xffu) ? 1 : 0), szm1);
+    for (int j = 0; j < RPT; j++) {
+        const uint32_t w = tn[node[j]];
+        uint32_t b;
+        if (SROWS) {
+            b = rowp[j][((w >> 5) & 0xff80u) | ((w >> 21) & 3u)];
+        } else {
+            const uint32_t f = ((w >> 10) & 0x7fcu) | ((w >> 21) & 3u);
+            b = __ldg(rowp[j] + f);
         }
+        if (NR) b = (b - ((w >> 23) & 1u)) & 0xffu;
+        node[j] = (int)(w & 0xfffu) + ((b << 24) > w ? 1 : 0);
     }
+}
+
+template <int RPT, bool SROWS, bool NR>
+__device__ __forceinline__ void walk_packed(const uint32_t *__restrict__ tn, int dep, const uint8_t *const *rowp,
+                                            int *node) {
+    if (dep == 8) {   // the common depth, unrolled
+#pragma unroll
+        for (int s = 0; s < 8; s++) step_packed<RPT, SROWS, NR>(tn, rowp, node);
+        return;
+    }
+    for (int s = 0; s < dep; s++) step_packed<RPT, SROWS, NR>(tn, rowp, node);
 }
 
 // The same in the 8-byte PNode format (the reference's numbering): walk
@@ -2385,7 +2408,7 @@ __device__ __forceinline__ void walk_pnode(const PNode *__restrict__ tn, int szm
 // (predict_all_trees_jit, E:863-884), and proba = sigmoid(clip(F, +-500))
 // (E:3318-3336).
 //
-// A CTA takes rpc <= RPT x 256 consecutive rows.  With SROWS their bins are
+// A CTA takes rpc <= RPT x kPredThreads consecutive rows.  With SROWS their bins are
 // staged in shared memory once, swizzled so that the 32 lanes of a warp (32
 // consecutive rows) read 32 different banks whatever features they test:
 // byte f of tile row r sits at byte 4 * ((r / 32) * P4 * 32 + r % 32) +
@@ -2396,18 +2419,21 @@ __device__ __forceinline__ void walk_pnode(const PNode *__restrict__ tn, int szm
 // c + 1 into the other buffer.
 //
 // Node formats.  PACKED: one 32-bit word per node of a tree renumbered
-// breadth-first (pack_model), children adjacent: nan_right << 31 | feature
-// << 20 | threshold << 12 | left child, right = left + 1 (a NaN-right split
+// breadth-first (pack_model), children adjacent: threshold, NaN direction,
+// feature and left child (walk_packed), right = left + 1 (a NaN-right split
 // holds threshold - 1 and compares bin - 1 mod 256, so the NaN bin goes
 // right), and a leaf pointing at itself with threshold 255; every row takes
 // exactly the tree's depth steps with no branch.  Level d of a complete tree is 2^d consecutive words,
 // conflict-free up to level 5.  Otherwise PNode (8 bytes, the reference's
 // own numbering), walked until a leaf.
 //
-// The walk is bounded whatever the node table holds: a feature is clamped
-// below p, a child below the tree's size, and a walk stops after size - 1
-// steps (a valid tree's children come after their parent, so a real walk
-// never needs more).
+// The walk is bounded.  PNode: whatever the node table holds, a feature is
+// clamped below p, a child below the tree's size, and a walk stops after
+// size - 1 steps (a valid tree's children come after their parent, so a
+// real walk never needs more).  PACKED: the words are built on the host
+// from a checked model (features below its feature count, which the rows
+// must match, children inside the tree, leaves pointing at themselves),
+// and every row takes at most min(depth, size - 1) steps.
 template <bool PACKED>
 struct PredBuf {
     static constexpr int kNodeBytes = PACKED ? 4 : 8;
@@ -2415,7 +2441,7 @@ struct PredBuf {
         (sizeof(double) + kNodeBytes) * kPredChunkNodes + 2 * sizeof(int32_t) * (kPredChunkTrees + 4);
 };
 
-template <int RPT, bool PACKED, bool SROWS>
+template <int RPT, bool PACKED, bool SROWS, bool NR>
 __global__ void __launch_bounds__(kPredThreads)
 k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const void *__restrict__ nodes_v,
           const double *__restrict__ vals, const int32_t *__restrict__ off, const int32_t *__restrict__ depth_g,
@@ -2518,8 +2544,8 @@ k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const void *__restri
                 const int ob = s_off[t - t0] - o0, sz = s_off[t - t0 + 1] - o0 - ob;
                 if (sz <= 0) continue;
                 if (PACKED)
-                    walk_packed<RPT, SROWS>(reinterpret_cast<const uint32_t *>(s_nd) + ob, min(s_dep[t - t0], sz - 1),
-                                            sz - 1, pm1, rowp, node);
+                    walk_packed<RPT, SROWS, NR>(reinterpret_cast<const uint32_t *>(s_nd) + ob,
+                                                min(s_dep[t - t0], sz - 1), rowp, node);
                 else
                     walk_pnode<RPT, SROWS>(reinterpret_cast<const PNode *>(s_nd) + ob, sz - 1, pm1, rowp, node, rid,
                                            bigidx, topbits, top_words);
@@ -2529,8 +2555,8 @@ k_predict(const uint8_t *__restrict__ xr, int64_t n, int p, const void *__restri
                 const int ob = __ldg(off + t), sz = __ldg(off + t + 1) - ob;
                 if (sz <= 0) continue;
                 if (PACKED)
-                    walk_packed<RPT, SROWS>(reinterpret_cast<const uint32_t *>(nodes_v) + ob,
-                                            min(__ldg(depth_g + t), sz - 1), sz - 1, pm1, rowp, node);
+                    walk_packed<RPT, SROWS, NR>(reinterpret_cast<const uint32_t *>(nodes_v) + ob,
+                                                min(__ldg(depth_g + t), sz - 1), rowp, node);
                 else
                     walk_pnode<RPT, SROWS>(reinterpret_cast<const PNode *>(nodes_v) + ob, sz - 1, pm1, rowp, node, rid,
                                            bigidx, topbits, top_words);
