@@ -1150,31 +1150,43 @@ k_partition(const uint8_t *__restrict__ xb, int64_t n, int32_t *__restrict__ row
             if (lane == 31) s_tot = incl;
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
+        if (warp == 0) {   // decoupled look-back, 32 predecessors at a time
             const long long tot = s_tot;
-            long long lcar = 0;
             volatile unsigned long long *vst = tile_st;
+            long long lcar = 0;
             if (tile == tk.tile0) {
-                vst[tile] = kTilePre | (unsigned long long)tot;
+                if (lane == 0) vst[tile] = kTilePre | (unsigned long long)tot;
             } else {
-                vst[tile] = kTileAgg | (unsigned long long)tot;
-                int j = tile - 1, spins = 0;
+                if (lane == 0) vst[tile] = kTileAgg | (unsigned long long)tot;
+                int top = tile - 1;   // the window's nearest tile; lane l reads tile top - l
+                bool bad = false;
                 while (true) {
-                    const unsigned long long v = vst[j];
-                    if ((v >> 62) == 0ull) {
-                        if (++spins > kLookbackSpins) { atomicExch(err, 1); break; }
+                    const int j = top - lane;
+                    // tiles before the task's first (which publishes its prefix at once) add nothing
+                    unsigned long long v = kTilePre + 0ull;
+                    if (j >= tk.tile0) v = vst[j];
+                    int spins = 0;
+                    while (!__all_sync(0xffffffffu, (v >> 62) != 0ull)) {
+                        if (++spins > kLookbackSpins) { bad = true; break; }
                         if (spins > 64) __nanosleep(32);
-                        continue;
+                        if ((v >> 62) == 0ull) v = vst[j];
                     }
-                    lcar += (long long)(v & kTileVal);
-                    if ((v >> 62) == 2ull) break;
-                    --j;
-                    spins = 0;
+                    if (bad) break;
+                    const unsigned pre = __ballot_sync(0xffffffffu, (v >> 62) == 2ull);
+                    const int k = pre ? __ffs(pre) - 1 : 31;   // the nearest tile with a prefix, else the window
+                    long long x = lane <= k ? (long long)(v & kTileVal) : 0ll;
+                    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+                    lcar += x;
+                    if (pre) break;
+                    top -= 32;
                 }
-                vst[tile] = kTilePre | (unsigned long long)(lcar + tot);
+                if (bad && lane == 0) atomicExch(err, 1);
+                if (lane == 0) vst[tile] = kTilePre | (unsigned long long)(lcar + tot);
             }
-            s_lcar = lcar;
-            if (tile == tk.tile0 + tk.ntile - 1) n_left[t] = lcar + tot;
+            if (lane == 0) {
+                s_lcar = lcar;
+                if (tile == tk.tile0 + tk.ntile - 1) n_left[t] = lcar + tot;
+            }
         }
         __syncthreads();
         const long long lcar = s_lcar;
