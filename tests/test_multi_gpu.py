@@ -1,6 +1,7 @@
 """Row-sharded training on 2 GPUs gives the trees of a 1-GPU fit, bit for bit:
 best-first at depth 6, 8 and 12 (capped speculation, host replay with
-on-demand expansion), depth-wise growth, NaN in every feature.
+on-demand expansion), depth-wise growth, NaN in every feature, the default
+constructor's 257-bin features and the learned NaN direction.
 
 Histograms (with the left counts and the root count in their count words),
 the last level's totals and the logloss are all-reduced as exact int64 words
