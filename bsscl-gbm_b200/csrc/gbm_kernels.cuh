@@ -1678,7 +1678,7 @@ __device__ __forceinline__ void block_scan_i128(i128 (&v)[NV], i128 (&tot)[NV], 
 }
 
 template <bool ROOT>
-__global__ void __launch_bounds__(kSplitThreads)
+__global__ void __launch_bounds__(kSplitThreads, 4)   // 64 registers, no spills: 4 CTAs per SM
 k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const int *__restrict__ lvl_count,
              const HistTask *__restrict__ ht, long long *__restrict__ stage, long long *__restrict__ pool, int nf,
              const int32_t *__restrict__ fidx, const int32_t *__restrict__ counts,
