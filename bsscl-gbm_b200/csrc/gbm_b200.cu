@@ -824,6 +824,19 @@ bool full_spec(const gbm_params *P) { return P->grow_policy == 1 || P->max_depth
 // expanded on demand.
 int pool_depth(const gbm_params *P) { return full_spec(P) ? P->max_depth - 1 : 1 << 30; }
 
+// Best-first trees grown with full speculation skip the nodes the
+// reference's loop can never split (k_level_close) when the depth allows
+// many more splits than max_leaves - 1 (a depth-6, 63-leaf tree has nothing
+// to skip); GBM_PRUNE=0 keeps every node.
+bool prune_best_first(const gbm_params *P) {
+    static const bool on = [] {
+        const char *e = std::getenv("GBM_PRUNE");
+        return !(e && std::strcmp(e, "0") == 0);
+    }();
+    const long long splits = P->max_depth >= 40 ? (1ll << 40) : (1ll << P->max_depth) - 1;
+    return on && P->grow_policy == 0 && full_spec(P) && splits > 2ll * (P->max_leaves - 1);
+}
+
 int level_cap(const gbm_params *P) {
     if (P->grow_policy == 1) return 1 << std::min(P->max_depth - 1, 12);
     int m = std::max(1, P->max_leaves - 1);
@@ -1097,12 +1110,13 @@ int launch_close(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, bool ro
         TRY(launch(ctx, k_level_close<true>, dim3(1), dim3(kCloseThreads), 0, ctx->st,
             ctx->d_nodes, nullptr, nullptr, ctx->d_pool, ctx->d_stage, rf.nf, ctx->d_fidx, ctx->d_fbest, ctx->S, next,
             next_cnt, ints(ctx, I_NODES), ctx->nmax, level_cap(P), P->gamma, P->grow_policy == 0, pt,
-            ints(ctx, I_TILES), np.W_ub, lw, ctx->d_nleft));
+            ints(ctx, I_TILES), np.W_ub, lw, ctx->d_nleft, 0, (long long)P->min_samples_leaf, P->max_leaves));
     else
         TRY(launch(ctx, k_level_close<false>, dim3(1), dim3(kCloseThreads), 0, ctx->st, 
             ctx->d_nodes, lvl, lvl_cnt, ctx->d_pool, ctx->d_stage, rf.nf, ctx->d_fidx, ctx->d_fbest, ctx->S, next,
             next_cnt, ints(ctx, I_NODES), ctx->nmax, level_cap(P), P->gamma, P->grow_policy == 0, pt,
-            ints(ctx, I_TILES), np.W_ub, lw, ctx->d_nleft));
+            ints(ctx, I_TILES), np.W_ub, lw, ctx->d_nleft, prune_best_first(P) ? 1 : 0,
+            (long long)P->min_samples_leaf, P->max_leaves));
     return GBM_OK;
 }
 

@@ -69,6 +69,8 @@ struct DNode {
     int expanded;           // 1 once both children's results are final
     int nan_right;          // the best split sends the NaN bin (bin 0) right (learned direction)
     int pad;
+    double mg;              // best-first pruning: the smallest gain on the path of valid splits from
+                            // the root to this node, -inf when the path holds a split that cannot be made
 };
 
 // Row lists live in two buffers: the rows of a node at depth d are in

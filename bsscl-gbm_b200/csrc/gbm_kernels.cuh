@@ -920,6 +920,7 @@ __device__ __forceinline__ DNode fresh_node(int depth, int parent) {
     d.expanded = 0;
     d.nan_right = 0;
     d.pad = 0;
+    d.mg = -INFINITY;
     return d;
 }
 
@@ -1881,7 +1882,20 @@ k_split_bins(const DNode *__restrict__ nodes, const int *__restrict__ lvl, const
 //      level (`leafw`), its zeroed count/total words.
 // The staging totals of this level's tasks are zeroed (read for the last
 // time by the split search).
+//
+// Best-first pruning (prune != 0; full speculation only).  The reference's
+// loop (E:642-801) makes at most max_leaves - 1 splits and always splits the
+// candidate of largest gain.  When it picks a node v, every candidate then
+// has gain <= g(v), so every node w whose whole path from the root is made of
+// splits that can be made (gain > gamma, both children >= min_samples_leaf)
+// with gains > g(v) has been split before v, as have v's depth(v) ancestors.
+// So if depth(v) + #{such w, not ancestors of v} >= max_leaves - 1, v is
+// never split and needs no expansion: the replay of the grown table gives the
+// same tree.  mg (DNode) holds each expanded node's smallest path gain; a
+// node whose split cannot be made, or that was not expanded, has -inf.
+// Only nodes already partitioned (this level's parents and above) count.
 constexpr int kCloseThreads = 1024;
+constexpr int kPruneNodes = 2048;   // node tables up to this size are pruned
 
 template <bool ROOT>
 __global__ void __launch_bounds__(kCloseThreads)
@@ -1890,10 +1904,13 @@ k_level_close(DNode *__restrict__ nodes, const int *__restrict__ lvl, const int 
               const int32_t *__restrict__ fidx, const FBest *__restrict__ fbest, int S,
               int *__restrict__ next, int *__restrict__ next_count, int *__restrict__ node_count, int nmax, int M,
               double gamma, int use_gamma, PartTask *__restrict__ pt, int *__restrict__ tiles_total, int w_max,
-              long long *__restrict__ leafw, long long *__restrict__ nleft) {
+              long long *__restrict__ leafw, long long *__restrict__ nleft, int prune, long long msl,
+              int max_leaves) {
     griddep_wait();
     __shared__ double s_g[1024];
     __shared__ int s_id[1024];
+    __shared__ double s_mg[kPruneNodes];
+    __shared__ int s_par[kPruneNodes];
     __shared__ int s_cnt, s_W, s_base;
     __shared__ int s_w[32];
     const int W = ROOT ? 1 : *lvl_count;
@@ -1948,6 +1965,36 @@ k_level_close(DNode *__restrict__ nodes, const int *__restrict__ lvl, const int 
         s_id[cc] = ok ? id : -1;
     }
     __syncthreads();
+    const int ncount = *node_count;
+    if (!ROOT && prune && ncount <= kPruneNodes && ncount >= max_leaves - 1) {   // else nothing can be skipped
+        // this level's parents, partitioned by now: their smallest path gain
+        for (int k = threadIdx.x; k < W; k += kCloseThreads) {
+            DNode &p = nodes[lvl[k]];
+            const bool valid = p.feat >= 0 && p.gain > gamma && p.gnl >= msl && p.n - p.gnl >= msl;
+            const double up = p.parent >= 0 ? nodes[p.parent].mg : INFINITY;
+            p.mg = valid ? fmin(up, p.gain) : -INFINITY;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < ncount; i += kCloseThreads) {
+            s_mg[i] = nodes[i].mg;
+            s_par[i] = nodes[i].parent;
+        }
+        __syncthreads();
+        for (int cc = threadIdx.x; cc < C; cc += kCloseThreads) {
+            const int id = s_id[cc];
+            if (id < 0) continue;
+            const double g = s_g[cc];
+            int cnt = 0;
+            for (int i = 0; i < ncount; i++) cnt += s_mg[i] > g ? 1 : 0;
+            int depth = 0;
+            for (int a = s_par[id]; a >= 0; a = s_par[a]) {
+                cnt -= s_mg[a] > g ? 1 : 0;   // ancestors count once, in depth
+                depth++;
+            }
+            if (depth + cnt >= max_leaves - 1) s_id[cc] = -1;
+        }
+        __syncthreads();
+    }
     {
         int cap = (nmax - *node_count) / 2;
         int Mc = M < cap ? M : cap;

@@ -70,12 +70,15 @@ def test_build_tree_matches_oracle_exact(engine, case):
 
 
 @pytest.mark.parametrize("depth", [10, 14])
-@pytest.mark.parametrize("case", ["basic", "few_bins", "tied", "nan_heavy", "leaves4"])
+@pytest.mark.parametrize("case", ["basic", "few_bins", "tied", "nan_heavy", "leaves4", "gamma", "msl_big",
+                                  "mcw_big"])
 def test_build_tree_deep_matches_oracle_exact(engine, case, depth):
-    """Depth 10 expands every level in full (512 parents at the last split
-    level) and replays on the device; depth 14 ranks each level's
-    expansions (capped at max_leaves - 1) and replays on the host, expanding
-    on demand what the ranking left out.  The same bit-exact bar."""
+    """Depth 10 expands every level that the best-first loop can still reach
+    (full speculation, with the nodes it can provably never split left out:
+    a node is skipped once max_leaves - 1 splits are certain to come before
+    it) and replays on the device; depth 14 ranks each level's expansions
+    (capped at max_leaves - 1) and replays on the host, expanding on demand
+    what the ranking left out.  The same bit-exact bar."""
     from bsscl_gbm_b200 import binning
     d = golden("tree_" + case)
     counts = d["counts"]
