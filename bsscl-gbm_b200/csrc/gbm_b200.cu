@@ -598,7 +598,22 @@ cudaError_t launch_predict(const uint8_t *xr, int64_t n, int p, const void *node
                            const int32_t *off, const int32_t *dep, int ntree, const int4 *cstart,
                            const int32_t *nchunk, double lr, double base, double *F, double *P,
                            const int32_t *bigidx, const uint32_t *topbits, cudaStream_t st, bool packed_nr = true) {
-    const PredShape sh = predict_shape(p, packed);
+    PredShape sh = predict_shape(p, packed);
+    if (sh.stage_rows && n > 0) {
+        // whole waves: the fewest waves of full SMs at the shape's rows per
+        // CTA, then the rows spread evenly over them (a multiple of 32 rows
+        // per CTA, at most the shape's)
+        int dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int per_sm = std::max<int>(1, std::min<int>(2048 / kPredThreads, (int)((228 * 1024) / (sh.smem + 1024))));
+        const int64_t slots = (int64_t)std::max(1, sms) * per_sm;
+        const int64_t waves = (n + slots * sh.rpc - 1) / (slots * sh.rpc);
+        const int64_t even = ((n + waves * slots - 1) / (waves * slots) + 31) / 32 * 32;
+        if (even < sh.rpc) {
+            sh.rpc = (int)std::max<int64_t>(32, even);
+            sh.smem = predict_smem(sh.rpc, p, packed);
+        }
+    }
     const unsigned grid = (unsigned)((n + sh.rpc - 1) / sh.rpc);
 #define GBM_PRED(R, K, S, N) launch_predict_t<R, K, S, N>(sh, grid, xr, n, p, nodes, vals, off, dep, ntree, cstart, nchunk, lr, base, F, P, bigidx, topbits, st)
     if (packed) {   // NaN-right splits in the packed words: the walk's extra step only when the model has some
