@@ -111,7 +111,6 @@ struct gbm_ctx {
     // 1110 rounds/s, 0 levels 1077, all levels 1057.
     bool hist_compact = true;          // histograms on the round's packed feature blocks (k_compact_feat)
     int hist_seg_cost = 150000;        // k_hist3's cost of a segment in row units (22 per row; measured)
-    bool hist_wide = false;            // k_hist3 with 64-bit shared-memory atomics (GBM_HIST_WIDE)
     int nf_cap = 0;
     long long *d_pool = nullptr;       // node histograms: slot i = node i
     long long *d_lpool = nullptr;      // several ranks: this rank's partial histograms, slot i = node i
@@ -1073,14 +1072,14 @@ int launch_hist(gbm_ctx *ctx, const RoundFeat &rf, const int *ntask_p) {
     long long *stage = ctx->p2p ? ctx->d_pst : ctx->d_stage;
     const unsigned long long *par = (const unsigned long long *)(ctx->p2p ? ctx->d_sync + ctx->p2p_n + kSyncLevel
                                                                           : nullptr);
-    const size_t hsm = (size_t)(ctx->hist_wide ? kAccWideWords : kAccV3Words) * sizeof(unsigned);
+    const size_t hsm = (size_t)kAccV3Words * sizeof(unsigned);
     const uint8_t *hx = compact_hist(ctx) ? ctx->xc_cur : ctx->d_xb;
-#define GBM_HIST3(C, W)                                                                                       \
-    launch(ctx, k_hist3<C, W>, dim3(ctx->sms), dim3(kHistV3Threads), hsm, ctx->st, hx, ctx->n, ctx->d_rows,   \
+#define GBM_HIST3(C)                                                                                          \
+    launch(ctx, k_hist3<C>, dim3(ctx->sms), dim3(kHistV3Threads), hsm, ctx->st, hx, ctx->n, ctx->d_rows,      \
            ctx->d_tmp, ctx->d_htask, ctx->d_hprefix, ntask_p, ctx->d_blist, d_nb, ctx->d_fpos, rf.nf, ctx->d_q, \
            stage, par, ctx->pst_stride, ctx->hist_seg_cost)
-    if (compact_hist(ctx)) TRY(ctx->hist_wide ? GBM_HIST3(true, true) : GBM_HIST3(true, false));
-    else TRY(ctx->hist_wide ? GBM_HIST3(false, true) : GBM_HIST3(false, false));
+    if (compact_hist(ctx)) TRY(GBM_HIST3(true));
+    else TRY(GBM_HIST3(false));
 #undef GBM_HIST3
     if (ctx->nbig)   // bin 256 of the 257-bin features, into the top cells
         TRY(launch(ctx, k_hist_top, dim3(ctx->nbig), dim3(128), 0, ctx->st, (const int32_t *)ctx->d_rows,
@@ -2060,15 +2059,10 @@ int gbm_ctx_create(int32_t device, gbm_ctx **out) {
     ctx->hist_grid = 2 * ctx->sms;
     if (const char *e = std::getenv("GBM_HIST_COMPACT")) ctx->hist_compact = std::atoi(e) != 0;
     if (const char *e = std::getenv("GBM_HIST_SEG_COST")) ctx->hist_seg_cost = std::max(0, std::atoi(e));
-    if (const char *e = std::getenv("GBM_HIST_WIDE")) ctx->hist_wide = std::atoi(e) != 0;
-    CK(cudaFuncSetAttribute(k_hist3<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    CK(cudaFuncSetAttribute(k_hist3<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             (int)(kAccV3Words * sizeof(unsigned))));
-    CK(cudaFuncSetAttribute(k_hist3<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    CK(cudaFuncSetAttribute(k_hist3<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             (int)(kAccV3Words * sizeof(unsigned))));
-    CK(cudaFuncSetAttribute(k_hist3<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            (int)(kAccWideWords * sizeof(unsigned))));
-    CK(cudaFuncSetAttribute(k_hist3<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            (int)(kAccWideWords * sizeof(unsigned))));
     CK(cudaFuncSetAttribute(k_compact_feat, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     // a function attribute is shared by every context of the process: set
     // the largest node-table copy any context may launch with

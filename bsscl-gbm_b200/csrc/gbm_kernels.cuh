@@ -703,17 +703,11 @@ constexpr int kChunk3 = 32768;
 constexpr int kBinsV3 = kBins + 1;                   // + the trash bin
 constexpr int kDigV3 = kBinsV3 * 2 * kBlk;           // words between two digits
 constexpr int kAccV3Words = 6 * kDigV3;              // 197,376 bytes
-// WIDE: one 64-bit shared-memory atomic per quantity instead of three digits.
-// |q| < 2^48 (the exponent's bound), so a run of 16,384 rows sums to less
-// than 2^62 in one int64 cell; two cells (g, h) per (bin, half, feature).
-constexpr int kChunkWide = 16384;
-constexpr int kQWide = kBinsV3 * 2 * kBlk;           // 64-bit words between g and h
-constexpr int kAccWideWords = 2 * 2 * kQWide;        // in 32-bit words: 131,584 bytes
 
 // COMPACT: xb is the round's packed blocks (k_compact_feat): block bi holds
 // feature positions 16 bi .. 16 bi + 15, every slot below nf selected; the
 // physical block list and feature positions are not read.
-template <bool COMPACT, bool WIDE>
+template <bool COMPACT>
 __global__ void __launch_bounds__(kHistV3Threads, 1)
 k_hist3(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
         const int32_t *__restrict__ rows1, const HistTask *__restrict__ tasks, const int32_t *__restrict__ rpre,
@@ -790,12 +784,11 @@ k_hist3(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ r
             const HistTask tk = tasks[t];
             const int32_t *__restrict__ rows = tk.buf ? rows1 : rows0;
             const int pe = min(k1, t1);
-            constexpr int kRun = WIDE ? kChunkWide : kChunk3;
-            const bool single = k == t0 && pe == t1 && (t1 - t0) <= kRun;
+            const bool single = k == t0 && pe == t1 && (t1 - t0) <= kChunk3;
             long long *dst = stage_hist + (int64_t)tk.stage * slot_words;
-            for (int c0 = k; c0 < pe; c0 += kRun) {
-                const int c1 = min(pe, c0 + kRun);
-                for (int i = threadIdx.x; i < (WIDE ? kAccWideWords : kAccV3Words) / 4; i += blockDim.x)
+            for (int c0 = k; c0 < pe; c0 += kChunk3) {
+                const int c1 = min(pe, c0 + kChunk3);
+                for (int i = threadIdx.x; i < kAccV3Words / 4; i += blockDim.x)
                     reinterpret_cast<uint4 *>(acc)[i] = make_uint4(0u, 0u, 0u, 0u);
                 __syncthreads();
                 const int r0 = (int)tk.begin + (c0 - t0), r1 = (int)tk.begin + (c1 - t0);
@@ -814,18 +807,6 @@ k_hist3(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ r
                     tg += qq.x;
                     th += qq.y;
                     // an invalid lane adds zeros (its q is 0) into real cells: harmless
-                    if (WIDE) {
-                        unsigned long long *my64 = reinterpret_cast<unsigned long long *>(acc) + half * kBlk;
-                        const uint4 vr = rot_bytes(v, fl);
-#pragma unroll
-                        for (int k = 0; k < kBlk; k++) {
-                            const unsigned b = ((unsel >> k) & 1u) ? (unsigned)kBins : byte_of(vr, k);
-                            unsigned long long *cc = my64 + b * (2 * kBlk) + ((fl + k) & (kBlk - 1));
-                            atomicAdd(cc, (unsigned long long)qq.x);
-                            atomicAdd(cc + kQWide, (unsigned long long)qq.y);
-                        }
-                        continue;
-                    }
                     const unsigned dg0 = (unsigned)qq.x & 0x1ffffu, dg1 = (unsigned)(qq.x >> kDig) & 0x1ffffu,
                                    dg2 = (unsigned)(int)(qq.x >> (2 * kDig));
                     const unsigned dh0 = (unsigned)qq.y & 0x1ffffu, dh1 = (unsigned)(qq.y >> kDig) & 0x1ffffu,
@@ -879,15 +860,6 @@ k_hist3(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ r
 #pragma unroll
                 for (int i = 0; i < kBins / (kHistV3Threads / 32); i++) {
                     const int b = warp + i * (kHistV3Threads / 32);
-                    if (WIDE) {   // the halves' two int64 cells; their sum as (hi, lo) words
-                        const long long *d64 = reinterpret_cast<const long long *>(acc) + (b * 2 + half) * kBlk + fl;
-                        const long long g = d64[0], h = d64[kQWide];
-                        const long long r = __shfl_xor_sync(0xffffffffu, half ? g : h, 16);
-                        const i128 tot = (i128)(half ? h : g) + (i128)r;
-                        fw[2 * i] = (long long)(tot >> 32);
-                        fw[2 * i + 1] = (long long)(tot & 0xffffffff);
-                        continue;
-                    }
                     const unsigned *d = acc + (b * 2 + half) * kBlk + fl;
                     const unsigned g0 = d[0], g1 = d[kDigV3], g2 = d[2 * kDigV3];
                     const unsigned h0 = d[3 * kDigV3], h1 = d[4 * kDigV3], h2 = d[5 * kDigV3];
