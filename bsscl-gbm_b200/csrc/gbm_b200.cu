@@ -1245,7 +1245,8 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
                (const int *)ints(ctx, I_TILES), ctx->d_tile_st, (unsigned *)ints(ctx, I_TICKET),
                ints(ctx, I_PART_ERR), ctx->d_nleft, (const int32_t *)ctx->d_bigidx,
                (const uint32_t *)ctx->d_topbits, ctx->d_nodes, (const int *)lvl, gl, ctx->d_htask, ctx->d_hprefix,
-               (unsigned *)ints(ctx, I_DONE)));
+               (unsigned *)ints(ctx, I_DONE), prune_best_first(P) && !ctx->comm ? 1 : 0,
+               (const int *)ints(ctx, I_NODES), P->gamma, (long long)P->min_samples_leaf, P->max_leaves));
     TRY(launch_hist(ctx, rf, lvl_cnt));
     if (ctx->comm) {
         const int cx = std::max(1, (2 * ctx->hist_grid + W_ub - 1) / W_ub);

@@ -1024,6 +1024,62 @@ __device__ __forceinline__ int find_task_by_tile(const PartTask *tasks, int ntas
     return lo;
 }
 
+// Best-first pruning after a level's partition (one rank, full speculation;
+// the rule of k_level_close, stronger here because this level's parents are
+// partitioned too, so their own splits count): a parent the reference's loop
+// can never split -- too many splits certain to come first, or a split that
+// cannot be made (min_samples_leaf, gain <= gamma) on its path -- leaves the
+// level list before its children are histogrammed or searched.  Returns the new list length; s_orig[k] is the
+// kept parent k's index in the old list.  W <= kPruneList.
+constexpr int kPruneList = 1024;
+constexpr int kPruneTable = 2048;
+__device__ int prune_parents(DNode *__restrict__ nodes, int *__restrict__ lvl, int W,
+                             const long long *__restrict__ gnl_of, int ncount, double gamma, long long msl,
+                             int max_leaves, double *s_mg, int *s_par, int *s_orig, int *s_w) {
+    for (int k = threadIdx.x; k < W; k += blockDim.x) {
+        DNode &p = nodes[lvl[k]];
+        const long long gnl = gnl_of[k];
+        const bool valid = p.feat >= 0 && p.gain > gamma && gnl >= msl && p.n - gnl >= msl;
+        const double up = p.parent >= 0 ? nodes[p.parent].mg : INFINITY;
+        p.mg = valid ? fmin(up, p.gain) : -INFINITY;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < ncount; i += blockDim.x) {
+        s_mg[i] = nodes[i].mg;
+        s_par[i] = nodes[i].parent;
+    }
+    __syncthreads();
+    int carry = 0;
+    for (int b0 = 0; b0 < W; b0 += blockDim.x) {
+        const int k = b0 + threadIdx.x;
+        int keep = 0, id = -1;
+        if (k < W) {
+            id = lvl[k];
+            const double g = nodes[id].gain;
+            int cnt = 0;
+            for (int i = 0; i < ncount; i++) cnt += s_mg[i] > g ? 1 : 0;
+            cnt -= s_mg[id] > g ? 1 : 0;                 // not the node itself
+            int depth = 0;
+            for (int a = s_par[id]; a >= 0; a = s_par[a]) {
+                cnt -= s_mg[a] > g ? 1 : 0;           // ancestors count once, in depth
+                depth++;
+            }
+            // a parent whose split cannot be made, or that sits under one, is never split either
+            keep = s_mg[id] > -INFINITY && depth + cnt < max_leaves - 1 ? 1 : 0;
+        }
+        int tot;
+        const int e = block_excl_scan(keep, s_w, tot);
+        if (keep) s_orig[carry + e] = k;
+        carry += tot;
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < carry; k += blockDim.x) s_par[k] = lvl[s_orig[k]];   // the kept ids
+    __syncthreads();
+    for (int k = threadIdx.x; k < carry; k += blockDim.x) lvl[k] = s_par[k];
+    __syncthreads();
+    return carry;
+}
+
 // Level plan after the partition: each parent's smaller child (by global
 // count) becomes a histogram task; the children get their row ranges.
 // gl == null (several ranks): each rank histograms its locally smaller child;
@@ -1032,7 +1088,8 @@ __device__ __forceinline__ int find_task_by_tile(const PartTask *tasks, int ntas
 // One CTA (the last of k_partition to finish) runs it.
 __device__ void plan_hist_block(DNode *__restrict__ nodes, const int *__restrict__ lvl, int W,
                                 const long long *__restrict__ nl_local, const long long *__restrict__ gl,
-                                HistTask *__restrict__ ht, int32_t *__restrict__ prefix, int *s_w) {
+                                HistTask *__restrict__ ht, int32_t *__restrict__ prefix, int *s_w,
+                                const int *s_orig = nullptr) {
     int carry = 0;
     for (int b0 = 0; b0 < W; b0 += blockDim.x) {
         int k = b0 + threadIdx.x;
@@ -1040,8 +1097,9 @@ __device__ void plan_hist_block(DNode *__restrict__ nodes, const int *__restrict
         if (k < W) {
             int i = lvl[k];
             DNode &p = nodes[i];
-            long long nl = nl_local[k];
-            long long gnl = gl ? gl[k] : nl, gtot = gl ? p.n : p.end - p.begin;
+            const int ko = s_orig ? s_orig[k] : k;   // the parent's index in the partition's list
+            long long nl = nl_local[ko];
+            long long gnl = gl ? gl[ko] : nl, gtot = gl ? p.n : p.end - p.begin;
             bool ls = gnl <= gtot - gnl;
             HistTask t;
             t.begin = ls ? p.begin : p.begin + nl;
@@ -1097,7 +1155,8 @@ k_partition(const uint8_t *__restrict__ xb, int64_t n, int32_t *__restrict__ row
             unsigned long long *__restrict__ tile_st, unsigned *__restrict__ ticket, int *__restrict__ err,
             long long *__restrict__ n_left, const int32_t *__restrict__ bigidx, const uint32_t *__restrict__ topbits,
             DNode *__restrict__ nodes, const int *__restrict__ lvl, const long long *__restrict__ gl,
-            HistTask *__restrict__ ht, int32_t *__restrict__ prefix, unsigned *__restrict__ done) {
+            HistTask *__restrict__ ht, int32_t *__restrict__ prefix, unsigned *__restrict__ done, int prune,
+            const int *__restrict__ node_count, double gamma, long long msl, int max_leaves) {
     griddep_wait();
     constexpr int J = kPartTile / kPartThreads;
     constexpr int NW = kPartTile / 32;   // ballot words of a tile
@@ -1215,7 +1274,19 @@ k_partition(const uint8_t *__restrict__ xb, int64_t n, int32_t *__restrict__ row
         *done = 0;
         *ticket = 0;
     }
-    plan_hist_block(nodes, lvl, *ntask_p, n_left, gl, ht, prefix, s_w);
+    const int W = *ntask_p;
+    const int ncount = prune ? *node_count : 0;
+    if (prune && gl && W <= kPruneList && ncount <= kPruneTable && ncount >= max_leaves) {
+        __shared__ double s_mg[kPruneTable];
+        __shared__ int s_par[kPruneTable];
+        __shared__ int s_orig[kPruneList];
+        const int W2 = prune_parents(nodes, const_cast<int *>(lvl), W, gl, ncount, gamma, msl, max_leaves, s_mg,
+                                     s_par, s_orig, s_w);
+        if (threadIdx.x == 0) *const_cast<int *>(ntask_p) = W2;
+        plan_hist_block(nodes, lvl, W2, n_left, gl, ht, prefix, s_w, s_orig);
+        return;
+    }
+    plan_hist_block(nodes, lvl, W, n_left, gl, ht, prefix, s_w);
 }
 
 
