@@ -381,6 +381,93 @@ def _partition_restated(rows, left, begin, end, tile=4096, threads=512):
     return out[begin:end], lcar
 
 
+def _best_first_splits(gain, valid, kids, max_leaves, gamma):
+    """The reference's best-first loop (E:642-801) over a fully grown tree:
+    split the candidate of largest gain (> gamma) while fewer than
+    max_leaves - 1 splits are made; a split that cannot be made (min_samples_leaf)
+    turns the candidate into a leaf.  Returns the nodes split."""
+    cand, done = [0], []
+    while len(done) < max_leaves - 1:
+        live = [c for c in cand if gain[c] > gamma]
+        if not live:
+            break
+        best = max(gain[c] for c in live)
+        v = min(c for c in live if gain[c] == best)
+        cand.remove(v)
+        if not valid[v] or kids[v] is None:
+            continue
+        done.append(v)
+        cand.extend(kids[v])
+    return set(done)
+
+
+def _prunable(v, gain, valid, parent, depth, known, max_leaves, gamma):
+    """k_level_close / k_partition's rule for node v, counting only the nodes
+    whose splits are known (`known`): v is skipped when its depth plus the
+    other known nodes whose whole path is of makeable splits with gains above
+    v's reach max_leaves - 1."""
+    def mg(w):
+        m = np.inf
+        while w >= 0:
+            if not (known[w] and valid[w] and gain[w] > gamma):
+                return -np.inf
+            m = min(m, gain[w])
+            w = parent[w]
+        return m
+    anc = set()
+    a = parent[v]
+    while a >= 0:
+        anc.add(a)
+        a = parent[a]
+    cnt = sum(1 for w in range(len(gain)) if w != v and w not in anc and known[w] and mg(w) > gain[v])
+    return depth[v] + cnt >= max_leaves - 1
+
+
+def _prune_case(seed):
+    """One random complete tree and the pruning rule checked on it; returns
+    how many (node, stage) pairs the rule skipped."""
+    rng = np.random.default_rng(seed)
+    D = int(rng.integers(5, 9))
+    N = 2 ** (D + 1) - 1
+    parent = np.array([-1] + [(i - 1) // 2 for i in range(1, N)])
+    depth = np.array([int(np.floor(np.log2(i + 1))) for i in range(N)])
+    gain = np.round(rng.exponential(1.0, N) * np.exp(-0.3 * depth), 1)   # rounding makes ties
+    valid = rng.random(N) > 0.1
+    kids = [(2 * i + 1, 2 * i + 2) if 2 * i + 2 < N else None for i in range(N)]
+    max_leaves = int(rng.integers(3, 40))
+    gamma = float(rng.choice([0.0, 0.2]))
+    split = _best_first_splits(gain, valid, kids, max_leaves, gamma)
+    skipped = 0
+    for v in range(1, N):
+        at_close = depth < depth[v]     # partitioned when v's parent level closes
+        after_part = depth <= depth[v]  # v's own level partitioned too
+        for known in (at_close, after_part):
+            if _prunable(v, gain, valid, parent, depth, known, max_leaves, gamma):
+                assert v not in split, (seed, v)
+                skipped += 1
+        # after the partition a parent under (or with) a split that cannot be made drops out too
+        w, reach = v, True
+        while w >= 0:
+            reach &= bool(valid[w] and gain[w] > gamma)
+            w = parent[w]
+        if not reach:
+            assert v not in split, (seed, v)
+    return skipped
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_best_first_pruning_never_skips_a_node_the_loop_splits(seed):
+    """On random complete trees (depth 5-8, ties, unmakeable splits, gains
+    that rise below their parents), every node the pruning rule skips -- with
+    the nodes above its level known (the level close) or its own level too
+    (after the partition) -- is one the best-first loop never splits."""
+    _prune_case(seed)
+
+
+def test_best_first_pruning_is_not_vacuous():
+    assert sum(_prune_case(seed) for seed in range(40)) > 100
+
+
 @pytest.mark.parametrize("size", [1, 31, 4096, 4097, 20_000])
 def test_partition_index_arithmetic_is_a_monotonic_permutation(size):
     """Every row lands once inside the task's range, the lefts first in list
