@@ -2281,31 +2281,17 @@ k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_coun
     auto cand_key = [&](const RNode &x) -> unsigned long long {
         return (x.feat >= 0 && x.gain > P.gamma) ? order_key(x.gain) : 0ull;
     };
-    // Slot s's key lives in lane s % 32, register s / 32; which slots are
-    // occupied is a bit map every lane holds alike (occ), so the two lowest
-    // free slots come from bit scans with no warp vote.
     unsigned long long key[5];
-    unsigned occ[5];
+    unsigned act = 0;                                            // bit r: slot lane + 32 r is active
 #pragma unroll
-    for (int r = 0; r < 5; r++) {
-        key[r] = 0ull;
-        occ[r] = 0u;
-    }
-    occ[0] = 1u;
+    for (int r = 0; r < 5; r++) key[r] = 0ull;
     if (lane == 0) {
         c_node[0] = 0;
         c_nid[0] = 0;
         key[0] = cand_key(r0);
+        act = 1u;
     }
     __syncwarp();
-    // (registers indexed only by unrolled constants, so key and occ stay in registers)
-#define GBM_SET_KEY(slot, k)                                                        \
-    _Pragma("unroll") for (int r_ = 0; r_ < 5; r_++)                               \
-        if (lane == ((slot) & 31) && r_ == ((slot) >> 5)) key[r_] = (k);
-#define GBM_SET_OCC(slot, on)                                                       \
-    _Pragma("unroll") for (int r_ = 0; r_ < 5; r_++)                               \
-        if (r_ == ((slot) >> 5))                                                   \
-            occ[r_] = (on) ? (occ[r_] | (1u << ((slot) & 31))) : (occ[r_] & ~(1u << ((slot) & 31)));
     int nc = 1, n_splits = 0, status = 0;
     while (n_splits < P.max_leaves - 1) {
         unsigned long long bk = 0ull;
@@ -2321,10 +2307,12 @@ k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_coun
         const RNode pn = sn[c_nid[ci]];
         if (!pn.expanded) { status = 1; break; }
         const long long gnl = sn[pn.kid0].n, gnr = sn[pn.kid1].n;
+        const int own = ci & 31, orr = ci >> 5;
         if (gnl < P.msl || gnr < P.msl) {                        // E:678-683
             if (lane == 0) { tf[cur] = -1; tv[cur] = pn.val; }
-            GBM_SET_KEY(ci, 0ull)
-            GBM_SET_OCC(ci, false)
+#pragma unroll
+            for (int r = 0; r < 5; r++)
+                if (lane == own && r == orr) { key[r] = 0ull; act &= ~(1u << r); }
             __syncwarp();
             continue;
         }
@@ -2332,11 +2320,13 @@ k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_coun
         int ss = -1, sl = -1;
 #pragma unroll
         for (int r = 0; r < 5; r++) {
-            const int lo_ = 32 * r;   // the slots below MAXC
-            unsigned m = ~occ[r] & (MAXC >= lo_ + 32 ? 0xffffffffu : (MAXC > lo_ ? (1u << (MAXC - lo_)) - 1u : 0u));
-            if (r == (ci >> 5)) m &= ~(1u << (ci & 31));
-            if (ss < 0 && m) { ss = 32 * r + __ffs(m) - 1; m &= m - 1; }
-            if (ss >= 0 && sl < 0 && m) sl = 32 * r + __ffs(m) - 1;
+            const int s = lane + 32 * r;
+            unsigned m = __ballot_sync(full, s < MAXC && s != ci && !((act >> r) & 1u));
+            while (m && sl < 0) {
+                const int b = __ffs(m) - 1;
+                m &= m - 1;
+                if (ss < 0) ss = 32 * r + b; else sl = 32 * r + b;
+            }
         }
         if (ss < 0 || sl < 0) { status = 2; break; }            // cannot happen: >= 3 slots are free
         const int lid = nc, rid = nc + 1;
@@ -2353,20 +2343,19 @@ k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_coun
             c_nid[sl] = kid_l;
         }
         const unsigned long long ks = cand_key(sn[kid_s]), kl = cand_key(sn[kid_l]);
-        GBM_SET_KEY(ci, 0ull)
-        GBM_SET_KEY(ss, ks)
-        GBM_SET_KEY(sl, kl)
-        GBM_SET_OCC(ci, false)
-        GBM_SET_OCC(ss, true)
-        GBM_SET_OCC(sl, true)
+#pragma unroll
+        for (int r = 0; r < 5; r++) {
+            const int s = lane + 32 * r;
+            if (s == ci) { key[r] = 0ull; act &= ~(1u << r); }
+            if (s == ss) { key[r] = ks; act |= 1u << r; }
+            if (s == sl) { key[r] = kl; act |= 1u << r; }
+        }
         __syncwarp();
     }
-#undef GBM_SET_KEY
-#undef GBM_SET_OCC
     if (!status) {
 #pragma unroll
         for (int r = 0; r < 5; r++) {
-            if ((occ[r] >> lane) & 1u) {
+            if ((act >> r) & 1u) {
                 const int s = lane + 32 * r;
                 tf[c_node[s]] = -1;
                 tv[c_node[s]] = sn[c_nid[s]].val;
