@@ -431,14 +431,16 @@ class Engine:
         """n_rounds rounds queued back to back (gbm_fit_rounds): a list of
         (tree, train_loss), the same as n_rounds round_sampled calls."""
         n_rounds = int(n_rounds)
-        arrays = []
-        outs = (GbmTreeOut * max(1, n_rounds))()
+        R = max(1, n_rounds)
+        # one block per field, a row per round (few allocations for long fits)
+        blocks = (np.empty((R, capacity), np.int32), np.empty((R, capacity), np.int64),
+                  np.empty((R, capacity), np.float64), np.empty((R, capacity), np.int32),
+                  np.empty((R, capacity), np.int32), np.empty((R, capacity), np.float64),
+                  np.empty((R, capacity), np.int32) if params.nan_direction else None)
+        arrays = [tuple(b[r] if b is not None else None for b in blocks) for r in range(n_rounds)]
+        outs = (GbmTreeOut * R)()
         for r in range(n_rounds):
-            a = (np.empty(capacity, np.int32), np.empty(capacity, np.int64),
-                 np.empty(capacity, np.float64), np.empty(capacity, np.int32),
-                 np.empty(capacity, np.int32), np.empty(capacity, np.float64),
-                 np.empty(capacity, np.int32) if params.nan_direction else None)
-            arrays.append(a)
+            a = arrays[r]
             outs[r] = GbmTreeOut(capacity, ptr(a[0]), ptr(a[1]), ptr(a[2]), ptr(a[3]), ptr(a[4]),
                                  ptr(a[5]), 0, None, ptr(a[6]))
         losses = np.zeros(max(1, n_rounds), np.float64)

@@ -259,12 +259,12 @@ struct gbm_ctx {
 
 namespace {
 
-// d_ints: I_DONE / I_DONE_UPD count finished CTAs of k_partition / k_update;
-// I_TICKET hands out k_partition's tiles in order; I_PART_ERR records a
-// partition look-back wait that ran out
-// (the last one runs the tail and resets it)
+// d_ints: I_DONE / I_DONE_UPD / I_DONE_LEAF count finished CTAs of
+// k_partition / k_update / k_leaf_totals (the last one runs the tail and
+// resets it); I_TICKET hands out k_partition's tiles in order; I_PART_ERR
+// records a partition look-back wait that ran out
 enum { I_ONE = 0, I_NODES = 1, I_TILES = 2, I_LVL0 = 3, I_LVL1 = 4, I_DONE = 5, I_DONE_UPD = 6, I_TICKET = 7,
-       I_PART_ERR = 8, I_COUNT = 10 };
+       I_PART_ERR = 8, I_DONE_LEAF = 9, I_COUNT = 10 };
 
 int fail(gbm_ctx *c, int code, const char *fmt, ...) {
     char buf[512];
@@ -1232,10 +1232,14 @@ int launch_level(gbm_ctx *ctx, const RoundFeat &rf, const gbm_params *P, int *lv
                                                               ctx->d_ptask, lvl_cnt,
                                                               ints(ctx, I_TILES), ctx->d_q, ctx->d_leafw,
                                                               ctx->d_nleft, (const int32_t *)ctx->d_bigidx,
-                                                              (const uint32_t *)ctx->d_topbits));
-        if (ctx->comm)
+                                                              (const uint32_t *)ctx->d_topbits,
+                                                              ctx->comm ? nullptr : (unsigned *)ints(ctx, I_DONE_LEAF),
+                                                              ctx->d_nodes, (const int *)lvl, ctx->S));
+        if (ctx->comm) {   // summed over ranks first (one rank: k_leaf_totals' last CTA finished them)
             TRY(allreduce_i64(ctx, ctx->d_leafw, (int64_t)kLeafWords * W_ub));
-        TRY(launch(ctx, k_leaf_finish, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, lvl, lvl_cnt, ctx->d_leafw, ctx->d_nleft, ctx->S));
+            TRY(launch(ctx, k_leaf_finish, dim3(1), dim3(256), 0, ctx->st, ctx->d_nodes, lvl, lvl_cnt, ctx->d_leafw,
+                       ctx->d_nleft, ctx->S));
+        }
         ctx->waves++;
         return GBM_OK;
     }
@@ -2048,8 +2052,9 @@ int gbm_ctx_create(int32_t device, gbm_ctx **out) {
     *out = ctx;
     CK(cudaSetDevice(device));
     // Both streams at the default priority: a high-priority engine stream
-    // measured slower (config 5: histograms 4.27 -> 5.53 ms per round), the
-    // sampler stream's packing then running late into the next round.
+    // measured slower on config 5 (6.67 -> 8.10 ms per round, the sampler
+    // stream's packing then running late into the next round) and the same
+    // on config 4 (0.739 against 0.741 ms).
     CK(cudaStreamCreateWithFlags(&ctx->st, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&ctx->cst, cudaStreamNonBlocking));
     for (auto &e : ctx->rows_freeP) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));

@@ -1613,93 +1613,115 @@ __global__ void k_fill_counts(DNode *__restrict__ nodes, const int *__restrict__
 // lo, hR hi lo, nL] int64 words, summed exactly over CTAs (and ranks).
 constexpr int kLeafWords = 9;
 
+// The last level's children from those sums (the same rounding as every
+// other node: exact integer total -> float64 -> * 2^-S).  Reads through L2:
+// the sums come from other CTAs' atomics.
+__device__ __forceinline__ void leaf_finish_one(DNode *__restrict__ nodes, const int *__restrict__ lvl, int k,
+                                                const long long *__restrict__ words,
+                                                const long long *__restrict__ nl_local, double sc) {
+    const long long *o = words + (int64_t)k * kLeafWords;
+    DNode &p = nodes[lvl[k]];
+    const long long nl = __ldcg(nl_local + k), gnl = __ldcg(o + 8);
+    DNode &a = nodes[p.kid0];
+    DNode &c = nodes[p.kid1];
+    a.begin = p.begin;
+    a.end = p.begin + nl;
+    a.n = gnl;
+    c.begin = p.begin + nl;
+    c.end = p.end;
+    c.n = p.n - gnl;
+    a.G = __dmul_rn(i128_to_double(cell(__ldcg(o + 0), __ldcg(o + 1))), sc);
+    a.H = __dmul_rn(i128_to_double(cell(__ldcg(o + 2), __ldcg(o + 3))), sc);
+    c.G = __dmul_rn(i128_to_double(cell(__ldcg(o + 4), __ldcg(o + 5))), sc);
+    c.H = __dmul_rn(i128_to_double(cell(__ldcg(o + 6), __ldcg(o + 7))), sc);
+    a.feat = c.feat = -1;
+    a.bin = c.bin = 0;
+    a.gain = c.gain = -1.0;
+    p.nl = nl;
+    p.gnl = gnl;
+    p.left_small = gnl <= p.n - gnl;
+    p.expanded = 1;
+}
+
+// With `done` (one rank: nothing to sum over ranks in between) the last CTA
+// to finish also finishes the children (leaf_finish_one) and resets *done;
+// with several ranks k_leaf_finish does that after the exchange.
 __global__ void __launch_bounds__(kPartThreads)
 k_leaf_totals(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ rows0,
               const int32_t *__restrict__ rows1, const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p,
               const int *__restrict__ tiles_total, const longlong2 *__restrict__ q,
               long long *__restrict__ words, long long *__restrict__ n_left, const int32_t *__restrict__ bigidx,
-              const uint32_t *__restrict__ topbits) {
+              const uint32_t *__restrict__ topbits, unsigned *__restrict__ done, DNode *__restrict__ nodes,
+              const int *__restrict__ lvl, int S) {
     griddep_wait();
     __shared__ long long s[5][kPartThreads / 32];
+    __shared__ int s_last;
     const int tile = blockIdx.x;
-    if (tile >= *tiles_total) return;
-    const int t = find_task_by_tile(tasks, *ntask_p, tile);
-    const PartTask tk = tasks[t];
-    const int32_t *__restrict__ rows = tk.src ? rows1 : rows0;
-    const long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
-    const int m = (int)min((long long)kPartTile, tk.end - r0);
-    constexpr int J = kPartTile / kPartThreads;
-    int rw[J];
+    if (tile < *tiles_total) {   // CTAs past the level's tiles still count in *done
+        const int t = find_task_by_tile(tasks, *ntask_p, tile);
+        const PartTask tk = tasks[t];
+        const int32_t *__restrict__ rows = tk.src ? rows1 : rows0;
+        const long long r0 = tk.begin + (long long)(tile - tk.tile0) * kPartTile;
+        const int m = (int)min((long long)kPartTile, tk.end - r0);
+        constexpr int J = kPartTile / kPartThreads;
+        int rw[J];
 #pragma unroll
-    for (int j = 0; j < J; j++) {
-        const int o = threadIdx.x + j * kPartThreads;
-        rw[j] = o < m ? rows[r0 + o] : -1;
-    }
-    long long v[5] = {0, 0, 0, 0, 0};   // gL hL gR hR nL; |sum| < 4096 * 2^48
+        for (int j = 0; j < J; j++) {
+            const int o = threadIdx.x + j * kPartThreads;
+            rw[j] = o < m ? rows[r0 + o] : -1;
+        }
+        long long v[5] = {0, 0, 0, 0, 0};   // gL hL gR hR nL; |sum| < 4096 * 2^48
 #pragma unroll
-    for (int j = 0; j < J; j++) {
-        if (rw[j] < 0) continue;
-        const longlong2 qq = __ldg(q + rw[j]);
-        const bool left = goes_left(bin_of(xb, n, rw[j], tk.feat), tk.thr, tk.nan_right) &&
-                          !(tk.thr >= 255 && top_bit(topbits, (n + 31) >> 5, bigidx[tk.feat], rw[j]));
-        v[left ? 0 : 2] += qq.x;
-        v[left ? 1 : 3] += qq.y;
-        v[4] += left;
-    }
+        for (int j = 0; j < J; j++) {
+            if (rw[j] < 0) continue;
+            const longlong2 qq = __ldg(q + rw[j]);
+            const bool left = goes_left(bin_of(xb, n, rw[j], tk.feat), tk.thr, tk.nan_right) &&
+                              !(tk.thr >= 255 && top_bit(topbits, (n + 31) >> 5, bigidx[tk.feat], rw[j]));
+            v[left ? 0 : 2] += qq.x;
+            v[left ? 1 : 3] += qq.y;
+            v[4] += left;
+        }
 #pragma unroll
-    for (int k = 0; k < 5; k++) {
-        long long x = warp_sum(v[k]);
-        if ((threadIdx.x & 31) == 0) s[k][threadIdx.x >> 5] = x;
-    }
-    __syncthreads();
-    if (threadIdx.x < 5) {
-        long long tot = 0;
-        for (int w = 0; w < kPartThreads / 32; w++) tot += s[threadIdx.x][w];
-        long long *o = words + (int64_t)t * kLeafWords;
-        if (threadIdx.x < 4) {
-            if (tot) {
-                atomicAdd((unsigned long long *)(o + 2 * threadIdx.x), (unsigned long long)(tot >> 32));
-                atomicAdd((unsigned long long *)(o + 2 * threadIdx.x + 1), (unsigned long long)(tot & 0xffffffffll));
+        for (int k = 0; k < 5; k++) {
+            long long x = warp_sum(v[k]);
+            if ((threadIdx.x & 31) == 0) s[k][threadIdx.x >> 5] = x;
+        }
+        __syncthreads();
+        if (threadIdx.x < 5) {
+            long long tot = 0;
+            for (int w = 0; w < kPartThreads / 32; w++) tot += s[threadIdx.x][w];
+            long long *o = words + (int64_t)t * kLeafWords;
+            if (threadIdx.x < 4) {
+                if (tot) {
+                    atomicAdd((unsigned long long *)(o + 2 * threadIdx.x), (unsigned long long)(tot >> 32));
+                    atomicAdd((unsigned long long *)(o + 2 * threadIdx.x + 1), (unsigned long long)(tot & 0xffffffffll));
+                }
+            } else if (tot) {
+                atomicAdd((unsigned long long *)(o + 8), (unsigned long long)tot);
+                atomicAdd((unsigned long long *)(n_left + t), (unsigned long long)tot);
             }
-        } else if (tot) {
-            atomicAdd((unsigned long long *)(o + 8), (unsigned long long)tot);
-            atomicAdd((unsigned long long *)(n_left + t), (unsigned long long)tot);
         }
     }
+    if (!done) return;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int W = *ntask_p;
+    const double sc = pow2(-S);
+    for (int k = threadIdx.x; k < W; k += blockDim.x) leaf_finish_one(nodes, lvl, k, words, n_left, sc);
+    if (threadIdx.x == 0) *done = 0;
 }
 
-// The last level's children from those sums (the same rounding as every
-// other node: exact integer total -> float64 -> * 2^-S).
 __global__ void k_leaf_finish(DNode *__restrict__ nodes, const int *__restrict__ lvl,
                               const int *__restrict__ lvl_count, const long long *__restrict__ words,
                               const long long *__restrict__ nl_local, int S) {
     griddep_wait();
     const int W = *lvl_count;
     const double sc = pow2(-S);
-    for (int k = threadIdx.x; k < W; k += blockDim.x) {
-        const long long *o = words + (int64_t)k * kLeafWords;
-        DNode &p = nodes[lvl[k]];
-        const long long nl = nl_local[k], gnl = o[8];
-        DNode &a = nodes[p.kid0];
-        DNode &c = nodes[p.kid1];
-        a.begin = p.begin;
-        a.end = p.begin + nl;
-        a.n = gnl;
-        c.begin = p.begin + nl;
-        c.end = p.end;
-        c.n = p.n - gnl;
-        a.G = __dmul_rn(i128_to_double(cell(o[0], o[1])), sc);
-        a.H = __dmul_rn(i128_to_double(cell(o[2], o[3])), sc);
-        c.G = __dmul_rn(i128_to_double(cell(o[4], o[5])), sc);
-        c.H = __dmul_rn(i128_to_double(cell(o[6], o[7])), sc);
-        a.feat = c.feat = -1;
-        a.bin = c.bin = 0;
-        a.gain = c.gain = -1.0;
-        p.nl = nl;
-        p.gnl = gnl;
-        p.left_small = gnl <= p.n - gnl;
-        p.expanded = 1;
-    }
+    for (int k = threadIdx.x; k < W; k += blockDim.x) leaf_finish_one(nodes, lvl, k, words, nl_local, sc);
 }
 
 // ===========================================================================
@@ -2157,6 +2179,7 @@ struct RNode {
     long long n, local;     // rows over all ranks / on this rank
     int feat, bin, kid0, kid1, expanded, depth;
     int nanr;               // the split sends the NaN bin right
+    int parent;             // -1 at the root
 };
 
 __device__ void load_rnodes(const DNode *__restrict__ nodes, int cnt, RNode *sn, double lam) {
@@ -2167,6 +2190,7 @@ __device__ void load_rnodes(const DNode *__restrict__ nodes, int cnt, RNode *sn,
         r.H = d.H; r.gain = d.gain; r.n = d.n; r.local = d.end - d.begin;
         r.feat = d.feat; r.bin = d.bin; r.kid0 = d.kid0; r.kid1 = d.kid1; r.expanded = d.expanded; r.depth = d.depth;
         r.nanr = d.nan_right;
+        r.parent = d.parent;
         sn[i] = r;
     }
     __syncthreads();
@@ -2246,6 +2270,150 @@ __device__ __forceinline__ unsigned long long order_key(double d) {
     return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
 }
 
+// The ranked form of the best-first loop below, run by the whole block at
+// once.  The loop pops, among its candidates, the one of largest key; so the
+// smallest key along a popped node's path never rises from pop to pop, and
+// two nodes u, v in different subtrees of their lowest common ancestor a are
+// popped in the order of the smallest key on their paths below a (larger
+// first), an ancestor before its descendants.  A split's number in the loop
+// is then the count of makeable candidates (key > 0, both children >=
+// min_samples_leaf) popped before it, which every candidate counts by
+// itself in one pass over the others.  The candidates are the nodes of key
+// > 0 whose ancestors are all makeable; the tree ids follow (a split of rank
+// r numbers its children 1 + 2r and 2 + 2r).  Returns false, having written
+// nothing, where the loop has to run: two candidates of equal key (the
+// loop's slot order decides between them), an unexpanded candidate the loop
+// would pop (its status 1), a root the loop keeps as a leaf, or a table
+// larger than the sizes below.
+constexpr int kRankC = kReplayLoaders;   // candidates ranked, one per thread
+constexpr int kRankDepth = 15;           // deepest candidate (its turns fit a 32-bit code)
+constexpr int kRankNodes = 2048;         // node tables ranked
+constexpr int kRankSm = kRankDepth + 2;  // row stride of the path minima (odd)
+
+__device__ __forceinline__ bool replay_ranked(const RNode *__restrict__ sn, int cnt, const RParams &P, int *tf, int *tl,
+                                              int *tr, long long *tt, double *tv, double *sg, int &nc_out,
+                                              long long &alg_out) {
+    __shared__ int s_ci[kRankNodes];                  // node -> candidate index, -1 if none
+    __shared__ int s_cl[kRankC], s_dm[kRankC], s_r[kRankC];
+    __shared__ unsigned s_code[kRankC];               // the path's turns (1: kid1), the root's first, from bit 31
+    __shared__ unsigned long long s_key[kRankC];
+    __shared__ unsigned short s_sm[kRankC * kRankSm];  // [c][d]: smallest key rank on c's path at depths >= d
+    __shared__ int s_nc, s_bad, s_ns;
+    __shared__ unsigned long long s_alg;
+    const RNode r0 = sn[0];
+    if (cnt > kRankNodes || r0.n < P.msl || r0.H < P.mcw || r0.feat < 0) return false;
+    const int K = P.max_leaves - 1;
+    auto key_of = [&](const RNode &x) -> unsigned long long {
+        return (x.feat >= 0 && x.gain > P.gamma) ? order_key(x.gain) : 0ull;
+    };
+    auto makeable = [&](const RNode &x) -> bool {
+        return key_of(x) != 0ull && x.expanded && sn[x.kid0].n >= P.msl && sn[x.kid1].n >= P.msl;
+    };
+    if (threadIdx.x == 0) { s_nc = 0; s_bad = 0; s_ns = 0; s_alg = 0ull; }
+    __syncthreads();
+    // 1. the candidates
+    for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+        s_ci[i] = -1;
+        const RNode x = sn[i];
+        const unsigned long long k = key_of(x);
+        if (k == 0ull) continue;
+        int a = x.parent;
+        while (a >= 0 && makeable(sn[a])) a = sn[a].parent;
+        if (a >= 0) continue;
+        const int c = atomicAdd(&s_nc, 1);
+        if (c >= kRankC || x.depth > kRankDepth) { s_bad = 1; continue; }
+        s_ci[i] = c;
+        s_cl[c] = i;
+        s_key[c] = k;
+        s_dm[c] = x.depth | (makeable(x) ? 0x100 : 0) | (x.expanded ? 0x200 : 0);
+    }
+    __syncthreads();
+    if (s_bad) return false;
+    const int nC = s_nc;
+    // 2. each candidate's key rank (distinct unless two keys are equal)
+    for (int t = threadIdx.x; t < nC; t += blockDim.x) {
+        const unsigned long long kv = s_key[t];
+        int kr = 0;
+        bool tie = false;
+#pragma unroll 8
+        for (int u = 0; u < nC; u++) {
+            const unsigned long long ku = s_key[u];
+            tie |= (u != t) & (ku == kv);
+            kr += ku < kv;
+        }
+        if (tie) s_bad = 1;
+        s_sm[t * kRankSm + (s_dm[t] & 0xff)] = (unsigned short)kr;
+    }
+    __syncthreads();
+    if (s_bad) return false;
+    // 3. paths: turns and the smallest key rank below each depth (every
+    // ancestor is a candidate; a thread writes only its own row, above its own depth)
+    for (int t = threadIdx.x; t < nC; t += blockDim.x) {
+        const int v = s_cl[t];
+        unsigned short m = s_sm[t * kRankSm + (s_dm[t] & 0xff)];
+        unsigned code = 0u;
+        for (int w = v, a = sn[v].parent; a >= 0; w = a, a = sn[a].parent) {
+            const int da = sn[a].depth;
+            if (sn[a].kid1 == w) code |= 1u << (31 - da);
+            const unsigned short ka = s_sm[s_ci[a] * kRankSm + da];
+            m = ka < m ? ka : m;
+            s_sm[t * kRankSm + da] = m;
+        }
+        s_code[t] = code;
+    }
+    __syncthreads();
+    // 4. ranks: the makeable candidates popped before each candidate
+    for (int t = threadIdx.x; t < nC; t += blockDim.x) {
+        const unsigned cv = s_code[t];
+        const int dmv = s_dm[t], dv = dmv & 0xff;
+        const unsigned short *smv = s_sm + t * kRankSm;
+        int before = 0;
+        // branch-free, so that unrolled steps overlap their shared-memory loads
+#pragma unroll 4
+        for (int u = 0; u < nC; u++) {
+            const int dmu = s_dm[u];
+            const int du = dmu & 0xff;
+            const int l = min(__clz(s_code[u] ^ cv), min(du, dv));   // depth of the lowest common ancestor
+            const bool anc = l == du;                                  // u is an ancestor of v
+            const int li = (anc || l == dv) ? 0 : l + 1;
+            const bool first = anc || (l != dv && s_sm[u * kRankSm + li] > smv[li]);
+            before += (u != t && (dmu & 0x100) && first) ? 1 : 0;
+        }
+        int r = INT_MAX;
+        if (!(dmv & 0x200) && before < K) s_bad = 1;
+        else if ((dmv & 0x100) && before < K) { r = before; atomicAdd(&s_ns, 1); }
+        s_r[t] = r;
+    }
+    __syncthreads();
+    if (s_bad) return false;
+    // 5. the tree
+    for (int k = threadIdx.x; k < 256; k += blockDim.x) { tf[k] = -1; tl[k] = -1; tr[k] = -1; tt[k] = 0; tv[k] = 0.0; sg[k] = 0.0; }
+    __syncthreads();
+    auto split_rank = [&](int node) -> int { const int c = s_ci[node]; return c < 0 ? INT_MAX : s_r[c]; };
+    const int ns = s_ns;
+    for (int t = threadIdx.x; t < nC; t += blockDim.x) {
+        const int r = s_r[t];
+        if (r == INT_MAX) continue;
+        const int v = s_cl[t];
+        const RNode &x = sn[v];
+        const int p = x.parent;
+        const int cur = p < 0 ? 0 : (sn[p].kid0 == v ? 1 : 2) + 2 * split_rank(p);
+        tf[cur] = x.feat; tt[cur] = x.bin | ((long long)x.nanr << 32); tl[cur] = 1 + 2 * r; tr[cur] = 2 + 2 * r;
+        tv[cur] = x.val; sg[cur] = x.gain;
+        if (split_rank(x.kid0) == INT_MAX) tv[1 + 2 * r] = sn[x.kid0].val;
+        if (split_rank(x.kid1) == INT_MAX) tv[2 + 2 * r] = sn[x.kid1].val;
+        if (x.depth + 1 < P.max_depth) {   // the last level builds no histogram
+            const int ks = sn[x.kid0].n <= sn[x.kid1].n ? x.kid0 : x.kid1;
+            atomicAdd(&s_alg, (unsigned long long)sn[ks].local);
+        }
+    }
+    if (ns == 0 && threadIdx.x == 0) tv[0] = r0.val;
+    __syncthreads();
+    nc_out = 1 + 2 * ns;
+    alg_out = r0.local + (long long)s_alg;
+    return true;
+}
+
 // One warp replays the reference's best-first loop over the grown node
 // table: the candidate slots, the strict '>' scan where the lowest slot wins
 // among equal gains, min_samples_leaf on the partition, the node numbering
@@ -2253,8 +2421,10 @@ __device__ __forceinline__ unsigned long long order_key(double d) {
 // lane s % 32, which keeps its key (the gain's order key when the slot is a
 // candidate with gain > gamma, else 0) in a register; the argmax is three
 // warp reductions.  status 1: the loop reached a node that was not expanded
-// (the caller then replays on the host).
-__global__ void __launch_bounds__(kReplayLoaders)
+// (the caller then replays on the host).  The block first tries the ranked
+// form (replay_ranked), which gives the same tree; the loop runs where it
+// hands over.
+__global__ void __launch_bounds__(kReplayLoaders, 1)
 k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_count, RParams P,
               const int *__restrict__ mono, TreeOut *__restrict__ out, TreeDev *__restrict__ td) {
     griddep_wait();
@@ -2263,7 +2433,16 @@ k_replay_leaf(const DNode *__restrict__ nodes, const int *__restrict__ node_coun
     __shared__ int tf[256], tl[256], tr[256];
     __shared__ long long tt[256];
     __shared__ double tv[256], sg[256];
-    load_rnodes(nodes, *node_count, sn, P.lam);
+    const int cnt = *node_count;
+    load_rnodes(nodes, cnt, sn, P.lam);
+    {
+        int nc_r;
+        long long alg_r;
+        if (replay_ranked(sn, cnt, P, tf, tl, tr, tt, tv, sg, nc_r, alg_r)) {
+            if (threadIdx.x < 32) finish_tree(nc_r, tf, tl, tr, tt, tv, sg, P, mono, out, td, 0, sn[0].local, alg_r);
+            return;
+        }
+    }
     if (threadIdx.x >= 32) return;
     const int lane = threadIdx.x;
     const unsigned full = 0xffffffffu;

@@ -545,3 +545,183 @@ def test_pickle_round_trip_of_a_fitted_model():
               "_tree_offsets", "bin_edges", "feature_bin_counts", "_nan_bin_id", "feature_importances_"):
         assert np.array_equal(getattr(m, k), getattr(b, k)), k
     assert b.base_score_ == m.base_score_
+
+
+# --- the ranked (parallel) form of the device's best-first replay -----------
+
+def _order_key(g):
+    """k_replay_leaf's order_key: a double as an unsigned key of the same order."""
+    import struct
+    u = struct.unpack("<Q", struct.pack("<d", float(g)))[0]
+    return (~u) & (2 ** 64 - 1) if u >> 63 else u | (1 << 63)
+
+
+def _replay_loop(T, max_leaves, gamma, msl, max_depth):
+    """k_replay_leaf's warp loop restated (candidate slots, lowest slot first
+    on equal keys, the two lowest free slots, E:642-823).  T: list of dicts
+    (feat, gain, n, local, kid0, kid1, expanded, depth, parent).  Returns
+    (status, nc, {tree id: ('split', node, lid, rid) | ('leaf', node)}, alg)."""
+    ck = lambda x: _order_key(x["gain"]) if x["feat"] >= 0 and x["gain"] > gamma else 0
+    MAXC = max_leaves + 2
+    key, act = [0] * MAXC, [False] * MAXC
+    c_node, c_nid = [0] * MAXC, [0] * MAXC
+    key[0], act[0] = ck(T[0]), True
+    nc, ns, status, out, alg = 1, 0, 0, {}, T[0]["local"]
+    while ns < max_leaves - 1:
+        best = max(key)
+        if best == 0:
+            break
+        ci = key.index(best)
+        cur, pn = c_node[ci], T[c_nid[ci]]
+        if not pn["expanded"]:
+            status = 1
+            break
+        gnl, gnr = T[pn["kid0"]]["n"], T[pn["kid1"]]["n"]
+        if gnl < msl or gnr < msl:
+            out[cur] = ("leaf", c_nid[ci])
+            key[ci], act[ci] = 0, False
+            continue
+        ss, sl = [s for s in range(MAXC) if s != ci and not act[s]][:2]
+        lid, rid = nc, nc + 1
+        nc += 2
+        ns += 1
+        small = gnl <= gnr
+        kid_s, kid_l = (pn["kid0"], pn["kid1"]) if small else (pn["kid1"], pn["kid0"])
+        if pn["depth"] + 1 < max_depth:
+            alg += T[kid_s]["local"]
+        out[cur] = ("split", c_nid[ci], lid, rid)
+        c_node[ss], c_nid[ss] = (lid if small else rid), kid_s
+        c_node[sl], c_nid[sl] = (rid if small else lid), kid_l
+        key[ci], act[ci] = 0, False
+        key[ss], act[ss] = ck(T[kid_s]), True
+        key[sl], act[sl] = ck(T[kid_l]), True
+    if not status:
+        for s in range(MAXC):
+            if act[s]:
+                out[c_node[s]] = ("leaf", c_nid[s])
+    return status, nc, out, alg
+
+
+def _replay_ranked(T, max_leaves, gamma, msl, max_depth, max_c=256, max_d=15):
+    """k_replay_leaf's ranked path restated: the candidates C (key > 0, every
+    ancestor a makeable split), u before v when u is v's ancestor or, below
+    their lowest common ancestor, u's path has the larger smallest key; a
+    split's rank is the number of makeable candidates before it.  None where
+    the kernel hands over to the loop (equal keys among C, an unexpanded
+    candidate the loop would reach, too many candidates or too deep)."""
+    ck = lambda x: _order_key(x["gain"]) if x["feat"] >= 0 and x["gain"] > gamma else 0
+    mk = lambda x: (ck(x) != 0 and x["expanded"] and T[x["kid0"]]["n"] >= msl and T[x["kid1"]]["n"] >= msl)
+    K = max_leaves - 1
+    C = []
+    for i, x in enumerate(T):
+        if ck(x) == 0:
+            continue
+        a = x["parent"]
+        while a >= 0 and mk(T[a]):
+            a = T[a]["parent"]
+        if a < 0:
+            C.append(i)
+    if len(C) > max_c or any(T[v]["depth"] > max_d for v in C):
+        return None
+    code, sm = {}, {}
+    for v in C:
+        c, m, w, s = 0, ck(T[v]), v, {}
+        s[T[v]["depth"]] = m
+        while T[w]["parent"] >= 0:
+            a = T[w]["parent"]
+            if T[a]["kid1"] == w:
+                c |= 1 << (31 - T[a]["depth"])
+            m = min(m, ck(T[a]))
+            s[T[a]["depth"]] = m
+            w = a
+        code[v], sm[v] = c, s
+    rank = {}
+    for v in C:
+        dv, before = T[v]["depth"], 0
+        for u in C:
+            if u == v:
+                continue
+            if ck(T[u]) == ck(T[v]):
+                return None
+            if not mk(T[u]):
+                continue
+            du = T[u]["depth"]
+            x = code[u] ^ code[v]
+            lca = min(32 - x.bit_length(), du, dv)
+            if lca == du:
+                before += 1
+            elif lca != dv:
+                before += sm[u][lca + 1] > sm[v][lca + 1]
+        if not T[v]["expanded"] and before < K:
+            return None
+        if mk(T[v]) and before < K:
+            rank[v] = before
+    out, alg = {}, T[0]["local"]
+    for v, r in rank.items():
+        p = T[v]["parent"]
+        cur = 0 if p < 0 else (1 if T[p]["kid0"] == v else 2) + 2 * rank[p]
+        out[cur] = ("split", v, 1 + 2 * r, 2 + 2 * r)
+        for kid, tid in ((T[v]["kid0"], 1 + 2 * r), (T[v]["kid1"], 2 + 2 * r)):
+            if kid not in rank:
+                out[tid] = ("leaf", kid)
+        if T[v]["depth"] + 1 < max_depth:
+            k0, k1 = T[v]["kid0"], T[v]["kid1"]
+            alg += T[k0 if T[k0]["n"] <= T[k1]["n"] else k1]["local"]
+    if not rank:
+        out[0] = ("leaf", 0)
+    return 0, 1 + 2 * len(rank), out, alg
+
+
+def _random_grown_table(rng, ties):
+    """A node table as the level loop leaves it: nodes numbered level by level,
+    some expanded nodes, some candidates left unexpanded (pruned), splits with
+    no valid feature, rows split unevenly (some under min_samples_leaf)."""
+    D = int(rng.integers(2, 9))
+    T = [dict(depth=0, parent=-1, n=int(rng.integers(50, 5000)))]
+    level = [0]
+    while level:
+        nxt = []
+        for v in level:
+            x = T[v]
+            x["feat"] = -1 if x["depth"] >= D or rng.random() < 0.08 else int(rng.integers(0, 50))
+            g = rng.exponential(1.0) * np.exp(-0.2 * x["depth"]) - 0.05
+            x["gain"] = float(np.round(g, 1) if ties else g)
+            x["local"] = int(x["n"] * rng.random())
+            x["expanded"] = int(x["feat"] >= 0 and rng.random() < 0.9)
+            x["kid0"] = x["kid1"] = -1
+        for v in level:
+            x = T[v]
+            if not x["expanded"]:
+                continue
+            n0 = int(rng.binomial(x["n"], rng.uniform(0.02, 0.98)))
+            x["kid0"], x["kid1"] = len(T), len(T) + 1
+            T.append(dict(depth=x["depth"] + 1, parent=v, n=n0))
+            T.append(dict(depth=x["depth"] + 1, parent=v, n=x["n"] - n0))
+            nxt += [x["kid0"], x["kid1"]]
+        level = nxt
+    return T, D
+
+
+def test_ranked_replay_matches_the_loop():
+    """The ranked replay gives the loop's tree (node numbering, leaves, rows
+    counted) whenever it does not hand over, and hands over only on equal keys
+    or an unexpanded candidate the loop reaches (where the loop reports
+    status 1)."""
+    rng = np.random.default_rng(11)
+    fast = handed = 0
+    for case in range(1500):
+        ties = case % 3 == 0
+        T, D = _random_grown_table(rng, ties)
+        max_leaves = int(rng.integers(1, 70))
+        gamma = float(rng.choice([0.0, 0.0, 0.3, -1.0]))
+        msl = int(rng.choice([1, 20, 200]))
+        max_depth = D + int(rng.integers(0, 2))
+        loop = _replay_loop(T, max_leaves, gamma, msl, max_depth)
+        ranked = _replay_ranked(T, max_leaves, gamma, msl, max_depth)
+        if ranked is None:
+            handed += 1
+            continue
+        assert loop[0] == 0, case    # the loop would have reached an unexpanded node
+        fast += 1
+        assert loop == ranked, case
+    assert fast > 800 and handed > 50, (fast, handed)
