@@ -458,7 +458,9 @@ def run_engine(args):
             print(json.dumps({"part": "rounds", "workload": c["workload"], "rounds": args.steps,
                               "ms_per_round": ms / args.steps, "rounds_per_s": args.steps / (ms / 1000.0),
                               "hist_launches": st["hist_launches"], "hist_ms": st["hist_ms"],
-                              "hist_alg_bytes": st["hist_alg_bytes"], "kernel_launches": st["kernel_launches"]}),
+                              "hist_alg_bytes": st["hist_alg_bytes"], "kernel_launches": st["kernel_launches"],
+                              "sampler_ms": st["sampler_ms"] / args.steps,
+                              "engine_wait_for_sampler_ms": st["sampler_stall_ms"] / args.steps}),
                   flush=True)
         sampler.close()
         eng.close()
@@ -637,6 +639,8 @@ def run_engine(args):
                 "collective_mb": st["comm_bytes"] / args.steps / 1e6,
                 "peer_wait": st["peer_wait_ms"] / args.steps,
                 "l2_flush_excluded": st["flush_ms"] / args.steps,
+                "sampler_stream_device": st["sampler_ms"] / args.steps,
+                "engine_wait_for_sampler_device": st["sampler_stall_ms"] / args.steps,
                 "waves": st["waves"] / args.steps},
             "e2e": ({"value": e2e, "unit": "rounds/s", "h2d_bytes_per_step": int(h2d),
                      "d2h_bytes_per_step": int(d2h), "parts_ms": e2e_parts} if e2e is not None else

@@ -76,7 +76,8 @@ class GbmStats(C.Structure):
                 ("host_sync_ms", C.c_double), ("host_replay_ms", C.c_double),
                 ("flush_ms", C.c_double), ("hist_updates", C.c_double),
                 ("host_comm_ms", C.c_double), ("comm_ms", C.c_double), ("comm_bytes", C.c_double),
-                ("peer_wait_ms", C.c_double)]
+                ("peer_wait_ms", C.c_double), ("sampler_ms", C.c_double),
+                ("sampler_stall_ms", C.c_double)]
 
 
 _lib = None

@@ -96,10 +96,12 @@ struct gbm_ctx {
     uint8_t *d_mask = nullptr;
     int32_t *d_rows = nullptr, *d_tmp = nullptr;
     uint8_t *d_maskP[2] = {};
-    int32_t *d_rowsP[2] = {}, *d_tmpP[2] = {}, *d_cntP[2] = {}, *d_offP[2] = {}, *d_totalP[2] = {};
+    int32_t *d_rowsP[2] = {}, *d_tmpP[2] = {}, *d_totalP[2] = {};
+    unsigned long long *d_compP[2] = {};   // k_compact_rows' tile words, then its [ticket, done]
     cudaEvent_t rows_freeP[2] = {};
     unsigned long long *d_tile_st = nullptr;       // k_partition's per-tile look-back words (zero between levels)
-    int32_t *d_cnt = nullptr, *d_off = nullptr, *d_total = nullptr;
+    int32_t *d_total = nullptr;
+    unsigned long long *d_comp = nullptr;
     int32_t *d_blist = nullptr, *d_fidx = nullptr;
     int16_t *d_fpos = nullptr, *d_fbi = nullptr;
     int hist_grid = 0;                 // 2 CTAs per SM: the grid of the multi-rank staging kernels
@@ -252,6 +254,7 @@ struct gbm_ctx {
     size_t flush_bytes = 0;
     unsigned flush_count = 0;
     double flush_ms = 0.0;
+    double samp_ms = 0.0, samp_stall_ms = 0.0;   // profiling: timing pairs of kinds 3 and 4
 
     cudaEvent_t mark[16] = {};
     std::unordered_map<void *, size_t> dcap, hcap;   // bytes of each buffer dalloc / halloc made
@@ -336,7 +339,8 @@ int wait_ev(gbm_ctx *ctx, cudaStream_t s, cudaEvent_t ev) {
 }
 
 // A timing pair (start, end) of the current slot's round; kind 0: k_hist,
-// 1: the L2 flush, 2: a collective.
+// 1: the L2 flush, 2: a collective, 3: the round's sampler-stream work, 4: the
+// engine stream's wait for it.
 int timing_pair(gbm_ctx *ctx, char kind, cudaEvent_t &e0, cudaEvent_t &e1) {
     gbm_ctx::Slot &s = ctx->slot[ctx->cur_slot];
     while ((int)s.tev.size() < 2 * (s.tused + 1)) {
@@ -352,6 +356,19 @@ int timing_pair(gbm_ctx *ctx, char kind, cudaEvent_t &e0, cudaEvent_t &e1) {
     return GBM_OK;
 }
 
+// The engine stream waits for the slot's sampler-stream work (profiling:
+// timed as kind 4).
+int wait_copied(gbm_ctx *ctx, gbm_ctx::Slot &s) {
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+    if (ctx->profiling) {
+        TRY(timing_pair(ctx, 4, t0, t1));
+        CK(cudaEventRecord(t0, ctx->st));
+    }
+    TRY(wait_ev(ctx, ctx->st, s.copied));
+    if (t1) CK(cudaEventRecord(t1, ctx->st));
+    return GBM_OK;
+}
+
 // Fold a slot's finished timing pairs into the totals (each pair once).
 int collect_slot_timing(gbm_ctx *ctx, int si) {
     gbm_ctx::Slot &s = ctx->slot[si];
@@ -359,7 +376,8 @@ int collect_slot_timing(gbm_ctx *ctx, int si) {
         float ms = 0.f;
         CK(cudaEventElapsedTime(&ms, s.tev[(size_t)(2 * k)], s.tev[(size_t)(2 * k + 1)]));
         const char kind = s.tkind[(size_t)k];
-        (kind == 0 ? ctx->hist_ms : kind == 1 ? ctx->flush_ms : ctx->comm_ms) += ms;
+        (kind == 0 ? ctx->hist_ms : kind == 1 ? ctx->flush_ms : kind == 2 ? ctx->comm_ms
+         : kind == 3 ? ctx->samp_ms : ctx->samp_stall_ms) += ms;
     }
     s.tdone = s.tused;
     return GBM_OK;
@@ -375,8 +393,7 @@ void use_parity(gbm_ctx *ctx, int q) {
     ctx->d_mask = ctx->d_maskP[q];
     ctx->d_rows = ctx->d_rowsP[q];
     ctx->d_tmp = ctx->d_tmpP[q];
-    ctx->d_cnt = ctx->d_cntP[q];
-    ctx->d_off = ctx->d_offP[q];
+    ctx->d_comp = ctx->d_compP[q];
     ctx->d_total = ctx->d_totalP[q];
     ctx->rows_free = ctx->rows_freeP[q];
 }
@@ -1283,7 +1300,7 @@ int fetch_nodes(gbm_ctx *ctx) {
     TRY(sync_stream(ctx));
     TRY(p2p_check(ctx, ctx->cur_slot));
     if (ctx->h_ints[I_PART_ERR])
-        return fail(ctx, GBM_ERR_STATE, "internal: a partition tile's wait for its predecessors ran out");
+        return fail(ctx, GBM_ERR_STATE, "internal: a partition or compaction tile's wait for its predecessors ran out");
     if (ctx->profiling) TRY(collect_slot_timing(ctx, ctx->cur_slot));
     return GBM_OK;
 }
@@ -1498,8 +1515,8 @@ int alloc_round_fixed(gbm_ctx *ctx) {
         TRY(dalloc(ctx, &ctx->d_maskP[q], (size_t)ctx->n));
         TRY(dalloc(ctx, &ctx->d_rowsP[q], (size_t)ctx->n));
         TRY(dalloc(ctx, &ctx->d_tmpP[q], (size_t)ctx->n));
-        TRY(dalloc(ctx, &ctx->d_cntP[q], (size_t)ntile));
-        TRY(dalloc(ctx, &ctx->d_offP[q], (size_t)ntile));
+        TRY(dalloc(ctx, &ctx->d_compP[q], (size_t)ntile + 1));
+        CK(cudaMemsetAsync(ctx->d_compP[q], 0, sizeof(unsigned long long) * ((size_t)ntile + 1), ctx->st));
         TRY(dalloc(ctx, &ctx->d_totalP[q], 1));
     }
     use_parity(ctx, 0);
@@ -1548,10 +1565,8 @@ int tree_need(const gbm_params *P) {
 // In-bag mask -> ascending row list of the root (row buffer 0) and its count.
 int enqueue_compaction(gbm_ctx *ctx, cudaStream_t s) {
     int ntile = (int)((ctx->n + kCompTile - 1) / kCompTile);
-    TRY(launch(ctx, k_comp_count, dim3(ntile), dim3(256), 0, s, ctx->d_mask, ctx->n, ctx->d_cnt));
-    TRY(launch(ctx, k_scan_small, dim3(1), dim3(1024), 0, s, ctx->d_cnt, ntile, ctx->d_off, ctx->d_total));
-    TRY(launch(ctx, k_comp_scatter, dim3(ntile), dim3(256), 0, s, ctx->d_mask, ctx->n, ctx->d_off, ctx->d_rows));
-    return GBM_OK;
+    return launch(ctx, k_compact_rows, dim3(ntile), dim3(kCompThreads), 0, s, (const uint8_t *)ctx->d_mask, ctx->n,
+                  ctx->d_rows, ctx->d_total, ctx->d_comp, (unsigned *)(ctx->d_comp + ntile), ints(ctx, I_PART_ERR));
 }
 
 // `compacted`: the root's row list was already built (stage_sample, on the
@@ -1682,7 +1697,7 @@ int harvest(gbm_ctx *ctx, int si, int nf, const gbm_params *P, gbm_tree_out *out
     TRY(p2p_check(ctx, si));
     const TreeOut &T = *ctx->slot[si].h_tout;
     if (T.status == 3)
-        return fail(ctx, GBM_ERR_STATE, "internal: a partition tile's wait for its predecessors ran out");
+        return fail(ctx, GBM_ERR_STATE, "internal: a partition or compaction tile's wait for its predecessors ran out");
     if (T.status != 0) return fail(ctx, GBM_ERR_STATE, "internal: the device replay reached an unexpanded node");
     ctx->alg_bytes += (double)T.alg_rows * (nf + 8);
     ctx->hist_updates += (double)T.alg_rows * ctx->slot[si].upd_per_row;
@@ -1776,6 +1791,11 @@ int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int
     // back: wait for that round's last level, then build them while the
     // previous round grows.
     TRY(wait_ev(ctx, ctx->cst, ctx->rows_free));
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+    if (ctx->profiling) {
+        TRY(timing_pair(ctx, 3, t0, t1));
+        CK(cudaEventRecord(t0, ctx->cst));
+    }
     s.xc_on_cst = nf > 0 && compact_hist(ctx);
     if (s.xc_on_cst) {
         CK(cudaMemcpyAsync(s.d_fidx_c, s.h_feat, sizeof(int32_t) * nf, cudaMemcpyHostToDevice, ctx->cst));
@@ -1810,6 +1830,7 @@ int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int
         CK(cudaMemsetAsync(ctx->d_mask, 1, (size_t)ctx->n, ctx->cst));
     }
     TRY(enqueue_compaction(ctx, ctx->cst));
+    if (t1) CK(cudaEventRecord(t1, ctx->cst));
     TRY(record_ev(ctx, s.copied, ctx->cst));
     return GBM_OK;
 }
@@ -2006,7 +2027,7 @@ int capture_round(gbm_ctx *ctx, int si, int nf, const gbm_params *P, int64_t N, 
     s.tused = s.tdone = 0;
     TRY(capture(ctx, ctx->cst, &s.g_cst, [&] { return enqueue_sample(ctx, si, N, m, rows_on, row_offset, nf, dr); }));
     TRY(capture(ctx, ctx->st, &s.g_st, [&] {
-        TRY(wait_ev(ctx, ctx->st, s.copied));
+        TRY(wait_copied(ctx, s));
         TRY(enqueue_features(ctx, si, nf));
         RoundFeat rf;
         rf.nf = nf;
@@ -2094,7 +2115,7 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
         for (cudaEvent_t e : s.tev) cudaEventDestroy(e);
     if (ctx->comm) gbm_comm_destroy(ctx->comm);
     for (int q = 0; q < 2; q++) {
-        void *pq[] = {ctx->d_maskP[q], ctx->d_rowsP[q], ctx->d_tmpP[q], ctx->d_cntP[q], ctx->d_offP[q], ctx->d_totalP[q]};
+        void *pq[] = {ctx->d_maskP[q], ctx->d_rowsP[q], ctx->d_tmpP[q], ctx->d_compP[q], ctx->d_totalP[q]};
         for (void *p : pq) if (p) cudaFree(p);
     }
     void *dev_ptrs[] = {ctx->d_xb, ctx->d_xc[0], ctx->d_xc[1], ctx->d_counts, ctx->d_y, ctx->d_F, ctx->d_q,
@@ -2705,7 +2726,7 @@ int gbm_fit_rounds(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const
             RoundFeat rf;
             TRY(setup_features(ctx, si, ctx->feat_buf.data(), nf, rf));   // before the sample packs its features
             TRY(enqueue_sample(ctx, si, N, m, rows_on, row_offset, nf, dr));
-            TRY(wait_ev(ctx, ctx->st, s.copied));
+            TRY(wait_copied(ctx, s));
             TRY(enqueue_features(ctx, si, nf));
             TRY(enqueue_grow(ctx, rf, P, true));
             TRY(enqueue_replay(ctx, P));
@@ -2974,6 +2995,8 @@ int gbm_get_stats(gbm_ctx *ctx, gbm_stats *out) {
     out->comm_ms = ctx->comm_ms;
     out->comm_bytes = ctx->comm_bytes;
     out->peer_wait_ms = 0.0;
+    out->sampler_ms = ctx->samp_ms;
+    out->sampler_stall_ms = ctx->samp_stall_ms;
     if (ctx->p2p && ctx->d_sync && cudaSetDevice(ctx->dev) == cudaSuccess) {
         unsigned long long ns = 0;
         if (cudaMemcpy(&ns, ctx->d_sync + ctx->p2p_n + kSyncWaitNs, sizeof ns, cudaMemcpyDeviceToHost) == cudaSuccess)
@@ -2987,7 +3010,7 @@ int gbm_reset_stats(gbm_ctx *ctx) {
     ctx->launches = ctx->hist_launches = ctx->hist_rows = ctx->waves = 0;
     ctx->hist_ms = ctx->alg_bytes = ctx->hist_updates = 0.0;
     ctx->host_sample_ms = ctx->host_sync_ms = ctx->host_replay_ms = ctx->flush_ms = ctx->host_comm_ms = 0.0;
-    ctx->comm_ms = ctx->comm_bytes = 0.0;
+    ctx->comm_ms = ctx->comm_bytes = ctx->samp_ms = ctx->samp_stall_ms = 0.0;
     if (ctx->p2p && ctx->d_sync && cudaSetDevice(ctx->dev) == cudaSuccess) {   // the counter only grows
         unsigned long long ns = 0;
         if (cudaMemcpy(&ns, ctx->d_sync + ctx->p2p_n + kSyncWaitNs, sizeof ns, cudaMemcpyDeviceToHost) == cudaSuccess)

@@ -370,57 +370,7 @@ __global__ void k_sum_partials(const double *__restrict__ part, int m, double *_
 // in-bag compaction: mask -> ascending row ids
 // ===========================================================================
 
-__global__ void k_comp_count(const uint8_t *__restrict__ mask, int64_t n, int32_t *__restrict__ cnt) {
-    griddep_wait();
-    __shared__ int s[32];
-    int64_t base = (int64_t)blockIdx.x * kCompTile;
-    int c = 0;
-    for (int k = threadIdx.x; k < kCompTile; k += blockDim.x) {
-        int64_t i = base + k;
-        if (i < n && mask[i]) c++;
-    }
-    c = warp_sum(c);
-    if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = c;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int t = 0;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += s[w];
-        cnt[blockIdx.x] = t;
-    }
-}
-
-// Exclusive scan of m ints by one CTA; *total = sum.
-__global__ void k_scan_small(const int32_t *__restrict__ in, int m, int32_t *__restrict__ out,
-                             int32_t *__restrict__ total) {
-    griddep_wait();
-    __shared__ int s_w[32];
-    int carry = 0;
-    for (int base = 0; base < m; base += blockDim.x) {
-        int k = base + threadIdx.x;
-        int v = k < m ? in[k] : 0;
-        int tot;
-        int e = block_excl_scan(v, s_w, tot);
-        if (k < m) out[k] = carry + e;
-        carry += tot;
-    }
-    if (threadIdx.x == 0 && total) *total = carry;
-}
-
-__global__ void k_comp_scatter(const uint8_t *__restrict__ mask, int64_t n, const int32_t *__restrict__ off,
-                               int32_t *__restrict__ rows) {
-    griddep_wait();
-    __shared__ int s_w[32];
-    int64_t base = (int64_t)blockIdx.x * kCompTile;
-    int carry = off[blockIdx.x];
-    for (int k0 = 0; k0 < kCompTile; k0 += blockDim.x) {
-        int64_t i = base + k0 + threadIdx.x;
-        int f = (i < n && mask[i]) ? 1 : 0;
-        int tot;
-        int e = block_excl_scan(f, s_w, tot);
-        if (f) rows[carry + e] = (int32_t)i;
-        carry += tot;
-    }
-}
+// (the mask's compaction into row ids, k_compact_rows, uses the partition's look-back below)
 
 // In-bag mask of this rank's rows [row0, row0 + n) from global row ids.
 __global__ void k_mask_from_rows(const int32_t *__restrict__ rows, int64_t m, int64_t row0, int64_t n,
@@ -1149,6 +1099,104 @@ __device__ void plan_hist_block(DNode *__restrict__ nodes, const int *__restrict
 constexpr unsigned long long kTileAgg = 1ull << 62, kTilePre = 2ull << 62, kTileVal = (1ull << 62) - 1;
 constexpr int kLookbackSpins = 1 << 22;
 
+// Warp 0 of a tile: the decoupled look-back over the tiles first .. tile - 1,
+// 32 predecessors at a time.  Publishes this tile's aggregate `tot`, sums the
+// predecessors back to the nearest one that has published its inclusive
+// prefix, publishes its own and returns the exclusive prefix (the first tile
+// publishes at once and returns 0).  A wait past kLookbackSpins polls sets
+// *err and publishes what it summed.
+__device__ __forceinline__ long long lookback_warp(volatile unsigned long long *vst, int tile, int first,
+                                                   long long tot, int *err) {
+    const int lane = threadIdx.x & 31;
+    if (tile == first) {
+        if (lane == 0) vst[tile] = kTilePre | (unsigned long long)tot;
+        return 0;
+    }
+    if (lane == 0) vst[tile] = kTileAgg | (unsigned long long)tot;
+    long long lcar = 0;
+    int top = tile - 1;   // the window's nearest tile; lane l reads tile top - l
+    bool bad = false;
+    while (true) {
+        const int j = top - lane;
+        // tiles before the first (which publishes its prefix at once) add nothing
+        unsigned long long v = kTilePre + 0ull;
+        if (j >= first) v = vst[j];
+        int spins = 0;
+        while (!__all_sync(0xffffffffu, (v >> 62) != 0ull)) {
+            if (++spins > kLookbackSpins) { bad = true; break; }
+            if (spins > 64) __nanosleep(32);
+            if ((v >> 62) == 0ull) v = vst[j];
+        }
+        if (bad) break;
+        const unsigned pre = __ballot_sync(0xffffffffu, (v >> 62) == 2ull);
+        const int k = pre ? __ffs(pre) - 1 : 31;   // the nearest tile with a prefix, else the window
+        long long x = lane <= k ? (long long)(v & kTileVal) : 0ll;
+        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        lcar += x;
+        if (pre) break;
+        top -= 32;
+    }
+    if (bad && lane == 0) atomicExch(err, 1);
+    if (lane == 0) vst[tile] = kTilePre | (unsigned long long)(lcar + tot);
+    return lcar;
+}
+
+// In-bag compaction in one pass: mask -> ascending row ids, *total = their
+// count.  Tiles of kCompTile rows (16 mask bytes per thread, one 16-byte
+// load) are handed out in order by a ticket; a block scan ranks the in-bag
+// rows inside the tile, the look-back gives the tile's offset, and the ids
+// are staged in shared memory so that the stores are contiguous.  ctl holds
+// [ticket, done]; the last CTA to finish zeroes the tile words and ctl.
+constexpr int kCompThreads = kCompTile / 16;
+
+__global__ void __launch_bounds__(kCompThreads)
+k_compact_rows(const uint8_t *__restrict__ mask, int64_t n, int32_t *__restrict__ rows, int32_t *__restrict__ total,
+               unsigned long long *__restrict__ tile_st, unsigned *__restrict__ ctl, int *__restrict__ err) {
+    griddep_wait();
+    __shared__ int s_out[kCompTile];
+    __shared__ int s_w[32];
+    __shared__ int s_tile, s_last;
+    __shared__ long long s_off;
+    if (threadIdx.x == 0) s_tile = (int)atomicAdd(ctl, 1u);
+    __syncthreads();
+    const int tile = s_tile;
+    const int64_t base = (int64_t)tile * kCompTile + 16 * threadIdx.x;
+    unsigned bits = 0u;
+    if (base + 16 <= n) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(mask + base);
+        const unsigned w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 16; k++) bits |= (((w[k >> 2] >> (8 * (k & 3))) & 0xffu) != 0u ? 1u : 0u) << k;
+    } else {
+        for (int k = 0; k < 16 && base + k < n; k++) bits |= (mask[base + k] != 0 ? 1u : 0u) << k;
+    }
+    int tot;
+    const int e = block_excl_scan(__popc(bits), s_w, tot);
+    for (int k = 0, o = e; k < 16; k++)
+        if ((bits >> k) & 1u) s_out[o++] = (int)(base + k);
+    if (threadIdx.x < 32) {
+        const long long off = lookback_warp(tile_st, tile, 0, tot, err);
+        if (threadIdx.x == 0) {
+            s_off = off;
+            if (tile == (int)gridDim.x - 1) *total = (int32_t)(off + tot);
+        }
+    }
+    __syncthreads();
+    const long long off = s_off;
+    for (int k = threadIdx.x; k < tot; k += blockDim.x) rows[off + k] = s_out[k];
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(ctl + 1, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) tile_st[i] = 0ull;
+    if (threadIdx.x == 0) {
+        ctl[0] = 0u;
+        ctl[1] = 0u;
+    }
+}
+
 __global__ void __launch_bounds__(kPartThreads)
 k_partition(const uint8_t *__restrict__ xb, int64_t n, int32_t *__restrict__ rows0, int32_t *__restrict__ rows1,
             const PartTask *__restrict__ tasks, const int *__restrict__ ntask_p, const int *__restrict__ tiles_total,
@@ -1210,39 +1258,9 @@ k_partition(const uint8_t *__restrict__ xb, int64_t n, int32_t *__restrict__ row
             if (lane == 31) s_tot = incl;
         }
         __syncthreads();
-        if (warp == 0) {   // decoupled look-back, 32 predecessors at a time
+        if (warp == 0) {   // decoupled look-back over the task's earlier tiles
             const long long tot = s_tot;
-            volatile unsigned long long *vst = tile_st;
-            long long lcar = 0;
-            if (tile == tk.tile0) {
-                if (lane == 0) vst[tile] = kTilePre | (unsigned long long)tot;
-            } else {
-                if (lane == 0) vst[tile] = kTileAgg | (unsigned long long)tot;
-                int top = tile - 1;   // the window's nearest tile; lane l reads tile top - l
-                bool bad = false;
-                while (true) {
-                    const int j = top - lane;
-                    // tiles before the task's first (which publishes its prefix at once) add nothing
-                    unsigned long long v = kTilePre + 0ull;
-                    if (j >= tk.tile0) v = vst[j];
-                    int spins = 0;
-                    while (!__all_sync(0xffffffffu, (v >> 62) != 0ull)) {
-                        if (++spins > kLookbackSpins) { bad = true; break; }
-                        if (spins > 64) __nanosleep(32);
-                        if ((v >> 62) == 0ull) v = vst[j];
-                    }
-                    if (bad) break;
-                    const unsigned pre = __ballot_sync(0xffffffffu, (v >> 62) == 2ull);
-                    const int k = pre ? __ffs(pre) - 1 : 31;   // the nearest tile with a prefix, else the window
-                    long long x = lane <= k ? (long long)(v & kTileVal) : 0ll;
-                    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-                    lcar += x;
-                    if (pre) break;
-                    top -= 32;
-                }
-                if (bad && lane == 0) atomicExch(err, 1);
-                if (lane == 0) vst[tile] = kTilePre | (unsigned long long)(lcar + tot);
-            }
+            const long long lcar = lookback_warp(tile_st, tile, tk.tile0, tot, err);
             if (lane == 0) {
                 s_lcar = lcar;
                 if (tile == tk.tile0 + tk.ntile - 1) n_left[t] = lcar + tot;

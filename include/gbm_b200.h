@@ -387,6 +387,10 @@ typedef struct {
     double comm_ms;            /* device time of the collectives (profiling), waits for peers included */
     double comm_bytes;         /* bytes this rank all-reduced or pulled from peers */
     double peer_wait_ms;       /* peer exchange: time spent waiting for the peers' signals */
+    double sampler_ms;         /* device time of the rounds' sampler-stream work (the row
+                                  shuffle, mask, root row list, packed feature blocks), from
+                                  the start of each round's work to its end (profiling) */
+    double sampler_stall_ms;   /* device time the engine stream waited for that work (profiling) */
 } gbm_stats;
 
 /* Instrumentation (no reference counterpart; the reference's times dict,
