@@ -744,16 +744,20 @@ k_hist3(const uint8_t *__restrict__ xb, int64_t n, const int32_t *__restrict__ r
                 const int r0 = (int)tk.begin + (c0 - t0), r1 = (int)tk.begin + (c1 - t0);
                 long long tg = 0, th = 0;
                 unsigned *my = acc + half * kBlk;
-                for (int rb = r0 + (int)(threadIdx.x & ~31u); rb < r1; rb += blockDim.x) {
+                int rb = r0 + (int)(threadIdx.x & ~31u);
+                int row_next = rb + lane < r1 ? rows[rb + lane] : 0;
+                longlong2 q_next = rb + lane < r1 ? __ldg(q + row_next) : make_longlong2(0, 0);
+                for (; rb < r1; rb += blockDim.x) {
                     const int r = rb + lane;
                     const bool valid = r < r1;
+                    const int row = row_next;
+                    const longlong2 qq = q_next;
                     uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                    longlong2 qq = make_longlong2(0, 0);
-                    if (valid) {
-                        const int row = rows[r];
-                        v = __ldg(xv + row);
-                        qq = __ldg(q + row);
-                    }
+                    if (valid) v = __ldg(xv + row);
+                    // the next step's row id and q, in flight with this step's atomics
+                    const bool vn = r + (int)blockDim.x < r1;
+                    row_next = vn ? rows[r + blockDim.x] : 0;
+                    q_next = vn ? __ldg(q + row_next) : make_longlong2(0, 0);
                     tg += qq.x;
                     th += qq.y;
                     // an invalid lane adds zeros (its q is 0) into real cells: harmless
