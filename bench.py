@@ -380,6 +380,35 @@ def config5_subrecord(eng, args, world, rank, local, dist):
                        "max_leaves": c["max_leaves"], "subsample": c["subsample"], "colsample": c["colsample"]}}
 
 
+def other_objectives(eng, local, X, y, c, rounds=20):
+    """The estimator's other device objectives on config 4's rows, `rounds`
+    rounds each: multi-class softmax over 3 classes (3 trees a round,
+    gbm_round_mc) and mse regression (gbm_round_reg), config 4's tree
+    parameters.  Both run one round per engine call, with no pipelining across
+    rounds; the figure is the host wall time of the rounds (the estimator's
+    times['rounds']).  The labels are synthetic functions of the rows."""
+    from bsscl_gbm_b200 import HybridHistGBMNumbaV1_0_1
+    f0 = np.nan_to_num(X[:, 0].astype(np.float64), nan=0.0)
+    f1 = np.nan_to_num(X[:, 1].astype(np.float64), nan=0.0)
+    y3 = y.astype(np.int64) + (f0 > np.median(f0)).astype(np.int64)
+    yr = f0 + 0.5 * f1 + 0.1 * y.astype(np.float64)
+    common = dict(n_estimators=rounds, max_depth=c["max_depth"], learning_rate=c["lr"],
+                  min_child_weight=c["mcw"], subsample=c["subsample"], colsample_bytree=c["colsample"],
+                  reg_lambda=c["lam"], n_bins=255, random_state=c["seed"], verbose=False)
+    out = {}
+    for name, kw, target in [("multiclass_3", {}, y3),
+                             ("regression_mse", {"objective": "regression", "loss": "mse"}, yr)]:
+        m = HybridHistGBMNumbaV1_0_1(**common, **kw)
+        m._engine, m._engine_dev = eng, local
+        m.fit(X, target)
+        ms = m.times["rounds"]
+        out[name] = {"value": rounds / (ms / 1000.0), "unit": "rounds/s", "rounds": rounds,
+                     "ms_per_round": ms / rounds}
+    out["note"] = ("HybridHistGBMNumbaV1_0_1.fit on config 4's 1M x 100 rows (3 synthetic classes; a "
+                   "synthetic float target), one round per engine call; host wall time of the rounds")
+    return out
+
+
 def run_engine(args):
     import torch
     from bsscl_gbm_b200 import Engine, GbmParams, HybridHistGBMNumbaV1_0_1, Sampler, binning
@@ -551,6 +580,7 @@ def run_engine(args):
                    "training_ms": m2.times["training"],
                    "note": "HybridHistGBMNumbaV1_0_1.fit(X float32 [n, p], y) wall time on this rank: "
                            "adaptive hyper-parameters, GPU edges and bins, labels, the rounds"}
+    other = other_objectives(eng, local, X, y, c) if X is not None and world == 1 else None
     rows = hi - lo
     nblk = (p + 15) // 16
     # once per fit: bins (1 byte per id: uint16 ids are narrowed on the host
@@ -658,6 +688,7 @@ def run_engine(args):
             "clocks": clk,
             "binning": bin_stats,
             "fit_from_raw": fit_raw,
+            "other_objectives": other,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
