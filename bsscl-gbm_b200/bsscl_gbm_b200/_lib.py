@@ -34,7 +34,8 @@ EXPORTS = (
     "gbm_set_l2_flush", "gbm_bin_edges", "gbm_upload_binned_rows", "gbm_bin_features",
     "gbm_predict_upload_raw", "gbm_predict_raw", "gbm_test_peer_wait", "gbm_upload_labels_mc",
     "gbm_round_mc", "gbm_get_F_mc", "gbm_get_grad_mc", "gbm_upload_targets", "gbm_round_reg",
-    "gbm_check_model", "gbm_sampler_create_device", "gbm_predict_upload_u16",
+    "gbm_check_model", "gbm_sampler_create_device", "gbm_predict_upload_u16", "gbm_round_mc_sampled",
+    "gbm_round_reg_sampled",
 )
 
 
@@ -155,6 +156,10 @@ def lib():
     L.gbm_test_peer_wait.argtypes = [i32, i32]
     L.gbm_upload_labels_mc.argtypes = [P, P, i32, P, i64]
     L.gbm_round_mc.argtypes = [P, P, P, i32, C.POINTER(GbmParams), C.POINTER(GbmTreeOut), C.POINTER(C.c_double)]
+    L.gbm_round_mc_sampled.argtypes = [P, P, i64, C.POINTER(GbmParams), C.POINTER(GbmTreeOut),
+                                       C.POINTER(C.c_double)]
+    L.gbm_round_reg_sampled.argtypes = [P, P, i64, C.POINTER(GbmParams), C.POINTER(GbmTreeOut),
+                                        C.POINTER(C.c_double)]
     L.gbm_get_F_mc.argtypes = [P, P]
     L.gbm_get_grad_mc.argtypes = [P, i32, P, P]
     L.gbm_upload_targets.argtypes = [P, P, f64, i32, i64]
@@ -374,6 +379,18 @@ class Engine:
                                          C.byref(out), C.byref(loss)), "gbm_round_reg")
         return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value), leaf
 
+    def round_reg_sampled(self, sampler, row_offset, params: GbmParams, capacity):
+        """gbm_round_reg_sampled: the tree with the round's subsample drawn by
+        `sampler` (its shuffle applied on the device) and the train loss."""
+        tf = np.empty(capacity, np.int32); tt = np.empty(capacity, np.int64)
+        tv = np.empty(capacity, np.float64); tl = np.empty(capacity, np.int32)
+        tr = np.empty(capacity, np.int32); sg = np.empty(capacity, np.float64)
+        out = GbmTreeOut(capacity, ptr(tf), ptr(tt), ptr(tv), ptr(tl), ptr(tr), ptr(sg), 0, None)
+        loss = C.c_double(0.0)
+        self.check(self._L.gbm_round_reg_sampled(self._h, sampler._h, int(row_offset), C.byref(params),
+                                                 C.byref(out), C.byref(loss)), "gbm_round_reg_sampled")
+        return (tf, tt, tv, tl, tr, int(out.n_nodes), sg), float(loss.value)
+
     # -- multi-class softmax --
     def upload_labels_mc(self, y, n_classes, class_w, n_global=0):
         yy = np.ascontiguousarray(y, dtype=np.uint8)
@@ -402,6 +419,22 @@ class Engine:
                                         C.byref(loss)), "gbm_round_mc")
         trees = [(a[0], a[1], a[2], a[3], a[4], int(outs[k].n_nodes), a[5]) for k, a in enumerate(arrs)]
         return trees, float(loss.value), leaves
+
+    def round_mc_sampled(self, sampler, row_offset, params: GbmParams, capacity):
+        """gbm_round_mc_sampled: K trees with the round's subsample drawn by
+        `sampler` (its shuffle applied on the device) and the train loss."""
+        K = self.K
+        blocks = [np.empty((K, capacity), t) for t in (np.int32, np.int64, np.float64, np.int32, np.int32,
+                                                        np.float64)]
+        outs = (GbmTreeOut * K)()
+        for k in range(K):
+            outs[k] = GbmTreeOut(capacity, *(ptr(b[k]) for b in blocks), 0, None)
+        loss = C.c_double(0.0)
+        self.check(self._L.gbm_round_mc_sampled(self._h, sampler._h, int(row_offset), C.byref(params), outs,
+                                                C.byref(loss)), "gbm_round_mc_sampled")
+        trees = [(blocks[0][k], blocks[1][k], blocks[2][k], blocks[3][k], blocks[4][k], int(outs[k].n_nodes),
+                  blocks[5][k]) for k in range(K)]
+        return trees, float(loss.value)
 
     def get_F_mc(self):
         F = np.empty((self.K, self.n), np.float64)

@@ -567,7 +567,7 @@ class HybridHistGBMNumbaV1_0_1:
 
     def _fit_regression_device(self, X_bin, y, X_val_bin, y_val):
         """The reference's ``_fit_regression`` loop (E:2607-2705) with every round
-        on the GPU (gbm_round_reg): F from mean(y), g = F - y (mse) or
+        on the GPU (gbm_round_reg_sampled): F from mean(y), g = F - y (mse) or
         sign(F - y) (mae), h = 1."""
         n, p = X_bin.shape
         self.init_score_ = float(np.mean(y))
@@ -600,8 +600,8 @@ class HybridHistGBMNumbaV1_0_1:
         t_rounds = time.perf_counter()
         try:
             for m in range(self.n_estimators):
-                _, mask, feat = sampler.next(want_sample=False, want_mask=True)
-                tree, loss, _ = eng.round_reg(mask[lo:hi], feat, params, cap)
+                # the round's shuffle applied on the device (the same sample as the host draw)
+                tree, loss = eng.round_reg_sampled(sampler, lo, params, cap)
                 self.trees.append(tree)
                 self.train_loss_history_.append(loss)
                 val_loss = None
@@ -644,7 +644,7 @@ class HybridHistGBMNumbaV1_0_1:
 
     def _fit_multiclass_device(self, X_bin, y, X_val_bin, y_val):
         """The reference's ``_fit_multiclass`` loop (E:2949-3065): per round one
-        shared subsample and K trees, all on the GPU (gbm_round_mc)."""
+        shared subsample and K trees, all on the GPU (gbm_round_mc_sampled)."""
         n, p = X_bin.shape
         K = self.n_classes_
         w = self._class_weights_mc(y)
@@ -680,8 +680,8 @@ class HybridHistGBMNumbaV1_0_1:
         t_rounds = time.perf_counter()
         try:
             for m in range(self.n_estimators):
-                _, mask, feat = sampler.next(want_sample=False, want_mask=True)
-                trees, loss, _ = eng.round_mc(mask[lo:hi], feat, params, cap)
+                # the round's shuffle applied on the device (the same sample as the host draw)
+                trees, loss = eng.round_mc_sampled(sampler, lo, params, cap)
                 for k in range(K):
                     self.mc_trees[k].append(trees[k])
                     if F_val is not None:

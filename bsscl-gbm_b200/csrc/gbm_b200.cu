@@ -149,6 +149,7 @@ struct gbm_ctx {
     int upd_blocks = 0;
     // pinned host mirrors
     DNode *h_nodes = nullptr;
+    TreeOut *h_tout_mc = nullptr;   // multi-class rounds: one tree record per class
     int *h_ints = nullptr;
     int *h_list = nullptr;
     double *h_loss = nullptr;
@@ -1692,17 +1693,22 @@ void write_tree_dev(const TreeOut &T, int need, gbm_tree_out *out) {
 }
 
 // A finished slot -> the caller's tree and loss, and the statistics.
-int harvest(gbm_ctx *ctx, int si, int nf, const gbm_params *P, gbm_tree_out *out, double *train_loss) {
-    if (ctx->profiling) TRY(collect_slot_timing(ctx, si));
-    TRY(p2p_check(ctx, si));
-    const TreeOut &T = *ctx->slot[si].h_tout;
+// A device-replayed tree record: its status, the statistics, the caller's arrays.
+int take_tree(gbm_ctx *ctx, const TreeOut &T, double upd_per_row, int nf, const gbm_params *P, gbm_tree_out *out) {
     if (T.status == 3)
         return fail(ctx, GBM_ERR_STATE, "internal: a partition or compaction tile's wait for its predecessors ran out");
     if (T.status != 0) return fail(ctx, GBM_ERR_STATE, "internal: the device replay reached an unexpanded node");
     ctx->alg_bytes += (double)T.alg_rows * (nf + 8);
-    ctx->hist_updates += (double)T.alg_rows * ctx->slot[si].upd_per_row;
+    ctx->hist_updates += (double)T.alg_rows * upd_per_row;
     ctx->hist_rows += T.root_rows;
     write_tree_dev(T, tree_need(P), out);
+    return GBM_OK;
+}
+
+int harvest(gbm_ctx *ctx, int si, int nf, const gbm_params *P, gbm_tree_out *out, double *train_loss) {
+    if (ctx->profiling) TRY(collect_slot_timing(ctx, si));
+    TRY(p2p_check(ctx, si));
+    TRY(take_tree(ctx, *ctx->slot[si].h_tout, ctx->slot[si].upd_per_row, nf, P, out));
     if (train_loss) *train_loss = -ctx->slot[si].h_loss[0] / (double)ctx->n_global;
     return GBM_OK;
 }
@@ -2132,7 +2138,8 @@ void gbm_ctx_destroy(gbm_ctx *ctx) {
                         ctx->d_pbigidx, ctx->d_ptopbits};
     for (int32_t *q : ctx->d_perm) if (q) cudaFree(q);
     for (void *p : dev_ptrs) if (p) cudaFree(p);
-    void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_mono, ctx->h_nanf};
+    void *host_ptrs[] = {ctx->h_nodes, ctx->h_ints, ctx->h_list, ctx->h_loss, ctx->h_mask, ctx->h_mono, ctx->h_nanf,
+                         ctx->h_tout_mc};
     for (void *p : host_ptrs) if (p) cudaFreeHost(p);
     for (auto &s : ctx->slot) {
         if (s.d_tg) cudaFree(s.d_tg);
@@ -2447,27 +2454,21 @@ int gbm_upload_targets(gbm_ctx *ctx, const double *y, double init_score, int32_t
     return GBM_OK;
 }
 
-int gbm_round_reg(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
-                  const gbm_params *P, gbm_tree_out *out, double *train_loss) {
-    if (!ctx || !inbag_mask || !feat_idx || !P || !out) return GBM_ERR_ARG;
-    if (!ctx->have_targets) return fail(ctx, GBM_ERR_STATE, "upload bins and gbm_upload_targets first");
-    TRY(check_tree_args(ctx, nfeat, P, out));
-    CK(cudaSetDevice(ctx->dev));
-    TRY(prepare_round(ctx, nfeat, P));
-    std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
-    CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
-    gbm_ctx::Slot &s = ctx->slot[0];
-    begin_round(ctx, 0);
+// One regression round on slot si (begun by the caller), its in-bag mask in
+// d_mask (and, with `compacted`, its root row list in d_rows).
+static int round_reg_body(gbm_ctx *ctx, int si, const int32_t *feat_idx, int32_t nfeat, const gbm_params *P,
+                          gbm_tree_out *out, double *train_loss, bool compacted) {
+    gbm_ctx::Slot &s = ctx->slot[si];
     RoundFeat rf;
-    TRY(setup_features(ctx, 0, feat_idx, nfeat, rf));
-    TRY(enqueue_features(ctx, 0, nfeat));
-    TRY(enqueue_grow(ctx, rf, P, false));
+    TRY(setup_features(ctx, si, feat_idx, nfeat, rf));
+    TRY(enqueue_features(ctx, si, nfeat));
+    TRY(enqueue_grow(ctx, rf, P, compacted));
     if (device_replay(ctx, P)) {
         TRY(enqueue_replay(ctx, P));
         CK(cudaMemcpyAsync(s.h_tout, ctx->d_tout, sizeof(TreeOut), cudaMemcpyDeviceToHost, ctx->st));
         CK(cudaEventRecord(s.done, ctx->st));
-        TRY(wait_slot(ctx, 0));
-        TRY(harvest(ctx, 0, nfeat, P, out, nullptr));
+        TRY(wait_slot(ctx, si));
+        TRY(harvest(ctx, si, nfeat, P, out, nullptr));
     } else {
         HostTree T;
         TRY(replay_on_host(ctx, rf, P, T));
@@ -2505,6 +2506,36 @@ int gbm_round_reg(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_i
     return sync_stream(ctx);
 }
 
+int gbm_round_reg(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
+                  const gbm_params *P, gbm_tree_out *out, double *train_loss) {
+    if (!ctx || !inbag_mask || !feat_idx || !P || !out) return GBM_ERR_ARG;
+    if (!ctx->have_targets) return fail(ctx, GBM_ERR_STATE, "upload bins and gbm_upload_targets first");
+    TRY(check_tree_args(ctx, nfeat, P, out));
+    CK(cudaSetDevice(ctx->dev));
+    TRY(prepare_round(ctx, nfeat, P));
+    std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
+    CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    begin_round(ctx, 0);
+    return round_reg_body(ctx, 0, feat_idx, nfeat, P, out, train_loss, false);
+}
+
+int gbm_round_reg_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *P,
+                          gbm_tree_out *out, double *train_loss) {
+    if (!ctx || !sampler || !P || !out || row_offset < 0) return GBM_ERR_ARG;
+    if (!ctx->have_targets) return fail(ctx, GBM_ERR_STATE, "upload bins and gbm_upload_targets first");
+    const int32_t nf = gbm_sampler_n_feat(sampler);
+    TRY(check_tree_args(ctx, nf, P, out));
+    CK(cudaSetDevice(ctx->dev));
+    TRY(prepare_round(ctx, nf, P));
+    const int si = (int)(gbm_sampler_taken(sampler) % gbm_ctx::kRing);
+    begin_round(ctx, si);
+    TRY(take_sample(ctx, si, sampler, row_offset));
+    TRY(enqueue_sample(ctx, si, gbm_sampler_rows(sampler), gbm_sampler_n_sub(sampler),
+                       gbm_sampler_shuffles_rows(sampler) != 0, row_offset, 0, dev_rows_of(sampler)));
+    TRY(wait_copied(ctx, ctx->slot[si]));
+    return round_reg_body(ctx, si, ctx->feat_buf.data(), nf, P, out, train_loss, true);
+}
+
 // ---- multi-class softmax (E:2949-3065) ---------------------------------------
 
 int gbm_upload_labels_mc(gbm_ctx *ctx, const uint8_t *y, int32_t n_classes, const double *class_w,
@@ -2540,28 +2571,49 @@ int gbm_upload_labels_mc(gbm_ctx *ctx, const uint8_t *y, int32_t n_classes, cons
     return GBM_OK;
 }
 
-int gbm_round_mc(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
-                 const gbm_params *P, gbm_tree_out *outs, double *train_loss) {
-    if (!ctx || !inbag_mask || !feat_idx || !P || !outs) return GBM_ERR_ARG;
-    if (!ctx->have_labels_mc) return fail(ctx, GBM_ERR_STATE, "upload bins and gbm_upload_labels_mc first");
+// One multi-class round on slot si, its in-bag mask in d_mask (and, with
+// `compacted`, its root row list in d_rows).
+static int round_mc_body(gbm_ctx *ctx, int si, const int32_t *feat_idx, int32_t nfeat, const gbm_params *P,
+                         gbm_tree_out *outs, double *train_loss, bool compacted) {
     const int K = ctx->K;
-    for (int k = 0; k < K; k++) TRY(check_tree_args(ctx, nfeat, P, &outs[k]));
-    CK(cudaSetDevice(ctx->dev));
-    TRY(prepare_round(ctx, nfeat, P));
-    std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
-    CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
     longlong2 *const q_bin = ctx->d_q;
     int rc = GBM_OK;
+    bool want_leaf = false;
+    for (int k = 0; k < K; k++) want_leaf |= outs[k].leaf_of_row != nullptr;
     // K trees on the same sample and features, each from its class's
-    // gradients of the round's start (E:2995-3006)
-    for (int k = 0; k < K && rc == GBM_OK; k++) {
+    // gradients of the round's start (E:2995-3006).  With the tree replayed
+    // on the device and no per-row leaves asked for, the K trees and class
+    // updates are queued back to back (each tree's record copied to its own
+    // pinned slot) and the host waits once, after the round's gradients.
+    const bool batched = device_replay(ctx, P) && !want_leaf;
+    if (batched) {
+        TRY(halloc(ctx, &ctx->h_tout_mc, (size_t)K));
+        RoundFeat rf;   // (the caller began slot si's round)
+        TRY(setup_features(ctx, si, feat_idx, nfeat, rf));
+        TRY(enqueue_features(ctx, si, nfeat));
+        for (int k = 0; k < K && rc == GBM_OK; k++) {
+            ctx->d_q = ctx->d_qmc + (int64_t)k * ctx->n;
+            // the row list from the mask, per tree (a partition overwrites it)
+            rc = enqueue_grow(ctx, rf, P, compacted && k == 0);
+            if (rc == GBM_OK) rc = enqueue_replay(ctx, P);
+            if (rc == GBM_OK && cudaMemcpyAsync(&ctx->h_tout_mc[k], ctx->d_tout, sizeof(TreeOut),
+                                                cudaMemcpyDeviceToHost, ctx->st) != cudaSuccess)
+                rc = fail(ctx, GBM_ERR_CUDA, "tree copy");
+            if (rc == GBM_OK)
+                rc = launch(ctx, k_update_class, dim3(ctx->upd_blocks), dim3(kUpdThreads), 0, ctx->st,
+                            (const TreeDev *)ctx->d_tree, (const uint8_t *)ctx->d_xb, ctx->n, P->learning_rate,
+                            ctx->d_Fmc + (int64_t)k * ctx->n, (int32_t *)nullptr, (const int32_t *)ctx->d_bigidx,
+                            (const uint32_t *)ctx->d_topbits);
+        }
+    }
+    for (int k = 0; k < K && rc == GBM_OK && !batched; k++) {
         ctx->d_q = ctx->d_qmc + (int64_t)k * ctx->n;
-        gbm_ctx::Slot &s = ctx->slot[0];
-        begin_round(ctx, 0);
+        gbm_ctx::Slot &s = ctx->slot[si];
+        begin_round(ctx, si);
         RoundFeat rf;
-        rc = setup_features(ctx, 0, feat_idx, nfeat, rf);
-        if (rc == GBM_OK) rc = enqueue_features(ctx, 0, nfeat);
-        if (rc == GBM_OK) rc = enqueue_grow(ctx, rf, P, false);   // the row list from the mask, per tree
+        rc = setup_features(ctx, si, feat_idx, nfeat, rf);
+        if (rc == GBM_OK) rc = enqueue_features(ctx, si, nfeat);
+        if (rc == GBM_OK) rc = enqueue_grow(ctx, rf, P, compacted && k == 0);   // the row list, per tree
         if (rc != GBM_OK) break;
         if (device_replay(ctx, P)) {
             rc = enqueue_replay(ctx, P);
@@ -2569,8 +2621,8 @@ int gbm_round_mc(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_id
                                                 ctx->st) != cudaSuccess)
                 rc = fail(ctx, GBM_ERR_CUDA, "tree copy");
             if (rc == GBM_OK && cudaEventRecord(s.done, ctx->st) != cudaSuccess) rc = fail(ctx, GBM_ERR_CUDA, "event");
-            if (rc == GBM_OK) rc = wait_slot(ctx, 0);
-            if (rc == GBM_OK) rc = harvest(ctx, 0, nfeat, P, &outs[k], nullptr);
+            if (rc == GBM_OK) rc = wait_slot(ctx, si);
+            if (rc == GBM_OK) rc = harvest(ctx, si, nfeat, P, &outs[k], nullptr);
         } else {
             HostTree T;
             rc = replay_on_host(ctx, rf, P, T);
@@ -2612,11 +2664,48 @@ int gbm_round_mc(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_id
     TRY(launch(ctx, k_sum_partials, dim3(1), dim3(256), 0, ctx->st, ctx->d_loss_part, ctx->upd_blocks, ctx->d_loss));
     if (ctx->comm) TRY(allreduce_f64(ctx, ctx->d_loss, 1));
     double loss = 0.0;
-    CK(cudaMemcpyAsync(ctx->slot[0].h_loss, ctx->d_loss, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
+    CK(cudaMemcpyAsync(ctx->slot[si].h_loss, ctx->d_loss, sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
     TRY(sync_stream(ctx));
-    loss = ctx->slot[0].h_loss[0];
+    if (batched) {
+        if (ctx->profiling) TRY(collect_slot_timing(ctx, si));
+        TRY(p2p_check(ctx, si));
+        for (int k = 0; k < K; k++)
+            TRY(take_tree(ctx, ctx->h_tout_mc[k], ctx->slot[si].upd_per_row, nfeat, P, &outs[k]));
+    }
+    loss = ctx->slot[si].h_loss[0];
     if (train_loss) *train_loss = -loss / (double)ctx->n_global;
     return GBM_OK;
+}
+
+
+int gbm_round_mc(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, int32_t nfeat,
+                 const gbm_params *P, gbm_tree_out *outs, double *train_loss) {
+    if (!ctx || !inbag_mask || !feat_idx || !P || !outs) return GBM_ERR_ARG;
+    if (!ctx->have_labels_mc) return fail(ctx, GBM_ERR_STATE, "upload bins and gbm_upload_labels_mc first");
+    for (int k = 0; k < ctx->K; k++) TRY(check_tree_args(ctx, nfeat, P, &outs[k]));
+    CK(cudaSetDevice(ctx->dev));
+    TRY(prepare_round(ctx, nfeat, P));
+    std::memcpy(ctx->h_mask, inbag_mask, (size_t)ctx->n);
+    CK(cudaMemcpyAsync(ctx->d_mask, ctx->h_mask, (size_t)ctx->n, cudaMemcpyHostToDevice, ctx->st));
+    begin_round(ctx, 0);
+    return round_mc_body(ctx, 0, feat_idx, nfeat, P, outs, train_loss, false);
+}
+
+int gbm_round_mc_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *P,
+                         gbm_tree_out *outs, double *train_loss) {
+    if (!ctx || !sampler || !P || !outs || row_offset < 0) return GBM_ERR_ARG;
+    if (!ctx->have_labels_mc) return fail(ctx, GBM_ERR_STATE, "upload bins and gbm_upload_labels_mc first");
+    const int32_t nf = gbm_sampler_n_feat(sampler);
+    for (int k = 0; k < ctx->K; k++) TRY(check_tree_args(ctx, nf, P, &outs[k]));
+    CK(cudaSetDevice(ctx->dev));
+    TRY(prepare_round(ctx, nf, P));
+    const int si = (int)(gbm_sampler_taken(sampler) % gbm_ctx::kRing);
+    begin_round(ctx, si);
+    TRY(take_sample(ctx, si, sampler, row_offset));
+    TRY(enqueue_sample(ctx, si, gbm_sampler_rows(sampler), gbm_sampler_n_sub(sampler),
+                       gbm_sampler_shuffles_rows(sampler) != 0, row_offset, 0, dev_rows_of(sampler)));
+    TRY(wait_copied(ctx, ctx->slot[si]));
+    return round_mc_body(ctx, si, ctx->feat_buf.data(), nf, P, outs, train_loss, true);
 }
 
 int gbm_get_F_mc(gbm_ctx *ctx, double *F_out) {

@@ -240,6 +240,20 @@ int gbm_round(gbm_ctx *ctx, const uint8_t *inbag_mask, const int32_t *feat_idx, 
 int gbm_round_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *params,
                       gbm_tree_out *out, double *train_loss);
 
+/* gbm_round_mc with the round's sample drawn from `sampler` as in
+ * gbm_round_sampled (the shuffle applied on the device, E:2502-2517), the
+ * loop body of _fit_multiclass (E:2989-3008): the same K trees and loss as
+ * gbm_round_mc with the equivalent mask.  Replaces the host's full shuffle
+ * of every round (gbm_sampler_next with a mask). */
+int gbm_round_mc_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *params,
+                         gbm_tree_out *outs, double *train_loss);
+
+/* gbm_round_reg with the round's sample drawn from `sampler` as in
+ * gbm_round_sampled, the loop body of _fit_regression (E:2625-2663): the
+ * same tree and loss as gbm_round_reg with the equivalent mask. */
+int gbm_round_reg_sampled(gbm_ctx *ctx, gbm_sampler *sampler, int64_t row_offset, const gbm_params *params,
+                          gbm_tree_out *out, double *train_loss);
+
 /* n_rounds consecutive gbm_round_sampled calls, the fit loop of
  * _fit_binary (E:2849-2905): outs[r] and train_loss[r] get round r's tree
  * and loss, identical to calling gbm_round_sampled n_rounds times.  When
