@@ -363,10 +363,10 @@ int wait_copied(gbm_ctx *ctx, gbm_ctx::Slot &s) {
     cudaEvent_t t0 = nullptr, t1 = nullptr;
     if (ctx->profiling) {
         TRY(timing_pair(ctx, 4, t0, t1));
-        CK(cudaEventRecord(t0, ctx->st));
+        TRY(record_ev(ctx, t0, ctx->st));
     }
     TRY(wait_ev(ctx, ctx->st, s.copied));
-    if (t1) CK(cudaEventRecord(t1, ctx->st));
+    if (t1) TRY(record_ev(ctx, t1, ctx->st));
     return GBM_OK;
 }
 
@@ -1800,7 +1800,7 @@ int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int
     cudaEvent_t t0 = nullptr, t1 = nullptr;
     if (ctx->profiling) {
         TRY(timing_pair(ctx, 3, t0, t1));
-        CK(cudaEventRecord(t0, ctx->cst));
+        TRY(record_ev(ctx, t0, ctx->cst));
     }
     s.xc_on_cst = nf > 0 && compact_hist(ctx);
     if (s.xc_on_cst) {
@@ -1836,7 +1836,7 @@ int enqueue_sample(gbm_ctx *ctx, int si, int64_t N, int64_t m, bool rows_on, int
         CK(cudaMemsetAsync(ctx->d_mask, 1, (size_t)ctx->n, ctx->cst));
     }
     TRY(enqueue_compaction(ctx, ctx->cst));
-    if (t1) CK(cudaEventRecord(t1, ctx->cst));
+    if (t1) TRY(record_ev(ctx, t1, ctx->cst));
     TRY(record_ev(ctx, s.copied, ctx->cst));
     return GBM_OK;
 }
