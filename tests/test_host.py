@@ -725,3 +725,45 @@ def test_ranked_replay_matches_the_loop():
         fast += 1
         assert loop == ranked, case
     assert fast > 800 and handed > 50, (fast, handed)
+
+
+def _compact_rows_restated(mask, tile=4096, per=16):
+    """k_compact_rows' index arithmetic: tiles of `tile` mask bytes, thread t
+    of a tile takes bytes 16 t .. 16 t + 15 (a 16-byte load, or byte loads
+    past the end), a block exclusive scan of the threads' in-bag counts, the
+    tiles' offsets from their predecessors' totals (the look-back), and each
+    thread's rows written in order from offset + its scan value."""
+    n = len(mask)
+    out = np.full(n, -1, np.int64)
+    total = 0
+    for t0 in range(0, n, tile):
+        counts, bits = [], []
+        for th in range(tile // per):
+            base = t0 + per * th
+            b = [k for k in range(per) if base + k < n and mask[base + k] != 0]
+            bits.append(b)
+            counts.append(len(b))
+        excl = np.concatenate([[0], np.cumsum(counts)[:-1]])
+        off = total   # the look-back: the sum of the earlier tiles' counts
+        for th, b in enumerate(bits):
+            o = off + int(excl[th])
+            for k in b:
+                assert out[o] == -1
+                out[o] = t0 + per * th + k
+                o += 1
+        total += int(sum(counts))
+    return out[:total], total
+
+
+@pytest.mark.parametrize("n", [1, 15, 16, 17, 4095, 4096, 4097, 20_003])
+@pytest.mark.parametrize("fill", ["random", "none", "all"])
+def test_compact_rows_index_arithmetic(n, fill):
+    """The one-pass compaction gives the in-bag rows in ascending order and
+    their count, for ragged tails, empty and full masks."""
+    rng = np.random.default_rng(n)
+    mask = {"random": (rng.random(n) < 0.75), "none": np.zeros(n, bool), "all": np.ones(n, bool)}[fill]
+    mask = mask.astype(np.uint8) * rng.integers(1, 255, n).astype(np.uint8)   # any nonzero byte is in bag
+    rows, total = _compact_rows_restated(mask)
+    want = np.flatnonzero(mask)
+    assert total == len(want)
+    assert np.array_equal(rows, want)
