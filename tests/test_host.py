@@ -672,11 +672,11 @@ def _replay_ranked(T, max_leaves, gamma, msl, max_depth, max_c=256, max_d=15):
     return 0, 1 + 2 * len(rank), out, alg
 
 
-def _random_grown_table(rng, ties):
+def _random_grown_table(rng, ties, D=None, p_expand=0.9, max_nodes=None):
     """A node table as the level loop leaves it: nodes numbered level by level,
     some expanded nodes, some candidates left unexpanded (pruned), splits with
     no valid feature, rows split unevenly (some under min_samples_leaf)."""
-    D = int(rng.integers(2, 9))
+    D = int(rng.integers(2, 9)) if D is None else D
     T = [dict(depth=0, parent=-1, n=int(rng.integers(50, 5000)))]
     level = [0]
     while level:
@@ -687,7 +687,8 @@ def _random_grown_table(rng, ties):
             g = rng.exponential(1.0) * np.exp(-0.2 * x["depth"]) - 0.05
             x["gain"] = float(np.round(g, 1) if ties else g)
             x["local"] = int(x["n"] * rng.random())
-            x["expanded"] = int(x["feat"] >= 0 and rng.random() < 0.9)
+            x["expanded"] = int(x["feat"] >= 0 and rng.random() < p_expand and
+                                (max_nodes is None or len(T) + 2 <= max_nodes))
             x["kid0"] = x["kid1"] = -1
         for v in level:
             x = T[v]
@@ -767,3 +768,38 @@ def test_compact_rows_index_arithmetic(n, fill):
     want = np.flatnonzero(mask)
     assert total == len(want)
     assert np.array_equal(rows, want)
+
+
+
+def test_ranked_replay_at_its_size_limits():
+    """Deep tables (depth 10-17, up to 2048 nodes): the ranked form matches the
+    loop wherever it does not hand over, and it hands over on every table with
+    a candidate deeper than 15 or more than 256 candidates."""
+    rng = np.random.default_rng(29)
+    over = fast = 0
+    for case in range(40):
+        D = int(rng.integers(10, 18))
+        T, D = _random_grown_table(rng, ties=False, D=D, p_expand=0.8, max_nodes=2048)
+        max_leaves = int(rng.integers(20, 128))
+        loop = _replay_loop(T, max_leaves, 0.0, 1, D + 1)
+        ranked = _replay_ranked(T, max_leaves, 0.0, 1, D + 1)
+        # the candidates: key > 0 and every ancestor a makeable split
+        mk = lambda x: (x["feat"] >= 0 and x["gain"] > 0.0 and x["expanded"] and T[x["kid0"]]["n"] >= 1 and
+                        T[x["kid1"]]["n"] >= 1)
+        cands = []
+        for i, x in enumerate(T):
+            if not (x["feat"] >= 0 and x["gain"] > 0.0):
+                continue
+            a = x["parent"]
+            while a >= 0 and mk(T[a]):
+                a = T[a]["parent"]
+            if a < 0:
+                cands.append(i)
+        beyond = len(cands) > 256 or any(T[v]["depth"] > 15 for v in cands)
+        if beyond:
+            assert ranked is None, case
+            over += 1
+        elif ranked is not None:
+            fast += 1
+            assert loop == ranked, case
+    assert fast > 0 and over > 0, (fast, over)
