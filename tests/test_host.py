@@ -672,12 +672,12 @@ def _replay_ranked(T, max_leaves, gamma, msl, max_depth, max_c=256, max_d=15):
     return 0, 1 + 2 * len(rank), out, alg
 
 
-def _random_grown_table(rng, ties, D=None, p_expand=0.9, max_nodes=None):
+def _random_grown_table(rng, ties, D=None, p_expand=0.9, max_nodes=None, n_root=None):
     """A node table as the level loop leaves it: nodes numbered level by level,
     some expanded nodes, some candidates left unexpanded (pruned), splits with
     no valid feature, rows split unevenly (some under min_samples_leaf)."""
     D = int(rng.integers(2, 9)) if D is None else D
-    T = [dict(depth=0, parent=-1, n=int(rng.integers(50, 5000)))]
+    T = [dict(depth=0, parent=-1, n=int(rng.integers(50, 5000)) if n_root is None else n_root)]
     level = [0]
     while level:
         nxt = []
@@ -779,7 +779,7 @@ def test_ranked_replay_at_its_size_limits():
     over = fast = 0
     for case in range(40):
         D = int(rng.integers(10, 18))
-        T, D = _random_grown_table(rng, ties=False, D=D, p_expand=0.8, max_nodes=2048)
+        T, D = _random_grown_table(rng, ties=False, D=D, p_expand=0.85, max_nodes=2048, n_root=1_000_000)
         max_leaves = int(rng.integers(20, 128))
         loop = _replay_loop(T, max_leaves, 0.0, 1, D + 1)
         ranked = _replay_ranked(T, max_leaves, 0.0, 1, D + 1)
